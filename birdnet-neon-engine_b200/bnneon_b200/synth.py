@@ -1,0 +1,505 @@
+"""Synthetic BirdNET-v2.4-architecture models and audio, and a writer for their neon-int8 packages.
+
+There is no BirdNET v2.4 ONNX file here (and no network), so the benchmark and the tests run a model of the v2.4
+architecture with seeded random weights:
+
+* ``v24_ir(seed)`` builds the fused intermediate representation the reference compiler lowers (the op dicts of
+  python/bnneon/compiler/recog.py after fusion: FE_STFT2_POW, CONV, DWCONV, SE, AFFINE, MEAN, DENSE) with the layer
+  shapes of results/graph_compact.txt and results/mac_table.txt: front end 2048/278 + 1024/280 on 144000 samples,
+  c0 4x8 stride 2 + ReLU + max|avg pool, p0 1x1, 16 inverted-residual blocks (b1.1-b4.4, SE on b2-b4), post BN +
+  ReLU + 3x3 pc conv + mean (the 1024-d embedding), and a dense head.
+* ``write_int8_package(path, ir)`` writes the ``neon-int8`` package the reference compiler would write for that IR
+  with the int8 policy ``pw,pwl,head,lin`` (bnc.py compile --paths neon-int8 --int8 pw,pwl,head,lin). The output is
+  byte-identical to the reference compiler's (the sha256 is pinned in tests/golden/packages.json, produced by
+  tests/golden/make_golden.py with the reference's own lower.py / pkgfmt.py), so the loader and the kernels are
+  tested on genuine package bytes.
+* ``audio(n, seed)`` makes seeded windows of noise plus linear chirps.
+
+Weights: He-normal N(0, sqrt(2 / fan_in)) for every expanding conv and the dense layers; the projecting 1x1 convs
+(pwl) use half of the LeCun scale so that the residual stack stays in range without batch norm; biases are small
+seeded normals. The front end uses periodic Hann windows and triangular mel filter banks below Nyquist.
+"""
+import hashlib
+import struct
+
+import numpy as np
+
+NSAMP = 144000
+SAMPLE_RATE = 48000
+
+# (tag, stride, c_in, c_mid, c_out, se_rd, residual): results/mac_table.txt:3-53, results/graph_compact.txt
+V24_BLOCKS = (
+    [("b1.1", 2, 24, 72, 36, 0, False), ("b1.2", 1, 36, 72, 36, 0, True), ("b1.3", 1, 36, 72, 36, 0, True),
+     ("b2.1", 2, 36, 288, 72, 18, False)]
+    + [(f"b2.{i}", 1, 72, 288, 72, 18, True) for i in (2, 3, 4)]
+    + [("b3.1", 2, 72, 864, 108, 27, False)]
+    + [(f"b3.{i}", 1, 108, 864, 108, 27, True) for i in (2, 3, 4, 5)]
+    + [("b4.1", 2, 108, 1536, 192, 48, False)]
+    + [(f"b4.{i}", 1, 192, 1536, 192, 48, True) for i in (2, 3, 4)])
+# the same stages with one (strided) block each: the same op kinds and end geometry, for quick tests
+MINI_BLOCKS = tuple(b for b in V24_BLOCKS if b[0].endswith(".1"))
+
+INT8_POLICY = "pw,pwl,head,lin"
+PATH = "neon-int8"
+
+
+# ------------------------------------------------------------------ the model IR
+
+def _mel_bank(nfft, fmin, fmax, nmel=96):
+    """Triangular filters on the HTK mel scale, [nmel][nfft/2 + 1] float32, zero at and above fmax."""
+    bins = nfft // 2 + 1
+    mel = lambda f: 2595.0 * np.log10(1.0 + f / 700.0)  # noqa: E731
+    imel = lambda m: 700.0 * (10.0 ** (m / 2595.0) - 1.0)  # noqa: E731
+    edges = imel(np.linspace(mel(fmin), mel(fmax), nmel + 2))
+    freqs = np.arange(bins) * SAMPLE_RATE / nfft
+    out = np.zeros((nmel, bins), np.float64)
+    for j in range(nmel):
+        lo, c, hi = edges[j], edges[j + 1], edges[j + 2]
+        up = (freqs - lo) / max(c - lo, 1e-9)
+        down = (hi - freqs) / max(hi - c, 1e-9)
+        out[j] = np.maximum(0.0, np.minimum(up, down))
+    return out.astype(np.float32)
+
+
+def _hann(n):
+    return (0.5 - 0.5 * np.cos(2 * np.pi * np.arange(n) / n)).astype(np.float32)
+
+
+def v24_ir(seed=0, n_classes=6522, blocks=V24_BLOCKS):
+    """The fused IR of a v2.4-architecture model with seeded random weights.
+
+    Returns:
+        (ops, vshape, logits_value, embedding_value): ops as the reference compiler's recognizer emits them after
+        fusion, vshape {value id: (H, W)}.
+    """
+    rng = np.random.default_rng(seed)
+    f32 = np.float32
+
+    def he(*shape, fan_in, scale=1.0):
+        return (rng.standard_normal(shape) * (scale * np.sqrt(2.0 / fan_in))).astype(f32)
+
+    def bias(n, s=0.02):
+        return (rng.standard_normal(n) * s).astype(f32)
+
+    ops, vshape = [], {}
+    nid = [0]
+
+    def val(h, w):
+        nid[0] += 1
+        vshape[nid[0]] = (h, w)
+        return nid[0]
+
+    img = val(96, 511)
+    ops.append(dict(op="FE_STFT2_POW", ins=[], out=img, eps=1e-6,
+                    branches=[dict(nfft=2048, hop=278, window=_hann(2048), dft=None,
+                                   mel=_mel_bank(2048, 0.0, 3000.0), pow=0.25),
+                              dict(nfft=1024, hop=280, window=_hann(1024), dft=None,
+                                   mel=_mel_bank(1024, 500.0, 15000.0), pow=0.3)],
+                    bn_s=np.array([0.8, 1.1], f32), bn_b=np.array([-0.2, 0.1], f32),
+                    nodes=["v24/fe"]))
+    c0 = val(48, 128)
+    ops.append(dict(op="CONV", ins=[img], out=c0, w=he(24, 2, 4, 8, fan_in=64), b=bias(24), k=[4, 8], s=[2, 2],
+                    pads=[1, 3, 1, 4], act="relu", pool="maxavg_w2", nodes=["v24/c0"]))
+    x = val(48, 128)
+    ops.append(dict(op="CONV", ins=[c0], out=x, w=he(24, 48, 1, 1, fan_in=48), b=bias(24), k=[1, 1], s=[1, 1],
+                    pads=[0, 0, 0, 0], act=None, nodes=["v24/p0"]))
+    h, w = 48, 128
+    for tag, st, cin, cm, cout, rd, skip in blocks:
+        ho, wo = (h + 2 - 3) // st + 1, (w + 2 - 3) // st + 1
+        e = val(h, w)
+        ops.append(dict(op="CONV", ins=[x], out=e, w=he(cm, cin, 1, 1, fan_in=cin), b=bias(cm), k=[1, 1], s=[1, 1],
+                        pads=[0, 0, 0, 0], act="swish", nodes=[f"v24/{tag}/pw"]))
+        d = val(ho, wo)
+        ops.append(dict(op="DWCONV", ins=[e], out=d, w=he(cm, 1, 3, 3, fan_in=9), b=bias(cm), k=[3, 3],
+                        s=[st, st], pads=[1, 1, 1, 1], act="swish", nodes=[f"v24/{tag}/dw"]))
+        if rd:
+            g = val(ho, wo)
+            ops.append(dict(op="SE", ins=[d], out=g, w1=he(rd, cm, fan_in=cm), b1=bias(rd), act1="swish",
+                            w2=he(cm, rd, fan_in=rd), b2=bias(cm, 0.5), nodes=[f"v24/{tag}/se"]))
+            d = g
+        y = val(ho, wo)
+        pwl = dict(op="CONV", ins=[d], out=y, w=he(cout, cm, 1, 1, fan_in=cm, scale=0.35), b=bias(cout), k=[1, 1],
+                   s=[1, 1], pads=[0, 0, 0, 0], act=None, nodes=[f"v24/{tag}/pwl"])
+        if skip:
+            pwl["res"] = x
+        ops.append(pwl)
+        x, h, w = y, ho, wo
+    a = val(h, w)
+    ops.append(dict(op="AFFINE", ins=[x], out=a, s=(1.0 + 0.1 * rng.standard_normal(192)).astype(f32),
+                    t=bias(192, 0.1), act="relu", nodes=["v24/post_bn"]))
+    pc = val(1, 6)
+    ops.append(dict(op="CONV", ins=[a], out=pc, w=he(1024, 192, 3, 3, fan_in=1728), b=bias(1024), k=[3, 3],
+                    s=[1, 1], pads=[0, 0, 0, 0], act="relu", nodes=["v24/pc"]))
+    feat = val(1, 1)
+    ops.append(dict(op="MEAN", ins=[pc], out=feat, nodes=["v24/mean"]))
+    logits = val(1, 1)
+    ops.append(dict(op="DENSE", ins=[feat], out=logits, w=he(n_classes, 1024, fan_in=1024, scale=0.5),
+                    b=bias(n_classes), nodes=["v24/head"]))
+    return ops, vshape, logits, feat
+
+
+def labels_for(n_classes):
+    """A label file (bytes) with one synthetic class name per line."""
+    return "".join(f"Synthetic species {i:05d}_Synthetic {i:05d}\n" for i in range(n_classes)).encode()
+
+
+def metadata(n_classes, emb_dim, labels, model_id="birdnet_v2.4_synthetic"):
+    """The package metadata records, in the compiler's order (cmd_compile.py _set_metadata)."""
+    return [("model_id", model_id), ("family", 24), ("sample_rate", SAMPLE_RATE), ("n_samples", NSAMP),
+            ("hop_samples", 0), ("n_classes", int(n_classes)), ("emb_dim", int(emb_dim)), ("post", 1),
+            ("logit_scale", 1.0), ("labels_sha256", hashlib.sha256(labels).digest()), ("labels_file", "labels.txt"),
+            ("labels", labels), ("license", "synthetic weights, no license restrictions"),
+            ("attribution", "synthetic BirdNET-v2.4-architecture model (random weights)"),
+            ("source_sha256", "0" * 64), ("input", f"float32 PCM in [-1, 1) at sample_rate, {NSAMP} samples per window"),
+            ("compiler", "bnc 3")]
+
+
+# ------------------------------------------------------------------ the neon-int8 lowering of that IR
+
+F32, F16, I8, I32 = 0, 1, 2, 3
+OPC = dict(FE_STFT2=1, C0POOL=2, DW3=4, POSTPC=6, PW_S8=22, GEMV_S8=23, SE_GATE=25)
+
+
+def _r8(x):
+    return (x + 7) & ~7
+
+
+def _r16(x):
+    return (x + 15) & ~15
+
+
+class _Int8Lowering:
+    """The neon-int8 lowering of the v2.4 IR (pw, pwl, head and dense layers on int8).
+
+    Follows the reference compiler's rules for these op kinds (python/bnneon/compiler/lower.py: buffer shapes and
+    element counts, tensor names and packing, op records and their int parameters, the order buffers and tensors are
+    created in), so the package it produces is the reference compiler's.
+    """
+
+    def __init__(self, ops):
+        self.ops = ops
+        self.bufs = [(F32, 1, 1, NSAMP, NSAMP, 0, NSAMP)]
+        self.tensors, self.tindex = [], {}
+        self.records, self.src = [], []
+        self.vbuf, self.gate, self.uses = {}, {}, {}
+        self.chsum = (None, None)
+        for o in ops:
+            for i in o["ins"] + ([o["res"]] if o.get("res") else []):
+                self.uses.setdefault(i, []).append(o)
+
+    # helpers
+    def buf(self, dt, h, w, c, ld=None, halo=0, elems=None):
+        ld = ld or c
+        if elems is None:
+            elems = (h + 2 * halo) * (w + 2 * halo) * ld if halo else _r8(h * w) * ld
+        self.bufs.append((dt, h, w, c, ld, halo, int(elems)))
+        return len(self.bufs) - 1
+
+    def tensor(self, name, a):
+        if name in self.tindex:
+            return self.tindex[name]
+        a = np.ascontiguousarray(a)
+        self.tindex[name] = len(self.tensors)
+        self.tensors.append((name, a))
+        return self.tindex[name]
+
+    def emit(self, code, bl, tl, il, o):
+        self.records.append((code, [int(x) for x in bl], [int(x) for x in tl], [int(x) for x in il]))
+        n = [x for x in o.get("nodes", []) if x] or ["?"]
+        self.src.append(f"'{n[0]}'" + (f" +{len(n) - 1}" if len(n) > 1 else "") if o.get("nodes") else "?")
+
+    @staticmethod
+    def pack_f32(w, b, kp):
+        n, k = w.shape
+        np_ = _r8(n)
+        panels = np.zeros((((np_ * kp * 4) + 127) & ~63) // 4, np.float32)
+        w32 = np.zeros((np_, k), np.float32)
+        w32[:n] = w
+        panels[:np_ * kp].reshape(np_ // 8, kp, 8)[:, :k, :] = w32.reshape(np_ // 8, 8, k).transpose(0, 2, 1)
+        bb = np.zeros(np_ + 8, np.float32)
+        bb[:n] = b
+        return panels, bb, (n, k, kp, np_)
+
+    def s8(self, tag, w, b):
+        """per-output-channel symmetric int8, ties away from zero, panels [Np/4][Kp/16][4][16] (lower.py:883-914)"""
+        n, k = w.shape
+        np_, kp = _r8(n), _r16(k)
+        wq = np.zeros((np_, kp), np.float64)
+        wq[:n, :k] = w
+        am = np.abs(wq).max(1)
+        sw = np.where(am > 0, am / 127.0, 1.0)
+        ws = wq / sw[:, None]
+        q = np.clip(np.sign(ws) * np.floor(np.abs(ws) + 0.5), -127, 127).astype(np.int8)
+        panels = q.reshape(np_ // 4, 4, kp // 16, 16).transpose(0, 2, 1, 3).copy()
+        cs = q.astype(np.int32).sum(1).astype(np.int32)
+        bb = np.zeros(np_ + 8, np.float32)
+        bb[:n] = b
+        swf = np.zeros(np_ + 8, np.float32)
+        swf[:np_] = sw
+        csp = np.zeros(np_ + 8, np.int32)
+        csp[:np_] = cs
+        t = [self.tensor(f"s8n/{tag}.q", panels), self.tensor(f"s8n/{tag}.sw", swf),
+             self.tensor(f"s8n/{tag}.cs", csp), self.tensor(f"s8n/{tag}.b", bb)]
+        return t, (n, k, kp, np_)
+
+    def out_buffer(self, o, ho, wo, co):
+        cons = self.uses.get(o["out"], [])
+        if len(cons) == 1 and cons[0]["op"] == "DWCONV" and co % 8 == 0:
+            return self.buf(F32, ho, wo, co, ld=co, halo=1), wo, 1, co
+        ldo = _r8(co)
+        return self.buf(F32, ho, wo, co, ld=ldo), 0, 0, ldo
+
+    # op kinds
+    def run(self):
+        i = 0
+        k = 0
+        while i < len(self.ops):
+            o = self.ops[i]
+            i = getattr(self, "l_" + o["op"].lower())(i, o, k)
+            k += 1
+
+    def l_fe_stft2_pow(self, i, o, k):
+        b1, b2 = o["branches"]
+        tl = [self.tensor("fe/win1", b1["window"]), self.tensor("fe/win2", b2["window"]),
+              self.tensor("fe/mel1", b1["mel"]), self.tensor("fe/mel2", b2["mel"]),
+              self.tensor("fe/pow1", np.array([b1["pow"]], np.float32)),
+              self.tensor("fe/pow2", np.array([b2["pow"]], np.float32)),
+              self.tensor("fe/bn_s", o["bn_s"]), self.tensor("fe/bn_b", o["bn_b"])]
+        ob = self.buf(F32, 96, 511, 2)
+        self.emit(OPC["FE_STFT2"], [0, ob], tl, [], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+    def l_conv(self, i, o, k):
+        w, b = o["w"], o["b"]
+        co = w.shape[0]
+        ib = self.vbuf[o["ins"][0]]
+        if o["k"] == [4, 8]:  # c0 + ReLU + max|avg pool
+            panels, bb, shp = self.pack_f32(w.transpose(0, 2, 3, 1).reshape(co, -1), b, 64)
+            tl = [self.tensor(f"s8n/c0.{k}.w", panels), self.tensor(f"s8n/c0.{k}.b", bb)]
+            ob = self.buf(F32, 48, 128, 48)
+            self.emit(OPC["C0POOL"], [ib, ob], tl, list(shp), o)
+            self.vbuf[o["out"]] = ob
+            return i + 1
+        _, h_in, w_in, _, ld, _, _ = self.bufs[ib]
+        tl, shp = self.s8(f"pw.{k}", w[:, :, 0, 0], b)
+        ob, ow, opad, ldo = self.out_buffer(o, h_in, w_in, co)
+        rb, ldr = -1, 0
+        if o.get("res"):
+            rb = self.vbuf[o["res"]]
+            ldr = self.bufs[rb][4]
+        gate = [self.gate[o["ins"][0]]] if o["ins"][0] in self.gate else []
+        m4 = (h_in * w_in + 3) & ~3
+        qb = self.buf(I8, m4, 1, shp[2])
+        sb = self.buf(F32, m4, 1, 1)
+        zb = self.buf(I32, m4, 1, 1)
+        act = {None: 0, "swish": 1, "relu": 2}[o.get("act")]
+        self.emit(OPC["PW_S8"], [ib, ob, rb, qb, sb, zb] + gate, tl,
+                  list(shp) + [h_in * w_in, ld, act, ldo, ow, opad, ldr], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+    def l_dwconv(self, i, o, k):
+        ib = self.vbuf[o["ins"][0]]
+        _, h, w, c, _, _, _ = self.bufs[ib]
+        ho, wo = self.vshape[o["out"]]
+        self.bufs.append((F32, 1, 1, c, c, 0, c))
+        cs = len(self.bufs) - 1
+        ob = self.buf(F32, ho, wo, c)
+        w9 = o["w"][:, 0].transpose(1, 2, 0).reshape(9, c)
+        tl = [self.tensor(f"s8n/dw.{k}.w", w9.astype(np.float32)),
+              self.tensor(f"s8n/dw.{k}.b", o["b"].astype(np.float32))]
+        self.emit(OPC["DW3"], [ib, ob, cs], tl, [h, w, c, o["s"][0], ho, wo], o)
+        self.vbuf[o["out"]] = ob
+        self.chsum = (ob, cs)
+        return i + 1
+
+    def l_se(self, i, o, k):
+        ib = self.vbuf[o["ins"][0]]
+        cs = self.chsum[1]
+        _, h, w, c, _, _, _ = self.bufs[ib]
+        rd = o["w1"].shape[0]
+        tl = [self.tensor(f"s8n/se.{k}.w1", o["w1"]), self.tensor(f"s8n/se.{k}.b1", o["b1"]),
+              self.tensor(f"s8n/se.{k}.w2t", np.ascontiguousarray(o["w2"].T)),
+              self.tensor(f"s8n/se.{k}.b2", o["b2"])]
+        gb = self.buf(F32, 1, 1, c, elems=c)
+        self.emit(OPC["SE_GATE"], [cs, gb], tl, [c, rd, h * w], o)
+        self.gate[o["out"]] = gb
+        self.vbuf[o["out"]] = ib
+        return i + 1
+
+    def l_affine(self, i, o, k):
+        nx, mn = self.ops[i + 1], self.ops[i + 2]
+        ib = self.vbuf[o["ins"][0]]
+        w = nx["w"].transpose(0, 2, 3, 1).reshape(1024, 1728)
+        panels, bb, shp = self.pack_f32(w, nx["b"], 1728)
+        tl = [self.tensor(f"s8n/pc.{k}.w", panels), self.tensor(f"s8n/pc.{k}.b", bb)]
+        tl = [self.tensor(f"s8n/post.{k}.s", o["s"]), self.tensor(f"s8n/post.{k}.t", o["t"])] + tl
+        fb = self.buf(F32, 1, 1, 1024)
+        pin = self.buf(F32, 8, 1, 1728)
+        pout = self.buf(F32, 8, 1, 1024)
+        self.emit(OPC["POSTPC"], [ib, fb, pin, pout], tl, list(shp), o)
+        self.vbuf[mn["out"]] = fb
+        return i + 3
+
+    def l_dense(self, i, o, k):
+        ib = self.vbuf[o["ins"][0]]
+        n = o["w"].shape[0]
+        self.buf(F32, 1, 1, n)  # the compiler allocates the fp32 head's output before choosing the int8 head
+        tl, shp = self.s8(f"gemv.{k}", o["w"], o["b"])
+        ob = self.buf(F32, 1, 1, shp[3])
+        qb = self.buf(I8, 4, 1, shp[2])
+        sb = self.buf(F32, 4, 1, 1)
+        zb = self.buf(I32, 4, 1, 1)
+        self.emit(OPC["GEMV_S8"], [ib, ob, qb, sb, zb], tl, list(shp) + [0], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+
+def plan_slots(bufs, records, pinned):
+    """Memory slots: buffers with disjoint op lifetimes and one dtype share a slot (best fit); buffer 0 and the pinned
+    outputs get their own (lower.py plan_slots rules)."""
+    first, last = {}, {}
+    for i, (_, bl, _, _) in enumerate(records):
+        for b in bl:
+            if b >= 0:
+                first.setdefault(b, i)
+                last[b] = i
+    esz = {0: 4, 1: 2, 2: 1, 3: 4}
+    slot = {0: 0}
+    slots = [None]
+    for b in pinned:
+        if b is not None and b not in slot:
+            slot[b] = len(slots)
+            slots.append([bufs[b][0], 0, 1 << 30])
+    for i, (_, bl, _, _) in enumerate(records):
+        for b in bl:
+            if b < 0 or b in slot or first[b] != i:
+                continue
+            need = bufs[b][6] * esz[bufs[b][0]]
+            free = [j for j in range(1, len(slots)) if slots[j][0] == bufs[b][0] and slots[j][2] < i]
+            if not free:
+                slots.append([bufs[b][0], 0, 0])
+                j = len(slots) - 1
+            else:
+                fit = [j for j in free if slots[j][1] >= need]
+                j = min(fit, key=lambda s: slots[s][1]) if fit else max(free, key=lambda s: slots[s][1])
+            slots[j][1] = max(slots[j][1], need)
+            slots[j][2] = last[b]
+            slot[b] = j
+    for b in range(len(bufs)):
+        if b not in slot:
+            slot[b] = len(slots)
+            slots.append([bufs[b][0], 0, 0])
+    return [tuple(bufs[b]) + (slot[b],) for b in range(len(bufs))]
+
+
+# ------------------------------------------------------------------ the .bnpk writer (pkgfmt.py:1-22 format)
+
+_DT = {np.dtype(np.float32): 0, np.dtype(np.float16): 1, np.dtype(np.int8): 2, np.dtype(np.int32): 3}
+
+
+def _pad8(b):
+    return b + b"\0" * ((8 - len(b) % 8) % 8)
+
+
+def _meta(k, v):
+    kb = k.encode()
+    if isinstance(v, (bytes, bytearray)):
+        ty, vb = 3, bytes(v)
+    elif isinstance(v, (bool, int, np.integer)):
+        ty, vb = 1, struct.pack("<q", int(v))
+    elif isinstance(v, float):
+        ty, vb = 2, struct.pack("<d", v)
+    else:
+        ty, vb = 0, str(v).encode()
+    return _pad8(struct.pack("<HHI", len(kb), ty, len(vb)) + kb + vb)
+
+
+def _record(code, bl, tl, il):
+    body = struct.pack(f"<{len(bl) + len(tl) + len(il)}i", *(list(bl) + list(tl) + list(il)))
+    rec = _pad8(struct.pack("<6H", code, 0, len(bl), len(tl), len(il), 0) + body)
+    return rec[:2] + struct.pack("<H", len(rec)) + rec[4:]
+
+
+def write_package(dst, meta, tensors, paths):
+    """Writes a .bnpk: meta [(key, value)], tensors [(name, array)], paths [(name, hwcap, bufs, records, in, out,
+    emb)]. Returns the file size."""
+    mb = b"".join(_meta(k, v) for k, v in meta)
+    meta_off = 64
+    tensor_off = meta_off + len(mb)
+    path_off = tensor_off + 96 * len(tensors)
+    off = path_off + 72 * len(paths)
+    pdesc, pblobs = [], []
+    for name, hw, bufs, recs, ib, ob, eb in paths:
+        bb = b"".join(struct.pack("<8IQ", *b[:6], b[7], 0, b[6]) for b in bufs)
+        rb = b"".join(_record(*r) for r in recs)
+        boff, ooff = off, off + len(bb)
+        off = ooff + len(rb)
+        pblobs += [bb, rb]
+        pdesc.append(name.encode().ljust(24, b"\0") + struct.pack(
+            "<8I2Q", hw, len(bufs), len(recs), len(rb), ib, ob, 0xffffffff if eb is None else eb, 0, boff, ooff))
+    off = (off + 63) & ~63
+    tdesc, tblobs = [], []
+    for name, a in tensors:
+        dims = list(a.shape) + [0] * (4 - a.ndim)
+        tdesc.append(name.encode().ljust(48, b"\0") + struct.pack("<II4IQQQ", _DT[a.dtype], a.ndim, *dims, off,
+                                                                  a.nbytes, 0))
+        tblobs.append((off, a))
+        off = (off + a.nbytes + 64 + 63) & ~63
+    size = off + 64
+    with open(dst, "wb") as f:
+        f.write(b"BNNPKG01" + struct.pack("<IHH4I4Q", 0x01020304, 1, 1, len(meta), len(tensors), len(paths), 0,
+                                          meta_off, tensor_off, path_off, size))
+        f.write(mb)
+        f.write(b"".join(tdesc))
+        f.write(b"".join(pdesc))
+        for b in pblobs:
+            f.write(b)
+        for o, a in tblobs:
+            f.write(b"\0" * (o - f.tell()))
+            f.write(a.tobytes())
+        f.write(b"\0" * (size - f.tell()))
+    return size
+
+
+def write_int8_package(dst, ir):
+    """Lowers v24_ir()'s result for the neon-int8 path and writes the package; returns (n_classes, emb_dim)."""
+    ops, vshape, logits, feat = ir
+    lw = _Int8Lowering(ops)
+    lw.vshape = vshape
+    lw.run()
+    ob, eb = lw.vbuf[logits], lw.vbuf[feat]
+    n_classes, emb_dim = lw.bufs[ob][3], lw.bufs[eb][3]
+    bufs = plan_slots(lw.bufs, lw.records, [ob, eb])
+    meta = [(f"src_nodes/{PATH}", "\n".join(lw.src))] + metadata(n_classes, emb_dim, labels_for(n_classes))
+    write_package(dst, meta, lw.tensors, [(PATH, 0, bufs, lw.records, 0, ob, eb)])
+    return n_classes, emb_dim
+
+
+def make_package(dst, seed=0, mini=False, n_classes=None):
+    """A synthetic v2.4-architecture neon-int8 package at dst; returns (n_classes, emb_dim)."""
+    nc = n_classes if n_classes is not None else (61 if mini else 6522)
+    return write_int8_package(dst, v24_ir(seed, nc, MINI_BLOCKS if mini else V24_BLOCKS))
+
+
+# ------------------------------------------------------------------ audio
+
+def audio(n, seed=0, n_samples=NSAMP, rate=SAMPLE_RATE):
+    """n windows [n][n_samples] float32: 0.1 N(0, 1) noise plus 1-3 linear chirps (1-12 kHz, amplitude 0.1-0.5,
+    random start and length) per window, window w seeded by (seed, w), clipped to [-1, 1)."""
+    out = np.empty((n, n_samples), np.float32)
+    t = np.arange(n_samples) / rate
+    for i in range(n):
+        rng = np.random.default_rng((seed, i))
+        x = 0.1 * rng.standard_normal(n_samples)
+        for _ in range(int(rng.integers(1, 4))):
+            f0, f1 = rng.uniform(1000.0, 12000.0, 2)
+            amp = rng.uniform(0.1, 0.5)
+            start = int(rng.integers(0, n_samples // 2))
+            length = int(rng.integers(n_samples // 8, n_samples - start))
+            tt = t[:length]
+            ph = 2 * np.pi * (f0 * tt + 0.5 * (f1 - f0) / max(tt[-1], 1e-9) * tt * tt)
+            x[start:start + length] += amp * np.sin(ph)
+        out[i] = np.clip(x, -1.0, np.nextafter(np.float32(1.0), np.float32(0.0)))
+    return out

@@ -1,0 +1,92 @@
+/* bnn oracle: a plain-C CPU restatement of the reference's BirdNET v2.4 neon-int8 hot path (TEST INFRASTRUCTURE).
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / --impl reference leg may load liboracle.so; the
+ * product library (libbnneon.so) never links or calls it. Every function restates one reference routine with the
+ * same per-element arithmetic (the NEON order of operations, FMA where the reference fuses, no FMA where it does
+ * not), so its outputs are the reference's outputs bit for bit wherever the reference's AArch64 arithmetic is
+ * emulated exactly (arm_emu.h). Layouts are the reference's (per window, NHWC fp32 activations, packed weights as
+ * stored in the .bnpk package).
+ *
+ * Parity pins: the int8 packing tests of the reference (tests/test_lower_units.py:139-156,
+ * tests/test_lower_s8.py:38-53) and packages written by the reference compiler (tests/golden). The per-op outputs
+ * have no reference fixtures (the reference ships none for PW_S8 / GEMV_S8 / DW3 / SE / FE_STFT2; its NEON build
+ * does not compile on x86): for those ops parity rests on this restatement. */
+#ifndef BNN_ORACLE_H
+#define BNN_ORACLE_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* elementwise helpers (src/gemm_f32.h, src/v24_fe.c, src/v24_f32.c:160) */
+float bnno_silu(float x);      /* silu_f32x4 / SILU_N_F32X4 */
+float bnno_sigmoid(float x);   /* sigmoid_f32x4 */
+float bnno_frecpe(float x);    /* FRECPE */
+float bnno_log2_acc(float x);  /* log2_acc_f32x4 */
+float bnno_exp2_acc(float x);  /* v24_fe.c exp2_acc */
+float bnno_expf(float x);      /* the host libm expf the reference calls (SE fc1) */
+
+/* s8n_quant_rows / s8n_quant_rows_gate (src/gemm_s8n.c:15-63): rows [0, M) of x (row stride ld) -> q [M][Kp] */
+void bnno_quant_rows(const float *x, int ld, int M, int K, int Kp, const float *gate, int8_t *q, float *sa, int32_t *za);
+
+/* int8 GEMM + epilogue (src/gemm_s8n.c:82-190) on quantized rows; w is the package tensor [Np/4][Kp/16][4][16].
+ * act: 0 none, 1 SiLU, 2 ReLU. opad/ow: padded output rows; rpad/rw: residual in a haloed buffer; res may be NULL. */
+void bnno_s8_gemm(const int8_t *q, const float *sa, const int32_t *za, int M, int N, int Kp, int Np, const int8_t *w,
+                  const float *sw, const int32_t *cs, const float *b, int act, float *out, int ldo, int ow, int opad,
+                  const float *res, int ldr, int rpad, int rw);
+
+/* PW_S8 run (src/rt_ops_s8n.c:119-134): halo zeroing of a padded output, quantization (optionally gated), GEMM */
+void bnno_pw_s8(const float *x, int lda, int M, int N, int K, int Kp, int Np, const float *gate, const int8_t *w,
+                const float *sw, const int32_t *cs, const float *b, int act, float *out, int ldo, int ow, int opad,
+                int out_h, const float *res, int ldr, int rpad, int rw, int8_t *q, float *sa, int32_t *za);
+
+/* DW3 (src/gemm_f32.c:214-440): depthwise 3x3 pad 1 stride s + SiLU + channel sums */
+void bnno_dw3(const float *xp, int H, int W, int C, int s, const float *w, const float *b, float *out, int Ho, int Wo,
+              float *chsum);
+
+/* SE_GATE (src/rt_ops_f32.c:314-325 = v24k32_se_fc1 + se_gate_range) */
+void bnno_se_gate(int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,
+                  const float *chsum, int P, float *gate);
+
+/* C0POOL (src/v24_f32.c:139-147, src/gemm_f32.c:60-70, :199-212): img [96][511][2] -> pin [48*128][48];
+ * w: fp32 panels [Np/8][Kp][8] (Np 24, Kp 64), b [>= 24] */
+void bnno_c0pool(const float *img, const float *w, const float *b, float *pin);
+
+/* POSTPC (src/v24_f32.c:245-266): X [24][192] -> feat [1024]; w: panels [128][1728][8], b [>= 1024] */
+void bnno_postpc(const float *X, const float *post_s, const float *post_b, const float *w, const float *b, float *feat);
+
+/* FE_STFT2 (src/v24_fe.c:127-224, src/fft_tab.h): pcm [144000] -> img [96][511][2] */
+typedef struct bnno_fe bnno_fe;
+bnno_fe *bnno_fe_new(const float *win1, const float *win2, const float *mel1, const float *mel2, float pow1,
+                     float pow2, const float bn_s[2], const float bn_b[2]);
+void bnno_fe_run(const bnno_fe *f, const float *pcm, float *img);
+void bnno_fe_free(bnno_fe *f);
+
+/* ---- a .bnpk package run on the CPU, window by window (the executor of src/rt_pkg.c:528-542) */
+typedef struct bnno_pkg bnno_pkg;
+/* path: the package; path_name: the package path to run ("neon-int8"). NULL on failure (err filled). */
+bnno_pkg *bnno_pkg_open(const char *path, const char *path_name, char *err, size_t errlen);
+void bnno_pkg_close(bnno_pkg *p);
+int bnno_pkg_n_ops(const bnno_pkg *p);
+int bnno_pkg_n_bufs(const bnno_pkg *p);
+int bnno_pkg_op_code(const bnno_pkg *p, int i);
+/* elements of buffer i (its descriptor's elems) and its dtype (0 f32, 1 f16, 2 i8, 3 i32) */
+long bnno_pkg_buf_elems(const bnno_pkg *p, int i, int *dtype);
+int bnno_pkg_out_elems(const bnno_pkg *p); /* n_classes (metadata) */
+int bnno_pkg_emb_elems(const bnno_pkg *p); /* emb_dim (metadata) */
+/* ops [op0, op1) on the buffers as they are (buffer 0 = pcm): a whole window is bnno_pkg_run_range(p, pcm, 0, n) */
+int bnno_pkg_run_range(bnno_pkg *p, const float *pcm, int op0, int op1);
+/* one window: out [n_classes], emb [emb_dim] (may be NULL) */
+int bnno_pkg_run(bnno_pkg *p, const float *pcm, float *out, float *emb);
+/* copy buffer i out of / into the executor (bytes = elems * dtype size) */
+int bnno_pkg_get_buf(const bnno_pkg *p, int i, void *dst, size_t bytes);
+int bnno_pkg_set_buf(bnno_pkg *p, int i, const void *src, size_t bytes);
+/* n windows [n][n_samples] on `threads` threads (each window independent): out [n][n_classes], emb [n][emb_dim] */
+int bnno_pkg_run_many(const char *path, const char *path_name, int n, const float *pcm, float *out, float *emb,
+                      int threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
