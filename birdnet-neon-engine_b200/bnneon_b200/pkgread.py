@@ -1,0 +1,44 @@
+"""A minimal reader of the .bnpk op list (python/bnneon/compiler/pkgfmt.py layout) for the op-level tests."""
+import struct
+
+# buffer arguments each kernel writes (the reference registry's outmask) and the ones that are the int8 path's row
+# scratch (q, sa, za), which the B200 runtime keeps in its own layout
+OUTMASK = {1: 0x2, 2: 0x2, 4: 0x6, 6: 0xE, 25: 0x2, 22: 0x3A, 23: 0x1E}
+SCRATCH = {22: (3, 4, 5), 23: (2, 3, 4), 6: (2, 3)}
+NAMES = {1: "FE_STFT2", 2: "C0POOL", 4: "DW3", 6: "POSTPC", 22: "PW_S8", 23: "GEMV_S8", 25: "SE_GATE"}
+
+
+def read_ops(path, path_name="neon-int8"):
+    """[(code, bufs, tensors, ints)] of the named path, and its buffer descriptors [(dtype, H, W, C, ld, halo, slot,
+    elems)]."""
+    with open(path, "rb") as f:
+        data = f.read()
+    _, _, n_paths, _ = struct.unpack_from("<4I", data, 16)
+    _, _, path_off, _ = struct.unpack_from("<4Q", data, 32)
+    for i in range(n_paths):
+        o = path_off + 72 * i
+        name = data[o:o + 24].rstrip(b"\0").decode()
+        if name != path_name:
+            continue
+        _, n_buf, n_ops, _, _, _, _, _ = struct.unpack_from("<8I", data, o + 24)
+        buf_off, ops_off = struct.unpack_from("<2Q", data, o + 56)
+        bufs = []
+        for b in range(n_buf):
+            v = struct.unpack_from("<8IQ", data, buf_off + 40 * b)
+            bufs.append((v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[8]))
+        ops, q = [], ops_off
+        for _ in range(n_ops):
+            code, rec, nb, nt, ni, _ = struct.unpack_from("<6H", data, q)
+            vals = struct.unpack_from(f"<{nb + nt + ni}i", data, q + 12)
+            ops.append((code, list(vals[:nb]), list(vals[nb:nb + nt]), list(vals[nb + nt:])))
+            q += rec
+        return ops, bufs
+    raise KeyError(path_name)
+
+
+def op_io(code, bl):
+    """(input buffer ids, output buffer ids) an op reads and writes, without the int8 row scratch."""
+    mask, scratch = OUTMASK[code], SCRATCH.get(code, ())
+    ins = [b for a, b in enumerate(bl) if b >= 0 and not (mask >> a & 1) and a not in scratch]
+    outs = [b for a, b in enumerate(bl) if b >= 0 and (mask >> a & 1) and a not in scratch]
+    return ins, outs

@@ -1,0 +1,98 @@
+/* Launchers of the sm_100a kernels (C ABI, device pointers, one CUDA stream each). Called by the host runtime
+ * (bnn_rt.c) and by the per-op entry points of include/bnneon_cuda.h. Every launcher returns 0 or a cudaError_t.
+ *
+ * Batched layout: a per-window buffer of the package (an activation, a vector) holds B windows at a fixed window
+ * stride (elements). Rows of a 1x1 conv are the Mw pixels of each window; the GEMM works on all B * Mw rows at
+ * once. */
+#ifndef BNN_KERNELS_H
+#define BNN_KERNELS_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *bnn_stream_t;
+
+/* device-side error word written by kernels whose bounded waits time out (0 = none) */
+enum { BNNK_ERR_NONE = 0, BNNK_ERR_TMA_WAIT = 1, BNNK_ERR_MMA_WAIT = 2, BNNK_ERR_EPI_WAIT = 3 };
+
+/* per device, once: the glibc expf table (computed on the host) and the FRECPE estimate table */
+int bnnk_device_init(void);
+
+/* ---- int8 1x1 conv / dense layer (PW_S8, GEMV_S8) */
+
+/* per-row dynamic quantization (s8n_quant_rows, optionally gated): rows r = w * Mw + m of x (window stride xws,
+ * row stride lda; gate [B][K] at window stride gws or NULL) -> q [rows][Kq] (Kq >= K, pads = zero point), sa, za */
+int bnnk_quant(int rows, int Mw, const float *x, long long xws, int lda, int K, int Kq, const float *gate,
+               long long gws, int8_t *q, float *sa, int32_t *za, bnn_stream_t st);
+
+/* The GEMM of one layer: weights [Nrows][Kq] int8 (row n = output channel, zero beyond N and K), q [rows_cap][Kq].
+ * The plan holds the TMA descriptors (opaque, 64-byte aligned) and the tiling. */
+typedef struct {
+  unsigned char tma_a[128] __attribute__((aligned(64)));
+  unsigned char tma_b[128] __attribute__((aligned(64)));
+  int kq, sw, nkb, stages, bn, n_tiles, n, np, tmem_cols;
+  unsigned int idesc;
+  size_t smem;
+} bnnk_gemm_plan;
+int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_cap, int kq, const int8_t *w, int n, int np);
+/* rows of the weight buffer the plan of a layer with np (padded) output channels reads: n_tiles * bn */
+int bnnk_gemm_weight_rows(int np);
+
+/* epilogue of PW_S8 (gemm_s8n.c:105-135): y = (float)(acc - za * cs) * (sw * sa) + b, act (0 none, 1 SiLU,
+ * 2 ReLU), + residual, stored at the padded row of each pixel (ow / opad) of each window */
+typedef struct {
+  int act;
+  float *out;
+  long long ows;
+  int ldo, ow, opad;
+  const float *res;
+  long long rws;
+  int ldr, rw, rpad;
+  const float *sw, *bias;
+  const int32_t *cs;
+} bnnk_epilogue;
+int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float *sa, const int32_t *za, const bnnk_epilogue *e,
+              int *err, bnn_stream_t st);
+
+/* ---- depthwise 3x3 + SiLU + channel sums (DW3): xp [B][(H+2)(W+2)][C] haloed, out [B][Ho Wo][C], chsum [B][C] */
+int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int C, int s, const float *w, const float *b,
+             float *out, long long ows, int Ho, int Wo, float *chsum, long long cws, bnn_stream_t st);
+
+/* ---- SE gate (SE_GATE): chsum [B][C] -> gate [B][C] */
+int bnnk_se_gate(int B, int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,
+                 const float *chsum, long long cws, int P, float *gate, long long gws, bnn_stream_t st);
+
+/* ---- c0 conv 4x8 s2 + ReLU + max|avg pool (C0POOL): img [B][96][511][2] -> pin [B][6144][48];
+ * wt: the weights k-major [64][24], b [24] */
+int bnnk_c0pool(int B, const float *img, long long iws, const float *wt, const float *b, float *pin, long long pws,
+                bnn_stream_t st);
+
+/* ---- post BN + ReLU + pc 3x3 conv + ReLU + mean (POSTPC): X [B][24][192] -> feat [B][1024];
+ * wt: pc weights k-major [1728][1024]; pcin: scratch [B][6][1728] */
+int bnnk_postpc(int B, const float *X, long long xws, const float *post_s, const float *post_b, const float *wt,
+                const float *b, float *pcin, float *feat, long long fws, bnn_stream_t st);
+
+/* ---- the v2.4 front end (FE_STFT2): pcm [B][144000] -> img [B][96][511][2] */
+typedef struct {
+  const float *win[2];        /* [N] */
+  const float *tw_re[2], *tw_im[2]; /* [M / 2] */
+  const float *pc[2], *ps[2]; /* [khi] */
+  const int *rev[2];          /* [M] */
+  const int *mel_off[2];      /* [97] */
+  const int *mel_k[2];
+  const float *mel_w[2];
+  int klo[2], khi[2];
+  float pw2[2], bn_s[2], bn_b[2];
+} bnnk_fe_tables;
+int bnnk_fe_stft2(int B, const float *pcm, long long pws, const bnnk_fe_tables *t, float *minmax, float *img,
+                  long long iws, bnn_stream_t st);
+
+/* ---- elementwise functions for the unit tests */
+int bnnk_test_fn(int fn, int n, const float *x, float *y, bnn_stream_t st);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,185 @@
+// Device arithmetic that reproduces the reference's AArch64 results bit for bit.
+//
+// Every floating-point step is an explicit round-to-nearest intrinsic (__fmul_rn, __fadd_rn, __fmaf_rn, ...) and the
+// translation units build with -fmad=false -ftz=false -prec-div=true -prec-sqrt=true, so nothing is contracted or
+// flushed behind our back.
+//   * FRECPE / FRECPS: the Arm ARM pseudocode (FPRecipEstimate, RecipEstimate, FPRecipStepFused) with the Linux FPCR
+//     defaults (FZ = 0, AH = 0): the reciprocal estimate and Newton step of the reference's SiLU and sigmoid
+//     (src/gemm_f32.h:87-118).
+//   * FMIN / FMAX: NaN-propagating (PTX min.NaN / max.NaN), as NEON vminq_f32 / vmaxq_f32.
+//   * FCVTNS: cvt.rni.s32.f32 saturates and maps NaN to 0, as NEON does.
+//   * glibc expf (the SE block's SiLU calls libm expf, src/v24_f32.c:160): the published table-driven algorithm of
+//     glibc >= 2.27 (ARM optimized-routines: k = round(x N / ln 2), N = 32, 2^(k/N) from a 32-entry table, a cubic in
+//     r for 2^(r/N), evaluated in double), with the products fused as the FMA build of glibc fuses them. The table is
+//     computed on the host from libm exp2 and uploaded once per device. Host tests compare this against libm expf.
+#pragma once
+#include <stdint.h>
+
+namespace bnn {
+
+// Per translation unit (the kernels build without relocatable device code, so each .cu file holds its own copy and
+// fills it in its *_tables_init): the glibc expf table and the FRECPE estimate table (est(256 + i) << 15).
+static __constant__ unsigned long long c_expf_tab[32];
+static __device__ uint32_t g_frecpe_lut[256];
+
+__device__ __forceinline__ float fmin_nan(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+// FCVTNS: nearest-even, saturating, NaN -> 0
+__device__ __forceinline__ int32_t cvtns(float x) {
+  int32_t r;
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+// FCVTZS: toward zero, saturating, NaN -> 0
+__device__ __forceinline__ int32_t cvtzs(float x) {
+  int32_t r;
+  asm("cvt.rzi.s32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+// glibc lrintf on AArch64 (nearest-even to 64 bits, saturating), then the C conversion to int32_t (modulo 2^32)
+__device__ __forceinline__ int32_t lrintf_i32(float x) {
+  long long r;
+  asm("cvt.rni.s64.f32 %0, %1;" : "=l"(r) : "f"(x));
+  return (int32_t)(uint32_t)(unsigned long long)r;
+}
+
+// RecipEstimate of the Arm ARM for a in [256, 512): ((2^19 / (2a + 1)) + 1) / 2
+__device__ __forceinline__ uint32_t recip_estimate(uint32_t a) {
+  uint32_t b = (1u << 19) / (2u * a + 1u);
+  return (b + 1u) >> 1;
+}
+
+// FRECPE (single precision), the whole pseudocode: special values, denormal inputs and outputs
+__device__ __forceinline__ float frecpe(float x) {
+  uint32_t u = __float_as_uint(x), sign = u & 0x80000000u;
+  uint32_t e = (u >> 23) & 0xffu, frac = u & 0x7fffffu;
+  if (e == 0xffu) return frac ? __uint_as_float(u | 0x400000u) : __uint_as_float(sign);
+  if (e == 0 && frac == 0) return __uint_as_float(sign | 0x7f800000u);
+  if (fabsf(x) < 0x1p-128f) return __uint_as_float(sign | 0x7f800000u);
+  int32_t ex = (int32_t)e;
+  uint32_t f = frac << 9;  // the pseudocode's 52-bit fraction, top 32 bits (bits 51..20)
+  if (ex == 0) {
+    if (!(f >> 31)) { ex = -1; f <<= 2; }
+    else f <<= 1;
+  }
+  uint32_t est = recip_estimate(256u | (f >> 24)) & 0xffu;
+  int32_t rexp = 253 - ex;
+  uint32_t m;
+  if (rexp > 0) m = est << 15;
+  else if (rexp == 0) m = (1u << 22) | (est << 14);
+  else { m = (1u << 21) | (est << 13); rexp = 0; }
+  return __uint_as_float(sign | ((uint32_t)rexp << 23) | m);
+}
+
+// FRECPE for a normal d in [1, 2^126) (the SiLU denominators): exponent 253 - e, 8-bit estimate from the table
+// (lut[i] = estimate(256 + i) << 15)
+__device__ __forceinline__ float frecpe_ge1(float d, const uint32_t *lut) {
+  uint32_t u = __float_as_uint(d);
+  return __uint_as_float((0x7e800000u - (u & 0x7f800000u)) | lut[(u >> 15) & 0xffu]);
+}
+
+// FRECPS(a, b) = 2 - a * b fused (finite operands: the infinity x zero case cannot arise here)
+__device__ __forceinline__ float frecps(float a, float b) { return __fmaf_rn(-a, b, 2.f); }
+
+// silu_f32x4 / SILU_N_F32X4 (src/gemm_f32.h:102-144)
+template <bool kLut>
+__device__ __forceinline__ float silu(float x, const uint32_t *lut) {
+  const float magic = 0x1.8p+23f;
+  float t = __fmul_rn(x, -0x1.715476p+0f);
+  t = fmin_nan(fmax_nan(t, -60.f), 60.f);
+  float tm = __fadd_rn(t, magic);
+  float f = __fsub_rn(t, __fsub_rn(tm, magic));
+  float p = __fmaf_rn(0x1.5d87fep-10f, f, 0x1.3b2ab6p-7f);
+  p = __fmaf_rn(p, f, 0x1.c6b08ep-5f);
+  p = __fmaf_rn(p, f, 0x1.ebfbep-3f);
+  p = __fmaf_rn(p, f, 0x1.62e43p-1f);
+  p = __fmaf_rn(p, f, 1.0f);
+  uint32_t ni = __float_as_uint(tm) << 23;
+  float d = __fadd_rn(1.f, __uint_as_float(__float_as_uint(p) + ni));
+  float r = kLut ? frecpe_ge1(d, lut) : frecpe(d);
+  r = __fmul_rn(r, frecps(d, r));
+  return __fmul_rn(x, r);
+}
+
+// exp2_f32x4 (src/gemm_f32.h:74-85)
+__device__ __forceinline__ float exp2_poly(float t) {
+  t = fmin_nan(fmax_nan(t, -126.f), 126.f);
+  float n = rintf(t), f = __fsub_rn(t, n);
+  float p = 0x1.430912p-13f;
+  p = __fmaf_rn(p, f, 0x1.5d87fep-10f);
+  p = __fmaf_rn(p, f, 0x1.3b2ab6p-7f);
+  p = __fmaf_rn(p, f, 0x1.c6b08ep-5f);
+  p = __fmaf_rn(p, f, 0x1.ebfbep-3f);
+  p = __fmaf_rn(p, f, 0x1.62e43p-1f);
+  p = __fmaf_rn(p, f, 1.f);
+  return __uint_as_float(__float_as_uint(p) + ((uint32_t)cvtzs(n) << 23));
+}
+// sigmoid_f32x4 (src/gemm_f32.h:93-96): FRECPE + two fused Newton steps
+__device__ __forceinline__ float sigmoid(float x) {
+  float d = __fadd_rn(1.f, exp2_poly(__fmul_rn(x, -0x1.715476p+0f)));
+  float r = frecpe(d);
+  r = __fmul_rn(r, frecps(d, r));
+  r = __fmul_rn(r, frecps(d, r));
+  return r;
+}
+
+// log2_acc_f32x4 (src/gemm_f32.h:57-71)
+__device__ __forceinline__ float log2_acc(float x) {
+  uint32_t xi = __float_as_uint(x);
+  int32_t e = ((int32_t)(xi - 0x3f3504f3u)) >> 23;
+  float z = __fsub_rn(__uint_as_float(xi - ((uint32_t)e << 23)), 1.f);
+  float p = __fmaf_rn(z, 0x1.f0a97ep-4f, -0x1.a6c552p-3f);
+  p = __fmaf_rn(z, p, 0x1.bcc44cp-3f);
+  p = __fmaf_rn(z, p, -0x1.e9aef8p-3f);
+  p = __fmaf_rn(z, p, 0x1.26a67p-2f);
+  p = __fmaf_rn(z, p, -0x1.7159ccp-2f);
+  p = __fmaf_rn(z, p, 0x1.ec75e6p-2f);
+  p = __fmaf_rn(z, p, -0x1.715476p-1f);
+  p = __fmaf_rn(z, p, 0x1.715474p+0f);
+  return __fmaf_rn(z, p, __int2float_rn(e));
+}
+// exp2_acc (src/v24_fe.c:109-123): exp2_poly without the upper clamp
+__device__ __forceinline__ float exp2_acc(float t) {
+  t = fmax_nan(t, -126.f);
+  float n = rintf(t), f = __fsub_rn(t, n);
+  float p = 0x1.430912p-13f;
+  p = __fmaf_rn(p, f, 0x1.5d87fep-10f);
+  p = __fmaf_rn(p, f, 0x1.3b2ab6p-7f);
+  p = __fmaf_rn(p, f, 0x1.c6b08ep-5f);
+  p = __fmaf_rn(p, f, 0x1.ebfbep-3f);
+  p = __fmaf_rn(p, f, 0x1.62e43p-1f);
+  p = __fmaf_rn(p, f, 1.f);
+  return __uint_as_float(__float_as_uint(p) + ((uint32_t)cvtzs(n) << 23));
+}
+
+// glibc expf (see the header comment). tab[i] = bits(2^(i/32)) - (i << 47).
+__device__ __forceinline__ float glibc_expf(float x, const unsigned long long *tab) {
+  const double inv_ln2_n = 0x1.71547652b82fep+0 * 32, shift = 0x1.8p+52;
+  const double c0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32, c1 = 0x1.ebfce50fac4f3p-3 / 32 / 32, c2 = 0x1.62e42ff0c52d6p-1 / 32;
+  uint32_t ux = __float_as_uint(x), abstop = (ux >> 20) & 0x7ffu;
+  if (abstop >= 0x42bu) {  // |x| >= 88 (top 12 bits of 88.0f), infinities and NaN
+    if (ux == 0xff800000u) return 0.f;
+    if (abstop >= 0x7f8u) return __fadd_rn(x, x);
+    if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);
+    if (x < -0x1.9fe368p6f) return 0.f;
+  }
+  double xd = (double)x;
+  double kd = __fma_rn(inv_ln2_n, xd, shift);
+  unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
+  kd = __dsub_rn(kd, shift);
+  double r = __fma_rn(inv_ln2_n, xd, -kd);
+  double s = __longlong_as_double((long long)(tab[ki & 31] + (ki << 47)));
+  double z = __fma_rn(c0, r, c1), r2 = __dmul_rn(r, r), y = __fma_rn(c2, r, 1.0);
+  y = __fma_rn(z, r2, y);
+  return __double2float_rn(__dmul_rn(y, s));
+}
+
+}  // namespace bnn

@@ -1,0 +1,515 @@
+// int8 1x1 conv / dense layer for sm_100a: the per-row dynamic quantizer and the tcgen05 kind::i8 GEMM with the
+// fused dequant / activation / residual / padded-store epilogue.
+//
+// Reference: src/gemm_s8n.c (s8n_quant_rows :15-63, acc4x4 / tile4x4 / s8n_gemm_range :82-190) driven by PW_S8 and
+// GEMV_S8 (src/rt_ops_s8n.c:92-158). The int32 sums are exact in both (|q|, |w| <= 127, K <= 4096), so the tensor
+// cores' summation order cannot change them; everything after the sum repeats the reference's fp32 steps.
+//
+// GEMM design: one CTA per 128-row x BN-column tile. Warp 0 lane 0 streams K blocks of A (the quantized rows) and B
+// (the weights, [Nrows][Kq] K-major) into a ring of shared-memory stages with TMA (2-D tiled loads, swizzled by the
+// K-block width: 32, 64 or 128 bytes; no multicast), warp 1 lane 0 issues tcgen05.mma.cta_group::1.kind::i8 (M 128,
+// N = BN, K 32 per instruction) into a TMEM accumulator of BN int32 columns and releases each stage with
+// tcgen05.commit, and all four warps then read their 32 TMEM lanes (= rows) with tcgen05.ld and run the epilogue.
+// Every mbarrier wait is bounded by a %globaltimer deadline; a timeout sets the error word and the CTA still frees
+// its TMEM before it returns.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "bnn_kernels.h"
+#include "emu.cuh"
+
+namespace bnn {
+
+// ------------------------------------------------------------------ quantizer
+
+// Quantizes one row held by a group of L lanes (each lane 4 consecutive k per step). K % 4 == 0 and lda % 4 == 0
+// (every v2.4 layer); the general case runs bnnk_quant_scalar.
+template <int L>
+__global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__restrict__ x, long long xws, int lda,
+                                               int K, int Kq, const float *__restrict__ gate, long long gws,
+                                               int8_t *__restrict__ q, float *__restrict__ sa,
+                                               int32_t *__restrict__ za) {
+  const int lane = threadIdx.x % L;
+  const int row = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) / L);
+  const bool valid = row < rows;
+  const int r = valid ? row : rows - 1;
+  const int w = r / Mw, m = r - w * Mw;
+  const float *xr = x + w * xws + (long long)m * lda;
+  const float *gr = gate ? gate + w * gws : nullptr;
+  const int K4 = K / 4;
+  float lo = __int_as_float(0x7f800000), hi = __int_as_float(0xff800000);
+  for (int j = lane; j < K4; j += L) {
+    float4 v = *reinterpret_cast<const float4 *>(xr + 4 * j);
+    if (gr) {
+      float4 g = *reinterpret_cast<const float4 *>(gr + 4 * j);
+      v.x = __fmul_rn(v.x, g.x); v.y = __fmul_rn(v.y, g.y); v.z = __fmul_rn(v.z, g.z); v.w = __fmul_rn(v.w, g.w);
+    }
+    lo = fmin_nan(lo, fmin_nan(fmin_nan(v.x, v.y), fmin_nan(v.z, v.w)));
+    hi = fmax_nan(hi, fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w)));
+  }
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) {
+    lo = fmin_nan(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = fmax_nan(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  float inv, s;
+  int32_t z;
+  const float d = __fsub_rn(hi, lo);
+  if (!(d > __fmul_rn(1e-30f, fmaxf(fabsf(hi), fabsf(lo)))) || !(d > 0.f)) {  // constant row: symmetric
+    float a = fmaxf(fabsf(hi), 1e-30f);
+    inv = __fdiv_rn(127.f, a); z = 0; s = __fdiv_rn(a, 127.f);
+  } else {
+    inv = __fdiv_rn(254.f, d);
+    z = (int32_t)(0u - 127u - (uint32_t)lrintf_i32(__fmul_rn(lo, inv)));
+    s = __fdiv_rn(d, 254.f);
+  }
+  if (valid && lane == 0) { sa[row] = s; za[row] = z; }
+  const int K8 = K & ~7;
+  int8_t *qr = q + (long long)r * Kq;
+  for (int j = lane; 4 * j < Kq; j += L) {
+    const int k = 4 * j;
+    uint32_t packed;
+    if (k < K) {
+      float4 v = *reinterpret_cast<const float4 *>(xr + k);
+      if (gr) {
+        float4 g = *reinterpret_cast<const float4 *>(gr + k);
+        v.x = __fmul_rn(v.x, g.x); v.y = __fmul_rn(v.y, g.y); v.z = __fmul_rn(v.z, g.z); v.w = __fmul_rn(v.w, g.w);
+      }
+      const float e[4] = {v.x, v.y, v.z, v.w};
+      packed = 0;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        float t = __fmul_rn(e[i], inv);
+        int32_t qi = (int32_t)((uint32_t)(k < K8 ? cvtns(t) : lrintf_i32(t)) + (uint32_t)z);
+        qi = qi < -127 ? -127 : qi > 127 ? 127 : qi;
+        packed |= ((uint32_t)qi & 0xffu) << (8 * i);
+      }
+    } else {
+      packed = ((uint32_t)z & 0xffu) * 0x01010101u;
+    }
+    if (valid) *reinterpret_cast<uint32_t *>(qr + k) = packed;
+  }
+}
+
+// The general form (any K, any lda): one thread per row, the reference's loops as written.
+__global__ void k_quant_scalar(int rows, int Mw, const float *__restrict__ x, long long xws, int lda, int K, int Kq,
+                               const float *__restrict__ gate, long long gws, int8_t *__restrict__ q,
+                               float *__restrict__ sa, int32_t *__restrict__ za) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const int w = row / Mw, m = row - w * Mw;
+  const float *xr = x + w * xws + (long long)m * lda;
+  const float *gr = gate ? gate + w * gws : nullptr;
+  auto val = [&](int k) { return gr ? __fmul_rn(xr[k], gr[k]) : xr[k]; };
+  float lo = __int_as_float(0x7f800000), hi = __int_as_float(0xff800000);
+  int k = 0;
+  for (; k + 4 <= K; k++) { lo = fmin_nan(lo, val(k)); hi = fmax_nan(hi, val(k)); }
+  for (; k < K; k++) { lo = fminf(lo, val(k)); hi = fmaxf(hi, val(k)); }
+  float inv, s;
+  int32_t z;
+  const float d = __fsub_rn(hi, lo);
+  if (!(d > __fmul_rn(1e-30f, fmaxf(fabsf(hi), fabsf(lo)))) || !(d > 0.f)) {
+    float a = fmaxf(fabsf(hi), 1e-30f);
+    inv = __fdiv_rn(127.f, a); z = 0; s = __fdiv_rn(a, 127.f);
+  } else {
+    inv = __fdiv_rn(254.f, d);
+    z = (int32_t)(0u - 127u - (uint32_t)lrintf_i32(__fmul_rn(lo, inv)));
+    s = __fdiv_rn(d, 254.f);
+  }
+  sa[row] = s;
+  za[row] = z;
+  int8_t *qr = q + (long long)row * Kq;
+  const int K8 = K & ~7;
+  for (k = 0; k < K; k++) {
+    float t = __fmul_rn(val(k), inv);
+    int32_t qi = (int32_t)((uint32_t)(k < K8 ? cvtns(t) : lrintf_i32(t)) + (uint32_t)z);
+    qr[k] = (int8_t)(qi < -127 ? -127 : qi > 127 ? 127 : qi);
+  }
+  for (; k < Kq; k++) qr[k] = (int8_t)z;
+}
+
+// ------------------------------------------------------------------ tcgen05 GEMM
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far above any legitimate wait
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// bounded wait for the phase with the given parity to complete; false on timeout
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = gtimer();
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (gtimer() - t0 > kWaitNs) return false;
+  }
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+// shared-memory matrix descriptor of a K-major tile with rows of SW bytes swizzled by SW (8-row groups of 8 * SW
+// bytes); version 1 (sm_100), base offset 0 (tiles are aligned to the swizzle repeat)
+template <int SW>
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  constexpr uint64_t layout = SW == 128 ? 2 : SW == 64 ? 4 : 6;
+  return (uint64_t)((addr & 0x3ffffu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)((8 * SW) >> 4) << 32) |
+         ((uint64_t)1 << 46) | (layout << 61);
+}
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int32_t v[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = (int32_t)r[i];
+}
+
+struct GemmArgs {
+  int rows, Mw, nkb, stages, bn, np, tmem_cols;
+  uint32_t idesc;
+  const float *sa;
+  const int32_t *za;
+  bnnk_epilogue e;
+  int *err;
+};
+
+__device__ __forceinline__ long long padded_row(int m, int w, int pad) {
+  return pad ? (long long)((m / w) + pad) * (w + 2 * pad) + (m % w) + pad : (long long)m;
+}
+
+template <int SW>
+__global__ void __launch_bounds__(128, 1) k_gemm_s8(const __grid_constant__ CUtensorMap tma_a,
+                                                    const __grid_constant__ CUtensorMap tma_b, const GemmArgs a) {
+  extern __shared__ uint8_t dsmem[];
+  __shared__ __align__(8) unsigned long long bar_full[8], bar_empty[8], bar_done;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+  __shared__ float s_sw[256], s_b[256];
+  __shared__ int32_t s_cs[256];
+  __shared__ uint32_t s_lut[256];
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m0 = blockIdx.x * 128, n0 = blockIdx.y * a.bn;
+  const uint32_t base = (smem_u32(dsmem) + 1023u) & ~1023u;
+  const uint32_t a_bytes = 128u * SW, stage_bytes = (128u + a.bn) * SW;
+
+  for (int i = threadIdx.x; i < a.bn; i += 128) {
+    const int n = n0 + i;
+    s_sw[i] = a.e.sw[n];
+    s_b[i] = a.e.bias[n];
+    s_cs[i] = a.e.cs[n];
+  }
+  for (int i = threadIdx.x; i < 256; i += 128) s_lut[i] = g_frecpe_lut[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.stages; s++) { mbar_init(smem_u32(&bar_full[s]), 1); mbar_init(smem_u32(&bar_empty[s]), 1); }
+    mbar_init(smem_u32(&bar_done), 1);
+    abort_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(a.tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0 && lane == 0) {  // TMA producer
+    for (int kb = 0; kb < a.nkb; kb++) {
+      const int s = kb % a.stages;
+      if (kb >= a.stages && !mbar_wait(smem_u32(&bar_empty[s]), ((kb / a.stages) - 1) & 1)) {
+        atomicExch(a.err, BNNK_ERR_TMA_WAIT);
+        abort_s = 1;
+        break;
+      }
+      const uint32_t st = base + s * stage_bytes, bar = smem_u32(&bar_full[s]);
+      mbar_expect_tx(bar, stage_bytes);
+      tma_load_2d(st, &tma_a, bar, kb * SW, m0);
+      tma_load_2d(st + a_bytes, &tma_b, bar, kb * SW, n0);
+    }
+  } else if (warp == 1 && lane == 0) {  // MMA issuer
+    bool ok = true;
+    for (int kb = 0; kb < a.nkb && ok; kb++) {
+      const int s = kb % a.stages;
+      if (!mbar_wait(smem_u32(&bar_full[s]), (kb / a.stages) & 1)) {
+        atomicExch(a.err, BNNK_ERR_MMA_WAIT);
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t st = base + s * stage_bytes;
+#pragma unroll
+      for (int kk = 0; kk < SW / 32; kk++)
+        mma_i8(tmem, smem_desc<SW>(st + kk * 32), smem_desc<SW>(st + a_bytes + kk * 32), a.idesc, (kb | kk) != 0);
+      mma_commit(smem_u32(&bar_empty[s]));
+    }
+    mma_commit(smem_u32(&bar_done));  // arrives once every MMA issued above has completed
+  }
+  __syncwarp();
+
+  // epilogue: thread = one row of the tile (TMEM lane 32 * warp + lane)
+  const bool ready = mbar_wait(smem_u32(&bar_done), 0);
+  if (!ready) atomicExch(a.err, BNNK_ERR_EPI_WAIT);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const int row = m0 + warp * 32 + lane;
+  const bool live = ready && row < a.rows && !abort_s;
+  int w = 0, mm = 0;
+  float sa = 0.f;
+  int32_t za = 0;
+  if (live) {
+    w = row / a.Mw;
+    mm = row - w * a.Mw;
+    sa = a.sa[row];
+    za = a.za[row];
+  }
+  float *orow = a.e.out + (long long)w * a.e.ows + padded_row(mm, a.e.ow, a.e.opad) * a.e.ldo + n0;
+  const float *rrow = a.e.res ? a.e.res + (long long)w * a.e.rws + padded_row(mm, a.e.rw, a.e.rpad) * a.e.ldr + n0
+                              : nullptr;
+  const int ncols = min(a.bn, a.np - n0);
+  for (int c0 = 0; c0 < a.bn; c0 += 16) {
+    int32_t acc[16];
+    if (ready) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, acc);
+    if (!live || c0 >= ncols) continue;
+    float y[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const int c = c0 + j;
+      // deq4 (gemm_s8n.c:105-114): int32 wrap, exact int -> fp32, sw * sa first, multiply then add (no FMA)
+      float f = __int2float_rn((int32_t)((uint32_t)acc[j] - (uint32_t)s_cs[c] * (uint32_t)za));
+      float v = __fadd_rn(__fmul_rn(f, __fmul_rn(s_sw[c], sa)), s_b[c]);
+      if (a.e.act == 1) v = silu<true>(v, s_lut);
+      else if (a.e.act == 2) v = (v > 0.f || v != v) ? v : 0.f;  // FMAX(v, +0): NaN stays NaN, -0 -> +0
+      y[j] = v;
+    }
+    if (c0 + 16 <= ncols) {
+      if (rrow) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+          float4 r4 = *reinterpret_cast<const float4 *>(rrow + c0 + j);
+          y[j] = __fadd_rn(y[j], r4.x); y[j + 1] = __fadd_rn(y[j + 1], r4.y);
+          y[j + 2] = __fadd_rn(y[j + 2], r4.z); y[j + 3] = __fadd_rn(y[j + 3], r4.w);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4 *>(orow + c0 + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+    } else {
+      for (int j = 0; j < 16 && c0 + j < ncols; j++) orow[c0 + j] = rrow ? __fadd_rn(y[j], rrow[c0 + j]) : y[j];
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols));
+}
+
+// ------------------------------------------------------------------ elementwise test kernel
+
+__global__ void k_test_fn(int fn, int n, const float *x, float *y) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float v = x[i], r;
+  switch (fn) {
+  case 0: r = silu<false>(v, nullptr); break;
+  case 1: r = silu<true>(v, g_frecpe_lut); break;
+  case 2: r = sigmoid(v); break;
+  case 3: r = frecpe(v); break;
+  case 4: r = log2_acc(v); break;
+  case 5: r = exp2_acc(v); break;
+  case 6: r = glibc_expf(v, c_expf_tab); break;
+  default: r = 0.f;
+  }
+  y[i] = r;
+}
+
+}  // namespace bnn
+
+using namespace bnn;
+
+// ------------------------------------------------------------------ launchers
+
+extern "C" int bnnk_fp32_tables_init(const unsigned long long *tab, const uint32_t *lut);
+
+extern "C" int bnnk_device_init(void) {
+  unsigned long long tab[32];
+  for (int i = 0; i < 32; i++) {
+    double v = exp2((double)i / 32);  // host libm, as glibc's table
+    unsigned long long u;
+    memcpy(&u, &v, 8);
+    tab[i] = u - ((unsigned long long)i << 47);
+  }
+  cudaError_t e = cudaMemcpyToSymbol(c_expf_tab, tab, sizeof tab);
+  if (e) return e;
+  uint32_t lut[256];
+  for (uint32_t i = 0; i < 256; i++) {
+    uint32_t a = 256 + i, b = (1u << 19) / (2 * a + 1);
+    lut[i] = (((b + 1) >> 1) & 0xffu) << 15;
+  }
+  e = cudaMemcpyToSymbol(g_frecpe_lut, lut, sizeof lut);
+  if (e) return e;
+  return bnnk_fp32_tables_init(tab, lut);
+}
+
+extern "C" int bnnk_quant(int rows, int Mw, const float *x, long long xws, int lda, int K, int Kq, const float *gate,
+                          long long gws, int8_t *q, float *sa, int32_t *za, bnn_stream_t st) {
+  if (rows <= 0) return 0;
+  const bool vec = K % 4 == 0 && lda % 4 == 0 && xws % 4 == 0 && (!gate || gws % 4 == 0) && Kq % 4 == 0 &&
+                   ((uintptr_t)x & 15) == 0 && (!gate || ((uintptr_t)gate & 15) == 0);
+  if (!vec) {
+    k_quant_scalar<<<(rows + 127) / 128, 128, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za);
+  } else if (K <= 128) {
+    const int per = 256 / 8;
+    k_quant<8><<<(rows + per - 1) / per, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za);
+  } else {
+    const int per = 256 / 32;
+    k_quant<32><<<(rows + per - 1) / per, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za);
+  }
+  return cudaGetLastError();
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode(void) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  }
+  return fn;
+}
+
+static int encode_2d(void *map, const void *base, int inner, int rows, int box_inner, int box_rows, int sw) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode();
+  if (!enc) return cudaErrorNotSupported;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)inner};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUtensorMapSwizzle swz = sw == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : sw == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                                             : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = enc((CUtensorMap *)map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box,
+                   es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : cudaErrorInvalidValue;
+}
+
+// N tiling: as few tiles of at most 256 columns as possible, equal widths rounded up to 16
+static void n_tiling(int np, int *n_tiles, int *bn) {
+  const int n16 = (np + 15) & ~15;
+  *n_tiles = (n16 + 255) / 256;
+  const int b = (n16 + *n_tiles - 1) / *n_tiles;
+  *bn = (b + 15) & ~15;
+}
+
+extern "C" int bnnk_gemm_weight_rows(int np) {
+  int t, bn;
+  n_tiling(np, &t, &bn);
+  return t * bn;
+}
+
+extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_cap, int kq, const int8_t *w, int n,
+                                   int np) {
+  memset(p, 0, sizeof *p);
+  if (kq % 32 || rows_cap <= 0 || n <= 0 || np < n) return cudaErrorInvalidValue;
+  p->kq = kq;
+  p->sw = kq % 128 == 0 ? 128 : kq % 64 == 0 ? 64 : 32;
+  p->nkb = kq / p->sw;
+  p->n = n;
+  p->np = np;
+  n_tiling(np, &p->n_tiles, &p->bn);
+  p->tmem_cols = p->bn <= 32 ? 32 : p->bn <= 64 ? 64 : p->bn <= 128 ? 128 : 256;
+  p->stages = p->nkb < 4 ? p->nkb : 4;
+  p->smem = (size_t)p->stages * (128 + p->bn) * p->sw + 1024;
+  // at most 512 / tmem_cols CTAs per SM may hold TMEM at once: ask for enough shared memory that no more fit
+  const int max_ctas = 512 / p->tmem_cols;
+  if (max_ctas < 16) {
+    const size_t need = 233472 / (size_t)(max_ctas + 1) + 1024;
+    if (p->smem < need) p->smem = need;
+  }
+  p->idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p->bn >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+  const int wrows = p->n_tiles * p->bn;  // the weight buffer holds n_tiles * bn rows (zero beyond n)
+  int e = encode_2d(p->tma_a, q, kq, rows_cap, p->sw, 128, p->sw);
+  if (!e) e = encode_2d(p->tma_b, w, kq, wrows, p->sw, p->bn, p->sw);
+  return e;
+}
+
+template <int SW>
+static int launch_gemm(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_gemm_s8<SW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
+  dim3 grid((a.rows + 127) / 128, p->n_tiles);
+  k_gemm_s8<SW><<<grid, 128, p->smem, st>>>(*(const CUtensorMap *)p->tma_a, *(const CUtensorMap *)p->tma_b, a);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float *sa, const int32_t *za,
+                         const bnnk_epilogue *e, int *err, bnn_stream_t st) {
+  if (rows <= 0) return 0;
+  GemmArgs a;
+  a.rows = rows;
+  a.Mw = Mw;
+  a.nkb = p->nkb;
+  a.stages = p->stages;
+  a.bn = p->bn;
+  a.np = p->np;
+  a.tmem_cols = p->tmem_cols;
+  a.idesc = p->idesc;
+  a.sa = sa;
+  a.za = za;
+  a.e = *e;
+  a.err = err;
+  switch (p->sw) {
+  case 128: return launch_gemm<128>(p, a, st);
+  case 64: return launch_gemm<64>(p, a, st);
+  default: return launch_gemm<32>(p, a, st);
+  }
+}
+
+extern "C" int bnnk_test_fn(int fn, int n, const float *x, float *y, bnn_stream_t st) {
+  if (n <= 0) return 0;
+  k_test_fn<<<(n + 255) / 256, 256, 0, st>>>(fn, n, x, y);
+  return cudaGetLastError();
+}

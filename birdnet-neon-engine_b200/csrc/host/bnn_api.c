@@ -1,0 +1,697 @@
+/* The public C API (include/bnneon.h, include/bnneon_cuda.h) over the B200 package runtime.
+ *
+ * Replaces src/bnneon.c:30-387 of the reference for compiled packages: probe / metadata / labels answer from the
+ * package exactly as there (the same keys, the same license-key alias, the same struct_size handshake and error
+ * texts); bnn_init picks the package path by name for the mode and builds the GPU context; bnn_infer runs the op list
+ * on the GPU. Legacy .bn24 / .bnv3 files (the hand-written NEON engines) are refused: there is no GPU engine for
+ * them. */
+#define _GNU_SOURCE
+#include <pthread.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <cuda_runtime_api.h>
+
+#include "../../../include/bnneon_cuda.h"
+#include "bnn_internal.h"
+
+static __thread char g_err[512];
+static __thread int g_kind;
+
+void bnn_set_error(int kind, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  g_kind = kind;
+}
+#define ERR(kind, ...) bnn_set_error((kind), __VA_ARGS__)
+
+const char *bnn_last_error(void) { return g_err; }
+int bnn_last_error_kind(void) { return g_kind; }
+int bnn_api_version(void) { return BNN_API_VERSION; }
+
+int bnn_cpu_supported(int model) {
+  return model == BNN_MODEL_V24 || model == BNN_MODEL_PERCH_V2 || model == BNN_MODEL_BAT_V24;
+}
+
+static const char *base_name(const char *path) {
+  const char *s = strrchr(path, '/');
+  return s ? s + 1 : path;
+}
+
+/* the package paths a mode names (src/bnneon.c:73-78: mode -> path name, precision text) */
+static const struct { int mode; const char *name, *precision; } PATHS[] = {
+    {BNN_MODE_FP16, "neon-fp16", "fp16"},
+    {BNN_MODE_INT8, "neon-int8", "int8 GEMMs, fp32 elsewhere"},
+    {BNN_MODE_FP32, "neon-fp32", "fp32"},
+};
+
+/* 1 when every op of path i has a GPU kernel here (the int8 path's ops, variant 0) */
+static int path_runs_here(const bnn_pkg *p, int i) {
+  static const int codes[] = {BNN_OP_FE_STFT2, BNN_OP_C0POOL, BNN_OP_PW_S8, BNN_OP_DW3, BNN_OP_SE_GATE,
+                              BNN_OP_POSTPC, BNN_OP_GEMV_S8};
+  const bnn_path_rec *d = &p->paths[i];
+  const uint8_t *q = p->map + d->ops_off, *end = q + d->ops_bytes;
+  for (uint32_t k = 0; k < d->n_ops; k++) {
+    if (q + 12 > end) return 0;
+    uint16_t h[6];
+    memcpy(h, q, 12);
+    int ok = 0;
+    for (size_t j = 0; j < sizeof codes / sizeof codes[0]; j++) ok |= h[0] == codes[j];
+    if (!ok || h[1] < 12) return 0;
+    q += h[1];
+  }
+  return 1;
+}
+
+/* the first path (paths are stored fastest first) this library runs; want: a path name, "" = any */
+static int pick_path(const bnn_pkg *p, const char *want) {
+  for (uint32_t i = 0; i < p->n_paths; i++) {
+    if (want[0] && strncmp(p->paths[i].name, want, sizeof p->paths[i].name)) continue;
+    if (path_runs_here(p, (int)i)) return (int)i;
+  }
+  return -1;
+}
+
+static void no_path_error(const char *path, const bnn_pkg *p, const char *want) {
+  char list[256] = "";
+  size_t k = 0;
+  int present = 0;
+  for (uint32_t i = 0; i < p->n_paths && k + 64 < sizeof list; i++) {
+    if (want[0] && !strncmp(p->paths[i].name, want, 24)) present = 1;
+    k += (size_t)snprintf(list + k, sizeof list - k, "%s%.24s", i ? ", " : "", p->paths[i].name);
+  }
+  char id[64] = "";
+  bnn_meta_str(p, "model_id", id, sizeof id);
+  if (want[0] && !present)
+    ERR(BNN_ERR_CPU, "%s: path %s is not in this package (it has: %s); hint: use mode 0 to let the library pick, or a "
+        "package of this model compiled for %s (%s-%s.bnpk)", path, want, list, want, id[0] ? id : "<model_id>", want);
+  else
+    ERR(BNN_ERR_CPU, "%s: this GPU library runs none of the package's paths%s%s (it has: %s; B200 kernels exist for the "
+        "neon-int8 path); hint: use the neon-int8 package of this model (%s-neon-int8.bnpk) or compile one with "
+        "--paths neon-int8", path, want[0] ? " named " : "", want, list, id[0] ? id : "<model_id>");
+}
+
+static void pkg_info(const bnn_pkg *p, int pi, bnn_info *info) {
+  int64_t v;
+  double x;
+#define I_(key, fld) do { if (!bnn_meta_i64(p, key, &v)) info->fld = (int)v; } while (0)
+  I_("family", model); I_("sample_rate", sample_rate); I_("n_samples", n_samples); I_("hop_samples", hop_samples);
+  I_("n_classes", n_classes); I_("post", post); I_("emb_dim", emb_dim);
+#undef I_
+  info->format_version = p->version;
+  info->output_kind = BNN_OUT_LOGITS;
+  info->logit_scale = bnn_meta_f64(p, "logit_scale", &x) ? 1.f : (float)x;
+  char sha[40];
+  if (bnn_meta_str(p, "labels_sha256", sha, sizeof sha) == 32) { memcpy(info->labels_sha256, sha, 32); info->has_labels_sha = 1; }
+  bnn_meta_str(p, "model_id", info->model_id, sizeof info->model_id);
+  if (pi >= 0) snprintf(info->path, sizeof info->path, "%.24s", p->paths[pi].name);
+}
+
+static void copy_info(bnn_info *dst, const bnn_info *src) {
+  uint32_t n = dst->struct_size;
+  if (n > sizeof *src) n = sizeof *src;
+  bnn_info tmp = *src;
+  tmp.struct_size = n;
+  memcpy(dst, &tmp, n);
+}
+
+/* header / metadata of a weights file; keep: receives the open package */
+static int probe_full(const char *path, bnn_info *info, bnn_pkg **keep) {
+  memset(info, 0, sizeof *info);
+  info->struct_size = sizeof *info;
+  info->logit_scale = 1.f;
+  info->precision = "";
+  FILE *f = fopen(path, "rb");
+  if (!f) { ERR(BNN_ERR_PACKAGE, "cannot open %s; hint: check the path and permissions", path); return -1; }
+  char magic[8];
+  const int ok = fread(magic, 1, 8, f) == 8;
+  fclose(f);
+  if (!ok) { ERR(BNN_ERR_PACKAGE, "%s: shorter than 8 bytes; hint: incomplete download or the wrong file", path); return -1; }
+  if (!memcmp(magic, "BNNPKG01", 8)) {
+    bnn_pkg *p = bnn_pkg_open(path, g_err, sizeof g_err);
+    if (!p) { g_kind = BNN_ERR_PACKAGE; return -1; }
+    pkg_info(p, pick_path(p, ""), info);
+    if (keep) *keep = p;
+    else bnn_pkg_close(p);
+    return 0;
+  }
+  if (!memcmp(magic, "BN24ENG1", 8) || !memcmp(magic, "BNV3ENG1", 8)) {
+    ERR(BNN_ERR_PACKAGE, "%s: a legacy %s file for the hand-written NEON engine, which this GPU library does not run; "
+        "hint: use the model's compiled package (.bnpk, neon-int8 path)", path,
+        magic[2] == '2' ? "BirdNET v2.4 .bn24" : "BirdNET v3.0 .bnv3");
+    return -1;
+  }
+  ERR(BNN_ERR_PACKAGE, "%s: not a bnneon weights file (magic '%.8s'; expected BNNPKG01 for a compiled package, "
+      "BN24ENG1 for a legacy BirdNET v2.4 file); hint: compile the model with compiler/bnc.py, or check the download "
+      "(sha256)", path, magic);
+  return -1;
+}
+
+int bnn_probe(const char *path, bnn_info *info) {
+  if (!info || info->struct_size < 8) { ERR(BNN_ERR_USAGE, "bnn_probe: bnn_info.struct_size not set"); return -1; }
+  bnn_info full;
+  if (probe_full(path, &full, NULL)) return -1;
+  copy_info(info, &full);
+  return 0;
+}
+
+static int is_license_key(const char *key) { return !strcmp(key, "license") || !strcmp(key, "licence"); }
+static int pkg_meta(const bnn_pkg *p, const char *key, char *buf, size_t n) {
+  int r = bnn_meta_str(p, key, buf, n);
+  if (r < 0 && is_license_key(key)) r = bnn_meta_str(p, strcmp(key, "licence") ? "licence" : "license", buf, n);
+  return r;
+}
+
+int bnn_probe_meta(const char *path, const char *key, char *buf, size_t n) {
+  bnn_info info;
+  bnn_pkg *p = NULL;
+  if (probe_full(path, &info, &p)) return -1;
+  const int r = pkg_meta(p, key, buf, n);
+  bnn_pkg_close(p);
+  return r;
+}
+
+int bnn_meta(const bnn_ctx *c, const char *key, char *buf, size_t n) {
+  if (!c) return -1;
+  return pkg_meta(c->pkg, key, buf, n);
+}
+
+/* ------------------------------------------------------------------ contexts */
+
+static int visible_devices(int *ids, int max) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) return 0;
+  const char *env = getenv("BNN_DEVICES");
+  int k = 0;
+  if (env && *env) {
+    char buf[256];
+    snprintf(buf, sizeof buf, "%s", env);
+    for (char *t = strtok(buf, ","); t && k < max; t = strtok(NULL, ",")) {
+      const int d = atoi(t);
+      if (d >= 0 && d < n) ids[k++] = d;
+    }
+    return k;
+  }
+  for (int d = 0; d < n && k < max; d++) ids[k++] = d;
+  return k;
+}
+
+static int make_devices(bnn_ctx *c, int n_dev) {
+  char err[512];
+  int kind = BNN_ERR_CPU;
+  for (int i = 0; i < n_dev; i++)
+    if (!c->dev[i] && bnn_rt_device(c, i, err, sizeof err, &kind)) {
+      ERR(kind, "%s path %.24s: %s", c->info.model_id, c->path->name, err);
+      return -1;
+    }
+  c->n_dev = n_dev;
+  return 0;
+}
+
+bnn_ctx *bnn_init(const char *path, int mode) {
+  bnn_info pi;
+  bnn_pkg *pkg = NULL;
+  if (probe_full(path, &pi, &pkg)) return NULL;
+  bnn_ctx *c = calloc(1, sizeof *c);
+  if (!c) { bnn_pkg_close(pkg); ERR(BNN_ERR_OOM, "out of memory (%zu bytes for the context)", sizeof *c); return NULL; }
+  c->pkg = pkg;
+  c->info = pi;
+  if (mode == BNN_MODE_REFERENCE || mode < 0 || mode > BNN_MODE_INT8) {
+    ERR(BNN_ERR_USAGE, "%s: mode %d is not available for compiled packages; hint: use mode 0 (best path for this "
+        "device), 2 (the neon-fp32 path), 3 (the neon-fp16 path) or 4 (the neon-int8 path); mode 1 (fp32 reference) "
+        "exists for the legacy .bn24 files only", path, mode);
+    bnn_free(c);
+    return NULL;
+  }
+  const char *want = "";
+  for (size_t i = 0; i < sizeof PATHS / sizeof PATHS[0]; i++)
+    if (PATHS[i].mode == mode) want = PATHS[i].name;
+  c->path_index = pick_path(pkg, want);
+  if (c->path_index < 0) { no_path_error(path, pkg, want); bnn_free(c); return NULL; }
+  c->path = &pkg->paths[c->path_index];
+  const char *eb = getenv("BNN_BATCH");
+  c->batch = eb && atoi(eb) > 0 ? atoi(eb) : 64;
+  const char *ep = getenv("BNN_PROF");
+  c->prof = ep ? atoi(ep) : 0;
+  char rerr[512];
+  int kind = BNN_ERR_PACKAGE;
+  if (bnn_rt_open(c, rerr, sizeof rerr, &kind)) {
+    ERR(kind, "%s path %.24s: %s", base_name(path), c->path->name, rerr);
+    bnn_free(c);
+    return NULL;
+  }
+  pkg_info(pkg, c->path_index, &c->info);
+  /* the metadata must agree with the buffers the outputs are read from (src/bnneon.c:255-274) */
+  const bnn_path_rec *d = c->path;
+  const bnn_buf_rec *ib = &c->bufd[d->in_buf], *ob = &c->bufd[d->out_buf];
+  const bnn_buf_rec *ebd = d->emb_buf == 0xffffffffu ? NULL : &c->bufd[d->emb_buf];
+#define META_HINT "; hint: the package is inconsistent: recompile it (compiler/bnc.py) and check its 'compiler' metadata"
+  if (c->info.n_samples <= 0 || ib->dtype != BNN_F32 || ib->elems != (uint64_t)c->info.n_samples) {
+    ERR(BNN_ERR_PACKAGE, "%s: metadata n_samples = %d but the input buffer is %s with %llu elements" META_HINT, path,
+        c->info.n_samples, bnn_dtype_name(ib->dtype), (unsigned long long)ib->elems);
+    bnn_free(c);
+    return NULL;
+  }
+  if (c->info.n_classes <= 0 || ob->dtype != BNN_F32 || ob->elems < (uint64_t)c->info.n_classes) {
+    ERR(BNN_ERR_PACKAGE, "%s: metadata n_classes = %d but the output buffer is %s with %llu elements" META_HINT, path,
+        c->info.n_classes, bnn_dtype_name(ob->dtype), (unsigned long long)ob->elems);
+    bnn_free(c);
+    return NULL;
+  }
+  if (c->info.emb_dim < 0 || (c->info.emb_dim && (!ebd || ebd->dtype != BNN_F32 || ebd->elems < (uint64_t)c->info.emb_dim))) {
+    ERR(BNN_ERR_PACKAGE, "%s: metadata emb_dim = %d but the path's embedding buffer is %s" META_HINT, path,
+        c->info.emb_dim, !ebd ? "absent" : bnn_dtype_name(ebd->dtype));
+    bnn_free(c);
+    return NULL;
+  }
+  c->info.precision = "int8 GEMMs, fp32 elsewhere";
+  for (size_t i = 0; i < sizeof PATHS / sizeof PATHS[0]; i++)
+    if (!strncmp(d->name, PATHS[i].name, 24)) c->info.precision = PATHS[i].precision;
+  /* the package is valid: now the GPU side (on a machine without one, the validation above still runs) */
+  int ids[64];
+  const int nvis = visible_devices(ids, 64);
+  if (nvis == 0) {
+    ERR(BNN_ERR_CPU, "%s: no CUDA device is visible (this library runs packages on NVIDIA B200 GPUs); hint: check "
+        "nvidia-smi, CUDA_VISIBLE_DEVICES and BNN_DEVICES", path);
+    bnn_free(c);
+    return NULL;
+  }
+  memcpy(c->dev_ids, ids, sizeof(int) * nvis);
+  if (make_devices(c, 1)) { bnn_free(c); return NULL; }
+  return c;
+}
+
+int bnn_get_info(const bnn_ctx *c, bnn_info *info) {
+  if (!c || !info || info->struct_size < 8) { ERR(BNN_ERR_USAGE, "bnn_get_info: no context or struct_size"); return -1; }
+  copy_info(info, &c->info);
+  return 0;
+}
+
+void bnn_free(bnn_ctx *c) {
+  if (!c) return;
+  bnn_rt_close(c);
+  bnn_pkg_close(c->pkg);
+  free(c);
+}
+
+int bnn_set_threads(bnn_ctx *c, int threads) {
+  if (!c) { ERR(BNN_ERR_USAGE, "bnn_set_threads: NULL context"); return -1; }
+  if (threads < 1 || threads > 64) {
+    ERR(BNN_ERR_USAGE, "bnn_set_threads: %d threads; hint: pass 1..64 (a host's 0 = all CPUs must be resolved by the host)",
+        threads);
+    return -1;
+  }
+  int ids[64];
+  const int nvis = visible_devices(ids, 64);
+  const int want = threads < nvis ? threads : nvis;
+  for (int i = want; i < 64; i++)
+    if (c->dev[i]) bnn_rt_device_free(c, i);
+  return make_devices(c, want);
+}
+
+int bnn_set_batch(bnn_ctx *c, int batch) {
+  if (!c || batch < 1 || batch > 65536) {
+    ERR(BNN_ERR_USAGE, "bnn_set_batch: batch %d; hint: pass 1..65536 windows", batch);
+    return -1;
+  }
+  if (batch == c->batch) return 0;
+  const int n = c->n_dev;
+  for (int i = 0; i < 64; i++)
+    if (c->dev[i]) bnn_rt_device_free(c, i);
+  c->batch = batch;
+  return make_devices(c, n);
+}
+int bnn_get_batch(const bnn_ctx *c) { return c ? c->batch : 0; }
+int bnn_launches_per_batch(const bnn_ctx *c) { return c ? c->launches : 0; }
+
+/* ------------------------------------------------------------------ inference */
+
+typedef struct {
+  bnn_ctx *c;
+  int di, w0, w1, rc;
+  const float *pcm;
+  float *out, *emb;
+  char err[512];
+  int kind;
+} dev_job;
+
+static int check_err_word(bnn_ctx *c, int di) {
+  bnn_dev *dv = c->dev[di];
+  if (*dv->err_host) {
+    const int code = *dv->err_host;
+    *dv->err_host = 0;
+    cudaMemsetAsync(dv->err, 0, sizeof(int), (cudaStream_t)dv->stream);
+    ERR(BNN_ERR_WINDOW, "window not scored: a GPU kernel's bounded wait ran out (code %d: %s) on GPU %d; hint: the GPU "
+        "is stalled or shared with a long job: retry, and check nvidia-smi", code,
+        code == BNNK_ERR_TMA_WAIT ? "TMA load" : code == BNNK_ERR_MMA_WAIT ? "tensor-core operands" : "GEMM result",
+        dv->dev);
+    return -1;
+  }
+  return 0;
+}
+
+static void *dev_worker(void *a) {
+  dev_job *j = a;
+  bnn_ctx *c = j->c;
+  bnn_dev *dv = c->dev[j->di];
+  const bnn_path_rec *d = c->path;
+  const int ns = c->info.n_samples, nc = c->info.n_classes, ne = c->info.emb_dim;
+  cudaStream_t st = (cudaStream_t)dv->stream;
+  cudaError_t e = cudaSetDevice(dv->dev);
+  for (int w = j->w0; w < j->w1 && !e && !j->rc; w += c->batch) {
+    const int nb = j->w1 - w < c->batch ? j->w1 - w : c->batch;
+    e = cudaMemcpyAsync(dv->buf[d->in_buf], j->pcm + (size_t)w * ns, sizeof(float) * (size_t)nb * ns,
+                        cudaMemcpyHostToDevice, st);
+    if (e) break;
+    if (bnn_rt_launch(c, j->di, nb, dv->buf[d->in_buf], 0, c->n_ops, st)) {
+      j->rc = -1;
+      snprintf(j->err, sizeof j->err, "%s", g_err);
+      j->kind = g_kind;
+      break;
+    }
+    e = cudaMemcpy2DAsync(j->out + (size_t)w * nc, sizeof(float) * nc, dv->buf[d->out_buf],
+                          sizeof(float) * dv->ws[d->out_buf], sizeof(float) * nc, nb, cudaMemcpyDeviceToHost, st);
+    if (!e && j->emb && ne)
+      e = cudaMemcpy2DAsync(j->emb + (size_t)w * ne, sizeof(float) * ne, dv->buf[d->emb_buf],
+                            sizeof(float) * dv->ws[d->emb_buf], sizeof(float) * ne, nb, cudaMemcpyDeviceToHost, st);
+  }
+  if (!e) e = cudaMemcpyAsync(dv->err_host, dv->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (!e) e = cudaStreamSynchronize(st);
+  if (e && !j->rc) {
+    j->rc = -1;
+    j->kind = BNN_ERR_WINDOW;
+    snprintf(j->err, sizeof j->err, "window not scored: CUDA error %d (%s) on GPU %d; hint: check the GPU (nvidia-smi)",
+             (int)e, cudaGetErrorString(e), dv->dev);
+  }
+  if (!j->rc && check_err_word(c, j->di)) {
+    j->rc = -1;
+    snprintf(j->err, sizeof j->err, "%s", g_err);
+    j->kind = g_kind;
+  }
+  return NULL;
+}
+
+int bnn_infer_batch(bnn_ctx *c, int n, const float *pcm, float *out, float *emb) {
+  if (!c || !pcm || !out || n < 0) { ERR(BNN_ERR_USAGE, "bnn_infer_batch: NULL context, pcm or out, or n < 0"); return -1; }
+  if (n == 0) return 0;
+  dev_job jobs[64];
+  pthread_t th[64];
+  const int nd = c->n_dev < n ? c->n_dev : n;
+  for (int i = 0; i < nd; i++) {
+    jobs[i] = (dev_job){c, i, (int)((long long)n * i / nd), (int)((long long)n * (i + 1) / nd), 0, pcm, out, emb, "", 0};
+    if (nd > 1) pthread_create(&th[i], NULL, dev_worker, &jobs[i]);
+    else dev_worker(&jobs[i]);
+  }
+  if (nd > 1)
+    for (int i = 0; i < nd; i++) pthread_join(th[i], NULL);
+  for (int i = 0; i < nd; i++)
+    if (jobs[i].rc) {
+      ERR(jobs[i].kind ? jobs[i].kind : BNN_ERR_WINDOW, "%s", jobs[i].err);
+      return -1;
+    }
+  return 0;
+}
+
+int bnn_infer(bnn_ctx *c, const float *pcm, float *out, float *emb) {
+  if (!c || !pcm || !out) { ERR(BNN_ERR_USAGE, "bnn_infer: NULL context, pcm or out"); return -1; }
+  return bnn_infer_batch(c, 1, pcm, out, emb);
+}
+
+int bnn_infer_device(bnn_ctx *c, int n, const float *d_pcm, float *d_out, float *d_emb, void *stream) {
+  if (!c || !d_pcm || !d_out || n < 0 || n > c->batch) {
+    ERR(BNN_ERR_USAGE, "bnn_infer_device: NULL context / pointers or n %d outside 0..%d (the batch capacity)", n,
+        c ? c->batch : 0);
+    return -1;
+  }
+  if (n == 0) return 0;
+  bnn_dev *dv = c->dev[0];
+  const bnn_path_rec *d = c->path;
+  const int nc = c->info.n_classes, ne = c->info.emb_dim;
+  cudaStream_t st = stream ? (cudaStream_t)stream : (cudaStream_t)dv->stream;
+  cudaSetDevice(dv->dev);
+  if (bnn_rt_launch(c, 0, n, d_pcm, 0, c->n_ops, st)) return -1;
+  cudaError_t e = cudaMemcpy2DAsync(d_out, sizeof(float) * nc, dv->buf[d->out_buf], sizeof(float) * dv->ws[d->out_buf],
+                                    sizeof(float) * nc, n, cudaMemcpyDeviceToDevice, st);
+  if (!e && d_emb && ne)
+    e = cudaMemcpy2DAsync(d_emb, sizeof(float) * ne, dv->buf[d->emb_buf], sizeof(float) * dv->ws[d->emb_buf],
+                          sizeof(float) * ne, n, cudaMemcpyDeviceToDevice, st);
+  if (!e && !stream) {
+    e = cudaMemcpyAsync(dv->err_host, dv->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (!e) e = cudaStreamSynchronize(st);
+    if (!e && check_err_word(c, 0)) return -1;
+  }
+  if (e) {
+    ERR(BNN_ERR_WINDOW, "window not scored: CUDA error %d (%s); hint: check the GPU (nvidia-smi)", (int)e, cudaGetErrorString(e));
+    return -1;
+  }
+  return 0;
+}
+
+int bnn_verify_labels(const char *weights_path, const char *labels_path) {
+  bnn_info info;
+  if (probe_full(weights_path, &info, NULL)) return -1;
+  if (!info.has_labels_sha) {
+    ERR(BNN_ERR_LABELS, "%s carries no label hash (legacy file or package compiled without --labels)", weights_path);
+    return -1;
+  }
+  FILE *f = fopen(labels_path, "rb");
+  if (!f) { ERR(BNN_ERR_LABELS, "cannot open label file %s", labels_path); return -1; }
+  unsigned char buf[65536];
+  size_t n, total = 0;
+  int lines = 0;
+  bnn_sha256 h;
+  bnn_sha256_init(&h);
+  while ((n = fread(buf, 1, sizeof buf, f)) > 0) {
+    bnn_sha256_update(&h, buf, n);
+    for (size_t i = 0; i < n; i++) lines += buf[i] == '\n';
+    total += n;
+  }
+  fclose(f);
+  unsigned char sum[32];
+  bnn_sha256_final(&h, sum);
+  if (!memcmp(sum, info.labels_sha256, 32)) return 0;
+  char a[17], b[17];
+  for (int i = 0; i < 8; i++) { snprintf(a + 2 * i, 3, "%02x", sum[i]); snprintf(b + 2 * i, 3, "%02x", info.labels_sha256[i]); }
+  ERR(BNN_ERR_LABELS, "label file %s (sha256 %s..., %d lines, %zu bytes) is not the label file %s was compiled with "
+      "(sha256 %s..., %d classes); hint: use the label file inside the package (bnn_probe_meta \"labels\", or `cli <pkg> "
+      "--labels`) or recompile the package with --labels %s", labels_path, a, lines, total, weights_path, b,
+      info.n_classes, labels_path);
+  return -1;
+}
+
+/* ------------------------------------------------------------------ per-op profile */
+
+int bnn_profile_begin(bnn_ctx *c) {
+  if (!c || !c->dev[0]) { ERR(BNN_ERR_USAGE, "bnn_profile_begin: no context"); return -1; }
+  bnn_dev *dv = c->dev[0];
+  cudaSetDevice(dv->dev);
+  if (!dv->events) {
+    dv->events = calloc(2 * (size_t)c->n_ops, sizeof(void *));
+    dv->op_ms = calloc((size_t)c->n_ops, sizeof(double));
+    if (!dv->events || !dv->op_ms) { ERR(BNN_ERR_OOM, "bnn_profile_begin: out of memory"); return -1; }
+    for (int k = 0; k < 2 * c->n_ops; k++)
+      if (cudaEventCreate((cudaEvent_t *)&dv->events[k])) {
+        ERR(BNN_ERR_CPU, "bnn_profile_begin: cudaEventCreate failed");
+        return -1;
+      }
+  }
+  memset(dv->op_ms, 0, sizeof(double) * (size_t)c->n_ops);
+  dv->prof_on = 1;
+  dv->prof_op0 = dv->prof_op1 = 0;
+  return 0;
+}
+
+int bnn_profile_collect(bnn_ctx *c) {
+  if (!c || !c->dev[0] || !c->dev[0]->prof_on) { ERR(BNN_ERR_USAGE, "bnn_profile_collect: profile not begun"); return -1; }
+  bnn_dev *dv = c->dev[0];
+  cudaSetDevice(dv->dev);
+  for (int i = dv->prof_op0; i < dv->prof_op1; i++) {
+    float ms = 0.f;
+    if (cudaEventSynchronize((cudaEvent_t)dv->events[2 * i + 1]) ||
+        cudaEventElapsedTime(&ms, (cudaEvent_t)dv->events[2 * i], (cudaEvent_t)dv->events[2 * i + 1])) {
+      ERR(BNN_ERR_CPU, "bnn_profile_collect: event query failed for op %d", i);
+      return -1;
+    }
+    dv->op_ms[i] += ms;
+  }
+  dv->prof_op0 = dv->prof_op1 = 0;
+  return 0;
+}
+
+double bnn_profile_op_ms(const bnn_ctx *c, int op) {
+  if (!c || !c->dev[0] || !c->dev[0]->op_ms || op < 0 || op >= c->n_ops) return -1.0;
+  return c->dev[0]->op_ms[op];
+}
+
+int bnn_profile_end(bnn_ctx *c) {
+  if (!c || !c->dev[0]) return -1;
+  c->dev[0]->prof_on = 0;
+  return 0;
+}
+
+/* ------------------------------------------------------------------ op-level debugging */
+
+int bnn_debug_n_ops(const bnn_ctx *c) { return c ? c->n_ops : 0; }
+int bnn_debug_op_code(const bnn_ctx *c, int i) { return c && i >= 0 && i < c->n_ops ? c->ops[i].code : -1; }
+
+static int dbg_check(bnn_ctx *c, int buf, int n) {
+  if (!c || n < 1 || n > c->batch || buf < 0 || (uint32_t)buf >= c->path->n_buf) {
+    ERR(BNN_ERR_USAGE, "bnn_debug: buffer %d / %d windows out of range", buf, n);
+    return -1;
+  }
+  if (!c->dev[0]->buf[buf]) {
+    ERR(BNN_ERR_USAGE, "bnn_debug: buffer %d is an int8 row buffer, which this runtime keeps in its own scratch layout", buf);
+    return -1;
+  }
+  return 0;
+}
+
+int bnn_debug_run_ops(bnn_ctx *c, int n, const float *pcm, int op0, int op1) {
+  if (dbg_check(c, 0, n)) return -1;
+  bnn_dev *dv = c->dev[0];
+  cudaStream_t st = (cudaStream_t)dv->stream;
+  cudaSetDevice(dv->dev);
+  const uint32_t in = c->path->in_buf;
+  if (pcm && cudaMemcpyAsync(dv->buf[in], pcm, sizeof(float) * (size_t)n * c->bufd[in].elems, cudaMemcpyHostToDevice, st)) {
+    ERR(BNN_ERR_WINDOW, "bnn_debug_run_ops: input copy failed");
+    return -1;
+  }
+  if (bnn_rt_launch(c, 0, n, dv->buf[in], op0, op1, st)) return -1;
+  cudaError_t e = cudaMemcpyAsync(dv->err_host, dv->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (!e) e = cudaStreamSynchronize(st);
+  if (e) { ERR(BNN_ERR_WINDOW, "bnn_debug_run_ops: CUDA error %d (%s)", (int)e, cudaGetErrorString(e)); return -1; }
+  return check_err_word(c, 0);
+}
+
+static int dbg_copy(bnn_ctx *c, int buf, int n, void *host, int to_host) {
+  if (dbg_check(c, buf, n)) return -1;
+  bnn_dev *dv = c->dev[0];
+  const bnn_buf_rec *b = &c->bufd[buf];
+  const size_t es = b->dtype == BNN_F16 ? 2 : b->dtype == BNN_I8 ? 1 : 4, row = es * b->elems;
+  cudaSetDevice(dv->dev);
+  cudaError_t e = to_host ? cudaMemcpy2D(host, row, dv->buf[buf], es * dv->ws[buf], row, n, cudaMemcpyDeviceToHost)
+                          : cudaMemcpy2D(dv->buf[buf], es * dv->ws[buf], host, row, row, n, cudaMemcpyHostToDevice);
+  if (e) { ERR(BNN_ERR_WINDOW, "bnn_debug buffer copy: CUDA error %d (%s)", (int)e, cudaGetErrorString(e)); return -1; }
+  return 0;
+}
+int bnn_debug_get_buffer(bnn_ctx *c, int buf, int n, void *dst) { return dbg_copy(c, buf, n, dst, 1); }
+int bnn_debug_set_buffer(bnn_ctx *c, int buf, int n, const void *src) { return dbg_copy(c, buf, n, (void *)src, 0); }
+
+/* ------------------------------------------------------------------ per-op entry points */
+
+int bnn_cuda_device_init(void) {
+  const int e = bnnk_device_init();
+  if (e) { ERR(BNN_ERR_CPU, "bnn_cuda_device_init: CUDA error %d (%s)", e, cudaGetErrorString((cudaError_t)e)); return -1; }
+  return 0;
+}
+
+static int launch_rc(const char *what, int e) {
+  if (!e) return 0;
+  ERR(BNN_ERR_WINDOW, "%s: CUDA error %d (%s)", what, e, cudaGetErrorString((cudaError_t)e));
+  return -1;
+}
+
+int bnn_cuda_quant_rows(int rows, int Mw, const float *d_x, long long xws, int lda, int K, int Kq, const float *d_gate,
+                        long long gws, int8_t *d_q, float *d_sa, int32_t *d_za, void *stream) {
+  if (rows < 0 || Mw < 1 || K < 1 || Kq < K || Kq % 4) {
+    ERR(BNN_ERR_USAGE, "bnn_cuda_quant_rows: rows %d Mw %d K %d Kq %d (need Mw >= 1, Kq >= K, Kq %% 4 == 0)", rows, Mw, K, Kq);
+    return -1;
+  }
+  return launch_rc("bnn_cuda_quant_rows",
+                   bnnk_quant(rows, Mw, d_x, xws, lda, K, Kq, d_gate, gws, d_q, d_sa, d_za, (bnn_stream_t)stream));
+}
+
+struct bnn_pw_s8 {
+  bnn_devop op;
+  int N, K, Kp, Np, rows_cap;
+  int8_t *q;
+  float *sa;
+  int32_t *za;
+  int *err;
+};
+
+bnn_pw_s8 *bnn_pw_s8_new(int N, int K, int Kp, int Np, const int8_t *w, const float *sw, const int32_t *cs,
+                         const float *b, int rows_cap) {
+  if (N <= 0 || K <= 0 || Np != ((N + 7) & ~7) || Kp != ((K + 15) & ~15) || rows_cap <= 0 || !w || !sw || !cs || !b) {
+    ERR(BNN_ERR_USAGE, "bnn_pw_s8_new: N %d K %d Kp %d Np %d rows %d (expected Np = N rounded up to 8, Kp = K rounded up "
+        "to 16)", N, K, Kp, Np, rows_cap);
+    return NULL;
+  }
+  bnn_pw_s8 *o = calloc(1, sizeof *o);
+  if (!o) { ERR(BNN_ERR_OOM, "out of memory"); return NULL; }
+  o->N = N; o->K = K; o->Kp = Kp; o->Np = Np; o->rows_cap = rows_cap;
+  char err[512];
+  int kind = BNN_ERR_CPU;
+  if (bnn_s8_weights(&o->op, N, K, Kp, Np, w, sw, cs, b, err, sizeof err, &kind)) {
+    ERR(kind, "bnn_pw_s8_new: %s", err);
+    bnn_pw_s8_free(o);
+    return NULL;
+  }
+  cudaError_t e = cudaMalloc((void **)&o->q, (size_t)rows_cap * o->op.kq);
+  if (!e) e = cudaMemset(o->q, 0, (size_t)rows_cap * o->op.kq);
+  if (!e) e = cudaMalloc((void **)&o->sa, sizeof(float) * rows_cap);
+  if (!e) e = cudaMalloc((void **)&o->za, sizeof(int32_t) * rows_cap);
+  if (!e) e = cudaMalloc((void **)&o->err, sizeof(int));
+  if (!e) e = cudaMemset(o->err, 0, sizeof(int));
+  if (!e) e = (cudaError_t)bnnk_gemm_plan_init(&o->op.plan, o->q, rows_cap, o->op.kq, o->op.w, N, Np);
+  if (e) {
+    ERR(e == cudaErrorMemoryAllocation ? BNN_ERR_OOM : BNN_ERR_CPU, "bnn_pw_s8_new: CUDA error %d (%s)", (int)e,
+        cudaGetErrorString(e));
+    bnn_pw_s8_free(o);
+    return NULL;
+  }
+  return o;
+}
+
+int bnn_pw_s8_run(bnn_pw_s8 *o, int B, int Mw, const float *d_x, long long xws, int lda, const float *d_gate,
+                  long long gws, int act, float *d_out, long long ows, int ldo, int ow, int opad, const float *d_res,
+                  long long rws, int ldr, int rw, int rpad, void *stream) {
+  if (!o || B < 0 || Mw < 1 || (long long)B * Mw > o->rows_cap || lda < o->K || ldo < o->Np || act < 0 || act > 2 ||
+      (opad && (ow <= 0 || Mw % ow)) || (rpad && (rw <= 0 || Mw % rw)) || (d_res && ldr < o->Np)) {
+    ERR(BNN_ERR_USAGE, "bnn_pw_s8_run: B %d Mw %d lda %d ldo %d act %d ow %d opad %d (capacity %d rows)", B, Mw, lda, ldo,
+        act, ow, opad, o ? o->rows_cap : 0);
+    return -1;
+  }
+  bnn_stream_t st = (bnn_stream_t)stream;
+  const int rows = B * Mw;
+  int e = bnnk_quant(rows, Mw, d_x, xws, lda, o->K, o->op.kq, d_gate, gws, o->q, o->sa, o->za, st);
+  if (!e) {
+    bnnk_epilogue ep = {act, d_out, ows, ldo, ow, opad, d_res, rws, ldr, rw, rpad, o->op.sw, o->op.bias, o->op.cs};
+    e = bnnk_gemm(&o->op.plan, rows, Mw, o->sa, o->za, &ep, o->err, st);
+  }
+  return launch_rc("bnn_pw_s8_run", e);
+}
+
+int bnn_pw_s8_error(bnn_pw_s8 *o) {
+  int v = 0;
+  if (o && o->err) cudaMemcpy(&v, o->err, sizeof v, cudaMemcpyDeviceToHost);
+  return v;
+}
+
+void bnn_pw_s8_free(bnn_pw_s8 *o) {
+  if (!o) return;
+  cudaFree(o->op.w); cudaFree(o->op.sw); cudaFree(o->op.bias); cudaFree(o->op.cs);
+  cudaFree(o->q); cudaFree(o->sa); cudaFree(o->za); cudaFree(o->err);
+  free(o);
+}
+
+int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, int s, const float *d_w, const float *d_b,
+                 float *d_out, long long ows, int Ho, int Wo, float *d_chsum, long long cws, void *stream) {
+  if (B < 0 || H <= 0 || W <= 0 || C <= 0 || C % 8 || (s != 1 && s != 2) || Ho <= 0 || Wo <= 0 ||
+      (Ho - 1) * s + 3 > H + 2 || (Wo - 1) * s + 3 > W + 2) {
+    ERR(BNN_ERR_USAGE, "bnn_cuda_dw3: H %d W %d C %d s %d Ho %d Wo %d (C %% 8 == 0, s 1|2, taps inside the halo)", H, W, C,
+        s, Ho, Wo);
+    return -1;
+  }
+  return launch_rc("bnn_cuda_dw3", bnnk_dw3(B, d_xp, xws, H, W, C, s, d_w, d_b, d_out, ows, Ho, Wo, d_chsum, cws,
+                                             (bnn_stream_t)stream));
+}
+
+int bnn_cuda_fn(int fn, int n, const float *d_x, float *d_y, void *stream) {
+  if (fn < 0 || fn > 6 || n < 0) { ERR(BNN_ERR_USAGE, "bnn_cuda_fn: fn %d n %d", fn, n); return -1; }
+  return launch_rc("bnn_cuda_fn", bnnk_test_fn(fn, n, d_x, d_y, (bnn_stream_t)stream));
+}

@@ -1,0 +1,138 @@
+/* Internal types of the B200 bnneon runtime (host side, C11). */
+#ifndef BNN_INTERNAL_H
+#define BNN_INTERNAL_H
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../../include/bnneon.h"
+#include "../cuda/bnn_kernels.h"
+
+/* ---- the .bnpk format (python/bnneon/compiler/pkgfmt.py:1-22; the same byte layout, read-only here) */
+enum { BNN_F32 = 0, BNN_F16 = 1, BNN_I8 = 2, BNN_I32 = 3 };
+typedef struct {
+  char name[48];
+  uint32_t dtype, ndim, dims[4];
+  uint64_t offset, nbytes, reserved;
+} bnn_tensor_rec; /* 96 bytes */
+typedef struct {
+  uint32_t dtype, H, W, C, ld, halo, slot, reserved;
+  uint64_t elems;
+} bnn_buf_rec; /* 40 bytes */
+typedef struct {
+  char name[24];
+  uint32_t hwcap, n_buf, n_ops, ops_bytes, in_buf, out_buf, emb_buf, reserved;
+  uint64_t buf_off, ops_off;
+} bnn_path_rec; /* 72 bytes */
+
+typedef struct bnn_pkg {
+  uint8_t *map;
+  size_t size;
+  uint32_t n_meta, n_tensors, n_paths;
+  int version;
+  const uint8_t *meta;
+  size_t meta_bytes;
+  bnn_tensor_rec *tensors;
+  bnn_path_rec *paths;
+} bnn_pkg;
+
+bnn_pkg *bnn_pkg_open(const char *path, char *err, size_t errlen);
+void bnn_pkg_close(bnn_pkg *p);
+int bnn_meta_str(const bnn_pkg *p, const char *key, char *buf, size_t n);
+int bnn_meta_i64(const bnn_pkg *p, const char *key, int64_t *v);
+int bnn_meta_f64(const bnn_pkg *p, const char *key, double *v);
+/* the raw value of a metadata record (type 0 string or 3 bytes): NULL if absent */
+const uint8_t *bnn_meta_raw(const bnn_pkg *p, const char *key, uint16_t *type, uint32_t *len);
+const char *bnn_dtype_name(uint32_t dt);
+
+/* ---- opcodes of the registry (src/rt.h:170-208; append-only, the same numbers) */
+enum {
+  BNN_OP_FE_STFT2 = 1, BNN_OP_C0POOL = 2, BNN_OP_PW = 3, BNN_OP_DW3 = 4, BNN_OP_SE = 5, BNN_OP_POSTPC = 6,
+  BNN_OP_DENSE = 7, BNN_OP_PW_S8 = 22, BNN_OP_GEMV_S8 = 23, BNN_OP_SE_GATE = 25, BNN_OP_PROTO_S8 = 35, BNN_OP_N = 36
+};
+enum { BNN_ACT_NONE = 0, BNN_ACT_SILU = 1, BNN_ACT_RELU = 2 };
+
+/* one decoded op record (pointers into the package) */
+typedef struct {
+  uint16_t code, nb, nt, ni;
+  const int32_t *b, *t, *p;
+  const char *kname;
+} bnn_op;
+
+/* per device, per op: the weights in the kernels' layouts */
+typedef struct {
+  /* PW_S8 / GEMV_S8 */
+  int8_t *w;
+  float *sw, *bias;
+  int32_t *cs;
+  bnnk_gemm_plan plan;
+  int kq;
+  /* DW3, SE_GATE, C0POOL, POSTPC */
+  float *f[6];
+} bnn_devop;
+
+typedef struct {
+  int dev;
+  void *stream; /* cudaStream_t */
+  int owns_tables;
+  void **buf;           /* device pointer per package buffer (NULL for the int8 scratch buffers) */
+  long long *ws;        /* window stride per buffer (elements) */
+  void *arena;          /* shared-slot memory */
+  void **priv;          /* per-buffer private allocations (halos, input) */
+  bnn_devop *ops;
+  int8_t *q;            /* int8 GEMM scratch: [batch * rows][kq] */
+  float *sa, *fe_minmax, *pcin;
+  int32_t *za;
+  int *err;             /* device error word */
+  int *err_host;        /* pinned */
+  bnnk_fe_tables fe;
+  void *fe_mem[16];
+  int n_fe_mem;
+  /* per-op CUDA-event profile (bnn_profile_*): events[2 i], events[2 i + 1] bracket op i of the last launch */
+  void **events;
+  double *op_ms;
+  int prof_on, prof_op0, prof_op1;
+} bnn_dev;
+
+struct bnn_ctx {
+  bnn_pkg *pkg;
+  int path_index;
+  const bnn_path_rec *path;
+  bnn_buf_rec *bufd;
+  bnn_op *ops;
+  int n_ops;
+  bnn_info info;
+  int batch;      /* windows per launch sequence and device */
+  int n_dev;      /* devices in use */
+  int dev_ids[64];
+  bnn_dev *dev[64];
+  int launches;   /* kernel launches per batch */
+  int prof;       /* BNN_PROF */
+};
+
+/* the runtime (bnn_rt.c) */
+/* decodes and validates the path's op list; 0 or -1 with err set (kind: BNN_ERR_*) */
+int bnn_rt_open(bnn_ctx *c, char *err, size_t errlen, int *kind);
+/* device state for c->dev_ids[i]: weights, arena for c->batch windows */
+int bnn_rt_device(bnn_ctx *c, int i, char *err, size_t errlen, int *kind);
+void bnn_rt_device_free(bnn_ctx *c, int i);
+/* n <= batch windows on device i: pcm at d_pcm (window stride n_samples); outputs stay in the arena */
+int bnn_rt_launch(bnn_ctx *c, int i, int n, const float *d_pcm, int op0, int op1, void *stream);
+void bnn_rt_close(bnn_ctx *c);
+int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src, const float *sw_src,
+                   const int32_t *cs_src, const float *b_src, char *err, size_t errlen, int *kind);
+
+/* errors (bnn_api.c): thread-local message and kind */
+void bnn_set_error(int kind, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+
+/* sha256 (sha256.c) */
+typedef struct {
+  uint32_t h[8];
+  uint64_t len;
+  uint8_t buf[64];
+  size_t fill;
+} bnn_sha256;
+void bnn_sha256_init(bnn_sha256 *s);
+void bnn_sha256_update(bnn_sha256 *s, const void *data, size_t n);
+void bnn_sha256_final(bnn_sha256 *s, uint8_t out[32]);
+
+#endif

@@ -1,0 +1,811 @@
+/* The package runtime on B200: op-list decoding and validation, per-device weights and activation arena, and the
+ * launch sequence of one batch.
+ *
+ * Replaces src/rt_pkg.c:168-542 (executor, arena, registry) and the inits / runs of the registry kernels the v2.4
+ * neon-int8 package uses (src/rt_ops_f32.c FE_STFT2 / C0POOL / DW3 / SE_GATE / POSTPC, src/rt_ops_s8n.c PW_S8 /
+ * GEMV_S8). The validation is the reference's: the same records are accepted and refused with the same messages
+ * (op index, kernel, source node, expected and found values, hint), so a package that loads on the reference loads
+ * here and a bad one fails the same way.
+ *
+ * Device layout of a context (per GPU, for `batch` windows):
+ *  - every package buffer keeps its per-window layout; a batch holds its windows at a fixed window stride;
+ *  - buffers with a zero halo (the pw outputs a depthwise conv reads) get memory of their own, zeroed once: no op
+ *    writes a halo, so it stays zero and needs no per-window clearing (the reference re-zeroes it in every PW run
+ *    because its slot memory is shared, src/rt_ops_s8n.c:125);
+ *  - the other buffers share memory by the package's slot plan (the compiler gave a slot's buffers disjoint
+ *    lifetimes), scaled by the batch;
+ *  - the int8 row buffers of PW_S8 / GEMV_S8 (q, sa, za) are replaced by one device scratch in the GEMM's layout
+ *    (rows of Kq = K rounded up to 32 bytes);
+ *  - weights are uploaded once per device in the kernels' layouts (int8 [N][Kq] rows for the tensor-core GEMM,
+ *    k-major fp32 for the CUDA-core convs). */
+#define _GNU_SOURCE
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <cuda_runtime_api.h>
+
+#include "bnn_internal.h"
+
+#define R8(x) (((x) + 7) & ~7)
+#define R16(x) (((x) + 15) & ~15)
+#define R32(x) (((x) + 31) & ~31)
+
+/* ------------------------------------------------------------------ validation (the reference's rt_need* family) */
+
+typedef struct {
+  bnn_ctx *c;
+  int i;               /* op index */
+  const bnn_op *op;
+  char *err;
+  size_t errlen;
+  int set;
+} vctx;
+
+static int vbad(vctx *v, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+static int vbad(vctx *v, const char *fmt, ...) {
+  if (v->set) return -1;
+  char msg[320], src[160] = "", params[160] = "";
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(msg, sizeof msg, fmt, ap);
+  va_end(ap);
+  /* the op's source node: metadata "src_nodes/<path>", one line per op */
+  char key[64];
+  uint16_t ty;
+  uint32_t vl;
+  snprintf(key, sizeof key, "src_nodes/%.24s", v->c->path->name);
+  const uint8_t *s = bnn_meta_raw(v->c->pkg, key, &ty, &vl);
+  if (s && (ty == 0 || ty == 3)) {
+    const char *p = (const char *)s, *end = p + vl;
+    for (int k = 0; k < v->i && p < end; k++) {
+      const char *nl = memchr(p, '\n', (size_t)(end - p));
+      p = nl ? nl + 1 : end;
+    }
+    if (p < end) {
+      const char *nl = memchr(p, '\n', (size_t)(end - p));
+      size_t l = (size_t)((nl ? nl : end) - p);
+      if (l > sizeof src - 1) l = sizeof src - 1;
+      memcpy(src, p, l);
+      src[l] = 0;
+      if (strlen(src) > 96) strcpy(src + 93, "...'");
+    }
+  }
+  size_t k = 0;
+  for (int j = 0; j < v->op->ni && k + 16 < sizeof params; j++)
+    k += (size_t)snprintf(params + k, sizeof params - k, "%s%d", j ? " " : "", v->op->p[j]);
+  char pfx[256];
+  if (src[0]) snprintf(pfx, sizeof pfx, "op %d %s (ONNX node %s)", v->i, v->op->kname, src);
+  else snprintf(pfx, sizeof pfx, "op %d %s (no source node names in the package: compile with bnc 2 or newer)", v->i,
+                v->op->kname);
+  int n = snprintf(v->err, v->errlen,
+                   "%s: %s; hint: package/library mismatch or a lowering bug: recompile with this checkout's "
+                   "compiler/bnc.py; if it reproduces, report this message", pfx, msg);
+  if (n > 0 && (size_t)n + 24 < v->errlen && params[0]) snprintf(v->err + n, v->errlen - (size_t)n, " (int params: [%s])", params);
+  v->set = 1;
+  return -1;
+}
+#define VREQ(v, cond) do { if (!(cond)) return vbad(v, "parameter check failed: %s", #cond); } while (0)
+
+static const bnn_buf_rec *vbd(vctx *v, int a) {
+  return a >= v->op->nb || v->op->b[a] < 0 ? NULL : &v->c->bufd[v->op->b[a]];
+}
+static size_t dsize(uint32_t dt) { return dt == BNN_F16 ? 2 : dt == BNN_I8 ? 1 : 4; }
+
+static int vneed(vctx *v, int a, int dt, size_t elems) {
+  const bnn_buf_rec *d = vbd(v, a);
+  if (!d) return vbad(v, "buffer argument %d is absent (the op record has %d buffer arguments)", a, v->op->nb);
+  if ((int)d->dtype == dt && d->elems >= elems) return 0;
+  return vbad(v, "buffer argument %d (buffer #%d): expected dtype %s with >= %zu elements, found dtype %s [%ux%ux%u ld "
+              "%u halo %u] with %llu elements", a, v->op->b[a], bnn_dtype_name((uint32_t)dt), elems,
+              bnn_dtype_name(d->dtype), d->H, d->W, d->C, d->ld, d->halo, (unsigned long long)d->elems);
+}
+static int vneed_haloed(vctx *v, int a, int dt, int H, int W, int ld, int h) {
+  if (vneed(v, a, dt, ((size_t)H + 2 * (size_t)h) * ((size_t)W + 2 * (size_t)h) * (size_t)ld)) return -1;
+  const bnn_buf_rec *d = vbd(v, a);
+  if ((int)d->halo != h || (int)d->ld != ld)
+    return vbad(v, "buffer argument %d (buffer #%d): expected halo %d and channel stride %d, found halo %u and stride %u",
+                a, v->op->b[a], h, ld, d->halo, d->ld);
+  return 0;
+}
+static int vneed_nohalo(vctx *v, int a, int dt, size_t elems) {
+  if (vneed(v, a, dt, elems)) return -1;
+  const bnn_buf_rec *d = vbd(v, a);
+  if (d->halo) return vbad(v, "buffer argument %d (buffer #%d, input): expected no halo, found halo %u", a, v->op->b[a], d->halo);
+  return 0;
+}
+static const void *vt(vctx *v, int a, size_t *nbytes) {
+  if (a >= v->op->nt || v->op->t[a] < 0) return NULL;
+  const bnn_tensor_rec *t = &v->c->pkg->tensors[v->op->t[a]];
+  if (nbytes) *nbytes = t->nbytes;
+  return v->c->pkg->map + t->offset;
+}
+static int vneed_t(vctx *v, int a, size_t nbytes, int atleast) {
+  size_t nb = 0;
+  if (!vt(v, a, &nb)) return vbad(v, "tensor argument %d is absent (the op record has %d tensor arguments)", a, v->op->nt);
+  if (atleast ? nb >= nbytes : nb == nbytes) return 0;
+  const bnn_tensor_rec *t = &v->c->pkg->tensors[v->op->t[a]];
+  return vbad(v, "tensor argument %d (tensor #%d '%.48s' %s [%u %u %u %u]): expected %s%zu bytes, found %llu bytes", a,
+              v->op->t[a], t->name, bnn_dtype_name(t->dtype), t->dims[0], t->dims[1], t->dims[2], t->dims[3],
+              atleast ? ">= " : "", nbytes, (unsigned long long)t->nbytes);
+}
+static int vneed_args(vctx *v, int nb, int nt, int ni) {
+  const bnn_op *op = v->op;
+  if ((nb < 0 || op->nb == nb) && (nt < 0 || op->nt == nt) && (ni < 0 || op->ni == ni)) return 0;
+  return vbad(v, "op record shape: expected %d buffer, %d tensor and %d int arguments, found %d, %d and %d", nb, nt, ni,
+              op->nb, op->nt, op->ni);
+}
+
+/* [N K Kp Np] of an int8 GEMM at int params po, tensors w sw cs b at ti (s8_view, src/rt_ops_s8n.c:13-25) */
+static int v_s8(vctx *v, int ti, int po) {
+  const int *p = v->op->p;
+  if (v->op->ni < po + 4) return vbad(v, "int8 GEMM shape [N K Kp Np] expected at int params %d..%d", po, po + 3);
+  const int N = p[po], K = p[po + 1], Kp = p[po + 2], Np = p[po + 3];
+  if (N <= 0 || K <= 0 || Np != R8(N) || Kp != R16(K))
+    return vbad(v, "int8 GEMM shape N %d K %d Kp %d Np %d: expected Np = N rounded up to 8, Kp = K rounded up to 16", N,
+                K, Kp, Np);
+  if (vneed_t(v, ti, (size_t)Np * Kp, 0) || vneed_t(v, ti + 1, (size_t)Np * 4, 1) || vneed_t(v, ti + 2, (size_t)Np * 4, 1) ||
+      vneed_t(v, ti + 3, (size_t)Np * 4, 1))
+    return -1;
+  return 0;
+}
+/* fp32 GEMM panels (rt_fpack_view, src/rt_ops_f32.c:49-59) */
+static int v_fpack(vctx *v, int ti, int po) {
+  const int *p = v->op->p;
+  if (v->op->ni < po + 4)
+    return vbad(v, "GEMM shape [N K Kp Np] expected at int params %d..%d, the op has %d ints", po, po + 3, v->op->ni);
+  const int N = p[po], K = p[po + 1], Kp = p[po + 2], Np = p[po + 3];
+  if (N <= 0 || K <= 0 || Np != R8(N) || Kp < K || Kp % 4)
+    return vbad(v, "GEMM shape N %d K %d Kp %d Np %d: expected Np = N rounded up to 8, Kp >= K, Kp %% 4 == 0", N, K, Kp, Np);
+  return vneed_t(v, ti, (size_t)Np * Kp * 4, 1) || vneed_t(v, ti + 1, (size_t)Np * 4, 1) ? -1 : 0;
+}
+/* the output of a 1x1 conv (rt_pw_out_check, src/rt_ops_f32.c:115-128) */
+static int v_pw_out(vctx *v, int dt) {
+  const int *p = v->op->p;
+  const int M = p[4], ldo = p[7], ow = p[8], opad = p[9];
+  const bnn_buf_rec *o = vbd(v, 1);
+  if (!o) return vbad(v, "buffer argument 1 (output) is absent");
+  if ((int)o->dtype != dt || o->ld != (uint32_t)ldo || o->halo != (uint32_t)opad)
+    return vbad(v, "buffer argument 1 (buffer #%d, output): expected dtype %s ld %d halo %d, found dtype %s ld %u halo %u",
+                v->op->b[1], bnn_dtype_name((uint32_t)dt), ldo, opad, bnn_dtype_name(o->dtype), o->ld, o->halo);
+  if (!opad) return vneed(v, 1, dt, (size_t)M * ldo);
+  VREQ(v, ow > 0 && M % ow == 0);
+  if (o->W != (uint32_t)ow || (size_t)o->H * o->W != (size_t)M)
+    return vbad(v, "buffer argument 1 (buffer #%d, padded output): expected %d x %d rows, found %u x %u", v->op->b[1],
+                M / ow, ow, o->H, o->W);
+  return vneed(v, 1, dt, (size_t)(M / ow + 2 * opad) * (ow + 2 * opad) * ldo);
+}
+
+static int init_pw_s8(vctx *v) { /* pw8_init, src/rt_ops_s8n.c:94-118 */
+  const bnn_op *op = v->op;
+  if (vneed_args(v, op->nb == 7 ? 7 : 6, 4, 11) || v_s8(v, 0, 0)) return -1;
+  const int *p = op->p;
+  const int K = p[1], Np = p[3];
+  if (op->nb == 7 && op->b[6] >= 0) {
+    VREQ(v, K % 4 == 0 && K <= 4096);
+    if (vneed(v, 6, BNN_F32, (size_t)K)) return -1;
+  }
+  const int M = p[4], lda = p[5], act = p[6], ldo = p[7], opad = p[9], ldr = p[10];
+  const size_t M4 = ((size_t)M + 3) & ~(size_t)3;
+  VREQ(v, M > 0 && lda >= K && act >= 0 && act <= 2 && ldo >= Np && opad >= 0 && opad <= 3);
+  const bnn_buf_rec *r = vbd(v, 2);
+  if (vneed_nohalo(v, 0, BNN_F32, (size_t)M * lda) || v_pw_out(v, BNN_F32)) return -1;
+  if (r) {
+    VREQ(v, ldr >= Np && r->dtype == BNN_F32 && r->ld == (uint32_t)ldr);
+    if (r->halo) {
+      VREQ(v, (size_t)r->H * r->W == (size_t)M && r->W > 0);
+      if (vneed(v, 2, BNN_F32, (size_t)(r->H + 2 * r->halo) * (r->W + 2 * r->halo) * ldr)) return -1;
+    } else if (vneed(v, 2, BNN_F32, (size_t)M * ldr))
+      return -1;
+  }
+  return vneed(v, 3, BNN_I8, M4 * p[2]) || vneed(v, 4, BNN_F32, M4) || vneed(v, 5, BNN_I32, M4) ? -1 : 0;
+}
+static int init_gemv_s8(vctx *v) { /* gemv8_init, src/rt_ops_s8n.c:138-148 */
+  if (vneed_args(v, 5, 4, 5) || v_s8(v, 0, 0)) return -1;
+  const int *p = v->op->p;
+  VREQ(v, p[4] == BNN_ACT_NONE || p[4] == BNN_ACT_RELU);
+  return vneed(v, 0, BNN_F32, (size_t)p[1]) || vneed(v, 1, BNN_F32, (size_t)p[3]) || vneed(v, 2, BNN_I8, (size_t)4 * p[2]) ||
+                 vneed(v, 3, BNN_F32, 4) || vneed(v, 4, BNN_I32, 4)
+             ? -1
+             : 0;
+}
+static int init_dw3(vctx *v) { /* dw3_init + rt_dw3_check, src/rt_ops_f32.c:216-233 */
+  if (vneed_args(v, 3, 2, 6)) return -1;
+  const int *p = v->op->p;
+  const int H = p[0], W = p[1], C = p[2], s = p[3], Ho = p[4], Wo = p[5];
+  VREQ(v, H > 0 && W > 0 && Ho > 0 && Wo > 0 && C > 0);
+  VREQ(v, C % 8 == 0);
+  VREQ(v, s == 1 || s == 2);
+  if (vneed_t(v, 0, (size_t)9 * C * 4, 0) || vneed_t(v, 1, (size_t)C * 4, 0)) return -1;
+  VREQ(v, (Ho - 1) * s - 1 + 1 + 3 <= H + 2);
+  VREQ(v, (Wo - 1) * s - 1 + 1 + 3 <= W + 2);
+  if (vneed_haloed(v, 0, BNN_F32, H, W, C, 1)) return -1;
+  return vneed(v, 1, BNN_F32, (size_t)Ho * Wo * C) || vneed(v, 2, BNN_F32, (size_t)C) ? -1 : 0;
+}
+static int init_se_gate(vctx *v) { /* rt_se_check(gate), src/rt_ops_f32.c:256-266 */
+  if (vneed_args(v, 2, 4, 3)) return -1;
+  const int C = v->op->p[0], rd = v->op->p[1], P = v->op->p[2];
+  VREQ(v, C > 0 && C % 8 == 0 && C <= 4096);
+  VREQ(v, rd > 0 && rd <= 512);
+  VREQ(v, P > 0);
+  const size_t want[4] = {(size_t)rd * C, (size_t)rd, (size_t)rd * C, (size_t)C};
+  for (int i = 0; i < 4; i++)
+    if (vneed_t(v, i, want[i] * 4, 0)) return -1;
+  return vneed(v, 0, BNN_F32, (size_t)C) || vneed(v, 1, BNN_F32, (size_t)C) ? -1 : 0;
+}
+static int init_c0pool(vctx *v) { /* c0_init, src/rt_ops_f32.c:63-72 */
+  if (vneed_args(v, 2, 2, 4) || v_fpack(v, 0, 0)) return -1;
+  const int *p = v->op->p;
+  VREQ(v, p[0] == 24 && p[1] == 64 && p[2] == 64);
+  return vneed(v, 0, BNN_F32, (size_t)96 * 511 * 2) || vneed(v, 1, BNN_F32, (size_t)48 * 128 * 48) ? -1 : 0;
+}
+static int init_postpc(vctx *v) { /* postpc_init + rt_postpc_check, src/rt_ops_f32.c:329-343 */
+  if (vneed_args(v, 4, 4, 4) || v_fpack(v, 2, 0)) return -1;
+  VREQ(v, v->op->p[0] == 1024 && v->op->p[1] == 1728);
+  if (vneed_t(v, 0, 192 * 4, 1) || vneed_t(v, 1, 192 * 4, 1)) return -1;
+  return vneed(v, 0, BNN_F32, 24 * 192) || vneed(v, 1, BNN_F32, 1024) || vneed(v, 2, BNN_F32, 8 * 1728) ||
+                 vneed(v, 3, BNN_F32, 8 * 1024)
+             ? -1
+             : 0;
+}
+static int init_fe_stft2(vctx *v) { /* fe_stft2_init, src/rt_ops_f32.c:25-40 */
+  const size_t want[8] = {2048, 1024, (size_t)96 * 1025, (size_t)96 * 513, 1, 1, 2, 2};
+  if (vneed_args(v, 2, 8, -1)) return -1;
+  for (int i = 0; i < 8; i++)
+    if (vneed_t(v, i, want[i] * 4, 0)) return -1;
+  return vneed(v, 0, BNN_F32, 144000) || vneed(v, 1, BNN_F32, (size_t)96 * 511 * 2) ? -1 : 0;
+}
+
+/* the registry of this library: (base opcode, variant 0) -> kernel; outmask / optmask as the reference's
+ * (src/rt_ops_f32.c:620-637, src/rt_ops_s8n.c:255-260) */
+typedef struct {
+  int code;
+  const char *name;
+  int (*init)(vctx *);
+  uint32_t outmask, optmask;
+  int launches;  /* kernel launches per run */
+} kdesc;
+static const kdesc KERNELS[] = {
+    {BNN_OP_FE_STFT2, "fe_stft2", init_fe_stft2, 0x2, 0, 2},
+    {BNN_OP_C0POOL, "c0pool_f32", init_c0pool, 0x2, 0, 1},
+    {BNN_OP_DW3, "dw3_f32", init_dw3, 0x6, 0, 1},
+    {BNN_OP_POSTPC, "postpc_f32", init_postpc, 0xe, 0, 2},
+    {BNN_OP_SE_GATE, "se_gate_f32", init_se_gate, 0x2, 0, 1},
+    {BNN_OP_PW_S8, "pw_s8n", init_pw_s8, 0x3a, 0x44, 2},
+    {BNN_OP_GEMV_S8, "gemv_s8n", init_gemv_s8, 0x1e, 0, 2},
+};
+static const kdesc *kernel_for(int code) {
+  if (code >> 8) return NULL; /* variants 1 and 2 are the fp16 / dotprod CPU paths: no GPU kernels */
+  for (size_t i = 0; i < sizeof KERNELS / sizeof KERNELS[0]; i++)
+    if (KERNELS[i].code == code) return &KERNELS[i];
+  return NULL;
+}
+
+/* ------------------------------------------------------------------ op list decoding (src/rt_pkg.c:349-509) */
+
+#define HINT_PKG "hint: package/library mismatch or a lowering bug: recompile with this checkout's compiler/bnc.py; if it " \
+                 "reproduces, report this message"
+
+int bnn_rt_open(bnn_ctx *c, char *err, size_t errlen, int *kind) {
+  *kind = BNN_ERR_PACKAGE;
+  const bnn_path_rec *d = c->path;
+  const uint8_t *m = c->pkg->map;
+  c->bufd = malloc(sizeof(bnn_buf_rec) * d->n_buf);
+  c->ops = calloc(d->n_ops, sizeof(bnn_op));
+  if (!c->bufd || !c->ops) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory (op list)"); return -1; }
+  memcpy(c->bufd, m + d->buf_off, sizeof(bnn_buf_rec) * d->n_buf);
+  const bnn_buf_rec *bd = c->bufd;
+  size_t *slot_sz = calloc(d->n_buf, sizeof(size_t)), total = 0;
+  if (!slot_sz) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory (slot table)"); return -1; }
+  for (uint32_t i = 0; i < d->n_buf; i++) {
+    if (bd[i].dtype > BNN_I32 || bd[i].elems > ((size_t)1 << 30) || bd[i].slot >= d->n_buf) {
+      snprintf(err, errlen, "path %.24s buffer #%u: bad descriptor (dtype %u, %llu elements, slot %u of %u); " HINT_PKG,
+               d->name, i, bd[i].dtype, (unsigned long long)bd[i].elems, bd[i].slot, d->n_buf);
+      free(slot_sz);
+      return -1;
+    }
+    if ((i == d->in_buf) != (bd[i].slot == bd[d->in_buf].slot)) {
+      snprintf(err, errlen, "path %.24s buffer #%u shares the input window's memory slot %u; " HINT_PKG, d->name, i, bd[i].slot);
+      free(slot_sz);
+      return -1;
+    }
+    const size_t b = ((size_t)bd[i].elems * dsize(bd[i].dtype) + 64 + 63) & ~(size_t)63;
+    if (b > slot_sz[bd[i].slot]) slot_sz[bd[i].slot] = b;
+  }
+  for (uint32_t s = 0; s < d->n_buf; s++) {
+    if (s == bd[d->in_buf].slot) continue;
+    total += slot_sz[s];
+    if (total > ((size_t)1 << 30)) {
+      snprintf(err, errlen, "path %.24s needs more than 1 GB of activation buffers; hint: the package is corrupt or the "
+               "model is far larger than this runtime is built for", d->name);
+      free(slot_sz);
+      return -1;
+    }
+  }
+  free(slot_sz);
+  for (uint32_t i = 0; i < d->n_buf; i++)
+    if (i != d->out_buf && (bd[i].slot == bd[d->out_buf].slot ||
+                            (d->emb_buf != 0xffffffffu && i != d->emb_buf && bd[i].slot == bd[d->emb_buf].slot))) {
+      snprintf(err, errlen, "path %.24s buffer #%u shares memory slot %u with the output buffer (#%u / #%u); " HINT_PKG,
+               d->name, i, bd[i].slot, d->out_buf, d->emb_buf);
+      return -1;
+    }
+  const uint8_t *q = m + d->ops_off, *end = q + d->ops_bytes;
+  for (uint32_t i = 0; i < d->n_ops; i++) {
+    uint16_t h[6];
+    if (q + 12 > end) {
+      snprintf(err, errlen, "op %u: truncated op list (%u ops declared, %u bytes); " HINT_PKG, i, d->n_ops, d->ops_bytes);
+      return -1;
+    }
+    memcpy(h, q, 12);
+    const size_t need = 12 + 4 * ((size_t)h[2] + h[3] + h[4]);
+    if (h[1] < need || q + h[1] > end || ((uintptr_t)(q - m) % 4)) {
+      snprintf(err, errlen, "op %u: bad op record (%u bytes for %u buffer, %u tensor, %u int arguments); " HINT_PKG, i,
+               h[1], h[2], h[3], h[4]);
+      return -1;
+    }
+    bnn_op *op = &c->ops[i];
+    op->code = h[0];
+    op->nb = h[2];
+    op->nt = h[3];
+    op->ni = h[4];
+    op->b = (const int32_t *)(q + 12);
+    op->t = op->b + op->nb;
+    op->p = op->t + op->nt;
+    op->kname = "?";
+    c->n_ops = (int)i + 1;
+    vctx v = {c, (int)i, op, err, errlen, 0};
+    for (int k = 0; k < op->nb; k++)
+      if (op->b[k] >= (int32_t)d->n_buf || op->b[k] < -1)
+        return vbad(&v, "buffer argument %d names buffer #%d but the path has %u buffers", k, op->b[k], d->n_buf);
+    for (int k = 0; k < op->nt; k++)
+      if (op->t[k] >= (int32_t)c->pkg->n_tensors)
+        return vbad(&v, "tensor argument %d names tensor #%d but the package has %u tensors", k, op->t[k],
+                    c->pkg->n_tensors);
+    const int var = op->code >> 8;
+    if (var && !(d->hwcap & 1))
+      return vbad(&v, "fp16 kernel (opcode 0x%x) in path %.24s, which does not declare the fp16 requirement", op->code,
+                  d->name);
+    if (var == 2 && !(d->hwcap & 2))
+      return vbad(&v, "dotprod kernel (opcode 0x%x) in path %.24s, which does not declare the dotprod requirement",
+                  op->code, d->name);
+    const kdesc *k = kernel_for(op->code);
+    if (!k) {
+      char comp[48];
+      if (bnn_meta_str(c->pkg, "compiler", comp, sizeof comp) < 0) snprintf(comp, sizeof comp, "unknown");
+      *kind = BNN_ERR_CPU;
+      return vbad(&v, "opcode 0x%x (base %d variant %d) has no B200 kernel in this library (it runs the neon-int8 ops "
+                  "FE_STFT2, C0POOL, PW_S8, DW3, SE_GATE, POSTPC and GEMV_S8; the package was written by compiler '%s')",
+                  op->code, op->code & 0xff, var, comp);
+    }
+    op->kname = k->name;
+    for (int a = 0; a < op->nb; a++) {
+      if (op->b[a] < 0 && !(a < 32 && (k->optmask >> a & 1)))
+        return vbad(&v, "buffer argument %d is required by the kernel but absent (-1) in the op record", a);
+      if (op->b[a] == (int32_t)d->in_buf && a < 32 && (k->outmask >> a & 1))
+        return vbad(&v, "buffer argument %d is the input window (#%u) but the kernel writes it", a, d->in_buf);
+    }
+    for (int a = 0; a < op->nb; a++)
+      for (int b2 = 0; b2 < op->nb; b2++)
+        if (a != b2 && op->b[a] >= 0 && op->b[b2] >= 0 && a < 32 && (k->outmask >> a & 1) &&
+            (op->b[a] == op->b[b2] || bd[op->b[a]].slot == bd[op->b[b2]].slot))
+          return vbad(&v, "buffer arguments %d (#%d, written) and %d (#%d) share memory slot %u", a, op->b[a], b2,
+                      op->b[b2], bd[op->b[a]].slot);
+    if (k->init(&v)) return -1;
+    c->launches += k->launches;
+    q += h[1];
+  }
+  return 0;
+}
+
+/* ------------------------------------------------------------------ device state */
+
+static int cerr(char *err, size_t errlen, int *kind, cudaError_t e, const char *what) {
+  *kind = e == cudaErrorMemoryAllocation ? BNN_ERR_OOM : BNN_ERR_CPU;
+  snprintf(err, errlen, "%s: CUDA error %d (%s); hint: %s", what, (int)e, cudaGetErrorString(e),
+           e == cudaErrorMemoryAllocation ? "free GPU memory or lower the batch (bnn_set_batch, BNN_BATCH)"
+                                          : "check the GPU and the driver (nvidia-smi)");
+  return -1;
+}
+#define CK(call, what)                                                  \
+  do {                                                                  \
+    cudaError_t e_ = (cudaError_t)(call);                               \
+    if (e_ != cudaSuccess) return cerr(err, errlen, kind, e_, (what));  \
+  } while (0)
+
+static const void *tptr(const bnn_ctx *c, const bnn_op *op, int a) {
+  return c->pkg->map + c->pkg->tensors[op->t[a]].offset;
+}
+static int upload(void **dst, const void *src, size_t bytes, char *err, size_t errlen, int *kind) {
+  CK(cudaMalloc(dst, bytes ? bytes : 16), "weight upload (cudaMalloc)");
+  if (bytes) CK(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice), "weight upload (cudaMemcpy)");
+  return 0;
+}
+static int is_int8_scratch(const bnn_ctx *c, int buf) {
+  /* PW_S8 b[3..5], GEMV_S8 b[2..4]: replaced by the device scratch */
+  for (int i = 0; i < c->n_ops; i++) {
+    const bnn_op *op = &c->ops[i];
+    int lo = op->code == BNN_OP_PW_S8 ? 3 : op->code == BNN_OP_GEMV_S8 ? 2 : -1;
+    for (int a = 0; a < op->nb; a++) {
+      if (op->b[a] != buf) continue;
+      if (lo < 0 || a < lo || a > lo + 2) return 0;
+    }
+  }
+  for (int i = 0; i < c->n_ops; i++) {
+    const bnn_op *op = &c->ops[i];
+    const int lo = op->code == BNN_OP_PW_S8 ? 3 : op->code == BNN_OP_GEMV_S8 ? 2 : -1;
+    if (lo >= 0)
+      for (int a = lo; a < lo + 3; a++)
+        if (op->b[a] == buf) return 1;
+  }
+  return 0;
+}
+
+/* FE_STFT2 tables (spec_init, src/v24_fe.c:45-84; fft_twiddles / fft_bitrev, src/fft_tab.h:9-21): twiddles and the
+ * real-split cos / sin in double, rounded once; the sparse mel as the nonzero range of each filter row
+ * (nz_range, src/rt_ops_f32.c:16-24) */
+static int fe_tables(bnn_ctx *c, bnn_dev *dv, const bnn_op *op, char *err, size_t errlen, int *kind) {
+  bnnk_fe_tables *t = &dv->fe;
+  for (int br = 0; br < 2; br++) {
+    const int N = br ? 1024 : 2048, M = N / 2, bins = M + 1;
+    int lg = 0;
+    while ((1 << lg) < M) lg++;
+    const float *win = tptr(c, op, br), *mel = tptr(c, op, 2 + br);
+    const float pw = ((const float *)tptr(c, op, 4 + br))[0];
+    int lo[96], hi[96], klo = bins, khi = 0, nnz = 0;
+    for (int j = 0; j < 96; j++) {
+      const float *f = mel + (size_t)j * bins;
+      int l = 0, h = 0;
+      for (int k = 0; k < bins; k++)
+        if (f[k] != 0.f) { if (h == 0) l = k; h = k + 1; }
+      lo[j] = l;
+      hi[j] = h;
+      if (h > l) { if (l < klo) klo = l; if (h > khi) khi = h; }
+      nnz += h - l;
+    }
+    if (khi <= klo) { klo = 0; khi = 0; }
+    float *twr = malloc(sizeof(float) * M / 2), *twi = malloc(sizeof(float) * M / 2);
+    float *pcv = malloc(sizeof(float) * (khi + 1)), *psv = malloc(sizeof(float) * (khi + 1));
+    int *rev = malloc(sizeof(int) * M), *off = malloc(sizeof(int) * 97), *mk = malloc(sizeof(int) * (nnz + 1));
+    float *mw = malloc(sizeof(float) * (nnz + 1));
+    if (!twr || !twi || !pcv || !psv || !rev || !off || !mk || !mw) {
+      *kind = BNN_ERR_OOM;
+      snprintf(err, errlen, "out of memory (front-end tables)");
+      return -1;
+    }
+    for (int k = 0; k < M / 2; k++) {
+      const double a = -2 * M_PI * k / M;
+      twr[k] = (float)cos(a);
+      twi[k] = (float)sin(a);
+    }
+    for (int k = 0; k < khi; k++) {
+      const double a = 2 * M_PI * k / N;
+      pcv[k] = (float)cos(a);
+      psv[k] = (float)sin(a);
+    }
+    for (int i = 0; i < M; i++) {
+      int r = 0;
+      for (int b = 0; b < lg; b++) r |= ((i >> b) & 1) << (lg - 1 - b);
+      rev[i] = r;
+    }
+    nnz = 0;
+    for (int j = 0; j < 96; j++) {
+      off[j] = nnz;
+      for (int k = lo[j]; k < hi[j]; k++) { mk[nnz] = k; mw[nnz] = mel[(size_t)j * bins + k]; nnz++; }
+    }
+    off[96] = nnz;
+    void *d;
+    int rc = 0;
+#define UP(field, src, bytes)                                     \
+    if (!rc) {                                                    \
+      rc = upload(&d, (src), (bytes), err, errlen, kind);         \
+      if (!rc) { t->field[br] = d; dv->fe_mem[dv->n_fe_mem++] = d; } \
+    }
+    UP(win, win, sizeof(float) * N);
+    UP(tw_re, twr, sizeof(float) * M / 2);
+    UP(tw_im, twi, sizeof(float) * M / 2);
+    UP(pc, pcv, sizeof(float) * (khi + 1));
+    UP(ps, psv, sizeof(float) * (khi + 1));
+    UP(rev, rev, sizeof(int) * M);
+    UP(mel_off, off, sizeof(int) * 97);
+    UP(mel_k, mk, sizeof(int) * (nnz + 1));
+#undef UP
+    if (!rc) {
+      rc = upload(&d, mw, sizeof(float) * (nnz + 1), err, errlen, kind);
+      if (!rc) { t->mel_w[br] = d; dv->fe_mem[dv->n_fe_mem++] = d; }
+    }
+    free(twr); free(twi); free(pcv); free(psv); free(rev); free(off); free(mk); free(mw);
+    if (rc) return rc;
+    t->klo[br] = klo;
+    t->khi[br] = khi;
+    t->pw2[br] = 2.f * pw;
+    t->bn_s[br] = ((const float *)tptr(c, op, 6))[br];
+    t->bn_b[br] = ((const float *)tptr(c, op, 7))[br];
+  }
+  return 0;
+}
+
+/* int8 GEMM weights in the GEMM's layout: the package's panels [Np/4][Kp/16][4][16] (lower.py:883-914) as rows
+ * [n_tiles * bn][Kq] (Kq = K rounded up to 32), zero beyond N and K; scales, column sums and biases padded with zeros */
+int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src, const float *sw_src,
+                   const int32_t *cs_src, const float *b_src, char *err, size_t errlen, int *kind) {
+  (void)N;
+  const int kq = R32(K), rows = bnnk_gemm_weight_rows(Np);
+  d->kq = kq;
+  int8_t *w = calloc((size_t)rows * kq, 1);
+  float *sw = calloc(rows, sizeof(float)), *b = calloc(rows, sizeof(float));
+  int32_t *cs = calloc(rows, sizeof(int32_t));
+  if (!w || !sw || !b || !cs) {
+    free(w); free(sw); free(b); free(cs);
+    *kind = BNN_ERR_OOM;
+    snprintf(err, errlen, "out of memory (int8 weights, %d x %d)", rows, kq);
+    return -1;
+  }
+  for (int n = 0; n < Np; n++)
+    for (int k = 0; k < Kp; k++)
+      w[(size_t)n * kq + k] = src[(((size_t)(n / 4) * (Kp / 16) + k / 16) * 4 + n % 4) * 16 + k % 16];
+  memcpy(sw, sw_src, sizeof(float) * Np);
+  memcpy(cs, cs_src, sizeof(int32_t) * Np);
+  memcpy(b, b_src, sizeof(float) * Np);
+  int rc = upload((void **)&d->w, w, (size_t)rows * kq, err, errlen, kind);
+  if (!rc) rc = upload((void **)&d->sw, sw, sizeof(float) * rows, err, errlen, kind);
+  if (!rc) rc = upload((void **)&d->cs, cs, sizeof(int32_t) * rows, err, errlen, kind);
+  if (!rc) rc = upload((void **)&d->bias, b, sizeof(float) * rows, err, errlen, kind);
+  free(w); free(sw); free(b); free(cs);
+  return rc;
+}
+
+/* the weights of op i in the kernels' layouts */
+static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, int *kind) {
+  const bnn_op *op = &c->ops[i];
+  bnn_devop *d = &dv->ops[i];
+  const int *p = op->p;
+  switch (op->code) {
+  case BNN_OP_PW_S8:
+  case BNN_OP_GEMV_S8:
+    return bnn_s8_weights(d, p[0], p[1], p[2], p[3], tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), tptr(c, op, 3),
+                          err, errlen, kind);
+  case BNN_OP_DW3: {
+    const int C = p[2];
+    return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * 9 * C, err, errlen, kind) ||
+           upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * C, err, errlen, kind);
+  }
+  case BNN_OP_SE_GATE: {
+    const int C = p[0], rd = p[1];
+    return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * rd * C, err, errlen, kind) ||
+           upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * rd, err, errlen, kind) ||
+           upload((void **)&d->f[2], tptr(c, op, 2), sizeof(float) * rd * C, err, errlen, kind) ||
+           upload((void **)&d->f[3], tptr(c, op, 3), sizeof(float) * C, err, errlen, kind);
+  }
+  case BNN_OP_C0POOL: { /* panels [Np/8][64][8] -> k-major [64][24] */
+    const float *src = tptr(c, op, 0);
+    float wt[64 * 24];
+    for (int k = 0; k < 64; k++)
+      for (int n = 0; n < 24; n++) wt[k * 24 + n] = src[((size_t)(n / 8) * 64 + k) * 8 + n % 8];
+    return upload((void **)&d->f[0], wt, sizeof wt, err, errlen, kind) ||
+           upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * 24, err, errlen, kind);
+  }
+  case BNN_OP_POSTPC: { /* panels [128][1728][8] -> k-major [1728][1024] */
+    const float *src = tptr(c, op, 2);
+    float *wt = malloc(sizeof(float) * 1728 * 1024);
+    if (!wt) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory (pc weights)"); return -1; }
+    for (int n = 0; n < 1024; n++)
+      for (int k = 0; k < 1728; k++) wt[(size_t)k * 1024 + n] = src[((size_t)(n / 8) * 1728 + k) * 8 + n % 8];
+    int rc = upload((void **)&d->f[0], wt, sizeof(float) * 1728 * 1024, err, errlen, kind);
+    free(wt);
+    return rc || upload((void **)&d->f[1], tptr(c, op, 3), sizeof(float) * 1024, err, errlen, kind) ||
+           upload((void **)&d->f[2], tptr(c, op, 0), sizeof(float) * 192, err, errlen, kind) ||
+           upload((void **)&d->f[3], tptr(c, op, 1), sizeof(float) * 192, err, errlen, kind);
+  }
+  case BNN_OP_FE_STFT2:
+    return fe_tables(c, dv, op, err, errlen, kind);
+  default:
+    return 0;
+  }
+}
+
+int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
+  *kind = BNN_ERR_CPU;
+  bnn_dev *dv = calloc(1, sizeof *dv);
+  if (!dv) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory (device state)"); return -1; }
+  c->dev[di] = dv;
+  dv->dev = c->dev_ids[di];
+  const bnn_path_rec *d = c->path;
+  const int B = c->batch;
+  CK(cudaSetDevice(dv->dev), "cudaSetDevice");
+  int major = 0, minor = 0;
+  CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dv->dev), "device query");
+  CK(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dv->dev), "device query");
+  if (major != 10 || minor != 0) {
+    *kind = BNN_ERR_CPU;
+    snprintf(err, errlen, "GPU %d has compute capability %d.%d, this library is built for sm_100a (B200) only; hint: "
+             "run on a B200", dv->dev, major, minor);
+    return -1;
+  }
+  CK(cudaStreamCreateWithFlags((cudaStream_t *)&dv->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  CK(bnnk_device_init(), "device tables");
+  dv->buf = calloc(d->n_buf, sizeof(void *));
+  dv->priv = calloc(d->n_buf, sizeof(void *));
+  dv->ws = calloc(d->n_buf, sizeof(long long));
+  dv->ops = calloc(c->n_ops, sizeof(bnn_devop));
+  if (!dv->buf || !dv->priv || !dv->ws || !dv->ops) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory"); return -1; }
+  /* activation memory */
+  size_t *slot_bytes = calloc(d->n_buf, sizeof(size_t));
+  size_t *slot_off = calloc(d->n_buf, sizeof(size_t));
+  if (!slot_bytes || !slot_off) { free(slot_bytes); free(slot_off); *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory"); return -1; }
+  for (uint32_t i = 0; i < d->n_buf; i++) {
+    const bnn_buf_rec *b = &c->bufd[i];
+    if (i == d->in_buf || b->halo || is_int8_scratch(c, (int)i)) continue;
+    const size_t bytes = ((size_t)b->elems * dsize(b->dtype) + 255) & ~(size_t)255;
+    if (bytes > slot_bytes[b->slot]) slot_bytes[b->slot] = bytes;
+  }
+  size_t total = 0;
+  for (uint32_t s = 0; s < d->n_buf; s++) { slot_off[s] = total; total += slot_bytes[s] * (size_t)B; }
+  cudaError_t e = cudaMalloc(&dv->arena, total ? total : 256);
+  if (!e) e = cudaMemset(dv->arena, 0, total ? total : 256);
+  if (e) { free(slot_bytes); free(slot_off); return cerr(err, errlen, kind, e, "activation arena"); }
+  for (uint32_t i = 0; i < d->n_buf; i++) {
+    const bnn_buf_rec *b = &c->bufd[i];
+    const size_t es = dsize(b->dtype);
+    if (i == d->in_buf) {
+      dv->ws[i] = (long long)b->elems;
+      e = cudaMalloc(&dv->priv[i], (size_t)b->elems * es * B + 256);
+      dv->buf[i] = dv->priv[i];
+    } else if (b->halo) {
+      dv->ws[i] = (long long)(((size_t)b->elems * es + 255) / 256 * 256 / es);
+      e = cudaMalloc(&dv->priv[i], (size_t)dv->ws[i] * es * B);
+      if (!e) e = cudaMemset(dv->priv[i], 0, (size_t)dv->ws[i] * es * B);
+      dv->buf[i] = dv->priv[i];
+    } else if (!is_int8_scratch(c, (int)i)) {
+      dv->ws[i] = (long long)(slot_bytes[b->slot] / es);
+      dv->buf[i] = (uint8_t *)dv->arena + slot_off[b->slot];
+    }
+    if (e) { free(slot_bytes); free(slot_off); return cerr(err, errlen, kind, e, "activation buffers"); }
+  }
+  free(slot_bytes);
+  free(slot_off);
+  /* int8 scratch, front-end and post-conv scratch, error word */
+  size_t qbytes = 256, rows = 8;
+  for (int i = 0; i < c->n_ops; i++) {
+    const bnn_op *op = &c->ops[i];
+    if (op->code != BNN_OP_PW_S8 && op->code != BNN_OP_GEMV_S8) continue;
+    const size_t r = (size_t)B * (op->code == BNN_OP_PW_S8 ? (size_t)op->p[4] : 1);
+    const size_t qb = r * R32(op->p[1]);
+    if (qb > qbytes) qbytes = qb;
+    if (r > rows) rows = r;
+  }
+  CK(cudaMalloc((void **)&dv->q, qbytes), "int8 row scratch");
+  CK(cudaMemset(dv->q, 0, qbytes), "int8 row scratch");
+  CK(cudaMalloc((void **)&dv->sa, sizeof(float) * rows), "int8 scale scratch");
+  CK(cudaMalloc((void **)&dv->za, sizeof(int32_t) * rows), "int8 zero-point scratch");
+  CK(cudaMalloc((void **)&dv->fe_minmax, sizeof(float) * 2 * B), "front-end scratch");
+  CK(cudaMalloc((void **)&dv->pcin, sizeof(float) * 6 * 1728 * B), "post-conv scratch");
+  CK(cudaMalloc((void **)&dv->err, sizeof(int)), "error word");
+  CK(cudaMemset(dv->err, 0, sizeof(int)), "error word");
+  CK(cudaMallocHost((void **)&dv->err_host, sizeof(int)), "error word (host)");
+  /* weights and GEMM plans */
+  for (int i = 0; i < c->n_ops; i++) {
+    if (op_weights(c, dv, i, err, errlen, kind)) return -1;
+    const bnn_op *op = &c->ops[i];
+    if (op->code == BNN_OP_PW_S8 || op->code == BNN_OP_GEMV_S8) {
+      bnn_devop *o = &dv->ops[i];
+      const int r = B * (op->code == BNN_OP_PW_S8 ? op->p[4] : 1);
+      if (bnnk_gemm_plan_init(&o->plan, dv->q, r, o->kq, o->w, op->p[0], op->p[3])) {
+        *kind = BNN_ERR_CPU;
+        snprintf(err, errlen, "op %d %s: TMA descriptors could not be made (driver too old?)", i, op->kname);
+        return -1;
+      }
+    }
+  }
+  CK(cudaDeviceSynchronize(), "device set-up");
+  return 0;
+}
+
+void bnn_rt_device_free(bnn_ctx *c, int di) {
+  bnn_dev *dv = c->dev[di];
+  if (!dv) return;
+  cudaSetDevice(dv->dev);
+  if (dv->stream) cudaStreamSynchronize((cudaStream_t)dv->stream);
+  if (dv->ops)
+    for (int i = 0; i < c->n_ops; i++) {
+      bnn_devop *o = &dv->ops[i];
+      cudaFree(o->w); cudaFree(o->sw); cudaFree(o->bias); cudaFree(o->cs);
+      for (int k = 0; k < 6; k++) cudaFree(o->f[k]);
+    }
+  for (int k = 0; k < dv->n_fe_mem; k++) cudaFree(dv->fe_mem[k]);
+  if (dv->events)
+    for (int k = 0; k < 2 * c->n_ops; k++)
+      if (dv->events[k]) cudaEventDestroy((cudaEvent_t)dv->events[k]);
+  free(dv->events);
+  free(dv->op_ms);
+  if (dv->priv)
+    for (uint32_t i = 0; i < c->path->n_buf; i++) cudaFree(dv->priv[i]);
+  cudaFree(dv->arena);
+  cudaFree(dv->q); cudaFree(dv->sa); cudaFree(dv->za); cudaFree(dv->fe_minmax); cudaFree(dv->pcin); cudaFree(dv->err);
+  if (dv->err_host) cudaFreeHost(dv->err_host);
+  if (dv->stream) cudaStreamDestroy((cudaStream_t)dv->stream);
+  free(dv->buf); free(dv->priv); free(dv->ws); free(dv->ops);
+  free(dv);
+  c->dev[di] = NULL;
+}
+
+/* ------------------------------------------------------------------ one batch */
+
+#define B_(a) (op->b[a] < 0 ? NULL : dv->buf[op->b[a]])
+#define WS(a) (op->b[a] < 0 ? 0 : dv->ws[op->b[a]])
+
+int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op1, void *stream) {
+  bnn_dev *dv = c->dev[di];
+  bnn_stream_t st = (bnn_stream_t)stream;
+  const uint32_t in = c->path->in_buf;
+  if (dv->prof_on) {
+    dv->prof_op0 = op0;
+    dv->prof_op1 = op1 < c->n_ops ? op1 : c->n_ops;
+  }
+  for (int i = op0; i < op1 && i < c->n_ops; i++) {
+    const bnn_op *op = &c->ops[i];
+    const bnn_devop *o = &dv->ops[i];
+    const int *p = op->p;
+    int rc = 0;
+    if (dv->prof_on) cudaEventRecord((cudaEvent_t)dv->events[2 * i], (cudaStream_t)st);
+#define IN_(a) ((uint32_t)op->b[a] == in ? (const float *)d_pcm : (const float *)B_(a))
+#define INWS(a) ((uint32_t)op->b[a] == in ? (long long)c->bufd[in].elems : WS(a))
+    switch (op->code) {
+    case BNN_OP_FE_STFT2:
+      rc = bnnk_fe_stft2(n, IN_(0), INWS(0), &dv->fe, dv->fe_minmax, B_(1), WS(1), st);
+      break;
+    case BNN_OP_C0POOL:
+      rc = bnnk_c0pool(n, IN_(0), INWS(0), o->f[0], o->f[1], B_(1), WS(1), st);
+      break;
+    case BNN_OP_PW_S8: {
+      const int M = p[4];
+      const float *gate = op->nb == 7 && op->b[6] >= 0 ? B_(6) : NULL;
+      rc = bnnk_quant(n * M, M, IN_(0), INWS(0), p[5], p[1], o->kq, gate, gate ? WS(6) : 0, dv->q, dv->sa, dv->za, st);
+      if (!rc) {
+        const bnn_buf_rec *r = op->b[2] >= 0 ? &c->bufd[op->b[2]] : NULL;
+        bnnk_epilogue e = {p[6], B_(1), WS(1), p[7], p[8], p[9], B_(2), WS(2), p[10],
+                           r && r->halo ? (int)r->W : 0, r && r->halo ? (int)r->halo : 0, o->sw, o->bias, o->cs};
+        rc = bnnk_gemm(&o->plan, n * M, M, dv->sa, dv->za, &e, dv->err, st);
+      }
+      break;
+    }
+    case BNN_OP_GEMV_S8: {
+      rc = bnnk_quant(n, 1, IN_(0), INWS(0), p[1], p[1], o->kq, NULL, 0, dv->q, dv->sa, dv->za, st);
+      if (!rc) {
+        bnnk_epilogue e = {p[4], B_(1), WS(1), p[3], 0, 0, NULL, 0, 0, 0, 0, o->sw, o->bias, o->cs};
+        rc = bnnk_gemm(&o->plan, n, 1, dv->sa, dv->za, &e, dv->err, st);
+      }
+      break;
+    }
+    case BNN_OP_DW3:
+      rc = bnnk_dw3(n, IN_(0), INWS(0), p[0], p[1], p[2], p[3], o->f[0], o->f[1], B_(1), WS(1), p[4], p[5], B_(2), WS(2), st);
+      break;
+    case BNN_OP_SE_GATE:
+      rc = bnnk_se_gate(n, p[0], p[1], o->f[0], o->f[1], o->f[2], o->f[3], IN_(0), INWS(0), p[2], B_(1), WS(1), st);
+      break;
+    case BNN_OP_POSTPC:
+      rc = bnnk_postpc(n, IN_(0), INWS(0), o->f[2], o->f[3], o->f[0], o->f[1], dv->pcin, B_(1), WS(1), st);
+      break;
+    default:
+      rc = cudaErrorNotSupported;
+    }
+#undef IN_
+#undef INWS
+    if (dv->prof_on) cudaEventRecord((cudaEvent_t)dv->events[2 * i + 1], (cudaStream_t)st);
+    if (rc) {
+      bnn_set_error(BNN_ERR_WINDOW, "window not scored: op %d %s could not be launched (CUDA error %d: %s); hint: check "
+                    "the GPU (nvidia-smi) and retry", i, op->kname, rc, cudaGetErrorString((cudaError_t)rc));
+      return -1;
+    }
+  }
+  return 0;
+}
+
+void bnn_rt_close(bnn_ctx *c) {
+  for (int i = 0; i < 64; i++)
+    if (c->dev[i]) bnn_rt_device_free(c, i);
+  free(c->bufd);
+  free(c->ops);
+}

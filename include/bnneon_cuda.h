@@ -1,0 +1,97 @@
+/* B200 additions to the bnneon API (additive: the reference's bnneon.h is unchanged; hosts check for these symbols
+ * with dlsym, as they do for bnn_set_threads, src/bnneon.h:94-98).
+ *
+ * Batching: the reference scores one window per bnn_infer call (src/bnneon.h:78-80, src/bnneon.c:310-330). A GPU
+ * needs many windows per launch, so bnn_infer_batch scores n windows per call; the results are bit-identical to n
+ * calls of bnn_infer (every op is per window).
+ *
+ * Per-op entry points: the kernel-level interface of the reference's int8 GEMM and depthwise routines
+ * (src/gemm_s8n.h:16-23 s8n_quant_rows / s8n_gemm_range, src/gemm_f32.h:46-51 dw3x3_f32), batched over windows and
+ * taking device pointers, for hosts that run their own graphs and for the parity tests.
+ *
+ * Pointers named d_* are device pointers on the current CUDA device; `stream` is a cudaStream_t (NULL = the legacy
+ * default stream). Functions return 0 on success, else -1 with bnn_last_error / bnn_last_error_kind set. */
+#ifndef BNNEON_CUDA_H
+#define BNNEON_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#include "bnneon.h"
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- batched inference */
+
+/* n windows of host memory: pcm [n][n_samples] -> out [n][n_classes], emb [n][emb_dim] (emb may be NULL). The
+ * windows are split into contiguous slices over the context's GPUs (bnn_set_threads) and into chunks of the batch
+ * capacity (bnn_set_batch). Synchronous. */
+int bnn_infer_batch(bnn_ctx *ctx, int n, const float *pcm, float *out, float *emb);
+/* the same with device-resident buffers on the context's first GPU (n <= the batch capacity); asynchronous on
+ * `stream` (NULL = the context's own stream, synchronized before return) */
+int bnn_infer_device(bnn_ctx *ctx, int n, const float *d_pcm, float *d_out, float *d_emb, void *stream);
+/* windows per launch sequence on each GPU (default 256, or the BNN_BATCH environment variable): sizes the device
+ * arena; 0 on success */
+int bnn_set_batch(bnn_ctx *ctx, int batch);
+int bnn_get_batch(const bnn_ctx *ctx);
+/* kernels launched by one bnn_infer_device call of n windows (the op list's launches) */
+int bnn_launches_per_batch(const bnn_ctx *ctx);
+
+/* ---- per-op profile on the first GPU (the reference's BNN_PROF per-op times, src/rt_pkg.c:558-625, measured with
+ * CUDA events on the launching stream): begin clears the totals and brackets every op of later launches with
+ * events; collect waits for the last launch and adds its op times; op_ms reads the totals (milliseconds). */
+int bnn_profile_begin(bnn_ctx *ctx);
+int bnn_profile_collect(bnn_ctx *ctx);
+double bnn_profile_op_ms(const bnn_ctx *ctx, int op);
+int bnn_profile_end(bnn_ctx *ctx);
+
+/* ---- op-level debugging (the reference's BNN_DUMP bisection, src/rt_pkg.c:512-526) on the first GPU:
+ * buffers are addressed by their package buffer id and hold n windows [n][elems] (elems from the package) */
+int bnn_debug_n_ops(const bnn_ctx *ctx);
+int bnn_debug_op_code(const bnn_ctx *ctx, int op);
+/* buffer 0 (the input window) <- pcm [n][n_samples] (host), then ops [op0, op1) on n windows */
+int bnn_debug_run_ops(bnn_ctx *ctx, int n, const float *pcm, int op0, int op1);
+int bnn_debug_get_buffer(bnn_ctx *ctx, int buf, int n, void *dst);
+int bnn_debug_set_buffer(bnn_ctx *ctx, int buf, int n, const void *src);
+
+/* ---- per-op entry points */
+
+/* loads the device tables (expf table, reciprocal-estimate table) on the current device; the context does this
+ * itself, the per-op entry points below need it once per device */
+int bnn_cuda_device_init(void);
+
+/* s8n_quant_rows (src/gemm_s8n.c:15-63), batched: rows r = w * Mw + m of d_x (window stride xws, row stride lda,
+ * floats), optionally times d_gate [B][K] (window stride gws) -> d_q [rows][Kq] int8 (Kq >= K; pads = zero point),
+ * d_sa, d_za [rows] */
+int bnn_cuda_quant_rows(int rows, int Mw, const float *d_x, long long xws, int lda, int K, int Kq,
+                        const float *d_gate, long long gws, int8_t *d_q, float *d_sa, int32_t *d_za, void *stream);
+
+/* PW_S8 / GEMV_S8 (src/rt_ops_s8n.c:92-158): an int8 1x1 conv built from the package's tensors (host pointers:
+ * w [Np/4][Kp/16][4][16], sw / cs / b [>= Np]) for up to rows_cap rows (windows x pixels) per run */
+typedef struct bnn_pw_s8 bnn_pw_s8;
+bnn_pw_s8 *bnn_pw_s8_new(int N, int K, int Kp, int Np, const int8_t *w, const float *sw, const int32_t *cs,
+                         const float *b, int rows_cap);
+/* B windows of Mw rows: quantize (gated if d_gate), GEMM, epilogue act (0 none, 1 SiLU, 2 ReLU) + residual, stored
+ * at the padded row of each pixel (ow / opad, as epi32, src/gemm_f32.h:15-24); window strides in floats. A padded
+ * output's halo is not written. */
+int bnn_pw_s8_run(bnn_pw_s8 *op, int B, int Mw, const float *d_x, long long xws, int lda, const float *d_gate,
+                  long long gws, int act, float *d_out, long long ows, int ldo, int ow, int opad, const float *d_res,
+                  long long rws, int ldr, int rw, int rpad, void *stream);
+/* the device error word of the op's GEMM (0 = no bounded wait ran out) */
+int bnn_pw_s8_error(bnn_pw_s8 *op);
+void bnn_pw_s8_free(bnn_pw_s8 *op);
+
+/* DW3 (src/gemm_f32.c:398-411, dw3x3_f32), batched: d_xp [B][(H+2)(W+2)][C] (zero halo 1), d_w [9][C], d_b [C] ->
+ * d_out [B][Ho Wo][C], d_chsum [B][C] */
+int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, int s, const float *d_w,
+                 const float *d_b, float *d_out, long long ows, int Ho, int Wo, float *d_chsum, long long cws,
+                 void *stream);
+
+/* elementwise functions of the int8 path, for tests: 0 SiLU, 1 SiLU (table estimate), 2 sigmoid, 3 FRECPE,
+ * 4 log2 polynomial, 5 exp2 polynomial (front end), 6 glibc expf */
+int bnn_cuda_fn(int fn, int n, const float *d_x, float *d_y, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,128 @@
+"""ctypes wrapper of liboracle.so, the CPU restatement of the reference's v2.4 neon-int8 path (TEST INFRASTRUCTURE).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs use this module; the product library never
+does. `make -C oracle` builds liboracle.so.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+_P, _I, _F, _L, _SZ, _S = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_long, ctypes.c_size_t, ctypes.c_char_p
+SIGS = {
+    "bnno_silu": (_F, [_F]), "bnno_sigmoid": (_F, [_F]), "bnno_frecpe": (_F, [_F]), "bnno_log2_acc": (_F, [_F]),
+    "bnno_exp2_acc": (_F, [_F]), "bnno_expf": (_F, [_F]),
+    "bnno_quant_rows": (None, [_P, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "bnno_s8_gemm": (None, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _I, _I, _I, _P, _I, _I, _I]),
+    "bnno_pw_s8": (None, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P, _I, _I, _I,
+                          _P, _P, _P]),
+    "bnno_dw3": (None, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
+    "bnno_se_gate": (None, [_I, _I, _P, _P, _P, _P, _P, _I, _P]),
+    "bnno_c0pool": (None, [_P, _P, _P, _P]),
+    "bnno_postpc": (None, [_P, _P, _P, _P, _P, _P]),
+    "bnno_pkg_open": (_P, [_S, _S, _S, _SZ]), "bnno_pkg_close": (None, [_P]),
+    "bnno_pkg_n_ops": (_I, [_P]), "bnno_pkg_n_bufs": (_I, [_P]), "bnno_pkg_op_code": (_I, [_P, _I]),
+    "bnno_pkg_buf_elems": (_L, [_P, _I, _P]), "bnno_pkg_out_elems": (_I, [_P]), "bnno_pkg_emb_elems": (_I, [_P]),
+    "bnno_pkg_run_range": (_I, [_P, _P, _I, _I]), "bnno_pkg_run": (_I, [_P, _P, _P, _P]),
+    "bnno_pkg_get_buf": (_I, [_P, _I, _P, _SZ]), "bnno_pkg_set_buf": (_I, [_P, _I, _P, _SZ]),
+    "bnno_pkg_run_many": (_I, [_S, _S, _I, _P, _P, _P, _I]),
+}
+DTYPES = {0: np.float32, 1: np.float16, 2: np.int8, 3: np.int32}
+_LIB = None
+
+
+def lib():
+    global _LIB  # pylint: disable=global-statement
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} missing: run `make -C oracle`")
+        h = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGS.items():
+            getattr(h, name).restype = res
+            getattr(h, name).argtypes = args
+        _LIB = h
+    return _LIB
+
+
+def ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+def fn(name, x):
+    """An elementwise oracle function over an array."""
+    f = getattr(lib(), name)
+    x = np.asarray(x, np.float32).reshape(-1)
+    return np.array([f(float(v)) for v in x], np.float32)
+
+
+class Package:
+    """A package executed on the CPU, one window at a time."""
+
+    def __init__(self, path, path_name="neon-int8"):
+        err = ctypes.create_string_buffer(256)
+        self.h = lib().bnno_pkg_open(path.encode(), path_name.encode(), err, 256)
+        if not self.h:
+            raise OSError(err.value.decode())
+        self.path, self.path_name = path, path_name
+
+    def close(self):
+        if self.h:
+            lib().bnno_pkg_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def n_ops(self):
+        return lib().bnno_pkg_n_ops(self.h)
+
+    @property
+    def n_bufs(self):
+        return lib().bnno_pkg_n_bufs(self.h)
+
+    def op_code(self, i):
+        return lib().bnno_pkg_op_code(self.h, i)
+
+    def buf_info(self, i):
+        dt = ctypes.c_int()
+        e = lib().bnno_pkg_buf_elems(self.h, i, ctypes.byref(dt))
+        return e, DTYPES[dt.value]
+
+    def run(self, pcm):
+        nc, ne = lib().bnno_pkg_out_elems(self.h), lib().bnno_pkg_emb_elems(self.h)
+        out, emb = np.empty(nc, np.float32), np.empty(ne, np.float32)
+        x = np.ascontiguousarray(pcm, np.float32)
+        if lib().bnno_pkg_run(self.h, ptr(x), ptr(out), ptr(emb)):
+            raise RuntimeError("oracle run failed")
+        return out, emb
+
+    def run_range(self, pcm, op0, op1):
+        self._pcm = np.ascontiguousarray(pcm, np.float32)  # keep alive: buffer 0 points at it
+        if lib().bnno_pkg_run_range(self.h, ptr(self._pcm), op0, op1):
+            raise RuntimeError("oracle run failed")
+
+    def get(self, i):
+        e, dt = self.buf_info(i)
+        a = np.empty(e, dt)
+        lib().bnno_pkg_get_buf(self.h, i, ptr(a), a.nbytes)
+        return a
+
+    def set(self, i, a):
+        a = np.ascontiguousarray(a)
+        lib().bnno_pkg_set_buf(self.h, i, ptr(a), a.nbytes)
+
+
+def run_many(path, pcm, threads=1, path_name="neon-int8"):
+    """n windows on `threads` CPU threads: (out [n][n_classes], emb [n][emb_dim])."""
+    p = Package(path, path_name)
+    nc, ne = lib().bnno_pkg_out_elems(p.h), lib().bnno_pkg_emb_elems(p.h)
+    p.close()
+    x = np.ascontiguousarray(pcm, np.float32)
+    out = np.empty((x.shape[0], nc), np.float32)
+    emb = np.empty((x.shape[0], ne), np.float32)
+    if lib().bnno_pkg_run_many(path.encode(), path_name.encode(), x.shape[0], ptr(x), ptr(out), ptr(emb), threads):
+        raise RuntimeError("oracle run failed")
+    return out, emb

@@ -80,7 +80,7 @@ def main():
         lw = lower.Lowering(pkgfmt.Package(), [], synth.PATH, 16)
         tl, shp = lw.s8_tensors("t", w, b)
         arrays[f"w{i}"] = w
-        arrays[f"b{i}"] = b
+        arrays[f"bias{i}"] = b
         arrays[f"shape{i}"] = np.array(shp, np.int32)
         for j, suffix in enumerate(("q", "sw", "cs", "b")):
             arrays[f"{suffix}{i}"] = lw.pkg.tensors[tl[j]][1]
