@@ -42,3 +42,23 @@ def op_io(code, bl):
     ins = [b for a, b in enumerate(bl) if b >= 0 and not (mask >> a & 1) and a not in scratch]
     outs = [b for a, b in enumerate(bl) if b >= 0 and (mask >> a & 1) and a not in scratch]
     return ins, outs
+
+
+def op_offsets(path, path_name="neon-int8"):
+    """File offsets of the op records of the named path (for tests that corrupt one record)."""
+    with open(path, "rb") as f:
+        data = f.read()
+    _, _, n_paths, _ = struct.unpack_from("<4I", data, 16)
+    _, _, path_off, _ = struct.unpack_from("<4Q", data, 32)
+    for i in range(n_paths):
+        o = path_off + 72 * i
+        if data[o:o + 24].rstrip(b"\0").decode() != path_name:
+            continue
+        _, _, n_ops, _, _, _, _, _ = struct.unpack_from("<8I", data, o + 24)
+        _, ops_off = struct.unpack_from("<2Q", data, o + 56)
+        offs, q = [], ops_off
+        for _ in range(n_ops):
+            offs.append(q)
+            q += struct.unpack_from("<H", data, q + 2)[0]
+        return offs
+    raise KeyError(path_name)

@@ -107,8 +107,8 @@ __global__ void k_quant_scalar(int rows, int Mw, const float *__restrict__ x, lo
   auto val = [&](int k) { return gr ? __fmul_rn(xr[k], gr[k]) : xr[k]; };
   float lo = __int_as_float(0x7f800000), hi = __int_as_float(0xff800000);
   int k = 0;
-  for (; k + 4 <= K; k++) { lo = fmin_nan(lo, val(k)); hi = fmax_nan(hi, val(k)); }
-  for (; k < K; k++) { lo = fminf(lo, val(k)); hi = fmaxf(hi, val(k)); }
+  for (; k < (K & ~3); k++) { lo = fmin_nan(lo, val(k)); hi = fmax_nan(hi, val(k)); }  // the 4-wide NEON part
+  for (; k < K; k++) { lo = fminf(lo, val(k)); hi = fmaxf(hi, val(k)); }                // the scalar tail
   float inv, s;
   int32_t z;
   const float d = __fsub_rn(hi, lo);

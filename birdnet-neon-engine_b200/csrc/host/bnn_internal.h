@@ -85,7 +85,7 @@ typedef struct {
   int *err;             /* device error word */
   int *err_host;        /* pinned */
   bnnk_fe_tables fe;
-  void *fe_mem[16];
+  void *fe_mem[32];     /* the front-end tables: 9 per spectrogram */
   int n_fe_mem;
   /* per-op CUDA-event profile (bnn_profile_*): events[2 i], events[2 i + 1] bracket op i of the last launch */
   void **events;

@@ -56,7 +56,9 @@ def test_elementwise(lib, fn, name):
     x = sample_floats(20000, fn)
     if fn == 4:
         x = np.abs(x[np.isfinite(x) & (np.abs(x) >= 1e-30)])  # the front end's log2 takes max(|m|, 1e-30)
-    if fn == 1:
+    if fn in (1, 5):
+        # the table estimate serves finite SiLU inputs; exp2_acc builds its result from the bits of its polynomial,
+        # so a NaN's payload (which differs between AArch64 and CUDA) would leak into the bits: finite inputs only
         x = x[np.isfinite(x)]
     y = torch.empty(x.size, dtype=torch.float32, device="cuda")
     xd = dev(x)
