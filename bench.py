@@ -182,6 +182,8 @@ def main():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu", action="store_true",
+                    help="for profiler captures: warm-up steps + one step through bnn_infer_device, no timing, no JSON")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -224,6 +226,14 @@ def main():
     d_out = torch.empty((B, nc), dtype=torch.float32, device="cuda")
     d_emb = torch.empty((B, ne), dtype=torch.float32, device="cuda")
     sp = stream.cuda_stream
+
+    if args.ncu:  # warm-up + 1 step for a profiler; nothing is timed or printed as a result
+        for _ in range(args.warmup + 1):
+            m.infer_device(B, d_pcm.data_ptr(), d_out.data_ptr(), d_emb.data_ptr(), sp)
+        stream.synchronize()
+        print(f"ncu mode: {args.warmup + 1} steps of {m.launches_per_batch} launches", flush=True)
+        m.close()
+        return
 
     # ---- device-resident throughput
     for _ in range(args.warmup):

@@ -1,0 +1,325 @@
+// The fp32 ops of the v2.4 int8 package on CUDA cores: depthwise 3x3 + SiLU + channel sums (DW3), the SE gate
+// (SE_GATE), the c0 conv + pool (C0POOL) and the post BN + pc conv + mean (POSTPC); the front end is in k_fe.cu.
+// Each output is computed with the reference's operations in the reference's order (fused where the NEON code fuses,
+// rounded where it rounds), so the values are bit-identical; only the parallel schedule is ours, and no reference
+// reduction is split across threads except where its order is restated exactly.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "bnn_kernels.h"
+#include "emu.cuh"
+
+namespace bnn {
+
+// ------------------------------------------------------------------ DW3 (src/gemm_f32.c:214-440)
+
+// depthwise 3x3 (pad 1, stride s) + SiLU: one thread per (window, output pixel, 4 channels). Per channel the three
+// column partial sums of DW_ACC (gemm_f32.c:221-225): acc = b + w0 A0 + w3 A1 + w6 A2 (fused, in that order),
+// acb = w1 B0 + w4 B1 + w7 B2, acd = w2 C0 + w5 C1 + w8 C2, out = SiLU(acc + (acb + acd)).
+__global__ void __launch_bounds__(256) k_dw3_out(long long total, const float *__restrict__ xp, long long xws, int W,
+                                                 int C, int s, const float *__restrict__ wt,
+                                                 const float *__restrict__ bias, float *__restrict__ out,
+                                                 long long ows, int Wo, int P) {
+  __shared__ uint32_t lut[256];
+  lut[threadIdx.x] = g_frecpe_lut[threadIdx.x];
+  __syncthreads();
+  const long long idx = blockIdx.x * 256LL + threadIdx.x;
+  if (idx >= total) return;
+  const int C4 = C >> 2;
+  const int c4 = (int)(idx % C4);
+  const long long rest = idx / C4;
+  const int p = (int)(rest % P), win = (int)(rest / P);
+  const int oy = p / Wo, ox = p - oy * Wo, Wp = W + 2, c = 4 * c4;
+  const float *q = xp + win * xws + ((long long)(oy * s) * Wp + (long long)ox * s) * C + c;
+  float4 x[3][3];
+#pragma unroll
+  for (int ky = 0; ky < 3; ky++)
+#pragma unroll
+    for (int kx = 0; kx < 3; kx++) x[ky][kx] = __ldg(reinterpret_cast<const float4 *>(q + ((long long)ky * Wp + kx) * C));
+  float4 w[9];
+#pragma unroll
+  for (int t = 0; t < 9; t++) w[t] = __ldg(reinterpret_cast<const float4 *>(wt + t * C + c));
+  const float4 b4 = __ldg(reinterpret_cast<const float4 *>(bias + c));
+  float r[4];
+#pragma unroll
+  for (int l = 0; l < 4; l++) {
+#define E_(v) (l == 0 ? (v).x : l == 1 ? (v).y : l == 2 ? (v).z : (v).w)
+    float acc = __fmaf_rn(E_(w[0]), E_(x[0][0]), E_(b4));
+    float acb = __fmul_rn(E_(w[1]), E_(x[0][1]));
+    float acd = __fmul_rn(E_(w[2]), E_(x[0][2]));
+    acc = __fmaf_rn(E_(w[3]), E_(x[1][0]), acc);
+    acb = __fmaf_rn(E_(w[4]), E_(x[1][1]), acb);
+    acd = __fmaf_rn(E_(w[5]), E_(x[1][2]), acd);
+    acc = __fmaf_rn(E_(w[6]), E_(x[2][0]), acc);
+    acb = __fmaf_rn(E_(w[7]), E_(x[2][1]), acb);
+    acd = __fmaf_rn(E_(w[8]), E_(x[2][2]), acd);
+#undef E_
+    r[l] = silu<true>(__fadd_rn(acc, __fadd_rn(acb, acd)), lut);
+  }
+  *reinterpret_cast<float4 *>(out + win * ows + (long long)p * C + c) = make_float4(r[0], r[1], r[2], r[3]);
+}
+
+// channel sums: chsum[c] = ((0 + v_0) + v_1) + ... over the output pixels in raster order (silu_rows_f32,
+// gemm_f32.c:303-328; dw_silu_row16 :342-365). One thread per (window, channel); 16 loads in flight per chain.
+__global__ void __launch_bounds__(256) k_dw3_chsum(int total, const float *__restrict__ out, long long ows, int P, int C,
+                                                   float *__restrict__ chsum, long long cws) {
+  const int idx = blockIdx.x * 256 + threadIdx.x;
+  if (idx >= total) return;
+  const int win = idx / C, c = idx - win * C;
+  const float *o = out + win * ows + c;
+  float cs = 0.f;
+  int p = 0;
+  for (; p + 16 <= P; p += 16) {
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __ldg(o + (long long)(p + i) * C);
+#pragma unroll
+    for (int i = 0; i < 16; i++) cs = __fadd_rn(cs, v[i]);
+  }
+  for (; p < P; p++) cs = __fadd_rn(cs, __ldg(o + (long long)p * C));
+  chsum[win * cws + c] = cs;
+}
+
+// ------------------------------------------------------------------ SE_GATE (src/v24_f32.c:164-179, rt_ops_f32.c:272-283)
+
+// One CTA per window. fc1 row r: 8 threads hold the 8 NEON accumulator lanes (a0 lanes 0-3, a1 lanes 0-3) over
+// c = 8i + lane, then (a0 + a1) lane-wise and the FADDP reduction (v0 + v1) + (v2 + v3); SiLU with libm expf and an
+// IEEE division. fc2 per channel from the bias, one FMA per r in order, then the sigmoid. The chains are sequential;
+// their loads are independent, so they are issued in batches ahead of the FMAs.
+constexpr int kSeThreads = 512;
+__global__ void __launch_bounds__(kSeThreads) k_se_gate(int C, int rd, const float *__restrict__ w1,
+                                                        const float *__restrict__ b1, const float *__restrict__ w2t,
+                                                        const float *__restrict__ b2, const float *__restrict__ chsum,
+                                                        long long cws, int P, float *__restrict__ gate, long long gws) {
+  extern __shared__ float sm[];
+  float *mean = sm, *s1 = sm + C;
+  const int win = blockIdx.x, tid = threadIdx.x;
+  const float inv = __fdiv_rn(1.f, __int2float_rn(P));
+  for (int c = tid; c < C; c += kSeThreads) mean[c] = __fmul_rn(chsum[win * cws + c], inv);
+  __syncthreads();
+  const int lane8 = tid & 7, C8 = C >> 3;
+  for (int r0 = 0; r0 < rd; r0 += kSeThreads / 8) {
+    const int r = r0 + tid / 8;
+    float a = 0.f;
+    if (r < rd) {
+      const float *wr = w1 + (long long)r * C + lane8;
+      const float *mr = mean + lane8;
+      int i = 0;
+      for (; i + 8 <= C8; i += 8) {
+        float wv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) wv[u] = __ldg(wr + 8 * (i + u));
+#pragma unroll
+        for (int u = 0; u < 8; u++) a = __fmaf_rn(wv[u], mr[8 * (i + u)], a);
+      }
+      for (; i < C8; i++) a = __fmaf_rn(__ldg(wr + 8 * i), mr[8 * i], a);
+    }
+    // lanes l and l + 4 hold a0[l] and a1[l]
+    const float other = __shfl_down_sync(0xffffffffu, a, 4, 8);
+    const float v = __fadd_rn(a, other);  // v[l] for l < 4
+    const float v1 = __shfl_down_sync(0xffffffffu, v, 1, 8), v2 = __shfl_down_sync(0xffffffffu, v, 2, 8),
+                v3 = __shfl_down_sync(0xffffffffu, v, 3, 8);
+    if (r < rd && lane8 == 0) {
+      const float xr = __fadd_rn(__fadd_rn(__fadd_rn(v, v1), __fadd_rn(v2, v3)), b1[r]);
+      s1[r] = __fdiv_rn(xr, __fadd_rn(1.f, glibc_expf(-xr, c_expf_tab)));
+    }
+  }
+  __syncthreads();
+  for (int c = tid; c < C; c += kSeThreads) {
+    float g = b2[c];
+    int r = 0;
+    for (; r + 16 <= rd; r += 16) {
+      float wv[16];
+#pragma unroll
+      for (int u = 0; u < 16; u++) wv[u] = __ldg(w2t + (long long)(r + u) * C + c);
+#pragma unroll
+      for (int u = 0; u < 16; u++) g = __fmaf_rn(wv[u], s1[r + u], g);
+    }
+    for (; r < rd; r++) g = __fmaf_rn(__ldg(w2t + (long long)r * C + c), s1[r], g);
+    gate[win * gws + c] = sigmoid(g);
+  }
+}
+
+// ------------------------------------------------------------------ C0POOL (src/v24_f32.c:139-147, gemm_f32.c:60-70)
+
+// One CTA per (output row oy, window); thread qx computes the pooled pixel qx: conv pixels 2qx and 2qx + 1, 24
+// channels each, K = 64 fused multiply-adds in (ky, kx, ci) order from 0, bias added after, ReLU, max | average.
+// The 4 padded input rows sit in shared memory transposed by 8-float phase (float 8i + r at [r][i]) so that the 32
+// threads of a warp, whose patches start 8 floats apart, read consecutive words.
+__global__ void __launch_bounds__(128) k_c0pool(const float *__restrict__ img, long long iws, const float *__restrict__ wt,
+                                                const float *__restrict__ bias, float *__restrict__ pin, long long pws) {
+  constexpr int PWD = 518, RF = PWD * 2, NI = (RF + 7) / 8 + 1;  // padded width: 3 + 511 + 4 pixels
+  __shared__ float rows[4][8][NI];
+  __shared__ __align__(16) float ws[64][24];
+  __shared__ float bs[24];
+  const int oy = blockIdx.x, win = blockIdx.y, tid = threadIdx.x;
+  const float *im = img + win * iws;
+  for (int i = tid; i < 4 * 8 * NI; i += 128) {
+    const int r = i / (8 * NI), rem = i - r * 8 * NI, ph = rem / NI, ii = rem - ph * NI;
+    const int cidx = 8 * ii + ph;  // float index within the padded row
+    const int y = 2 * oy + r - 1, xcol = cidx / 2 - 3, ch = cidx & 1;
+    rows[r][ph][ii] = (cidx < RF && y >= 0 && y < 96 && xcol >= 0 && xcol < 511) ? im[((long long)y * 511 + xcol) * 2 + ch]
+                                                                                  : 0.f;
+  }
+  for (int i = tid; i < 64 * 24; i += 128) ws[i / 24][i % 24] = wt[i];
+  if (tid < 24) bs[tid] = bias[tid];
+  __syncthreads();
+  const int qx = tid;
+  float acc0[24], acc1[24];
+#pragma unroll
+  for (int n = 0; n < 24; n++) acc0[n] = acc1[n] = 0.f;
+  for (int ky = 0; ky < 4; ky++) {
+#pragma unroll 2
+    for (int kk = 0; kk < 16; kk++) {
+      const int c0 = kk, c1 = kk + 4;  // float offsets of the two pixels' patches from 8 qx
+      const float a0 = rows[ky][c0 & 7][qx + (c0 >> 3)], a1 = rows[ky][c1 & 7][qx + (c1 >> 3)];
+      const float4 *wr = reinterpret_cast<const float4 *>(ws[ky * 16 + kk]);
+#pragma unroll
+      for (int n4 = 0; n4 < 6; n4++) {
+        const float4 w = wr[n4];
+        acc0[4 * n4] = __fmaf_rn(w.x, a0, acc0[4 * n4]);
+        acc0[4 * n4 + 1] = __fmaf_rn(w.y, a0, acc0[4 * n4 + 1]);
+        acc0[4 * n4 + 2] = __fmaf_rn(w.z, a0, acc0[4 * n4 + 2]);
+        acc0[4 * n4 + 3] = __fmaf_rn(w.w, a0, acc0[4 * n4 + 3]);
+        acc1[4 * n4] = __fmaf_rn(w.x, a1, acc1[4 * n4]);
+        acc1[4 * n4 + 1] = __fmaf_rn(w.y, a1, acc1[4 * n4 + 1]);
+        acc1[4 * n4 + 2] = __fmaf_rn(w.z, a1, acc1[4 * n4 + 2]);
+        acc1[4 * n4 + 3] = __fmaf_rn(w.w, a1, acc1[4 * n4 + 3]);
+      }
+    }
+  }
+  float *o = pin + win * pws + ((long long)oy * 128 + qx) * 48;
+#pragma unroll
+  for (int n4 = 0; n4 < 6; n4++) {
+    float mx[4], av[4];
+#pragma unroll
+    for (int l = 0; l < 4; l++) {
+      const int n = 4 * n4 + l;
+      const float u = fmax_nan(__fadd_rn(acc0[n], bs[n]), 0.f), v = fmax_nan(__fadd_rn(acc1[n], bs[n]), 0.f);
+      mx[l] = fmax_nan(u, v);
+      av[l] = __fmul_rn(__fadd_rn(u, v), 0.5f);
+    }
+    *reinterpret_cast<float4 *>(o + 4 * n4) = make_float4(mx[0], mx[1], mx[2], mx[3]);
+    *reinterpret_cast<float4 *>(o + 24 + 4 * n4) = make_float4(av[0], av[1], av[2], av[3]);
+  }
+}
+
+// ------------------------------------------------------------------ POSTPC (src/v24_f32.c:245-266)
+
+// post BN + ReLU and the 3x3 valid im2col: pcin [B][6][1728]
+__global__ void k_postpc_im2col(const float *__restrict__ X, long long xws, const float *__restrict__ ps,
+                                const float *__restrict__ pb, float *__restrict__ pcin) {
+  const int win = blockIdx.x;
+  for (int i = threadIdx.x; i < 6 * 1728; i += blockDim.x) {
+    const int ox = i / 1728, k = i - ox * 1728, tap = k / 192, c = k - tap * 192;
+    const int ky = tap / 3, kx = tap - ky * 3;
+    const float v = X[win * xws + (long long)(ky * 8 + ox + kx) * 192 + c];
+    pcin[(long long)win * 6 * 1728 + i] = fmax_nan(__fmaf_rn(v, ps[c], pb[c]), 0.f);
+  }
+}
+
+// pc GEMM + ReLU + mean: thread = 2 output channels for WG windows x 6 rows, sequential fused multiply-adds from 0 over
+// k (the reference's K loop), bias after, ReLU, then the 6 rows added in order and scaled by 1/6. The rows of a
+// window-group sit in shared memory, read 4 k at a time.
+constexpr int kPcWG = 8, kPcKC = 64, kPcT = 64;
+__global__ void __launch_bounds__(kPcT) k_postpc_gemm(int B, const float *__restrict__ pcin, const float *__restrict__ wt,
+                                                     const float *__restrict__ bias, float *__restrict__ feat,
+                                                     long long fws) {
+  __shared__ __align__(16) float a_s[kPcWG][6][kPcKC];
+  const int n = blockIdx.x * (2 * kPcT) + 2 * threadIdx.x, w0 = blockIdx.y * kPcWG;
+  float acc[kPcWG][6][2];
+#pragma unroll
+  for (int j = 0; j < kPcWG; j++)
+#pragma unroll
+    for (int r = 0; r < 6; r++) acc[j][r][0] = acc[j][r][1] = 0.f;
+  for (int k0 = 0; k0 < 1728; k0 += kPcKC) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kPcWG * 6 * kPcKC / 4; i += kPcT) {
+      const int e = 4 * i, j = e / (6 * kPcKC), rem = e - j * 6 * kPcKC, r = rem / kPcKC, kk = rem - r * kPcKC;
+      const float4 v = (w0 + j < B) ? *reinterpret_cast<const float4 *>(pcin + ((long long)(w0 + j) * 6 + r) * 1728 + k0 + kk)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4 *>(&a_s[j][r][kk]) = v;
+    }
+    __syncthreads();
+    for (int kk = 0; kk < kPcKC; kk += 4) {
+      float2 w[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) w[u] = __ldg(reinterpret_cast<const float2 *>(wt + (long long)(k0 + kk + u) * 1024 + n));
+#pragma unroll
+      for (int j = 0; j < kPcWG; j++)
+#pragma unroll
+        for (int r = 0; r < 6; r++) {
+          const float4 a = *reinterpret_cast<const float4 *>(&a_s[j][r][kk]);
+          acc[j][r][0] = __fmaf_rn(a.x, w[0].x, acc[j][r][0]);
+          acc[j][r][1] = __fmaf_rn(a.x, w[0].y, acc[j][r][1]);
+          acc[j][r][0] = __fmaf_rn(a.y, w[1].x, acc[j][r][0]);
+          acc[j][r][1] = __fmaf_rn(a.y, w[1].y, acc[j][r][1]);
+          acc[j][r][0] = __fmaf_rn(a.z, w[2].x, acc[j][r][0]);
+          acc[j][r][1] = __fmaf_rn(a.z, w[2].y, acc[j][r][1]);
+          acc[j][r][0] = __fmaf_rn(a.w, w[3].x, acc[j][r][0]);
+          acc[j][r][1] = __fmaf_rn(a.w, w[3].y, acc[j][r][1]);
+        }
+    }
+  }
+  const float b0 = bias[n], b1v = bias[n + 1];
+#pragma unroll
+  for (int j = 0; j < kPcWG; j++) {
+    if (w0 + j >= B) break;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int r = 0; r < 6; r++) {
+      s0 = __fadd_rn(s0, fmax_nan(__fadd_rn(acc[j][r][0], b0), 0.f));
+      s1 = __fadd_rn(s1, fmax_nan(__fadd_rn(acc[j][r][1], b1v), 0.f));
+    }
+    *reinterpret_cast<float2 *>(feat + (long long)(w0 + j) * fws + n) =
+        make_float2(__fmul_rn(s0, 0x1.555556p-3f), __fmul_rn(s1, 0x1.555556p-3f));
+  }
+}
+
+}  // namespace bnn
+
+using namespace bnn;
+
+// ------------------------------------------------------------------ launchers
+
+extern "C" int bnnk_fp32_tables_init(const unsigned long long *tab, const uint32_t *lut) {
+  cudaError_t e = cudaMemcpyToSymbol(c_expf_tab, tab, sizeof(unsigned long long) * 32);
+  if (e) return e;
+  return cudaMemcpyToSymbol(g_frecpe_lut, lut, sizeof(uint32_t) * 256);
+}
+
+extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int C, int s, const float *w,
+                        const float *b, float *out, long long ows, int Ho, int Wo, float *chsum, long long cws,
+                        bnn_stream_t st) {
+  (void)H;
+  if (B <= 0) return 0;
+  const int P = Ho * Wo;
+  const long long total = (long long)B * P * (C / 4);
+  k_dw3_out<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(total, xp, xws, W, C, s, w, b, out, ows, Wo, P);
+  const int tc = B * C;
+  k_dw3_chsum<<<(tc + 255) / 256, 256, 0, st>>>(tc, out, ows, P, C, chsum, cws);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_se_gate(int B, int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,
+                            const float *chsum, long long cws, int P, float *gate, long long gws, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  const size_t smem = sizeof(float) * (size_t)(C + rd);
+  k_se_gate<<<B, kSeThreads, smem, st>>>(C, rd, w1, b1, w2t, b2, chsum, cws, P, gate, gws);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_c0pool(int B, const float *img, long long iws, const float *wt, const float *b, float *pin,
+                           long long pws, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  k_c0pool<<<dim3(48, B), 128, 0, st>>>(img, iws, wt, b, pin, pws);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_postpc(int B, const float *X, long long xws, const float *post_s, const float *post_b,
+                           const float *wt, const float *b, float *pcin, float *feat, long long fws, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  k_postpc_im2col<<<B, 256, 0, st>>>(X, xws, post_s, post_b, pcin);
+  k_postpc_gemm<<<dim3(1024 / (2 * kPcT), (B + kPcWG - 1) / kPcWG), kPcT, 0, st>>>(B, pcin, wt, b, feat, fws);
+  return cudaGetLastError();
+}

@@ -1,0 +1,247 @@
+// FE_STFT2 on B200: the BirdNET v2.4 two-spectrogram front end (src/v24_fe.c:127-224, src/fft_tab.h:25-77).
+//
+// Arithmetic is the reference's, element for element: y = ((x - mn) / den - 0.5) * 2 per sample; z[n] = y[2n] w[2n]
+// + i y[2n+1] w[2n+1] in bit-reversed order; the DIT transform with the first two levels fused (no twiddles), then
+// radix-2^2 passes over level pairs (len, 2 len) with twiddles w1 = tw[j M/len], w2 = tw[j M/(2 len)], then one
+// radix-2 level when log2 M is odd; complex products formed as (x w)_r = fma(-x_i, w_i, x_r w_r),
+// (x w)_i = fma(x_i, w_r, x_r w_i); the real part of the half-size transform; the sparse mel with two alternating
+// accumulators; max(|.|, 1e-30); |m|^(2p) by the log2 / exp2 polynomials; BN as one fma; rows written reversed.
+//
+// Schedule (ours): one CTA per (8 frames, spectrogram, window). The frames' samples are normalized once into a
+// shared segment. A frame of M points is owned by M/16 threads holding 16 points each in registers; the 16-point
+// sets are chosen so that two consecutive passes close over them (levels 1-4: 16 consecutive bit-reversed
+// positions; levels 5-8: the points j + 16a + 64b of a 256-block; levels 9-10: four points 256 apart), so a frame
+// makes 3 round trips through shared memory instead of one per pass. Shared indices are padded (p + p/16) so the
+// 16-strided accesses do not collide in banks.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "bnn_kernels.h"
+#include "emu.cuh"
+
+namespace bnn {
+
+constexpr int kNsamp = 144000, kNfr = 511, kNmel = 96, kFG = 8;
+
+__device__ __forceinline__ int sx(int p) { return p + (p >> 4); }
+
+struct cpx {
+  float r, i;
+};
+// x * w as the reference forms it
+__device__ __forceinline__ cpx cmul(cpx x, float wr, float wi) {
+  return {__fmaf_rn(-x.i, wi, __fmul_rn(x.r, wr)), __fmaf_rn(x.i, wr, __fmul_rn(x.r, wi))};
+}
+
+// one radix-2^2 butterfly group (fft_tab.h:51-62): a, b, c, d = points i+j, +h, +2h, +3h
+__device__ __forceinline__ void r22(cpx &a, cpx &b, cpx &c, cpx &d, float w1r, float w1i, float w2r, float w2i) {
+  cpx t = cmul(b, w1r, w1i);
+  const cpx a1 = {__fadd_rn(a.r, t.r), __fadd_rn(a.i, t.i)}, b1 = {__fsub_rn(a.r, t.r), __fsub_rn(a.i, t.i)};
+  t = cmul(d, w1r, w1i);
+  const cpx c1 = {__fadd_rn(c.r, t.r), __fadd_rn(c.i, t.i)}, d1 = {__fsub_rn(c.r, t.r), __fsub_rn(c.i, t.i)};
+  t = cmul(c1, w2r, w2i);
+  a = {__fadd_rn(a1.r, t.r), __fadd_rn(a1.i, t.i)};
+  c = {__fsub_rn(a1.r, t.r), __fsub_rn(a1.i, t.i)};
+  const cpx u = cmul(d1, w2r, w2i);
+  b = {__fadd_rn(b1.r, u.i), __fsub_rn(b1.i, u.r)};  // b1 + (-i) u
+  d = {__fsub_rn(b1.r, u.i), __fadd_rn(b1.i, u.r)};
+}
+
+// the first two levels fused, without twiddles (fft_tab.h:28-38)
+__device__ __forceinline__ void r4first(cpx &a, cpx &b, cpx &c, cpx &d) {
+  const cpx s0 = {__fadd_rn(a.r, b.r), __fadd_rn(a.i, b.i)}, d0 = {__fsub_rn(a.r, b.r), __fsub_rn(a.i, b.i)};
+  const cpx s1 = {__fadd_rn(c.r, d.r), __fadd_rn(c.i, d.i)}, d1 = {__fsub_rn(c.r, d.r), __fsub_rn(c.i, d.i)};
+  a = {__fadd_rn(s0.r, s1.r), __fadd_rn(s0.i, s1.i)};
+  c = {__fsub_rn(s0.r, s1.r), __fsub_rn(s0.i, s1.i)};
+  b = {__fadd_rn(d0.r, d1.i), __fsub_rn(d0.i, d1.r)};
+  d = {__fsub_rn(d0.r, d1.i), __fadd_rn(d0.i, d1.r)};
+}
+
+template <int LG>
+__device__ __forceinline__ void spec(const float *__restrict__ x, float mn, float den, const bnnk_fe_tables &t,
+                                     float *__restrict__ img, int t0, float *sm) {
+  constexpr int M = 1 << LG, BR = LG == 10 ? 0 : 1, HOP = BR ? 280 : 278, TPF = M / 16, FF = 256 / TPF;
+  constexpr int SEG = (kFG - 1) * HOP + 2 * M, MP = M + M / 16;
+  float *seg = sm, *re = sm + SEG, *im = re + FF * MP, *R = im + FF * MP;
+  const int tid = threadIdx.x, fl = tid / TPF, lt = tid % TPF;
+  const float *__restrict__ win = t.win[BR];
+  const float *__restrict__ twr = t.tw_re[BR];
+  const float *__restrict__ twi = t.tw_im[BR];
+  const int nfr = min(kFG, kNfr - t0);
+  const int start = t0 * HOP, len = (nfr - 1) * HOP + 2 * M;
+  for (int i = tid; i < len; i += 256)
+    seg[i] = __fmul_rn(__fsub_rn(__fdiv_rn(__fsub_rn(x[start + i], mn), den), 0.5f), 2.f);
+  const int klo = t.klo[BR], nk = t.khi[BR] - klo;
+  __syncthreads();
+  for (int f0 = 0; f0 < nfr; f0 += FF) {
+    const int f = f0 + fl;  // this thread's frame within the CTA's group
+    const bool live = f < nfr;
+    float *fr = re + fl * MP, *fi = im + fl * MP;
+    if (live) {
+      // levels 1-4 on the 16 consecutive bit-reversed positions 16 lt .. 16 lt + 15
+      cpx z[16];
+      const int st = f * HOP;
+#pragma unroll
+      for (int e = 0; e < 16; e++) {
+        const int n = (int)(__brev((unsigned)(16 * lt + e)) >> (32 - LG));
+        z[e] = {__fmul_rn(seg[st + 2 * n], win[2 * n]), __fmul_rn(seg[st + 2 * n + 1], win[2 * n + 1])};
+      }
+#pragma unroll
+      for (int g = 0; g < 4; g++) r4first(z[4 * g], z[4 * g + 1], z[4 * g + 2], z[4 * g + 3]);
+#pragma unroll
+      for (int j = 0; j < 4; j++)  // len 8: h 4, st1 = M / 8, st2 = M / 16
+        r22(z[j], z[j + 4], z[j + 8], z[j + 12], twr[j * (M / 8)], twi[j * (M / 8)], twr[j * (M / 16)],
+            twi[j * (M / 16)]);
+#pragma unroll
+      for (int e = 0; e < 16; e++) {
+        fr[sx(16 * lt + e)] = z[e].r;
+        fi[sx(16 * lt + e)] = z[e].i;
+      }
+    }
+    __syncthreads();
+    if (live) {
+      // levels 5-8 on the points base + 16 a + 64 b of a 256-block
+      const int j = lt & 15, base = (lt >> 4) * 256 + j;
+      cpx z[16];
+#pragma unroll
+      for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) z[a + 4 * b] = {fr[sx(base + 16 * a + 64 * b)], fi[sx(base + 16 * a + 64 * b)]};
+      {  // len 32: h 16, groups (a = 0..3) for each b, twiddle index j
+        const float w1r = twr[j * (M / 32)], w1i = twi[j * (M / 32)], w2r = twr[j * (M / 64)], w2i = twi[j * (M / 64)];
+#pragma unroll
+        for (int b = 0; b < 4; b++) r22(z[4 * b], z[4 * b + 1], z[4 * b + 2], z[4 * b + 3], w1r, w1i, w2r, w2i);
+      }
+#pragma unroll
+      for (int a = 0; a < 4; a++) {  // len 128: h 64, groups (b = 0..3) for each a, twiddle index j + 16 a
+        const int jj = j + 16 * a;
+        r22(z[a], z[a + 4], z[a + 8], z[a + 12], twr[jj * (M / 128)], twi[jj * (M / 128)], twr[jj * (M / 256)],
+            twi[jj * (M / 256)]);
+      }
+#pragma unroll
+      for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+          fr[sx(base + 16 * a + 64 * b)] = z[a + 4 * b].r;
+          fi[sx(base + 16 * a + 64 * b)] = z[a + 4 * b].i;
+        }
+    }
+    __syncthreads();
+    if (live) {
+      if (LG == 10) {  // levels 9-10: len 512, h 256, st1 2, st2 1
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const int jj = lt + 64 * c;
+          cpx a = {fr[sx(jj)], fi[sx(jj)]}, b = {fr[sx(jj + 256)], fi[sx(jj + 256)]};
+          cpx cc = {fr[sx(jj + 512)], fi[sx(jj + 512)]}, d = {fr[sx(jj + 768)], fi[sx(jj + 768)]};
+          r22(a, b, cc, d, twr[jj * 2], twi[jj * 2], twr[jj], twi[jj]);
+          fr[sx(jj)] = a.r; fi[sx(jj)] = a.i;
+          fr[sx(jj + 256)] = b.r; fi[sx(jj + 256)] = b.i;
+          fr[sx(jj + 512)] = cc.r; fi[sx(jj + 512)] = cc.i;
+          fr[sx(jj + 768)] = d.r; fi[sx(jj + 768)] = d.i;
+        }
+      } else {  // level 9 alone (radix 2): len 512, half 256, step 1 (fft_tab.h:64-76)
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          const int jj = lt + 32 * c;
+          const cpx v = cmul({fr[sx(jj + 256)], fi[sx(jj + 256)]}, twr[jj], twi[jj]);
+          const float ur = fr[sx(jj)], ui = fi[sx(jj)];
+          fr[sx(jj)] = __fadd_rn(ur, v.r); fi[sx(jj)] = __fadd_rn(ui, v.i);
+          fr[sx(jj + 256)] = __fsub_rn(ur, v.r); fi[sx(jj + 256)] = __fsub_rn(ui, v.i);
+        }
+      }
+    }
+    __syncthreads();
+    // real part of X_k for the bins the filters use: 1/2 [(Zr_k + Zr_{M-k}) + c (Zi_k + Zi_{M-k}) - s (Zr_k - Zr_{M-k})]
+    for (int i = tid; i < FF * nk; i += 256) {
+      const int ff = i / nk, k = klo + (i - ff * nk);
+      if (f0 + ff >= nfr) continue;
+      const int k1 = k == M ? 0 : k, k2 = k == 0 ? 0 : M - k;  // Z_M = Z_0 (the reference reads past its buffer)
+      const float *gr = re + ff * MP, *gi = im + ff * MP;
+      const float zr = gr[sx(k1)], zi = gi[sx(k1)], yr = gr[sx(k2)], yi = gi[sx(k2)];
+      float v = __fadd_rn(zr, yr);
+      v = __fmaf_rn(__fadd_rn(zi, yi), t.pc[BR][k], v);
+      v = __fmaf_rn(-__fsub_rn(zr, yr), t.ps[BR][k], v);
+      R[ff * nk + (k - klo)] = __fmul_rn(v, 0.5f);
+    }
+    __syncthreads();
+    const int *__restrict__ moff = t.mel_off[BR];
+    const int *__restrict__ mk = t.mel_k[BR];
+    const float *__restrict__ mw = t.mel_w[BR];
+    const float pw2 = t.pw2[BR], bs = t.bn_s[BR], bb = t.bn_b[BR];
+    for (int i = tid; i < FF * kNmel; i += 256) {
+      const int ff = i / kNmel, j = i - ff * kNmel, fi2 = f0 + ff;
+      if (fi2 >= nfr) continue;
+      const float *Rf = R + ff * nk - klo;
+      float a0 = 0.f, a1 = 0.f;
+      int e = moff[j];
+      const int e1 = moff[j + 1];
+      for (; e + 2 <= e1; e += 2) {
+        a0 = __fmaf_rn(Rf[mk[e]], mw[e], a0);
+        a1 = __fmaf_rn(Rf[mk[e + 1]], mw[e + 1], a1);
+      }
+      if (e < e1) a0 = __fmaf_rn(Rf[mk[e]], mw[e], a0);
+      const float m = fmax_nan(fabsf(__fadd_rn(a0, a1)), 1e-30f);
+      const float p = exp2_acc(__fmul_rn(pw2, log2_acc(m)));
+      img[((long long)(kNmel - 1 - j) * kNfr + t0 + fi2) * 2 + BR] = __fmaf_rn(p, bs, bb);
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(256) k_fe_spec(const float *__restrict__ pcm, long long pws,
+                                                 const float *__restrict__ mm, const bnnk_fe_tables t,
+                                                 float *__restrict__ img, long long iws) {
+  extern __shared__ float sm[];
+  const int win = blockIdx.z, t0 = blockIdx.x * kFG;
+  const float *x = pcm + win * pws;
+  float *imgw = img + win * iws;
+  if (blockIdx.y == 0) spec<10>(x, mm[2 * win], mm[2 * win + 1], t, imgw, t0, sm);
+  else spec<9>(x, mm[2 * win], mm[2 * win + 1], t, imgw, t0, sm);
+}
+
+// per window: mn = min, den = (max - mn) + 1e-6 (NaN-propagating NEON min/max)
+__global__ void __launch_bounds__(512) k_fe_minmax(const float *__restrict__ pcm, long long pws, float *__restrict__ mm) {
+  __shared__ float smn[16], smx[16];
+  const float *x = pcm + blockIdx.x * pws;
+  float mn = x[0], mx = x[0];
+  for (int i = threadIdx.x; i < kNsamp / 4; i += 512) {
+    const float4 v = reinterpret_cast<const float4 *>(x)[i];
+    mn = fmin_nan(mn, fmin_nan(fmin_nan(v.x, v.y), fmin_nan(v.z, v.w)));
+    mx = fmax_nan(mx, fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w)));
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fmin_nan(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if (threadIdx.x % 32 == 0) { smn[threadIdx.x / 32] = mn; smx[threadIdx.x / 32] = mx; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < 16; i++) { mn = fmin_nan(mn, smn[i]); mx = fmax_nan(mx, smx[i]); }
+    mm[2 * blockIdx.x] = mn;
+    mm[2 * blockIdx.x + 1] = __fadd_rn(__fsub_rn(mx, mn), 1e-6f);
+  }
+}
+
+}  // namespace bnn
+
+using namespace bnn;
+
+extern "C" int bnnk_fe_stft2(int B, const float *pcm, long long pws, const bnnk_fe_tables *t, float *minmax,
+                             float *img, long long iws, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  // shared memory: the larger of the two spectrograms' layouts
+  auto need = [&](int lg, int br) {
+    const int M = 1 << lg, hop = br ? 280 : 278, tpf = M / 16, ff = 256 / tpf;
+    return sizeof(float) * (size_t)((kFG - 1) * hop + 2 * M + 2 * ff * (M + M / 16) + ff * (t->khi[br] - t->klo[br]));
+  };
+  const size_t smem = need(10, 0) > need(9, 1) ? need(10, 0) : need(9, 1);
+  static size_t attr = 0;
+  if (smem > attr) {
+    cudaFuncSetAttribute(k_fe_spec, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = smem;
+  }
+  k_fe_minmax<<<B, 512, 0, st>>>(pcm, pws, minmax);
+  k_fe_spec<<<dim3((kNfr + kFG - 1) / kFG, 2, B), 256, smem, st>>>(pcm, pws, minmax, *t, img, iws);
+  return cudaGetLastError();
+}

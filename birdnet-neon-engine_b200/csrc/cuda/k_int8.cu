@@ -1,17 +1,19 @@
-// int8 1x1 conv / dense layer for sm_100a: the per-row dynamic quantizer and the tcgen05 kind::i8 GEMM with the
-// fused dequant / activation / residual / padded-store epilogue.
+// int8 1x1 conv / dense layer on sm_100a: the per-row dynamic quantizer and a persistent tcgen05 kind::i8 GEMM with
+// the fused dequant / activation / residual / padded-store epilogue.
 //
 // Reference: src/gemm_s8n.c (s8n_quant_rows :15-63, acc4x4 / tile4x4 / s8n_gemm_range :82-190) driven by PW_S8 and
 // GEMV_S8 (src/rt_ops_s8n.c:92-158). The int32 sums are exact in both (|q|, |w| <= 127, K <= 4096), so the tensor
 // cores' summation order cannot change them; everything after the sum repeats the reference's fp32 steps.
 //
-// GEMM design: one CTA per 128-row x BN-column tile. Warp 0 lane 0 streams K blocks of A (the quantized rows) and B
-// (the weights, [Nrows][Kq] K-major) into a ring of shared-memory stages with TMA (2-D tiled loads, swizzled by the
-// K-block width: 32, 64 or 128 bytes; no multicast), warp 1 lane 0 issues tcgen05.mma.cta_group::1.kind::i8 (M 128,
-// N = BN, K 32 per instruction) into a TMEM accumulator of BN int32 columns and releases each stage with
-// tcgen05.commit, and all four warps then read their 32 TMEM lanes (= rows) with tcgen05.ld and run the epilogue.
-// Every mbarrier wait is bounded by a %globaltimer deadline; a timeout sets the error word and the CTA still frees
-// its TMEM before it returns.
+// GEMM: one persistent CTA per SM walks the 128-row x BN-column tiles (N tiles inner, so consecutive tiles reuse the
+// same rows of A from L2). Warp 0 lane 0 streams K blocks of A (quantized rows) and B (weights [Nrows][Kq], K-major)
+// into a ring of shared-memory stages with 2-D TMA loads (swizzle = the K-block width, 32/64/128 bytes; no
+// multicast). Warp 1 lane 0 issues tcgen05.mma.cta_group::1.kind::i8 (M 128, N BN, K 32 per instruction) into one of
+// NE TMEM accumulators (tile i uses accumulator i mod NE) and releases smem stages and finished accumulators with
+// tcgen05.commit. NE epilogue warpgroups each own one accumulator: a warp reads its 32 TMEM lanes (= rows) with
+// tcgen05.ld, frees the accumulator and runs the fp32 epilogue, while the MMA warp already fills the others. Every
+// mbarrier wait is bounded by a %globaltimer deadline; a timeout sets the error word, the CTA stops and still frees
+// its TMEM.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -26,8 +28,6 @@ namespace bnn {
 
 // ------------------------------------------------------------------ quantizer
 
-// Quantizes one row held by a group of L lanes (each lane 4 consecutive k per step). K % 4 == 0 and lda % 4 == 0
-// (every v2.4 layer); the general case runs bnnk_quant_scalar.
 template <int L>
 __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__restrict__ x, long long xws, int lda,
                                                int K, int Kq, const float *__restrict__ gate, long long gws,
@@ -141,12 +141,16 @@ __device__ __forceinline__ unsigned long long gtimer() {
   return t;
 }
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far above any legitimate wait
+constexpr int kMaxStages = 8, kMaxEpi = 4;
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
 }
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 // bounded wait for the phase with the given parity to complete; false on timeout
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
@@ -172,7 +176,7 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       : "memory");
 }
 // shared-memory matrix descriptor of a K-major tile with rows of SW bytes swizzled by SW (8-row groups of 8 * SW
-// bytes); version 1 (sm_100), base offset 0 (tiles are aligned to the swizzle repeat)
+// bytes); version 1 (sm_100), base offset 0 (stages are aligned to the swizzle repeat)
 template <int SW>
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   constexpr uint64_t layout = SW == 128 ? 2 : SW == 64 ? 4 : 6;
@@ -203,7 +207,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, int32_t v[16]) {
 }
 
 struct GemmArgs {
-  int rows, Mw, nkb, stages, bn, np, tmem_cols;
+  int rows, Mw, nkb, stages, bn, np, n_tiles, tiles, acc_cols, ne;
   uint32_t idesc;
   const float *sa;
   const int32_t *za;
@@ -215,84 +219,9 @@ __device__ __forceinline__ long long padded_row(int m, int w, int pad) {
   return pad ? (long long)((m / w) + pad) * (w + 2 * pad) + (m % w) + pad : (long long)m;
 }
 
-template <int SW>
-__global__ void __launch_bounds__(128, 1) k_gemm_s8(const __grid_constant__ CUtensorMap tma_a,
-                                                    const __grid_constant__ CUtensorMap tma_b, const GemmArgs a) {
-  extern __shared__ uint8_t dsmem[];
-  __shared__ __align__(8) unsigned long long bar_full[8], bar_empty[8], bar_done;
-  __shared__ uint32_t tmem_base_s;
-  __shared__ int abort_s;
-  __shared__ float s_sw[256], s_b[256];
-  __shared__ int32_t s_cs[256];
-  __shared__ uint32_t s_lut[256];
-
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int m0 = blockIdx.x * 128, n0 = blockIdx.y * a.bn;
-  const uint32_t base = (smem_u32(dsmem) + 1023u) & ~1023u;
-  const uint32_t a_bytes = 128u * SW, stage_bytes = (128u + a.bn) * SW;
-
-  for (int i = threadIdx.x; i < a.bn; i += 128) {
-    const int n = n0 + i;
-    s_sw[i] = a.e.sw[n];
-    s_b[i] = a.e.bias[n];
-    s_cs[i] = a.e.cs[n];
-  }
-  for (int i = threadIdx.x; i < 256; i += 128) s_lut[i] = g_frecpe_lut[i];
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < a.stages; s++) { mbar_init(smem_u32(&bar_full[s]), 1); mbar_init(smem_u32(&bar_empty[s]), 1); }
-    mbar_init(smem_u32(&bar_done), 1);
-    abort_s = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
-                 "r"(a.tmem_cols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem = tmem_base_s;
-
-  if (warp == 0 && lane == 0) {  // TMA producer
-    for (int kb = 0; kb < a.nkb; kb++) {
-      const int s = kb % a.stages;
-      if (kb >= a.stages && !mbar_wait(smem_u32(&bar_empty[s]), ((kb / a.stages) - 1) & 1)) {
-        atomicExch(a.err, BNNK_ERR_TMA_WAIT);
-        abort_s = 1;
-        break;
-      }
-      const uint32_t st = base + s * stage_bytes, bar = smem_u32(&bar_full[s]);
-      mbar_expect_tx(bar, stage_bytes);
-      tma_load_2d(st, &tma_a, bar, kb * SW, m0);
-      tma_load_2d(st + a_bytes, &tma_b, bar, kb * SW, n0);
-    }
-  } else if (warp == 1 && lane == 0) {  // MMA issuer
-    bool ok = true;
-    for (int kb = 0; kb < a.nkb && ok; kb++) {
-      const int s = kb % a.stages;
-      if (!mbar_wait(smem_u32(&bar_full[s]), (kb / a.stages) & 1)) {
-        atomicExch(a.err, BNNK_ERR_MMA_WAIT);
-        ok = false;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t st = base + s * stage_bytes;
-#pragma unroll
-      for (int kk = 0; kk < SW / 32; kk++)
-        mma_i8(tmem, smem_desc<SW>(st + kk * 32), smem_desc<SW>(st + a_bytes + kk * 32), a.idesc, (kb | kk) != 0);
-      mma_commit(smem_u32(&bar_empty[s]));
-    }
-    mma_commit(smem_u32(&bar_done));  // arrives once every MMA issued above has completed
-  }
-  __syncwarp();
-
-  // epilogue: thread = one row of the tile (TMEM lane 32 * warp + lane)
-  const bool ready = mbar_wait(smem_u32(&bar_done), 0);
-  if (!ready) atomicExch(a.err, BNNK_ERR_EPI_WAIT);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const int row = m0 + warp * 32 + lane;
-  const bool live = ready && row < a.rows && !abort_s;
+// the epilogue of one tile for one row (gemm_s8n.c:105-135): all 32 lanes of the warp take part in the TMEM loads
+__device__ __forceinline__ void epilogue_row(const GemmArgs &a, uint32_t taddr, int row, int n0, bool live,
+                                             const uint32_t *lut) {
   int w = 0, mm = 0;
   float sa = 0.f;
   int32_t za = 0;
@@ -308,24 +237,31 @@ __global__ void __launch_bounds__(128, 1) k_gemm_s8(const __grid_constant__ CUte
   const int ncols = min(a.bn, a.np - n0);
   for (int c0 = 0; c0 < a.bn; c0 += 16) {
     int32_t acc[16];
-    if (ready) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, acc);
+    tmem_ld16(taddr + (uint32_t)c0, acc);
     if (!live || c0 >= ncols) continue;
     float y[16];
 #pragma unroll
-    for (int j = 0; j < 16; j++) {
-      const int c = c0 + j;
-      // deq4 (gemm_s8n.c:105-114): int32 wrap, exact int -> fp32, sw * sa first, multiply then add (no FMA)
-      float f = __int2float_rn((int32_t)((uint32_t)acc[j] - (uint32_t)s_cs[c] * (uint32_t)za));
-      float v = __fadd_rn(__fmul_rn(f, __fmul_rn(s_sw[c], sa)), s_b[c]);
-      if (a.e.act == 1) v = silu<true>(v, s_lut);
-      else if (a.e.act == 2) v = (v > 0.f || v != v) ? v : 0.f;  // FMAX(v, +0): NaN stays NaN, -0 -> +0
-      y[j] = v;
+    for (int j4 = 0; j4 < 16; j4 += 4) {
+      const float4 sw4 = __ldg(reinterpret_cast<const float4 *>(a.e.sw + n0 + c0 + j4));
+      const float4 b4 = __ldg(reinterpret_cast<const float4 *>(a.e.bias + n0 + c0 + j4));
+      const int4 cs4 = __ldg(reinterpret_cast<const int4 *>(a.e.cs + n0 + c0 + j4));
+      const float swv[4] = {sw4.x, sw4.y, sw4.z, sw4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+      const int32_t csv[4] = {cs4.x, cs4.y, cs4.z, cs4.w};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        // deq4 (gemm_s8n.c:105-114): int32 wrap, exact int -> fp32, sw * sa first, multiply then add (no FMA)
+        const float f = __int2float_rn((int32_t)((uint32_t)acc[j4 + q] - (uint32_t)csv[q] * (uint32_t)za));
+        float v = __fadd_rn(__fmul_rn(f, __fmul_rn(swv[q], sa)), bv[q]);
+        if (a.e.act == 1) v = silu<true>(v, lut);
+        else if (a.e.act == 2) v = (v > 0.f || v != v) ? v : 0.f;  // FMAX(v, +0): NaN stays NaN, -0 -> +0
+        y[j4 + q] = v;
+      }
     }
     if (c0 + 16 <= ncols) {
       if (rrow) {
 #pragma unroll
         for (int j = 0; j < 16; j += 4) {
-          float4 r4 = *reinterpret_cast<const float4 *>(rrow + c0 + j);
+          const float4 r4 = *reinterpret_cast<const float4 *>(rrow + c0 + j);
           y[j] = __fadd_rn(y[j], r4.x); y[j + 1] = __fadd_rn(y[j + 1], r4.y);
           y[j + 2] = __fadd_rn(y[j + 2], r4.z); y[j + 3] = __fadd_rn(y[j + 3], r4.w);
         }
@@ -337,9 +273,115 @@ __global__ void __launch_bounds__(128, 1) k_gemm_s8(const __grid_constant__ CUte
       for (int j = 0; j < 16 && c0 + j < ncols; j++) orow[c0 + j] = rrow ? __fadd_rn(y[j], rrow[c0 + j]) : y[j];
     }
   }
+}
+
+template <int SW>
+__global__ void __launch_bounds__(64 + 128 * kMaxEpi, 1) k_gemm_s8(const __grid_constant__ CUtensorMap tma_a,
+                                                                  const __grid_constant__ CUtensorMap tma_b,
+                                                                  const GemmArgs a) {
+  extern __shared__ uint8_t dsmem[];
+  __shared__ __align__(8) unsigned long long bar_full[kMaxStages], bar_empty[kMaxStages];
+  __shared__ __align__(8) unsigned long long bar_acc_full[kMaxEpi], bar_acc_empty[kMaxEpi];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int abort_s;
+  __shared__ uint32_t s_lut[256];
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t base = (smem_u32(dsmem) + 1023u) & ~1023u;
+  const uint32_t a_bytes = 128u * SW, stage_bytes = (128u + a.bn) * SW;
+  const int S = a.stages;
+
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) s_lut[i] = g_frecpe_lut[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) { mbar_init(smem_u32(&bar_full[s]), 1); mbar_init(smem_u32(&bar_empty[s]), 1); }
+    for (int g = 0; g < a.ne; g++) { mbar_init(smem_u32(&bar_acc_full[g]), 1); mbar_init(smem_u32(&bar_acc_empty[g]), 4); }
+    abort_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(a.acc_cols * a.ne));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols));
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      int it = 0;
+      for (int t = blockIdx.x; t < a.tiles && !abort_s; t += gridDim.x) {
+        const int m0 = (t / a.n_tiles) * 128, n0 = (t % a.n_tiles) * a.bn;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % S;
+          if (it >= S && !mbar_wait(smem_u32(&bar_empty[s]), ((it / S) - 1) & 1)) {
+            atomicExch(a.err, BNNK_ERR_TMA_WAIT);
+            abort_s = 1;
+            break;
+          }
+          const uint32_t st = base + s * stage_bytes, bar = smem_u32(&bar_full[s]);
+          mbar_expect_tx(bar, stage_bytes);
+          tma_load_2d(st, &tma_a, bar, kb * SW, m0);
+          tma_load_2d(st + a_bytes, &tma_b, bar, kb * SW, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      int it = 0, lt = 0;
+      for (int t = blockIdx.x; t < a.tiles && !abort_s; t += gridDim.x, lt++) {
+        const int g = lt % a.ne, use = lt / a.ne;
+        if (use > 0 && !mbar_wait(smem_u32(&bar_acc_empty[g]), (use - 1) & 1)) {
+          atomicExch(a.err, BNNK_ERR_MMA_WAIT);
+          abort_s = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t tacc = tmem + (uint32_t)(g * a.acc_cols);
+        bool ok = true;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % S;
+          if (!mbar_wait(smem_u32(&bar_full[s]), (it / S) & 1)) {
+            atomicExch(a.err, BNNK_ERR_MMA_WAIT);
+            abort_s = 1;
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t st = base + s * stage_bytes;
+#pragma unroll
+          for (int kk = 0; kk < SW / 32; kk++)
+            mma_i8(tacc, smem_desc<SW>(st + kk * 32), smem_desc<SW>(st + a_bytes + kk * 32), a.idesc, (kb | kk) != 0);
+          mma_commit(smem_u32(&bar_empty[s]));
+        }
+        if (!ok) break;
+        mma_commit(smem_u32(&bar_acc_full[g]));  // arrives when this tile's MMAs have completed
+      }
+    }
+  } else if (warp - 2 < 4 * a.ne) {  // epilogue warpgroup g, TMEM lanes 32 q .. 32 q + 31
+    const int g = (warp - 2) / 4, q = warp % 4;
+    int use = 0;
+    for (int t = blockIdx.x + g * gridDim.x; t < a.tiles; t += a.ne * gridDim.x, use++) {
+      bool ok = mbar_wait(smem_u32(&bar_acc_full[g]), use & 1);
+      ok = __all_sync(0xffffffffu, ok) && !abort_s;
+      if (!ok) {
+        if (lane == 0) { atomicExch(a.err, BNNK_ERR_EPI_WAIT); abort_s = 1; }
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int m0 = (t / a.n_tiles) * 128, n0 = (t % a.n_tiles) * a.bn;
+      const int row = m0 + q * 32 + lane;
+      epilogue_row(a, tmem + (uint32_t)(g * a.acc_cols) + ((uint32_t)(q * 32) << 16), row, n0, row < a.rows, s_lut);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[g]));
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.acc_cols * a.ne));
 }
 
 // ------------------------------------------------------------------ elementwise test kernel
@@ -447,6 +489,8 @@ extern "C" int bnnk_gemm_weight_rows(int np) {
   return t * bn;
 }
 
+static int g_num_sms = 0;
+
 extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_cap, int kq, const int8_t *w, int n,
                                    int np) {
   memset(p, 0, sizeof *p);
@@ -458,14 +502,10 @@ extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_
   p->np = np;
   n_tiling(np, &p->n_tiles, &p->bn);
   p->tmem_cols = p->bn <= 32 ? 32 : p->bn <= 64 ? 64 : p->bn <= 128 ? 128 : 256;
-  p->stages = p->nkb < 4 ? p->nkb : 4;
-  p->smem = (size_t)p->stages * (128 + p->bn) * p->sw + 1024;
-  // at most 512 / tmem_cols CTAs per SM may hold TMEM at once: ask for enough shared memory that no more fit
-  const int max_ctas = 512 / p->tmem_cols;
-  if (max_ctas < 16) {
-    const size_t need = 233472 / (size_t)(max_ctas + 1) + 1024;
-    if (p->smem < need) p->smem = need;
-  }
+  const size_t stage = (size_t)(128 + p->bn) * p->sw;
+  int s = (int)((200 * 1024) / stage);
+  p->stages = s < 2 ? 2 : s > kMaxStages ? kMaxStages : s;
+  p->smem = (size_t)p->stages * stage + 1024;
   p->idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p->bn >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
   const int wrows = p->n_tiles * p->bn;  // the weight buffer holds n_tiles * bn rows (zero beyond n)
   int e = encode_2d(p->tma_a, q, kq, rows_cap, p->sw, 128, p->sw);
@@ -477,11 +517,18 @@ template <int SW>
 static int launch_gemm(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_gemm_s8<SW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(k_gemm_s8<SW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024);
     attr = true;
   }
-  dim3 grid((a.rows + 127) / 128, p->n_tiles);
-  k_gemm_s8<SW><<<grid, 128, p->smem, st>>>(*(const CUtensorMap *)p->tma_a, *(const CUtensorMap *)p->tma_b, a);
+  if (!g_num_sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  const int grid = a.tiles < g_num_sms ? a.tiles : g_num_sms;
+  k_gemm_s8<SW><<<grid, 64 + 128 * a.ne, p->smem, st>>>(*(const CUtensorMap *)p->tma_a,
+                                                        *(const CUtensorMap *)p->tma_b, a);
   return cudaGetLastError();
 }
 
@@ -495,7 +542,10 @@ extern "C" int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float 
   a.stages = p->stages;
   a.bn = p->bn;
   a.np = p->np;
-  a.tmem_cols = p->tmem_cols;
+  a.n_tiles = p->n_tiles;
+  a.tiles = ((rows + 127) / 128) * p->n_tiles;
+  a.acc_cols = p->tmem_cols;
+  a.ne = 512 / p->tmem_cols < kMaxEpi ? 512 / p->tmem_cols : kMaxEpi;
   a.idesc = p->idesc;
   a.sa = sa;
   a.za = za;
