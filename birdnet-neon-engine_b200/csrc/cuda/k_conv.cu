@@ -60,21 +60,22 @@ __global__ void __launch_bounds__(256) k_dw3_out(long long total, const float *_
 }
 
 // channel sums: chsum[c] = ((0 + v_0) + v_1) + ... over the output pixels in raster order (silu_rows_f32,
-// gemm_f32.c:303-328; dw_silu_row16 :342-365). One thread per (window, channel); 16 loads in flight per chain.
-__global__ void __launch_bounds__(256) k_dw3_chsum(int total, const float *__restrict__ out, long long ows, int P, int C,
-                                                   float *__restrict__ chsum, long long cws) {
-  const int idx = blockIdx.x * 256 + threadIdx.x;
+// gemm_f32.c:303-328; dw_silu_row16 :342-365). One thread per (window, channel); 32 loads in flight per chain, small
+// blocks so that every SM holds some of the chains.
+__global__ void __launch_bounds__(64) k_dw3_chsum(int total, const float *__restrict__ out, long long ows, int P, int C,
+                                                  float *__restrict__ chsum, long long cws) {
+  const int idx = blockIdx.x * 64 + threadIdx.x;
   if (idx >= total) return;
   const int win = idx / C, c = idx - win * C;
   const float *o = out + win * ows + c;
   float cs = 0.f;
   int p = 0;
-  for (; p + 16 <= P; p += 16) {
-    float v[16];
+  for (; p + 32 <= P; p += 32) {
+    float v[32];
 #pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __ldg(o + (long long)(p + i) * C);
+    for (int i = 0; i < 32; i++) v[i] = __ldg(o + (long long)(p + i) * C);
 #pragma unroll
-    for (int i = 0; i < 16; i++) cs = __fadd_rn(cs, v[i]);
+    for (int i = 0; i < 32; i++) cs = __fadd_rn(cs, v[i]);
   }
   for (; p < P; p++) cs = __fadd_rn(cs, __ldg(o + (long long)p * C));
   chsum[win * cws + c] = cs;
@@ -297,7 +298,7 @@ extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int
   const long long total = (long long)B * P * (C / 4);
   k_dw3_out<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(total, xp, xws, W, C, s, w, b, out, ows, Wo, P);
   const int tc = B * C;
-  k_dw3_chsum<<<(tc + 255) / 256, 256, 0, st>>>(tc, out, ows, P, C, chsum, cws);
+  k_dw3_chsum<<<(tc + 63) / 64, 64, 0, st>>>(tc, out, ows, P, C, chsum, cws);
   return cudaGetLastError();
 }
 
