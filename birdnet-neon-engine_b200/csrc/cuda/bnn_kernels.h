@@ -56,6 +56,15 @@ typedef struct {
 int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float *sa, const int32_t *za, const bnnk_epilogue *e,
               int *err, bnn_stream_t st);
 
+/* quantizer + GEMM of a planned layer with q / sa / za in the file-scope static array of k_int8.cu instead of the
+ * layer's own scratch; allocates nothing. At most BNNK_STATIC_ROWS rows and rows * kq <= BNNK_STATIC_QBYTES
+ * (cudaErrorInvalidValue beyond). The first call on a device (rows = 0 does only this) looks up the array's address
+ * there. Calls on one device share the array. */
+#define BNNK_STATIC_ROWS 32768
+#define BNNK_STATIC_QBYTES (4 << 20)
+int bnnk_pw_s8_static(const bnnk_gemm_plan *p, int rows, int Mw, const float *x, long long xws, int lda, int K,
+                      const float *gate, long long gws, const bnnk_epilogue *e, int *err, bnn_stream_t st);
+
 /* ---- depthwise 3x3 + SiLU + channel sums (DW3): xp [B][(H+2)(W+2)][C] haloed, out [B][Ho Wo][C], chsum [B][C] */
 int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int C, int s, const float *w, const float *b,
              float *out, long long ows, int Ho, int Wo, float *chsum, long long cws, bnn_stream_t st);

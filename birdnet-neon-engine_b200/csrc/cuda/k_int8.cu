@@ -21,6 +21,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "bnn_kernels.h"
 #include "emu.cuh"
 
@@ -556,6 +558,56 @@ extern "C" int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float 
   case 64: return launch_gemm<64>(p, a, st);
   default: return launch_gemm<32>(p, a, st);
   }
+}
+
+// ------------------------------------------------------------------ PW_S8 on file-scope scratch
+// Some hosts must not allocate device memory once they run: a live-audio loop scoring each 3 s window as it
+// arrives cannot absorb cudaMalloc / cudaFree, which may synchronise the whole device and take unbounded time, and a
+// server that sized its device memory at start-up for a fixed set of streams must not grow on the first use of an
+// op. For them the quantized activations of a PW_S8 run (q, and the per-row scale sa and zero point za) live in this
+// one static array, which exists as soon as the module is loaded. Layout: sa [BNNK_STATIC_ROWS] f32, then za
+// [BNNK_STATIC_ROWS] i32, then q: rows of kq int8 bytes, at most BNNK_STATIC_QBYTES in all. Nothing in it has to start
+// at zero: the quantizer writes every q byte (pads included), sa and za of each row the GEMM's stored rows read; rows
+// of a tile past the call's last row only feed accumulator rows that the epilogue does not store.
+static __device__ __align__(256) unsigned char g_pw_scratch[8 * BNNK_STATIC_ROWS + BNNK_STATIC_QBYTES];
+
+constexpr int kScratchDevices = 64;
+static unsigned char *g_pw_scratch_at[kScratchDevices];  // the array's device address, per device (set-up)
+static std::mutex g_pw_scratch_mu;
+
+// set-up, once per device, with that device current: the address of the array on it
+static int pw_scratch(unsigned char **at) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e) return e;
+  if (dev < 0 || dev >= kScratchDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_pw_scratch_mu);
+  if (!g_pw_scratch_at[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_pw_scratch);
+    if (e) return e;
+    g_pw_scratch_at[dev] = (unsigned char *)p;
+  }
+  *at = g_pw_scratch_at[dev];
+  return 0;
+}
+
+extern "C" int bnnk_pw_s8_static(const bnnk_gemm_plan *p, int rows, int Mw, const float *x, long long xws, int lda,
+                                 int K, const float *gate, long long gws, const bnnk_epilogue *e, int *err,
+                                 bnn_stream_t st) {
+  unsigned char *at = nullptr;
+  int rc = pw_scratch(&at);
+  if (rc || rows <= 0) return rc;
+  if (rows > BNNK_STATIC_ROWS || (long long)rows * p->kq > BNNK_STATIC_QBYTES) return cudaErrorInvalidValue;
+  float *sa = (float *)at;
+  int32_t *za = (int32_t *)(at + 4 * BNNK_STATIC_ROWS);
+  int8_t *q = (int8_t *)(at + 8 * BNNK_STATIC_ROWS);
+  // the op's plan with its A operand moved onto the q region (a host-side encode: no device memory)
+  bnnk_gemm_plan pl = *p;
+  rc = encode_2d(pl.tma_a, q, p->kq, (int)(BNNK_STATIC_QBYTES / p->kq), p->sw, 128, p->sw);
+  if (!rc) rc = bnnk_quant(rows, Mw, x, xws, lda, K, p->kq, gate, gws, q, sa, za, st);
+  if (!rc) rc = bnnk_gemm(&pl, rows, Mw, sa, za, e, err, st);
+  return rc;
 }
 
 extern "C" int bnnk_test_fn(int fn, int n, const float *x, float *y, bnn_stream_t st) {

@@ -666,6 +666,30 @@ int bnn_pw_s8_run(bnn_pw_s8 *o, int B, int Mw, const float *d_x, long long xws, 
   return launch_rc("bnn_pw_s8_run", e);
 }
 
+_Static_assert(BNN_PW_S8_STATIC_MAX_ROWS == BNNK_STATIC_ROWS && BNN_PW_S8_STATIC_MAX_QBYTES == BNNK_STATIC_QBYTES,
+               "the public limits of bnn_pw_s8_run_static are the static array's");
+
+int bnn_pw_s8_run_static(bnn_pw_s8 *o, int B, int Mw, const float *d_x, long long xws, int lda, const float *d_gate,
+                         long long gws, int act, float *d_out, long long ows, int ldo, int ow, int opad,
+                         const float *d_res, long long rws, int ldr, int rw, int rpad, void *stream) {
+  if (!o || B < 0 || Mw < 1 || lda < o->K || ldo < o->Np || act < 0 || act > 2 || (opad && (ow <= 0 || Mw % ow)) ||
+      (rpad && (rw <= 0 || Mw % rw)) || (d_res && ldr < o->Np)) {
+    ERR(BNN_ERR_USAGE, "bnn_pw_s8_run_static: B %d Mw %d lda %d ldo %d act %d ow %d opad %d", B, Mw, lda, ldo, act, ow,
+        opad);
+    return -1;
+  }
+  const long long rows = (long long)B * Mw;
+  if (rows > BNN_PW_S8_STATIC_MAX_ROWS || rows * o->op.kq > BNN_PW_S8_STATIC_MAX_QBYTES) {
+    ERR(BNN_ERR_USAGE, "bnn_pw_s8_run_static: %lld rows of %d quantized bytes exceed the static scratch (at most %d "
+        "rows and %d bytes); use bnn_pw_s8_run", rows, o->op.kq, BNN_PW_S8_STATIC_MAX_ROWS,
+        BNN_PW_S8_STATIC_MAX_QBYTES);
+    return -1;
+  }
+  bnnk_epilogue ep = {act, d_out, ows, ldo, ow, opad, d_res, rws, ldr, rw, rpad, o->op.sw, o->op.bias, o->op.cs};
+  return launch_rc("bnn_pw_s8_run_static", bnnk_pw_s8_static(&o->op.plan, (int)rows, Mw, d_x, xws, lda, o->K, d_gate,
+                                                             gws, &ep, o->err, (bnn_stream_t)stream));
+}
+
 int bnn_pw_s8_error(bnn_pw_s8 *o) {
   int v = 0;
   if (o && o->err) cudaMemcpy(&v, o->err, sizeof v, cudaMemcpyDeviceToHost);

@@ -77,6 +77,21 @@ bnn_pw_s8 *bnn_pw_s8_new(int N, int K, int Kp, int Np, const int8_t *w, const fl
 int bnn_pw_s8_run(bnn_pw_s8 *op, int B, int Mw, const float *d_x, long long xws, int lda, const float *d_gate,
                   long long gws, int act, float *d_out, long long ows, int ldo, int ow, int opad, const float *d_res,
                   long long rws, int ldr, int rw, int rpad, void *stream);
+/* No counterpart in the reference: bnn_pw_s8_run for hosts that must not allocate device memory while they run (a
+ * live-audio loop, where cudaMalloc / cudaFree may synchronise the device and take unbounded time; a server whose
+ * device memory was sized at start-up). The quantized activations and their per-row scale / zero point go to one
+ * file-scope static device array instead of the op's own buffers, and the call allocates nothing. Limits:
+ * B * Mw <= BNN_PW_S8_STATIC_MAX_ROWS and B * Mw * Kq <= BNN_PW_S8_STATIC_MAX_QBYTES (Kq = K rounded up to 32);
+ * larger calls fail with BNN_ERR_USAGE. The first call on each device, with that device current, looks up the array's
+ * address there (B = 0 does only this); make it before any stream capture. Every call on a device uses the same
+ * array, so calls whose work may overlap in time (different streams, or host threads, with no ordering between them)
+ * race on it: serialise them. Nothing in the array has to start at zero. Results equal bnn_pw_s8_run's; the op's
+ * error word (bnn_pw_s8_error) is shared by both calls. */
+#define BNN_PW_S8_STATIC_MAX_ROWS 32768
+#define BNN_PW_S8_STATIC_MAX_QBYTES (4 << 20)
+int bnn_pw_s8_run_static(bnn_pw_s8 *op, int B, int Mw, const float *d_x, long long xws, int lda,
+                         const float *d_gate, long long gws, int act, float *d_out, long long ows, int ldo, int ow,
+                         int opad, const float *d_res, long long rws, int ldr, int rw, int rpad, void *stream);
 /* the device error word of the op's GEMM (0 = no bounded wait ran out) */
 int bnn_pw_s8_error(bnn_pw_s8 *op);
 void bnn_pw_s8_free(bnn_pw_s8 *op);
