@@ -33,6 +33,7 @@ typedef struct {
   unsigned char tma_a[128] __attribute__((aligned(64)));
   unsigned char tma_b[128] __attribute__((aligned(64)));
   int kq, sw, nkb, stages, bn, n_tiles, n, np, tmem_cols;
+  int ne, nh, sp;  /* TMEM accumulators, epilogue warps per lane quarter, parameters staged in shared memory */
   unsigned int idesc;
   size_t smem;
 } bnnk_gemm_plan;

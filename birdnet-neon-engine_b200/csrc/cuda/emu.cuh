@@ -109,6 +109,60 @@ __device__ __forceinline__ float silu(float x, const uint32_t *lut) {
   return __fmul_rn(x, r);
 }
 
+// sm_100's paired fp32 instructions (each half an IEEE fp32 operation). Measured with this toolchain: a paired
+// multiply whose result feeds a paired add comes out fused into one rounding although both carry .rn, while the
+// scalar forms never are. So the paired forms serve only chains in which no product feeds an add or a
+// subtraction (a product into a multiply, an fma, a min / max or a store); products that feed an add stay scalar.
+__device__ __forceinline__ unsigned long long pk2(float2 v) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 up2(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)));
+  return up2(d);
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)));
+  return up2(d);
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)), "l"(pk2(c)));
+  return up2(d);
+}
+__device__ __forceinline__ float2 neg2(float2 v) { return make_float2(-v.x, -v.y); }
+__device__ __forceinline__ float2 splat2(float v) { return make_float2(v, v); }
+
+// The SiLU above on two lanes (a - b is a + (-b), exactly). Its one product that meets an add, x * -log2(e), is
+// clamped by the scalar min / max first; the result x * r is a product, so callers add to it with scalar __fadd_rn.
+__device__ __forceinline__ float2 silu2(float2 x, const uint32_t *lut) {
+  const float magic = 0x1.8p+23f;
+  float2 t = mul2_rn(x, splat2(-0x1.715476p+0f));
+  t.x = fmin_nan(fmax_nan(t.x, -60.f), 60.f);
+  t.y = fmin_nan(fmax_nan(t.y, -60.f), 60.f);
+  const float2 tm = add2_rn(t, splat2(magic));
+  const float2 f = add2_rn(t, neg2(add2_rn(tm, splat2(-magic))));
+  float2 p = fma2_rn(splat2(0x1.5d87fep-10f), f, splat2(0x1.3b2ab6p-7f));
+  p = fma2_rn(p, f, splat2(0x1.c6b08ep-5f));
+  p = fma2_rn(p, f, splat2(0x1.ebfbep-3f));
+  p = fma2_rn(p, f, splat2(0x1.62e43p-1f));
+  p = fma2_rn(p, f, splat2(1.0f));
+  const float2 e = make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(tm.x) << 23)),
+                               __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(tm.y) << 23)));
+  const float2 d = add2_rn(splat2(1.f), e);
+  float2 r = make_float2(frecpe_ge1(d.x, lut), frecpe_ge1(d.y, lut));
+  r = mul2_rn(r, fma2_rn(neg2(d), r, splat2(2.f)));
+  return mul2_rn(x, r);
+}
+
 // exp2_f32x4 (src/gemm_f32.h:74-85)
 __device__ __forceinline__ float exp2_poly(float t) {
   t = fmin_nan(fmax_nan(t, -126.f), 126.f);

@@ -19,6 +19,8 @@
 #include <cudaTypedefs.h>
 #include <math.h>
 #include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -144,6 +146,8 @@ __device__ __forceinline__ unsigned long long gtimer() {
 }
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far above any legitimate wait
 constexpr int kMaxStages = 8, kMaxEpi = 4;
+constexpr int kMaxThreads = 832;  // 2 + 24 warps: 64 + 128 * ne * nh with ne * nh <= 6
+constexpr int kSPMax = 1536;      // widest layer whose epilogue parameters are staged in shared memory
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
@@ -195,21 +199,34 @@ __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int32_t v[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; i++) v[i] = (int32_t)r[i];
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+constexpr int kEpiUnits = 3;  // 8-column TMEM loads in flight per epilogue warp
+// wait for this thread's TMEM loads; the registers they fill are operands of the wait, so no use moves above it
+__device__ __forceinline__ void tmem_wait(uint32_t (&r)[kEpiUnits][8]) {
+#define BNN_R8(u) "+r"(r[u][0]), "+r"(r[u][1]), "+r"(r[u][2]), "+r"(r[u][3]), "+r"(r[u][4]), "+r"(r[u][5]), \
+                  "+r"(r[u][6]), "+r"(r[u][7])
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : BNN_R8(0), BNN_R8(1), BNN_R8(2)::"memory");
+#undef BNN_R8
+}
+__device__ __forceinline__ void ld8_global(const float *p, float (&v)[8]) {
+  asm volatile("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+               : "l"(p));
+}
+__device__ __forceinline__ void st8_global(float *p, const float (&v)[8]) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]),
+               "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
 }
 
 struct GemmArgs {
-  int rows, Mw, nkb, stages, bn, np, n_tiles, tiles, acc_cols, ne;
+  int rows, Mw, nkb, stages, bn, np, n_tiles, tiles, acc_cols, ne, nh;
+  int tmem_alloc;  // TMEM columns allocated: ne * acc_cols rounded up to a power of two (tcgen05.alloc's rule)
+  int vec_out, vec_res;  // output / residual rows start on 32-byte boundaries: 8-float stores / loads
   uint32_t idesc;
   const float *sa;
   const int32_t *za;
@@ -221,66 +238,59 @@ __device__ __forceinline__ long long padded_row(int m, int w, int pad) {
   return pad ? (long long)((m / w) + pad) * (w + 2 * pad) + (m % w) + pad : (long long)m;
 }
 
-// the epilogue of one tile for one row (gemm_s8n.c:105-135): all 32 lanes of the warp take part in the TMEM loads
-__device__ __forceinline__ void epilogue_row(const GemmArgs &a, uint32_t taddr, int row, int n0, bool live,
-                                             const uint32_t *lut) {
-  int w = 0, mm = 0;
-  float sa = 0.f;
-  int32_t za = 0;
-  if (live) {
-    w = row / a.Mw;
-    mm = row - w * a.Mw;
-    sa = a.sa[row];
-    za = a.za[row];
+// The epilogue of 8 columns n .. n+7 of one row (gemm_s8n.c:105-135): dequantize, bias, activation, residual, store.
+// psw / pb / pcs point at column n of the per-column parameters (shared or global memory).
+__device__ __forceinline__ void epilogue8(const GemmArgs &a, const uint32_t (&acc)[8], float sa, int32_t za,
+                                          const float *psw, const float *pb, const int32_t *pcs, float *o,
+                                          const float *r, const uint32_t *lut) {
+  const float4 sw0 = *reinterpret_cast<const float4 *>(psw), sw1 = *reinterpret_cast<const float4 *>(psw + 4);
+  const float4 b0 = *reinterpret_cast<const float4 *>(pb), b1 = *reinterpret_cast<const float4 *>(pb + 4);
+  const int4 c0 = *reinterpret_cast<const int4 *>(pcs), c1 = *reinterpret_cast<const int4 *>(pcs + 4);
+  const float sw[8] = {sw0.x, sw0.y, sw0.z, sw0.w, sw1.x, sw1.y, sw1.z, sw1.w};
+  const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  const int32_t cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const float2 sa2 = splat2(sa);
+  float y[8];
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    // deq4 (gemm_s8n.c:105-114): int32 wrap, exact int -> fp32, sw * sa first, multiply then add (no FMA)
+    const float f0 = __int2float_rn((int32_t)(acc[j] - (uint32_t)cs[j] * (uint32_t)za));
+    const float f1 = __int2float_rn((int32_t)(acc[j + 1] - (uint32_t)cs[j + 1] * (uint32_t)za));
+    const float2 s = mul2_rn(make_float2(sw[j], sw[j + 1]), sa2);
+    float2 v = make_float2(__fadd_rn(__fmul_rn(f0, s.x), bb[j]), __fadd_rn(__fmul_rn(f1, s.y), bb[j + 1]));
+    if (a.e.act == 1) {
+      v = silu2(v, lut);
+    } else if (a.e.act == 2) {  // FMAX(v, +0): NaN stays NaN, -0 -> +0
+      v.x = (v.x > 0.f || v.x != v.x) ? v.x : 0.f;
+      v.y = (v.y > 0.f || v.y != v.y) ? v.y : 0.f;
+    }
+    y[j] = v.x;
+    y[j + 1] = v.y;
   }
-  float *orow = a.e.out + (long long)w * a.e.ows + padded_row(mm, a.e.ow, a.e.opad) * a.e.ldo + n0;
-  const float *rrow = a.e.res ? a.e.res + (long long)w * a.e.rws + padded_row(mm, a.e.rw, a.e.rpad) * a.e.ldr + n0
-                              : nullptr;
-  const int ncols = min(a.bn, a.np - n0);
-  for (int c0 = 0; c0 < a.bn; c0 += 16) {
-    int32_t acc[16];
-    tmem_ld16(taddr + (uint32_t)c0, acc);
-    if (!live || c0 >= ncols) continue;
-    float y[16];
-#pragma unroll
-    for (int j4 = 0; j4 < 16; j4 += 4) {
-      const float4 sw4 = __ldg(reinterpret_cast<const float4 *>(a.e.sw + n0 + c0 + j4));
-      const float4 b4 = __ldg(reinterpret_cast<const float4 *>(a.e.bias + n0 + c0 + j4));
-      const int4 cs4 = __ldg(reinterpret_cast<const int4 *>(a.e.cs + n0 + c0 + j4));
-      const float swv[4] = {sw4.x, sw4.y, sw4.z, sw4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
-      const int32_t csv[4] = {cs4.x, cs4.y, cs4.z, cs4.w};
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        // deq4 (gemm_s8n.c:105-114): int32 wrap, exact int -> fp32, sw * sa first, multiply then add (no FMA)
-        const float f = __int2float_rn((int32_t)((uint32_t)acc[j4 + q] - (uint32_t)csv[q] * (uint32_t)za));
-        float v = __fadd_rn(__fmul_rn(f, __fmul_rn(swv[q], sa)), bv[q]);
-        if (a.e.act == 1) v = silu<true>(v, lut);
-        else if (a.e.act == 2) v = (v > 0.f || v != v) ? v : 0.f;  // FMAX(v, +0): NaN stays NaN, -0 -> +0
-        y[j4 + q] = v;
-      }
-    }
-    if (c0 + 16 <= ncols) {
-      if (rrow) {
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          const float4 r4 = *reinterpret_cast<const float4 *>(rrow + c0 + j);
-          y[j] = __fadd_rn(y[j], r4.x); y[j + 1] = __fadd_rn(y[j + 1], r4.y);
-          y[j + 2] = __fadd_rn(y[j + 2], r4.z); y[j + 3] = __fadd_rn(y[j + 3], r4.w);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 16; j += 4)
-        *reinterpret_cast<float4 *>(orow + c0 + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+  if (r) {
+    float rv[8];
+    if (a.vec_res) {
+      ld8_global(r, rv);
     } else {
-      for (int j = 0; j < 16 && c0 + j < ncols; j++) orow[c0 + j] = rrow ? __fadd_rn(y[j], rrow[c0 + j]) : y[j];
+#pragma unroll
+      for (int j = 0; j < 8; j++) rv[j] = __ldg(r + j);
     }
+#pragma unroll
+    for (int j = 0; j < 8; j++) y[j] = __fadd_rn(y[j], rv[j]);
+  }
+  if (a.vec_out) {
+    st8_global(o, y);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; j++) o[j] = y[j];
   }
 }
 
-template <int SW>
-__global__ void __launch_bounds__(64 + 128 * kMaxEpi, 1) k_gemm_s8(const __grid_constant__ CUtensorMap tma_a,
-                                                                  const __grid_constant__ CUtensorMap tma_b,
-                                                                  const GemmArgs a) {
+// kSP: the per-column parameters (sw, bias, cs; np <= kSPMax columns) are staged in shared memory once per CTA
+template <int SW, bool kSP>
+__global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constant__ CUtensorMap tma_a,
+                                                           const __grid_constant__ CUtensorMap tma_b,
+                                                           const GemmArgs a) {
   extern __shared__ uint8_t dsmem[];
   __shared__ __align__(8) unsigned long long bar_full[kMaxStages], bar_empty[kMaxStages];
   __shared__ __align__(8) unsigned long long bar_acc_full[kMaxEpi], bar_acc_empty[kMaxEpi];
@@ -292,17 +302,31 @@ __global__ void __launch_bounds__(64 + 128 * kMaxEpi, 1) k_gemm_s8(const __grid_
   const uint32_t base = (smem_u32(dsmem) + 1023u) & ~1023u;
   const uint32_t a_bytes = 128u * SW, stage_bytes = (128u + a.bn) * SW;
   const int S = a.stages;
+  // parameters after the stage ring: sw [np], bias [np], cs [np]
+  uint8_t *par = dsmem + (base - smem_u32(dsmem)) + (size_t)S * stage_bytes;
+  float *p_sw = reinterpret_cast<float *>(par), *p_b = p_sw + a.np;
+  int32_t *p_cs = reinterpret_cast<int32_t *>(p_b + a.np);
+  if (kSP) {
+    for (int i = threadIdx.x; i < a.np; i += blockDim.x) {
+      p_sw[i] = __ldg(a.e.sw + i);
+      p_b[i] = __ldg(a.e.bias + i);
+      p_cs[i] = __ldg(a.e.cs + i);
+    }
+  }
 
   for (int i = threadIdx.x; i < 256; i += blockDim.x) s_lut[i] = g_frecpe_lut[i];
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) { mbar_init(smem_u32(&bar_full[s]), 1); mbar_init(smem_u32(&bar_empty[s]), 1); }
-    for (int g = 0; g < a.ne; g++) { mbar_init(smem_u32(&bar_acc_full[g]), 1); mbar_init(smem_u32(&bar_acc_empty[g]), 4); }
+    for (int g = 0; g < a.ne; g++) {
+      mbar_init(smem_u32(&bar_acc_full[g]), 1);
+      mbar_init(smem_u32(&bar_acc_empty[g]), 4 * a.nh);
+    }
     abort_s = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
-                 "r"(a.acc_cols * a.ne));
+                 "r"(a.tmem_alloc));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -323,7 +347,7 @@ __global__ void __launch_bounds__(64 + 128 * kMaxEpi, 1) k_gemm_s8(const __grid_
             break;
           }
           const uint32_t st = base + s * stage_bytes, bar = smem_u32(&bar_full[s]);
-          mbar_expect_tx(bar, stage_bytes);
+          mbar_expect_tx(bar, stage_bytes);  // the full boxes: bytes past Kq arrive as zero fill
           tma_load_2d(st, &tma_a, bar, kb * SW, m0);
           tma_load_2d(st + a_bytes, &tma_b, bar, kb * SW, n0);
         }
@@ -361,10 +385,24 @@ __global__ void __launch_bounds__(64 + 128 * kMaxEpi, 1) k_gemm_s8(const __grid_
         mma_commit(smem_u32(&bar_acc_full[g]));  // arrives when this tile's MMAs have completed
       }
     }
-  } else if (warp - 2 < 4 * a.ne) {  // epilogue warpgroup g, TMEM lanes 32 q .. 32 q + 31
-    const int g = (warp - 2) / 4, q = warp % 4;
+  } else if (warp - 2 < 4 * a.ne * a.nh) {
+    // epilogue: group g drains accumulator g; its 4 * nh warps split the 8-column units of a tile round robin, the
+    // warp's TMEM lane quarter q (= warp % 4) fixing its 32 rows
+    const int e = warp - 2, g = e / (4 * a.nh), h = (e % (4 * a.nh)) / 4, q = warp % 4;
     int use = 0;
     for (int t = blockIdx.x + g * gridDim.x; t < a.tiles; t += a.ne * gridDim.x, use++) {
+      const int m0 = (t / a.n_tiles) * 128, n0 = (t % a.n_tiles) * a.bn;
+      const int row = m0 + q * 32 + lane;
+      const bool live = row < a.rows;
+      int w = 0, mm = 0;
+      float sa = 0.f;
+      int32_t za = 0;
+      if (live) {
+        w = row / a.Mw;
+        mm = row - w * a.Mw;
+        sa = __ldg(a.sa + row);
+        za = __ldg(a.za + row);
+      }
       bool ok = mbar_wait(smem_u32(&bar_acc_full[g]), use & 1);
       ok = __all_sync(0xffffffffu, ok) && !abort_s;
       if (!ok) {
@@ -372,9 +410,30 @@ __global__ void __launch_bounds__(64 + 128 * kMaxEpi, 1) k_gemm_s8(const __grid_
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int m0 = (t / a.n_tiles) * 128, n0 = (t % a.n_tiles) * a.bn;
-      const int row = m0 + q * 32 + lane;
-      epilogue_row(a, tmem + (uint32_t)(g * a.acc_cols) + ((uint32_t)(q * 32) << 16), row, n0, row < a.rows, s_lut);
+      const int units = (min(a.bn, a.np - n0) + 7) / 8;  // np is a multiple of 8
+      float *orow = a.e.out + (long long)w * a.e.ows + padded_row(mm, a.e.ow, a.e.opad) * a.e.ldo + n0;
+      const float *rrow = a.e.res ? a.e.res + (long long)w * a.e.rws + padded_row(mm, a.e.rw, a.e.rpad) * a.e.ldr + n0
+                                  : nullptr;
+      const float *qsw = kSP ? p_sw + n0 : a.e.sw + n0, *qb = kSP ? p_b + n0 : a.e.bias + n0;
+      const int32_t *qcs = kSP ? p_cs + n0 : a.e.cs + n0;
+      const uint32_t tq = tmem + (uint32_t)(g * a.acc_cols) + ((uint32_t)(q * 32) << 16);
+      for (int u0 = h; u0 < units; u0 += kEpiUnits * a.nh) {
+        uint32_t acc[kEpiUnits][8];
+#pragma unroll
+        for (int k = 0; k < kEpiUnits; k++) {
+          const int u = u0 + k * a.nh;
+          if (u < units) tmem_ld8(tq + (uint32_t)(8 * u), acc[k]);
+        }
+        tmem_wait(acc);
+        if (live) {
+#pragma unroll
+          for (int k = 0; k < kEpiUnits; k++) {
+            const int c = 8 * (u0 + k * a.nh);
+            if (c < 8 * units)
+              epilogue8(a, acc[k], sa, za, qsw + c, qb + c, qcs + c, orow + c, rrow ? rrow + c : nullptr, s_lut);
+          }
+        }
+      }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[g]));
@@ -383,7 +442,7 @@ __global__ void __launch_bounds__(64 + 128 * kMaxEpi, 1) k_gemm_s8(const __grid_
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.acc_cols * a.ne));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_alloc));
 }
 
 // ------------------------------------------------------------------ elementwise test kernel
@@ -400,6 +459,8 @@ __global__ void k_test_fn(int fn, int n, const float *x, float *y) {
   case 4: r = log2_acc(v); break;
   case 5: r = exp2_acc(v); break;
   case 6: r = glibc_expf(v, c_expf_tab); break;
+  case 7: r = silu2(make_float2(v, -v), g_frecpe_lut).x; break;
+  case 8: r = fma2_rn(make_float2(v, -v), splat2(1.7f), splat2(0.3f)).x; break;
   default: r = 0.f;
   }
   y[i] = r;
@@ -493,21 +554,50 @@ extern "C" int bnnk_gemm_weight_rows(int np) {
 
 static int g_num_sms = 0;
 
+// tcgen05.alloc takes a power of two from 32 to 512 columns
+static int tmem_pow2(int cols) {
+  int c = 32;
+  while (c < cols) c *= 2;
+  return c;
+}
+
+// epilogue shape: the widest epilogue that the thread limit allows with at least two accumulators, so that the MMA
+// of the next tile overlaps the epilogue of the last
+static void epi_shape(int tmem_cols, int *ne, int *nh) {
+  const int e = 2;  // tmem_cols <= 256: two accumulators always fit the 512 columns
+  const int h = (kMaxThreads - 64) / (128 * e);
+  const char *env = getenv("BNN_GEMM_EPI");  // "ne,nh" override for tuning sweeps
+  int ee = 0, hh = 0;
+  if (env && sscanf(env, "%d,%d", &ee, &hh) == 2 && ee >= 1 && ee <= kMaxEpi && tmem_pow2(ee * tmem_cols) <= 512 &&
+      hh >= 1 && 64 + 128 * ee * hh <= kMaxThreads) {
+    *ne = ee;
+    *nh = hh;
+    return;
+  }
+  *ne = e;
+  *nh = h;
+}
+
 extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_cap, int kq, const int8_t *w, int n,
                                    int np) {
   memset(p, 0, sizeof *p);
   if (kq % 32 || rows_cap <= 0 || n <= 0 || np < n) return cudaErrorInvalidValue;
   p->kq = kq;
-  p->sw = kq % 128 == 0 ? 128 : kq % 64 == 0 ? 64 : 32;
-  p->nkb = kq / p->sw;
+  // K blocks of 128 bytes (the widest swizzle); a ragged last block reads TMA zero fill past Kq on both operands,
+  // which adds nothing to the sums. K of 32 or 64 bytes: one block of exactly that width.
+  p->sw = kq <= 32 ? 32 : kq <= 64 ? 64 : 128;
+  p->nkb = (kq + p->sw - 1) / p->sw;
   p->n = n;
   p->np = np;
   n_tiling(np, &p->n_tiles, &p->bn);
   p->tmem_cols = p->bn <= 32 ? 32 : p->bn <= 64 ? 64 : p->bn <= 128 ? 128 : 256;
+  epi_shape(p->tmem_cols, &p->ne, &p->nh);
+  p->sp = np <= kSPMax;
+  const size_t par = p->sp ? (size_t)12 * np : 0;
   const size_t stage = (size_t)(128 + p->bn) * p->sw;
-  int s = (int)((200 * 1024) / stage);
+  int s = (int)((200 * 1024 - par) / stage);
   p->stages = s < 2 ? 2 : s > kMaxStages ? kMaxStages : s;
-  p->smem = (size_t)p->stages * stage + 1024;
+  p->smem = (size_t)p->stages * stage + 1024 + par;
   p->idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p->bn >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
   const int wrows = p->n_tiles * p->bn;  // the weight buffer holds n_tiles * bn rows (zero beyond n)
   int e = encode_2d(p->tma_a, q, kq, rows_cap, p->sw, 128, p->sw);
@@ -515,11 +605,11 @@ extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_
   return e;
 }
 
-template <int SW>
+template <int SW, bool kSP>
 static int launch_gemm(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(k_gemm_s8<SW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024);
+    cudaFuncSetAttribute(k_gemm_s8<SW, kSP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
     attr = true;
   }
   if (!g_num_sms) {
@@ -529,9 +619,13 @@ static int launch_gemm(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t 
     if (g_num_sms <= 0) g_num_sms = 148;
   }
   const int grid = a.tiles < g_num_sms ? a.tiles : g_num_sms;
-  k_gemm_s8<SW><<<grid, 64 + 128 * a.ne, p->smem, st>>>(*(const CUtensorMap *)p->tma_a,
-                                                        *(const CUtensorMap *)p->tma_b, a);
+  k_gemm_s8<SW, kSP><<<grid, 64 + 128 * a.ne * a.nh, p->smem, st>>>(*(const CUtensorMap *)p->tma_a,
+                                                                    *(const CUtensorMap *)p->tma_b, a);
   return cudaGetLastError();
+}
+
+static bool aligned32(const float *ptr, long long ws, int ld) {
+  return ((uintptr_t)ptr & 31) == 0 && ws % 8 == 0 && ld % 8 == 0;
 }
 
 extern "C" int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float *sa, const int32_t *za,
@@ -547,16 +641,28 @@ extern "C" int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float 
   a.n_tiles = p->n_tiles;
   a.tiles = ((rows + 127) / 128) * p->n_tiles;
   a.acc_cols = p->tmem_cols;
-  a.ne = 512 / p->tmem_cols < kMaxEpi ? 512 / p->tmem_cols : kMaxEpi;
+  a.ne = p->ne;
+  a.nh = p->nh;
+  a.tmem_alloc = tmem_pow2(p->ne * p->tmem_cols);
+  if (a.tmem_alloc > 512) return cudaErrorInvalidValue;
+  a.vec_out = aligned32(e->out, e->ows, e->ldo);
+  a.vec_res = e->res ? aligned32(e->res, e->rws, e->ldr) : 0;
   a.idesc = p->idesc;
   a.sa = sa;
   a.za = za;
   a.e = *e;
   a.err = err;
+  if (p->sp) {
+    switch (p->sw) {
+    case 128: return launch_gemm<128, true>(p, a, st);
+    case 64: return launch_gemm<64, true>(p, a, st);
+    default: return launch_gemm<32, true>(p, a, st);
+    }
+  }
   switch (p->sw) {
-  case 128: return launch_gemm<128>(p, a, st);
-  case 64: return launch_gemm<64>(p, a, st);
-  default: return launch_gemm<32>(p, a, st);
+  case 128: return launch_gemm<128, false>(p, a, st);
+  case 64: return launch_gemm<64, false>(p, a, st);
+  default: return launch_gemm<32, false>(p, a, st);
   }
 }
 

@@ -716,6 +716,6 @@ int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, i
 }
 
 int bnn_cuda_fn(int fn, int n, const float *d_x, float *d_y, void *stream) {
-  if (fn < 0 || fn > 6 || n < 0) { ERR(BNN_ERR_USAGE, "bnn_cuda_fn: fn %d n %d", fn, n); return -1; }
+  if (fn < 0 || fn > 8 || n < 0) { ERR(BNN_ERR_USAGE, "bnn_cuda_fn: fn %d n %d", fn, n); return -1; }
   return launch_rc("bnn_cuda_fn", bnnk_test_fn(fn, n, d_x, d_y, (bnn_stream_t)stream));
 }

@@ -103,7 +103,8 @@ int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, i
                  void *stream);
 
 /* elementwise functions of the int8 path, for tests: 0 SiLU, 1 SiLU (table estimate), 2 sigmoid, 3 FRECPE,
- * 4 log2 polynomial, 5 exp2 polynomial (front end), 6 glibc expf */
+ * 4 log2 polynomial, 5 exp2 polynomial (front end), 6 glibc expf, 7 SiLU on paired fp32 lanes (table estimate),
+ * 8 fma(x, 1.7f, 0.3f) on paired fp32 lanes */
 int bnn_cuda_fn(int fn, int n, const float *d_x, float *d_y, void *stream);
 
 #ifdef __cplusplus

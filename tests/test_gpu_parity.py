@@ -67,6 +67,22 @@ def test_elementwise(lib, fn, name):
     assert bits_equal(got, want), mismatch_report(got, want)
 
 
+def test_paired_fp32(lib):
+    """sm_100's paired fp32 fma rounds each lane once, as fmaf; the paired SiLU equals the reference's SiLU."""
+    x = sample_floats(20000, 8)
+    x = x[np.isfinite(x)]
+    xd = dev(x)
+    y = torch.empty(x.size, dtype=torch.float32, device="cuda")
+    ok = np.abs(x) < 1e30  # the double product is exact there, so rounding the double sum once equals fmaf
+    fused = (x[ok].astype(np.float64) * np.float64(np.float32(1.7)) + np.float64(np.float32(0.3))).astype(np.float32)
+    assert lib.bnn_cuda_fn(8, x.size, xd.data_ptr(), y.data_ptr(), None) == 0
+    got = host(y)[ok]
+    assert bits_equal(got, fused), mismatch_report(got, fused)
+    assert lib.bnn_cuda_fn(7, x.size, xd.data_ptr(), y.data_ptr(), None) == 0
+    got, want = host(y), oracle.fn("bnno_silu", x)
+    assert bits_equal(got, want), mismatch_report(got, want)
+
+
 def test_expf_matches_libm_exhaustive_slice(lib):
     """glibc expf restated on the GPU against the host libm over a dense slice of the floats around the SE range."""
     u = np.arange(0xC2D00000, 0xC2D00000 + 2 ** 22, dtype=np.uint32)  # [-104, ...]
@@ -145,6 +161,7 @@ PW_CASES = [  # (N, K, Mw, B, act, residual, padded output (ow), gated)
     (1536, 192, 24, 3, 1, False, 8, False),    # b4 pw
     (6522, 1024, 1, 300, 0, False, 0, False),  # the head (GEMV_S8 batched: M = windows)
     (10, 20, 7, 3, 2, True, 0, False),         # ragged: ReLU, residual, N and M not multiples of anything
+    (40, 36, 100, 2, 1, True, 0, True),        # SiLU + residual + gate (the C ABI allows what v2.4 never uses)
     (5, 3, 129, 1, 1, False, 0, False),        # tiny K
 ]
 
