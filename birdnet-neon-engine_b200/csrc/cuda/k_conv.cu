@@ -13,72 +13,106 @@ namespace bnn {
 
 // ------------------------------------------------------------------ DW3 (src/gemm_f32.c:214-440)
 
-// depthwise 3x3 (pad 1, stride s) + SiLU: one thread per (window, output pixel, 4 channels). Per channel the three
-// column partial sums of DW_ACC (gemm_f32.c:221-225): acc = b + w0 A0 + w3 A1 + w6 A2 (fused, in that order),
-// acb = w1 B0 + w4 B1 + w7 B2, acd = w2 C0 + w5 C1 + w8 C2, out = SiLU(acc + (acb + acd)).
-__global__ void __launch_bounds__(256) k_dw3_out(long long total, const float *__restrict__ xp, long long xws, int W,
-                                                 int C, int s, const float *__restrict__ wt,
-                                                 const float *__restrict__ bias, float *__restrict__ out,
-                                                 long long ows, int Wo, int P) {
-  __shared__ uint32_t lut[256];
-  lut[threadIdx.x] = g_frecpe_lut[threadIdx.x];
-  __syncthreads();
-  const long long idx = blockIdx.x * 256LL + threadIdx.x;
-  if (idx >= total) return;
-  const int C4 = C >> 2;
-  const int c4 = (int)(idx % C4);
-  const long long rest = idx / C4;
-  const int p = (int)(rest % P), win = (int)(rest / P);
-  const int oy = p / Wo, ox = p - oy * Wo, Wp = W + 2, c = 4 * c4;
-  const float *q = xp + win * xws + ((long long)(oy * s) * Wp + (long long)ox * s) * C + c;
-  float4 x[3][3];
-#pragma unroll
-  for (int ky = 0; ky < 3; ky++)
-#pragma unroll
-    for (int kx = 0; kx < 3; kx++) x[ky][kx] = __ldg(reinterpret_cast<const float4 *>(q + ((long long)ky * Wp + kx) * C));
-  float4 w[9];
-#pragma unroll
-  for (int t = 0; t < 9; t++) w[t] = __ldg(reinterpret_cast<const float4 *>(wt + t * C + c));
-  const float4 b4 = __ldg(reinterpret_cast<const float4 *>(bias + c));
-  float r[4];
-#pragma unroll
-  for (int l = 0; l < 4; l++) {
-#define E_(v) (l == 0 ? (v).x : l == 1 ? (v).y : l == 2 ? (v).z : (v).w)
-    float acc = __fmaf_rn(E_(w[0]), E_(x[0][0]), E_(b4));
-    float acb = __fmul_rn(E_(w[1]), E_(x[0][1]));
-    float acd = __fmul_rn(E_(w[2]), E_(x[0][2]));
-    acc = __fmaf_rn(E_(w[3]), E_(x[1][0]), acc);
-    acb = __fmaf_rn(E_(w[4]), E_(x[1][1]), acb);
-    acd = __fmaf_rn(E_(w[5]), E_(x[1][2]), acd);
-    acc = __fmaf_rn(E_(w[6]), E_(x[2][0]), acc);
-    acb = __fmaf_rn(E_(w[7]), E_(x[2][1]), acb);
-    acd = __fmaf_rn(E_(w[8]), E_(x[2][2]), acd);
-#undef E_
-    r[l] = silu<true>(__fadd_rn(acc, __fadd_rn(acb, acd)), lut);
-  }
-  *reinterpret_cast<float4 *>(out + win * ows + (long long)p * C + c) = make_float4(r[0], r[1], r[2], r[3]);
-}
+// Depthwise 3x3 (pad 1, stride S) + SiLU + channel sums, one kernel. Per channel the three column partial sums of
+// DW_ACC (gemm_f32.c:221-225): acc = b + w0 A0 + w3 A1 + w6 A2 (fused, in that order), acb = w1 B0 + w4 B1 + w7 B2,
+// acd = w2 C0 + w5 C1 + w8 C2, out = SiLU(acc + (acb + acd)); then chsum[c] = ((0 + v_0) + v_1) + ... over the
+// output pixels in raster order (silu_rows_f32, gemm_f32.c:303-328; dw_silu_row16 :342-365).
+//
+// One CTA per (window, group of 4 * cg4 channels) walks the output pixels in raster order, a chunk of nl * R pixels
+// at a time: thread (lane, c4) computes R consecutive pixels of one output row for 4 channels (R > 1 shares the
+// input columns of neighbouring taps; channel pairs go through sm_100's paired fp32 FMA and the paired SiLU), stores
+// them, and leaves them in shared memory; after the barrier one thread per channel continues its channel's sum over
+// the chunk in pixel order while the others compute the next chunk into the other buffer.
+constexpr int kDwThreads = 256;
 
-// channel sums: chsum[c] = ((0 + v_0) + v_1) + ... over the output pixels in raster order (silu_rows_f32,
-// gemm_f32.c:303-328; dw_silu_row16 :342-365). One thread per (window, channel); 32 loads in flight per chain, small
-// blocks so that every SM holds some of the chains.
-__global__ void __launch_bounds__(64) k_dw3_chsum(int total, const float *__restrict__ out, long long ows, int P, int C,
-                                                  float *__restrict__ chsum, long long cws) {
-  const int idx = blockIdx.x * 64 + threadIdx.x;
-  if (idx >= total) return;
-  const int win = idx / C, c = idx - win * C;
-  const float *o = out + win * ows + c;
-  float cs = 0.f;
-  int p = 0;
-  for (; p + 32 <= P; p += 32) {
-    float v[32];
+template <int S, int R>
+__global__ void __launch_bounds__(kDwThreads) k_dw3(const float *__restrict__ xp, long long xws, int W, int C, int cg4,
+                                                    int nl, const float *__restrict__ wt,
+                                                    const float *__restrict__ bias, float *__restrict__ out,
+                                                    long long ows, int Wo, int P, float *__restrict__ chsum,
+                                                    long long cws) {
+  extern __shared__ float sb[];  // [2][nl * R][4 * cg4]
+  __shared__ uint32_t lut[256];
+  const int tid = threadIdx.x;
+  lut[tid] = g_frecpe_lut[tid];
+  const int CG = 4 * cg4, ngroups = (C >> 2) / cg4;
+  const int win = blockIdx.x / ngroups, grp = blockIdx.x - win * ngroups;
+  const int c4l = tid % cg4, lane = tid / cg4;
+  const bool comp = lane < nl;
+  const int c = grp * CG + 4 * c4l, Wp = W + 2, chunk = nl * R;
+  float2 w[9][2], b[2];
+  if (comp) {
 #pragma unroll
-    for (int i = 0; i < 32; i++) v[i] = __ldg(o + (long long)(p + i) * C);
-#pragma unroll
-    for (int i = 0; i < 32; i++) cs = __fadd_rn(cs, v[i]);
+    for (int t = 0; t < 9; t++) {
+      const float4 v = __ldg(reinterpret_cast<const float4 *>(wt + t * C + c));
+      w[t][0] = make_float2(v.x, v.y);
+      w[t][1] = make_float2(v.z, v.w);
+    }
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(bias + c));
+    b[0] = make_float2(v.x, v.y);
+    b[1] = make_float2(v.z, v.w);
   }
-  for (; p < P; p++) cs = __fadd_rn(cs, __ldg(o + (long long)p * C));
-  chsum[win * cws + c] = cs;
+  const float *xw = xp + win * xws + c;
+  float *ow = out + win * ows + c;
+  float cs = 0.f;
+  __syncthreads();
+  for (int k = 0, p0c = 0; p0c < P; k++, p0c += chunk) {
+    float *buf = sb + (k & 1) * chunk * CG;
+    const int p0 = p0c + lane * R;
+    if (comp && p0 < P) {
+      const int oy = p0 / Wo, ox = p0 - oy * Wo;  // R pixels of one row (Wo % R == 0)
+      const float *q = xw + ((long long)(oy * S) * Wp + (long long)ox * S) * C;
+      constexpr int NX = (R - 1) * S + 3;  // input columns the R pixels read
+      float2 acc[R][2], acb[R][2], acd[R][2];
+#pragma unroll
+      for (int ky = 0; ky < 3; ky++) {
+        float2 xin[NX][2];
+#pragma unroll
+        for (int j = 0; j < NX; j++) {
+          const float4 v = __ldg(reinterpret_cast<const float4 *>(q + ((long long)ky * Wp + j) * C));
+          xin[j][0] = make_float2(v.x, v.y);
+          xin[j][1] = make_float2(v.z, v.w);
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            const float2 A = xin[r * S][h], Bv = xin[r * S + 1][h], Cv = xin[r * S + 2][h];
+            if (ky == 0) {
+              acc[r][h] = fma2_rn(w[0][h], A, b[h]);
+              acb[r][h] = mul2_rn(w[1][h], Bv);
+              acd[r][h] = mul2_rn(w[2][h], Cv);
+            } else {
+              acc[r][h] = fma2_rn(w[3 * ky][h], A, acc[r][h]);
+              acb[r][h] = fma2_rn(w[3 * ky + 1][h], Bv, acb[r][h]);
+              acd[r][h] = fma2_rn(w[3 * ky + 2][h], Cv, acd[r][h]);
+            }
+          }
+      }
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const float2 y0 = silu2(add2_rn(acc[r][0], add2_rn(acb[r][0], acd[r][0])), lut);
+        const float2 y1 = silu2(add2_rn(acc[r][1], add2_rn(acb[r][1], acd[r][1])), lut);
+        const float4 v = make_float4(y0.x, y0.y, y1.x, y1.y);
+        *reinterpret_cast<float4 *>(ow + (long long)(p0 + r) * C) = v;
+        *reinterpret_cast<float4 *>(buf + (lane * R + r) * CG + 4 * c4l) = v;
+      }
+    }
+    __syncthreads();
+    if (tid < CG) {
+      const int n = min(chunk, P - p0c);
+      int i = 0;
+      for (; i + 8 <= n; i += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = buf[(i + j) * CG + tid];
+#pragma unroll
+        for (int j = 0; j < 8; j++) cs = __fadd_rn(cs, v[j]);
+      }
+      for (; i < n; i++) cs = __fadd_rn(cs, buf[i * CG + tid]);
+    }
+  }
+  if (tid < CG) chsum[win * cws + grp * CG + tid] = cs;
 }
 
 // ------------------------------------------------------------------ SE_GATE (src/v24_f32.c:164-179, rt_ops_f32.c:272-283)
@@ -289,17 +323,34 @@ extern "C" int bnnk_fp32_tables_init(const unsigned long long *tab, const uint32
   return cudaMemcpyToSymbol(g_frecpe_lut, lut, sizeof(uint32_t) * 256);
 }
 
+template <int S, int R>
+static int launch_dw3(int B, int cg4, const float *xp, long long xws, int W, int C, const float *w, const float *b,
+                      float *out, long long ows, int Wo, int P, float *chsum, long long cws, bnn_stream_t st) {
+  const int nl = kDwThreads / cg4;
+  const size_t smem = sizeof(float) * 2 * nl * R * 4 * cg4;
+  const unsigned grid = (unsigned)B * (unsigned)((C / 4) / cg4);
+  k_dw3<S, R><<<grid, kDwThreads, smem, st>>>(xp, xws, W, C, cg4, nl, w, b, out, ows, Wo, P, chsum, cws);
+  return cudaGetLastError();
+}
+
 extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int C, int s, const float *w,
                         const float *b, float *out, long long ows, int Ho, int Wo, float *chsum, long long cws,
                         bnn_stream_t st) {
   (void)H;
   if (B <= 0) return 0;
-  const int P = Ho * Wo;
-  const long long total = (long long)B * P * (C / 4);
-  k_dw3_out<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(total, xp, xws, W, C, s, w, b, out, ows, Wo, P);
-  const int tc = B * C;
-  k_dw3_chsum<<<(tc + 63) / 64, 64, 0, st>>>(tc, out, ows, P, C, chsum, cws);
-  return cudaGetLastError();
+  const int P = Ho * Wo, C4 = C / 4;
+  // channel quads per CTA: a divisor of C4 of at most 32, the largest that still gives about four CTAs per SM
+  int cg4 = 1;
+  for (int d = 1; d <= 32 && d <= C4; d++)
+    if (C4 % d == 0 && (d == 1 || (long long)B * (C4 / d) >= 4 * 148)) cg4 = d;
+  if (cg4 == 1)
+    for (int d = 2; d <= 32 && d <= C4; d++)
+      if (C4 % d == 0 && d <= 8) cg4 = d;
+  const bool pair = Wo % 2 == 0;
+  if (s == 1) return pair ? launch_dw3<1, 2>(B, cg4, xp, xws, W, C, w, b, out, ows, Wo, P, chsum, cws, st)
+                          : launch_dw3<1, 1>(B, cg4, xp, xws, W, C, w, b, out, ows, Wo, P, chsum, cws, st);
+  return pair ? launch_dw3<2, 2>(B, cg4, xp, xws, W, C, w, b, out, ows, Wo, P, chsum, cws, st)
+              : launch_dw3<2, 1>(B, cg4, xp, xws, W, C, w, b, out, ows, Wo, P, chsum, cws, st);
 }
 
 extern "C" int bnnk_se_gate(int B, int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,

@@ -270,7 +270,7 @@ typedef struct {
 static const kdesc KERNELS[] = {
     {BNN_OP_FE_STFT2, "fe_stft2", init_fe_stft2, 0x2, 0, 2},
     {BNN_OP_C0POOL, "c0pool_f32", init_c0pool, 0x2, 0, 1},
-    {BNN_OP_DW3, "dw3_f32", init_dw3, 0x6, 0, 2},
+    {BNN_OP_DW3, "dw3_f32", init_dw3, 0x6, 0, 1},
     {BNN_OP_POSTPC, "postpc_f32", init_postpc, 0xe, 0, 2},
     {BNN_OP_SE_GATE, "se_gate_f32", init_se_gate, 0x2, 0, 1},
     {BNN_OP_PW_S8, "pw_s8n", init_pw_s8, 0x3a, 0x44, 2},
