@@ -200,26 +200,23 @@ __global__ void __launch_bounds__(128) k_c0pool(const float *__restrict__ img, l
   if (tid < 24) bs[tid] = bias[tid];
   __syncthreads();
   const int qx = tid;
-  float acc0[24], acc1[24];
+  float2 acc0[12], acc1[12];  // channel pairs (paired fp32 FMA: each lane one fused multiply-add)
 #pragma unroll
-  for (int n = 0; n < 24; n++) acc0[n] = acc1[n] = 0.f;
+  for (int n = 0; n < 12; n++) acc0[n] = acc1[n] = make_float2(0.f, 0.f);
   for (int ky = 0; ky < 4; ky++) {
-#pragma unroll 2
+#pragma unroll 4
     for (int kk = 0; kk < 16; kk++) {
       const int c0 = kk, c1 = kk + 4;  // float offsets of the two pixels' patches from 8 qx
-      const float a0 = rows[ky][c0 & 7][qx + (c0 >> 3)], a1 = rows[ky][c1 & 7][qx + (c1 >> 3)];
+      const float2 a0 = splat2(rows[ky][c0 & 7][qx + (c0 >> 3)]), a1 = splat2(rows[ky][c1 & 7][qx + (c1 >> 3)]);
       const float4 *wr = reinterpret_cast<const float4 *>(ws[ky * 16 + kk]);
 #pragma unroll
       for (int n4 = 0; n4 < 6; n4++) {
         const float4 w = wr[n4];
-        acc0[4 * n4] = __fmaf_rn(w.x, a0, acc0[4 * n4]);
-        acc0[4 * n4 + 1] = __fmaf_rn(w.y, a0, acc0[4 * n4 + 1]);
-        acc0[4 * n4 + 2] = __fmaf_rn(w.z, a0, acc0[4 * n4 + 2]);
-        acc0[4 * n4 + 3] = __fmaf_rn(w.w, a0, acc0[4 * n4 + 3]);
-        acc1[4 * n4] = __fmaf_rn(w.x, a1, acc1[4 * n4]);
-        acc1[4 * n4 + 1] = __fmaf_rn(w.y, a1, acc1[4 * n4 + 1]);
-        acc1[4 * n4 + 2] = __fmaf_rn(w.z, a1, acc1[4 * n4 + 2]);
-        acc1[4 * n4 + 3] = __fmaf_rn(w.w, a1, acc1[4 * n4 + 3]);
+        const float2 wl = make_float2(w.x, w.y), wh = make_float2(w.z, w.w);
+        acc0[2 * n4] = fma2_rn(wl, a0, acc0[2 * n4]);
+        acc0[2 * n4 + 1] = fma2_rn(wh, a0, acc0[2 * n4 + 1]);
+        acc1[2 * n4] = fma2_rn(wl, a1, acc1[2 * n4]);
+        acc1[2 * n4 + 1] = fma2_rn(wh, a1, acc1[2 * n4 + 1]);
       }
     }
   }
@@ -230,7 +227,8 @@ __global__ void __launch_bounds__(128) k_c0pool(const float *__restrict__ img, l
 #pragma unroll
     for (int l = 0; l < 4; l++) {
       const int n = 4 * n4 + l;
-      const float u = fmax_nan(__fadd_rn(acc0[n], bs[n]), 0.f), v = fmax_nan(__fadd_rn(acc1[n], bs[n]), 0.f);
+      const float c0v = (l & 1) ? acc0[n >> 1].y : acc0[n >> 1].x, c1v = (l & 1) ? acc1[n >> 1].y : acc1[n >> 1].x;
+      const float u = fmax_nan(__fadd_rn(c0v, bs[n]), 0.f), v = fmax_nan(__fadd_rn(c1v, bs[n]), 0.f);
       mx[l] = fmax_nan(u, v);
       av[l] = __fmul_rn(__fadd_rn(u, v), 0.5f);
     }
@@ -253,62 +251,86 @@ __global__ void k_postpc_im2col(const float *__restrict__ X, long long xws, cons
   }
 }
 
-// pc GEMM + ReLU + mean: thread = 2 output channels for WG windows x 6 rows, sequential fused multiply-adds from 0 over
-// k (the reference's K loop), bias after, ReLU, then the 6 rows added in order and scaled by 1/6. The rows of a
-// window-group sit in shared memory, read 4 k at a time.
-constexpr int kPcWG = 8, kPcKC = 64, kPcT = 64;
-__global__ void __launch_bounds__(kPcT) k_postpc_gemm(int B, const float *__restrict__ pcin, const float *__restrict__ wt,
-                                                     const float *__restrict__ bias, float *__restrict__ feat,
-                                                     long long fws) {
-  __shared__ __align__(16) float a_s[kPcWG][6][kPcKC];
-  const int n = blockIdx.x * (2 * kPcT) + 2 * threadIdx.x, w0 = blockIdx.y * kPcWG;
-  float acc[kPcWG][6][2];
+// pc GEMM + ReLU + mean. Each output (row m = 6 w + r, column n) is one sequential chain of fused multiply-adds from
+// 0 over k = 0 .. 1727 (the reference's K loop), so only the schedule around the chains is free: a CTA owns 16
+// windows (96 rows) x 64 columns, its 256 threads 6 rows x 4 columns each (two paired-fp32 FMA chains per row, each
+// lane rounded once as fmaf), with 32-k slices of both operands double-buffered in shared memory by cp.async. The
+// epilogue adds the bias, applies ReLU and sums the window's 6 rows in order, scaled by 1/6.
+constexpr int kPcM = 96, kPcN = 64, kPcK = 32, kPcKs = kPcK + 4, kPcThreads = 256, kPcKTot = 1728;
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  const int n = valid ? 16 : 0;  // zero fill past the last row
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
+
+__global__ void __launch_bounds__(kPcThreads) k_postpc_gemm(int B, const float *__restrict__ pcin,
+                                                            const float *__restrict__ wt,
+                                                            const float *__restrict__ bias, float *__restrict__ feat,
+                                                            long long fws) {
+  __shared__ __align__(16) float a_s[2][kPcM][kPcKs];
+  __shared__ __align__(16) float w_s[2][kPcK][kPcN];
+  const int tid = threadIdx.x, wl = tid / 16, cg = tid % 16;
+  const int m0 = blockIdx.y * kPcM, n0 = blockIdx.x * kPcN, rows = min(kPcM, 6 * B - m0);
+  auto load = [&](int st, int k0) {
+    for (int i = tid; i < kPcM * kPcK / 4; i += kPcThreads) {
+      const int m = i / (kPcK / 4), kq = i - m * (kPcK / 4);
+      const bool ok = m < rows;
+      cp_async16(&a_s[st][m][4 * kq], pcin + (long long)(m0 + (ok ? m : 0)) * kPcKTot + k0 + 4 * kq, ok);
+    }
+    for (int i = tid; i < kPcK * kPcN / 4; i += kPcThreads) {
+      const int kk = i / (kPcN / 4), nq = i - kk * (kPcN / 4);
+      cp_async16(&w_s[st][kk][4 * nq], wt + (long long)(k0 + kk) * 1024 + n0 + 4 * nq, true);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float2 acc[6][2];
 #pragma unroll
-  for (int j = 0; j < kPcWG; j++)
-#pragma unroll
-    for (int r = 0; r < 6; r++) acc[j][r][0] = acc[j][r][1] = 0.f;
-  for (int k0 = 0; k0 < 1728; k0 += kPcKC) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < kPcWG * 6 * kPcKC / 4; i += kPcT) {
-      const int e = 4 * i, j = e / (6 * kPcKC), rem = e - j * 6 * kPcKC, r = rem / kPcKC, kk = rem - r * kPcKC;
-      const float4 v = (w0 + j < B) ? *reinterpret_cast<const float4 *>(pcin + ((long long)(w0 + j) * 6 + r) * 1728 + k0 + kk)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<float4 *>(&a_s[j][r][kk]) = v;
+  for (int r = 0; r < 6; r++) acc[r][0] = acc[r][1] = make_float2(0.f, 0.f);
+  constexpr int kChunks = kPcKTot / kPcK;
+  load(0, 0);
+  for (int c = 0; c < kChunks; c++) {
+    if (c + 1 < kChunks) {
+      load((c + 1) & 1, (c + 1) * kPcK);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
-    for (int kk = 0; kk < kPcKC; kk += 4) {
-      float2 w[4];
+    const int st = c & 1;
 #pragma unroll
-      for (int u = 0; u < 4; u++) w[u] = __ldg(reinterpret_cast<const float2 *>(wt + (long long)(k0 + kk + u) * 1024 + n));
+    for (int kk = 0; kk < kPcK; kk += 4) {
+      float4 a[6];
 #pragma unroll
-      for (int j = 0; j < kPcWG; j++)
+      for (int r = 0; r < 6; r++) a[r] = *reinterpret_cast<const float4 *>(&a_s[st][wl * 6 + r][kk]);
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const float4 w4 = *reinterpret_cast<const float4 *>(&w_s[st][kk + u][4 * cg]);
+        const float2 w01 = make_float2(w4.x, w4.y), w23 = make_float2(w4.z, w4.w);
 #pragma unroll
         for (int r = 0; r < 6; r++) {
-          const float4 a = *reinterpret_cast<const float4 *>(&a_s[j][r][kk]);
-          acc[j][r][0] = __fmaf_rn(a.x, w[0].x, acc[j][r][0]);
-          acc[j][r][1] = __fmaf_rn(a.x, w[0].y, acc[j][r][1]);
-          acc[j][r][0] = __fmaf_rn(a.y, w[1].x, acc[j][r][0]);
-          acc[j][r][1] = __fmaf_rn(a.y, w[1].y, acc[j][r][1]);
-          acc[j][r][0] = __fmaf_rn(a.z, w[2].x, acc[j][r][0]);
-          acc[j][r][1] = __fmaf_rn(a.z, w[2].y, acc[j][r][1]);
-          acc[j][r][0] = __fmaf_rn(a.w, w[3].x, acc[j][r][0]);
-          acc[j][r][1] = __fmaf_rn(a.w, w[3].y, acc[j][r][1]);
+          const float av = u == 0 ? a[r].x : u == 1 ? a[r].y : u == 2 ? a[r].z : a[r].w;
+          acc[r][0] = fma2_rn(splat2(av), w01, acc[r][0]);
+          acc[r][1] = fma2_rn(splat2(av), w23, acc[r][1]);
         }
+      }
     }
+    __syncthreads();
   }
-  const float b0 = bias[n], b1v = bias[n + 1];
+  if (wl * 6 >= rows) return;
+  const int n = n0 + 4 * cg;
+  const float4 b4 = *reinterpret_cast<const float4 *>(bias + n);
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int j = 0; j < kPcWG; j++) {
-    if (w0 + j >= B) break;
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-    for (int r = 0; r < 6; r++) {
-      s0 = __fadd_rn(s0, fmax_nan(__fadd_rn(acc[j][r][0], b0), 0.f));
-      s1 = __fadd_rn(s1, fmax_nan(__fadd_rn(acc[j][r][1], b1v), 0.f));
-    }
-    *reinterpret_cast<float2 *>(feat + (long long)(w0 + j) * fws + n) =
-        make_float2(__fmul_rn(s0, 0x1.555556p-3f), __fmul_rn(s1, 0x1.555556p-3f));
+  for (int r = 0; r < 6; r++) {
+    s[0] = __fadd_rn(s[0], fmax_nan(__fadd_rn(acc[r][0].x, b4.x), 0.f));
+    s[1] = __fadd_rn(s[1], fmax_nan(__fadd_rn(acc[r][0].y, b4.y), 0.f));
+    s[2] = __fadd_rn(s[2], fmax_nan(__fadd_rn(acc[r][1].x, b4.z), 0.f));
+    s[3] = __fadd_rn(s[3], fmax_nan(__fadd_rn(acc[r][1].y, b4.w), 0.f));
   }
+  const float k6 = 0x1.555556p-3f;
+  *reinterpret_cast<float4 *>(feat + (long long)(m0 / 6 + wl) * fws + n) =
+      make_float4(__fmul_rn(s[0], k6), __fmul_rn(s[1], k6), __fmul_rn(s[2], k6), __fmul_rn(s[3], k6));
 }
 
 }  // namespace bnn
@@ -372,6 +394,6 @@ extern "C" int bnnk_postpc(int B, const float *X, long long xws, const float *po
                            const float *wt, const float *b, float *pcin, float *feat, long long fws, bnn_stream_t st) {
   if (B <= 0) return 0;
   k_postpc_im2col<<<B, 256, 0, st>>>(X, xws, post_s, post_b, pcin);
-  k_postpc_gemm<<<dim3(1024 / (2 * kPcT), (B + kPcWG - 1) / kPcWG), kPcT, 0, st>>>(B, pcin, wt, b, feat, fws);
+  k_postpc_gemm<<<dim3(1024 / kPcN, (6 * B + kPcM - 1) / kPcM), kPcThreads, 0, st>>>(B, pcin, wt, b, feat, fws);
   return cudaGetLastError();
 }

@@ -32,7 +32,11 @@ namespace bnn {
 
 // ------------------------------------------------------------------ quantizer
 
-template <int L>
+// L lanes per row hold the row's float4 groups j = lane + i L (i < NV) in registers across both passes: the row's
+// NaN-propagating min / max (the 4-wide part of s8n_quant_rows; K % 4 == 0 here, so there is no scalar tail),
+// reduced over the lanes, then the quantized bytes. Gate and scale multiplies run paired (each lane an IEEE
+// multiply; their products feed no add).
+template <int L, int NV>
 __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__restrict__ x, long long xws, int lda,
                                                int K, int Kq, const float *__restrict__ gate, long long gws,
                                                int8_t *__restrict__ q, float *__restrict__ sa,
@@ -44,16 +48,24 @@ __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__
   const int w = r / Mw, m = r - w * Mw;
   const float *xr = x + w * xws + (long long)m * lda;
   const float *gr = gate ? gate + w * gws : nullptr;
-  const int K4 = K / 4;
+  const int K4 = K >> 2;
+  float4 v[NV];
   float lo = __int_as_float(0x7f800000), hi = __int_as_float(0xff800000);
-  for (int j = lane; j < K4; j += L) {
-    float4 v = *reinterpret_cast<const float4 *>(xr + 4 * j);
-    if (gr) {
-      float4 g = *reinterpret_cast<const float4 *>(gr + 4 * j);
-      v.x = __fmul_rn(v.x, g.x); v.y = __fmul_rn(v.y, g.y); v.z = __fmul_rn(v.z, g.z); v.w = __fmul_rn(v.w, g.w);
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    const int j = lane + i * L;
+    if (j < K4) {
+      float4 t = __ldg(reinterpret_cast<const float4 *>(xr + 4 * j));
+      if (gr) {
+        const float4 g = __ldg(reinterpret_cast<const float4 *>(gr + 4 * j));
+        const float2 a = mul2_rn(make_float2(t.x, t.y), make_float2(g.x, g.y));
+        const float2 c = mul2_rn(make_float2(t.z, t.w), make_float2(g.z, g.w));
+        t = make_float4(a.x, a.y, c.x, c.y);
+      }
+      v[i] = t;
+      lo = fmin_nan(lo, fmin_nan(fmin_nan(t.x, t.y), fmin_nan(t.z, t.w)));
+      hi = fmax_nan(hi, fmax_nan(fmax_nan(t.x, t.y), fmax_nan(t.z, t.w)));
     }
-    lo = fmin_nan(lo, fmin_nan(fmin_nan(v.x, v.y), fmin_nan(v.z, v.w)));
-    hi = fmax_nan(hi, fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w)));
   }
 #pragma unroll
   for (int o = L / 2; o > 0; o >>= 1) {
@@ -71,32 +83,29 @@ __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__
     z = (int32_t)(0u - 127u - (uint32_t)lrintf_i32(__fmul_rn(lo, inv)));
     s = __fdiv_rn(d, 254.f);
   }
-  if (valid && lane == 0) { sa[row] = s; za[row] = z; }
+  if (!valid) return;
+  if (lane == 0) { sa[row] = s; za[row] = z; }
   const int K8 = K & ~7;
-  int8_t *qr = q + (long long)r * Kq;
-  for (int j = lane; 4 * j < Kq; j += L) {
-    const int k = 4 * j;
-    uint32_t packed;
-    if (k < K) {
-      float4 v = *reinterpret_cast<const float4 *>(xr + k);
-      if (gr) {
-        float4 g = *reinterpret_cast<const float4 *>(gr + k);
-        v.x = __fmul_rn(v.x, g.x); v.y = __fmul_rn(v.y, g.y); v.z = __fmul_rn(v.z, g.z); v.w = __fmul_rn(v.w, g.w);
-      }
-      const float e[4] = {v.x, v.y, v.z, v.w};
-      packed = 0;
+  uint32_t *qr = reinterpret_cast<uint32_t *>(q + (long long)r * Kq);
+  const float2 inv2 = splat2(inv);
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        float t = __fmul_rn(e[i], inv);
-        int32_t qi = (int32_t)((uint32_t)(k < K8 ? cvtns(t) : lrintf_i32(t)) + (uint32_t)z);
-        qi = qi < -127 ? -127 : qi > 127 ? 127 : qi;
-        packed |= ((uint32_t)qi & 0xffu) << (8 * i);
+  for (int i = 0; i < NV; i++) {
+    const int j = lane + i * L;
+    if (j < K4) {
+      const float2 a = mul2_rn(make_float2(v[i].x, v[i].y), inv2), c = mul2_rn(make_float2(v[i].z, v[i].w), inv2);
+      int32_t qi[4];
+      if (4 * j < K8) {  // the 8-wide part: FCVTNS
+        qi[0] = cvtns(a.x); qi[1] = cvtns(a.y); qi[2] = cvtns(c.x); qi[3] = cvtns(c.y);
+      } else {           // the tail: lrintf
+        qi[0] = lrintf_i32(a.x); qi[1] = lrintf_i32(a.y); qi[2] = lrintf_i32(c.x); qi[3] = lrintf_i32(c.y);
       }
-    } else {
-      packed = ((uint32_t)z & 0xffu) * 0x01010101u;
+#pragma unroll
+      for (int e = 0; e < 4; e++) qi[e] = min(max((int32_t)((uint32_t)qi[e] + (uint32_t)z), -127), 127);
+      qr[j] = __byte_perm(__byte_perm(qi[0], qi[1], 0x0040), __byte_perm(qi[2], qi[3], 0x0040), 0x5410);
     }
-    if (valid) *reinterpret_cast<uint32_t *>(qr + k) = packed;
   }
+  const uint32_t zp = ((uint32_t)z & 0xffu) * 0x01010101u;  // pads past K: the zero point
+  for (int j = K4 + lane; j < (Kq >> 2); j += L) qr[j] = zp;
 }
 
 // The general form (any K, any lda): one thread per row, the reference's loops as written.
@@ -499,15 +508,24 @@ extern "C" int bnnk_quant(int rows, int Mw, const float *x, long long xws, int l
   if (rows <= 0) return 0;
   const bool vec = K % 4 == 0 && lda % 4 == 0 && xws % 4 == 0 && (!gate || gws % 4 == 0) && Kq % 4 == 0 &&
                    ((uintptr_t)x & 15) == 0 && (!gate || ((uintptr_t)gate & 15) == 0);
-  if (!vec) {
+  const int K4 = K / 4;
+  if (!vec || K4 > 32 * 12) {
     k_quant_scalar<<<(rows + 127) / 128, 128, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za);
-  } else if (K <= 128) {
-    const int per = 256 / 8;
-    k_quant<8><<<(rows + per - 1) / per, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za);
-  } else {
-    const int per = 256 / 32;
-    k_quant<32><<<(rows + per - 1) / per, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za);
+    return cudaGetLastError();
   }
+  // lanes per row: the fewest (a power of two) that hold the row in at most 4 float4 each, else 32 lanes x 12
+  int L = 1;
+  while (L < 32 && (K4 + L - 1) / L > 4) L *= 2;
+  const unsigned grid = (unsigned)(((long long)rows * L + 255) / 256);
+#define BNN_Q(LL, NV) k_quant<LL, NV><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za)
+  if ((K4 + L - 1) / L > 4) BNN_Q(32, 12);
+  else if (L == 1) BNN_Q(1, 4);
+  else if (L == 2) BNN_Q(2, 4);
+  else if (L == 4) BNN_Q(4, 4);
+  else if (L == 8) BNN_Q(8, 4);
+  else if (L == 16) BNN_Q(16, 4);
+  else BNN_Q(32, 4);
+#undef BNN_Q
   return cudaGetLastError();
 }
 
