@@ -247,52 +247,77 @@ __device__ __forceinline__ long long padded_row(int m, int w, int pad) {
   return pad ? (long long)((m / w) + pad) * (w + 2 * pad) + (m % w) + pad : (long long)m;
 }
 
-// The epilogue of 8 columns n .. n+7 of one row (gemm_s8n.c:105-135): dequantize, bias, activation, residual, store.
-// psw / pb / pcs point at column n of the per-column parameters (shared or global memory).
-__device__ __forceinline__ void epilogue8(const GemmArgs &a, const uint32_t (&acc)[8], float sa, int32_t za,
-                                          const float *psw, const float *pb, const int32_t *pcs, float *o,
-                                          const float *r, const uint32_t *lut) {
-  const float4 sw0 = *reinterpret_cast<const float4 *>(psw), sw1 = *reinterpret_cast<const float4 *>(psw + 4);
-  const float4 b0 = *reinterpret_cast<const float4 *>(pb), b1 = *reinterpret_cast<const float4 *>(pb + 4);
-  const int4 c0 = *reinterpret_cast<const int4 *>(pcs), c1 = *reinterpret_cast<const int4 *>(pcs + 4);
-  const float sw[8] = {sw0.x, sw0.y, sw0.z, sw0.w, sw1.x, sw1.y, sw1.z, sw1.w};
-  const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-  const int32_t cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+// The epilogue of NU 8-column units of one row (gemm_s8n.c:105-135): unit k covers the columns c_k .. c_k + 7, c_k =
+// 8 (u0 + k nh) from the tile's first column. Dequantize, bias, activation ACT (0 none, 1 SiLU, 2 ReLU), residual
+// (RES), store; VEC: 32-byte aligned rows (8-float loads and stores). Branch-free for fixed template arguments, so
+// the units' independent chains can overlap. psw / pb / pcs point at the tile's first column of the per-column
+// parameters (shared or global memory).
+template <int ACT, bool RES, bool VEC, int NU>
+__device__ __forceinline__ void epilogue_units(const uint32_t (&acc)[kEpiUnits][8], int kofs, int u0, int nh, float sa,
+                                               int32_t za, const float *psw, const float *pb, const int32_t *pcs,
+                                               float *orow, const float *rrow, const uint32_t *lut) {
   const float2 sa2 = splat2(sa);
-  float y[8];
 #pragma unroll
-  for (int j = 0; j < 8; j += 2) {
-    // deq4 (gemm_s8n.c:105-114): int32 wrap, exact int -> fp32, sw * sa first, multiply then add (no FMA)
-    const float f0 = __int2float_rn((int32_t)(acc[j] - (uint32_t)cs[j] * (uint32_t)za));
-    const float f1 = __int2float_rn((int32_t)(acc[j + 1] - (uint32_t)cs[j + 1] * (uint32_t)za));
-    const float2 s = mul2_rn(make_float2(sw[j], sw[j + 1]), sa2);
-    float2 v = make_float2(__fadd_rn(__fmul_rn(f0, s.x), bb[j]), __fadd_rn(__fmul_rn(f1, s.y), bb[j + 1]));
-    if (a.e.act == 1) {
-      v = silu2(v, lut);
-    } else if (a.e.act == 2) {  // FMAX(v, +0): NaN stays NaN, -0 -> +0
-      v.x = (v.x > 0.f || v.x != v.x) ? v.x : 0.f;
-      v.y = (v.y > 0.f || v.y != v.y) ? v.y : 0.f;
-    }
-    y[j] = v.x;
-    y[j + 1] = v.y;
-  }
-  if (r) {
+  for (int k = 0; k < NU; k++) {
+    const int c = 8 * (u0 + k * nh);
     float rv[8];
-    if (a.vec_res) {
-      ld8_global(r, rv);
+    if (RES) {
+      if (VEC) {
+        ld8_global(rrow + c, rv);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) rv[j] = __ldg(rrow + c + j);
+      }
+    }
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      const float2 sw = *reinterpret_cast<const float2 *>(psw + c + j), bb = *reinterpret_cast<const float2 *>(pb + c + j);
+      const int2 cs = *reinterpret_cast<const int2 *>(pcs + c + j);
+      // deq4 (gemm_s8n.c:105-114): int32 wrap, exact int -> fp32, sw * sa first, multiply then add (no FMA)
+      const float f0 = __int2float_rn((int32_t)(acc[kofs + k][j] - (uint32_t)cs.x * (uint32_t)za));
+      const float f1 = __int2float_rn((int32_t)(acc[kofs + k][j + 1] - (uint32_t)cs.y * (uint32_t)za));
+      const float2 sc = mul2_rn(sw, sa2);
+      float2 v = make_float2(__fadd_rn(__fmul_rn(f0, sc.x), bb.x), __fadd_rn(__fmul_rn(f1, sc.y), bb.y));
+      if (ACT == 1) {
+        v = silu2(v, lut);
+      } else if (ACT == 2) {  // FMAX(v, +0): NaN stays NaN, -0 -> +0
+        v.x = (v.x > 0.f || v.x != v.x) ? v.x : 0.f;
+        v.y = (v.y > 0.f || v.y != v.y) ? v.y : 0.f;
+      }
+      y[j] = RES ? __fadd_rn(v.x, rv[j]) : v.x;
+      y[j + 1] = RES ? __fadd_rn(v.y, rv[j + 1]) : v.y;
+    }
+    if (VEC) {
+      st8_global(orow + c, y);
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; j++) rv[j] = __ldg(r + j);
+      for (int j = 0; j < 8; j++) orow[c + j] = y[j];
     }
-#pragma unroll
-    for (int j = 0; j < 8; j++) y[j] = __fadd_rn(y[j], rv[j]);
   }
-  if (a.vec_out) {
-    st8_global(o, y);
+}
+
+template <int NU>
+__device__ __forceinline__ void epilogue_act(const GemmArgs &a, const uint32_t (&acc)[kEpiUnits][8], int kofs, int u0,
+                                             int nh, float sa, int32_t za, const float *psw, const float *pb,
+                                             const int32_t *pcs, float *orow, const float *rrow, const uint32_t *lut) {
+#define BNN_E(ACT, RES, VEC) \
+  epilogue_units<ACT, RES, VEC, NU>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut)
+  const bool vec = a.vec_out && (!rrow || a.vec_res);
+  if (!vec) {  // rows off 32-byte boundaries (per-op API callers): one general form
+    if (rrow) {
+      if (a.e.act == 1) BNN_E(1, true, false); else if (a.e.act == 2) BNN_E(2, true, false); else BNN_E(0, true, false);
+    } else {
+      if (a.e.act == 1) BNN_E(1, false, false); else if (a.e.act == 2) BNN_E(2, false, false); else BNN_E(0, false, false);
+    }
+    return;
+  }
+  if (rrow) {
+    if (a.e.act == 1) BNN_E(1, true, true); else if (a.e.act == 2) BNN_E(2, true, true); else BNN_E(0, true, true);
   } else {
-#pragma unroll
-    for (int j = 0; j < 8; j++) o[j] = y[j];
+    if (a.e.act == 1) BNN_E(1, false, true); else if (a.e.act == 2) BNN_E(2, false, true); else BNN_E(0, false, true);
   }
+#undef BNN_E
 }
 
 // kSP: the per-column parameters (sw, bias, cs; np <= kSPMax columns) are staged in shared memory once per CTA
@@ -435,11 +460,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
         }
         tmem_wait(acc);
         if (live) {
+          if (u0 + (kEpiUnits - 1) * a.nh < units) {  // every unit of the batch is a real column block
+            epilogue_act<kEpiUnits>(a, acc, 0, u0, a.nh, sa, za, qsw, qb, qcs, orow, rrow, s_lut);
+          } else {
 #pragma unroll
-          for (int k = 0; k < kEpiUnits; k++) {
-            const int c = 8 * (u0 + k * a.nh);
-            if (c < 8 * units)
-              epilogue8(a, acc[k], sa, za, qsw + c, qb + c, qcs + c, orow + c, rrow ? rrow + c : nullptr, s_lut);
+            for (int k = 0; k < kEpiUnits; k++)
+              if (u0 + k * a.nh < units)
+                epilogue_act<1>(a, acc, k, u0 + k * a.nh, a.nh, sa, za, qsw, qb, qcs, orow, rrow, s_lut);
           }
         }
       }
