@@ -32,11 +32,12 @@ namespace bnn {
 
 // ------------------------------------------------------------------ quantizer
 
-// L lanes per row hold the row's float4 groups j = lane + i L (i < NV) in registers across both passes: the row's
+// L lanes per row; lane l owns the 16-element chunks ch = l + i L (i < NC) of the quantized row (Kq / 16 chunks:
+// 64 contiguous input bytes, 16 contiguous output bytes each), held in registers across both passes: the row's
 // NaN-propagating min / max (the 4-wide part of s8n_quant_rows; K % 4 == 0 here, so there is no scalar tail),
-// reduced over the lanes, then the quantized bytes. Gate and scale multiplies run paired (each lane an IEEE
-// multiply; their products feed no add).
-template <int L, int NV>
+// reduced over the lanes, then the quantized bytes (pads past K = the zero point), one 16-byte store per chunk.
+// Gate and scale multiplies run paired (each lane an IEEE multiply; their products feed no add).
+template <int L, int NC>
 __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__restrict__ x, long long xws, int lda,
                                                int K, int Kq, const float *__restrict__ gate, long long gws,
                                                int8_t *__restrict__ q, float *__restrict__ sa,
@@ -48,23 +49,27 @@ __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__
   const int w = r / Mw, m = r - w * Mw;
   const float *xr = x + w * xws + (long long)m * lda;
   const float *gr = gate ? gate + w * gws : nullptr;
-  const int K4 = K >> 2;
-  float4 v[NV];
+  const int K4 = K >> 2, nch = Kq >> 4;
+  float4 v[NC][4];
   float lo = __int_as_float(0x7f800000), hi = __int_as_float(0xff800000);
 #pragma unroll
-  for (int i = 0; i < NV; i++) {
-    const int j = lane + i * L;
-    if (j < K4) {
-      float4 t = __ldg(reinterpret_cast<const float4 *>(xr + 4 * j));
-      if (gr) {
-        const float4 g = __ldg(reinterpret_cast<const float4 *>(gr + 4 * j));
-        const float2 a = mul2_rn(make_float2(t.x, t.y), make_float2(g.x, g.y));
-        const float2 c = mul2_rn(make_float2(t.z, t.w), make_float2(g.z, g.w));
-        t = make_float4(a.x, a.y, c.x, c.y);
+  for (int i = 0; i < NC; i++) {
+    const int ch = lane + i * L;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const int g = 4 * ch + e;  // float4 group
+      if (ch < nch && g < K4) {
+        float4 t = __ldg(reinterpret_cast<const float4 *>(xr + 4 * g));
+        if (gr) {
+          const float4 gg = __ldg(reinterpret_cast<const float4 *>(gr + 4 * g));
+          const float2 p0 = mul2_rn(make_float2(t.x, t.y), make_float2(gg.x, gg.y));
+          const float2 p1 = mul2_rn(make_float2(t.z, t.w), make_float2(gg.z, gg.w));
+          t = make_float4(p0.x, p0.y, p1.x, p1.y);
+        }
+        v[i][e] = t;
+        lo = fmin_nan(lo, fmin_nan(fmin_nan(t.x, t.y), fmin_nan(t.z, t.w)));
+        hi = fmax_nan(hi, fmax_nan(fmax_nan(t.x, t.y), fmax_nan(t.z, t.w)));
       }
-      v[i] = t;
-      lo = fmin_nan(lo, fmin_nan(fmin_nan(t.x, t.y), fmin_nan(t.z, t.w)));
-      hi = fmax_nan(hi, fmax_nan(fmax_nan(t.x, t.y), fmax_nan(t.z, t.w)));
     }
   }
 #pragma unroll
@@ -86,26 +91,35 @@ __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__
   if (!valid) return;
   if (lane == 0) { sa[row] = s; za[row] = z; }
   const int K8 = K & ~7;
-  uint32_t *qr = reinterpret_cast<uint32_t *>(q + (long long)r * Kq);
+  uint4 *qr = reinterpret_cast<uint4 *>(q + (long long)r * Kq);
   const float2 inv2 = splat2(inv);
+  const uint32_t zp = ((uint32_t)z & 0xffu) * 0x01010101u;  // a pad word: the zero point
 #pragma unroll
-  for (int i = 0; i < NV; i++) {
-    const int j = lane + i * L;
-    if (j < K4) {
-      const float2 a = mul2_rn(make_float2(v[i].x, v[i].y), inv2), c = mul2_rn(make_float2(v[i].z, v[i].w), inv2);
-      int32_t qi[4];
-      if (4 * j < K8) {  // the 8-wide part: FCVTNS
-        qi[0] = cvtns(a.x); qi[1] = cvtns(a.y); qi[2] = cvtns(c.x); qi[3] = cvtns(c.y);
-      } else {           // the tail: lrintf
-        qi[0] = lrintf_i32(a.x); qi[1] = lrintf_i32(a.y); qi[2] = lrintf_i32(c.x); qi[3] = lrintf_i32(c.y);
+  for (int i = 0; i < NC; i++) {
+    const int ch = lane + i * L;
+    if (ch >= nch) break;
+    uint32_t wd[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const int g = 4 * ch + e;
+      if (g < K4) {
+        const float2 p0 = mul2_rn(make_float2(v[i][e].x, v[i][e].y), inv2);
+        const float2 p1 = mul2_rn(make_float2(v[i][e].z, v[i][e].w), inv2);
+        int32_t qi[4];
+        if (4 * g < K8) {  // the 8-wide part: FCVTNS
+          qi[0] = cvtns(p0.x); qi[1] = cvtns(p0.y); qi[2] = cvtns(p1.x); qi[3] = cvtns(p1.y);
+        } else {           // the tail: lrintf
+          qi[0] = lrintf_i32(p0.x); qi[1] = lrintf_i32(p0.y); qi[2] = lrintf_i32(p1.x); qi[3] = lrintf_i32(p1.y);
+        }
+#pragma unroll
+        for (int t = 0; t < 4; t++) qi[t] = min(max((int32_t)((uint32_t)qi[t] + (uint32_t)z), -127), 127);
+        wd[e] = __byte_perm(__byte_perm(qi[0], qi[1], 0x0040), __byte_perm(qi[2], qi[3], 0x0040), 0x5410);
+      } else {
+        wd[e] = zp;
       }
-#pragma unroll
-      for (int e = 0; e < 4; e++) qi[e] = min(max((int32_t)((uint32_t)qi[e] + (uint32_t)z), -127), 127);
-      qr[j] = __byte_perm(__byte_perm(qi[0], qi[1], 0x0040), __byte_perm(qi[2], qi[3], 0x0040), 0x5410);
     }
+    qr[ch] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
   }
-  const uint32_t zp = ((uint32_t)z & 0xffu) * 0x01010101u;  // pads past K: the zero point
-  for (int j = K4 + lane; j < (Kq >> 2); j += L) qr[j] = zp;
 }
 
 // The general form (any K, any lda): one thread per row, the reference's loops as written.
@@ -535,23 +549,28 @@ extern "C" int bnnk_quant(int rows, int Mw, const float *x, long long xws, int l
   if (rows <= 0) return 0;
   const bool vec = K % 4 == 0 && lda % 4 == 0 && xws % 4 == 0 && (!gate || gws % 4 == 0) && Kq % 4 == 0 &&
                    ((uintptr_t)x & 15) == 0 && (!gate || ((uintptr_t)gate & 15) == 0);
-  const int K4 = K / 4;
-  if (!vec || K4 > 32 * 12) {
+  const int nch = Kq / 16;  // 16-byte chunks of a quantized row
+  if (!vec || Kq % 16 || nch > 32 * 3) {
     k_quant_scalar<<<(rows + 127) / 128, 128, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za);
     return cudaGetLastError();
   }
-  // lanes per row: the fewest (a power of two) that hold the row in at most 4 float4 each, else 32 lanes x 12
+  // lanes per row: the largest power of two up to 32 that is not above the chunk count; chunks per lane from that
   int L = 1;
-  while (L < 32 && (K4 + L - 1) / L > 4) L *= 2;
+  while (L < 32 && 2 * L <= nch) L *= 2;
+  const int NC = (nch + L - 1) / L;
   const unsigned grid = (unsigned)(((long long)rows * L + 255) / 256);
-#define BNN_Q(LL, NV) k_quant<LL, NV><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za)
-  if ((K4 + L - 1) / L > 4) BNN_Q(32, 12);
-  else if (L == 1) BNN_Q(1, 4);
-  else if (L == 2) BNN_Q(2, 4);
-  else if (L == 4) BNN_Q(4, 4);
-  else if (L == 8) BNN_Q(8, 4);
-  else if (L == 16) BNN_Q(16, 4);
-  else BNN_Q(32, 4);
+#define BNN_Q(LL, NN) k_quant<LL, NN><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za)
+#define BNN_QL(LL) \
+  if (NC == 1) BNN_Q(LL, 1); else if (NC == 2) BNN_Q(LL, 2); else BNN_Q(LL, 3)
+  switch (L) {
+  case 1: BNN_QL(1); break;
+  case 2: BNN_QL(2); break;
+  case 4: BNN_QL(4); break;
+  case 8: BNN_QL(8); break;
+  case 16: BNN_QL(16); break;
+  default: BNN_QL(32); break;
+  }
+#undef BNN_QL
 #undef BNN_Q
   return cudaGetLastError();
 }
