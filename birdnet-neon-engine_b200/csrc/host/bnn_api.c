@@ -354,6 +354,43 @@ static int check_err_word(bnn_ctx *c, int di) {
   return 0;
 }
 
+/* the upload pipeline's buffers, stream and events on the current device, sized for the context's batch */
+static cudaError_t upload_setup(bnn_ctx *c, bnn_dev *dv) {
+  cudaError_t e = cudaSuccess;
+  if (dv->up_cap < c->batch) {
+    if (dv->up_stream) e = cudaStreamSynchronize((cudaStream_t)dv->up_stream);
+    cudaFree(dv->up[0]); cudaFree(dv->up[1]);
+    dv->up[0] = dv->up[1] = NULL;
+    dv->up_cap = 0;
+    const size_t bytes = sizeof(float) * (size_t)c->batch * c->info.n_samples;
+    if (!e) e = cudaMalloc((void **)&dv->up[0], bytes);
+    if (!e) e = cudaMalloc((void **)&dv->up[1], bytes);
+    if (e) return e;
+    dv->up_cap = c->batch;
+  }
+  if (!dv->up_stream) {
+    e = cudaStreamCreateWithFlags((cudaStream_t *)&dv->up_stream, cudaStreamNonBlocking);
+    for (int k = 0; k < 2 && !e; k++) {
+      e = cudaEventCreateWithFlags((cudaEvent_t *)&dv->up_ready[k], cudaEventDisableTiming);
+      if (!e) e = cudaEventCreateWithFlags((cudaEvent_t *)&dv->up_free[k], cudaEventDisableTiming);
+    }
+  }
+  return e;
+}
+
+/* windows per pipeline chunk: the first is half of min(call, batch) (from 64 windows on; smaller calls run in one
+ * chunk), the next ones a full batch, and a tail shorter than half a chunk joins its predecessor. Only the first
+ * upload is not hidden behind kernels; every chunk pays the op list's fixed launch latencies, so chunks stay large. */
+static int next_chunk(int rem, int batch, int prev) {
+  const int first = rem < batch ? rem : batch;
+  int s = prev ? batch : first >= 64 ? (first / 2 + 7) / 8 * 8 : first;
+  if (s > rem) s = rem;
+  if (rem - s > 0 && rem - s < s / 2 && rem <= batch) s = rem;
+  return s;
+}
+
+/* one device's share [w0, w1) of a bnn_infer_batch call: chunk i is uploaded into buffer i % 2 on the copy stream
+ * (after chunk i - 2's kernels have finished reading it) while chunk i - 1 computes on the context's stream */
 static void *dev_worker(void *a) {
   dev_job *j = a;
   bnn_ctx *c = j->c;
@@ -362,25 +399,34 @@ static void *dev_worker(void *a) {
   const int ns = c->info.n_samples, nc = c->info.n_classes, ne = c->info.emb_dim;
   cudaStream_t st = (cudaStream_t)dv->stream;
   cudaError_t e = cudaSetDevice(dv->dev);
-  for (int w = j->w0; w < j->w1 && !e && !j->rc; w += c->batch) {
-    const int nb = j->w1 - w < c->batch ? j->w1 - w : c->batch;
-    e = cudaMemcpyAsync(dv->buf[d->in_buf], j->pcm + (size_t)w * ns, sizeof(float) * (size_t)nb * ns,
-                        cudaMemcpyHostToDevice, st);
+  if (!e) e = upload_setup(c, dv);
+  cudaStream_t cs = (cudaStream_t)dv->up_stream;
+  for (int w = j->w0, k = 0, nb = 0; w < j->w1 && !e && !j->rc; w += nb, k ^= 1) {
+    nb = next_chunk(j->w1 - w, c->batch, nb);
+    float *buf = dv->up[k];
+    e = cudaStreamWaitEvent(cs, (cudaEvent_t)dv->up_free[k], 0);
+    if (!e) e = cudaMemcpyAsync(buf, j->pcm + (size_t)w * ns, sizeof(float) * (size_t)nb * ns,
+                                cudaMemcpyHostToDevice, cs);
+    if (!e) e = cudaEventRecord((cudaEvent_t)dv->up_ready[k], cs);
+    if (!e) e = cudaStreamWaitEvent(st, (cudaEvent_t)dv->up_ready[k], 0);
     if (e) break;
-    if (bnn_rt_launch(c, j->di, nb, dv->buf[d->in_buf], 0, c->n_ops, st)) {
+    if (bnn_rt_launch(c, j->di, nb, buf, 0, c->n_ops, st)) {
       j->rc = -1;
       snprintf(j->err, sizeof j->err, "%s", g_err);
       j->kind = g_kind;
       break;
     }
-    e = cudaMemcpy2DAsync(j->out + (size_t)w * nc, sizeof(float) * nc, dv->buf[d->out_buf],
-                          sizeof(float) * dv->ws[d->out_buf], sizeof(float) * nc, nb, cudaMemcpyDeviceToHost, st);
+    e = cudaEventRecord((cudaEvent_t)dv->up_free[k], st);
+    if (!e)
+      e = cudaMemcpy2DAsync(j->out + (size_t)w * nc, sizeof(float) * nc, dv->buf[d->out_buf],
+                            sizeof(float) * dv->ws[d->out_buf], sizeof(float) * nc, nb, cudaMemcpyDeviceToHost, st);
     if (!e && j->emb && ne)
       e = cudaMemcpy2DAsync(j->emb + (size_t)w * ne, sizeof(float) * ne, dv->buf[d->emb_buf],
                             sizeof(float) * dv->ws[d->emb_buf], sizeof(float) * ne, nb, cudaMemcpyDeviceToHost, st);
   }
   if (!e) e = cudaMemcpyAsync(dv->err_host, dv->err, sizeof(int), cudaMemcpyDeviceToHost, st);
   if (!e) e = cudaStreamSynchronize(st);
+  if (!e && cs) e = cudaStreamSynchronize(cs);
   if (e && !j->rc) {
     j->rc = -1;
     j->kind = BNN_ERR_WINDOW;

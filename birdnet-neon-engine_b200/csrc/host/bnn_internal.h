@@ -87,6 +87,12 @@ typedef struct {
   bnnk_fe_tables fe;
   void *fe_mem[32];     /* the front-end tables: 9 per spectrogram */
   int n_fe_mem;
+  /* bnn_infer_batch's upload pipeline: two device input buffers of up_cap windows (outside the slot plan, whose
+   * input slot later ops may reuse), a copy stream, and per buffer an upload-done and a compute-done event */
+  float *up[2];
+  int up_cap;
+  void *up_stream;
+  void *up_ready[2], *up_free[2];
   /* per-op CUDA-event profile (bnn_profile_*): events[2 i], events[2 i + 1] bracket op i of the last launch */
   void **events;
   double *op_ms;

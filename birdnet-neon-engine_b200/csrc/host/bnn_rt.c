@@ -725,6 +725,12 @@ void bnn_rt_device_free(bnn_ctx *c, int di) {
   cudaFree(dv->arena);
   cudaFree(dv->q); cudaFree(dv->sa); cudaFree(dv->za); cudaFree(dv->fe_minmax); cudaFree(dv->pcin); cudaFree(dv->err);
   if (dv->err_host) cudaFreeHost(dv->err_host);
+  cudaFree(dv->up[0]); cudaFree(dv->up[1]);
+  for (int k = 0; k < 2; k++) {
+    if (dv->up_ready[k]) cudaEventDestroy((cudaEvent_t)dv->up_ready[k]);
+    if (dv->up_free[k]) cudaEventDestroy((cudaEvent_t)dv->up_free[k]);
+  }
+  if (dv->up_stream) cudaStreamDestroy((cudaStream_t)dv->up_stream);
   if (dv->stream) cudaStreamDestroy((cudaStream_t)dv->stream);
   free(dv->buf); free(dv->priv); free(dv->ws); free(dv->ops);
   free(dv);
