@@ -83,6 +83,7 @@ SIGNATURES = {
     "bnn_pw_s8_free": (None, [_P]),
     "bnn_cuda_dw3": (_I, [_I, _P, _LL, _I, _I, _I, _I, _P, _P, _P, _LL, _I, _I, _P, _LL, _P]),
     "bnn_cuda_fn": (_I, [_I, _I, _P, _P, _P]),
+    "bnn_cuda_op_error": (_I, []),
 }
 
 _LIB = None

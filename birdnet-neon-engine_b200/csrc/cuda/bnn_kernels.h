@@ -15,7 +15,7 @@ extern "C" {
 typedef struct CUstream_st *bnn_stream_t;
 
 /* device-side error word written by kernels whose bounded waits time out (0 = none) */
-enum { BNNK_ERR_NONE = 0, BNNK_ERR_TMA_WAIT = 1, BNNK_ERR_MMA_WAIT = 2, BNNK_ERR_EPI_WAIT = 3 };
+enum { BNNK_ERR_NONE = 0, BNNK_ERR_TMA_WAIT = 1, BNNK_ERR_MMA_WAIT = 2, BNNK_ERR_EPI_WAIT = 3, BNNK_ERR_DW3_WAIT = 4 };
 
 /* per device, once: the glibc expf table (computed on the host) and the FRECPE estimate table */
 int bnnk_device_init(void);
@@ -66,9 +66,10 @@ int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float *sa, const 
 int bnnk_pw_s8_static(const bnnk_gemm_plan *p, int rows, int Mw, const float *x, long long xws, int lda, int K,
                       const float *gate, long long gws, const bnnk_epilogue *e, int *err, bnn_stream_t st);
 
-/* ---- depthwise 3x3 + SiLU + channel sums (DW3): xp [B][(H+2)(W+2)][C] haloed, out [B][Ho Wo][C], chsum [B][C] */
+/* ---- depthwise 3x3 + SiLU + channel sums (DW3): xp [B][(H+2)(W+2)][C] haloed, out [B][Ho Wo][C], chsum [B][C].
+ * err: the device error word a timed-out input wait is reported in (NULL: not reported) */
 int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int C, int s, const float *w, const float *b,
-             float *out, long long ows, int Ho, int Wo, float *chsum, long long cws, bnn_stream_t st);
+             float *out, long long ows, int Ho, int Wo, float *chsum, long long cws, int *err, bnn_stream_t st);
 
 /* ---- SE gate (SE_GATE): chsum [B][C] -> gate [B][C] */
 int bnnk_se_gate(int B, int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,

@@ -3,11 +3,14 @@
 // Each output is computed with the reference's operations in the reference's order (fused where the NEON code fuses,
 // rounded where it rounds), so the values are bit-identical; only the parallel schedule is ours, and no reference
 // reduction is split across threads except where its order is restated exactly.
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <stdint.h>
 
 #include "bnn_kernels.h"
 #include "emu.cuh"
+#include "sync.cuh"
 
 namespace bnn {
 
@@ -111,6 +114,136 @@ __global__ void __launch_bounds__(kDwThreads) k_dw3(const float *__restrict__ xp
       }
       for (; i < n; i++) cs = __fadd_rn(cs, buf[i * CG + tid]);
     }
+  }
+  if (tid < CG) chsum[win * cws + grp * CG + tid] = cs;
+}
+
+// The same DW3 with the input streamed by TMA. One CTA per (window, group of CG channels) walks the output rows:
+// the haloed input rows (W + 2 pixels x CG channels each, one 3-D tensor-map box) pass through a ring of NR slots in
+// shared memory, loaded one row step ahead (NR = S + 3: the 3 rows of this step plus the S new rows of the next), so
+// every input byte is read from HBM once and no thread waits on a global load. Thread (lane, channel quad) keeps its
+// quad's weights in registers and computes pixel groups lane, lane + NL, ... of the row (R consecutive pixels per
+// group share their input columns), stores them and leaves them in a double-buffered row tile; after the step's
+// barrier the first CG threads continue their channel's sum over the row in pixel order.
+template <int S, int R>
+__global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMap tmx, int W, int C, int CG, int Ho,
+                                              int Wo, const float *__restrict__ wt, const float *__restrict__ bias,
+                                              float *__restrict__ out, long long ows, float *__restrict__ chsum,
+                                              long long cws, int *err) {
+  constexpr int NR = S + 3, NX = (R - 1) * S + 3;
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ __align__(8) unsigned long long bar[NR];
+  __shared__ uint32_t lut[256];
+  const int tid = threadIdx.x, nt = blockDim.x;
+  for (int i = tid; i < 256; i += nt) lut[i] = g_frecpe_lut[i];
+  const int ngroups = C / CG;
+  const int win = blockIdx.x / ngroups, grp = blockIdx.x - win * ngroups;
+  const int Wp = W + 2, Q = CG >> 2, NL = nt / Q, ngrp = Wo / R;
+  const uint32_t row_bytes = (uint32_t)Wp * CG * 4, row_stride = (row_bytes + 127u) & ~127u;
+  const uint32_t ring = smem_u32(dsm);
+  const float *ringf = reinterpret_cast<const float *>(dsm);
+  float *obuf = reinterpret_cast<float *>(dsm + NR * row_stride);  // [2][Wo][CG]
+  const int q = tid % Q, lane = tid / Q;  // lanes >= NL (the last nt % Q threads) only sum
+  const bool comp = lane < NL;
+  const int c = grp * CG + 4 * q;
+  float2 w[9][2], b[2];
+#pragma unroll
+  for (int t = 0; t < 9; t++) {
+    const float4 v = comp ? __ldg(reinterpret_cast<const float4 *>(wt + t * C + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    w[t][0] = make_float2(v.x, v.y);
+    w[t][1] = make_float2(v.z, v.w);
+  }
+  {
+    const float4 v = comp ? __ldg(reinterpret_cast<const float4 *>(bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    b[0] = make_float2(v.x, v.y);
+    b[1] = make_float2(v.z, v.w);
+  }
+  if (tid == 0) {
+    for (int i = 0; i < NR; i++) mbar_init(smem_u32(&bar[i]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int rows_in = (Ho - 1) * S + 3;  // input rows the outputs read
+  int issued = 0;                        // rows whose load thread 0 has issued
+  auto issue_to = [&](int last) {        // thread 0: load rows issued .. last
+    for (; issued <= last && issued < rows_in; issued++) {
+      const int sl = issued % NR;
+      mbar_expect_tx(smem_u32(&bar[sl]), row_bytes);
+      tma_load_3d(ring + sl * row_stride, &tmx, smem_u32(&bar[sl]), grp * CG, issued * Wp, win);
+    }
+  };
+  if (tid == 0) issue_to(S + 2);  // the rows of steps 0 and 1
+  float cs = 0.f;
+  int oy = 0;
+  for (; oy < Ho; oy++) {
+    bool ok = true;
+#pragma unroll
+    for (int ky = 0; ky < 3; ky++) {
+      const int iy = oy * S + ky;
+      ok = ok && mbar_wait(smem_u32(&bar[iy % NR]), (uint32_t)(iy / NR) & 1u);
+    }
+    float *ob = obuf + (oy & 1) * Wo * CG;
+    if (comp) {
+      for (int g = lane; g < ngrp; g += NL) {
+        const int x0 = g * R;
+        float2 acc[R][2], acb[R][2], acd[R][2];
+#pragma unroll
+        for (int ky = 0; ky < 3; ky++) {
+          const float *rw = ringf + ((oy * S + ky) % NR) * (row_stride >> 2) + (x0 * S) * CG + 4 * q;
+          float4 xin[NX];
+#pragma unroll
+          for (int j = 0; j < NX; j++) xin[j] = *reinterpret_cast<const float4 *>(rw + j * CG);
+#pragma unroll
+          for (int r = 0; r < R; r++) {
+            const float4 A4 = xin[r * S], B4 = xin[r * S + 1], C4 = xin[r * S + 2];
+            const float2 A[2] = {make_float2(A4.x, A4.y), make_float2(A4.z, A4.w)};
+            const float2 Bv[2] = {make_float2(B4.x, B4.y), make_float2(B4.z, B4.w)};
+            const float2 Cv[2] = {make_float2(C4.x, C4.y), make_float2(C4.z, C4.w)};
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              if (ky == 0) {
+                acc[r][h] = fma2_rn(w[0][h], A[h], b[h]);
+                acb[r][h] = mul2_rn(w[1][h], Bv[h]);
+                acd[r][h] = mul2_rn(w[2][h], Cv[h]);
+              } else {
+                acc[r][h] = fma2_rn(w[3 * ky][h], A[h], acc[r][h]);
+                acb[r][h] = fma2_rn(w[3 * ky + 1][h], Bv[h], acb[r][h]);
+                acd[r][h] = fma2_rn(w[3 * ky + 2][h], Cv[h], acd[r][h]);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          const float2 y0 = silu2(add2_rn(acc[r][0], add2_rn(acb[r][0], acd[r][0])), lut);
+          const float2 y1 = silu2(add2_rn(acc[r][1], add2_rn(acb[r][1], acd[r][1])), lut);
+          const float4 v = make_float4(y0.x, y0.y, y1.x, y1.y);
+          *reinterpret_cast<float4 *>(out + win * ows + (long long)(oy * Wo + x0 + r) * C + c) = v;
+          *reinterpret_cast<float4 *>(ob + (x0 + r) * CG + 4 * q) = v;
+        }
+      }
+    }
+    if (!__syncthreads_and(ok)) break;  // every thread has left this step's rows and written its outputs
+    if (tid == 0) issue_to((oy + 2) * S + 2);
+    if (tid < CG) {
+      int x = 0;
+      for (; x + 8 <= Wo; x += 8) {
+        float u[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) u[j] = ob[(x + j) * CG + tid];
+#pragma unroll
+        for (int j = 0; j < 8; j++) cs = __fadd_rn(cs, u[j]);
+      }
+      for (; x < Wo; x++) cs = __fadd_rn(cs, ob[x * CG + tid]);
+    }
+  }
+  if (oy < Ho) {  // a load never arrived: report it, then let the loads still in flight land before leaving
+    if (tid == 0) {
+      if (err) atomicExch(err, BNNK_ERR_DW3_WAIT);
+      for (int iy = oy * S; iy < issued; iy++) mbar_wait(smem_u32(&bar[iy % NR]), (uint32_t)(iy / NR) & 1u);
+    }
+    __syncthreads();
+    return;
   }
   if (tid < CG) chsum[win * cws + grp * CG + tid] = cs;
 }
@@ -355,13 +488,70 @@ static int launch_dw3(int B, int cg4, const float *xp, long long xws, int W, int
   return cudaGetLastError();
 }
 
+static PFN_cuTensorMapEncodeTiled_v12000 conv_encode_fn(void) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult qr;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  }
+  return fn;
+}
+
+// shared memory of the TMA form for CG channels: the ring of S + 3 input rows and the two output-row tiles
+static size_t dw3t_smem(int W, int Wo, int s, int cg) {
+  const size_t row_stride = ((size_t)(W + 2) * cg * 4 + 127) & ~(size_t)127;
+  return (size_t)(s + 3) * row_stride + sizeof(float) * 2 * Wo * cg;
+}
+
+// channels per CTA for the TMA form: the largest multiple of 4 dividing C, at most 256 (one box dimension) and with
+// at most 113 KB of shared memory (two CTAs per SM); 0 if none
+static int dw3t_group(int C, int W, int Wo, int s) {
+  int best = 0;
+  for (int cg = 4; cg <= C && cg <= 256; cg += 4)
+    if (C % cg == 0 && dw3t_smem(W, Wo, s, cg) <= 113 * 1024) best = cg;
+  return best;
+}
+
 extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int C, int s, const float *w,
                         const float *b, float *out, long long ows, int Ho, int Wo, float *chsum, long long cws,
-                        bnn_stream_t st) {
-  (void)H;
+                        int *err, bnn_stream_t st) {
   if (B <= 0) return 0;
   const int P = Ho * Wo, C4 = C / 4;
-  // channel quads per CTA: a divisor of C4 of at most 32, the largest that still gives about four CTAs per SM
+  const int cg = dw3t_group(C, W, Wo, s);
+  PFN_cuTensorMapEncodeTiled_v12000 enc = conv_encode_fn();
+  if (cg && enc && ((uintptr_t)xp & 15) == 0 && (xws * 4) % 16 == 0 && W + 2 <= 256 && (s == 1 || s == 2) &&
+      (Ho - 1) * s + 3 <= H + 2 && ((uintptr_t)out & 15) == 0 && ows % 4 == 0) {
+    CUtensorMap map;
+    cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)(H + 2) * (W + 2), (cuuint64_t)B};
+    cuuint64_t strides[2] = {(cuuint64_t)C * 4, (cuuint64_t)xws * 4};
+    cuuint32_t box[3] = {(cuuint32_t)cg, (cuuint32_t)(W + 2), 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(xp), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+      const size_t smem = dw3t_smem(W, Wo, s, cg);
+      const unsigned grid = (unsigned)B * (unsigned)(C / cg);
+      // threads: whole channel quads up to 256, at least the CG summing threads
+      const int Q = cg / 4;
+      int nt = (256 / Q) * Q;
+      if (nt < cg) nt = cg;
+      nt = (nt + 31) / 32 * 32;
+      const bool pair = Wo % 2 == 0;
+#define BNN_DW3T(SS, RR)                                                                                   \
+  do {                                                                                                    \
+    cudaFuncSetAttribute(k_dw3t<SS, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);         \
+    k_dw3t<SS, RR><<<grid, nt, smem, st>>>(map, W, C, cg, Ho, Wo, w, b, out, ows, chsum, cws, err);       \
+  } while (0)
+      if (s == 1) { if (pair) BNN_DW3T(1, 2); else BNN_DW3T(1, 1); }
+      else { if (pair) BNN_DW3T(2, 2); else BNN_DW3T(2, 1); }
+#undef BNN_DW3T
+      return cudaGetLastError();
+    }
+  }
+  // general strides: the form that loads its taps directly
   int cg4 = 1;
   for (int d = 1; d <= 32 && d <= C4; d++)
     if (C4 % d == 0 && (d == 1 || (long long)B * (C4 / d) >= 4 * 148)) cg4 = d;

@@ -27,6 +27,7 @@
 
 #include "bnn_kernels.h"
 #include "emu.cuh"
+#include "sync.cuh"
 
 namespace bnn {
 
@@ -161,49 +162,10 @@ __global__ void k_quant_scalar(int rows, int Mw, const float *__restrict__ x, lo
 
 // ------------------------------------------------------------------ tcgen05 GEMM
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far above any legitimate wait
 constexpr int kMaxStages = 8, kMaxEpi = 4;
 constexpr int kMaxThreads = 832;  // 2 + 24 warps: 64 + 128 * ne * nh with ne * nh <= 6
 constexpr int kSPMax = 1536;      // widest layer whose epilogue parameters are staged in shared memory
 
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-// bounded wait for the phase with the given parity to complete; false on timeout
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  const unsigned long long t0 = gtimer();
-  for (;;) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (gtimer() - t0 > kWaitNs) return false;
-  }
-}
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          dst),
-      "l"(map), "r"(bar), "r"(x), "r"(y)
-      : "memory");
-}
 // shared-memory matrix descriptor of a K-major tile with rows of SW bytes swizzled by SW (8-row groups of 8 * SW
 // bytes); version 1 (sm_100), base offset 0 (stages are aligned to the swizzle repeat)
 template <int SW>

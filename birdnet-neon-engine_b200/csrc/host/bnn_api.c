@@ -629,10 +629,36 @@ int bnn_debug_set_buffer(bnn_ctx *c, int buf, int n, const void *src) { return d
 
 /* ------------------------------------------------------------------ per-op entry points */
 
+/* per device: the error word of the per-op entry points (bnn_cuda_op_error) */
+static int *g_op_err[64];
+static pthread_mutex_t g_op_err_mu = PTHREAD_MUTEX_INITIALIZER;
+
+static int *op_err_word(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) || dev < 0 || dev >= 64) return NULL;
+  pthread_mutex_lock(&g_op_err_mu);
+  if (!g_op_err[dev] && !cudaMalloc((void **)&g_op_err[dev], sizeof(int)) &&
+      cudaMemset(g_op_err[dev], 0, sizeof(int))) {
+    cudaFree(g_op_err[dev]);
+    g_op_err[dev] = NULL;
+  }
+  int *w = g_op_err[dev];
+  pthread_mutex_unlock(&g_op_err_mu);
+  return w;
+}
+
 int bnn_cuda_device_init(void) {
-  const int e = bnnk_device_init();
+  int e = bnnk_device_init();
+  if (!e && !op_err_word()) e = cudaErrorMemoryAllocation;
   if (e) { ERR(BNN_ERR_CPU, "bnn_cuda_device_init: CUDA error %d (%s)", e, cudaGetErrorString((cudaError_t)e)); return -1; }
   return 0;
+}
+
+int bnn_cuda_op_error(void) {
+  int *w = op_err_word(), v = 0;
+  if (!w || cudaMemcpy(&v, w, sizeof v, cudaMemcpyDeviceToHost)) return -1;
+  if (v) cudaMemset(w, 0, sizeof(int));
+  return v;
 }
 
 static int launch_rc(const char *what, int e) {
@@ -758,7 +784,7 @@ int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, i
     return -1;
   }
   return launch_rc("bnn_cuda_dw3", bnnk_dw3(B, d_xp, xws, H, W, C, s, d_w, d_b, d_out, ows, Ho, Wo, d_chsum, cws,
-                                             (bnn_stream_t)stream));
+                                             op_err_word(), (bnn_stream_t)stream));
 }
 
 int bnn_cuda_fn(int fn, int n, const float *d_x, float *d_y, void *stream) {

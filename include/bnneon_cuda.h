@@ -97,10 +97,14 @@ int bnn_pw_s8_error(bnn_pw_s8 *op);
 void bnn_pw_s8_free(bnn_pw_s8 *op);
 
 /* DW3 (src/gemm_f32.c:398-411, dw3x3_f32), batched: d_xp [B][(H+2)(W+2)][C] (zero halo 1), d_w [9][C], d_b [C] ->
- * d_out [B][Ho Wo][C], d_chsum [B][C] */
+ * d_out [B][Ho Wo][C], d_chsum [B][C]. A bounded device wait that ran out is reported by bnn_cuda_op_error. */
 int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, int s, const float *d_w,
                  const float *d_b, float *d_out, long long ows, int Ho, int Wo, float *d_chsum, long long cws,
                  void *stream);
+
+/* the current device's error word of the per-op entry points (0 = no bounded device wait ran out; then reset to 0;
+ * -1 if it cannot be read); synchronous */
+int bnn_cuda_op_error(void);
 
 /* elementwise functions of the int8 path, for tests: 0 SiLU, 1 SiLU (table estimate), 2 sigmoid, 3 FRECPE,
  * 4 log2 polynomial, 5 exp2 polynomial (front end), 6 glibc expf, 7 SiLU on paired fp32 lanes (table estimate),
