@@ -67,6 +67,98 @@ def op_cost(code, p, bufs, bl):
     return 0, 0, 0
 
 
+PROFILE = os.path.join(REPO, "profiles", "launch_list_v24_int8_b256.md")
+NCU_CMD = ("ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum --clock-control none "
+           "-s {skip} -c {count} --csv --log-file gpurun_out/launches.csv python bench.py --ncu --warmup 3")
+# the kernels each op launches, in order (the runtime's op registry)
+OP_KERNELS = {1: ("k_fe_minmax", "k_fe_spec"), 2: ("k_c0pool",), 22: ("k_quant", "k_gemm_s8"),
+              23: ("k_quant", "k_gemm_s8"), 4: ("k_dw3",), 25: ("k_se_gate",), 6: ("k_postpc_im2col", "k_postpc_gemm")}
+
+
+def ncu_summary(csv_path, batch):
+    """Reads an ncu launch list (gpu__time_duration.sum + dram bytes, one step of the full package) and writes
+    PROFILE: per kernel and per op class the device time, share and DRAM traffic, plus a JSON block with the DRAM
+    bytes per op that bench runs report as roofline.traffic."""
+    import csv  # pylint: disable=import-outside-toplevel
+    from collections import OrderedDict  # pylint: disable=import-outside-toplevel
+    from bnneon_b200 import pkgread, synth  # pylint: disable=import-outside-toplevel
+    launches = OrderedDict()
+    hdr = None
+    with open(csv_path, encoding="utf-8", errors="replace") as f:
+        for r in csv.reader(f):
+            if r and r[0] == "ID":
+                hdr = r
+                continue
+            if not hdr or len(r) != len(hdr):
+                continue
+            d = dict(zip(hdr, r))
+            e = launches.setdefault(int(d["ID"]), {"name": d["Kernel Name"].split("(")[0].replace("void ", "").strip()})
+            v, u, name = float(d["Metric Value"].replace(",", "")), d["Metric Unit"], d["Metric Name"]
+            if name == "gpu__time_duration.sum":
+                e["us"] = v * {"ns": 1e-3, "nsecond": 1e-3, "us": 1.0, "usecond": 1.0, "ms": 1e3, "msecond": 1e3,
+                              "s": 1e6, "second": 1e6}[u]
+            elif name.startswith("dram__bytes"):
+                e["bytes"] = e.get("bytes", 0.0) + v * {"byte": 1, "Kbyte": 1e3, "KB": 1e3, "Mbyte": 1e6, "MB": 1e6,
+                                                         "Gbyte": 1e9, "GB": 1e9}[u]
+    lst = list(launches.values())
+    td = tempfile.mkdtemp()
+    pkg = os.path.join(td, "v24_full.bnpk")
+    synth.make_package(pkg, seed=0)
+    ops, _ = pkgread.read_ops(pkg)
+    cls, i = OrderedDict(), 0
+    for code, _, _, _ in ops:  # assign the launches to the ops in order
+        c = cls.setdefault(OPCODE_NAMES.get(code, str(code)), {"us": 0.0, "bytes": 0.0, "ops": 0, "launches": 0})
+        c["ops"] += 1
+        for kname in OP_KERNELS[code]:
+            if i >= len(lst) or not lst[i]["name"].startswith(kname):
+                raise SystemExit(f"launch {i} ({lst[i]['name'] if i < len(lst) else 'none'}) is not {kname}")
+            c["us"] += lst[i]["us"]
+            c["bytes"] += lst[i].get("bytes", 0.0)
+            c["launches"] += 1
+            i += 1
+    tot = sum(e["us"] for e in lst)
+    kern = OrderedDict()
+    for e in lst:
+        k = kern.setdefault(e["name"], [0, 0.0, 0.0])
+        k[0] += 1
+        k[1] += e["us"]
+        k[2] += e.get("bytes", 0.0)
+    out = [f"# Launch list: full v2.4 int8 package, batch {batch}, one step ({len(lst)} launches)", "",
+           "Command (GPU box, after the same command line without `ncu` exited 0):", "",
+           "    python bench.py --ncu --warmup 3 && \\",
+           "    " + NCU_CMD.format(skip=3 * len(lst), count=len(lst)), "",
+           "then `python bench.py --ncu-summary gpurun_out/launches.csv` wrote this file. Per-launch times are",
+           "serialised and cold-cache (ncu flushes caches between launches); the shares are what compare with the",
+           "bench's per-op CUDA-event times. DRAM bytes are `dram__bytes_read.sum + dram__bytes_write.sum`.", "",
+           "| kernel | launches | total µs | share | DRAM MB | GB/s |", "|---|---:|---:|---:|---:|---:|"]
+    for k, (n, us, by) in sorted(kern.items(), key=lambda kv: -kv[1][1]):
+        out.append(f"| {k} | {n} | {us:.1f} | {100 * us / tot:.1f}% | {by / 1e6:.1f} | {by / us / 1e3:.0f} |")
+    out += [f"| **total** | {len(lst)} | {tot:.1f} | | | |", "", "Per op class (the package's ops):", "",
+            "| op class | ops | launches | total µs | share | DRAM MB per op |", "|---|---:|---:|---:|---:|---:|"]
+    for k, c in sorted(cls.items(), key=lambda kv: -kv[1]["us"]):
+        out.append(f"| {k} | {c['ops']} | {c['launches']} | {c['us']:.1f} | {100 * c['us'] / tot:.1f}% | "
+                   f"{c['bytes'] / c['ops'] / 1e6:.2f} |")
+    traffic = {k: {"dram_bytes_per_op": round(c["bytes"] / c["ops"]), "ops": c["ops"]} for k, c in cls.items()}
+    out += ["", "Traffic per op, read by bench.py for roofline.traffic:", "", "```json",
+            json.dumps({"batch": batch, "traffic": traffic}), "```", ""]
+    with open(PROFILE, "w", encoding="utf-8") as f:
+        f.write("\n".join(out))
+    print(f"wrote {PROFILE}")
+
+
+def profile_traffic(cls_name, batch):
+    """DRAM bytes per op of an op class from the committed launch-list summary (None if absent or another batch)."""
+    try:
+        with open(PROFILE, encoding="utf-8") as f:
+            txt = f.read()
+        blk = json.loads(txt.split("```json", 1)[1].split("```", 1)[0])
+        if blk["batch"] != batch:
+            return None
+        return blk["traffic"][cls_name]["dram_bytes_per_op"]
+    except (OSError, IndexError, KeyError, ValueError):
+        return None
+
+
 def load_peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json"), encoding="utf-8") as f:
@@ -77,52 +169,90 @@ def load_peaks():
 
 
 class Clocks:
-    """nvidia-smi clock / throttle samples while the timed region runs."""
+    """SM clock and throttle-reason samples (NVML, every 10 ms) while the timed region runs; nvidia-smi if NVML is
+    missing. The first sample is taken before the timed region starts."""
+
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index):
-        self.index, self.rows, self.proc = index, [], None
+        self.index, self.rows, self.proc, self.nv, self.stop = index, [], None, None, threading.Event()
+
+    def _handle(self):
+        import pynvml  # pylint: disable=import-outside-toplevel
+        pynvml.nvmlInit()
+        try:
+            import torch  # pylint: disable=import-outside-toplevel
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:  # pylint: disable=broad-except
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _sample_nvml(self, nv, h):
+        while True:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((float(sm), float(mx), int(rs)))
+            except Exception:  # pylint: disable=broad-except
+                pass
+            if self.stop.wait(0.01):
+                break
 
     def __enter__(self):
+        try:
+            nv, h = self._handle()
+            self.nv = nv
+            self.th = threading.Thread(target=self._sample_nvml, args=(nv, h), daemon=True)
+            self.th.start()
+            t = time.time()
+            while not self.rows and time.time() - t < 2:
+                time.sleep(0.005)
+            return self
+        except Exception:  # pylint: disable=broad-except
+            self.nv = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
                  "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th = threading.Thread(target=self._read_smi, daemon=True)
             self.th.start()
+            t = time.time()
+            while not self.rows and time.time() - t < 3:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
         return self
 
-    def _read(self):
+    def _read_smi(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+            r = [x.strip() for x in line.split(",")]
+            try:
+                mask = sum(self.REASONS[n] for i, n in enumerate(names) if r[4 + i].lower().startswith("active"))
+                self.rows.append((float(r[0]), float(r[1]), mask))
+            except (ValueError, IndexError):
+                continue
 
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if getattr(self, "th", None):
             self.th.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            try:
-                sm.append(float(r[0]))
-                mx = float(r[1])
-                for i, n in enumerate(names):
-                    if r[4 + i].lower().startswith("active"):
-                        reasons.add(n)
-            except (ValueError, IndexError):
-                continue
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = [r[0] for r in self.rows]
+        reasons = sorted({n for r in self.rows for n, bit in self.REASONS.items() if r[2] & bit})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": self.rows[-1][1] if self.rows else None,
+                "reasons": reasons, "samples": len(sm), "source": "nvml" if self.nv else "nvidia-smi"}
 
 
 def cpu_baseline(pkg, pcm, seconds=12.0):
@@ -182,10 +312,15 @@ def main():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-summary", metavar="CSV",
+                    help="write profiles/launch_list_v24_int8_b256.md from an ncu launch-list CSV (no GPU needed)")
     ap.add_argument("--ncu", action="store_true",
                     help="for profiler captures: warm-up steps + one step through bnn_infer_device, no timing, no JSON")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.ncu_summary:
+        ncu_summary(args.ncu_summary, args.batch)
+        return
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -242,12 +377,12 @@ def main():
     barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local) as clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            m.infer_device(B, d_pcm.data_ptr(), d_out.data_ptr(), d_emb.data_ptr(), sp)
-        ev1.record(stream)
-        ev1.synchronize()
+    clk = Clocks(local).__enter__()  # sampled through both timed regions (device-resident and end to end)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        m.infer_device(B, d_pcm.data_ptr(), d_out.data_ptr(), d_emb.data_ptr(), sp)
+    ev1.record(stream)
+    ev1.synchronize()
     torch.cuda.synchronize()
     barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
@@ -270,6 +405,7 @@ def main():
     e1.record()
     e1.synchronize()
     wall = (time.perf_counter() - t0) * 1e3 / args.steps
+    clk.__exit__(None, None, None)
     e2e_ms = max_over_ranks(max(e0.elapsed_time(e1) / args.steps, wall))
     e2e = {"value": round(world * B / (e2e_ms / 1e3), 3), "unit": UNIT, "h2d_bytes_per_step": B * 144000 * 4,
            "d2h_bytes_per_step": B * (nc + ne) * 4, "ms_per_step": round(e2e_ms, 3),
@@ -299,10 +435,13 @@ def main():
     s8_ms = cls.get("pw_s8n", {"ms": 0})["ms"] + cls.get("gemv_s8n", {"ms": 0})["ms"]
     s8_macs = cls.get("pw_s8n", {"macs": 0})["macs"] + cls.get("gemv_s8n", {"macs": 0})["macs"]
     roofline = {"bound": "hbm", "kernel": f"{top} ({cls[top]['ops']} ops per step)", "achieved": round(ach, 1),
-                "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "traffic": None,
+                "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "traffic": profile_traffic(top, B),
+                "algorithmic_bytes_per_op": round(cls[top]["bytes"] / cls[top]["ops"]),
                 "peak_source": peak_src,
-                "note": "achieved = algorithmic bytes of the op class per step / its CUDA-event time; traffic from "
-                        "ncu is in profiles/"}
+                "note": "achieved = algorithmic bytes of the op class per step / its CUDA-event time (the per-op "
+                        "average); traffic = ncu DRAM bytes per op of the same class at the same batch "
+                        "(profiles/launch_list_v24_int8_b256.md)"}
     ops_summary = {k: {"ms": round(v["ms"], 4), "share": round(v["ms"] / sum(x["ms"] for x in cls.values()), 4),
                        "GB/s": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1) if v["ms"] else None, "ops": v["ops"]}
                    for k, v in sorted(cls.items(), key=lambda kv: -kv[1]["ms"])}

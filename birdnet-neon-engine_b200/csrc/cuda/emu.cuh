@@ -133,6 +133,11 @@ __device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)));
   return up2(d);
 }
+__device__ __forceinline__ float2 sub2_rn(float2 a, float2 b) {
+  unsigned long long d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)));
+  return up2(d);
+}
 __device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
   unsigned long long d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)), "l"(pk2(c)));
