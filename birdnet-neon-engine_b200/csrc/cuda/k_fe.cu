@@ -69,8 +69,19 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
   const float *__restrict__ twi = t.tw_im[BR];
   const int nfr = min(kFG, kNfr - t0);
   const int start = t0 * HOP, len = (nfr - 1) * HOP + 2 * M;
-  for (int i = tid; i < len; i += 256)
-    seg[i] = __fmul_rn(__fsub_rn(__fdiv_rn(__fsub_rn(x[start + i], mn), den), 0.5f), 2.f);
+  for (int i0 = 0; i0 < len; i0 += 256 * 8) {  // 8 loads in flight per thread before the divisions
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = i0 + u * 256 + tid;
+      v[u] = i < len ? __ldg(x + start + i) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = i0 + u * 256 + tid;
+      if (i < len) seg[i] = __fmul_rn(__fsub_rn(__fdiv_rn(__fsub_rn(v[u], mn), den), 0.5f), 2.f);
+    }
+  }
   const int klo = t.klo[BR], nk = t.khi[BR] - klo;
   __syncthreads();
   for (int f0 = 0; f0 < nfr; f0 += FF) {
