@@ -164,16 +164,17 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
     }
     __syncthreads();
     // real part of X_k for the bins the filters use: 1/2 [(Zr_k + Zr_{M-k}) + c (Zi_k + Zi_{M-k}) - s (Zr_k - Zr_{M-k})]
-    for (int i = tid; i < FF * nk; i += 256) {
-      const int ff = i / nk, k = klo + (i - ff * nk);
-      if (f0 + ff >= nfr) continue;
-      const int k1 = k == M ? 0 : k, k2 = k == 0 ? 0 : M - k;  // Z_M = Z_0 (the reference reads past its buffer)
+    for (int ff = 0; ff < FF && f0 + ff < nfr; ff++) {
       const float *gr = re + ff * MP, *gi = im + ff * MP;
-      const float zr = gr[sx(k1)], zi = gi[sx(k1)], yr = gr[sx(k2)], yi = gi[sx(k2)];
-      float v = __fadd_rn(zr, yr);
-      v = __fmaf_rn(__fadd_rn(zi, yi), t.pc[BR][k], v);
-      v = __fmaf_rn(-__fsub_rn(zr, yr), t.ps[BR][k], v);
-      R[ff * nk + (k - klo)] = __fmul_rn(v, 0.5f);
+      for (int kk = tid; kk < nk; kk += 256) {
+        const int k = klo + kk;
+        const int k1 = k == M ? 0 : k, k2 = k == 0 ? 0 : M - k;  // Z_M = Z_0 (the reference reads past its buffer)
+        const float zr = gr[sx(k1)], zi = gi[sx(k1)], yr = gr[sx(k2)], yi = gi[sx(k2)];
+        float v = __fadd_rn(zr, yr);
+        v = __fmaf_rn(__fadd_rn(zi, yi), t.pc[BR][k], v);
+        v = __fmaf_rn(-__fsub_rn(zr, yr), t.ps[BR][k], v);
+        R[ff * nk + kk] = __fmul_rn(v, 0.5f);
+      }
     }
     __syncthreads();
     const int *__restrict__ moff = t.mel_off[BR];
@@ -183,15 +184,28 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
     for (int i = tid; i < FF * kNmel; i += 256) {
       const int ff = i / kNmel, j = i - ff * kNmel, fi2 = f0 + ff;
       if (fi2 >= nfr) continue;
-      const float *Rf = R + ff * nk - klo;
+      // a filter's taps are the consecutive bins lo .. lo + n - 1 (its nonzero range), so only the weights are
+      // loaded per tap
+      const int e0 = moff[j], n = moff[j + 1] - e0;
+      const float *Rf = R + ff * nk - klo + (n > 0 ? mk[e0] : klo);
+      const float *wf = mw + e0;
       float a0 = 0.f, a1 = 0.f;
-      int e = moff[j];
-      const int e1 = moff[j + 1];
-      for (; e + 2 <= e1; e += 2) {
-        a0 = __fmaf_rn(Rf[mk[e]], mw[e], a0);
-        a1 = __fmaf_rn(Rf[mk[e + 1]], mw[e + 1], a1);
+      int e = 0;
+      for (; e + 8 <= n; e += 8) {
+        float wv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) wv[u] = __ldg(wf + e + u);
+#pragma unroll
+        for (int u = 0; u < 8; u += 2) {
+          a0 = __fmaf_rn(Rf[e + u], wv[u], a0);
+          a1 = __fmaf_rn(Rf[e + u + 1], wv[u + 1], a1);
+        }
       }
-      if (e < e1) a0 = __fmaf_rn(Rf[mk[e]], mw[e], a0);
+      for (; e + 2 <= n; e += 2) {
+        a0 = __fmaf_rn(Rf[e], __ldg(wf + e), a0);
+        a1 = __fmaf_rn(Rf[e + 1], __ldg(wf + e + 1), a1);
+      }
+      if (e < n) a0 = __fmaf_rn(Rf[e], __ldg(wf + e), a0);
       const float m = fmax_nan(fabsf(__fadd_rn(a0, a1)), 1e-30f);
       const float p = exp2_acc(__fmul_rn(pw2, log2_acc(m)));
       img[((long long)(kNmel - 1 - j) * kNfr + t0 + fi2) * 2 + BR] = __fmaf_rn(p, bs, bb);
