@@ -110,8 +110,8 @@ def ncu_summary(csv_path, batch):
         c = cls.setdefault(OPCODE_NAMES.get(code, str(code)), {"us": 0.0, "bytes": 0.0, "ops": 0, "launches": 0})
         c["ops"] += 1
         for kname in OP_KERNELS[code]:
-            if code == 25 and (i >= len(lst) or not lst[i]["name"].startswith(kname)):
-                break  # an SE gate computed inside the DW3 launch before it
+            if (code == 25 or kname == "k_quant") and (i >= len(lst) or not lst[i]["name"].startswith(kname)):
+                continue  # work done inside the launch of the op before (a fused SE gate or quantizer)
             if i >= len(lst) or not lst[i]["name"].startswith(kname):
                 raise SystemExit(f"launch {i} ({lst[i]['name'] if i < len(lst) else 'none'}) is not {kname}")
             c["us"] += lst[i]["us"]

@@ -75,10 +75,19 @@ int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int C, int s, 
 int bnnk_se_gate(int B, int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,
                  const float *chsum, long long cws, int P, float *gate, long long gws, bnn_stream_t st);
 
+/* a producer kernel's quantization of its output rows for the PW_S8 that reads them next (s8n_quant_rows): q
+ * [rows][kq], sa, za; keep = 0: the fp32 rows are not written (no other op reads them) */
+typedef struct {
+  int8_t *q;
+  float *sa;
+  int32_t *za;
+  int kq, keep;
+} bnnk_qrows;
+
 /* ---- c0 conv 4x8 s2 + ReLU + max|avg pool (C0POOL): img [B][96][511][2] -> pin [B][6144][48];
- * wt: the weights k-major [64][24], b [24] */
+ * wt: the weights k-major [64][24], b [24]; qr (or NULL): the rows quantized for the next op too */
 int bnnk_c0pool(int B, const float *img, long long iws, const float *wt, const float *b, float *pin, long long pws,
-                bnn_stream_t st);
+                const bnnk_qrows *qr, bnn_stream_t st);
 
 /* ---- post BN + ReLU + pc 3x3 conv + ReLU + mean (POSTPC): X [B][24][192] -> feat [B][1024];
  * wt: pc weights k-major [1728][1024]; pcin: scratch [B][6][1728] */

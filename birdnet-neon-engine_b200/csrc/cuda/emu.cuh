@@ -51,6 +51,35 @@ __device__ __forceinline__ int32_t lrintf_i32(float x) {
   return (int32_t)(uint32_t)(unsigned long long)r;
 }
 
+// s8n_quant_rows' per-row parameters (gemm_s8n.c:15-63) from the row's min lo and max hi: a constant row (range
+// not above 1e-30 of its magnitude) is quantized symmetrically (zero point 0), else asymmetrically into [-127, 127]
+__device__ __forceinline__ void quant_params(float lo, float hi, float &inv, int32_t &z, float &s) {
+  const float d = __fsub_rn(hi, lo);
+  if (!(d > __fmul_rn(1e-30f, fmaxf(fabsf(hi), fabsf(lo)))) || !(d > 0.f)) {
+    const float a = fmaxf(fabsf(hi), 1e-30f);
+    inv = __fdiv_rn(127.f, a);
+    z = 0;
+    s = __fdiv_rn(a, 127.f);
+  } else {
+    inv = __fdiv_rn(254.f, d);
+    z = (int32_t)(0u - 127u - (uint32_t)lrintf_i32(__fmul_rn(lo, inv)));
+    s = __fdiv_rn(d, 254.f);
+  }
+}
+// four quantized values packed little-endian: clamp(round(t) + z, -127, 127); the 8-wide part rounds with FCVTNS,
+// the tail (columns past the last multiple of 8) with lrintf
+__device__ __forceinline__ uint32_t quant_word(float t0, float t1, float t2, float t3, int32_t z, bool eight_wide) {
+  int32_t qi[4];
+  if (eight_wide) {
+    qi[0] = cvtns(t0); qi[1] = cvtns(t1); qi[2] = cvtns(t2); qi[3] = cvtns(t3);
+  } else {
+    qi[0] = lrintf_i32(t0); qi[1] = lrintf_i32(t1); qi[2] = lrintf_i32(t2); qi[3] = lrintf_i32(t3);
+  }
+#pragma unroll
+  for (int t = 0; t < 4; t++) qi[t] = min(max((int32_t)((uint32_t)qi[t] + (uint32_t)z), -127), 127);
+  return __byte_perm(__byte_perm(qi[0], qi[1], 0x0040), __byte_perm(qi[2], qi[3], 0x0040), 0x5410);
+}
+
 // RecipEstimate of the Arm ARM for a in [256, 512): ((2^19 / (2a + 1)) + 1) / 2
 __device__ __forceinline__ uint32_t recip_estimate(uint32_t a) {
   uint32_t b = (1u << 19) / (2u * a + 1u);

@@ -314,8 +314,13 @@ __global__ void __launch_bounds__(kSeThreads) k_se_gate(int C, int rd, const flo
 // channels each, K = 64 fused multiply-adds in (ky, kx, ci) order from 0, bias added after, ReLU, max | average.
 // The 4 padded input rows sit in shared memory transposed by 8-float phase (float 8i + r at [r][i]) so that the 32
 // threads of a warp, whose patches start 8 floats apart, read consecutive words.
+// kQ: also quantize each output row (48 channels, s8n_quant_rows) for the PW_S8 that reads it: q [rows][kq] (pads =
+// zero point), sa, za; wpin = 0 leaves the fp32 output unwritten (no other op reads it)
+template <bool kQ>
 __global__ void __launch_bounds__(128) k_c0pool(const float *__restrict__ img, long long iws, const float *__restrict__ wt,
-                                                const float *__restrict__ bias, float *__restrict__ pin, long long pws) {
+                                                const float *__restrict__ bias, float *__restrict__ pin, long long pws,
+                                                int8_t *__restrict__ q, float *__restrict__ qsa,
+                                                int32_t *__restrict__ qza, int kq, int wpin) {
   constexpr int PWD = 518, RF = PWD * 2, NI = (RF + 7) / 8 + 1;  // padded width: 3 + 511 + 4 pixels
   __shared__ float rows[4][8][NI];
   __shared__ __align__(16) float ws[64][24];
@@ -354,19 +359,39 @@ __global__ void __launch_bounds__(128) k_c0pool(const float *__restrict__ img, l
     }
   }
   float *o = pin + win * pws + ((long long)oy * 128 + qx) * 48;
+  float y[48];  // [0, 24): max pool, [24, 48): average pool
 #pragma unroll
-  for (int n4 = 0; n4 < 6; n4++) {
-    float mx[4], av[4];
+  for (int n = 0; n < 24; n++) {
+    const float c0v = (n & 1) ? acc0[n >> 1].y : acc0[n >> 1].x, c1v = (n & 1) ? acc1[n >> 1].y : acc1[n >> 1].x;
+    const float u = fmax_nan(__fadd_rn(c0v, bs[n]), 0.f), v = fmax_nan(__fadd_rn(c1v, bs[n]), 0.f);
+    y[n] = fmax_nan(u, v);
+    y[24 + n] = __fmul_rn(__fadd_rn(u, v), 0.5f);
+  }
+  if (!kQ || wpin) {
 #pragma unroll
-    for (int l = 0; l < 4; l++) {
-      const int n = 4 * n4 + l;
-      const float c0v = (l & 1) ? acc0[n >> 1].y : acc0[n >> 1].x, c1v = (l & 1) ? acc1[n >> 1].y : acc1[n >> 1].x;
-      const float u = fmax_nan(__fadd_rn(c0v, bs[n]), 0.f), v = fmax_nan(__fadd_rn(c1v, bs[n]), 0.f);
-      mx[l] = fmax_nan(u, v);
-      av[l] = __fmul_rn(__fadd_rn(u, v), 0.5f);
-    }
-    *reinterpret_cast<float4 *>(o + 4 * n4) = make_float4(mx[0], mx[1], mx[2], mx[3]);
-    *reinterpret_cast<float4 *>(o + 24 + 4 * n4) = make_float4(av[0], av[1], av[2], av[3]);
+    for (int i = 0; i < 48; i += 4) *reinterpret_cast<float4 *>(o + i) = make_float4(y[i], y[i + 1], y[i + 2], y[i + 3]);
+  }
+  if (kQ) {
+    float lo = __int_as_float(0x7f800000), hi = __int_as_float(0xff800000);
+#pragma unroll
+    for (int i = 0; i < 48; i++) { lo = fmin_nan(lo, y[i]); hi = fmax_nan(hi, y[i]); }  // 48 = the 4-wide part
+    float inv, s;
+    int32_t z;
+    quant_params(lo, hi, inv, z, s);
+    const long long row = (long long)win * 6144 + oy * 128 + qx;
+    qsa[row] = s;
+    qza[row] = z;
+    uint32_t wd[12];
+#pragma unroll
+    for (int i = 0; i < 12; i++)  // 48 columns: all in the 8-wide part
+      wd[i] = quant_word(__fmul_rn(y[4 * i], inv), __fmul_rn(y[4 * i + 1], inv), __fmul_rn(y[4 * i + 2], inv),
+                         __fmul_rn(y[4 * i + 3], inv), z, true);
+    uint4 *qr = reinterpret_cast<uint4 *>(q + row * kq);
+    const uint32_t zp = ((uint32_t)z & 0xffu) * 0x01010101u;
+    qr[0] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    qr[1] = make_uint4(wd[4], wd[5], wd[6], wd[7]);
+    qr[2] = make_uint4(wd[8], wd[9], wd[10], wd[11]);
+    for (int i = 3; i < kq / 16; i++) qr[i] = make_uint4(zp, zp, zp, zp);
   }
 }
 
@@ -574,9 +599,12 @@ extern "C" int bnnk_se_gate(int B, int C, int rd, const float *w1, const float *
 }
 
 extern "C" int bnnk_c0pool(int B, const float *img, long long iws, const float *wt, const float *b, float *pin,
-                           long long pws, bnn_stream_t st) {
+                           long long pws, const bnnk_qrows *qr, bnn_stream_t st) {
   if (B <= 0) return 0;
-  k_c0pool<<<dim3(48, B), 128, 0, st>>>(img, iws, wt, b, pin, pws);
+  if (qr && qr->kq >= 48 && qr->kq % 16 == 0)
+    k_c0pool<true><<<dim3(48, B), 128, 0, st>>>(img, iws, wt, b, pin, pws, qr->q, qr->sa, qr->za, qr->kq, qr->keep);
+  else
+    k_c0pool<false><<<dim3(48, B), 128, 0, st>>>(img, iws, wt, b, pin, pws, nullptr, nullptr, nullptr, 0, 1);
   return cudaGetLastError();
 }
 

@@ -80,15 +80,7 @@ __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__
   }
   float inv, s;
   int32_t z;
-  const float d = __fsub_rn(hi, lo);
-  if (!(d > __fmul_rn(1e-30f, fmaxf(fabsf(hi), fabsf(lo)))) || !(d > 0.f)) {  // constant row: symmetric
-    float a = fmaxf(fabsf(hi), 1e-30f);
-    inv = __fdiv_rn(127.f, a); z = 0; s = __fdiv_rn(a, 127.f);
-  } else {
-    inv = __fdiv_rn(254.f, d);
-    z = (int32_t)(0u - 127u - (uint32_t)lrintf_i32(__fmul_rn(lo, inv)));
-    s = __fdiv_rn(d, 254.f);
-  }
+  quant_params(lo, hi, inv, z, s);
   if (!valid) return;
   if (lane == 0) { sa[row] = s; za[row] = z; }
   const int K8 = K & ~7;
@@ -106,15 +98,7 @@ __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__
       if (g < K4) {
         const float2 p0 = mul2_rn(make_float2(v[i][e].x, v[i][e].y), inv2);
         const float2 p1 = mul2_rn(make_float2(v[i][e].z, v[i][e].w), inv2);
-        int32_t qi[4];
-        if (4 * g < K8) {  // the 8-wide part: FCVTNS
-          qi[0] = cvtns(p0.x); qi[1] = cvtns(p0.y); qi[2] = cvtns(p1.x); qi[3] = cvtns(p1.y);
-        } else {           // the tail: lrintf
-          qi[0] = lrintf_i32(p0.x); qi[1] = lrintf_i32(p0.y); qi[2] = lrintf_i32(p1.x); qi[3] = lrintf_i32(p1.y);
-        }
-#pragma unroll
-        for (int t = 0; t < 4; t++) qi[t] = min(max((int32_t)((uint32_t)qi[t] + (uint32_t)z), -127), 127);
-        wd[e] = __byte_perm(__byte_perm(qi[0], qi[1], 0x0040), __byte_perm(qi[2], qi[3], 0x0040), 0x5410);
+        wd[e] = quant_word(p0.x, p0.y, p1.x, p1.y, z, 4 * g < K8);
       } else {
         wd[e] = zp;
       }
@@ -139,15 +123,7 @@ __global__ void k_quant_scalar(int rows, int Mw, const float *__restrict__ x, lo
   for (; k < K; k++) { lo = fminf(lo, val(k)); hi = fmaxf(hi, val(k)); }                // the scalar tail
   float inv, s;
   int32_t z;
-  const float d = __fsub_rn(hi, lo);
-  if (!(d > __fmul_rn(1e-30f, fmaxf(fabsf(hi), fabsf(lo)))) || !(d > 0.f)) {
-    float a = fmaxf(fabsf(hi), 1e-30f);
-    inv = __fdiv_rn(127.f, a); z = 0; s = __fdiv_rn(a, 127.f);
-  } else {
-    inv = __fdiv_rn(254.f, d);
-    z = (int32_t)(0u - 127u - (uint32_t)lrintf_i32(__fmul_rn(lo, inv)));
-    s = __fdiv_rn(d, 254.f);
-  }
+  quant_params(lo, hi, inv, z, s);
   sa[row] = s;
   za[row] = z;
   int8_t *qr = q + (long long)row * Kq;

@@ -123,6 +123,7 @@ int bnn_rt_device(bnn_ctx *c, int i, char *err, size_t errlen, int *kind);
 void bnn_rt_device_free(bnn_ctx *c, int i);
 /* n <= batch windows on device i: pcm at d_pcm (window stride n_samples); outputs stay in the arena */
 int bnn_rt_launch(bnn_ctx *c, int i, int n, const float *d_pcm, int op0, int op1, void *stream);
+int c0_quantizes_next(const bnn_ctx *c, int i);
 void bnn_rt_close(bnn_ctx *c);
 int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src, const float *sw_src,
                    const int32_t *cs_src, const float *b_src, char *err, size_t errlen, int *kind);

@@ -397,6 +397,8 @@ int bnn_rt_open(bnn_ctx *c, char *err, size_t errlen, int *kind) {
     c->launches += k->launches;
     q += h[1];
   }
+  for (int i = 0; i + 1 < c->n_ops; i++)  /* quantizers done by the launch before */
+    if (c0_quantizes_next(c, i)) c->launches -= 1;
   return 0;
 }
 
@@ -742,6 +744,24 @@ void bnn_rt_device_free(bnn_ctx *c, int di) {
 #define B_(a) (op->b[a] < 0 ? NULL : dv->buf[op->b[a]])
 #define WS(a) (op->b[a] < 0 ? 0 : dv->ws[op->b[a]])
 
+/* op i is a C0POOL whose output rows the ungated PW_S8 op i + 1 quantizes (K = 48): the C0POOL launch quantizes
+ * them itself */
+int c0_quantizes_next(const bnn_ctx *c, int i) {
+  if (i + 1 >= c->n_ops) return 0;
+  const bnn_op *a = &c->ops[i], *b = &c->ops[i + 1];
+  return a->code == BNN_OP_C0POOL && b->code == BNN_OP_PW_S8 && a->nb > 1 && a->b[1] >= 0 && b->b[0] == a->b[1] &&
+         !(b->nb == 7 && b->b[6] >= 0) && b->p[1] == 48 && b->p[5] == 48 && b->p[4] == 6144;
+}
+
+/* buffer buf is an argument of some op other than i and j */
+static int used_elsewhere(const bnn_ctx *c, int buf, int i, int j) {
+  for (int k = 0; k < c->n_ops; k++)
+    if (k != i && k != j)
+      for (int a = 0; a < c->ops[k].nb; a++)
+        if (c->ops[k].b[a] == buf) return 1;
+  return 0;
+}
+
 int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op1, void *stream) {
   bnn_dev *dv = c->dev[di];
   bnn_stream_t st = (bnn_stream_t)stream;
@@ -750,11 +770,12 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
     dv->prof_op0 = op0;
     dv->prof_op1 = op1 < c->n_ops ? op1 : c->n_ops;
   }
+  int pre_q = 0;  /* this op's input rows were quantized by the launch of the op before */
   for (int i = op0; i < op1 && i < c->n_ops; i++) {
     const bnn_op *op = &c->ops[i];
     const bnn_devop *o = &dv->ops[i];
     const int *p = op->p;
-    int rc = 0;
+    int rc = 0, next_q = 0;
     if (dv->prof_on) cudaEventRecord((cudaEvent_t)dv->events[2 * i], (cudaStream_t)st);
 #define IN_(a) ((uint32_t)op->b[a] == in ? (const float *)d_pcm : (const float *)B_(a))
 #define INWS(a) ((uint32_t)op->b[a] == in ? (long long)c->bufd[in].elems : WS(a))
@@ -762,13 +783,21 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
     case BNN_OP_FE_STFT2:
       rc = bnnk_fe_stft2(n, IN_(0), INWS(0), &dv->fe, dv->fe_minmax, B_(1), WS(1), st);
       break;
-    case BNN_OP_C0POOL:
-      rc = bnnk_c0pool(n, IN_(0), INWS(0), o->f[0], o->f[1], B_(1), WS(1), st);
+    case BNN_OP_C0POOL: {
+      bnnk_qrows qr = {dv->q, dv->sa, dv->za, 0, 1};
+      if (i + 1 < op1 && c0_quantizes_next(c, i)) {
+        qr.kq = dv->ops[i + 1].kq;
+        qr.keep = used_elsewhere(c, op->b[1], i, i + 1);
+        next_q = 1;
+      }
+      rc = bnnk_c0pool(n, IN_(0), INWS(0), o->f[0], o->f[1], B_(1), WS(1), next_q ? &qr : NULL, st);
       break;
+    }
     case BNN_OP_PW_S8: {
       const int M = p[4];
       const float *gate = op->nb == 7 && op->b[6] >= 0 ? B_(6) : NULL;
-      rc = bnnk_quant(n * M, M, IN_(0), INWS(0), p[5], p[1], o->kq, gate, gate ? WS(6) : 0, dv->q, dv->sa, dv->za, st);
+      if (!pre_q)
+        rc = bnnk_quant(n * M, M, IN_(0), INWS(0), p[5], p[1], o->kq, gate, gate ? WS(6) : 0, dv->q, dv->sa, dv->za, st);
       if (!rc) {
         const bnn_buf_rec *r = op->b[2] >= 0 ? &c->bufd[op->b[2]] : NULL;
         bnnk_epilogue e = {p[6], B_(1), WS(1), p[7], p[8], p[9], B_(2), WS(2), p[10],
@@ -806,6 +835,7 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
                     "the GPU (nvidia-smi) and retry", i, op->kname, rc, cudaGetErrorString((cudaError_t)rc));
       return -1;
     }
+    pre_q = next_q;
   }
   return 0;
 }
