@@ -609,10 +609,12 @@ extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_
 
 template <int SW, bool kSP>
 static int launch_gemm(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k_gemm_s8<SW, kSP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-    attr = true;
+  static size_t attr = 0;  // the dynamic shared memory this instantiation may use so far (static + dynamic <= 227 KB)
+  if (p->smem > attr) {
+    const cudaError_t e = cudaFuncSetAttribute(k_gemm_s8<SW, kSP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)p->smem);
+    if (e) return e;
+    attr = p->smem;
   }
   if (!g_num_sms) {
     int dev = 0;
