@@ -609,12 +609,16 @@ extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_
 
 template <int SW, bool kSP>
 static int launch_gemm(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
-  static size_t attr = 0;  // the dynamic shared memory this instantiation may use so far (static + dynamic <= 227 KB)
-  if (p->smem > attr) {
+  // the dynamic shared memory this instantiation may use so far, per device (function attributes are per context;
+  // static + dynamic <= 227 KB)
+  static size_t attr[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (p->smem > attr[dev]) {
     const cudaError_t e = cudaFuncSetAttribute(k_gemm_s8<SW, kSP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                (int)p->smem);
     if (e) return e;
-    attr = p->smem;
+    attr[dev] = p->smem;
   }
   if (!g_num_sms) {
     int dev = 0;
