@@ -96,7 +96,8 @@ int bnnk_postpc(int B, const float *X, long long xws, const float *post_s, const
 
 /* ---- the v2.4 front end (FE_STFT2): pcm [B][144000] -> img [B][96][511][2] */
 typedef struct {
-  const float *win[2];        /* [N] */
+  const float *win[2];        /* [M][2]: the window pairs (w[2n], w[2n+1]) in gather order: entry e * (M / 16) + l
+                               * holds bit-reversed position p = 16 l + e, n = rev(p) */
   const float *tw_re[2], *tw_im[2]; /* [M / 2] */
   const float *pc[2], *ps[2]; /* [khi] */
   const int *rev[2];          /* [M] */

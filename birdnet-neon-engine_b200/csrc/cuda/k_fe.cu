@@ -24,6 +24,9 @@ namespace bnn {
 constexpr int kNsamp = 144000, kNfr = 511, kNmel = 96, kFG = 8;
 
 __device__ __forceinline__ int sx(int p) { return p + (p >> 4); }
+// the sample segment's padded index (one word per 32): the bit-reversed gathers, 4 words apart across a warp, then
+// fall in distinct banks
+__device__ __forceinline__ int sg(int i) { return i + (i >> 5); }
 
 struct cpx {
   float r, i;
@@ -61,7 +64,7 @@ template <int LG>
 __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, float den, const bnnk_fe_tables &t,
                                      float *__restrict__ img, int t0, float *sm) {
   constexpr int M = 1 << LG, BR = LG == 10 ? 0 : 1, HOP = BR ? 280 : 278, TPF = M / 16, FF = 256 / TPF;
-  constexpr int SEG = (kFG - 1) * HOP + 2 * M, MP = M + M / 16;
+  constexpr int SEG = ((kFG - 1) * HOP + 2 * M) * 33 / 32 + 1, MP = M + M / 16;
   float *seg = sm, *re = sm + SEG, *im = re + FF * MP, *R = im + FF * MP;
   const int tid = threadIdx.x, fl = tid / TPF, lt = tid % TPF;
   const float *__restrict__ win = t.win[BR];
@@ -79,7 +82,7 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
 #pragma unroll
     for (int u = 0; u < 8; u++) {
       const int i = i0 + u * 256 + tid;
-      if (i < len) seg[i] = __fmul_rn(__fsub_rn(__fdiv_rn(__fsub_rn(v[u], mn), den), 0.5f), 2.f);
+      if (i < len) seg[sg(i)] = __fmul_rn(__fsub_rn(__fdiv_rn(__fsub_rn(v[u], mn), den), 0.5f), 2.f);
     }
   }
   const int klo = t.klo[BR], nk = t.khi[BR] - klo;
@@ -95,7 +98,8 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
 #pragma unroll
       for (int e = 0; e < 16; e++) {
         const int n = (int)(__brev((unsigned)(16 * lt + e)) >> (32 - LG));
-        z[e] = {__fmul_rn(seg[st + 2 * n], win[2 * n]), __fmul_rn(seg[st + 2 * n + 1], win[2 * n + 1])};
+        const float2 w = reinterpret_cast<const float2 *>(win)[e * TPF + lt];  // (w[2n], w[2n+1]), lanes adjacent
+        z[e] = {__fmul_rn(seg[sg(st + 2 * n)], w.x), __fmul_rn(seg[sg(st + 2 * n + 1)], w.y)};
       }
 #pragma unroll
       for (int g = 0; g < 4; g++) r4first(z[4 * g], z[4 * g + 1], z[4 * g + 2], z[4 * g + 3]);
@@ -258,7 +262,8 @@ extern "C" int bnnk_fe_stft2(int B, const float *pcm, long long pws, const bnnk_
   // shared memory: the larger of the two spectrograms' layouts
   auto need = [&](int lg, int br) {
     const int M = 1 << lg, hop = br ? 280 : 278, tpf = M / 16, ff = 256 / tpf;
-    return sizeof(float) * (size_t)((kFG - 1) * hop + 2 * M + 2 * ff * (M + M / 16) + ff * (t->khi[br] - t->klo[br]));
+    return sizeof(float) * (size_t)(((kFG - 1) * hop + 2 * M) * 33 / 32 + 1 + 2 * ff * (M + M / 16) +
+                                    ff * (t->khi[br] - t->klo[br]));
   };
   const size_t smem = need(10, 0) > need(9, 1) ? need(10, 0) : need(9, 1);
   static size_t attr[64];  // per device: function attributes are per context

@@ -505,7 +505,22 @@ static int fe_tables(bnn_ctx *c, bnn_dev *dv, const bnn_op *op, char *err, size_
       rc = upload(&d, (src), (bytes), err, errlen, kind);         \
       if (!rc) { t->field[br] = d; dv->fe_mem[dv->n_fe_mem++] = d; } \
     }
-    UP(win, win, sizeof(float) * N);
+    /* the window in the gather order of the spectrogram kernel: thread l of a frame reads bit-reversed positions
+     * 16 l .. 16 l + 15, its e-th pair stored at e * (M / 16) + l */
+    float *wg = malloc(sizeof(float) * N);
+    if (!wg) {
+      free(twr); free(twi); free(pcv); free(psv); free(rev); free(off); free(mk); free(mw);
+      *kind = BNN_ERR_OOM;
+      snprintf(err, errlen, "out of memory (front-end tables)");
+      return -1;
+    }
+    for (int p = 0; p < M; p++) {
+      const int r = rev[p], e = p % 16, l = p / 16;
+      wg[2 * (e * (M / 16) + l)] = win[2 * r];
+      wg[2 * (e * (M / 16) + l) + 1] = win[2 * r + 1];
+    }
+    UP(win, wg, sizeof(float) * N);
+    free(wg);
     UP(tw_re, twr, sizeof(float) * M / 2);
     UP(tw_im, twi, sizeof(float) * M / 2);
     UP(pc, pcv, sizeof(float) * (khi + 1));
