@@ -99,6 +99,8 @@ typedef struct {
   const float *win[2];        /* [M][2]: the window pairs (w[2n], w[2n+1]) in gather order: entry e * (M / 16) + l
                                * holds bit-reversed position p = 16 l + e, n = rev(p) */
   const float *tw_re[2], *tw_im[2]; /* [M / 2] */
+  const float *tw_st[2];      /* [4 + 16 + 64 + 256][4]: per radix-2^2 stage (len 8, 32, 128, 512) and group index j,
+                               * (w1, w2) = (tw[j M / len], tw[j M / (2 len)]) as (re, im, re, im) */
   const float *pc[2], *ps[2]; /* [khi] */
   const int *rev[2];          /* [M] */
   const int *mel_off[2];      /* [97] */

@@ -70,6 +70,8 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
   const float *__restrict__ win = t.win[BR];
   const float *__restrict__ twr = t.tw_re[BR];
   const float *__restrict__ twi = t.tw_im[BR];
+  // the radix-2^2 stages' twiddle pairs (w1, w2) in the order the stages read them
+  const float4 *__restrict__ tws = reinterpret_cast<const float4 *>(t.tw_st[BR]);
   const int nfr = min(kFG, kNfr - t0);
   const int start = t0 * HOP, len = (nfr - 1) * HOP + 2 * M;
   for (int i0 = 0; i0 < len; i0 += 256 * 8) {  // 8 loads in flight per thread before the divisions
@@ -105,8 +107,10 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
       for (int g = 0; g < 4; g++) r4first(z[4 * g], z[4 * g + 1], z[4 * g + 2], z[4 * g + 3]);
 #pragma unroll
       for (int j = 0; j < 4; j++)  // len 8: h 4, st1 = M / 8, st2 = M / 16
-        r22(z[j], z[j + 4], z[j + 8], z[j + 12], twr[j * (M / 8)], twi[j * (M / 8)], twr[j * (M / 16)],
-            twi[j * (M / 16)]);
+      {
+        const float4 w = __ldg(tws + j);  // stage 0 (len 8): w1 = tw[j M / 8], w2 = tw[j M / 16]
+        r22(z[j], z[j + 4], z[j + 8], z[j + 12], w.x, w.y, w.z, w.w);
+      }
 #pragma unroll
       for (int e = 0; e < 16; e++) {
         fr[sx(16 * lt + e)] = z[e].r;
@@ -123,15 +127,16 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
 #pragma unroll
         for (int b = 0; b < 4; b++) z[a + 4 * b] = {fr[sx(base + 16 * a + 64 * b)], fi[sx(base + 16 * a + 64 * b)]};
       {  // len 32: h 16, groups (a = 0..3) for each b, twiddle index j
-        const float w1r = twr[j * (M / 32)], w1i = twi[j * (M / 32)], w2r = twr[j * (M / 64)], w2i = twi[j * (M / 64)];
+        const float4 w = __ldg(tws + 4 + j);  // stage 1 (len 32): w1 = tw[j M / 32], w2 = tw[j M / 64]
+        const float w1r = w.x, w1i = w.y, w2r = w.z, w2i = w.w;
 #pragma unroll
         for (int b = 0; b < 4; b++) r22(z[4 * b], z[4 * b + 1], z[4 * b + 2], z[4 * b + 3], w1r, w1i, w2r, w2i);
       }
 #pragma unroll
       for (int a = 0; a < 4; a++) {  // len 128: h 64, groups (b = 0..3) for each a, twiddle index j + 16 a
         const int jj = j + 16 * a;
-        r22(z[a], z[a + 4], z[a + 8], z[a + 12], twr[jj * (M / 128)], twi[jj * (M / 128)], twr[jj * (M / 256)],
-            twi[jj * (M / 256)]);
+        const float4 w = __ldg(tws + 20 + jj);  // stage 2 (len 128): w1 = tw[jj M / 128], w2 = tw[jj M / 256]
+        r22(z[a], z[a + 4], z[a + 8], z[a + 12], w.x, w.y, w.z, w.w);
       }
 #pragma unroll
       for (int a = 0; a < 4; a++)
@@ -149,7 +154,8 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
           const int jj = lt + 64 * c;
           cpx a = {fr[sx(jj)], fi[sx(jj)]}, b = {fr[sx(jj + 256)], fi[sx(jj + 256)]};
           cpx cc = {fr[sx(jj + 512)], fi[sx(jj + 512)]}, d = {fr[sx(jj + 768)], fi[sx(jj + 768)]};
-          r22(a, b, cc, d, twr[jj * 2], twi[jj * 2], twr[jj], twi[jj]);
+          const float4 w = __ldg(tws + 84 + jj);  // stage 3 (len 512): w1 = tw[2 jj], w2 = tw[jj]
+          r22(a, b, cc, d, w.x, w.y, w.z, w.w);
           fr[sx(jj)] = a.r; fi[sx(jj)] = a.i;
           fr[sx(jj + 256)] = b.r; fi[sx(jj + 256)] = b.i;
           fr[sx(jj + 512)] = cc.r; fi[sx(jj + 512)] = cc.i;

@@ -523,6 +523,20 @@ static int fe_tables(bnn_ctx *c, bnn_dev *dv, const bnn_op *op, char *err, size_
     free(wg);
     UP(tw_re, twr, sizeof(float) * M / 2);
     UP(tw_im, twi, sizeof(float) * M / 2);
+    {  /* the stage table: stages of length 8, 32, 128, 512 hold 4, 16, 64, 256 groups (the last only for M = 1024) */
+      float st[(4 + 16 + 64 + 256) * 4];
+      memset(st, 0, sizeof st);
+      static const int lens[4] = {8, 32, 128, 512}, base[4] = {0, 4, 20, 84};
+      for (int g = 0; g < 4; g++) {
+        if (2 * lens[g] > M) continue; /* a stage of length 512 only runs when M = 1024 */
+        for (int j = 0; j < lens[g] / 2; j++) {
+          const int i1 = j * (M / lens[g]), i2 = j * (M / (2 * lens[g]));
+          float *e = st + 4 * (base[g] + j);
+          e[0] = twr[i1]; e[1] = twi[i1]; e[2] = twr[i2]; e[3] = twi[i2];
+        }
+      }
+      UP(tw_st, st, sizeof st);
+    }
     UP(pc, pcv, sizeof(float) * (khi + 1));
     UP(ps, psv, sizeof(float) * (khi + 1));
     UP(rev, rev, sizeof(int) * M);
