@@ -11,8 +11,8 @@
 // shared segment. A frame of M points is owned by M/16 threads holding 16 points each in registers; the 16-point
 // sets are chosen so that two consecutive passes close over them (levels 1-4: 16 consecutive bit-reversed
 // positions; levels 5-8: the points j + 16a + 64b of a 256-block; levels 9-10: four points 256 apart), so a frame
-// makes 3 round trips through shared memory instead of one per pass. Shared indices are padded (p + p/16) so the
-// 16-strided accesses do not collide in banks.
+// makes 3 round trips through shared memory instead of one per pass. Points are stored as (re, im) pairs, their
+// shared indices padded (p + p/16) so the 16-strided accesses do not collide in banks.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -64,8 +64,10 @@ template <int LG>
 __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, float den, const bnnk_fe_tables &t,
                                      float *__restrict__ img, int t0, float *sm) {
   constexpr int M = 1 << LG, BR = LG == 10 ? 0 : 1, HOP = BR ? 280 : 278, TPF = M / 16, FF = 256 / TPF;
-  constexpr int SEG = ((kFG - 1) * HOP + 2 * M) * 33 / 32 + 1, MP = M + M / 16;
-  float *seg = sm, *re = sm + SEG, *im = re + FF * MP, *R = im + FF * MP;
+  constexpr int SEG = (((kFG - 1) * HOP + 2 * M) * 33 / 32 + 2) & ~1, MP = M + M / 16;  // SEG even: pts 8-byte aligned
+  float *seg = sm;
+  float2 *pts = reinterpret_cast<float2 *>(sm + SEG);  // [FF][MP] (re, im)
+  float *R = reinterpret_cast<float *>(pts + FF * MP);
   const int tid = threadIdx.x, fl = tid / TPF, lt = tid % TPF;
   const float *__restrict__ win = t.win[BR];
   const float *__restrict__ twr = t.tw_re[BR];
@@ -92,7 +94,7 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
   for (int f0 = 0; f0 < nfr; f0 += FF) {
     const int f = f0 + fl;  // this thread's frame within the CTA's group
     const bool live = f < nfr;
-    float *fr = re + fl * MP, *fi = im + fl * MP;
+    float2 *fp = pts + fl * MP;
     if (live) {
       // levels 1-4 on the 16 consecutive bit-reversed positions 16 lt .. 16 lt + 15
       cpx z[16];
@@ -112,10 +114,7 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
         r22(z[j], z[j + 4], z[j + 8], z[j + 12], w.x, w.y, w.z, w.w);
       }
 #pragma unroll
-      for (int e = 0; e < 16; e++) {
-        fr[sx(16 * lt + e)] = z[e].r;
-        fi[sx(16 * lt + e)] = z[e].i;
-      }
+      for (int e = 0; e < 16; e++) fp[sx(16 * lt + e)] = make_float2(z[e].r, z[e].i);
     }
     __syncthreads();
     if (live) {
@@ -125,7 +124,10 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
 #pragma unroll
       for (int a = 0; a < 4; a++)
 #pragma unroll
-        for (int b = 0; b < 4; b++) z[a + 4 * b] = {fr[sx(base + 16 * a + 64 * b)], fi[sx(base + 16 * a + 64 * b)]};
+        for (int b = 0; b < 4; b++) {
+          const float2 v = fp[sx(base + 16 * a + 64 * b)];
+          z[a + 4 * b] = {v.x, v.y};
+        }
       {  // len 32: h 16, groups (a = 0..3) for each b, twiddle index j
         const float4 w = __ldg(tws + 4 + j);  // stage 1 (len 32): w1 = tw[j M / 32], w2 = tw[j M / 64]
         const float w1r = w.x, w1i = w.y, w2r = w.z, w2i = w.w;
@@ -141,10 +143,7 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
 #pragma unroll
       for (int a = 0; a < 4; a++)
 #pragma unroll
-        for (int b = 0; b < 4; b++) {
-          fr[sx(base + 16 * a + 64 * b)] = z[a + 4 * b].r;
-          fi[sx(base + 16 * a + 64 * b)] = z[a + 4 * b].i;
-        }
+        for (int b = 0; b < 4; b++) fp[sx(base + 16 * a + 64 * b)] = make_float2(z[a + 4 * b].r, z[a + 4 * b].i);
     }
     __syncthreads();
     if (live) {
@@ -152,34 +151,35 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
 #pragma unroll
         for (int c = 0; c < 4; c++) {
           const int jj = lt + 64 * c;
-          cpx a = {fr[sx(jj)], fi[sx(jj)]}, b = {fr[sx(jj + 256)], fi[sx(jj + 256)]};
-          cpx cc = {fr[sx(jj + 512)], fi[sx(jj + 512)]}, d = {fr[sx(jj + 768)], fi[sx(jj + 768)]};
+          const float2 va = fp[sx(jj)], vb = fp[sx(jj + 256)], vc = fp[sx(jj + 512)], vd = fp[sx(jj + 768)];
+          cpx a = {va.x, va.y}, b = {vb.x, vb.y}, cc = {vc.x, vc.y}, d = {vd.x, vd.y};
           const float4 w = __ldg(tws + 84 + jj);  // stage 3 (len 512): w1 = tw[2 jj], w2 = tw[jj]
           r22(a, b, cc, d, w.x, w.y, w.z, w.w);
-          fr[sx(jj)] = a.r; fi[sx(jj)] = a.i;
-          fr[sx(jj + 256)] = b.r; fi[sx(jj + 256)] = b.i;
-          fr[sx(jj + 512)] = cc.r; fi[sx(jj + 512)] = cc.i;
-          fr[sx(jj + 768)] = d.r; fi[sx(jj + 768)] = d.i;
+          fp[sx(jj)] = make_float2(a.r, a.i);
+          fp[sx(jj + 256)] = make_float2(b.r, b.i);
+          fp[sx(jj + 512)] = make_float2(cc.r, cc.i);
+          fp[sx(jj + 768)] = make_float2(d.r, d.i);
         }
       } else {  // level 9 alone (radix 2): len 512, half 256, step 1 (fft_tab.h:64-76)
 #pragma unroll
         for (int c = 0; c < 8; c++) {
           const int jj = lt + 32 * c;
-          const cpx v = cmul({fr[sx(jj + 256)], fi[sx(jj + 256)]}, twr[jj], twi[jj]);
-          const float ur = fr[sx(jj)], ui = fi[sx(jj)];
-          fr[sx(jj)] = __fadd_rn(ur, v.r); fi[sx(jj)] = __fadd_rn(ui, v.i);
-          fr[sx(jj + 256)] = __fsub_rn(ur, v.r); fi[sx(jj + 256)] = __fsub_rn(ui, v.i);
+          const float2 hv = fp[sx(jj + 256)], uv = fp[sx(jj)];
+          const cpx v = cmul({hv.x, hv.y}, twr[jj], twi[jj]);
+          fp[sx(jj)] = make_float2(__fadd_rn(uv.x, v.r), __fadd_rn(uv.y, v.i));
+          fp[sx(jj + 256)] = make_float2(__fsub_rn(uv.x, v.r), __fsub_rn(uv.y, v.i));
         }
       }
     }
     __syncthreads();
     // real part of X_k for the bins the filters use: 1/2 [(Zr_k + Zr_{M-k}) + c (Zi_k + Zi_{M-k}) - s (Zr_k - Zr_{M-k})]
     for (int ff = 0; ff < FF && f0 + ff < nfr; ff++) {
-      const float *gr = re + ff * MP, *gi = im + ff * MP;
+      const float2 *g = pts + ff * MP;
       for (int kk = tid; kk < nk; kk += 256) {
         const int k = klo + kk;
         const int k1 = k == M ? 0 : k, k2 = k == 0 ? 0 : M - k;  // Z_M = Z_0 (the reference reads past its buffer)
-        const float zr = gr[sx(k1)], zi = gi[sx(k1)], yr = gr[sx(k2)], yi = gi[sx(k2)];
+        const float2 zv = g[sx(k1)], yv = g[sx(k2)];
+        const float zr = zv.x, zi = zv.y, yr = yv.x, yi = yv.y;
         float v = __fadd_rn(zr, yr);
         v = __fmaf_rn(__fadd_rn(zi, yi), t.pc[BR][k], v);
         v = __fmaf_rn(-__fsub_rn(zr, yr), t.ps[BR][k], v);
@@ -268,7 +268,7 @@ extern "C" int bnnk_fe_stft2(int B, const float *pcm, long long pws, const bnnk_
   // shared memory: the larger of the two spectrograms' layouts
   auto need = [&](int lg, int br) {
     const int M = 1 << lg, hop = br ? 280 : 278, tpf = M / 16, ff = 256 / tpf;
-    return sizeof(float) * (size_t)(((kFG - 1) * hop + 2 * M) * 33 / 32 + 1 + 2 * ff * (M + M / 16) +
+    return sizeof(float) * (size_t)(((((kFG - 1) * hop + 2 * M) * 33 / 32 + 2) & ~1) + 2 * ff * (M + M / 16) +
                                     ff * (t->khi[br] - t->klo[br]));
   };
   const size_t smem = need(10, 0) > need(9, 1) ? need(10, 0) : need(9, 1);
