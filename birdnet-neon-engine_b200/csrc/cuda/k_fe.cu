@@ -36,18 +36,30 @@ __device__ __forceinline__ cpx cmul(cpx x, float wr, float wi) {
   return {__fmaf_rn(-x.i, wi, __fmul_rn(x.r, wr)), __fmaf_rn(x.i, wr, __fmul_rn(x.r, wi))};
 }
 
-// one radix-2^2 butterfly group (fft_tab.h:51-62): a, b, c, d = points i+j, +h, +2h, +3h
+// one radix-2^2 butterfly group (fft_tab.h:51-62): a, b, c, d = points i+j, +h, +2h, +3h. On paired fp32 lanes:
+// x w = fma2((x_i, x_i), (-w_i, w_r), (x_r, x_r) (w_r, w_i)) gives (fma(-x_i, w_i, x_r w_r), fma(x_i, w_r, x_r w_i)),
+// each lane rounded as the scalar form; the leg b1 + (-i) u uses u' = d1 (-i w2) = -i u exactly (the negations and
+// swaps are exact), so both legs are paired sums.
+__device__ __forceinline__ float2 cmul2(float2 x, float2 w, float2 wn) {  // wn = (-w_i, w_r)
+  return fma2_rn(splat2(x.y), wn, mul2_rn(splat2(x.x), w));
+}
 __device__ __forceinline__ void r22(cpx &a, cpx &b, cpx &c, cpx &d, float w1r, float w1i, float w2r, float w2i) {
-  cpx t = cmul(b, w1r, w1i);
-  const cpx a1 = {__fadd_rn(a.r, t.r), __fadd_rn(a.i, t.i)}, b1 = {__fsub_rn(a.r, t.r), __fsub_rn(a.i, t.i)};
-  t = cmul(d, w1r, w1i);
-  const cpx c1 = {__fadd_rn(c.r, t.r), __fadd_rn(c.i, t.i)}, d1 = {__fsub_rn(c.r, t.r), __fsub_rn(c.i, t.i)};
-  t = cmul(c1, w2r, w2i);
-  a = {__fadd_rn(a1.r, t.r), __fadd_rn(a1.i, t.i)};
-  c = {__fsub_rn(a1.r, t.r), __fsub_rn(a1.i, t.i)};
-  const cpx u = cmul(d1, w2r, w2i);
-  b = {__fadd_rn(b1.r, u.i), __fsub_rn(b1.i, u.r)};  // b1 + (-i) u
-  d = {__fsub_rn(b1.r, u.i), __fadd_rn(b1.i, u.r)};
+  const float2 w1 = make_float2(w1r, w1i), w1n = make_float2(-w1i, w1r);
+  const float2 w2 = make_float2(w2r, w2i), w2n = make_float2(-w2i, w2r), w2m = make_float2(w2i, -w2r);  // -i w2
+  const float2 A = make_float2(a.r, a.i), B = make_float2(b.r, b.i), C = make_float2(c.r, c.i),
+               D = make_float2(d.r, d.i);
+  float2 t = cmul2(B, w1, w1n);
+  const float2 a1 = add2_rn(A, t), b1 = sub2_rn(A, t);
+  t = cmul2(D, w1, w1n);
+  const float2 c1 = add2_rn(C, t), d1 = sub2_rn(C, t);
+  t = cmul2(c1, w2, w2n);
+  const float2 ao = add2_rn(a1, t), co = sub2_rn(a1, t);
+  const float2 u = cmul2(d1, w2m, w2);  // -i (d1 w2): its (-w_i, w_r) is (w2r, w2i)
+  const float2 bo = add2_rn(b1, u), dd = sub2_rn(b1, u);
+  a = {ao.x, ao.y};
+  b = {bo.x, bo.y};
+  c = {co.x, co.y};
+  d = {dd.x, dd.y};
 }
 
 // the first two levels fused, without twiddles (fft_tab.h:28-38)
