@@ -161,6 +161,54 @@ def profile_traffic(cls_name, batch):
         return None
 
 
+def c1_gemm(m, torch, stream, peak_bf16):
+    """BASELINE config 1 timed: one int8 GEMM M 4096 x K 256 x N 512 on given int8 rows through
+    bnn_pw_s8_gemm, 50 launches back to back, CUDA events on their stream; fp32 outputs (the harness requant is in
+    the parity test). int8 ops = 2 M N K per launch."""
+    from bnneon_b200 import synth  # pylint: disable=import-outside-toplevel
+    Mr, K, N = 4096, 256, 512
+    a = np.random.default_rng(1).integers(-127, 128, (Mr, K)).astype(np.int8)
+    w = np.random.default_rng(2).normal(0.0, 0.02, (N, K)).astype(np.float32)
+    lw = synth._Int8Lowering([])  # pylint: disable=protected-access
+    tl, (n, k, kp, np_) = lw.s8("c1", w, np.zeros(N, np.float32))
+    wq, sw, cs, bb = [lw.tensors[t][1] for t in tl]
+    h = m.h.bnn_pw_s8_new(n, k, kp, np_, wq.ctypes.data, sw.ctypes.data, cs.ctypes.data, bb.ctypes.data, Mr)
+    if not h:
+        return None
+    try:
+        q = torch.from_numpy(a).cuda()
+        sa = torch.full((Mr,), 0.05, dtype=torch.float32, device="cuda")
+        za = torch.zeros(Mr, dtype=torch.int32, device="cuda")
+        out = torch.empty(Mr * np_, dtype=torch.float32, device="cuda")
+
+        def run():
+            return m.h.bnn_pw_s8_gemm(h, 1, Mr, q.data_ptr(), kp, sa.data_ptr(), za.data_ptr(), 0, out.data_ptr(),
+                                      Mr * np_, np_, 0, 0, None, 0, 0, 0, 0, stream.cuda_stream)
+        for _ in range(5):
+            run()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 50
+        e0.record(stream)
+        for _ in range(reps):
+            run()
+        e1.record(stream)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+    finally:
+        m.h.bnn_pw_s8_free(h)
+    ops = 2.0 * Mr * N * K
+    peak = 2.0 * peak_bf16
+    nbytes = Mr * K + N * K + 3 * 4 * N + Mr * N * 4
+    return {"shape": "M 4096 x K 256 x N 512, int8 rows given, fp32 out", "us_per_launch": round(us, 2),
+            "tops": round(ops / (us * 1e-6) / 1e12, 1), "int8_peak_tops": round(peak, 1),
+            "frac_of_int8_peak": round(ops / (us * 1e-6) / 1e12 / peak, 4),
+            "algorithmic_bytes": nbytes, "GB/s": round(nbytes / (us * 1e-6) / 1e9, 1),
+            "note": "int8 peak = 2 x the measured dense bf16 GEMM rate (MEASURED_PEAKS.json bf16_tflops; B200 runs "
+                    "dense int8 at twice bf16); the shape is HBM / latency bound (AI 112 op/B), so TOPS is far below "
+                    "the int8 ridge"}
+
+
 def load_peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json"), encoding="utf-8") as f:
@@ -448,6 +496,13 @@ def main():
                        "GB/s": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1) if v["ms"] else None, "ops": v["ops"]}
                    for k, v in sorted(cls.items(), key=lambda kv: -kv[1]["ms"])}
 
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json"), encoding="utf-8") as f:
+            bf16 = float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        bf16 = 1590.0  # the profiling recipe's fallback
+    c1 = c1_gemm(m, torch, stream, bf16) if rank == 0 else None
+
     line = None
     if rank == 0:
         clocks = clk.summary()
@@ -463,7 +518,7 @@ def main():
                             "ms_per_step": round(s8_ms, 4),
                             "note": "int8 ops of PW_S8 + GEMV_S8 (quantizer + tcgen05 GEMM) per second; these GEMMs "
                                     "are HBM-bound (AI far below the int8 ridge)"},
-                "ops": ops_summary, "clocks": clocks}
+                "ops": ops_summary, "clocks": clocks, "s8_gemm_c1": c1}
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(pkg, pcm)
     m.close()

@@ -79,6 +79,7 @@ SIGNATURES = {
     "bnn_pw_s8_new": (_P, [_I, _I, _I, _I, _P, _P, _P, _P, _I]),
     "bnn_pw_s8_run": (_I, [_P, _I, _I, _P, _LL, _I, _P, _LL, _I, _P, _LL, _I, _I, _I, _P, _LL, _I, _I, _I, _P]),
     "bnn_pw_s8_run_static": (_I, [_P, _I, _I, _P, _LL, _I, _P, _LL, _I, _P, _LL, _I, _I, _I, _P, _LL, _I, _I, _I, _P]),
+    "bnn_pw_s8_gemm": (_I, [_P, _I, _I, _P, _LL, _P, _P, _I, _P, _LL, _I, _I, _I, _P, _LL, _I, _I, _I, _P]),
     "bnn_pw_s8_error": (_I, [_P]),
     "bnn_pw_s8_free": (None, [_P]),
     "bnn_cuda_dw3": (_I, [_I, _P, _LL, _I, _I, _I, _I, _P, _P, _P, _LL, _I, _I, _P, _LL, _P]),

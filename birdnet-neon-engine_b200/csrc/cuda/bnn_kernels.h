@@ -57,6 +57,11 @@ typedef struct {
 int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float *sa, const int32_t *za, const bnnk_epilogue *e,
               int *err, bnn_stream_t st);
 
+/* the GEMM of a planned layer on quantized rows the caller holds: q [rows][ldq] (ldq % 16 == 0, the first kp bytes
+ * of each row are the row, kp <= the plan's kq), sa, za [rows] */
+int bnnk_gemm_q(const bnnk_gemm_plan *p, const int8_t *q, long long ldq, int kp, int rows, int Mw, const float *sa,
+                const int32_t *za, const bnnk_epilogue *e, int *err, bnn_stream_t st);
+
 /* quantizer + GEMM of a planned layer with q / sa / za in the file-scope static array of k_int8.cu instead of the
  * layer's own scratch; allocates nothing. At most BNNK_STATIC_ROWS rows and rows * kq <= BNNK_STATIC_QBYTES
  * (cudaErrorInvalidValue beyond). The first call on a device (rows = 0 does only this) looks up the array's address

@@ -525,11 +525,12 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode(void) {
   return fn;
 }
 
-static int encode_2d(void *map, const void *base, int inner, int rows, int box_inner, int box_rows, int sw) {
+static int encode_2d_ld(void *map, const void *base, int inner, long long ld, int rows, int box_inner, int box_rows,
+                        int sw) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode();
   if (!enc) return cudaErrorNotSupported;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)inner};
+  cuuint64_t strides[1] = {(cuuint64_t)ld};
   cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
   cuuint32_t es[2] = {1, 1};
   CUtensorMapSwizzle swz = sw == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : sw == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
@@ -538,6 +539,9 @@ static int encode_2d(void *map, const void *base, int inner, int rows, int box_i
                    es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : cudaErrorInvalidValue;
+}
+static int encode_2d(void *map, const void *base, int inner, int rows, int box_inner, int box_rows, int sw) {
+  return encode_2d_ld(map, base, inner, inner, rows, box_inner, box_rows, sw);
 }
 
 // N tiling: as few tiles of at most 256 columns as possible, equal widths rounded up to 16
@@ -722,6 +726,16 @@ extern "C" int bnnk_pw_s8_static(const bnnk_gemm_plan *p, int rows, int Mw, cons
   if (!rc) rc = bnnk_quant(rows, Mw, x, xws, lda, K, p->kq, gate, gws, q, sa, za, st);
   if (!rc) rc = bnnk_gemm(&pl, rows, Mw, sa, za, e, err, st);
   return rc;
+}
+
+// the GEMM of a planned layer on quantized rows the caller holds: q [rows][ldq] (the first kp bytes of a row used,
+// TMA zero fill past them), sa, za [rows] (s8n_gemm_range on the rows s8n_quant_rows wrote)
+extern "C" int bnnk_gemm_q(const bnnk_gemm_plan *p, const int8_t *q, long long ldq, int kp, int rows, int Mw,
+                           const float *sa, const int32_t *za, const bnnk_epilogue *e, int *err, bnn_stream_t st) {
+  if (rows <= 0) return 0;
+  bnnk_gemm_plan pl = *p;
+  const int rc = encode_2d_ld(pl.tma_a, q, kp, ldq, rows, p->sw, 128, p->sw);
+  return rc ? rc : bnnk_gemm(&pl, rows, Mw, sa, za, e, err, st);
 }
 
 extern "C" int bnnk_test_fn(int fn, int n, const float *x, float *y, bnn_stream_t st) {

@@ -762,6 +762,21 @@ int bnn_pw_s8_run_static(bnn_pw_s8 *o, int B, int Mw, const float *d_x, long lon
                                                              gws, &ep, o->err, (bnn_stream_t)stream));
 }
 
+int bnn_pw_s8_gemm(bnn_pw_s8 *o, int B, int Mw, const int8_t *d_q, long long ldq, const float *d_sa,
+                   const int32_t *d_za, int act, float *d_out, long long ows, int ldo, int ow, int opad,
+                   const float *d_res, long long rws, int ldr, int rw, int rpad, void *stream) {
+  if (!o || B < 0 || Mw < 1 || !d_q || !d_sa || !d_za || ldq < o->Kp || ldq % 16 || ((uintptr_t)d_q & 15) ||
+      ldo < o->Np || act < 0 || act > 2 || (opad && (ow <= 0 || Mw % ow)) || (rpad && (rw <= 0 || Mw % rw)) ||
+      (d_res && ldr < o->Np)) {
+    ERR(BNN_ERR_USAGE, "bnn_pw_s8_gemm: B %d Mw %d ldq %lld (>= Kp %d, a multiple of 16, 16-byte aligned rows) ldo %d "
+        "act %d ow %d opad %d", B, Mw, ldq, o ? o->Kp : 0, ldo, act, ow, opad);
+    return -1;
+  }
+  bnnk_epilogue ep = {act, d_out, ows, ldo, ow, opad, d_res, rws, ldr, rw, rpad, o->op.sw, o->op.bias, o->op.cs};
+  return launch_rc("bnn_pw_s8_gemm", bnnk_gemm_q(&o->op.plan, d_q, ldq, o->Kp, B * Mw, Mw, d_sa, d_za, &ep, o->err,
+                                                 (bnn_stream_t)stream));
+}
+
 int bnn_pw_s8_error(bnn_pw_s8 *o) {
   int v = 0;
   if (o && o->err) cudaMemcpy(&v, o->err, sizeof v, cudaMemcpyDeviceToHost);

@@ -77,6 +77,12 @@ bnn_pw_s8 *bnn_pw_s8_new(int N, int K, int Kp, int Np, const int8_t *w, const fl
 int bnn_pw_s8_run(bnn_pw_s8 *op, int B, int Mw, const float *d_x, long long xws, int lda, const float *d_gate,
                   long long gws, int act, float *d_out, long long ows, int ldo, int ow, int opad, const float *d_res,
                   long long rws, int ldr, int rw, int rpad, void *stream);
+/* s8n_gemm_range (src/gemm_s8n.c:176-190 with its tiles :82-175, declared src/gemm_s8n.h:22) on quantized rows the
+ * caller holds, as s8n_quant_rows / bnn_cuda_quant_rows write them: d_q [B * Mw][ldq] int8 (ldq >= Kp, a multiple of
+ * 16; the row's first Kp bytes are used), d_sa, d_za [B * Mw]; then the same epilogue and store as bnn_pw_s8_run */
+int bnn_pw_s8_gemm(bnn_pw_s8 *op, int B, int Mw, const int8_t *d_q, long long ldq, const float *d_sa,
+                   const int32_t *d_za, int act, float *d_out, long long ows, int ldo, int ow, int opad,
+                   const float *d_res, long long rws, int ldr, int rw, int rpad, void *stream);
 /* No counterpart in the reference: bnn_pw_s8_run for hosts that must not allocate device memory while they run (a
  * live-audio loop, where cudaMalloc / cudaFree may synchronise the device and take unbounded time; a server whose
  * device memory was sized at start-up). The quantized activations and their per-row scale / zero point go to one
