@@ -307,3 +307,17 @@ def test_device_entry_point(lib, mini_pkg):
         d_emb = torch.zeros((4, m.info.emb_dim), dtype=torch.float32, device="cuda")
         m.infer_device(4, d_pcm.data_ptr(), d_out.data_ptr(), d_emb.data_ptr())
         assert bits_equal(host(d_out), want) and bits_equal(host(d_emb), wemb)
+
+
+def test_two_gpus_in_one_context(lib, mini_pkg):
+    """bnn_set_threads(ctx, 2) spreads a batch over two GPUs in one process; outputs equal one GPU's bit for bit."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two visible GPUs")
+    pcm = synth.audio(9, seed=5)
+    with Model(mini_pkg, mode=4, batch=4) as m1:
+        out1, emb1 = m1.infer_batch(pcm)
+    with Model(mini_pkg, mode=4, batch=4) as m2:
+        m2.set_threads(2)
+        out2, emb2 = m2.infer_batch(pcm)
+    assert bits_equal(out1, out2), mismatch_report(out1, out2)
+    assert bits_equal(emb1, emb2), mismatch_report(emb1, emb2)
