@@ -7,13 +7,13 @@
 //
 // GEMM: one persistent CTA per SM walks the 128-row x BN-column tiles (N tiles inner, so consecutive tiles reuse the
 // same rows of A from L2). Warp 0 lane 0 streams K blocks of A (quantized rows) and B (weights [Nrows][Kq], K-major)
-// into a ring of shared-memory stages with 2-D TMA loads (swizzle = the K-block width, 32/64/128 bytes; no
-// multicast). Warp 1 lane 0 issues tcgen05.mma.cta_group::1.kind::i8 (M 128, N BN, K 32 per instruction) into one of
-// NE TMEM accumulators (tile i uses accumulator i mod NE) and releases smem stages and finished accumulators with
-// tcgen05.commit. NE epilogue warpgroups each own one accumulator: a warp reads its 32 TMEM lanes (= rows) with
-// tcgen05.ld, frees the accumulator and runs the fp32 epilogue, while the MMA warp already fills the others. Every
-// mbarrier wait is bounded by a %globaltimer deadline; a timeout sets the error word, the CTA stops and still frees
-// its TMEM.
+// into a ring of shared-memory stages with 2-D TMA loads (128-byte K blocks, swizzle 128 B; a ragged last block reads
+// zero fill; every CTA loads its own tiles). Warp 1 lane 0 issues tcgen05.mma.cta_group::1.kind::i8 (M 128, N BN,
+// K 32 per instruction) into one of NE TMEM accumulators (tile i uses accumulator i mod NE) and releases stages and
+// finished accumulators with tcgen05.commit. Each accumulator has an epilogue group of 4 NH warps: the warps of a
+// TMEM lane quarter (= 32 rows) split the tile's 8-column units round robin, read them with tcgen05.ld, free the
+// accumulator and run the fp32 epilogue while the MMA warp fills the other one. Every mbarrier wait is bounded by a
+// %globaltimer deadline; a timeout sets the error word, the CTA stops and still frees its TMEM.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
