@@ -3,9 +3,9 @@ import struct
 
 # buffer arguments each kernel writes (the reference registry's outmask) and the ones that are the int8 path's row
 # scratch (q, sa, za), which the B200 runtime keeps in its own layout
-OUTMASK = {1: 0x2, 2: 0x2, 4: 0x6, 6: 0xE, 25: 0x2, 22: 0x3A, 23: 0x1E}
-SCRATCH = {22: (3, 4, 5), 23: (2, 3, 4), 6: (2, 3)}
-NAMES = {1: "FE_STFT2", 2: "C0POOL", 4: "DW3", 6: "POSTPC", 22: "PW_S8", 23: "GEMV_S8", 25: "SE_GATE"}
+OUTMASK = {1: 0x2, 2: 0x2, 4: 0x6, 6: 0xE, 25: 0x2, 22: 0x3A, 23: 0x1E, 35: 0xE}
+SCRATCH = {22: (3, 4, 5), 23: (2, 3, 4), 6: (2, 3), 35: (2,)}
+NAMES = {1: "FE_STFT2", 2: "C0POOL", 4: "DW3", 6: "POSTPC", 22: "PW_S8", 23: "GEMV_S8", 25: "SE_GATE", 35: "PROTO_S8"}
 
 
 def read_ops(path, path_name="neon-int8"):
@@ -62,3 +62,16 @@ def op_offsets(path, path_name="neon-int8"):
             q += struct.unpack_from("<H", data, q + 2)[0]
         return offs
     raise KeyError(path_name)
+
+
+def tensor_offset(path, name):
+    """File offset of the data of the tensor called `name` (for tests that corrupt one tensor)."""
+    with open(path, "rb") as f:
+        data = f.read()
+    _, n_tensors, _, _ = struct.unpack_from("<4I", data, 16)
+    _, tensor_off, _, _ = struct.unpack_from("<4Q", data, 32)
+    for i in range(n_tensors):
+        o = tensor_off + 96 * i
+        if data[o:o + 48].rstrip(b"\0").decode() == name:
+            return struct.unpack_from("<Q", data, o + 72)[0]
+    raise KeyError(name)

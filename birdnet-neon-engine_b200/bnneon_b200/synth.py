@@ -143,14 +143,16 @@ def labels_for(n_classes):
     return "".join(f"Synthetic species {i:05d}_Synthetic {i:05d}\n" for i in range(n_classes)).encode()
 
 
-def metadata(n_classes, emb_dim, labels, model_id="birdnet_v2.4_synthetic"):
+def metadata(n_classes, emb_dim, labels, model_id="birdnet_v2.4_synthetic", family=24, sample_rate=SAMPLE_RATE,
+             n_samples=NSAMP, attribution="synthetic BirdNET-v2.4-architecture model (random weights)"):
     """The package metadata records, in the compiler's order (cmd_compile.py _set_metadata)."""
-    return [("model_id", model_id), ("family", 24), ("sample_rate", SAMPLE_RATE), ("n_samples", NSAMP),
+    return [("model_id", model_id), ("family", family), ("sample_rate", sample_rate), ("n_samples", n_samples),
             ("hop_samples", 0), ("n_classes", int(n_classes)), ("emb_dim", int(emb_dim)), ("post", 1),
             ("logit_scale", 1.0), ("labels_sha256", hashlib.sha256(labels).digest()), ("labels_file", "labels.txt"),
             ("labels", labels), ("license", "synthetic weights, no license restrictions"),
-            ("attribution", "synthetic BirdNET-v2.4-architecture model (random weights)"),
-            ("source_sha256", "0" * 64), ("input", f"float32 PCM in [-1, 1) at sample_rate, {NSAMP} samples per window"),
+            ("attribution", attribution),
+            ("source_sha256", "0" * 64),
+            ("input", f"float32 PCM in [-1, 1) at sample_rate, {n_samples} samples per window"),
             ("compiler", "bnc 3")]
 
 
@@ -481,6 +483,101 @@ def make_package(dst, seed=0, mini=False, n_classes=None):
     """A synthetic v2.4-architecture neon-int8 package at dst; returns (n_classes, emb_dim)."""
     nc = n_classes if n_classes is not None else (61 if mini else 6522)
     return write_int8_package(dst, v24_ir(seed, nc, MINI_BLOCKS if mini else V24_BLOCKS))
+
+
+# ------------------------------------------------------------------ the int8 prototype head (PROTO_S8)
+
+OPC_PROTO_S8 = 35
+PERCH_SAMPLE_RATE = 32000
+BNN_MODEL_PERCH_V2 = 120
+
+
+def quant_rows_s8(w):
+    """Per-row symmetric int8 of a float32 [N][K] matrix, as lower.py quant_rows_s8: sw = max |row| / 127 (0 for a
+    zero row), q = round half away from zero of w / sw clipped to [-127, 127], in float32 arithmetic."""
+    am = np.abs(w).max(1)
+    sw = np.where(am > 0, am / 127.0, 0.0).astype(np.float32)
+    sw_safe = np.where(sw > 0, sw, 1)
+    q = np.where(sw[:, None] > 0, w / sw_safe[:, None], 0)
+    q = np.clip(np.sign(q) * np.floor(np.abs(q) + 0.5), -127, 127).astype(np.int8)
+    return q, sw
+
+
+N4_LANE_LIMIT = 258
+
+
+def n4_panel_flags(q):
+    """One flag per 4-row panel of int8 [Np][Kp] weights: 1 where every int16 lane of the reference's n=4 K loop (bytes
+    l, l + 8, l + 16, l + 24 of each 32-byte step) has sum |w| <= 258; all 0 when Kp % 32 != 0 (lower.py
+    n4_panel_flags)."""
+    rows, kp = q.shape
+    if kp % 32:
+        return np.zeros(rows // 4, np.int8)
+    lane = np.abs(q.astype(np.int32)).reshape(rows, kp // 32, 4, 8).sum(2)
+    worst = lane.max(axis=(1, 2))
+    return (worst.reshape(rows // 4, 4).max(1) <= N4_LANE_LIMIT).astype(np.int8)
+
+
+def proto_head(seed, n_cells, channels, n_classes, ppc, eps=1e-6, scale=1.0):
+    """A seeded prototype head: prototypes [n_classes * ppc][channels] N(0, scale), class weights [n_classes][ppc]
+    N(1, 0.1), class biases N(0, 0.05)."""
+    rng = np.random.default_rng(seed)
+    n = n_classes * ppc
+    protos = (rng.standard_normal((n, channels)) * scale).astype(np.float32)
+    cw = (1.0 + 0.1 * rng.standard_normal((n_classes, ppc))).astype(np.float32)
+    cb = (0.05 * rng.standard_normal(n_classes)).astype(np.float32)
+    return dict(P=protos, cw=cw, cb=cb, eps=float(eps), n_cells=int(n_cells))
+
+
+def pack_proto_s8(protos):
+    """The neon-int8 prototype tensors (lower.py proto_s8n): q [Np/4][Kp/16][4][16] int8 (Np = N rounded up to 4,
+    Kp = K rounded up to 16, zero padding), sw [Np], n4 [Np/4]; also returns the unpacked q [Np][Kp]."""
+    n, c = protos.shape
+    n_pad, k_pad = (n + 3) & ~3, _r16(c)
+    wq = np.zeros((n_pad, k_pad), np.float32)
+    wq[:n, :c] = protos
+    q, sw = quant_rows_s8(wq)
+    qp = q.reshape(n_pad // 4, 4, k_pad // 16, 16).transpose(0, 2, 1, 3).copy()
+    return qp, sw, n4_panel_flags(q), q
+
+
+def write_proto_package(dst, head, ld=None, model_id="perch_v2_proto_head_synthetic"):
+    """A one-op neon-int8 package: PROTO_S8 on the input window taken as cells [n_cells][ld] (the first C = K
+    channels of each row used), logits [n_classes] out. Buffers, tensors, record and slots as the reference compiler
+    makes them for a prototype head (lower.py proto_s8n / emit_proto / cls_tensors, plan_slots). Returns
+    (n_classes, n_samples)."""
+    protos = head["P"]
+    n, c = protos.shape
+    p_cells = head["n_cells"]
+    ld = ld or c
+    nc, ppc = head["cw"].shape
+    ns = p_cells * ld
+    qp, sw, n4, _ = pack_proto_s8(protos)
+    n_pad, k_pad = qp.shape[0] * 4, qp.shape[1] * 16
+    lw = _Int8Lowering([])
+    lw.bufs = [(F32, 1, 1, ns, ns, 0, ns)]
+    tl = [lw.tensor("s8n/proto.0.q", qp), lw.tensor("s8n/proto.0.s", sw), lw.tensor("s8n/proto.0.n4", n4),
+          lw.tensor("cls.0.w", head["cw"]), lw.tensor("cls.0.b", head["cb"]),
+          lw.tensor("cls.0.eps", np.array([head["eps"]], np.float32))]
+    ob = lw.buf(F32, 1, 1, nc)
+    ab = lw.buf(I8, p_cells, 1, k_pad)
+    cm = lw.buf(F32, 1, 1, n_pad)
+    lw.emit(OPC_PROTO_S8, [0, ob, ab, cm], tl, [n, c, k_pad, n_pad, p_cells, c, ld, nc, ppc], {})
+    bufs = plan_slots(lw.bufs, lw.records, [ob])
+    meta = [(f"src_nodes/{PATH}", "\n".join(lw.src))] + metadata(
+        nc, 0, labels_for(nc), model_id=model_id, family=BNN_MODEL_PERCH_V2, sample_rate=PERCH_SAMPLE_RATE,
+        n_samples=ns, attribution="synthetic prototype head (random weights)")
+    write_package(dst, meta, lw.tensors, [(PATH, 0, bufs, lw.records, 0, ob, None)])
+    return nc, ns
+
+
+def cells(n, n_cells, ld, seed=0, scale=1.0):
+    """n windows of cells [n][n_cells][ld] float32, N(0, scale) (a prototype head's input), window w seeded by
+    (seed, w)."""
+    out = np.empty((n, n_cells, ld), np.float32)
+    for i in range(n):
+        out[i] = np.random.default_rng((seed, i)).standard_normal((n_cells, ld)) * scale
+    return out
 
 
 # ------------------------------------------------------------------ audio

@@ -16,6 +16,9 @@ typedef struct CUstream_st *bnn_stream_t;
 
 /* device-side error word written by kernels whose bounded waits time out (0 = none) */
 enum { BNNK_ERR_NONE = 0, BNNK_ERR_TMA_WAIT = 1, BNNK_ERR_MMA_WAIT = 2, BNNK_ERR_EPI_WAIT = 3, BNNK_ERR_DW3_WAIT = 4 };
+/* the failed-window word beside it: the smallest failed window index, or BNNK_NO_FAIL (every byte 0x7f, so that a
+ * byte memset restores it) */
+#define BNNK_NO_FAIL 0x7f7f7f7f
 
 /* per device, once: the glibc expf table (computed on the host) and the FRECPE estimate table */
 int bnnk_device_init(void);
@@ -116,6 +119,35 @@ typedef struct {
 } bnnk_fe_tables;
 int bnnk_fe_stft2(int B, const float *pcm, long long pws, const bnnk_fe_tables *t, float *minmax, float *img,
                   long long iws, bnn_stream_t st);
+
+/* ---- the int8 prototype head (PROTO_S8) */
+
+/* per-cell quantization (pc_quant_cells_f32): cells r = w * P + p of x (window stride xws, row stride ld floats;
+ * C % 8 == 0) -> qa [B * P][Kq] int8 (Kq % 8 == 0, zero from C), sx [B * P] */
+int bnnk_proto_quant(int B, int P, const float *x, long long xws, int ld, int C, int Kq, float eps, int8_t *qa,
+                     float *sx, bnn_stream_t st);
+
+/* the column-maximum GEMM of one head: prototypes w [np][kp] int8 (row j = prototype j, zero from K), cells qa
+ * [batch_cap * P][kp]. Cell tiles hold wt = floor(256 / P) whole windows when P <= 256 (bn = wt P rounded up to 16
+ * MMA columns), else chunks of cs cells (nch per window) whose partial maxima go through scratch. */
+typedef struct {
+  unsigned char tma_w[128] __attribute__((aligned(64)));
+  unsigned char tma_q[128] __attribute__((aligned(64)));
+  int np, kp, P, batch_cap;
+  int wt, nch, cs, bn, unit, acc_cols, nkb, stages;
+  unsigned int idesc;
+  size_t smem;
+} bnnk_proto_plan;
+int bnnk_proto_plan_init(bnnk_proto_plan *p, const int8_t *w, int np, int kp, const int8_t *qa, int batch_cap, int P);
+/* colmax [batch][cws] = sw[j] * max over the window's cells of (float)acc * sx[cell]; part: scratch of
+ * batch * nch * np floats when the plan has wt == 0 (else NULL) */
+int bnnk_proto_colmax(const bnnk_proto_plan *p, int batch, const float *sx, const float *sw, float *colmax,
+                      long long cws, float *part, int *err, bnn_stream_t st);
+/* logits [batch][lws] from colmax [batch][cws], class weights [nc][ppc], biases [nc]. A window with a logit that is not
+ * finite or above 3e38 in magnitude failed: status [batch] (or NULL) gets -2 for it (else 0), and *fail (or NULL) is
+ * lowered to w_base + its index (atomic minimum) */
+int bnnk_proto_logits(int batch, int nc, int ppc, const float *colmax, long long cws, const float *cw, const float *cb,
+                      float *logits, long long lws, int *status, int *fail, int w_base, bnn_stream_t st);
 
 /* ---- elementwise functions for the unit tests */
 int bnnk_test_fn(int fn, int n, const float *x, float *y, bnn_stream_t st);

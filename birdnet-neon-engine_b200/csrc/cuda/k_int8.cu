@@ -28,6 +28,7 @@
 #include "bnn_kernels.h"
 #include "emu.cuh"
 #include "sync.cuh"
+#include "tc.cuh"
 
 namespace bnn {
 
@@ -142,29 +143,6 @@ constexpr int kMaxStages = 8, kMaxEpi = 4;
 constexpr int kMaxThreads = 832;  // 2 + 24 warps: 64 + 128 * ne * nh with ne * nh <= 6
 constexpr int kSPMax = 1536;      // widest layer whose epilogue parameters are staged in shared memory
 
-// shared-memory matrix descriptor of a K-major tile with rows of SW bytes swizzled by SW (8-row groups of 8 * SW
-// bytes); version 1 (sm_100), base offset 0 (stages are aligned to the swizzle repeat)
-template <int SW>
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
-  constexpr uint64_t layout = SW == 128 ? 2 : SW == 64 ? 4 : 6;
-  return (uint64_t)((addr & 0x3ffffu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)((8 * SW) >> 4) << 32) |
-         ((uint64_t)1 << 46) | (layout << 61);
-}
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
-}
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
 constexpr int kEpiUnits = 3;  // 8-column TMEM loads in flight per epilogue warp
 // wait for this thread's TMEM loads; the registers they fill are operands of the wait, so no use moves above it
 __device__ __forceinline__ void tmem_wait(uint32_t (&r)[kEpiUnits][8]) {
@@ -525,8 +503,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode(void) {
   return fn;
 }
 
-static int encode_2d_ld(void *map, const void *base, int inner, long long ld, int rows, int box_inner, int box_rows,
-                        int sw) {
+int bnn::encode_2d_ld(void *map, const void *base, int inner, long long ld, int rows, int box_inner, int box_rows,
+                      int sw) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode();
   if (!enc) return cudaErrorNotSupported;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
@@ -559,6 +537,15 @@ extern "C" int bnnk_gemm_weight_rows(int np) {
 }
 
 static int g_num_sms = 0;
+int bnn::num_sms() {
+  if (!g_num_sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
 
 // tcgen05.alloc takes a power of two from 32 to 512 columns
 static int tmem_pow2(int cols) {
@@ -604,7 +591,7 @@ extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_
   int s = (int)((200 * 1024 - par) / stage);
   p->stages = s < 2 ? 2 : s > kMaxStages ? kMaxStages : s;
   p->smem = (size_t)p->stages * stage + 1024 + par;
-  p->idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p->bn >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+  p->idesc = idesc_i8(p->bn);
   const int wrows = p->n_tiles * p->bn;  // the weight buffer holds n_tiles * bn rows (zero beyond n)
   int e = encode_2d(p->tma_a, q, kq, rows_cap, p->sw, 128, p->sw);
   if (!e) e = encode_2d(p->tma_b, w, kq, wrows, p->sw, p->bn, p->sw);
@@ -624,13 +611,7 @@ static int launch_gemm(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t 
     if (e) return e;
     attr[dev] = p->smem;
   }
-  if (!g_num_sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  const int grid = a.tiles < g_num_sms ? a.tiles : g_num_sms;
+  const int grid = a.tiles < num_sms() ? a.tiles : num_sms();
   k_gemm_s8<SW, kSP><<<grid, 64 + 128 * a.ne * a.nh, p->smem, st>>>(*(const CUtensorMap *)p->tma_a,
                                                                     *(const CUtensorMap *)p->tma_b, a);
   return cudaGetLastError();

@@ -1,0 +1,461 @@
+// The int8 prototype head (PROTO_S8) on sm_100a: per-cell symmetric quantizer, a persistent tcgen05 kind::i8 GEMM
+// whose epilogue takes each prototype's maximum over a window's cells, and the per-class logits.
+//
+// Reference: src/proto_s8n.c (pc_quant_cells_f32 :28-52, pc_proto_colmax_s8n :130-164) driven by PROTO_S8
+// (src/rt_ops_s8n.c:212-250), logits pc_proto_logits (src/pc_kern_f32.c:364-376).
+//   colmax[w][j] = sw[j] * max over the cells p of window w of (float)(sum_k qa[p][k] qw[j][k]) * sx[p]
+// The int32 sums are exact in both (|q| <= 127, K <= 2^17), so the tensor cores' summation order cannot change them;
+// the conversion, scale, maximum and final scale repeat the reference's fp32 steps (max is exact, so the order in
+// which cells are visited does not matter; NaN propagates, -0 < +0 as in FMAX).
+//
+// GEMM orientation: the prototypes are the MMA's M side (128 per tile, TMEM lanes) and the cells its N side (TMEM
+// columns), so one epilogue thread owns one prototype and reduces over cells along its own TMEM row, with no
+// exchange between threads. A cell tile holds whole windows (floor(256 / P) of them) when P <= 256; longer windows
+// are split into chunks of at most 256 cells whose partial maxima a second kernel combines.
+//
+// Pipeline (as the 1x1-conv GEMM): warp 0 lane 0 streams 128-byte K blocks of prototypes and cells into a ring of
+// shared-memory stages with 2-D TMA loads (swizzle 128 B, zero fill past K); warp 1 lane 0 issues
+// tcgen05.mma.cta_group::1.kind::i8 (M 128, N = the cell tile, K 32 per instruction) into one of two TMEM
+// accumulators; each accumulator has an epilogue group of 4 NH warps that split the tile's windows. Tiles run
+// prototype-tile major with the cell tiles inner, so the prototypes stream from HBM once while the (smaller) cell
+// matrix stays in L2. Every mbarrier wait is bounded; a timeout sets the error word and the CTA winds down, still
+// freeing its TMEM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "bnn_kernels.h"
+#include "emu.cuh"
+#include "sync.cuh"
+#include "tc.cuh"
+
+namespace bnn {
+
+// ------------------------------------------------------------------ per-cell quantizer
+
+// FCVTAS (nearest, ties away from zero, saturating, NaN -> 0) narrowed with saturation to int8 and raised to -127:
+// the bytes of src/proto_s8n.c:44-48. trunc(v) and v - trunc(v) are exact, so the tie test is exact.
+__device__ __forceinline__ int q_ties_away(float v) {
+  float t = truncf(v);
+  const float d = __fsub_rn(v, t);
+  if (fabsf(d) >= 0.5f) t = __fadd_rn(t, copysignf(1.f, v));
+  const int i = cvtzs(t);
+  return i > 127 ? 127 : i < -127 ? -127 : i;
+}
+
+constexpr int kQCells = 128;  // cells per quantizer block (2 threads each in the reduction)
+
+// cells r = w * P + p of x (window stride xws, row stride ld floats) -> qa [cells][Kq] (zero from C to Kq), sx [cells].
+// Reduction: thread pair (2 cp, 2 cp + 1) holds the reference's accumulators s0 (lanes 0-3) and s1 (lanes 4-7) of
+// cell cp: lane l of the 8-channel step c is channel c + l, fused x x + s in channel order. Quantization: each warp
+// takes cells of the block, a lane 8 channels (two 16-byte loads, one 8-byte store) at a time.
+template <bool VEC>
+__global__ void __launch_bounds__(256) k_proto_quant(int cells, int P, const float *__restrict__ x, long long xws,
+                                                     int ld, int C, int Kq, float eps, int8_t *__restrict__ qa,
+                                                     float *__restrict__ sx) {
+  __shared__ float s_inv[kQCells];
+  const int c0 = blockIdx.x * kQCells;
+  {
+    const int cl = threadIdx.x >> 1, half = threadIdx.x & 1, cell = c0 + cl;
+    float s[4] = {0.f, 0.f, 0.f, 0.f}, m[4] = {0.f, 0.f, 0.f, 0.f};
+    if (cell < cells) {
+      const int w = cell / P, p = cell - w * P;
+      const float *r = x + (long long)w * xws + (long long)p * ld + 4 * half;
+      for (int c = 0; c < C; c += 8) {
+        float u[4];
+        if (VEC) {
+          const float4 v = __ldg(reinterpret_cast<const float4 *>(r + c));
+          u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
+        } else {
+#pragma unroll
+          for (int l = 0; l < 4; l++) u[l] = __ldg(r + c + l);
+        }
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+          s[l] = __fmaf_rn(u[l], u[l], s[l]);
+          m[l] = fmax_nan(m[l], fabsf(u[l]));
+        }
+      }
+    }
+    float o[4], om[4];
+#pragma unroll
+    for (int l = 0; l < 4; l++) {
+      o[l] = __shfl_xor_sync(0xffffffffu, s[l], 1);
+      om[l] = __shfl_xor_sync(0xffffffffu, m[l], 1);
+    }
+    if (cell < cells && half == 0) {
+      // vaddvq_f32(s0 + s1): lanewise sums, then pairwise
+      const float v0 = __fadd_rn(s[0], o[0]), v1 = __fadd_rn(s[1], o[1]), v2 = __fadd_rn(s[2], o[2]),
+                  v3 = __fadd_rn(s[3], o[3]);
+      const float sum = __fadd_rn(__fadd_rn(v0, v1), __fadd_rn(v2, v3));
+      const float den = __fadd_rn(__fsqrt_rn(sum), eps);
+      float mx = fmax_nan(fmax_nan(fmax_nan(m[0], om[0]), fmax_nan(m[1], om[1])),
+                          fmax_nan(fmax_nan(m[2], om[2]), fmax_nan(m[3], om[3])));
+      if (!(mx > 0.f)) mx = 1e-30f;
+      sx[cell] = __fdiv_rn(mx, __fmul_rn(127.f, den));
+      s_inv[cl] = __fdiv_rn(127.f, mx);
+    }
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nchunk = Kq / 8;
+  for (int cl = warp; cl < kQCells; cl += 8) {
+    const int cell = c0 + cl;
+    if (cell >= cells) break;
+    const int w = cell / P, p = cell - w * P;
+    const float *r = x + (long long)w * xws + (long long)p * ld;
+    const float inv = s_inv[cl];
+    int8_t *qrow = qa + (long long)cell * Kq;
+    for (int ch = lane; ch < nchunk; ch += 32) {
+      uint32_t lo = 0, hi = 0;
+      if (8 * ch < C) {  // C % 8 == 0: a chunk is all inside or all outside the row
+        float u[8];
+        if (VEC) {
+          const float4 a = __ldg(reinterpret_cast<const float4 *>(r + 8 * ch));
+          const float4 b = __ldg(reinterpret_cast<const float4 *>(r + 8 * ch + 4));
+          u[0] = a.x; u[1] = a.y; u[2] = a.z; u[3] = a.w; u[4] = b.x; u[5] = b.y; u[6] = b.z; u[7] = b.w;
+        } else {
+#pragma unroll
+          for (int l = 0; l < 8; l++) u[l] = __ldg(r + 8 * ch + l);
+        }
+        int b[8];
+#pragma unroll
+        for (int l = 0; l < 8; l++) b[l] = q_ties_away(__fmul_rn(u[l], inv));
+        lo = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+        hi = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
+      }
+      *reinterpret_cast<uint2 *>(qrow + 8 * ch) = make_uint2(lo, hi);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ the column-maximum GEMM
+
+constexpr int kPMaxStages = 8;
+constexpr int kPMaxThreads = 64 + 128 * 2 * 2;  // 2 accumulators x 4 lane quarters x up to 2 warps
+constexpr int kPLoads = 4;  // TMEM loads in flight per epilogue thread
+
+struct ProtoArgs {
+  int np;             // prototypes (rows of A, columns of colmax)
+  int batch, P;       // windows, cells per window
+  int wt;             // windows per cell tile (P <= 256), else 0
+  int nch, cs;        // P > 256: chunks per window, cells per chunk
+  int n_ct, tiles;    // cell tiles, all tiles (prototype tiles x cell tiles)
+  int nkb, stages, bn, acc_cols, ne, nh, tmem_alloc;
+  uint32_t idesc;
+  const float *sx, *sw;
+  float *out;         // colmax [batch][ows] (wt > 0) or partial maxima [batch * nch][np]
+  long long ows;
+  int *err;
+};
+
+// the maximum over tile columns [col0, col0 + n) of (float)acc * sx[cell0 + col] for this thread's prototype: U
+// columns per TMEM load (8, or 4 when windows start on odd multiples of 4), kPLoads loads in flight
+template <int U>
+__device__ __forceinline__ float col_max(uint32_t trow, int col0, int n, const float *__restrict__ sxc, float mx) {
+  for (int c = col0; c < col0 + n; c += U * kPLoads) {
+    uint32_t acc[kPLoads][U];
+#pragma unroll
+    for (int k = 0; k < kPLoads; k++) {
+      if (c + k * U < col0 + n) {
+        if constexpr (U == 8) tmem_ld8(trow + (uint32_t)(c + k * U), acc[k]);
+        else tmem_ld4(trow + (uint32_t)(c + k * U), acc[k]);
+      }
+    }
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int k = 0; k < kPLoads; k++) {
+      if (c + k * U < col0 + n) {
+#pragma unroll
+        for (int v = 0; v < U; v += 4) {
+          const float4 s = __ldg(reinterpret_cast<const float4 *>(sxc + c + k * U + v));
+          mx = fmax_nan(mx, __fmul_rn(__int2float_rn((int)acc[k][v + 0]), s.x));
+          mx = fmax_nan(mx, __fmul_rn(__int2float_rn((int)acc[k][v + 1]), s.y));
+          mx = fmax_nan(mx, __fmul_rn(__int2float_rn((int)acc[k][v + 2]), s.z));
+          mx = fmax_nan(mx, __fmul_rn(__int2float_rn((int)acc[k][v + 3]), s.w));
+        }
+      }
+    }
+  }
+  return mx;
+}
+
+template <int U>
+__global__ void __launch_bounds__(kPMaxThreads, 1) k_proto_colmax(const __grid_constant__ CUtensorMap tma_w,
+                                                                 const __grid_constant__ CUtensorMap tma_q,
+                                                                 const ProtoArgs a) {
+  constexpr int SW = 128;
+  extern __shared__ uint8_t dsmem[];
+  __shared__ __align__(8) unsigned long long bar_full[kPMaxStages], bar_empty[kPMaxStages];
+  __shared__ __align__(8) unsigned long long bar_acc_full[2], bar_acc_empty[2];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int abort_s;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t base = (smem_u32(dsmem) + 1023u) & ~1023u;
+  const uint32_t a_bytes = 128u * SW, stage_bytes = (128u + a.bn) * SW;
+  const int S = a.stages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) { mbar_init(smem_u32(&bar_full[s]), 1); mbar_init(smem_u32(&bar_empty[s]), 1); }
+    for (int g = 0; g < a.ne; g++) {
+      mbar_init(smem_u32(&bar_acc_full[g]), 1);
+      mbar_init(smem_u32(&bar_acc_empty[g]), 4 * a.nh);
+    }
+    abort_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(a.tmem_alloc));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      int it = 0;
+      for (int t = blockIdx.x; t < a.tiles && !abort_s; t += gridDim.x) {
+        const int m0 = (t / a.n_ct) * 128, ct = t % a.n_ct;
+        const int n0 = a.wt ? ct * a.wt * a.P : (ct / a.nch) * a.P + (ct % a.nch) * a.cs;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % S;
+          if (it >= S && !mbar_wait(smem_u32(&bar_empty[s]), ((it / S) - 1) & 1)) {
+            atomicExch(a.err, BNNK_ERR_TMA_WAIT);
+            abort_s = 1;
+            break;
+          }
+          const uint32_t st = base + s * stage_bytes, bar = smem_u32(&bar_full[s]);
+          mbar_expect_tx(bar, stage_bytes);  // full boxes: rows and bytes out of bounds arrive as zero fill
+          tma_load_2d(st, &tma_w, bar, kb * SW, m0);
+          tma_load_2d(st + a_bytes, &tma_q, bar, kb * SW, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      int it = 0, lt = 0;
+      for (int t = blockIdx.x; t < a.tiles && !abort_s; t += gridDim.x, lt++) {
+        const int g = lt % a.ne, use = lt / a.ne;
+        if (use > 0 && !mbar_wait(smem_u32(&bar_acc_empty[g]), (use - 1) & 1)) {
+          atomicExch(a.err, BNNK_ERR_MMA_WAIT);
+          abort_s = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t tacc = tmem + (uint32_t)(g * a.acc_cols);
+        bool ok = true;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % S;
+          if (!mbar_wait(smem_u32(&bar_full[s]), (it / S) & 1)) {
+            atomicExch(a.err, BNNK_ERR_MMA_WAIT);
+            abort_s = 1;
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t st = base + s * stage_bytes;
+#pragma unroll
+          for (int kk = 0; kk < SW / 32; kk++)
+            mma_i8(tacc, smem_desc<SW>(st + kk * 32), smem_desc<SW>(st + a_bytes + kk * 32), a.idesc, (kb | kk) != 0);
+          mma_commit(smem_u32(&bar_empty[s]));
+        }
+        if (!ok) break;
+        mma_commit(smem_u32(&bar_acc_full[g]));
+      }
+    }
+  } else if (warp - 2 < 4 * a.ne * a.nh) {
+    // epilogue: group g drains accumulator g; warp h of lane quarter q takes the tile's windows h, h + nh, ...
+    const int e = warp - 2, g = e / (4 * a.nh), h = (e % (4 * a.nh)) / 4, q = warp % 4;
+    int use = 0;
+    for (int t = blockIdx.x + g * gridDim.x; t < a.tiles; t += a.ne * gridDim.x, use++) {
+      const int m0 = (t / a.n_ct) * 128, ct = t % a.n_ct;
+      const int j = m0 + q * 32 + lane;
+      const float swj = j < a.np ? __ldg(a.sw + j) : 0.f;
+      bool ok = mbar_wait(smem_u32(&bar_acc_full[g]), use & 1);
+      ok = __all_sync(0xffffffffu, ok) && !abort_s;
+      if (!ok) {
+        if (lane == 0) { atomicExch(a.err, BNNK_ERR_EPI_WAIT); abort_s = 1; }
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t trow = tmem + (uint32_t)(g * a.acc_cols) + ((uint32_t)(q * 32) << 16);
+      if (a.wt) {
+        const int w0 = ct * a.wt, nw = min(a.wt, a.batch - w0);
+        const float *sxc = a.sx + (long long)w0 * a.P;
+        for (int wi = h; wi < nw; wi += a.nh) {
+          const float mx = col_max<U>(trow, wi * a.P, a.P, sxc, -INFINITY);
+          if (j < a.np) a.out[(long long)(w0 + wi) * a.ows + j] = __fmul_rn(mx, swj);
+        }
+      } else if (h == 0) {
+        const int w = ct / a.nch, k = ct % a.nch, cell0 = w * a.P + k * a.cs;
+        const int n = min(a.cs, a.P - k * a.cs);
+        const float mx = col_max<U>(trow, 0, n, a.sx + cell0, -INFINITY);
+        if (j < a.np) a.out[(long long)ct * a.np + j] = mx;
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[g]));
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_alloc));
+}
+
+// windows longer than one cell tile: colmax[w][j] = sw[j] * the maximum of the chunks' partial maxima
+__global__ void k_proto_chunks(int batch, int np, int nch, const float *__restrict__ part, const float *__restrict__ sw,
+                               float *__restrict__ out, long long ows) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x, w = blockIdx.y;
+  if (j >= np) return;
+  float mx = -INFINITY;
+  for (int k = 0; k < nch; k++) mx = fmax_nan(mx, part[((long long)w * nch + k) * np + j]);
+  out[(long long)w * ows + j] = __fmul_rn(mx, __ldg(sw + j));
+}
+
+// ------------------------------------------------------------------ logits
+
+// one block per window: logits[c] = (sum over q < ppc, in order, of colmax[c ppc + q] * w[c ppc + q]) + b[c], each
+// product and sum rounded. A window with a logit that is not finite or above 3e38 in magnitude failed
+// (pc_proto_logits returns -2): status[w] = -2 (else 0), and fail holds the smallest failed w_base + w.
+__global__ void __launch_bounds__(256) k_proto_logits(int nc, int ppc, const float *__restrict__ colmax,
+                                                      long long cws, const float *__restrict__ cw,
+                                                      const float *__restrict__ cb, float *__restrict__ logits,
+                                                      long long lws, int *__restrict__ status, int *fail, int w_base) {
+  const int w = blockIdx.x;
+  const float *cm = colmax + (long long)w * cws;
+  int bad = 0;
+  for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+    float s = 0.f;
+    for (int q = 0; q < ppc; q++) {
+      const long long i = (long long)c * ppc + q;
+      s = __fadd_rn(s, __fmul_rn(cm[i], __ldg(cw + i)));
+    }
+    const float v = __fadd_rn(s, __ldg(cb + c));
+    logits[(long long)w * lws + c] = v;
+    bad |= !(fabsf(v) <= 3.0e38f);
+  }
+  bad = __syncthreads_or(bad);
+  if (threadIdx.x == 0) {
+    if (status) status[w] = bad ? -2 : 0;
+    if (bad && fail) atomicMin(fail, w_base + w);
+  }
+}
+
+}  // namespace bnn
+
+using namespace bnn;
+
+// ------------------------------------------------------------------ launchers
+
+extern "C" int bnnk_proto_quant(int batch, int P, const float *x, long long xws, int ld, int C, int Kq, float eps,
+                                int8_t *qa, float *sx, bnn_stream_t st) {
+  const int cells = batch * P;
+  if (cells <= 0) return 0;
+  const bool vec = ((uintptr_t)x & 15) == 0 && xws % 4 == 0 && ld % 4 == 0;
+  const int grid = (cells + kQCells - 1) / kQCells;
+  if (vec) k_proto_quant<true><<<grid, 256, 0, st>>>(cells, P, x, xws, ld, C, Kq, eps, qa, sx);
+  else k_proto_quant<false><<<grid, 256, 0, st>>>(cells, P, x, xws, ld, C, Kq, eps, qa, sx);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_proto_plan_init(bnnk_proto_plan *p, const int8_t *w, int np, int kp, const int8_t *qa,
+                                    int batch_cap, int P) {
+  memset(p, 0, sizeof *p);
+  if (np <= 0 || np % 4 || kp <= 0 || kp % 16 || batch_cap <= 0 || P <= 0 || P % 4) return cudaErrorInvalidValue;
+  p->np = np;
+  p->kp = kp;
+  p->P = P;
+  p->batch_cap = batch_cap;
+  p->nkb = (kp + 127) / 128;
+  if (P <= 256) {
+    p->wt = 256 / P;
+    if (p->wt > batch_cap) p->wt = batch_cap;
+    p->bn = (p->wt * P + 15) & ~15;
+    p->nch = 1;
+    p->cs = P;
+  } else {
+    p->wt = 0;
+    p->nch = (P + 255) / 256;
+    p->cs = ((P + p->nch - 1) / p->nch + 15) & ~15;
+    if (p->cs > 256) p->cs = 256;
+    p->nch = (P + p->cs - 1) / p->cs;
+    p->bn = p->cs;
+  }
+  p->unit = (P % 8 == 0 && p->cs % 8 == 0) ? 8 : 4;
+  p->acc_cols = p->bn <= 32 ? 32 : p->bn <= 64 ? 64 : p->bn <= 128 ? 128 : 256;
+  const size_t stage = (size_t)(128 + p->bn) * 128;
+  int s = (int)((200 * 1024) / stage);
+  p->stages = s < 2 ? 2 : s > kPMaxStages ? kPMaxStages : s;
+  p->smem = (size_t)p->stages * stage + 1024;
+  p->idesc = idesc_i8(p->bn);
+  // prototypes [np][kp] (row stride kp), cells [batch_cap * P][kp]
+  int e = encode_2d_ld(p->tma_w, w, kp, kp, np, 128, 128, 128);
+  if (!e) e = encode_2d_ld(p->tma_q, qa, kp, kp, batch_cap * P, 128, p->bn, 128);
+  return e;
+}
+
+template <int U>
+static int launch_colmax(const bnnk_proto_plan *p, const ProtoArgs &a, bnn_stream_t st) {
+  static size_t attr[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (p->smem > attr[dev]) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k_proto_colmax<U>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p->smem);
+    if (e) return e;
+    attr[dev] = p->smem;
+  }
+  const int grid = a.tiles < num_sms() ? a.tiles : num_sms();
+  k_proto_colmax<U><<<grid, 64 + 128 * a.ne * a.nh, p->smem, st>>>(*(const CUtensorMap *)p->tma_w,
+                                                                  *(const CUtensorMap *)p->tma_q, a);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_proto_colmax(const bnnk_proto_plan *p, int batch, const float *sx, const float *sw, float *colmax,
+                                 long long cws, float *part, int *err, bnn_stream_t st) {
+  if (batch <= 0) return 0;
+  if (batch > p->batch_cap || (!p->wt && !part)) return cudaErrorInvalidValue;
+  ProtoArgs a;
+  a.np = p->np;
+  a.batch = batch;
+  a.P = p->P;
+  a.wt = p->wt;
+  a.nch = p->nch;
+  a.cs = p->cs;
+  a.n_ct = p->wt ? (batch + p->wt - 1) / p->wt : batch * p->nch;
+  a.tiles = ((p->np + 127) / 128) * a.n_ct;
+  a.nkb = p->nkb;
+  a.stages = p->stages;
+  a.bn = p->bn;
+  a.acc_cols = p->acc_cols;
+  a.ne = 2;
+  // epilogue warps per lane quarter: one per window of a tile, at most 2
+  a.nh = p->wt ? (p->wt < 2 ? p->wt : 2) : 1;
+  a.tmem_alloc = 2 * p->acc_cols;  // a power of two: acc_cols is one and at most 256
+  a.idesc = p->idesc;
+  a.sx = sx;
+  a.sw = sw;
+  a.out = p->wt ? colmax : part;
+  a.ows = cws;
+  a.err = err;
+  int e = p->unit == 8 ? launch_colmax<8>(p, a, st) : launch_colmax<4>(p, a, st);
+  if (e || p->wt) return e;
+  const dim3 grid((p->np + 255) / 256, batch);
+  k_proto_chunks<<<grid, 256, 0, st>>>(batch, p->np, p->nch, part, sw, colmax, cws);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_proto_logits(int batch, int nc, int ppc, const float *colmax, long long cws, const float *cw,
+                                 const float *cb, float *logits, long long lws, int *status, int *fail, int w_base,
+                                 bnn_stream_t st) {
+  if (batch <= 0) return 0;
+  k_proto_logits<<<batch, 256, 0, st>>>(nc, ppc, colmax, cws, cw, cb, logits, lws, status, fail, w_base);
+  return cudaGetLastError();
+}

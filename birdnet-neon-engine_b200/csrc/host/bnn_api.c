@@ -52,7 +52,7 @@ static const struct { int mode; const char *name, *precision; } PATHS[] = {
 /* 1 when every op of path i has a GPU kernel here (the int8 path's ops, variant 0) */
 static int path_runs_here(const bnn_pkg *p, int i) {
   static const int codes[] = {BNN_OP_FE_STFT2, BNN_OP_C0POOL, BNN_OP_PW_S8, BNN_OP_DW3, BNN_OP_SE_GATE,
-                              BNN_OP_POSTPC, BNN_OP_GEMV_S8};
+                              BNN_OP_POSTPC, BNN_OP_GEMV_S8, BNN_OP_PROTO_S8};
   const bnn_path_rec *d = &p->paths[i];
   const uint8_t *q = p->map + d->ops_off, *end = q + d->ops_bytes;
   for (uint32_t k = 0; k < d->n_ops; k++) {
@@ -339,8 +339,22 @@ typedef struct {
   int kind;
 } dev_job;
 
+/* after a call's copy of the device words to err_host: a bounded wait that ran out (-1), a window that an op reported
+ * as failed (-2: PROTO_S8's non-finite logits, as rt_run / bnn_infer report it, src/bnneon.c:313-325), else 0; both
+ * words are reset */
 static int check_err_word(bnn_ctx *c, int di) {
   bnn_dev *dv = c->dev[di];
+  if (dv->err_host[1] != BNNK_NO_FAIL) {
+    const int w = dv->err_host[1];
+    dv->err_host[1] = BNNK_NO_FAIL;
+    cudaMemsetAsync(dv->err + 1, 0x7f, sizeof(int), (cudaStream_t)dv->stream);
+    int i = 0;
+    while (i < c->n_ops && c->ops[i].code != BNN_OP_PROTO_S8) i++;
+    ERR(BNN_ERR_WINDOW, "window not scored: op %d %s reported a failed window (code -2: non-finite values on the %s "
+        "path) for window %d of the call; hint: skip this window (the input itself is probably non-finite or extreme)",
+        i, i < c->n_ops ? c->ops[i].kname : "?", c->info.path, w);
+    return -2;
+  }
   if (*dv->err_host) {
     const int code = *dv->err_host;
     *dv->err_host = 0;
@@ -403,6 +417,7 @@ static void *dev_worker(void *a) {
   cudaStream_t cs = (cudaStream_t)dv->up_stream;
   for (int w = j->w0, k = 0, nb = 0; w < j->w1 && !e && !j->rc; w += nb, k ^= 1) {
     nb = next_chunk(j->w1 - w, c->batch, nb);
+    dv->w_base = w;
     float *buf = dv->up[k];
     e = cudaStreamWaitEvent(cs, (cudaEvent_t)dv->up_free[k], 0);
     if (!e) e = cudaMemcpyAsync(buf, j->pcm + (size_t)w * ns, sizeof(float) * (size_t)nb * ns,
@@ -424,7 +439,7 @@ static void *dev_worker(void *a) {
       e = cudaMemcpy2DAsync(j->emb + (size_t)w * ne, sizeof(float) * ne, dv->buf[d->emb_buf],
                             sizeof(float) * dv->ws[d->emb_buf], sizeof(float) * ne, nb, cudaMemcpyDeviceToHost, st);
   }
-  if (!e) e = cudaMemcpyAsync(dv->err_host, dv->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (!e) e = cudaMemcpyAsync(dv->err_host, dv->err, 2 * sizeof(int), cudaMemcpyDeviceToHost, st);
   if (!e) e = cudaStreamSynchronize(st);
   if (!e && cs) e = cudaStreamSynchronize(cs);
   if (e && !j->rc) {
@@ -433,10 +448,13 @@ static void *dev_worker(void *a) {
     snprintf(j->err, sizeof j->err, "window not scored: CUDA error %d (%s) on GPU %d; hint: check the GPU (nvidia-smi)",
              (int)e, cudaGetErrorString(e), dv->dev);
   }
-  if (!j->rc && check_err_word(c, j->di)) {
-    j->rc = -1;
-    snprintf(j->err, sizeof j->err, "%s", g_err);
-    j->kind = g_kind;
+  if (!j->rc) {
+    const int r = check_err_word(c, j->di);
+    if (r) {
+      j->rc = r;
+      snprintf(j->err, sizeof j->err, "%s", g_err);
+      j->kind = g_kind;
+    }
   }
   return NULL;
 }
@@ -457,7 +475,7 @@ int bnn_infer_batch(bnn_ctx *c, int n, const float *pcm, float *out, float *emb)
   for (int i = 0; i < nd; i++)
     if (jobs[i].rc) {
       ERR(jobs[i].kind ? jobs[i].kind : BNN_ERR_WINDOW, "%s", jobs[i].err);
-      return -1;
+      return jobs[i].rc == -2 ? -2 : -1;
     }
   return 0;
 }
@@ -479,6 +497,7 @@ int bnn_infer_device(bnn_ctx *c, int n, const float *d_pcm, float *d_out, float 
   const int nc = c->info.n_classes, ne = c->info.emb_dim;
   cudaStream_t st = stream ? (cudaStream_t)stream : (cudaStream_t)dv->stream;
   cudaSetDevice(dv->dev);
+  dv->w_base = 0;
   if (bnn_rt_launch(c, 0, n, d_pcm, 0, c->n_ops, st)) return -1;
   cudaError_t e = cudaMemcpy2DAsync(d_out, sizeof(float) * nc, dv->buf[d->out_buf], sizeof(float) * dv->ws[d->out_buf],
                                     sizeof(float) * nc, n, cudaMemcpyDeviceToDevice, st);
@@ -486,9 +505,12 @@ int bnn_infer_device(bnn_ctx *c, int n, const float *d_pcm, float *d_out, float 
     e = cudaMemcpy2DAsync(d_emb, sizeof(float) * ne, dv->buf[d->emb_buf], sizeof(float) * dv->ws[d->emb_buf],
                           sizeof(float) * ne, n, cudaMemcpyDeviceToDevice, st);
   if (!e && !stream) {
-    e = cudaMemcpyAsync(dv->err_host, dv->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    e = cudaMemcpyAsync(dv->err_host, dv->err, 2 * sizeof(int), cudaMemcpyDeviceToHost, st);
     if (!e) e = cudaStreamSynchronize(st);
-    if (!e && check_err_word(c, 0)) return -1;
+    if (!e) {
+      const int r = check_err_word(c, 0);
+      if (r) return r;
+    }
   }
   if (e) {
     ERR(BNN_ERR_WINDOW, "window not scored: CUDA error %d (%s); hint: check the GPU (nvidia-smi)", (int)e, cudaGetErrorString(e));
@@ -606,8 +628,9 @@ int bnn_debug_run_ops(bnn_ctx *c, int n, const float *pcm, int op0, int op1) {
     ERR(BNN_ERR_WINDOW, "bnn_debug_run_ops: input copy failed");
     return -1;
   }
+  dv->w_base = 0;
   if (bnn_rt_launch(c, 0, n, dv->buf[in], op0, op1, st)) return -1;
-  cudaError_t e = cudaMemcpyAsync(dv->err_host, dv->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+  cudaError_t e = cudaMemcpyAsync(dv->err_host, dv->err, 2 * sizeof(int), cudaMemcpyDeviceToHost, st);
   if (!e) e = cudaStreamSynchronize(st);
   if (e) { ERR(BNN_ERR_WINDOW, "bnn_debug_run_ops: CUDA error %d (%s)", (int)e, cudaGetErrorString(e)); return -1; }
   return check_err_word(c, 0);
@@ -787,6 +810,105 @@ void bnn_pw_s8_free(bnn_pw_s8 *o) {
   if (!o) return;
   cudaFree(o->op.w); cudaFree(o->op.sw); cudaFree(o->op.bias); cudaFree(o->op.cs);
   cudaFree(o->q); cudaFree(o->sa); cudaFree(o->za); cudaFree(o->err);
+  free(o);
+}
+
+/* ---- PROTO_S8 (src/rt_ops_s8n.c:212-250) */
+
+struct bnn_proto_s8 {
+  bnn_devop op;
+  int N, K, Kp, Np, nc, ppc, P, batch_cap;
+  int8_t *qa;
+  float *sx;
+  int *err;
+};
+
+bnn_proto_s8 *bnn_proto_s8_new(int N, int K, int Kp, int Np, const int8_t *qw, const float *sw, const uint8_t *n4,
+                               const float *cls_w, const float *cls_b, int nc, int ppc, float eps, int P,
+                               int batch_cap) {
+  /* the checks of proto8n_init and rt_proto_geom on the record's numbers (src/rt_ops_s8n.c:220-240,
+   * src/rt_ops_f32.c:525-535) */
+  if (!qw || !sw || !n4 || !cls_w || !cls_b || P <= 0 || P > 65536 || P % 4 || nc <= 0 || ppc < 1 || N <= 0 ||
+      N > (1 << 26) || K <= 0 || K > (1 << 17) || K % 8 || (long long)nc * ppc != N || Kp != ((K + 15) & ~15) ||
+      Np != ((N + 3) & ~3) || batch_cap <= 0) {
+    ERR(BNN_ERR_USAGE, "bnn_proto_s8_new: N %d K %d Kp %d Np %d P %d classes %d x %d batch %d (expected K %% 8 == 0, "
+        "K <= 2^17, Kp = K rounded up to 16, Np = N rounded up to 4, N = classes x prototypes per class, P %% 4 == 0)",
+        N, K, Kp, Np, P, nc, ppc, batch_cap);
+    return NULL;
+  }
+  const int bad = bnn_proto_n4_check(qw, Kp, n4, Np / 4);
+  if (bad >= 0) {
+    ERR(BNN_ERR_PACKAGE, "bnn_proto_s8_new: prototype panel %d is flagged for 4 products per int16 lane, but a lane's 4 "
+        "weights sum to more than 258 (the sums could wrap)", bad);
+    return NULL;
+  }
+  bnn_proto_s8 *o = calloc(1, sizeof *o);
+  if (!o) { ERR(BNN_ERR_OOM, "out of memory"); return NULL; }
+  o->N = N; o->K = K; o->Kp = Kp; o->Np = Np; o->nc = nc; o->ppc = ppc; o->P = P; o->batch_cap = batch_cap;
+  char err[512];
+  int kind = BNN_ERR_CPU;
+  if (bnn_proto_weights(&o->op, N, Kp, Np, qw, sw, cls_w, cls_b, nc, eps, err, sizeof err, &kind)) {
+    ERR(kind, "bnn_proto_s8_new: %s", err);
+    bnn_proto_s8_free(o);
+    return NULL;
+  }
+  const size_t cells = (size_t)batch_cap * P;
+  cudaError_t e = cudaMalloc((void **)&o->qa, cells * Kp);
+  if (!e) e = cudaMemset(o->qa, 0, cells * Kp);
+  if (!e) e = cudaMalloc((void **)&o->sx, sizeof(float) * cells);
+  if (!e) e = cudaMalloc((void **)&o->err, sizeof(int));
+  if (!e) e = cudaMemset(o->err, 0, sizeof(int));
+  if (!e) e = (cudaError_t)bnnk_proto_plan_init(&o->op.pplan, o->op.w, Np, Kp, o->qa, batch_cap, P);
+  if (!e && !o->op.pplan.wt)
+    e = cudaMalloc((void **)&o->op.f[0], sizeof(float) * (size_t)batch_cap * o->op.pplan.nch * Np);
+  if (e) {
+    ERR(e == cudaErrorMemoryAllocation ? BNN_ERR_OOM : BNN_ERR_CPU, "bnn_proto_s8_new: CUDA error %d (%s)", (int)e,
+        cudaGetErrorString(e));
+    bnn_proto_s8_free(o);
+    return NULL;
+  }
+  return o;
+}
+
+int bnn_proto_s8_run(bnn_proto_s8 *o, int B, const float *d_x, long long xws, int ld, float *d_logits, long long lws,
+                     float *d_colmax, long long cws, int *d_status, void *stream) {
+  if (!o || B < 0 || B > o->batch_cap || !d_x || !d_logits || !d_colmax || ld < o->K || lws < o->nc ||
+      cws < o->Np || (B > 1 && xws < (long long)o->P * ld)) {
+    ERR(BNN_ERR_USAGE, "bnn_proto_s8_run: B %d (capacity %d) ld %d logits stride %lld colmax stride %lld (expected "
+        "ld >= K, strides >= classes / Np, window stride >= P ld)", B, o ? o->batch_cap : 0, ld, lws, cws);
+    return -1;
+  }
+  bnn_stream_t st = (bnn_stream_t)stream;
+  int e = bnnk_proto_quant(B, o->P, d_x, xws, ld, o->K, o->Kp, o->op.eps, o->qa, o->sx, st);
+  if (!e) e = bnnk_proto_colmax(&o->op.pplan, B, o->sx, o->op.sw, d_colmax, cws, o->op.f[0], o->err, st);
+  if (!e) e = bnnk_proto_logits(B, o->nc, o->ppc, d_colmax, cws, o->op.f[1], o->op.f[2], d_logits, lws, d_status, NULL, 0,
+                                st);
+  return launch_rc("bnn_proto_s8_run", e);
+}
+
+int bnn_proto_s8_read_scratch(bnn_proto_s8 *o, int B, int8_t *qa, float *sx) {
+  if (!o || B < 0 || B > o->batch_cap) {
+    ERR(BNN_ERR_USAGE, "bnn_proto_s8_read_scratch: NULL op or B %d outside 0..%d", B, o ? o->batch_cap : 0);
+    return -1;
+  }
+  const size_t cells = (size_t)B * o->P;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (!e && qa) e = cudaMemcpy(qa, o->qa, cells * o->Kp, cudaMemcpyDeviceToHost);
+  if (!e && sx) e = cudaMemcpy(sx, o->sx, sizeof(float) * cells, cudaMemcpyDeviceToHost);
+  return launch_rc("bnn_proto_s8_read_scratch", e);
+}
+
+int bnn_proto_s8_error(bnn_proto_s8 *o) {
+  int v = 0;
+  if (o && o->err) cudaMemcpy(&v, o->err, sizeof v, cudaMemcpyDeviceToHost);
+  return v;
+}
+
+void bnn_proto_s8_free(bnn_proto_s8 *o) {
+  if (!o) return;
+  cudaFree(o->op.w); cudaFree(o->op.sw);
+  for (int k = 0; k < 6; k++) cudaFree(o->op.f[k]);
+  cudaFree(o->qa); cudaFree(o->sx); cudaFree(o->err);
   free(o);
 }
 

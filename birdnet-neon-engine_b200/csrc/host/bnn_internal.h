@@ -66,8 +66,11 @@ typedef struct {
   int32_t *cs;
   bnnk_gemm_plan plan;
   int kq;
-  /* DW3, SE_GATE, C0POOL, POSTPC */
+  /* DW3, SE_GATE, C0POOL, POSTPC; PROTO_S8: f[0] chunk maxima scratch, f[1] class weights, f[2] class biases */
   float *f[6];
+  /* PROTO_S8: prototype rows w [Np][Kp], sw, the GEMM plan, eps */
+  bnnk_proto_plan pplan;
+  float eps;
 } bnn_devop;
 
 typedef struct {
@@ -82,8 +85,10 @@ typedef struct {
   int8_t *q;            /* int8 GEMM scratch: [batch * rows][kq] */
   float *sa, *fe_minmax, *pcin;
   int32_t *za;
-  int *err;             /* device error word */
-  int *err_host;        /* pinned */
+  int *err;             /* device words: [0] the error word of the bounded waits, [1] the smallest failed window index
+                         * of the call (BNNK_NO_FAIL if none; set by PROTO_S8's logits) */
+  int *err_host;        /* pinned copy of both */
+  int w_base;           /* index of the launch's first window in the caller's call (failed-window reports) */
   bnnk_fe_tables fe;
   void *fe_mem[32];     /* the front-end tables: 9 per spectrogram */
   int n_fe_mem;
@@ -127,6 +132,9 @@ int c0_quantizes_next(const bnn_ctx *c, int i);
 void bnn_rt_close(bnn_ctx *c);
 int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src, const float *sw_src,
                    const int32_t *cs_src, const float *b_src, char *err, size_t errlen, int *kind);
+int bnn_proto_weights(bnn_devop *d, int N, int Kp, int Np, const int8_t *src, const float *sw_src, const float *cw,
+                      const float *cb, int nc, float eps, char *err, size_t errlen, int *kind);
+int bnn_proto_n4_check(const int8_t *qw, int Kp, const uint8_t *n4, int npanels);
 
 /* errors (bnn_api.c): thread-local message and kind */
 void bnn_set_error(int kind, const char *fmt, ...) __attribute__((format(printf, 2, 3)));

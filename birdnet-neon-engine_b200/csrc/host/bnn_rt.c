@@ -258,6 +258,50 @@ static int init_fe_stft2(vctx *v) { /* fe_stft2_init, src/rt_ops_f32.c:25-40 */
   return vneed(v, 0, BNN_F32, 144000) || vneed(v, 1, BNN_F32, (size_t)96 * 511 * 2) ? -1 : 0;
 }
 
+/* pc_proto_n4_check (src/proto_s8n.c:110-128): the first 4-prototype panel flagged for 4 products per int16 lane in
+ * which some lane's 4 weights (bytes l, l + 8 of two consecutive 16-byte steps of one prototype) have sum |w| > 258
+ * (|w| as an unsigned byte: -128 counts 128); -1 if none or Kp % 32 != 0 */
+int bnn_proto_n4_check(const int8_t *qw, int Kp, const uint8_t *n4, int npanels) {
+  if (Kp % 32) return -1;
+  for (int pn = 0; pn < npanels; pn++) {
+    if (!n4[pn]) continue;
+    const int8_t *w = qw + (size_t)pn * Kp * 4;
+    for (int k = 0; k < Kp; k += 32, w += 128)
+      for (int ch = 0; ch < 4; ch++)
+        for (int l = 0; l < 8; l++) {
+          const int8_t *a = w + 16 * ch, *b = w + 64 + 16 * ch;
+          const unsigned sum = (uint8_t)abs(a[l]) + (uint8_t)abs(a[l + 8]) + (uint8_t)abs(b[l]) + (uint8_t)abs(b[l + 8]);
+          if (sum > 258) return pn;
+        }
+  }
+  return -1;
+}
+
+static int init_proto_s8(vctx *v) { /* proto8n_init (src/rt_ops_s8n.c:220-240) after rt_proto_geom / rt_proto_io
+                                     * (src/rt_ops_f32.c:525-545) */
+  if (vneed_args(v, 4, 6, 9)) return -1;
+  const int *p = v->op->p;
+  const int N = p[0], K = p[1], Kp = p[2], Np = p[3], P = p[4], C = p[5], ld = p[6], nc = p[7], ppc = p[8];
+  VREQ(v, P > 0 && P <= 65536 && nc > 0 && ppc >= 1);
+  VREQ(v, N > 0 && N <= (1 << 26) && K > 0 && K <= (1 << 17));
+  VREQ(v, K == C);
+  VREQ(v, ld >= C);
+  VREQ(v, (size_t)nc * ppc == (size_t)N);
+  VREQ(v, C % 8 == 0 && Kp == ((K + 15) & ~15));
+  VREQ(v, P % 4 == 0 && Np == ((N + 3) & ~3));
+  if (vneed_t(v, 0, (size_t)Np * Kp, 0) || vneed_t(v, 1, (size_t)Np * 4, 1) || vneed_t(v, 2, (size_t)Np / 4, 1))
+    return -1;
+  if (vneed_t(v, 3, (size_t)N * 4, 0) || vneed_t(v, 4, (size_t)nc * 4, 0) || vneed_t(v, 5, 4, 0)) return -1;
+  if (vneed_nohalo(v, 0, BNN_F32, (size_t)P * ld) || vneed(v, 1, BNN_F32, (size_t)nc)) return -1;
+  if (vneed(v, 2, BNN_I8, (size_t)P * Kp) || vneed(v, 3, BNN_F32, (size_t)Np)) return -1;
+  const int bad = bnn_proto_n4_check(vt(v, 0, NULL), Kp, vt(v, 2, NULL), Np / 4);
+  if (bad >= 0)
+    return vbad(v, "prototype panel %d is flagged for 4 products per int16 lane, but a lane's 4 weights sum to more "
+                "than 258 (the sums could wrap)", bad);
+  if (P > 256) v->c->launches += 1; /* the chunk maxima */
+  return 0;
+}
+
 /* the registry of this library: (base opcode, variant 0) -> kernel; outmask / optmask as the reference's
  * (src/rt_ops_f32.c:620-637, src/rt_ops_s8n.c:255-260) */
 typedef struct {
@@ -275,6 +319,7 @@ static const kdesc KERNELS[] = {
     {BNN_OP_SE_GATE, "se_gate_f32", init_se_gate, 0x2, 0, 1},
     {BNN_OP_PW_S8, "pw_s8n", init_pw_s8, 0x3a, 0x44, 2},
     {BNN_OP_GEMV_S8, "gemv_s8n", init_gemv_s8, 0x1e, 0, 2},
+    {BNN_OP_PROTO_S8, "proto_s8n", init_proto_s8, 0xe, 0, 3},
 };
 static const kdesc *kernel_for(int code) {
   if (code >> 8) return NULL; /* variants 1 and 2 are the fp16 / dotprod CPU paths: no GPU kernels */
@@ -377,7 +422,8 @@ int bnn_rt_open(bnn_ctx *c, char *err, size_t errlen, int *kind) {
       if (bnn_meta_str(c->pkg, "compiler", comp, sizeof comp) < 0) snprintf(comp, sizeof comp, "unknown");
       *kind = BNN_ERR_CPU;
       return vbad(&v, "opcode 0x%x (base %d variant %d) has no B200 kernel in this library (it runs the neon-int8 ops "
-                  "FE_STFT2, C0POOL, PW_S8, DW3, SE_GATE, POSTPC and GEMV_S8; the package was written by compiler '%s')",
+                  "FE_STFT2, C0POOL, PW_S8, DW3, SE_GATE, POSTPC, GEMV_S8 and PROTO_S8; the package was written by compiler "
+                  "'%s')",
                   op->code, op->code & 0xff, var, comp);
     }
     op->kname = k->name;
@@ -425,21 +471,28 @@ static int upload(void **dst, const void *src, size_t bytes, char *err, size_t e
   if (bytes) CK(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice), "weight upload (cudaMemcpy)");
   return 0;
 }
+/* the buffer arguments [lo, lo + n) of an op that the device scratch replaces: PW_S8 b[3..5], GEMV_S8 b[2..4] (q, sa,
+ * za), PROTO_S8 b[2] (the quantized cells) */
+static void scratch_args(const bnn_op *op, int *lo, int *n) {
+  *lo = op->code == BNN_OP_PW_S8 ? 3 : op->code == BNN_OP_GEMV_S8 || op->code == BNN_OP_PROTO_S8 ? 2 : -1;
+  *n = op->code == BNN_OP_PROTO_S8 ? 1 : 3;
+}
 static int is_int8_scratch(const bnn_ctx *c, int buf) {
-  /* PW_S8 b[3..5], GEMV_S8 b[2..4]: replaced by the device scratch */
   for (int i = 0; i < c->n_ops; i++) {
     const bnn_op *op = &c->ops[i];
-    int lo = op->code == BNN_OP_PW_S8 ? 3 : op->code == BNN_OP_GEMV_S8 ? 2 : -1;
+    int lo, n;
+    scratch_args(op, &lo, &n);
     for (int a = 0; a < op->nb; a++) {
       if (op->b[a] != buf) continue;
-      if (lo < 0 || a < lo || a > lo + 2) return 0;
+      if (lo < 0 || a < lo || a >= lo + n) return 0;
     }
   }
   for (int i = 0; i < c->n_ops; i++) {
     const bnn_op *op = &c->ops[i];
-    const int lo = op->code == BNN_OP_PW_S8 ? 3 : op->code == BNN_OP_GEMV_S8 ? 2 : -1;
+    int lo, n;
+    scratch_args(op, &lo, &n);
     if (lo >= 0)
-      for (int a = lo; a < lo + 3; a++)
+      for (int a = lo; a < lo + n; a++)
         if (op->b[a] == buf) return 1;
   }
   return 0;
@@ -588,6 +641,29 @@ int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src
   return rc;
 }
 
+/* PROTO_S8 tensors in the kernels' layouts: the package's prototype panels [Np/4][Kp/16][4][16] (lower.py
+ * proto_s8n) as rows [Np][Kp]; sw [Np]; class weights [N], biases [nc]; eps */
+int bnn_proto_weights(bnn_devop *d, int N, int Kp, int Np, const int8_t *src, const float *sw_src, const float *cw,
+                      const float *cb, int nc, float eps, char *err, size_t errlen, int *kind) {
+  int8_t *w = malloc((size_t)Np * Kp);
+  if (!w) {
+    *kind = BNN_ERR_OOM;
+    snprintf(err, errlen, "out of memory (prototypes, %d x %d)", Np, Kp);
+    return -1;
+  }
+  for (int j = 0; j < Np; j++)
+    for (int k = 0; k < Kp; k++)
+      w[(size_t)j * Kp + k] = src[(((size_t)(j / 4) * (Kp / 16) + k / 16) * 4 + j % 4) * 16 + k % 16];
+  int rc = upload((void **)&d->w, w, (size_t)Np * Kp, err, errlen, kind);
+  free(w);
+  if (!rc) rc = upload((void **)&d->sw, sw_src, sizeof(float) * Np, err, errlen, kind);
+  if (!rc) rc = upload((void **)&d->f[1], cw, sizeof(float) * N, err, errlen, kind);
+  if (!rc) rc = upload((void **)&d->f[2], cb, sizeof(float) * nc, err, errlen, kind);
+  d->kq = Kp;
+  d->eps = eps;
+  return rc;
+}
+
 /* the weights of op i in the kernels' layouts */
 static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, int *kind) {
   const bnn_op *op = &c->ops[i];
@@ -632,6 +708,9 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
   }
   case BNN_OP_FE_STFT2:
     return fe_tables(c, dv, op, err, errlen, kind);
+  case BNN_OP_PROTO_S8:
+    return bnn_proto_weights(d, p[0], p[2], p[3], tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 3), tptr(c, op, 4),
+                             p[7], ((const float *)tptr(c, op, 5))[0], err, errlen, kind);
   default:
     return 0;
   }
@@ -701,9 +780,9 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
   size_t qbytes = 256, rows = 8;
   for (int i = 0; i < c->n_ops; i++) {
     const bnn_op *op = &c->ops[i];
-    if (op->code != BNN_OP_PW_S8 && op->code != BNN_OP_GEMV_S8) continue;
-    const size_t r = (size_t)B * (op->code == BNN_OP_PW_S8 ? (size_t)op->p[4] : 1);
-    const size_t qb = r * R32(op->p[1]);
+    if (op->code != BNN_OP_PW_S8 && op->code != BNN_OP_GEMV_S8 && op->code != BNN_OP_PROTO_S8) continue;
+    const size_t r = (size_t)B * (op->code == BNN_OP_GEMV_S8 ? 1 : (size_t)op->p[4]);
+    const size_t qb = r * (op->code == BNN_OP_PROTO_S8 ? (size_t)op->p[2] : (size_t)R32(op->p[1]));
     if (qb > qbytes) qbytes = qb;
     if (r > rows) rows = r;
   }
@@ -713,9 +792,12 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
   CK(cudaMalloc((void **)&dv->za, sizeof(int32_t) * rows), "int8 zero-point scratch");
   CK(cudaMalloc((void **)&dv->fe_minmax, sizeof(float) * 2 * B), "front-end scratch");
   CK(cudaMalloc((void **)&dv->pcin, sizeof(float) * 6 * 1728 * B), "post-conv scratch");
-  CK(cudaMalloc((void **)&dv->err, sizeof(int)), "error word");
+  CK(cudaMalloc((void **)&dv->err, 2 * sizeof(int)), "error word");
   CK(cudaMemset(dv->err, 0, sizeof(int)), "error word");
-  CK(cudaMallocHost((void **)&dv->err_host, sizeof(int)), "error word (host)");
+  CK(cudaMemset(dv->err + 1, 0x7f, sizeof(int)), "error word");
+  CK(cudaMallocHost((void **)&dv->err_host, 2 * sizeof(int)), "error word (host)");
+  dv->err_host[0] = 0;
+  dv->err_host[1] = BNNK_NO_FAIL;
   /* weights and GEMM plans */
   for (int i = 0; i < c->n_ops; i++) {
     if (op_weights(c, dv, i, err, errlen, kind)) return -1;
@@ -728,6 +810,16 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
         snprintf(err, errlen, "op %d %s: TMA descriptors could not be made (driver too old?)", i, op->kname);
         return -1;
       }
+    }
+    if (op->code == BNN_OP_PROTO_S8) {
+      bnn_devop *o = &dv->ops[i];
+      if (bnnk_proto_plan_init(&o->pplan, o->w, op->p[3], op->p[2], dv->q, B, op->p[4])) {
+        *kind = BNN_ERR_CPU;
+        snprintf(err, errlen, "op %d %s: TMA descriptors could not be made (driver too old?)", i, op->kname);
+        return -1;
+      }
+      if (!o->pplan.wt)
+        CK(cudaMalloc((void **)&o->f[0], sizeof(float) * (size_t)B * o->pplan.nch * op->p[3]), "prototype scratch");
     }
   }
   CK(cudaDeviceSynchronize(), "device set-up");
@@ -852,6 +944,13 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
       break;
     case BNN_OP_POSTPC:
       rc = bnnk_postpc(n, IN_(0), INWS(0), o->f[2], o->f[3], o->f[0], o->f[1], dv->pcin, B_(1), WS(1), st);
+      break;
+    case BNN_OP_PROTO_S8:
+      rc = bnnk_proto_quant(n, p[4], IN_(0), INWS(0), p[6], p[5], p[2], o->eps, dv->q, dv->sa, st);
+      if (!rc) rc = bnnk_proto_colmax(&o->pplan, n, dv->sa, o->sw, B_(3), WS(3), o->f[0], dv->err, st);
+      if (!rc)
+        rc = bnnk_proto_logits(n, p[7], p[8], B_(3), WS(3), o->f[1], o->f[2], B_(1), WS(1), NULL, dv->err + 1,
+                               dv->w_base, st);
       break;
     default:
       rc = cudaErrorNotSupported;

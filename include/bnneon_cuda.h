@@ -25,10 +25,13 @@ extern "C" {
 
 /* n windows of host memory: pcm [n][n_samples] -> out [n][n_classes], emb [n][emb_dim] (emb may be NULL). The
  * windows are split into contiguous slices over the context's GPUs (bnn_set_threads) and into chunks of the batch
- * capacity (bnn_set_batch). Synchronous. */
+ * capacity (bnn_set_batch). Synchronous. Returns -2 (kind BNN_ERR_WINDOW, as bnn_infer on a failed window,
+ * src/bnneon.c:313-325) when an op reported a failed window (the prototype head's non-finite logits); the message
+ * names the first such window, and the other windows' outputs are still written. */
 int bnn_infer_batch(bnn_ctx *ctx, int n, const float *pcm, float *out, float *emb);
 /* the same with device-resident buffers on the context's first GPU (n <= the batch capacity); asynchronous on
- * `stream` (NULL = the context's own stream, synchronized before return) */
+ * `stream` (NULL = the context's own stream, synchronized before return, failed windows reported as above; with a
+ * caller's stream they are reported by the context's next synchronous call) */
 int bnn_infer_device(bnn_ctx *ctx, int n, const float *d_pcm, float *d_out, float *d_emb, void *stream);
 /* windows per launch sequence on each GPU (default 256, or the BNN_BATCH environment variable): sizes the device
  * arena; 0 on success */
@@ -101,6 +104,28 @@ int bnn_pw_s8_run_static(bnn_pw_s8 *op, int B, int Mw, const float *d_x, long lo
 /* the device error word of the op's GEMM (0 = no bounded wait ran out) */
 int bnn_pw_s8_error(bnn_pw_s8 *op);
 void bnn_pw_s8_free(bnn_pw_s8 *op);
+
+/* PROTO_S8, the int8 prototype head (src/rt_ops_s8n.c:212-250: pc_quant_cells_f32 and pc_proto_colmax_s8n,
+ * src/proto_s8n.c:28-164, then pc_proto_logits, src/pc_kern_f32.c:364-376), batched. The package's tensors (host
+ * pointers): prototypes qw [Np/4][Kp/16][4][16] int8, sw [Np], n4 [Np/4] (checked as pc_proto_n4_check does; the GPU
+ * sums never wrap, so the flags only gate loading), class weights cls_w [N = nc x ppc], biases cls_b [nc], eps; P
+ * cells of K = C channels per window (K % 8 == 0, P % 4 == 0), up to batch_cap windows per run. */
+typedef struct bnn_proto_s8 bnn_proto_s8;
+bnn_proto_s8 *bnn_proto_s8_new(int N, int K, int Kp, int Np, const int8_t *qw, const float *sw, const uint8_t *n4,
+                               const float *cls_w, const float *cls_b, int nc, int ppc, float eps, int P,
+                               int batch_cap);
+/* B windows of cells d_x [B][P][ld] (window stride xws floats) -> d_colmax [B][cws] (the column maxima, Np per
+ * window) and d_logits [B][lws] (nc per window). d_status [B] (or NULL): -2 for a window whose logits failed the
+ * finite check (where pc_proto_logits returns -2), else 0. */
+int bnn_proto_s8_run(bnn_proto_s8 *op, int B, const float *d_x, long long xws, int ld, float *d_logits, long long lws,
+                     float *d_colmax, long long cws, int *d_status, void *stream);
+/* copies the op's own device scratch as the last run of B windows left it to host memory (synchronous; either pointer
+ * may be NULL): the quantized cells qa [B * P][Kp] int8 and their scales sx [B * P] (the reference's qa buffer and
+ * per-cell scale state) */
+int bnn_proto_s8_read_scratch(bnn_proto_s8 *op, int B, int8_t *qa, float *sx);
+/* the device error word of the op's GEMM (0 = no bounded wait ran out) */
+int bnn_proto_s8_error(bnn_proto_s8 *op);
+void bnn_proto_s8_free(bnn_proto_s8 *op);
 
 /* DW3 (src/gemm_f32.c:398-411, dw3x3_f32), batched: d_xp [B][(H+2)(W+2)][C] (zero halo 1), d_w [9][C], d_b [C] ->
  * d_out [B][Ho Wo][C], d_chsum [B][C]. A bounded device wait that ran out is reported by bnn_cuda_op_error. */

@@ -47,6 +47,14 @@ static inline int32_t emu_cvtzs(float x) {
   if (x <= -2147483904.0f) return INT32_MIN;
   return (int32_t)x;
 }
+/* FCVTAS (vcvtaq_s32_f32): nearest with ties away from zero, saturating to int32, NaN -> 0 */
+static inline int32_t emu_cvtas(float x) {
+  if (x != x) return 0;
+  float r = roundf(x); /* C roundf: halfway cases away from zero */
+  if (r >= 2147483648.0f) return INT32_MAX;
+  if (r < -2147483648.0f) return INT32_MIN;
+  return (int32_t)r;
+}
 /* glibc lrintf on AArch64 (FRINTX + FCVTZS to 64 bits), then the C conversion to int32_t (modulo 2^32). The
  * reference only reaches values well inside int64. */
 static inline int32_t emu_lrintf_i32(float x) {

@@ -63,6 +63,29 @@ bnno_fe *bnno_fe_new(const float *win1, const float *win2, const float *mel1, co
 void bnno_fe_run(const bnno_fe *f, const float *pcm, float *img);
 void bnno_fe_free(bnno_fe *f);
 
+/* ---- the int8 prototype head PROTO_S8 (src/proto_s8n.c, src/rt_ops_s8n.c:212-250, src/pc_kern_f32.c:364-376) */
+/* pc_quant_cells_f32: x [P][ld] -> qa [P][Kp] (ties away, never -128, zero past C), sx [P]; C % 8 == 0 */
+void bnno_proto_quant_cells(const float *x, int P, int C, int ld, float eps, int8_t *qa, int Kp, float *sx);
+/* the package's prototype bytes [Np/4][Kp/16][4][16] -> rows [Np][Kp] */
+void bnno_proto_unpack(const int8_t *qw, int Np, int Kp, int8_t *rows);
+/* pc_proto_colmax_s8n: colmax[j] = sw[j] * max_p (float)(qa[p] . w[j]) * sx[p]; packed or unpacked prototypes */
+void bnno_proto_colmax(const int8_t *qa, int Kp, const float *sx, int P, const int8_t *qw, const float *sw, int Np,
+                       float *colmax);
+void bnno_proto_colmax_rows(const int8_t *qa, int Kp, const float *sx, int P, const int8_t *rows, const float *sw,
+                            int Np, float *colmax);
+/* pc_proto_logits: 0, or -2 when a logit is not finite or above 3e38 in magnitude */
+int bnno_proto_logits(const float *colmax, const float *w, const float *b, int nc, int ppc, float *logits);
+/* pc_proto_n4_check: the first flagged 4-prototype panel whose int16 lanes could wrap, or -1 */
+int bnno_proto_n4_check(const int8_t *qw, int Kp, const uint8_t *n4, int npanels);
+/* the whole op on one window (prototype rows unpacked); 0 or -2 */
+int bnno_proto_s8(const float *x, int P, int C, int ld, float eps, const int8_t *rows, const float *sw, int Np, int Kp,
+                  const float *cls_w, const float *cls_b, int nc, int ppc, int8_t *qa, float *sx, float *colmax,
+                  float *logits);
+/* n windows at window stride xws on `threads` threads: logits [n][nc]; 0 or -2 */
+int bnno_proto_s8_many(int n, int threads, const float *x, long long xws, int P, int C, int ld, float eps,
+                       const int8_t *rows, const float *sw, int Np, int Kp, const float *cls_w, const float *cls_b,
+                       int nc, int ppc, float *logits);
+
 /* ---- a .bnpk package run on the CPU, window by window (the executor of src/rt_pkg.c:528-542) */
 typedef struct bnno_pkg bnno_pkg;
 /* path: the package; path_name: the package path to run ("neon-int8"). NULL on failure (err filled). */

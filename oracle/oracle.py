@@ -22,6 +22,13 @@ SIGS = {
     "bnno_se_gate": (None, [_I, _I, _P, _P, _P, _P, _P, _I, _P]),
     "bnno_c0pool": (None, [_P, _P, _P, _P]),
     "bnno_postpc": (None, [_P, _P, _P, _P, _P, _P]),
+    "bnno_proto_quant_cells": (None, [_P, _I, _I, _I, _F, _P, _I, _P]),
+    "bnno_proto_unpack": (None, [_P, _I, _I, _P]),
+    "bnno_proto_colmax": (None, [_P, _I, _P, _I, _P, _P, _I, _P]),
+    "bnno_proto_colmax_rows": (None, [_P, _I, _P, _I, _P, _P, _I, _P]),
+    "bnno_proto_logits": (_I, [_P, _P, _P, _I, _I, _P]),
+    "bnno_proto_n4_check": (_I, [_P, _I, _P, _I]),
+    "bnno_proto_s8_many": (_I, [_I, _I, _P, ctypes.c_longlong, _I, _I, _I, _F, _P, _P, _I, _I, _P, _P, _I, _I, _P]),
     "bnno_pkg_open": (_P, [_S, _S, _S, _SZ]), "bnno_pkg_close": (None, [_P]),
     "bnno_pkg_n_ops": (_I, [_P]), "bnno_pkg_n_bufs": (_I, [_P]), "bnno_pkg_op_code": (_I, [_P, _I]),
     "bnno_pkg_buf_elems": (_L, [_P, _I, _P]), "bnno_pkg_out_elems": (_I, [_P]), "bnno_pkg_emb_elems": (_I, [_P]),
@@ -55,6 +62,40 @@ def fn(name, x):
     f = getattr(lib(), name)
     x = np.asarray(x, np.float32).reshape(-1)
     return np.array([f(float(v)) for v in x], np.float32)
+
+
+def proto_unpack(qp):
+    """The package's prototype panels [Np/4][Kp/16][4][16] as rows [Np][Kp]."""
+    qp = np.ascontiguousarray(qp, np.int8)
+    n_pad, k_pad = qp.shape[0] * 4, qp.shape[1] * 16
+    rows = np.empty((n_pad, k_pad), np.int8)
+    lib().bnno_proto_unpack(ptr(qp), n_pad, k_pad, ptr(rows))
+    return rows
+
+
+def proto_s8(x, rows, sw, cls_w, cls_b, eps, C, Kp):
+    """PROTO_S8 on windows x [B][P][ld] with prototype rows [Np][Kp]: (qa [B][P][Kp], sx [B][P], colmax [B][Np],
+    logits [B][nc], status [B]: 0 or -2), window by window."""
+    x = np.ascontiguousarray(x, np.float32)
+    B, P, ld = x.shape
+    rows = np.ascontiguousarray(rows, np.int8)
+    Np = rows.shape[0]
+    sw = np.ascontiguousarray(sw, np.float32)
+    cls_w = np.ascontiguousarray(cls_w, np.float32).reshape(-1)
+    cls_b = np.ascontiguousarray(cls_b, np.float32)
+    nc = cls_b.shape[0]
+    ppc = cls_w.shape[0] // nc
+    qa = np.zeros((B, P, Kp), np.int8)
+    sx = np.zeros((B, P), np.float32)
+    cm = np.zeros((B, Np), np.float32)
+    lg = np.zeros((B, nc), np.float32)
+    st = np.zeros(B, np.int32)
+    h = lib()
+    for w in range(B):
+        h.bnno_proto_quant_cells(ptr(x[w]), P, C, ld, float(eps), ptr(qa[w]), Kp, ptr(sx[w]))
+        h.bnno_proto_colmax_rows(ptr(qa[w]), Kp, ptr(sx[w]), P, ptr(rows), ptr(sw), Np, ptr(cm[w]))
+        st[w] = h.bnno_proto_logits(ptr(cm[w]), ptr(cls_w), ptr(cls_b), nc, ppc, ptr(lg[w]))
+    return qa, sx, cm, lg, st
 
 
 class Package:

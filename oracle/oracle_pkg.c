@@ -176,6 +176,16 @@ static int run_op(bnno_pkg *p, const o_op *op) {
   case 6: /* POSTPC: b = [X, feat, pcin, pcout] */
     bnno_postpc(bptr(p, op, 0), tdata(p, op, 0), tdata(p, op, 1), tdata(p, op, 2), tdata(p, op, 3), bptr(p, op, 1));
     return 0;
+  case 35: { /* PROTO_S8: b = [x, logits, qa, colmax]; t = [qw, sw, n4, cls w, cls b, eps];
+             * p = [N K Kp Np P C ld nc ppc] */
+    float *sx = malloc(sizeof(float) * (size_t)P[4]);
+    if (!sx) return -1;
+    const float *eps = tdata(p, op, 5);
+    bnno_proto_quant_cells(bptr(p, op, 0), P[4], P[5], P[6], eps[0], bptr(p, op, 2), P[2], sx);
+    bnno_proto_colmax(bptr(p, op, 2), P[2], sx, P[4], tdata(p, op, 0), tdata(p, op, 1), P[3], bptr(p, op, 3));
+    free(sx);
+    return bnno_proto_logits(bptr(p, op, 3), tdata(p, op, 3), tdata(p, op, 4), P[7], P[8], bptr(p, op, 1));
+  }
   default:
     return -1;
   }

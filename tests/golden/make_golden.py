@@ -10,7 +10,10 @@ packages.json; tests/test_package_golden.py checks that bnneon_b200.synth writes
 and kernels run on the reference compiler's bytes without the reference being present.
 
 It also records the reference packer's output for a few weight matrices (s8_tensors, quant_rows_s8) in
-s8_packing.npz.
+s8_packing.npz, and for the int8 prototype head (PROTO_S8): the reference lowering's own proto_s8n packs seeded
+prototype heads into one-op neon-int8 packages (sha256 in proto_packages.json; bnneon_b200.synth.write_proto_package
+must write the same bytes) and its packer (quant_rows_s8, n4_panel_flags, the [Np/4][Kp/16][4][16] layout) runs on
+fixed matrices (proto_packing.npz).
 """
 import hashlib
 import json
@@ -43,6 +46,80 @@ def reference_package(ref_root, ir, dst):
         pkg.set(k, v)
     pkg.write(dst)
     return n_classes, emb_dim
+
+
+# the prototype-head packages the tests use: (name, seed, cells, channels, classes, prototypes per class, ld, eps)
+PROTO_HEADS = (("proto_small", 11, 8, 40, 10, 3, 40, 1e-6),
+               ("proto_ld", 12, 12, 64, 25, 4, 72, 1e-3),
+               ("proto_wide", 13, 300, 96, 9, 2, 96, 1e-6),
+               ("proto_mid", 14, 64, 256, 130, 4, 256, 1e-6))
+
+
+def reference_proto_package(ref_root, head, ld, dst):
+    """The reference lowering's PROTO_S8 record (lower.py proto_s8n -> emit_proto) on the input window taken as the
+    cells, in a one-op neon-int8 package."""
+    sys.path.insert(0, os.path.join(ref_root, "python"))
+    from bnneon.compiler import lower, pkgfmt  # pylint: disable=import-outside-toplevel
+    n, c = head["P"].shape
+    nc, ppc = head["cw"].shape
+    ns = head["n_cells"] * ld
+    pkg = pkgfmt.Package()
+    lw = lower.Lowering(pkg, [], synth.PATH, ns)
+    o = {"P": head["P"], "cw": head["cw"], "cb": head["cb"], "eps": head["eps"], "out": "logits"}
+    lw.proto_s8n(0, o, 0, head["n_cells"], c, ld, n, nc, ppc)
+    ob = lw.vbuf["logits"]
+    bufs, _ = lower.plan_slots(lw.bufs, lw.out, [ob])
+    pkg.add_path(synth.PATH, lower.path_info(synth.PATH).hwcap, bufs, lw.out, 0, ob, None)
+    pkg.set(f"src_nodes/{synth.PATH}", "\n".join(lw.src))
+    for k, v in synth.metadata(nc, 0, synth.labels_for(nc), model_id="perch_v2_proto_head_synthetic",
+                               family=synth.BNN_MODEL_PERCH_V2, sample_rate=synth.PERCH_SAMPLE_RATE, n_samples=ns,
+                               attribution="synthetic prototype head (random weights)"):
+        pkg.set(k, v)
+    pkg.write(dst)
+
+
+def proto_fixtures(ref_root):
+    sys.path.insert(0, os.path.join(ref_root, "python"))
+    from bnneon.compiler import lower  # pylint: disable=import-outside-toplevel
+    out = {}
+    with tempfile.TemporaryDirectory() as td:
+        for name, seed, p_cells, c, nc, ppc, ld, eps in PROTO_HEADS:
+            head = synth.proto_head(seed, p_cells, c, nc, ppc, eps)
+            ref = os.path.join(td, name + ".ref.bnpk")
+            reference_proto_package(ref_root, head, ld, ref)
+            mine = os.path.join(td, name + ".mine.bnpk")
+            synth.write_proto_package(mine, head, ld)
+            out[name] = dict(seed=seed, cells=p_cells, channels=c, classes=nc, ppc=ppc, ld=ld, eps=eps,
+                             size=os.path.getsize(ref), sha256=sha(ref))
+            print(name, out[name], "writer matches" if sha(mine) == sha(ref) else "WRITER DIFFERS")
+    with open(os.path.join(HERE, "proto_packages.json"), "w", encoding="utf-8") as f:
+        json.dump(out, f, indent=1, sort_keys=True)
+        f.write("\n")
+    # the reference packer on fixed matrices: random rows, a zero row, rows that tie at .5, rows whose 32-byte steps
+    # overflow an int16 lane of the n=4 loop, and K not a multiple of 32 (no n4 panels)
+    rng = np.random.default_rng(21)
+    arrays = {}
+    mats = [(rng.standard_normal((10, 64)) * 0.5).astype(np.float32),
+            (rng.standard_normal((7, 40)) * 2.0).astype(np.float32),
+            np.tile(np.array([[2.5, -2.5, 0.5, 1.0] * 16], np.float32), (8, 1)),
+            np.concatenate([np.full((4, 96), 1.0, np.float32), (rng.standard_normal((4, 96)) * 0.1).astype(np.float32)]),
+            (rng.standard_normal((12, 128)) * 0.3).astype(np.float32)]
+    mats[0][3, :] = 0.0
+    mats[2][:, 1] = 127.0   # the row maximum: 127 maps to 127 and the rest to (ties) 2.5, 0.5 -> 3, 1
+    mats[4][:4, :32] = 40.0  # the first panel: every int16 lane of its first step sums 4 x 127 > 258
+    for i, w in enumerate(mats):
+        n, c = w.shape
+        n_pad, k_pad = (n + 3) & ~3, (c + 15) & ~15
+        wq = np.zeros((n_pad, k_pad), np.float32)
+        wq[:n, :c] = w
+        q, sw = lower.quant_rows_s8(wq)
+        arrays[f"w{i}"] = w
+        arrays[f"q{i}"] = q
+        arrays[f"sw{i}"] = sw
+        arrays[f"n4_{i}"] = lower.n4_panel_flags(q)
+        arrays[f"qp{i}"] = q.reshape(n_pad // 4, 4, k_pad // 16, 16).transpose(0, 2, 1, 3).copy()
+    np.savez(os.path.join(HERE, "proto_packing.npz"), **arrays)
+    print("wrote proto_packages.json and proto_packing.npz")
 
 
 def sha(path):
@@ -86,6 +163,7 @@ def main():
             arrays[f"{suffix}{i}"] = lw.pkg.tensors[tl[j]][1]
     np.savez(os.path.join(HERE, "s8_packing.npz"), **arrays)
     print("wrote packages.json and s8_packing.npz")
+    proto_fixtures(ref_root)
 
 
 if __name__ == "__main__":
