@@ -209,6 +209,98 @@ def c1_gemm(m, torch, stream, peak_bf16):
                     "the int8 ridge"}
 
 
+PROTO_C4 = dict(batch=512, cells=64, channels=1536, classes=14795, ppc=4)
+
+
+def int8_peak(torch):
+    """Dense int8 tensor-core throughput measured here: torch._int_mm (cuBLASLt, int8 x int8 -> int32) on 8192^3, best
+    of 10 launches (CUDA events); None if the library call is unavailable."""
+    try:
+        a = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda")
+        b = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda").t()
+        for _ in range(3):
+            torch._int_mm(a, b)  # pylint: disable=protected-access
+        best = None
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)  # pylint: disable=protected-access
+            e1.record()
+            e1.synchronize()
+            t = e0.elapsed_time(e1)
+            best = t if best is None else min(best, t)
+        return 2.0 * 8192 ** 3 / (best * 1e-3) / 1e12
+    except (RuntimeError, AttributeError):
+        return None
+
+
+def proto_setup(h, torch, batch, seed=2024):
+    """The Perch v2 prototype head (64 cells x 1536 channels -> 14795 classes x 4 prototypes) as a
+    bnn_proto_s8 op for `batch` windows, with seeded N(0, 1) cells resident on the device."""
+    from bnneon_b200 import synth  # pylint: disable=import-outside-toplevel
+    c = PROTO_C4
+    head = synth.proto_head(seed, c["cells"], c["channels"], c["classes"], c["ppc"], 1e-6)
+    qp, sw, n4, rows = synth.pack_proto_s8(head["P"])
+    del head["P"]
+    cw, cb = np.ascontiguousarray(head["cw"]), np.ascontiguousarray(head["cb"])
+    n = c["classes"] * c["ppc"]
+    np_, kp = rows.shape
+    op = h.bnn_proto_s8_new(n, c["channels"], kp, np_, qp.ctypes.data, sw.ctypes.data, n4.ctypes.data, cw.ctypes.data,
+                            cb.ctypes.data, c["classes"], c["ppc"], 1e-6, c["cells"], batch)
+    if not op:
+        raise RuntimeError(h.bnn_last_error().decode())
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn((batch, c["cells"], c["channels"]), generator=g, device="cuda", dtype=torch.float32)
+    lg = torch.empty((batch, c["classes"]), dtype=torch.float32, device="cuda")
+    cm = torch.empty((batch, np_), dtype=torch.float32, device="cuda")
+    st = torch.empty(batch, dtype=torch.int32, device="cuda")
+
+    def run(stream_ptr):
+        return h.bnn_proto_s8_run(op, batch, x.data_ptr(), c["cells"] * c["channels"], c["channels"], lg.data_ptr(),
+                                  c["classes"], cm.data_ptr(), np_, st.data_ptr(), stream_ptr)
+    return op, run, (x, lg, cm, st), np_, kp
+
+
+def proto_head_c4(h, torch, stream, peak_bf16):
+    """SURVEY C4's int8 head timed: PROTO_S8 (per-cell quantizer, tcgen05 column-max GEMM, logits) on 512 windows
+    through bnn_proto_s8_run, inputs resident, 20 runs back to back after 3 warm-ups, CUDA events on their stream.
+    The GEMM is tensor-core bound (M 32768 cells x N 59180 x K 1536: 5.96 T int8 ops per run)."""
+    c = PROTO_C4
+    B = c["batch"]
+    op, run, keep, np_, kp = proto_setup(h, torch, B)
+    try:
+        sp = stream.cuda_stream
+        for _ in range(3):
+            assert run(sp) == 0
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        e0.record(stream)
+        for _ in range(reps):
+            run(sp)
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        err = h.bnn_proto_s8_error(op)
+    finally:
+        h.bnn_proto_s8_free(op)
+        del keep
+    n = c["classes"] * c["ppc"]
+    ops = 2.0 * B * c["cells"] * n * c["channels"]
+    tops = ops / (ms * 1e-3) / 1e12
+    meas = int8_peak(torch)
+    peak = meas if meas else 2.0 * peak_bf16
+    return {"shape": f"{B} windows x {c['cells']} cells x K {c['channels']} -> {n} prototypes ({c['classes']} classes "
+                     f"x {c['ppc']}), fp32 cells in, logits out", "ms_per_run": round(ms, 4),
+            "windows_per_s": round(B / (ms * 1e-3), 1), "int8_ops_per_run": ops, "tops": round(tops, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tops, 1), "peak": round(peak, 1), "unit": "TOP/s",
+                         "frac": round(tops / peak, 4),
+                         "peak_source": "measured here: torch._int_mm (cuBLASLt int8) 8192^3, best of 10" if meas
+                         else "2 x MEASURED_PEAKS.json bf16_tflops (torch._int_mm unavailable)"},
+            "gemm_error_word": err,
+            "note": "time = the whole op (quantizer + GEMM + logits); ops = the GEMM's 2 M N K"}
+
+
 def load_peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json"), encoding="utf-8") as f:
@@ -364,6 +456,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-summary", metavar="CSV",
                     help="write profiles/launch_list_v24_int8_b256.md from an ncu launch-list CSV (no GPU needed)")
+    ap.add_argument("--no-proto", action="store_true", help="skip the prototype-head (C4 int8 head) line")
+    ap.add_argument("--proto-ncu", type=int, metavar="B", default=0,
+                    help="for profiler captures: the prototype head on B windows, 3 warm-ups + 1 run, no timing")
     ap.add_argument("--ncu", action="store_true",
                     help="for profiler captures: warm-up steps + one step through bnn_infer_device, no timing, no JSON")
     args = ap.parse_args()
@@ -385,6 +480,18 @@ def main():
 
     torch.cuda.set_device(local)
     os.environ["BNN_DEVICES"] = str(local)
+    if args.proto_ncu:  # the prototype head alone, for a profiler; nothing is timed or printed as a result
+        from bnneon_b200 import load_library  # pylint: disable=import-outside-toplevel
+        h = load_library()
+        assert h.bnn_cuda_device_init() == 0
+        op, run, keep, _, _ = proto_setup(h, torch, args.proto_ncu)
+        for _ in range(4):
+            assert run(None) == 0
+        torch.cuda.synchronize()
+        h.bnn_proto_s8_free(op)
+        del keep
+        print(f"proto ncu mode: 4 runs of {args.proto_ncu} windows", flush=True)
+        return
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=datetime.timedelta(seconds=120))
 
@@ -502,6 +609,7 @@ def main():
     except (OSError, KeyError, ValueError):
         bf16 = 1590.0  # the profiling recipe's fallback
     c1 = c1_gemm(m, torch, stream, bf16) if rank == 0 else None
+    proto = proto_head_c4(m.h, torch, stream, bf16) if rank == 0 and not args.no_proto else None
 
     line = None
     if rank == 0:
@@ -518,7 +626,7 @@ def main():
                             "ms_per_step": round(s8_ms, 4),
                             "note": "int8 ops of PW_S8 + GEMV_S8 (quantizer + tcgen05 GEMM) per second; these GEMMs "
                                     "are HBM-bound (AI far below the int8 ridge)"},
-                "ops": ops_summary, "clocks": clocks, "s8_gemm_c1": c1}
+                "ops": ops_summary, "clocks": clocks, "s8_gemm_c1": c1, "proto_s8_c4": proto}
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(pkg, pcm)
     m.close()

@@ -165,6 +165,11 @@ __device__ __forceinline__ float col_max(uint32_t trow, int col0, int n, const f
       }
     }
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    // the loaded registers pass through an empty asm after the wait, so that no use of them moves above it
+#pragma unroll
+    for (int k = 0; k < kPLoads; k++)
+#pragma unroll
+      for (int v = 0; v < U; v++) asm volatile("" : "+r"(acc[k][v]));
 #pragma unroll
     for (int k = 0; k < kPLoads; k++) {
       if (c + k * U < col0 + n) {
@@ -421,7 +426,7 @@ static int launch_colmax(const bnnk_proto_plan *p, const ProtoArgs &a, bnn_strea
 extern "C" int bnnk_proto_colmax(const bnnk_proto_plan *p, int batch, const float *sx, const float *sw, float *colmax,
                                  long long cws, float *part, int *err, bnn_stream_t st) {
   if (batch <= 0) return 0;
-  if (batch > p->batch_cap || (!p->wt && !part)) return cudaErrorInvalidValue;
+  if (batch > p->batch_cap || (!p->wt && (!part || batch > 65535))) return cudaErrorInvalidValue;
   ProtoArgs a;
   a.np = p->np;
   a.batch = batch;
