@@ -134,7 +134,7 @@ typedef struct {
   unsigned char tma_w[128] __attribute__((aligned(64)));
   unsigned char tma_q[128] __attribute__((aligned(64)));
   int np, kp, P, batch_cap;
-  int wt, nch, cs, bn, unit, acc_cols, nkb, stages;
+  int wt, nch, cs, bn, unit, acc_cols, mh, nkb, stages;
   unsigned int idesc;
   size_t smem;
 } bnnk_proto_plan;

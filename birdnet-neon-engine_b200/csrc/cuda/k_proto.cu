@@ -45,54 +45,40 @@ __device__ __forceinline__ int q_ties_away(float v) {
   return i > 127 ? 127 : i < -127 ? -127 : i;
 }
 
-constexpr int kQCells = 128;  // cells per quantizer block (2 threads each in the reduction)
+constexpr int kQCells = 8;  // cells per quantizer block: their rows are re-read from L2 right after the reduction
 
 // cells r = w * P + p of x (window stride xws, row stride ld floats) -> qa [cells][Kq] (zero from C to Kq), sx [cells].
-// Reduction: thread pair (2 cp, 2 cp + 1) holds the reference's accumulators s0 (lanes 0-3) and s1 (lanes 4-7) of
-// cell cp: lane l of the 8-channel step c is channel c + l, fused x x + s in channel order. Quantization: each warp
-// takes cells of the block, a lane 8 channels (two 16-byte loads, one 8-byte store) at a time.
+// Reduction: 8 threads per cell, thread l holding the reference's accumulator lane l (lanes 0-3 of s0, 4-7 of s1):
+// channel c + l of each 8-channel step, fused x x + s in channel order; then vaddvq_f32(s0 + s1) = (v0 + v1) + (v2 + v3)
+// with v_l = s0_l + s1_l, by shuffles in that order. Quantization: each warp takes cells of the block, a lane 8
+// channels (two 16-byte loads, one 8-byte store) at a time.
 template <bool VEC>
-__global__ void __launch_bounds__(256) k_proto_quant(int cells, int P, const float *__restrict__ x, long long xws,
+__global__ void __launch_bounds__(128) k_proto_quant(int cells, int P, const float *__restrict__ x, long long xws,
                                                      int ld, int C, int Kq, float eps, int8_t *__restrict__ qa,
                                                      float *__restrict__ sx) {
   __shared__ float s_inv[kQCells];
   const int c0 = blockIdx.x * kQCells;
   {
-    const int cl = threadIdx.x >> 1, half = threadIdx.x & 1, cell = c0 + cl;
-    float s[4] = {0.f, 0.f, 0.f, 0.f}, m[4] = {0.f, 0.f, 0.f, 0.f};
-    if (cell < cells) {
+    const int cl = threadIdx.x >> 3, l = threadIdx.x & 7, cell = c0 + cl;
+    float s = 0.f, m = 0.f;
+    if (cl < kQCells && cell < cells) {
       const int w = cell / P, p = cell - w * P;
-      const float *r = x + (long long)w * xws + (long long)p * ld + 4 * half;
+      const float *r = x + (long long)w * xws + (long long)p * ld + l;
+#pragma unroll 8
       for (int c = 0; c < C; c += 8) {
-        float u[4];
-        if (VEC) {
-          const float4 v = __ldg(reinterpret_cast<const float4 *>(r + c));
-          u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
-        } else {
-#pragma unroll
-          for (int l = 0; l < 4; l++) u[l] = __ldg(r + c + l);
-        }
-#pragma unroll
-        for (int l = 0; l < 4; l++) {
-          s[l] = __fmaf_rn(u[l], u[l], s[l]);
-          m[l] = fmax_nan(m[l], fabsf(u[l]));
-        }
+        const float u = __ldg(r + c);
+        s = __fmaf_rn(u, u, s);
+        m = fmax_nan(m, fabsf(u));
       }
     }
-    float o[4], om[4];
-#pragma unroll
-    for (int l = 0; l < 4; l++) {
-      o[l] = __shfl_xor_sync(0xffffffffu, s[l], 1);
-      om[l] = __shfl_xor_sync(0xffffffffu, m[l], 1);
-    }
-    if (cell < cells && half == 0) {
-      // vaddvq_f32(s0 + s1): lanewise sums, then pairwise
-      const float v0 = __fadd_rn(s[0], o[0]), v1 = __fadd_rn(s[1], o[1]), v2 = __fadd_rn(s[2], o[2]),
-                  v3 = __fadd_rn(s[3], o[3]);
-      const float sum = __fadd_rn(__fadd_rn(v0, v1), __fadd_rn(v2, v3));
+    const float v = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, 4, 8));  // lanes 0-3: v_l = s0_l + s1_l
+    const float a = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1, 8));  // lane 0: v0 + v1, lane 2: v2 + v3
+    const float sum = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 2, 8));
+    float mx = fmax_nan(m, __shfl_down_sync(0xffffffffu, m, 4, 8));
+    mx = fmax_nan(mx, __shfl_down_sync(0xffffffffu, mx, 2, 8));
+    mx = fmax_nan(mx, __shfl_down_sync(0xffffffffu, mx, 1, 8));
+    if (l == 0 && cl < kQCells && cell < cells) {
       const float den = __fadd_rn(__fsqrt_rn(sum), eps);
-      float mx = fmax_nan(fmax_nan(fmax_nan(m[0], om[0]), fmax_nan(m[1], om[1])),
-                          fmax_nan(fmax_nan(m[2], om[2]), fmax_nan(m[3], om[3])));
       if (!(mx > 0.f)) mx = 1e-30f;
       sx[cell] = __fdiv_rn(mx, __fmul_rn(127.f, den));
       s_inv[cl] = __fdiv_rn(127.f, mx);
@@ -101,7 +87,7 @@ __global__ void __launch_bounds__(256) k_proto_quant(int cells, int P, const flo
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nchunk = Kq / 8;
-  for (int cl = warp; cl < kQCells; cl += 8) {
+  for (int cl = warp; cl < kQCells; cl += 4) {
     const int cell = c0 + cl;
     if (cell >= cells) break;
     const int w = cell / P, p = cell - w * P;
@@ -118,11 +104,11 @@ __global__ void __launch_bounds__(256) k_proto_quant(int cells, int P, const flo
           u[0] = a.x; u[1] = a.y; u[2] = a.z; u[3] = a.w; u[4] = b.x; u[5] = b.y; u[6] = b.z; u[7] = b.w;
         } else {
 #pragma unroll
-          for (int l = 0; l < 8; l++) u[l] = __ldg(r + 8 * ch + l);
+          for (int k = 0; k < 8; k++) u[k] = __ldg(r + 8 * ch + k);
         }
         int b[8];
 #pragma unroll
-        for (int l = 0; l < 8; l++) b[l] = q_ties_away(__fmul_rn(u[l], inv));
+        for (int k = 0; k < 8; k++) b[k] = q_ties_away(__fmul_rn(u[k], inv));
         lo = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
         hi = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
       }
@@ -135,7 +121,10 @@ __global__ void __launch_bounds__(256) k_proto_quant(int cells, int P, const flo
 
 constexpr int kPMaxStages = 8;
 constexpr int kPMaxThreads = 64 + 128 * 2 * 2;  // 2 accumulators x 4 lane quarters x up to 2 warps
-constexpr int kPLoads = 4;  // TMEM loads in flight per epilogue thread
+// TMEM loads in flight per epilogue thread (24 or 16 columns per wait; more would spill at the 576-thread register
+// budget)
+template <int U>
+constexpr int kPLoads = U == 8 ? 3 : 4;
 
 struct ProtoArgs {
   int np;             // prototypes (rows of A, columns of colmax)
@@ -152,13 +141,17 @@ struct ProtoArgs {
 };
 
 // the maximum over tile columns [col0, col0 + n) of (float)acc * sx[cell0 + col] for this thread's prototype: U
-// columns per TMEM load (8, or 4 when windows start on odd multiples of 4), kPLoads loads in flight
+// columns per TMEM load (8, or 4 when windows start on odd multiples of 4), kPLoads<U> loads in flight. Four running
+// maxima (column mod 4) break the dependency chain; max is exact, so combining them at the end gives the maximum in
+// any order (NaN-propagating, +0 above -0). The products run paired: each lane is one IEEE multiply, and none feeds
+// an add.
 template <int U>
-__device__ __forceinline__ float col_max(uint32_t trow, int col0, int n, const float *__restrict__ sxc, float mx) {
-  for (int c = col0; c < col0 + n; c += U * kPLoads) {
-    uint32_t acc[kPLoads][U];
+__device__ __forceinline__ float col_max(uint32_t trow, int col0, int n, const float *__restrict__ sxc) {
+  float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+  for (int c = col0; c < col0 + n; c += U * kPLoads<U>) {
+    uint32_t acc[kPLoads<U>][U];
 #pragma unroll
-    for (int k = 0; k < kPLoads; k++) {
+    for (int k = 0; k < kPLoads<U>; k++) {
       if (c + k * U < col0 + n) {
         if constexpr (U == 8) tmem_ld8(trow + (uint32_t)(c + k * U), acc[k]);
         else tmem_ld4(trow + (uint32_t)(c + k * U), acc[k]);
@@ -167,27 +160,33 @@ __device__ __forceinline__ float col_max(uint32_t trow, int col0, int n, const f
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
     // the loaded registers pass through an empty asm after the wait, so that no use of them moves above it
 #pragma unroll
-    for (int k = 0; k < kPLoads; k++)
+    for (int k = 0; k < kPLoads<U>; k++)
 #pragma unroll
       for (int v = 0; v < U; v++) asm volatile("" : "+r"(acc[k][v]));
 #pragma unroll
-    for (int k = 0; k < kPLoads; k++) {
+    for (int k = 0; k < kPLoads<U>; k++) {
       if (c + k * U < col0 + n) {
 #pragma unroll
         for (int v = 0; v < U; v += 4) {
           const float4 s = __ldg(reinterpret_cast<const float4 *>(sxc + c + k * U + v));
-          mx = fmax_nan(mx, __fmul_rn(__int2float_rn((int)acc[k][v + 0]), s.x));
-          mx = fmax_nan(mx, __fmul_rn(__int2float_rn((int)acc[k][v + 1]), s.y));
-          mx = fmax_nan(mx, __fmul_rn(__int2float_rn((int)acc[k][v + 2]), s.z));
-          mx = fmax_nan(mx, __fmul_rn(__int2float_rn((int)acc[k][v + 3]), s.w));
+          const float2 p01 = mul2_rn(make_float2(__int2float_rn((int)acc[k][v + 0]), __int2float_rn((int)acc[k][v + 1])),
+                                     make_float2(s.x, s.y));
+          const float2 p23 = mul2_rn(make_float2(__int2float_rn((int)acc[k][v + 2]), __int2float_rn((int)acc[k][v + 3])),
+                                     make_float2(s.z, s.w));
+          m0 = fmax_nan(m0, p01.x);
+          m1 = fmax_nan(m1, p01.y);
+          m2 = fmax_nan(m2, p23.x);
+          m3 = fmax_nan(m3, p23.y);
         }
       }
     }
   }
-  return mx;
+  return fmax_nan(fmax_nan(m0, m1), fmax_nan(m2, m3));
 }
 
-template <int U>
+// MH prototype halves of 128 rows per tile: with MH = 2 a tile is 256 prototypes x bn cells, two MMAs per K step
+// share the stage's cell block (a third less operand traffic per MAC than 128-row tiles)
+template <int U, int MH>
 __global__ void __launch_bounds__(kPMaxThreads, 1) k_proto_colmax(const __grid_constant__ CUtensorMap tma_w,
                                                                  const __grid_constant__ CUtensorMap tma_q,
                                                                  const ProtoArgs a) {
@@ -200,7 +199,7 @@ __global__ void __launch_bounds__(kPMaxThreads, 1) k_proto_colmax(const __grid_c
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t base = (smem_u32(dsmem) + 1023u) & ~1023u;
-  const uint32_t a_bytes = 128u * SW, stage_bytes = (128u + a.bn) * SW;
+  const uint32_t a_bytes = 128u * MH * SW, stage_bytes = (128u * MH + a.bn) * SW;
   const int S = a.stages;
 
   if (threadIdx.x == 0) {
@@ -226,7 +225,7 @@ __global__ void __launch_bounds__(kPMaxThreads, 1) k_proto_colmax(const __grid_c
     if (lane == 0) {  // TMA producer
       int it = 0;
       for (int t = blockIdx.x; t < a.tiles && !abort_s; t += gridDim.x) {
-        const int m0 = (t / a.n_ct) * 128, ct = t % a.n_ct;
+        const int m0 = (t / a.n_ct) * 128 * MH, ct = t % a.n_ct;
         const int n0 = a.wt ? ct * a.wt * a.P : (ct / a.nch) * a.P + (ct % a.nch) * a.cs;
         for (int kb = 0; kb < a.nkb; kb++, it++) {
           const int s = it % S;
@@ -237,7 +236,8 @@ __global__ void __launch_bounds__(kPMaxThreads, 1) k_proto_colmax(const __grid_c
           }
           const uint32_t st = base + s * stage_bytes, bar = smem_u32(&bar_full[s]);
           mbar_expect_tx(bar, stage_bytes);  // full boxes: rows and bytes out of bounds arrive as zero fill
-          tma_load_2d(st, &tma_w, bar, kb * SW, m0);
+#pragma unroll
+          for (int hm = 0; hm < MH; hm++) tma_load_2d(st + hm * 128u * SW, &tma_w, bar, kb * SW, m0 + 128 * hm);
           tma_load_2d(st + a_bytes, &tma_q, bar, kb * SW, n0);
         }
       }
@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(kPMaxThreads, 1) k_proto_colmax(const __grid_c
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t tacc = tmem + (uint32_t)(g * a.acc_cols);
+        const uint32_t tacc = tmem + (uint32_t)(g * MH * a.acc_cols);
         bool ok = true;
         for (int kb = 0; kb < a.nkb; kb++, it++) {
           const int s = it % S;
@@ -267,7 +267,10 @@ __global__ void __launch_bounds__(kPMaxThreads, 1) k_proto_colmax(const __grid_c
           const uint32_t st = base + s * stage_bytes;
 #pragma unroll
           for (int kk = 0; kk < SW / 32; kk++)
-            mma_i8(tacc, smem_desc<SW>(st + kk * 32), smem_desc<SW>(st + a_bytes + kk * 32), a.idesc, (kb | kk) != 0);
+#pragma unroll
+            for (int hm = 0; hm < MH; hm++)
+              mma_i8(tacc + (uint32_t)(hm * a.acc_cols), smem_desc<SW>(st + hm * 128u * SW + kk * 32),
+                     smem_desc<SW>(st + a_bytes + kk * 32), a.idesc, (kb | kk) != 0);
           mma_commit(smem_u32(&bar_empty[s]));
         }
         if (!ok) break;
@@ -275,13 +278,12 @@ __global__ void __launch_bounds__(kPMaxThreads, 1) k_proto_colmax(const __grid_c
       }
     }
   } else if (warp - 2 < 4 * a.ne * a.nh) {
-    // epilogue: group g drains accumulator g; warp h of lane quarter q takes the tile's windows h, h + nh, ...
+    // epilogue: group g drains accumulator g; warp h of lane quarter q takes the tile's units (prototype half, window)
+    // h, h + nh, ...
     const int e = warp - 2, g = e / (4 * a.nh), h = (e % (4 * a.nh)) / 4, q = warp % 4;
     int use = 0;
     for (int t = blockIdx.x + g * gridDim.x; t < a.tiles; t += a.ne * gridDim.x, use++) {
-      const int m0 = (t / a.n_ct) * 128, ct = t % a.n_ct;
-      const int j = m0 + q * 32 + lane;
-      const float swj = j < a.np ? __ldg(a.sw + j) : 0.f;
+      const int m0 = (t / a.n_ct) * 128 * MH, ct = t % a.n_ct;
       bool ok = mbar_wait(smem_u32(&bar_acc_full[g]), use & 1);
       ok = __all_sync(0xffffffffu, ok) && !abort_s;
       if (!ok) {
@@ -289,18 +291,19 @@ __global__ void __launch_bounds__(kPMaxThreads, 1) k_proto_colmax(const __grid_c
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t trow = tmem + (uint32_t)(g * a.acc_cols) + ((uint32_t)(q * 32) << 16);
+      const uint32_t tq = tmem + (uint32_t)(g * MH * a.acc_cols) + ((uint32_t)(q * 32) << 16);
       if (a.wt) {
         const int w0 = ct * a.wt, nw = min(a.wt, a.batch - w0);
         const float *sxc = a.sx + (long long)w0 * a.P;
-        for (int wi = h; wi < nw; wi += a.nh) {
-          const float mx = col_max<U>(trow, wi * a.P, a.P, sxc, -INFINITY);
-          if (j < a.np) a.out[(long long)(w0 + wi) * a.ows + j] = __fmul_rn(mx, swj);
+        for (int u = h; u < MH * nw; u += a.nh) {
+          const int hm = u / nw, wi = u - hm * nw, j = m0 + 128 * hm + q * 32 + lane;
+          const float mx = col_max<U>(tq + (uint32_t)(hm * a.acc_cols), wi * a.P, a.P, sxc);
+          if (j < a.np) a.out[(long long)(w0 + wi) * a.ows + j] = __fmul_rn(mx, __ldg(a.sw + j));
         }
-      } else if (h == 0) {
+      } else if (h < MH) {
         const int w = ct / a.nch, k = ct % a.nch, cell0 = w * a.P + k * a.cs;
-        const int n = min(a.cs, a.P - k * a.cs);
-        const float mx = col_max<U>(trow, 0, n, a.sx + cell0, -INFINITY);
+        const int n = min(a.cs, a.P - k * a.cs), j = m0 + 128 * h + q * 32 + lane;
+        const float mx = col_max<U>(tq + (uint32_t)(h * a.acc_cols), 0, n, a.sx + cell0);
         if (j < a.np) a.out[(long long)ct * a.np + j] = mx;
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -328,19 +331,28 @@ __global__ void k_proto_chunks(int batch, int np, int nch, const float *__restri
 
 // one block per window: logits[c] = (sum over q < ppc, in order, of colmax[c ppc + q] * w[c ppc + q]) + b[c], each
 // product and sum rounded. A window with a logit that is not finite or above 3e38 in magnitude failed
-// (pc_proto_logits returns -2): status[w] = -2 (else 0), and fail holds the smallest failed w_base + w.
-__global__ void __launch_bounds__(256) k_proto_logits(int nc, int ppc, const float *__restrict__ colmax,
-                                                      long long cws, const float *__restrict__ cw,
-                                                      const float *__restrict__ cb, float *__restrict__ logits,
-                                                      long long lws, int *__restrict__ status, int *fail, int w_base) {
+// (pc_proto_logits returns -2): status[w] = -2 (else 0), and fail holds the smallest failed w_base + w. V4: ppc == 4
+// with 16-byte aligned rows (one 16-byte load of each operand per class).
+template <bool V4>
+__global__ void __launch_bounds__(1024) k_proto_logits(int nc, int ppc, const float *__restrict__ colmax,
+                                                       long long cws, const float *__restrict__ cw,
+                                                       const float *__restrict__ cb, float *__restrict__ logits,
+                                                       long long lws, int *__restrict__ status, int *fail, int w_base) {
   const int w = blockIdx.x;
   const float *cm = colmax + (long long)w * cws;
   int bad = 0;
   for (int c = threadIdx.x; c < nc; c += blockDim.x) {
     float s = 0.f;
-    for (int q = 0; q < ppc; q++) {
-      const long long i = (long long)c * ppc + q;
-      s = __fadd_rn(s, __fmul_rn(cm[i], __ldg(cw + i)));
+    if (V4) {
+      const float4 a = __ldg(reinterpret_cast<const float4 *>(cm) + c);
+      const float4 b = __ldg(reinterpret_cast<const float4 *>(cw) + c);
+      s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, __fmul_rn(a.x, b.x)), __fmul_rn(a.y, b.y)), __fmul_rn(a.z, b.z)),
+                    __fmul_rn(a.w, b.w));
+    } else {
+      for (int q = 0; q < ppc; q++) {
+        const long long i = (long long)c * ppc + q;
+        s = __fadd_rn(s, __fmul_rn(__ldg(cm + i), __ldg(cw + i)));
+      }
     }
     const float v = __fadd_rn(s, __ldg(cb + c));
     logits[(long long)w * lws + c] = v;
@@ -365,8 +377,8 @@ extern "C" int bnnk_proto_quant(int batch, int P, const float *x, long long xws,
   if (cells <= 0) return 0;
   const bool vec = ((uintptr_t)x & 15) == 0 && xws % 4 == 0 && ld % 4 == 0;
   const int grid = (cells + kQCells - 1) / kQCells;
-  if (vec) k_proto_quant<true><<<grid, 256, 0, st>>>(cells, P, x, xws, ld, C, Kq, eps, qa, sx);
-  else k_proto_quant<false><<<grid, 256, 0, st>>>(cells, P, x, xws, ld, C, Kq, eps, qa, sx);
+  if (vec) k_proto_quant<true><<<grid, 128, 0, st>>>(cells, P, x, xws, ld, C, Kq, eps, qa, sx);
+  else k_proto_quant<false><<<grid, 128, 0, st>>>(cells, P, x, xws, ld, C, Kq, eps, qa, sx);
   return cudaGetLastError();
 }
 
@@ -395,7 +407,11 @@ extern "C" int bnnk_proto_plan_init(bnnk_proto_plan *p, const int8_t *w, int np,
   }
   p->unit = (P % 8 == 0 && p->cs % 8 == 0) ? 8 : 4;
   p->acc_cols = p->bn <= 32 ? 32 : p->bn <= 64 ? 64 : p->bn <= 128 ? 128 : 256;
-  const size_t stage = (size_t)(128 + p->bn) * 128;
+  // 256-prototype tiles (two 128-row halves sharing each cell block) when there are at least two prototype tiles
+  // of 128; BNN_PROTO_MH=1 forces 128-row tiles (tuning sweeps)
+  const char *env = getenv("BNN_PROTO_MH");
+  p->mh = np > 128 && !(env && atoi(env) == 1) ? 2 : 1;
+  const size_t stage = (size_t)(128 * p->mh + p->bn) * 128;
   int s = (int)((200 * 1024) / stage);
   p->stages = s < 2 ? 2 : s > kPMaxStages ? kPMaxStages : s;
   p->smem = (size_t)p->stages * stage + 1024;
@@ -406,20 +422,20 @@ extern "C" int bnnk_proto_plan_init(bnnk_proto_plan *p, const int8_t *w, int np,
   return e;
 }
 
-template <int U>
+template <int U, int MH>
 static int launch_colmax(const bnnk_proto_plan *p, const ProtoArgs &a, bnn_stream_t st) {
   static size_t attr[64];
   int dev = 0;
   if (cudaGetDevice(&dev) || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (p->smem > attr[dev]) {
     const cudaError_t e =
-        cudaFuncSetAttribute(k_proto_colmax<U>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p->smem);
+        cudaFuncSetAttribute(k_proto_colmax<U, MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p->smem);
     if (e) return e;
     attr[dev] = p->smem;
   }
   const int grid = a.tiles < num_sms() ? a.tiles : num_sms();
-  k_proto_colmax<U><<<grid, 64 + 128 * a.ne * a.nh, p->smem, st>>>(*(const CUtensorMap *)p->tma_w,
-                                                                  *(const CUtensorMap *)p->tma_q, a);
+  k_proto_colmax<U, MH><<<grid, 64 + 128 * a.ne * a.nh, p->smem, st>>>(*(const CUtensorMap *)p->tma_w,
+                                                                      *(const CUtensorMap *)p->tma_q, a);
   return cudaGetLastError();
 }
 
@@ -435,22 +451,25 @@ extern "C" int bnnk_proto_colmax(const bnnk_proto_plan *p, int batch, const floa
   a.nch = p->nch;
   a.cs = p->cs;
   a.n_ct = p->wt ? (batch + p->wt - 1) / p->wt : batch * p->nch;
-  a.tiles = ((p->np + 127) / 128) * a.n_ct;
+  a.tiles = ((p->np + 128 * p->mh - 1) / (128 * p->mh)) * a.n_ct;
   a.nkb = p->nkb;
   a.stages = p->stages;
   a.bn = p->bn;
   a.acc_cols = p->acc_cols;
-  a.ne = 2;
-  // epilogue warps per lane quarter: one per window of a tile, at most 2
-  a.nh = p->wt ? (p->wt < 2 ? p->wt : 2) : 1;
-  a.tmem_alloc = 2 * p->acc_cols;  // a power of two: acc_cols is one and at most 256
+  // two accumulators (the MMA of the next tile overlaps the epilogue of the last) when they fit the 512 TMEM columns
+  a.ne = 2 * p->mh * p->acc_cols <= 512 ? 2 : 1;
+  a.tmem_alloc = a.ne * p->mh * p->acc_cols;  // a power of two: acc_cols is one, mh and ne are 1 or 2
+  // epilogue warps per lane quarter: one per unit (prototype half, window) of a tile, 16 warps at most
+  const int units = p->mh * (p->wt ? p->wt : 1), hmax = 4 / a.ne;
+  a.nh = units < hmax ? units : hmax;
   a.idesc = p->idesc;
   a.sx = sx;
   a.sw = sw;
   a.out = p->wt ? colmax : part;
   a.ows = cws;
   a.err = err;
-  int e = p->unit == 8 ? launch_colmax<8>(p, a, st) : launch_colmax<4>(p, a, st);
+  int e = p->mh == 2 ? (p->unit == 8 ? launch_colmax<8, 2>(p, a, st) : launch_colmax<4, 2>(p, a, st))
+                     : (p->unit == 8 ? launch_colmax<8, 1>(p, a, st) : launch_colmax<4, 1>(p, a, st));
   if (e || p->wt) return e;
   const dim3 grid((p->np + 255) / 256, batch);
   k_proto_chunks<<<grid, 256, 0, st>>>(batch, p->np, p->nch, part, sw, colmax, cws);
@@ -461,6 +480,8 @@ extern "C" int bnnk_proto_logits(int batch, int nc, int ppc, const float *colmax
                                  const float *cb, float *logits, long long lws, int *status, int *fail, int w_base,
                                  bnn_stream_t st) {
   if (batch <= 0) return 0;
-  k_proto_logits<<<batch, 256, 0, st>>>(nc, ppc, colmax, cws, cw, cb, logits, lws, status, fail, w_base);
+  const bool v4 = ppc == 4 && ((uintptr_t)colmax & 15) == 0 && cws % 4 == 0 && ((uintptr_t)cw & 15) == 0;
+  if (v4) k_proto_logits<true><<<batch, 1024, 0, st>>>(nc, ppc, colmax, cws, cw, cb, logits, lws, status, fail, w_base);
+  else k_proto_logits<false><<<batch, 1024, 0, st>>>(nc, ppc, colmax, cws, cw, cb, logits, lws, status, fail, w_base);
   return cudaGetLastError();
 }
