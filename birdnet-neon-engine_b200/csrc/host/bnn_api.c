@@ -373,6 +373,7 @@ static cudaError_t upload_setup(bnn_ctx *c, bnn_dev *dv) {
   cudaError_t e = cudaSuccess;
   if (dv->up_cap < c->batch) {
     if (dv->up_stream) e = cudaStreamSynchronize((cudaStream_t)dv->up_stream);
+    if (!e && dv->up_stream2) e = cudaStreamSynchronize((cudaStream_t)dv->up_stream2);
     cudaFree(dv->up[0]); cudaFree(dv->up[1]);
     dv->up[0] = dv->up[1] = NULL;
     dv->up_cap = 0;
@@ -384,27 +385,37 @@ static cudaError_t upload_setup(bnn_ctx *c, bnn_dev *dv) {
   }
   if (!dv->up_stream) {
     e = cudaStreamCreateWithFlags((cudaStream_t *)&dv->up_stream, cudaStreamNonBlocking);
+    if (!e) e = cudaStreamCreateWithFlags((cudaStream_t *)&dv->up_stream2, cudaStreamNonBlocking);
     for (int k = 0; k < 2 && !e; k++) {
       e = cudaEventCreateWithFlags((cudaEvent_t *)&dv->up_ready[k], cudaEventDisableTiming);
       if (!e) e = cudaEventCreateWithFlags((cudaEvent_t *)&dv->up_free[k], cudaEventDisableTiming);
+      if (!e) e = cudaEventCreateWithFlags((cudaEvent_t *)&dv->up_half[k], cudaEventDisableTiming);
     }
   }
   return e;
 }
 
-/* windows per pipeline chunk: the first is half of min(call, batch) (from 64 windows on; smaller calls run in one
- * chunk), the next ones a full batch, and a tail shorter than half a chunk joins its predecessor. Only the first
- * upload is not hidden behind kernels; every chunk pays the op list's fixed launch latencies, so chunks stay large. */
+/* windows per pipeline chunk: the first is a quarter of min(call, batch) (from 64 windows on; smaller calls run in one
+ * chunk), the next ones a full batch, and a tail shorter than half a chunk joins its predecessor. The first upload is
+ * the only one not hidden behind kernels, while every chunk pays the op list's fixed GPU latencies (~1 ms per launch
+ * sequence even for one window): at batch 256 a first chunk of 64 measured best (37.5k windows/s end to end against
+ * 34.9k for 128 and 34.4k for 32). BNN_CHUNK0 sets the first chunk (tuning sweeps). */
+static int chunk0_env = -1;
 static int next_chunk(int rem, int batch, int prev) {
+  if (chunk0_env < 0) {
+    const char *e0 = getenv("BNN_CHUNK0");
+    chunk0_env = e0 && atoi(e0) >= 1 ? atoi(e0) : 0;
+  }
   const int first = rem < batch ? rem : batch;
-  int s = prev ? batch : first >= 64 ? (first / 2 + 7) / 8 * 8 : first;
+  int s = prev ? batch : chunk0_env ? chunk0_env : first >= 64 ? (first / 4 + 7) / 8 * 8 : first;
   if (s > rem) s = rem;
   if (rem - s > 0 && rem - s < s / 2 && rem <= batch) s = rem;
   return s;
 }
 
-/* one device's share [w0, w1) of a bnn_infer_batch call: chunk i is uploaded into buffer i % 2 on the copy stream
- * (after chunk i - 2's kernels have finished reading it) while chunk i - 1 computes on the context's stream */
+/* one device's share [w0, w1) of a bnn_infer_batch call: chunk i is uploaded into buffer i % 2 by two copies in
+ * parallel on the two copy streams (after chunk i - 2's kernels have finished reading it) while chunk i - 1 computes
+ * on the context's stream */
 static void *dev_worker(void *a) {
   dev_job *j = a;
   bnn_ctx *c = j->c;
@@ -414,18 +425,25 @@ static void *dev_worker(void *a) {
   cudaStream_t st = (cudaStream_t)dv->stream;
   cudaError_t e = cudaSetDevice(dv->dev);
   if (!e) e = upload_setup(c, dv);
-  cudaStream_t cs = (cudaStream_t)dv->up_stream;
+  cudaStream_t cs = (cudaStream_t)dv->up_stream, cs2 = (cudaStream_t)dv->up_stream2;
   for (int w = j->w0, k = 0, nb = 0; w < j->w1 && !e && !j->rc; w += nb, k ^= 1) {
     nb = next_chunk(j->w1 - w, c->batch, nb);
     dv->w_base = w;
     float *buf = dv->up[k];
+    const int na = (nb + 1) / 2;  /* windows of the first copy */
     e = cudaStreamWaitEvent(cs, (cudaEvent_t)dv->up_free[k], 0);
-    if (!e) e = cudaMemcpyAsync(buf, j->pcm + (size_t)w * ns, sizeof(float) * (size_t)nb * ns,
+    if (!e) e = cudaStreamWaitEvent(cs2, (cudaEvent_t)dv->up_free[k], 0);
+    if (!e) e = cudaMemcpyAsync(buf, j->pcm + (size_t)w * ns, sizeof(float) * (size_t)na * ns,
                                 cudaMemcpyHostToDevice, cs);
+    if (!e && nb > na)
+      e = cudaMemcpyAsync(buf + (size_t)na * ns, j->pcm + (size_t)(w + na) * ns, sizeof(float) * (size_t)(nb - na) * ns,
+                          cudaMemcpyHostToDevice, cs2);
+    if (!e) e = cudaEventRecord((cudaEvent_t)dv->up_half[k], cs2);
+    if (!e) e = cudaStreamWaitEvent(cs, (cudaEvent_t)dv->up_half[k], 0);
     if (!e) e = cudaEventRecord((cudaEvent_t)dv->up_ready[k], cs);
     if (!e) e = cudaStreamWaitEvent(st, (cudaEvent_t)dv->up_ready[k], 0);
     if (e) break;
-    if (bnn_rt_launch(c, j->di, nb, buf, 0, c->n_ops, st)) {
+    if (bnn_rt_run(c, j->di, nb, buf, st)) {
       j->rc = -1;
       snprintf(j->err, sizeof j->err, "%s", g_err);
       j->kind = g_kind;
@@ -442,6 +460,7 @@ static void *dev_worker(void *a) {
   if (!e) e = cudaMemcpyAsync(dv->err_host, dv->err, 2 * sizeof(int), cudaMemcpyDeviceToHost, st);
   if (!e) e = cudaStreamSynchronize(st);
   if (!e && cs) e = cudaStreamSynchronize(cs);
+  if (!e && cs2) e = cudaStreamSynchronize(cs2);
   if (e && !j->rc) {
     j->rc = -1;
     j->kind = BNN_ERR_WINDOW;
@@ -498,7 +517,7 @@ int bnn_infer_device(bnn_ctx *c, int n, const float *d_pcm, float *d_out, float 
   cudaStream_t st = stream ? (cudaStream_t)stream : (cudaStream_t)dv->stream;
   cudaSetDevice(dv->dev);
   dv->w_base = 0;
-  if (bnn_rt_launch(c, 0, n, d_pcm, 0, c->n_ops, st)) return -1;
+  if (bnn_rt_run(c, 0, n, d_pcm, st)) return -1;
   cudaError_t e = cudaMemcpy2DAsync(d_out, sizeof(float) * nc, dv->buf[d->out_buf], sizeof(float) * dv->ws[d->out_buf],
                                     sizeof(float) * nc, n, cudaMemcpyDeviceToDevice, st);
   if (!e && d_emb && ne)

@@ -96,8 +96,13 @@ typedef struct {
    * input slot later ops may reuse), a copy stream, and per buffer an upload-done and a compute-done event */
   float *up[2];
   int up_cap;
-  void *up_stream;
-  void *up_ready[2], *up_free[2];
+  void *up_stream, *up_stream2;  /* two copy streams: each chunk's upload is split between them (one host-to-device
+                                  * copy reaches ~29 GB/s on PCIe Gen5 x16, two concurrent ones ~39 GB/s) */
+  void *up_ready[2], *up_free[2], *up_half[2];
+  /* CUDA graphs of whole launch sequences (bnn_rt_run): one per (windows, input buffer, first window of the call);
+   * a key seen once runs eagerly, the second time it is captured. graphs_off: capture failed or BNN_GRAPHS=0. */
+  struct { int n, w_base, seen; const void *in; void *exec; } graphs[8];
+  int n_graphs, graphs_off;
   /* per-op CUDA-event profile (bnn_profile_*): events[2 i], events[2 i + 1] bracket op i of the last launch */
   void **events;
   double *op_ms;
@@ -128,6 +133,8 @@ int bnn_rt_device(bnn_ctx *c, int i, char *err, size_t errlen, int *kind);
 void bnn_rt_device_free(bnn_ctx *c, int i);
 /* n <= batch windows on device i: pcm at d_pcm (window stride n_samples); outputs stay in the arena */
 int bnn_rt_launch(bnn_ctx *c, int i, int n, const float *d_pcm, int op0, int op1, void *stream);
+/* the whole op list on n windows, replayed from a CUDA graph when the same (n, d_pcm, w_base) ran before */
+int bnn_rt_run(bnn_ctx *c, int i, int n, const float *d_pcm, void *stream);
 int c0_quantizes_next(const bnn_ctx *c, int i);
 void bnn_rt_close(bnn_ctx *c);
 int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src, const float *sw_src,
