@@ -243,6 +243,7 @@ def proto_setup(h, torch, batch, seed=2024):
     qp, sw, n4, rows = synth.pack_proto_s8(head["P"])
     del head["P"]
     cw, cb = np.ascontiguousarray(head["cw"]), np.ascontiguousarray(head["cb"])
+    host = {"rows": rows, "sw": sw, "cw": cw, "cb": cb}
     n = c["classes"] * c["ppc"]
     np_, kp = rows.shape
     op = h.bnn_proto_s8_new(n, c["channels"], kp, np_, qp.ctypes.data, sw.ctypes.data, n4.ctypes.data, cw.ctypes.data,
@@ -258,10 +259,38 @@ def proto_setup(h, torch, batch, seed=2024):
     def run(stream_ptr):
         return h.bnn_proto_s8_run(op, batch, x.data_ptr(), c["cells"] * c["channels"], c["channels"], lg.data_ptr(),
                                   c["classes"], cm.data_ptr(), np_, st.data_ptr(), stream_ptr)
-    return op, run, (x, lg, cm, st), np_, kp
+    return op, run, (x, lg, cm, st, host), np_, kp
 
 
-def proto_head_c4(h, torch, stream, peak_bf16):
+def proto_cpu_baseline(keep, n, seconds=15.0):
+    """The oracle port of PROTO_S8 (oracle/oracle_proto.c, restating src/proto_s8n.c and pc_proto_logits) on this
+    host's cores: windows of the same cells, one window per thread; a first round of one window per thread, then, if
+    that was short, one sample of whole rounds sized to about half of `seconds`."""
+    from oracle import oracle  # pylint: disable=import-outside-toplevel
+    c = PROTO_C4
+    x_dev, host = keep[0], keep[4]
+    threads = os.cpu_count() or 1
+    lib = oracle.lib()
+    def run(n_win):
+        x = np.ascontiguousarray(x_dev[:n_win].cpu().numpy())
+        lg = np.empty((n_win, c["classes"]), np.float32)
+        t0 = time.perf_counter()
+        lib.bnno_proto_s8_many(n_win, threads, oracle.ptr(x), c["cells"] * c["channels"], c["cells"], c["channels"],
+                               c["channels"], 1e-6, oracle.ptr(host["rows"]), oracle.ptr(host["sw"]),
+                               host["rows"].shape[0], host["rows"].shape[1], oracle.ptr(host["cw"]),
+                               oracle.ptr(host["cb"]), c["classes"], c["ppc"], oracle.ptr(lg))
+        return time.perf_counter() - t0
+    n_win = min(threads, n)
+    dt = run(n_win)
+    if dt < seconds / 3:  # one more, longer sample: whole rounds of one window per thread
+        n_win = min(n, threads * max(1, int(seconds / 2 / dt)))
+        dt = run(n_win)
+    return {"value": round(n_win / dt, 3), "unit": "windows/s", "cores": threads, "kind": "port",
+            "sample": f"{n_win} windows of the same head and cells ({dt:.1f} s, oracle/oracle_proto.c, one thread per "
+                      f"window)"}
+
+
+def proto_head_c4(h, torch, stream, peak_bf16, cpu=True):
     """SURVEY C4's int8 head timed: PROTO_S8 (per-cell quantizer, tcgen05 column-max GEMM, logits) on 512 windows
     through bnn_proto_s8_run, inputs resident, 20 runs back to back after 3 warm-ups, CUDA events on their stream.
     The GEMM is tensor-core bound (M 32768 cells x N 59180 x K 1536: 5.96 T int8 ops per run)."""
@@ -282,6 +311,7 @@ def proto_head_c4(h, torch, stream, peak_bf16):
         e1.synchronize()
         ms = e0.elapsed_time(e1) / reps
         err = h.bnn_proto_s8_error(op)
+        base = proto_cpu_baseline(keep, B) if cpu else None
     finally:
         h.bnn_proto_s8_free(op)
         del keep
@@ -297,7 +327,7 @@ def proto_head_c4(h, torch, stream, peak_bf16):
                          "frac": round(tops / peak, 4),
                          "peak_source": "measured here: torch._int_mm (cuBLASLt int8) 8192^3, best of 10" if meas
                          else "2 x MEASURED_PEAKS.json bf16_tflops (torch._int_mm unavailable)"},
-            "gemm_error_word": err,
+            "gemm_error_word": err, "cpu_baseline": base,
             "note": "time = the whole op (quantizer + GEMM + logits); ops = the GEMM's 2 M N K"}
 
 
@@ -609,7 +639,8 @@ def main():
     except (OSError, KeyError, ValueError):
         bf16 = 1590.0  # the profiling recipe's fallback
     c1 = c1_gemm(m, torch, stream, bf16) if rank == 0 else None
-    proto = proto_head_c4(m.h, torch, stream, bf16) if rank == 0 and not args.no_proto else None
+    proto = (proto_head_c4(m.h, torch, stream, bf16, cpu=not args.no_cpu_baseline and world == 1)
+             if rank == 0 and not args.no_proto else None)
 
     line = None
     if rank == 0:
