@@ -41,8 +41,9 @@ typedef struct {
   size_t smem;
 } bnnk_gemm_plan;
 int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_cap, int kq, const int8_t *w, int n, int np);
-/* rows of the weight buffer the plan of a layer with np (padded) output channels reads: n_tiles * bn */
-int bnnk_gemm_weight_rows(int np);
+/* rows of the weight buffer the plan of a layer with np (padded) output channels and rows_cap rows reads:
+ * n_tiles * bn */
+int bnnk_gemm_weight_rows(int np, int rows_cap);
 
 /* epilogue of PW_S8 (gemm_s8n.c:105-135): y = (float)(acc - za * cs) * (sw * sa) + b, act (0 none, 1 SiLU,
  * 2 ReLU), + residual, stored at the padded row of each pixel (ow / opad) of each window */

@@ -522,17 +522,21 @@ static int encode_2d(void *map, const void *base, int inner, int rows, int box_i
   return encode_2d_ld(map, base, inner, inner, rows, box_inner, box_rows, sw);
 }
 
-// N tiling: as few tiles of at most 256 columns as possible, equal widths rounded up to 16
-static void n_tiling(int np, int *n_tiles, int *bn) {
-  const int n16 = (np + 15) & ~15;
-  *n_tiles = (n16 + 255) / 256;
-  const int b = (n16 + *n_tiles - 1) / *n_tiles;
+// N tiling: as few tiles of at most 256 columns as possible, equal widths rounded up to 16; then, while the tiles of
+// rows_cap rows (128 each) do not give every SM one and tiles stay at least 32 columns wide, one N tile more (a small
+// GEMM is latency bound: narrower tiles spread it over more SMs, the extra reads of A come from L2)
+static void n_tiling(int np, int rows_cap, int *n_tiles, int *bn) {
+  const int n16 = (np + 15) & ~15, m_tiles = (rows_cap + 127) / 128, sms = 148;
+  int t = (n16 + 255) / 256;
+  while ((long long)m_tiles * t < sms && ((n16 + t) / (t + 1) + 15) / 16 * 16 >= 32) t++;
+  *n_tiles = t;
+  const int b = (n16 + t - 1) / t;
   *bn = (b + 15) & ~15;
 }
 
-extern "C" int bnnk_gemm_weight_rows(int np) {
+extern "C" int bnnk_gemm_weight_rows(int np, int rows_cap) {
   int t, bn;
-  n_tiling(np, &t, &bn);
+  n_tiling(np, rows_cap, &t, &bn);
   return t * bn;
 }
 
@@ -582,7 +586,7 @@ extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_
   p->nkb = (kq + p->sw - 1) / p->sw;
   p->n = n;
   p->np = np;
-  n_tiling(np, &p->n_tiles, &p->bn);
+  n_tiling(np, rows_cap, &p->n_tiles, &p->bn);
   p->tmem_cols = p->bn <= 32 ? 32 : p->bn <= 64 ? 64 : p->bn <= 128 ? 128 : 256;
   epi_shape(p->tmem_cols, &p->ne, &p->nh);
   p->sp = np <= kSPMax;

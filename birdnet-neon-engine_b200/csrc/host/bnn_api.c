@@ -740,7 +740,7 @@ bnn_pw_s8 *bnn_pw_s8_new(int N, int K, int Kp, int Np, const int8_t *w, const fl
   o->N = N; o->K = K; o->Kp = Kp; o->Np = Np; o->rows_cap = rows_cap;
   char err[512];
   int kind = BNN_ERR_CPU;
-  if (bnn_s8_weights(&o->op, N, K, Kp, Np, w, sw, cs, b, err, sizeof err, &kind)) {
+  if (bnn_s8_weights(&o->op, N, K, Kp, Np, w, sw, cs, b, rows_cap, err, sizeof err, &kind)) {
     ERR(kind, "bnn_pw_s8_new: %s", err);
     bnn_pw_s8_free(o);
     return NULL;

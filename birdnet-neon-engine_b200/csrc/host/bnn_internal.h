@@ -138,7 +138,7 @@ int bnn_rt_run(bnn_ctx *c, int i, int n, const float *d_pcm, void *stream);
 int c0_quantizes_next(const bnn_ctx *c, int i);
 void bnn_rt_close(bnn_ctx *c);
 int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src, const float *sw_src,
-                   const int32_t *cs_src, const float *b_src, char *err, size_t errlen, int *kind);
+                   const int32_t *cs_src, const float *b_src, int rows_cap, char *err, size_t errlen, int *kind);
 int bnn_proto_weights(bnn_devop *d, int N, int Kp, int Np, const int8_t *src, const float *sw_src, const float *cw,
                       const float *cb, int nc, float eps, char *err, size_t errlen, int *kind);
 int bnn_proto_n4_check(const int8_t *qw, int Kp, const uint8_t *n4, int npanels);

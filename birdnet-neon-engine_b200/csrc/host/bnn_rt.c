@@ -614,9 +614,9 @@ static int fe_tables(bnn_ctx *c, bnn_dev *dv, const bnn_op *op, char *err, size_
 /* int8 GEMM weights in the GEMM's layout: the package's panels [Np/4][Kp/16][4][16] (lower.py:883-914) as rows
  * [n_tiles * bn][Kq] (Kq = K rounded up to 32), zero beyond N and K; scales, column sums and biases padded with zeros */
 int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src, const float *sw_src,
-                   const int32_t *cs_src, const float *b_src, char *err, size_t errlen, int *kind) {
+                   const int32_t *cs_src, const float *b_src, int rows_cap, char *err, size_t errlen, int *kind) {
   (void)N;
-  const int kq = R32(K), rows = bnnk_gemm_weight_rows(Np);
+  const int kq = R32(K), rows = bnnk_gemm_weight_rows(Np, rows_cap);
   d->kq = kq;
   int8_t *w = calloc((size_t)rows * kq, 1);
   float *sw = calloc(rows, sizeof(float)), *b = calloc(rows, sizeof(float));
@@ -673,6 +673,7 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
   case BNN_OP_PW_S8:
   case BNN_OP_GEMV_S8:
     return bnn_s8_weights(d, p[0], p[1], p[2], p[3], tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), tptr(c, op, 3),
+                          c->batch * (op->code == BNN_OP_PW_S8 ? p[4] : 1),
                           err, errlen, kind);
   case BNN_OP_DW3: {
     const int C = p[2];
