@@ -298,6 +298,28 @@ def test_batch_split_invariance(lib, mini_pkg):
     assert bits_equal(a, b) and bits_equal(ea, eb)
 
 
+def test_graph_replay(lib, mini_pkg):
+    """Launch sequences are replayed from CUDA graphs from the second call with the same windows and input buffer on:
+    four calls with different audio (the 1st eager, the 2nd captured, the 3rd and 4th replayed; both upload buffers),
+    each against the oracle; then the device entry point the same way."""
+    n = 6
+    with Model(mini_pkg, mode=4, batch=3) as m:  # chunks of 3 windows alternate between the two upload buffers
+        for call in range(4):
+            pcm = synth.audio(n, seed=100 + call)
+            want, wemb = oracle.run_many(mini_pkg, pcm, threads=4)
+            got, gemb = m.infer_batch(pcm)
+            assert bits_equal(got, want) and bits_equal(gemb, wemb), (call, mismatch_report(got, want))
+        d_out = torch.zeros((3, m.info.n_classes), dtype=torch.float32, device="cuda")
+        d_emb = torch.zeros((3, m.info.emb_dim), dtype=torch.float32, device="cuda")
+        d_pcm = torch.zeros((3, synth.NSAMP), dtype=torch.float32, device="cuda")
+        for call in range(3):
+            pcm = synth.audio(3, seed=200 + call)
+            d_pcm.copy_(torch.from_numpy(pcm))
+            m.infer_device(3, d_pcm.data_ptr(), d_out.data_ptr(), d_emb.data_ptr())
+            want, wemb = oracle.run_many(mini_pkg, pcm, threads=3)
+            assert bits_equal(host(d_out), want) and bits_equal(host(d_emb), wemb), call
+
+
 def test_device_entry_point(lib, mini_pkg):
     pcm = synth.audio(4, seed=2)
     with Model(mini_pkg, batch=4) as m:
