@@ -502,6 +502,10 @@ def main():
     if args.impl == "reference":
         reference_arm(args, rank)
         return
+    if args.ncu or args.proto_ncu:
+        # profiler captures use eager launches: a run that replays the op list from CUDA graphs stopped with a driver
+        # LaunchFailed under ncu (the same command exits 0 without ncu)
+        os.environ["BNN_GRAPHS"] = "0"
 
     import torch  # pylint: disable=import-outside-toplevel
     import torch.distributed as dist  # pylint: disable=import-outside-toplevel
