@@ -82,6 +82,10 @@ SIGNATURES = {
     "bnn_pw_s8_gemm": (_I, [_P, _I, _I, _P, _LL, _P, _P, _I, _P, _LL, _I, _I, _I, _P, _LL, _I, _I, _I, _P]),
     "bnn_pw_s8_error": (_I, [_P]),
     "bnn_pw_s8_free": (None, [_P]),
+    "bnn_logmel_new": (_P, [_I, _I, _I, _I, _I, _I, _P, _P, ctypes.c_float, ctypes.c_float]),
+    "bnn_logmel_frames": (_I, [_P]),
+    "bnn_logmel_run": (_I, [_P, _I, _P, _LL, _P, _LL, _P]),
+    "bnn_logmel_free": (None, [_P]),
     "bnn_proto_s8_new": (_P, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, ctypes.c_float, _I, _I]),
     "bnn_proto_s8_run": (_I, [_P, _I, _P, _LL, _I, _P, _LL, _P, _LL, _P, _P]),
     "bnn_proto_s8_read_scratch": (_I, [_P, _I, _P, _P]),

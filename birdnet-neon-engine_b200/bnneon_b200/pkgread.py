@@ -3,9 +3,10 @@ import struct
 
 # buffer arguments each kernel writes (the reference registry's outmask) and the ones that are the int8 path's row
 # scratch (q, sa, za), which the B200 runtime keeps in its own layout
-OUTMASK = {1: 0x2, 2: 0x2, 4: 0x6, 6: 0xE, 25: 0x2, 22: 0x3A, 23: 0x1E, 35: 0xE}
+OUTMASK = {1: 0x2, 2: 0x2, 4: 0x6, 6: 0xE, 8: 0x2, 25: 0x2, 22: 0x3A, 23: 0x1E, 35: 0xE}
 SCRATCH = {22: (3, 4, 5), 23: (2, 3, 4), 6: (2, 3), 35: (2,)}
-NAMES = {1: "FE_STFT2", 2: "C0POOL", 4: "DW3", 6: "POSTPC", 22: "PW_S8", 23: "GEMV_S8", 25: "SE_GATE", 35: "PROTO_S8"}
+NAMES = {1: "FE_STFT2", 2: "C0POOL", 4: "DW3", 6: "POSTPC", 8: "FE_LOGMEL", 22: "PW_S8", 23: "GEMV_S8", 25: "SE_GATE",
+         35: "PROTO_S8"}
 
 
 def read_ops(path, path_name="neon-int8"):

@@ -45,13 +45,13 @@ PATH = "neon-int8"
 
 # ------------------------------------------------------------------ the model IR
 
-def _mel_bank(nfft, fmin, fmax, nmel=96):
+def _mel_bank(nfft, fmin, fmax, nmel=96, rate=None):
     """Triangular filters on the HTK mel scale, [nmel][nfft/2 + 1] float32, zero at and above fmax."""
     bins = nfft // 2 + 1
     mel = lambda f: 2595.0 * np.log10(1.0 + f / 700.0)  # noqa: E731
     imel = lambda m: 700.0 * (10.0 ** (m / 2595.0) - 1.0)  # noqa: E731
     edges = imel(np.linspace(mel(fmin), mel(fmax), nmel + 2))
-    freqs = np.arange(bins) * SAMPLE_RATE / nfft
+    freqs = np.arange(bins) * (rate or SAMPLE_RATE) / nfft
     out = np.zeros((nmel, bins), np.float64)
     for j in range(nmel):
         lo, c, hi = edges[j], edges[j + 1], edges[j + 2]
@@ -578,6 +578,49 @@ def cells(n, n_cells, ld, seed=0, scale=1.0):
     for i in range(n):
         out[i] = np.random.default_rng((seed, i)).standard_normal((n_cells, ld)) * scale
     return out
+
+
+# ------------------------------------------------------------------ the framed log-mel front end (FE_LOGMEL)
+
+OPC_FE_LOGMEL = 8
+# Perch-like geometry (32 kHz, 5 s windows; 20 ms frames, 10 ms hop, 1024-point FFT, 128 mel bins): the real Perch
+# constants come from its ONNX graph, which is not available here
+PERCH_FE = dict(nsamp=160000, frame=640, hop=320, pad=0, nfft=1024, nmel=128, fmin=60.0, fmax=16000.0,
+                floor=1e-5, scale=1.0)
+
+
+def logmel_frontend(nsamp, frame, hop, pad, nfft, nmel, fmin=60.0, fmax=None, floor=1e-5, scale=1.0,
+                    rate=PERCH_SAMPLE_RATE):
+    """A log-mel front end: periodic Hann window of `frame` samples, triangular mel filters up to fmax (default
+    Nyquist) at `rate`."""
+    fmax = fmax or rate / 2.0
+    return dict(nsamp=nsamp, frame=frame, hop=hop, pad=pad, nfft=nfft, window=_hann(frame),
+                mel=_mel_bank(nfft, fmin, fmax, nmel, rate), floor=float(floor), scale=float(scale))
+
+
+def logmel_frames(fe):
+    return (fe["nsamp"] + 2 * fe["pad"] - fe["frame"]) // fe["hop"] + 1
+
+
+def write_logmel_package(dst, fe, model_id="perch_v2_frontend_synthetic"):
+    """A one-op neon-int8 package: FE_LOGMEL on the input window, the spectrogram [frames][nmel] out (as lower.py
+    l_fe_logmel writes the op: tensors fe/window, fe/mel, fe/consts; buffer [frames][nmel]). n_classes in the
+    metadata is the spectrogram's size. Returns (frames, nmel)."""
+    nmel = fe["mel"].shape[0]
+    nfr = logmel_frames(fe)
+    lw = _Int8Lowering([])
+    lw.bufs = [(F32, 1, 1, fe["nsamp"], fe["nsamp"], 0, fe["nsamp"])]
+    tl = [lw.tensor("fe/window", fe["window"]), lw.tensor("fe/mel", fe["mel"]),
+          lw.tensor("fe/consts", np.array([fe["floor"], fe["scale"]], np.float32))]
+    ob = lw.buf(F32, nfr, nmel, 1)
+    lw.emit(OPC_FE_LOGMEL, [0, ob], tl, [fe["nsamp"], fe["frame"], fe["hop"], fe["pad"], fe["nfft"], nmel], {})
+    bufs = plan_slots(lw.bufs, lw.records, [ob])
+    n_out = nfr * nmel
+    meta = [(f"src_nodes/{PATH}", "\n".join(lw.src))] + metadata(
+        n_out, 0, labels_for(n_out), model_id=model_id, family=BNN_MODEL_PERCH_V2, sample_rate=PERCH_SAMPLE_RATE,
+        n_samples=fe["nsamp"], attribution="synthetic log-mel front end")
+    write_package(dst, meta, lw.tensors, [(PATH, 0, bufs, lw.records, 0, ob, None)])
+    return nfr, nmel
 
 
 # ------------------------------------------------------------------ audio

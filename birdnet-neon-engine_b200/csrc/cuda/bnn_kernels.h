@@ -121,6 +121,18 @@ typedef struct {
 int bnnk_fe_stft2(int B, const float *pcm, long long pws, const bnnk_fe_tables *t, float *minmax, float *img,
                   long long iws, bnn_stream_t st);
 
+/* ---- the framed log-mel front end (FE_LOGMEL): pcm [B][nsamp] -> spec [B][nfr][nmel]. Device tables: window
+ * [nfft] (zero past frame), twiddles [M / 2], real-split cos / sin [khi], the sparse mel (row offsets [nmel + 1],
+ * bins and weights of the nonzero entries) */
+typedef struct {
+  int nsamp, frame, hop, pad, nfft, M, lg, nmel, nfr, klo, khi, nz;
+  float floor_, scale;
+  const float *win, *tw_re, *tw_im, *pc, *ps, *mel_w;
+  const int *mel_off, *mel_k;
+} bnnk_logmel_tables;
+int bnnk_logmel(int B, const float *pcm, long long pws, const bnnk_logmel_tables *t, float *spec, long long sws,
+                bnn_stream_t st);
+
 /* ---- the int8 prototype head (PROTO_S8) */
 
 /* per-cell quantization (pc_quant_cells_f32): cells r = w * P + p of x (window stride xws, row stride ld floats;

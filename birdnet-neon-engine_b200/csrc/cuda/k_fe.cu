@@ -270,6 +270,105 @@ __global__ void __launch_bounds__(512) k_fe_minmax(const float *__restrict__ pcm
   }
 }
 
+// ------------------------------------------------------------------ FE_LOGMEL (src/pc_kern_f32.c:85-149)
+// The framed log-mel front end of compiled models (Perch): any power-of-two nfft from 16 to 2048. The arithmetic is
+// the reference's, element for element (group(), one lane per frame): windowed samples in bit-reversed order, the
+// same DIT transform as FE_STFT2 (the butterflies above), |X_k| from the real split, the sparse mel over the nonzero
+// weights with two alternating accumulators, ln = log2_acc * 0.69314718, times scale. Schedule (ours): one CTA per
+// (kLmFrames frames, window); each frame's M points live in shared memory and kLmThreads threads run the passes
+// over them (first two levels fused, radix-2^2 level pairs, a last radix-2 level when log2 M is odd).
+
+constexpr int kLmFrames = 2, kLmThreads = 128;
+
+__global__ void __launch_bounds__(kLmFrames * kLmThreads) k_logmel(const float *__restrict__ pcm, long long pws,
+                                                                 const bnnk_logmel_tables t, float *__restrict__ spec,
+                                                                 long long sws) {
+  extern __shared__ float lsm[];
+  const int M = t.M, lg = t.lg;
+  const int fl = threadIdx.x / kLmThreads, lt = threadIdx.x % kLmThreads;
+  const int f = blockIdx.x * kLmFrames + fl, win = blockIdx.y;
+  float *re = lsm + fl * (3 * M + 2), *im = re + M, *mag = im + M;
+  const float *x = pcm + win * pws;
+  const bool live = f < t.nfr;
+  {
+    // z[n] = w[2n] y[st + 2n] + i w[2n + 1] y[st + 2n + 1] (y: pad zeros, the window's samples, zeros); 0 past the
+    // frame's (frame + 1) / 2 points
+    const int st = f * t.hop - t.pad;
+    for (int n = lt; n < M; n += kLmThreads) {
+      float vr = 0.f, vi = 0.f;
+      if (live && n < t.nz) {
+        const int i0 = st + 2 * n, i1 = i0 + 1;
+        const float y0 = (i0 >= 0 && i0 < t.nsamp) ? __ldg(x + i0) : 0.f;
+        const float y1 = (i1 >= 0 && i1 < t.nsamp) ? __ldg(x + i1) : 0.f;
+        vr = __fmul_rn(y0, __ldg(t.win + 2 * n));
+        vi = __fmul_rn(y1, __ldg(t.win + 2 * n + 1));
+      }
+      const int r = (int)(__brev((unsigned)n) >> (32 - lg));
+      re[r] = vr;
+      im[r] = vi;
+    }
+  }
+  __syncthreads();
+  for (int g = lt; g < M / 4; g += kLmThreads) {  // levels 1-2 (fft_tab.h:28-38)
+    const int i = 4 * g;
+    cpx a = {re[i], im[i]}, b = {re[i + 1], im[i + 1]}, c = {re[i + 2], im[i + 2]}, d = {re[i + 3], im[i + 3]};
+    r4first(a, b, c, d);
+    re[i] = a.r; im[i] = a.i; re[i + 1] = b.r; im[i + 1] = b.i;
+    re[i + 2] = c.r; im[i + 2] = c.i; re[i + 3] = d.r; im[i + 3] = d.i;
+  }
+  __syncthreads();
+  int len = 8;
+  for (; 2 * len <= M; len <<= 2) {  // radix-2^2 over the level pair (len, 2 len) (fft_tab.h:40-64)
+    const int h = len / 2, st1 = M / len, st2 = M / (2 * len);
+    for (int q = lt; q < M / 4; q += kLmThreads) {
+      const int j = q % h, i = (q / h) * 2 * len + j;
+      cpx a = {re[i], im[i]}, b = {re[i + h], im[i + h]}, c = {re[i + 2 * h], im[i + 2 * h]},
+          d = {re[i + 3 * h], im[i + 3 * h]};
+      r22(a, b, c, d, __ldg(t.tw_re + j * st1), __ldg(t.tw_im + j * st1), __ldg(t.tw_re + j * st2),
+          __ldg(t.tw_im + j * st2));
+      re[i] = a.r; im[i] = a.i; re[i + h] = b.r; im[i + h] = b.i;
+      re[i + 2 * h] = c.r; im[i + 2 * h] = c.i; re[i + 3 * h] = d.r; im[i + 3 * h] = d.i;
+    }
+    __syncthreads();
+  }
+  for (; len <= M; len <<= 1) {  // a last radix-2 level (fft_tab.h:65-76)
+    const int half = len / 2, step = M / len;
+    for (int q = lt; q < M / 2; q += kLmThreads) {
+      const int j = q % half, i = (q / half) * len + j;
+      const cpx v = cmul({re[i + half], im[i + half]}, __ldg(t.tw_re + j * step), __ldg(t.tw_im + j * step));
+      const float ur = re[i], ui = im[i];
+      re[i] = __fadd_rn(ur, v.r); im[i] = __fadd_rn(ui, v.i);
+      re[i + half] = __fsub_rn(ur, v.r); im[i + half] = __fsub_rn(ui, v.i);
+    }
+    __syncthreads();
+  }
+  // |X_k|: A = Z_k, B = conj Z_{M-k}; E = (A + B) / 2, O = (A - B) / (2i); X = E + W^k O
+  for (int k = t.klo + lt; k < t.khi; k += kLmThreads) {
+    const int k2 = (k == 0 || k == M) ? 0 : M - k, ka = k == M ? 0 : k;
+    const float Ar = re[ka], Ai = im[ka], Br = re[k2], Bi = -im[k2];
+    const float Er = __fmul_rn(__fadd_rn(Ar, Br), 0.5f), Ei = __fmul_rn(__fadd_rn(Ai, Bi), 0.5f);
+    const float Or = __fmul_rn(__fsub_rn(Ai, Bi), 0.5f), Oi = __fmul_rn(__fsub_rn(Br, Ar), 0.5f);
+    const float c = __ldg(t.pc + k), sn = __ldg(t.ps + k);
+    const float Xr = __fmaf_rn(Oi, sn, __fmaf_rn(Or, c, Er));
+    const float Xi = __fmaf_rn(-Or, sn, __fmaf_rn(Oi, c, Ei));
+    mag[k] = __fsqrt_rn(__fmaf_rn(Xi, Xi, __fmul_rn(Xr, Xr)));
+  }
+  __syncthreads();
+  if (!live) return;
+  float *out = spec + win * sws + (long long)f * t.nmel;
+  for (int j = lt; j < t.nmel; j += kLmThreads) {
+    float a0 = 0.f, a1 = 0.f;
+    int e = __ldg(t.mel_off + j);
+    const int e1 = __ldg(t.mel_off + j + 1);
+    for (; e + 2 <= e1; e += 2) {
+      a0 = __fmaf_rn(mag[__ldg(t.mel_k + e)], __ldg(t.mel_w + e), a0);
+      a1 = __fmaf_rn(mag[__ldg(t.mel_k + e + 1)], __ldg(t.mel_w + e + 1), a1);
+    }
+    if (e < e1) a0 = __fmaf_rn(mag[__ldg(t.mel_k + e)], __ldg(t.mel_w + e), a0);
+    out[j] = __fmul_rn(__fmul_rn(log2_acc(fmax_nan(__fadd_rn(a0, a1), t.floor_)), 0.69314718f), t.scale);
+  }
+}
+
 }  // namespace bnn
 
 using namespace bnn;
@@ -294,5 +393,15 @@ extern "C" int bnnk_fe_stft2(int B, const float *pcm, long long pws, const bnnk_
   }
   k_fe_minmax<<<B, 512, 0, st>>>(pcm, pws, minmax);
   k_fe_spec<<<dim3((kNfr + kFG - 1) / kFG, 2, B), 256, smem, st>>>(pcm, pws, minmax, *t, img, iws);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_logmel(int B, const float *pcm, long long pws, const bnnk_logmel_tables *t, float *spec,
+                           long long sws, bnn_stream_t st) {
+  if (B <= 0 || t->nfr <= 0) return 0;
+  if (B > 65535) return cudaErrorInvalidValue;
+  const size_t smem = sizeof(float) * (size_t)kLmFrames * (3 * t->M + 2);
+  const dim3 grid((t->nfr + kLmFrames - 1) / kLmFrames, B);
+  k_logmel<<<grid, kLmFrames * kLmThreads, smem, st>>>(pcm, pws, *t, spec, sws);
   return cudaGetLastError();
 }

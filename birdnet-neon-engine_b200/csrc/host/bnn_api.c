@@ -52,7 +52,7 @@ static const struct { int mode; const char *name, *precision; } PATHS[] = {
 /* 1 when every op of path i has a GPU kernel here (the int8 path's ops, variant 0) */
 static int path_runs_here(const bnn_pkg *p, int i) {
   static const int codes[] = {BNN_OP_FE_STFT2, BNN_OP_C0POOL, BNN_OP_PW_S8, BNN_OP_DW3, BNN_OP_SE_GATE,
-                              BNN_OP_POSTPC, BNN_OP_GEMV_S8, BNN_OP_PROTO_S8};
+                              BNN_OP_POSTPC, BNN_OP_GEMV_S8, BNN_OP_PROTO_S8, BNN_OP_FE_LOGMEL};
   const bnn_path_rec *d = &p->paths[i];
   const uint8_t *q = p->map + d->ops_off, *end = q + d->ops_bytes;
   for (uint32_t k = 0; k < d->n_ops; k++) {
@@ -829,6 +829,52 @@ void bnn_pw_s8_free(bnn_pw_s8 *o) {
   if (!o) return;
   cudaFree(o->op.w); cudaFree(o->op.sw); cudaFree(o->op.bias); cudaFree(o->op.cs);
   cudaFree(o->q); cudaFree(o->sa); cudaFree(o->za); cudaFree(o->err);
+  free(o);
+}
+
+/* ---- FE_LOGMEL (src/rt_ops_f32.c:362-385, src/pc_kern_f32.c:14-149) */
+
+struct bnn_logmel {
+  bnn_devop op;
+};
+
+bnn_logmel *bnn_logmel_new(int nsamp, int frame, int hop, int pad, int nfft, int nmel, const float *window,
+                           const float *mel, float floor_, float scale) {
+  /* logmel_init's and pc_logmel_new's limits */
+  if (!window || !mel || nsamp <= 0 || frame <= 0 || hop <= 0 || pad < 0 || nfft < frame || nmel <= 0 ||
+      (nfft & (nfft - 1)) || nfft < 16 || nfft > 2048 || nmel > 512) {
+    ERR(BNN_ERR_USAGE, "bnn_logmel_new: nsamp %d frame %d hop %d pad %d nfft %d nmel %d (expected nfft a power of two "
+        "in 16..2048, 0 < frame <= nfft, hop > 0, pad >= 0, 1 <= nmel <= 512)", nsamp, frame, hop, pad, nfft, nmel);
+    return NULL;
+  }
+  bnn_logmel *o = calloc(1, sizeof *o);
+  if (!o) { ERR(BNN_ERR_OOM, "out of memory"); return NULL; }
+  char err[512];
+  int kind = BNN_ERR_CPU;
+  if (bnn_logmel_build(&o->op, nsamp, frame, hop, pad, nfft, nmel, window, mel, floor_, scale, err, sizeof err, &kind)) {
+    ERR(kind, "bnn_logmel_new: %s", err);
+    bnn_logmel_free(o);
+    return NULL;
+  }
+  return o;
+}
+
+int bnn_logmel_frames(const bnn_logmel *o) { return o ? o->op.lm.nfr : -1; }
+
+int bnn_logmel_run(bnn_logmel *o, int B, const float *d_pcm, long long pws, float *d_spec, long long sws,
+                   void *stream) {
+  if (!o || B < 0 || B > 65535 || !d_pcm || !d_spec || (B > 1 && (pws < o->op.lm.nsamp ||
+                                                                  sws < (long long)o->op.lm.nfr * o->op.lm.nmel))) {
+    ERR(BNN_ERR_USAGE, "bnn_logmel_run: B %d window strides %lld / %lld (expected 0 <= B <= 65535, strides >= nsamp "
+        "and >= frames x mel bins)", B, pws, sws);
+    return -1;
+  }
+  return launch_rc("bnn_logmel_run", bnnk_logmel(B, d_pcm, pws, &o->op.lm, d_spec, sws, (bnn_stream_t)stream));
+}
+
+void bnn_logmel_free(bnn_logmel *o) {
+  if (!o) return;
+  bnn_logmel_release(&o->op);
   free(o);
 }
 

@@ -47,7 +47,7 @@ const char *bnn_dtype_name(uint32_t dt);
 /* ---- opcodes of the registry (src/rt.h:170-208; append-only, the same numbers) */
 enum {
   BNN_OP_FE_STFT2 = 1, BNN_OP_C0POOL = 2, BNN_OP_PW = 3, BNN_OP_DW3 = 4, BNN_OP_SE = 5, BNN_OP_POSTPC = 6,
-  BNN_OP_DENSE = 7, BNN_OP_PW_S8 = 22, BNN_OP_GEMV_S8 = 23, BNN_OP_SE_GATE = 25, BNN_OP_PROTO_S8 = 35, BNN_OP_N = 36
+  BNN_OP_DENSE = 7, BNN_OP_FE_LOGMEL = 8, BNN_OP_PW_S8 = 22, BNN_OP_GEMV_S8 = 23, BNN_OP_SE_GATE = 25, BNN_OP_PROTO_S8 = 35, BNN_OP_N = 36
 };
 enum { BNN_ACT_NONE = 0, BNN_ACT_SILU = 1, BNN_ACT_RELU = 2 };
 
@@ -71,6 +71,9 @@ typedef struct {
   /* PROTO_S8: prototype rows w [Np][Kp], sw, the GEMM plan, eps */
   bnnk_proto_plan pplan;
   float eps;
+  /* FE_LOGMEL: the device tables and their allocations */
+  bnnk_logmel_tables lm;
+  void *lm_mem[8];
 } bnn_devop;
 
 typedef struct {
@@ -142,6 +145,10 @@ int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src
 int bnn_proto_weights(bnn_devop *d, int N, int Kp, int Np, const int8_t *src, const float *sw_src, const float *cw,
                       const float *cb, int nc, float eps, char *err, size_t errlen, int *kind);
 int bnn_proto_n4_check(const int8_t *qw, int Kp, const uint8_t *n4, int npanels);
+/* pc_logmel_new's tables on the current device (t points into d->lm_mem); -1 with err set on failure */
+int bnn_logmel_build(bnn_devop *d, int nsamp, int frame, int hop, int pad, int nfft, int nmel, const float *window,
+                     const float *mel, float floor_, float scale, char *err, size_t errlen, int *kind);
+void bnn_logmel_release(bnn_devop *d);
 
 /* errors (bnn_api.c): thread-local message and kind */
 void bnn_set_error(int kind, const char *fmt, ...) __attribute__((format(printf, 2, 3)));

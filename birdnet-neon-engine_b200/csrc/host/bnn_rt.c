@@ -277,6 +277,20 @@ int bnn_proto_n4_check(const int8_t *qw, int Kp, const uint8_t *n4, int npanels)
   return -1;
 }
 
+static int init_fe_logmel(vctx *v) { /* logmel_init (src/rt_ops_f32.c:364-380) */
+  if (vneed_args(v, 2, 3, 6)) return -1;
+  const int *p = v->op->p;
+  VREQ(v, p[0] > 0 && p[1] > 0 && p[2] > 0 && p[3] >= 0 && p[4] >= p[1] && p[5] > 0);
+  if (vneed_t(v, 0, (size_t)p[1] * 4, 0) || vneed_t(v, 1, (size_t)p[5] * (p[4] / 2 + 1) * 4, 0) || vneed_t(v, 2, 8, 0))
+    return -1;
+  if (vneed(v, 0, BNN_F32, (size_t)p[0]) || vneed(v, 1, BNN_F32, 1)) return -1;
+  /* the FFT's limits (pc_kern_f32.c pc_logmel_new): nfft a power of two in 16..2048, frame <= nfft, nmel <= 512 */
+  VREQ(v, (p[4] & (p[4] - 1)) == 0 && p[4] >= 16 && p[4] <= 2048); /* nfft */
+  VREQ(v, p[1] <= p[4] && p[5] <= 512);                            /* frame, nmel */
+  const int nfr = (p[0] + 2 * p[3] - p[1]) / p[2] + 1;
+  return vneed(v, 1, BNN_F32, (size_t)nfr * p[5]);
+}
+
 static int init_proto_s8(vctx *v) { /* proto8n_init (src/rt_ops_s8n.c:220-240) after rt_proto_geom / rt_proto_io
                                      * (src/rt_ops_f32.c:525-545) */
   if (vneed_args(v, 4, 6, 9)) return -1;
@@ -320,6 +334,7 @@ static const kdesc KERNELS[] = {
     {BNN_OP_PW_S8, "pw_s8n", init_pw_s8, 0x3a, 0x44, 2},
     {BNN_OP_GEMV_S8, "gemv_s8n", init_gemv_s8, 0x1e, 0, 2},
     {BNN_OP_PROTO_S8, "proto_s8n", init_proto_s8, 0xe, 0, 3},
+    {BNN_OP_FE_LOGMEL, "fe_logmel", init_fe_logmel, 0x2, 0, 1},
 };
 static const kdesc *kernel_for(int code) {
   if (code >> 8) return NULL; /* variants 1 and 2 are the fp16 / dotprod CPU paths: no GPU kernels */
@@ -422,8 +437,8 @@ int bnn_rt_open(bnn_ctx *c, char *err, size_t errlen, int *kind) {
       if (bnn_meta_str(c->pkg, "compiler", comp, sizeof comp) < 0) snprintf(comp, sizeof comp, "unknown");
       *kind = BNN_ERR_CPU;
       return vbad(&v, "opcode 0x%x (base %d variant %d) has no B200 kernel in this library (it runs the neon-int8 ops "
-                  "FE_STFT2, C0POOL, PW_S8, DW3, SE_GATE, POSTPC, GEMV_S8 and PROTO_S8; the package was written by compiler "
-                  "'%s')",
+                  "FE_STFT2, C0POOL, PW_S8, DW3, SE_GATE, POSTPC, GEMV_S8, PROTO_S8 and FE_LOGMEL; the package was "
+                  "written by compiler '%s')",
                   op->code, op->code & 0xff, var, comp);
     }
     op->kname = k->name;
@@ -664,6 +679,73 @@ int bnn_proto_weights(bnn_devop *d, int N, int Kp, int Np, const int8_t *src, co
   return rc;
 }
 
+/* pc_logmel_new (src/pc_kern_f32.c:28-72): the window zero past frame; twiddles e^{-2 pi i k / M} and the real-split
+ * cos / sin (2 pi k / nfft) in double, rounded once; the sparse mel as each row's nonzero entries in bin order; [klo,
+ * khi) the bins any row uses (0, 0 when none) */
+int bnn_logmel_build(bnn_devop *d, int nsamp, int frame, int hop, int pad, int nfft, int nmel, const float *window,
+                     const float *mel, float floor_, float scale, char *err, size_t errlen, int *kind) {
+  bnnk_logmel_tables *t = &d->lm;
+  memset(t, 0, sizeof *t);
+  const int M = nfft / 2, bins = nfft / 2 + 1;
+  t->nsamp = nsamp; t->frame = frame; t->hop = hop; t->pad = pad; t->nfft = nfft; t->M = M; t->nmel = nmel;
+  t->nfr = (nsamp + 2 * pad - frame) / hop + 1;
+  while ((1 << t->lg) < M) t->lg++;
+  t->nz = (frame + 1) / 2;
+  t->floor_ = floor_;
+  t->scale = scale;
+  t->klo = bins;
+  int nnz = 0;
+  for (int j = 0; j < nmel; j++)
+    for (int k = 0; k < bins; k++)
+      if (mel[(size_t)j * bins + k] != 0.f) { nnz++; if (k < t->klo) t->klo = k; if (k + 1 > t->khi) t->khi = k + 1; }
+  if (t->khi == 0) t->klo = 0;
+  float *win = calloc((size_t)nfft, sizeof(float)), *twr = malloc(sizeof(float) * (size_t)(M / 2 + 1)),
+        *twi = malloc(sizeof(float) * (size_t)(M / 2 + 1)), *pc = malloc(sizeof(float) * (size_t)(t->khi + 1)),
+        *ps = malloc(sizeof(float) * (size_t)(t->khi + 1)), *mw = malloc(sizeof(float) * (size_t)(nnz + 1));
+  int *moff = malloc(sizeof(int) * (size_t)(nmel + 1)), *mk = malloc(sizeof(int) * (size_t)(nnz + 1));
+  int rc = 0;
+  if (!win || !twr || !twi || !pc || !ps || !mw || !moff || !mk) {
+    *kind = BNN_ERR_OOM;
+    snprintf(err, errlen, "out of memory (log-mel tables)");
+    rc = -1;
+  } else {
+    memcpy(win, window, sizeof(float) * (size_t)frame);
+    for (int k = 0; k < M / 2; k++) {
+      const double a = -2 * M_PI * k / M;
+      twr[k] = (float)cos(a); twi[k] = (float)sin(a);
+    }
+    for (int k = 0; k < t->khi; k++) {
+      const double a = 2 * M_PI * k / nfft;
+      pc[k] = (float)cos(a); ps[k] = (float)sin(a);
+    }
+    nnz = 0;
+    for (int j = 0; j < nmel; j++) {
+      moff[j] = nnz;
+      for (int k = 0; k < bins; k++)
+        if (mel[(size_t)j * bins + k] != 0.f) { mk[nnz] = k; mw[nnz] = mel[(size_t)j * bins + k]; nnz++; }
+    }
+    moff[nmel] = nnz;
+    const void *src[8] = {win, twr, twi, pc, ps, mw, moff, mk};
+    const size_t sz[8] = {sizeof(float) * (size_t)nfft, sizeof(float) * (size_t)(M / 2 + 1),
+                          sizeof(float) * (size_t)(M / 2 + 1), sizeof(float) * (size_t)(t->khi + 1),
+                          sizeof(float) * (size_t)(t->khi + 1), sizeof(float) * (size_t)(nnz + 1),
+                          sizeof(int) * (size_t)(nmel + 1), sizeof(int) * (size_t)(nnz + 1)};
+    for (int i = 0; i < 8 && !rc; i++) rc = upload(&d->lm_mem[i], src[i], sz[i], err, errlen, kind);
+    if (!rc) {
+      t->win = d->lm_mem[0]; t->tw_re = d->lm_mem[1]; t->tw_im = d->lm_mem[2]; t->pc = d->lm_mem[3];
+      t->ps = d->lm_mem[4]; t->mel_w = d->lm_mem[5]; t->mel_off = d->lm_mem[6]; t->mel_k = d->lm_mem[7];
+    }
+  }
+  free(win); free(twr); free(twi); free(pc); free(ps); free(mw); free(moff); free(mk);
+  return rc;
+}
+void bnn_logmel_release(bnn_devop *d) {
+  for (int i = 0; i < 8; i++) {
+    cudaFree(d->lm_mem[i]);
+    d->lm_mem[i] = NULL;
+  }
+}
+
 /* the weights of op i in the kernels' layouts */
 static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, int *kind) {
   const bnn_op *op = &c->ops[i];
@@ -709,6 +791,11 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
   }
   case BNN_OP_FE_STFT2:
     return fe_tables(c, dv, op, err, errlen, kind);
+  case BNN_OP_FE_LOGMEL: {
+    const float *k = tptr(c, op, 2);
+    return bnn_logmel_build(d, p[0], p[1], p[2], p[3], p[4], p[5], tptr(c, op, 0), tptr(c, op, 1), k[0], k[1], err,
+                            errlen, kind);
+  }
   case BNN_OP_PROTO_S8:
     return bnn_proto_weights(d, p[0], p[2], p[3], tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 3), tptr(c, op, 4),
                              p[7], ((const float *)tptr(c, op, 5))[0], err, errlen, kind);
@@ -837,6 +924,7 @@ void bnn_rt_device_free(bnn_ctx *c, int di) {
       bnn_devop *o = &dv->ops[i];
       cudaFree(o->w); cudaFree(o->sw); cudaFree(o->bias); cudaFree(o->cs);
       for (int k = 0; k < 6; k++) cudaFree(o->f[k]);
+      bnn_logmel_release(o);
     }
   for (int k = 0; k < dv->n_fe_mem; k++) cudaFree(dv->fe_mem[k]);
   if (dv->events)
@@ -949,6 +1037,9 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
       break;
     case BNN_OP_POSTPC:
       rc = bnnk_postpc(n, IN_(0), INWS(0), o->f[2], o->f[3], o->f[0], o->f[1], dv->pcin, B_(1), WS(1), st);
+      break;
+    case BNN_OP_FE_LOGMEL:
+      rc = bnnk_logmel(n, IN_(0), INWS(0), &o->lm, B_(1), WS(1), st);
       break;
     case BNN_OP_PROTO_S8:
       rc = bnnk_proto_quant(n, p[4], IN_(0), INWS(0), p[6], p[5], p[2], o->eps, dv->q, dv->sa, st);

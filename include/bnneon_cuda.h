@@ -105,6 +105,19 @@ int bnn_pw_s8_run_static(bnn_pw_s8 *op, int B, int Mw, const float *d_x, long lo
 int bnn_pw_s8_error(bnn_pw_s8 *op);
 void bnn_pw_s8_free(bnn_pw_s8 *op);
 
+/* FE_LOGMEL, the framed log-mel front end of compiled models such as Perch (src/pc_kern_f32.c:14-149 driven by
+ * src/rt_ops_f32.c:362-385), batched: the package's tensors (host pointers) window [frame], mel [nmel][nfft / 2 + 1],
+ * floor, scale; nfft a power of two in 16..2048, frame <= nfft, nmel <= 512. A window of nsamp samples gives
+ * bnn_logmel_frames() = (nsamp + 2 pad - frame) / hop + 1 frames of nmel log-mel values. */
+typedef struct bnn_logmel bnn_logmel;
+bnn_logmel *bnn_logmel_new(int nsamp, int frame, int hop, int pad, int nfft, int nmel, const float *window,
+                           const float *mel, float floor_, float scale);
+int bnn_logmel_frames(const bnn_logmel *op);
+/* d_pcm [B][nsamp] (window stride pws floats) -> d_spec [B][frames][nmel] (window stride sws floats) */
+int bnn_logmel_run(bnn_logmel *op, int B, const float *d_pcm, long long pws, float *d_spec, long long sws,
+                   void *stream);
+void bnn_logmel_free(bnn_logmel *op);
+
 /* PROTO_S8, the int8 prototype head (src/rt_ops_s8n.c:212-250: pc_quant_cells_f32 and pc_proto_colmax_s8n,
  * src/proto_s8n.c:28-164, then pc_proto_logits, src/pc_kern_f32.c:364-376), batched. The package's tensors (host
  * pointers): prototypes qw [Np/4][Kp/16][4][16] int8, sw [Np], n4 [Np/4] (checked as pc_proto_n4_check does; the GPU

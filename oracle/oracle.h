@@ -63,6 +63,17 @@ bnno_fe *bnno_fe_new(const float *win1, const float *win2, const float *mel1, co
 void bnno_fe_run(const bnno_fe *f, const float *pcm, float *img);
 void bnno_fe_free(bnno_fe *f);
 
+/* ---- FE_LOGMEL, the framed log-mel front end (src/pc_kern_f32.c:14-149, record src/rt_ops_f32.c:362-385) */
+typedef struct bnno_logmel bnno_logmel;
+/* NULL when the geometry is outside pc_logmel_new's limits (nfft a power of two in 16..2048, frame <= nfft, hop > 0,
+ * pad >= 0, 1 <= nmel <= 512); window [frame], mel [nmel][nfft / 2 + 1] */
+bnno_logmel *bnno_logmel_new(int nsamp, int frame, int hop, int pad, int nfft, int nmel, const float *window,
+                             const float *mel, float floor_, float scale);
+int bnno_logmel_frames(const bnno_logmel *f);
+/* pcm [nsamp] -> spec [nfr][nmel] */
+void bnno_logmel_run(const bnno_logmel *f, const float *pcm, float *spec);
+void bnno_logmel_free(bnno_logmel *f);
+
 /* ---- the int8 prototype head PROTO_S8 (src/proto_s8n.c, src/rt_ops_s8n.c:212-250, src/pc_kern_f32.c:364-376) */
 /* pc_quant_cells_f32: x [P][ld] -> qa [P][Kp] (ties away, never -128, zero past C), sx [P]; C % 8 == 0 */
 void bnno_proto_quant_cells(const float *x, int P, int C, int ld, float eps, int8_t *qa, int Kp, float *sx);

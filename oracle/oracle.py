@@ -22,6 +22,8 @@ SIGS = {
     "bnno_se_gate": (None, [_I, _I, _P, _P, _P, _P, _P, _I, _P]),
     "bnno_c0pool": (None, [_P, _P, _P, _P]),
     "bnno_postpc": (None, [_P, _P, _P, _P, _P, _P]),
+    "bnno_logmel_new": (_P, [_I, _I, _I, _I, _I, _I, _P, _P, _F, _F]),
+    "bnno_logmel_frames": (_I, [_P]), "bnno_logmel_run": (None, [_P, _P, _P]), "bnno_logmel_free": (None, [_P]),
     "bnno_proto_quant_cells": (None, [_P, _I, _I, _I, _F, _P, _I, _P]),
     "bnno_proto_unpack": (None, [_P, _I, _I, _P]),
     "bnno_proto_colmax": (None, [_P, _I, _P, _I, _P, _P, _I, _P]),
@@ -62,6 +64,26 @@ def fn(name, x):
     f = getattr(lib(), name)
     x = np.asarray(x, np.float32).reshape(-1)
     return np.array([f(float(v)) for v in x], np.float32)
+
+
+def logmel(pcm, frame, hop, pad, nfft, window, mel, floor, scale):
+    """FE_LOGMEL on windows pcm [n][nsamp]: spec [n][nfr][nmel] (None if the geometry is refused)."""
+    pcm = np.ascontiguousarray(pcm, np.float32)
+    window = np.ascontiguousarray(window, np.float32)
+    mel = np.ascontiguousarray(mel, np.float32)
+    h = lib()
+    f = h.bnno_logmel_new(pcm.shape[1], frame, hop, pad, nfft, mel.shape[0], ptr(window), ptr(mel), float(floor),
+                          float(scale))
+    if not f:
+        return None
+    try:
+        nfr = h.bnno_logmel_frames(f)
+        out = np.zeros((pcm.shape[0], max(nfr, 0), mel.shape[0]), np.float32)
+        for w in range(pcm.shape[0]):
+            h.bnno_logmel_run(f, ptr(pcm[w]), ptr(out[w]))
+        return out
+    finally:
+        h.bnno_logmel_free(f)
 
 
 def proto_unpack(qp):

@@ -494,6 +494,115 @@ static void fe_frame(const fe_spec *s, const float *y, int t, float *re, float *
   }
 }
 
+/* ------------------------------------------------------------------ FE_LOGMEL (src/pc_kern_f32.c:14-149) */
+
+struct bnno_logmel {
+  int nsamp, frame, hop, pad, nfft, M, lg, nmel, nfr, klo, khi;
+  float *win, *tw_re, *tw_im, *pc, *ps;
+  int *rev, *mel_off, *mel_k;
+  float *mel_w;
+  float floor_, scale;
+};
+
+/* pc_logmel_new (src/pc_kern_f32.c:28-72): frames nfr = (nsamp + 2 pad - frame) / hop + 1 (C division); the window
+ * zero past frame; twiddles and the real-split cos / sin in double, rounded once; the sparse mel as the NONZERO
+ * entries of each row in bin order (zeros inside a row are skipped); [klo, khi) the bins any row uses */
+bnno_logmel *bnno_logmel_new(int nsamp, int frame, int hop, int pad, int nfft, int nmel, const float *window,
+                             const float *mel, float floor_, float scale) {
+  if (nfft < 16 || nfft > 2048 || (nfft & (nfft - 1)) || frame > nfft || hop <= 0 || pad < 0 || nmel < 1 || nmel > 512)
+    return NULL;
+  bnno_logmel *f = calloc(1, sizeof *f);
+  f->nsamp = nsamp; f->frame = frame; f->hop = hop; f->pad = pad; f->nfft = nfft; f->M = nfft / 2; f->nmel = nmel;
+  f->nfr = (nsamp + 2 * pad - frame) / hop + 1;
+  while ((1 << f->lg) < f->M) f->lg++;
+  const int bins = nfft / 2 + 1;
+  f->klo = bins; f->khi = 0;
+  int nnz = 0;
+  for (int j = 0; j < nmel; j++)
+    for (int k = 0; k < bins; k++)
+      if (mel[(size_t)j * bins + k] != 0.f) { nnz++; if (k < f->klo) f->klo = k; if (k + 1 > f->khi) f->khi = k + 1; }
+  if (f->khi == 0) f->klo = 0;
+  f->win = calloc(nfft, sizeof(float));
+  memcpy(f->win, window, sizeof(float) * frame);
+  f->tw_re = malloc(sizeof(float) * (f->M / 2 + 1)); f->tw_im = malloc(sizeof(float) * (f->M / 2 + 1));
+  for (int k = 0; k < f->M / 2; k++) {
+    double a = -2 * M_PI * k / f->M;
+    f->tw_re[k] = (float)cos(a); f->tw_im[k] = (float)sin(a);
+  }
+  f->pc = malloc(sizeof(float) * (f->khi + 1)); f->ps = malloc(sizeof(float) * (f->khi + 1));
+  for (int k = 0; k < f->khi; k++) {
+    double a = 2 * M_PI * k / nfft;
+    f->pc[k] = (float)cos(a); f->ps[k] = (float)sin(a);
+  }
+  f->rev = malloc(sizeof(int) * f->M);
+  for (int i = 0; i < f->M; i++) {
+    int r = 0;
+    for (int bt = 0; bt < f->lg; bt++) r |= ((i >> bt) & 1) << (f->lg - 1 - bt);
+    f->rev[i] = r;
+  }
+  f->mel_off = malloc(sizeof(int) * (nmel + 1));
+  f->mel_k = malloc(sizeof(int) * (nnz + 1)); f->mel_w = malloc(sizeof(float) * (nnz + 1));
+  nnz = 0;
+  for (int j = 0; j < nmel; j++) {
+    f->mel_off[j] = nnz;
+    for (int k = 0; k < bins; k++)
+      if (mel[(size_t)j * bins + k] != 0.f) { f->mel_k[nnz] = k; f->mel_w[nnz] = mel[(size_t)j * bins + k]; nnz++; }
+  }
+  f->mel_off[nmel] = nnz;
+  f->floor_ = floor_; f->scale = scale;
+  return f;
+}
+int bnno_logmel_frames(const bnno_logmel *f) { return f->nfr; }
+void bnno_logmel_free(bnno_logmel *f) {
+  if (!f) return;
+  free(f->win); free(f->tw_re); free(f->tw_im); free(f->pc); free(f->ps); free(f->rev); free(f->mel_off);
+  free(f->mel_k); free(f->mel_w); free(f);
+}
+
+/* pc_logmel_run / group (src/pc_kern_f32.c:85-149), one frame at a time: y = pad zeros, pcm, zeros;
+ * z[n] = w[2n] y[st + 2n] + i w[2n + 1] y[st + 2n + 1] for n < (frame + 1) / 2, else 0, in bit-reversed order; the
+ * DIT transform; |X_k| = sqrt(Xr Xr + Xi Xi) (the square of Xr rounded, Xi Xi fused) from the real split
+ * Xr = fma(Oi, s, fma(Or, c, Er)), Xi = fma(-Or, s, fma(Oi, c, Ei)) with E = (A + B) / 2, O = (A - B) / (2i),
+ * A = Z_k, B = conj Z_{M-k}; mel over the nonzero weights with two alternating fused accumulators;
+ * spec = (log2_acc(max(a0 + a1, floor)) * 0.69314718) * scale (FMAX NaN-propagating). spec [nfr][nmel]. */
+void bnno_logmel_run(const bnno_logmel *f, const float *pcm, float *spec) {
+  const int M = f->M, nz = (f->frame + 1) / 2;
+  const size_t ylen = (size_t)(f->nfr > 0 ? f->nfr - 1 : 0) * f->hop + f->nfft + (size_t)f->nsamp + 2 * f->pad + 64;
+  float *y = calloc(ylen, sizeof(float));
+  memcpy(y + f->pad, pcm, sizeof(float) * f->nsamp);
+  float *re = malloc(sizeof(float) * M), *im = malloc(sizeof(float) * M), *mag = malloc(sizeof(float) * (M + 2));
+  for (int t = 0; t < f->nfr; t++) {
+    const int st = t * f->hop;
+    for (int n = 0; n < M; n++) {
+      if (n >= nz) { re[f->rev[n]] = 0.f; im[f->rev[n]] = 0.f; continue; }
+      re[f->rev[n]] = y[st + 2 * n] * f->win[2 * n];
+      im[f->rev[n]] = y[st + 2 * n + 1] * f->win[2 * n + 1];
+    }
+    fft_dit(re, im, M, f->tw_re, f->tw_im);
+    for (int k = f->klo; k < f->khi; k++) {
+      const int k2 = (k == 0 || k == M) ? 0 : M - k, ka = k == M ? 0 : k;
+      const float Ar = re[ka], Ai = im[ka], Br = re[k2], Bi = -im[k2];
+      const float Er = (Ar + Br) * 0.5f, Ei = (Ai + Bi) * 0.5f;
+      const float Or = (Ai - Bi) * 0.5f, Oi = (Br - Ar) * 0.5f;
+      const float c = f->pc[k], s = f->ps[k];
+      const float Xr = fmaf(Oi, s, fmaf(Or, c, Er));
+      const float Xi = fmaf(-Or, s, fmaf(Oi, c, Ei));
+      mag[k] = sqrtf(fmaf(Xi, Xi, Xr * Xr));
+    }
+    for (int j = 0; j < f->nmel; j++) {
+      float a0 = 0.f, a1 = 0.f;
+      int e = f->mel_off[j], e1 = f->mel_off[j + 1];
+      for (; e + 2 <= e1; e += 2) {
+        a0 = fmaf(mag[f->mel_k[e]], f->mel_w[e], a0);
+        a1 = fmaf(mag[f->mel_k[e + 1]], f->mel_w[e + 1], a1);
+      }
+      if (e < e1) a0 = fmaf(mag[f->mel_k[e]], f->mel_w[e], a0);
+      spec[(size_t)t * f->nmel + j] = (bnno_log2_acc(emu_fmax(a0 + a1, f->floor_)) * 0.69314718f) * f->scale;
+    }
+  }
+  free(y); free(re); free(im); free(mag);
+}
+
 /* b24_fe_run (src/v24_fe.c:192-224) */
 void bnno_fe_run(const bnno_fe *f, const float *pcm, float *img) {
   float mn = pcm[0], mx = pcm[0];

@@ -25,6 +25,7 @@ struct bnno_pkg {
   o_op *ops;
   void **buf;
   bnno_fe *fe;
+  bnno_logmel **logmel; /* per op: the FE_LOGMEL state (NULL for other ops) */
   int n_classes, emb_dim;
 };
 
@@ -103,8 +104,14 @@ bnno_pkg *bnno_pkg_open(const char *path, const char *path_name, char *err, size
   int64_t v;
   p->n_classes = meta_i64(m + off[0], off[1] - off[0], cnt[0], "n_classes", &v) ? 0 : (int)v;
   p->emb_dim = meta_i64(m + off[0], off[1] - off[0], cnt[0], "emb_dim", &v) ? 0 : (int)v;
+  p->logmel = calloc(p->n_ops, sizeof(bnno_logmel *));
   for (uint32_t i = 0; i < p->n_ops; i++) {
     const o_op *op = &p->ops[i];
+    if (op->code == 8) { /* FE_LOGMEL: t = window, mel, consts {floor, scale}; p = nsamp frame hop pad nfft nmel */
+      const float *k = tdata(p, op, 2);
+      p->logmel[i] = bnno_logmel_new(op->p[0], op->p[1], op->p[2], op->p[3], op->p[4], op->p[5], tdata(p, op, 0),
+                                     tdata(p, op, 1), k[0], k[1]);
+    }
     if ((op->code & 0xff) == 1) { /* FE_STFT2: t = win1 win2 mel1 mel2 pow1 pow2 bn_s bn_b */
       const float *pw1 = tdata(p, op, 4), *pw2 = tdata(p, op, 5);
       p->fe = bnno_fe_new(tdata(p, op, 0), tdata(p, op, 1), tdata(p, op, 2), tdata(p, op, 3), pw1[0], pw2[0],
@@ -121,6 +128,9 @@ void bnno_pkg_close(bnno_pkg *p) {
       if (i != p->in_buf) free(p->buf[i]);
   free(p->buf);
   free(p->bufd);
+  if (p->logmel)
+    for (uint32_t i = 0; i < p->n_ops; i++) bnno_logmel_free(p->logmel[i]);
+  free(p->logmel);
   free(p->ops);
   bnno_fe_free(p->fe);
   free(p->file);
@@ -176,6 +186,12 @@ static int run_op(bnno_pkg *p, const o_op *op) {
   case 6: /* POSTPC: b = [X, feat, pcin, pcout] */
     bnno_postpc(bptr(p, op, 0), tdata(p, op, 0), tdata(p, op, 1), tdata(p, op, 2), tdata(p, op, 3), bptr(p, op, 1));
     return 0;
+  case 8: { /* FE_LOGMEL: b = [pcm, spec] */
+    const bnno_logmel *f = p->logmel[op - p->ops];
+    if (!f) return -1;
+    bnno_logmel_run(f, bptr(p, op, 0), bptr(p, op, 1));
+    return 0;
+  }
   case 35: { /* PROTO_S8: b = [x, logits, qa, colmax]; t = [qw, sw, n4, cls w, cls b, eps];
              * p = [N K Kp Np P C ld nc ppc] */
     float *sx = malloc(sizeof(float) * (size_t)P[4]);

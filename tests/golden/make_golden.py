@@ -13,7 +13,8 @@ It also records the reference packer's output for a few weight matrices (s8_tens
 s8_packing.npz, and for the int8 prototype head (PROTO_S8): the reference lowering's own proto_s8n packs seeded
 prototype heads into one-op neon-int8 packages (sha256 in proto_packages.json; bnneon_b200.synth.write_proto_package
 must write the same bytes) and its packer (quant_rows_s8, n4_panel_flags, the [Np/4][Kp/16][4][16] layout) runs on
-fixed matrices (proto_packing.npz).
+fixed matrices (proto_packing.npz); and the reference lowering's l_fe_logmel writes one-op log-mel front-end packages
+(logmel_packages.json).
 """
 import hashlib
 import json
@@ -122,6 +123,50 @@ def proto_fixtures(ref_root):
     print("wrote proto_packages.json and proto_packing.npz")
 
 
+# the log-mel front-end packages: (name, nsamp, frame, hop, pad, nfft, nmel, floor, scale)
+LOGMEL_FES = (("logmel_small", 4000, 400, 160, 0, 512, 40, 1e-5, 1.0),
+              ("logmel_odd", 3001, 255, 100, 64, 256, 20, 1e-3, 0.5),
+              ("logmel_tiny", 2000, 16, 16, 0, 16, 3, 1e-5, 1.0))
+
+
+def reference_logmel_package(ref_root, fe, dst):
+    """The reference lowering's FE_LOGMEL record (lower.py l_fe_logmel) in a one-op neon-int8 package."""
+    sys.path.insert(0, os.path.join(ref_root, "python"))
+    from bnneon.compiler import lower, pkgfmt  # pylint: disable=import-outside-toplevel
+    pkg = pkgfmt.Package()
+    lw = lower.Lowering(pkg, [], synth.PATH, fe["nsamp"])
+    o = {"mode": "dft-op", "pad": fe["pad"], "frame": fe["frame"], "hop": fe["hop"], "nfft": fe["nfft"],
+         "mel": fe["mel"], "window": fe["window"], "floor": fe["floor"], "scale": fe["scale"], "out": "spec"}
+    lw.l_fe_logmel(0, o)
+    ob = lw.vbuf["spec"]
+    bufs, _ = lower.plan_slots(lw.bufs, lw.out, [ob])
+    pkg.add_path(synth.PATH, lower.path_info(synth.PATH).hwcap, bufs, lw.out, 0, ob, None)
+    pkg.set(f"src_nodes/{synth.PATH}", "\n".join(lw.src))
+    n_out = synth.logmel_frames(fe) * fe["mel"].shape[0]
+    for k, v in synth.metadata(n_out, 0, synth.labels_for(n_out), model_id="perch_v2_frontend_synthetic",
+                               family=synth.BNN_MODEL_PERCH_V2, sample_rate=synth.PERCH_SAMPLE_RATE,
+                               n_samples=fe["nsamp"], attribution="synthetic log-mel front end"):
+        pkg.set(k, v)
+    pkg.write(dst)
+
+
+def logmel_fixtures(ref_root):
+    out = {}
+    with tempfile.TemporaryDirectory() as td:
+        for name, nsamp, frame, hop, pad, nfft, nmel, floor, scale in LOGMEL_FES:
+            fe = synth.logmel_frontend(nsamp, frame, hop, pad, nfft, nmel, floor=floor, scale=scale)
+            ref = os.path.join(td, name + ".ref.bnpk")
+            reference_logmel_package(ref_root, fe, ref)
+            mine = os.path.join(td, name + ".mine.bnpk")
+            synth.write_logmel_package(mine, fe)
+            out[name] = dict(nsamp=nsamp, frame=frame, hop=hop, pad=pad, nfft=nfft, nmel=nmel, floor=floor,
+                             scale=scale, size=os.path.getsize(ref), sha256=sha(ref))
+            print(name, out[name], "writer matches" if sha(mine) == sha(ref) else "WRITER DIFFERS")
+    with open(os.path.join(HERE, "logmel_packages.json"), "w", encoding="utf-8") as f:
+        json.dump(out, f, indent=1, sort_keys=True)
+        f.write("\n")
+
+
 def sha(path):
     with open(path, "rb") as f:
         return hashlib.sha256(f.read()).hexdigest()
@@ -164,6 +209,7 @@ def main():
     np.savez(os.path.join(HERE, "s8_packing.npz"), **arrays)
     print("wrote packages.json and s8_packing.npz")
     proto_fixtures(ref_root)
+    logmel_fixtures(ref_root)
 
 
 if __name__ == "__main__":
