@@ -174,7 +174,7 @@ def test_logmel_edge_values(lib):
             keep = ~((st <= bad) & (bad < st + fe["nfft"]))
             assert keep.sum() > 0 and not keep.all()
         assert bits_equal(got[w][keep], want[w][keep]), (w, mismatch_report(got[w][keep], want[w][keep]))
-    assert (want[0] == np.float32(np.log2(1e-5) * 0.69314718) * 0 + want[0][0, 0]).all()  # silence: one value
+    assert (want[0] == want[0][0, 0]).all()  # silence: every band at the floor
     fe2 = dict(fe, floor=-1.0, window=(fe["window"] - 0.25).astype(np.float32))
     got = run_op(lib, fe2, x[3:5])
     want = oracle.logmel(x[3:5], fe2["frame"], fe2["hop"], fe2["pad"], fe2["nfft"], fe2["window"], fe2["mel"],
