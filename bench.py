@@ -331,6 +331,65 @@ def proto_head_c4(h, torch, stream, peak_bf16, cpu=True):
             "note": "time = the whole op (quantizer + GEMM + logits); ops = the GEMM's 2 M N K"}
 
 
+def logmel_perch(h, torch, stream, hbm_peak, cpu=True, batch=512):
+    """The Perch-like log-mel front end (FE_LOGMEL: 160000 samples at 32 kHz, 640-sample frames, hop 320, 1024-point
+    FFT, 128 mel bins -> 499 x 128) on `batch` windows through bnn_logmel_run, inputs resident, CUDA events over 20
+    runs after 3 warm-ups; CPU baseline: the oracle port on this host's cores."""
+    from bnneon_b200 import synth  # pylint: disable=import-outside-toplevel
+    p = synth.PERCH_FE
+    fe = synth.logmel_frontend(p["nsamp"], p["frame"], p["hop"], p["pad"], p["nfft"], p["nmel"], p["fmin"], p["fmax"],
+                               p["floor"], p["scale"])
+    mel = np.ascontiguousarray(fe["mel"])
+    op = h.bnn_logmel_new(p["nsamp"], p["frame"], p["hop"], p["pad"], p["nfft"], p["nmel"], fe["window"].ctypes.data,
+                          mel.ctypes.data, p["floor"], p["scale"])
+    if not op:
+        return None
+    try:
+        nfr = h.bnn_logmel_frames(op)
+        g = torch.Generator(device="cuda").manual_seed(7)
+        x = (0.1 * torch.randn((batch, p["nsamp"]), generator=g, device="cuda")).float()
+        out = torch.empty((batch, nfr * p["nmel"]), dtype=torch.float32, device="cuda")
+        sp = stream.cuda_stream
+
+        def run():
+            return h.bnn_logmel_run(op, batch, x.data_ptr(), p["nsamp"], out.data_ptr(), nfr * p["nmel"], sp)
+        for _ in range(3):
+            assert run() == 0
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(20):
+            run()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / 20
+        base = None
+        if cpu:
+            from oracle import oracle  # pylint: disable=import-outside-toplevel
+            threads = os.cpu_count() or 1
+            xs = x[:threads].cpu().numpy()
+            t0 = time.perf_counter()
+            import concurrent.futures  # pylint: disable=import-outside-toplevel
+            with concurrent.futures.ThreadPoolExecutor(threads) as ex:  # the oracle releases the GIL in C
+                list(ex.map(lambda w: oracle.logmel(xs[w:w + 1], p["frame"], p["hop"], p["pad"], p["nfft"],
+                                                    fe["window"], mel, p["floor"], p["scale"]), range(len(xs))))
+            dt = time.perf_counter() - t0
+            base = {"value": round(len(xs) / dt, 2), "unit": "windows/s", "cores": threads, "kind": "port",
+                    "sample": f"{len(xs)} windows, one per thread (oracle/oracle_ops.c bnno_logmel_run), {dt:.2f} s"}
+    finally:
+        h.bnn_logmel_free(op)
+    nbytes = batch * (p["nsamp"] + nfr * p["nmel"]) * 4
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"shape": f"{batch} windows x {p['nsamp']} samples -> {nfr} x {p['nmel']} (frame {p['frame']}, hop "
+                     f"{p['hop']}, nfft {p['nfft']})", "ms_per_run": round(ms, 4),
+            "windows_per_s": round(batch / (ms * 1e-3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(gbs / hbm_peak, 4),
+                         "note": "algorithmic bytes = samples in + spectrogram out; the shared-memory FFT passes, "
+                                 "not HBM, bound this kernel"},
+            "cpu_baseline": base}
+
+
 def load_peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json"), encoding="utf-8") as f:
@@ -489,6 +548,8 @@ def main():
     ap.add_argument("--no-proto", action="store_true", help="skip the prototype-head (C4 int8 head) line")
     ap.add_argument("--proto-ncu", type=int, metavar="B", default=0,
                     help="for profiler captures: the prototype head on B windows, 3 warm-ups + 1 run, no timing")
+    ap.add_argument("--logmel-ncu", type=int, metavar="B", default=0,
+                    help="for profiler captures: the Perch-like log-mel front end on B windows, 3 warm-ups + 1 run")
     ap.add_argument("--ncu", action="store_true",
                     help="for profiler captures: warm-up steps + one step through bnn_infer_device, no timing, no JSON")
     args = ap.parse_args()
@@ -502,7 +563,7 @@ def main():
     if args.impl == "reference":
         reference_arm(args, rank)
         return
-    if args.ncu or args.proto_ncu:
+    if args.ncu or args.proto_ncu or args.logmel_ncu:
         # profiler captures use eager launches: a run that replays the op list from CUDA graphs stopped with a driver
         # LaunchFailed under ncu (the same command exits 0 without ncu)
         os.environ["BNN_GRAPHS"] = "0"
@@ -514,6 +575,25 @@ def main():
 
     torch.cuda.set_device(local)
     os.environ["BNN_DEVICES"] = str(local)
+    if args.logmel_ncu:  # the log-mel front end alone, for a profiler; nothing is timed or printed as a result
+        from bnneon_b200 import load_library, synth  # pylint: disable=import-outside-toplevel
+        h = load_library()
+        assert h.bnn_cuda_device_init() == 0
+        p = synth.PERCH_FE
+        fe = synth.logmel_frontend(p["nsamp"], p["frame"], p["hop"], p["pad"], p["nfft"], p["nmel"], p["fmin"],
+                                   p["fmax"], p["floor"], p["scale"])
+        mel = np.ascontiguousarray(fe["mel"])
+        op = h.bnn_logmel_new(p["nsamp"], p["frame"], p["hop"], p["pad"], p["nfft"], p["nmel"],
+                              fe["window"].ctypes.data, mel.ctypes.data, p["floor"], p["scale"])
+        nfr, B = h.bnn_logmel_frames(op), args.logmel_ncu
+        x = torch.randn((B, p["nsamp"]), device="cuda") * 0.1
+        out = torch.empty((B, nfr * p["nmel"]), device="cuda")
+        for _ in range(4):
+            assert h.bnn_logmel_run(op, B, x.data_ptr(), p["nsamp"], out.data_ptr(), nfr * p["nmel"], None) == 0
+        torch.cuda.synchronize()
+        h.bnn_logmel_free(op)
+        print(f"logmel ncu mode: 4 runs of {B} windows", flush=True)
+        return
     if args.proto_ncu:  # the prototype head alone, for a profiler; nothing is timed or printed as a result
         from bnneon_b200 import load_library  # pylint: disable=import-outside-toplevel
         h = load_library()
@@ -645,6 +725,8 @@ def main():
     c1 = c1_gemm(m, torch, stream, bf16) if rank == 0 else None
     proto = (proto_head_c4(m.h, torch, stream, bf16, cpu=not args.no_cpu_baseline and world == 1)
              if rank == 0 and not args.no_proto else None)
+    logmel = (logmel_perch(m.h, torch, stream, load_peaks()[0], cpu=not args.no_cpu_baseline and world == 1)
+              if rank == 0 and not args.no_proto else None)
 
     line = None
     if rank == 0:
@@ -661,7 +743,8 @@ def main():
                             "ms_per_step": round(s8_ms, 4),
                             "note": "int8 ops of PW_S8 + GEMV_S8 (quantizer + tcgen05 GEMM) per second; these GEMMs "
                                     "are HBM-bound (AI far below the int8 ridge)"},
-                "ops": ops_summary, "clocks": clocks, "s8_gemm_c1": c1, "proto_s8_c4": proto}
+                "ops": ops_summary, "clocks": clocks, "s8_gemm_c1": c1, "proto_s8_c4": proto,
+                "fe_logmel_perch": logmel}
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(pkg, pcm)
     m.close()
