@@ -88,6 +88,8 @@ SIGNATURES = {
     "bnn_logmel_free": (None, [_P]),
     "bnn_proto_s8_new": (_P, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, ctypes.c_float, _I, _I]),
     "bnn_proto_s8_run": (_I, [_P, _I, _P, _LL, _I, _P, _LL, _P, _LL, _P, _P]),
+    "bnn_proto_s8h_new": (_P, [_I, _I, _I, _P, _P, _P, _P, _I, _I, ctypes.c_float, _I, _I]),
+    "bnn_proto_s8h_run": (_I, [_P, _I, _P, _LL, _I, _P, _LL, _P, _LL, _P, _P]),
     "bnn_proto_s8_read_scratch": (_I, [_P, _I, _P, _P]),
     "bnn_proto_s8_error": (_I, [_P]),
     "bnn_proto_s8_free": (None, [_P]),

@@ -541,6 +541,18 @@ def pack_proto_s8(protos):
     return qp, sw, n4_panel_flags(q), q
 
 
+def pack_proto_s8_sdot(protos):
+    """The neon-fp16 path's SDOT prototype tensors (lower.py proto_s8, PROTO variant 2): q [Np/12][K/4][12][4] int8
+    (Np = N rounded up to 12, zero rows), sw [Np]; also returns the unpacked q [Np][K]. K % 4 == 0."""
+    n, c = protos.shape
+    n_pad = (n + 11) // 12 * 12
+    wq = np.zeros((n_pad, c), np.float32)
+    wq[:n] = protos
+    q, sw = quant_rows_s8(wq)
+    qp = q.reshape(n_pad // 12, 12, c // 4, 4).transpose(0, 2, 1, 3).copy()
+    return qp, sw, q
+
+
 def write_proto_package(dst, head, ld=None, model_id="perch_v2_proto_head_synthetic"):
     """A one-op neon-int8 package: PROTO_S8 on the input window taken as cells [n_cells][ld] (the first C = K
     channels of each row used), logits [n_classes] out. Buffers, tensors, record and slots as the reference compiler

@@ -140,6 +140,10 @@ int bnnk_logmel(int B, const float *pcm, long long pws, const bnnk_logmel_tables
 int bnnk_proto_quant(int B, int P, const float *x, long long xws, int ld, int C, int Kq, float eps, int8_t *qa,
                      float *sx, bnn_stream_t st);
 
+/* the same on IEEE-half cells (PROTO variant 2, pc_quant_cells_f16): bytes saturated to [-128, 127] */
+int bnnk_proto_quant_h(int B, int P, const uint16_t *x, long long xws, int ld, int C, int Kq, float eps, int8_t *qa,
+                       float *sx, bnn_stream_t st);
+
 /* the column-maximum GEMM of one head: prototypes w [np][kp] int8 (row j = prototype j, zero from K), cells qa
  * [batch_cap * P][kp]. Cell tiles hold wt = floor(256 / P) whole windows when P <= 256 (bn = wt P rounded up to 16
  * MMA columns), else chunks of cs cells (nch per window) whose partial maxima go through scratch. */

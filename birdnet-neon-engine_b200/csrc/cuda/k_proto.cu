@@ -21,6 +21,7 @@
 // matrix stays in L2. Every mbarrier wait is bounded; a timeout sets the error word and the CTA winds down, still
 // freeing its TMEM.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -35,15 +36,21 @@ namespace bnn {
 
 // ------------------------------------------------------------------ per-cell quantizer
 
-// FCVTAS (nearest, ties away from zero, saturating, NaN -> 0) narrowed with saturation to int8 and raised to -127:
-// the bytes of src/proto_s8n.c:44-48. trunc(v) and v - trunc(v) are exact, so the tie test is exact.
+// FCVTAS (nearest, ties away from zero, saturating, NaN -> 0) narrowed with saturation to int8, raised to -127 (the
+// fp32 cells' bytes, src/proto_s8n.c:44-48) or not (LO = -128: the fp16 cells', src/pc_proto_s8.c:33-37). trunc(v)
+// and v - trunc(v) are exact, so the tie test is exact.
+template <int LO = -127>
 __device__ __forceinline__ int q_ties_away(float v) {
   float t = truncf(v);
   const float d = __fsub_rn(v, t);
   if (fabsf(d) >= 0.5f) t = __fadd_rn(t, copysignf(1.f, v));
   const int i = cvtzs(t);
-  return i > 127 ? 127 : i < -127 ? -127 : i;
+  return i > 127 ? 127 : i < LO ? LO : i;
 }
+
+// the cells' element type: fp32, or IEEE half (exact conversion to fp32)
+__device__ __forceinline__ float load_cell(const float *p) { return __ldg(p); }
+__device__ __forceinline__ float load_cell(const __half *p) { return __half2float(__ldg(p)); }
 
 constexpr int kQCells = 8;  // cells per quantizer block: their rows are re-read from L2 right after the reduction
 
@@ -52,10 +59,12 @@ constexpr int kQCells = 8;  // cells per quantizer block: their rows are re-read
 // channel c + l of each 8-channel step, fused x x + s in channel order; then vaddvq_f32(s0 + s1) = (v0 + v1) + (v2 + v3)
 // with v_l = s0_l + s1_l, by shuffles in that order. Quantization: each warp takes cells of the block, a lane 8
 // channels (two 16-byte loads, one 8-byte store) at a time.
-template <bool VEC>
-__global__ void __launch_bounds__(128) k_proto_quant(int cells, int P, const float *__restrict__ x, long long xws,
+// T: float or __half cells (the half form narrows without the -127 clamp)
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(128) k_proto_quant(int cells, int P, const T *__restrict__ x, long long xws,
                                                      int ld, int C, int Kq, float eps, int8_t *__restrict__ qa,
                                                      float *__restrict__ sx) {
+  constexpr bool kHalf = sizeof(T) == 2;
   __shared__ float s_inv[kQCells];
   const int c0 = blockIdx.x * kQCells;
   {
@@ -63,10 +72,10 @@ __global__ void __launch_bounds__(128) k_proto_quant(int cells, int P, const flo
     float s = 0.f, m = 0.f;
     if (cl < kQCells && cell < cells) {
       const int w = cell / P, p = cell - w * P;
-      const float *r = x + (long long)w * xws + (long long)p * ld + l;
+      const T *r = x + (long long)w * xws + (long long)p * ld + l;
 #pragma unroll 8
       for (int c = 0; c < C; c += 8) {
-        const float u = __ldg(r + c);
+        const float u = load_cell(r + c);
         s = __fmaf_rn(u, u, s);
         m = fmax_nan(m, fabsf(u));
       }
@@ -91,24 +100,33 @@ __global__ void __launch_bounds__(128) k_proto_quant(int cells, int P, const flo
     const int cell = c0 + cl;
     if (cell >= cells) break;
     const int w = cell / P, p = cell - w * P;
-    const float *r = x + (long long)w * xws + (long long)p * ld;
+    const T *r = x + (long long)w * xws + (long long)p * ld;
     const float inv = s_inv[cl];
     int8_t *qrow = qa + (long long)cell * Kq;
     for (int ch = lane; ch < nchunk; ch += 32) {
       uint32_t lo = 0, hi = 0;
       if (8 * ch < C) {  // C % 8 == 0: a chunk is all inside or all outside the row
         float u[8];
-        if (VEC) {
+        if constexpr (VEC && !kHalf) {
           const float4 a = __ldg(reinterpret_cast<const float4 *>(r + 8 * ch));
           const float4 b = __ldg(reinterpret_cast<const float4 *>(r + 8 * ch + 4));
           u[0] = a.x; u[1] = a.y; u[2] = a.z; u[3] = a.w; u[4] = b.x; u[5] = b.y; u[6] = b.z; u[7] = b.w;
+        } else if constexpr (VEC) {  // 8 halves in one 16-byte load
+          const uint4 a = __ldg(reinterpret_cast<const uint4 *>(r + 8 * ch));
+          const uint32_t wv[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wv[k]));
+            u[2 * k] = f.x;
+            u[2 * k + 1] = f.y;
+          }
         } else {
 #pragma unroll
-          for (int k = 0; k < 8; k++) u[k] = __ldg(r + 8 * ch + k);
+          for (int k = 0; k < 8; k++) u[k] = load_cell(r + 8 * ch + k);
         }
         int b[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) b[k] = q_ties_away(__fmul_rn(u[k], inv));
+        for (int k = 0; k < 8; k++) b[k] = q_ties_away<kHalf ? -128 : -127>(__fmul_rn(u[k], inv));
         lo = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
         hi = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
       }
@@ -377,8 +395,20 @@ extern "C" int bnnk_proto_quant(int batch, int P, const float *x, long long xws,
   if (cells <= 0) return 0;
   const bool vec = ((uintptr_t)x & 15) == 0 && xws % 4 == 0 && ld % 4 == 0;
   const int grid = (cells + kQCells - 1) / kQCells;
-  if (vec) k_proto_quant<true><<<grid, 128, 0, st>>>(cells, P, x, xws, ld, C, Kq, eps, qa, sx);
-  else k_proto_quant<false><<<grid, 128, 0, st>>>(cells, P, x, xws, ld, C, Kq, eps, qa, sx);
+  if (vec) k_proto_quant<float, true><<<grid, 128, 0, st>>>(cells, P, x, xws, ld, C, Kq, eps, qa, sx);
+  else k_proto_quant<float, false><<<grid, 128, 0, st>>>(cells, P, x, xws, ld, C, Kq, eps, qa, sx);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_proto_quant_h(int batch, int P, const uint16_t *x, long long xws, int ld, int C, int Kq, float eps,
+                                  int8_t *qa, float *sx, bnn_stream_t st) {
+  const int cells = batch * P;
+  if (cells <= 0) return 0;
+  const __half *xh = reinterpret_cast<const __half *>(x);
+  const bool vec = ((uintptr_t)x & 15) == 0 && xws % 8 == 0 && ld % 8 == 0;
+  const int grid = (cells + kQCells - 1) / kQCells;
+  if (vec) k_proto_quant<__half, true><<<grid, 128, 0, st>>>(cells, P, xh, xws, ld, C, Kq, eps, qa, sx);
+  else k_proto_quant<__half, false><<<grid, 128, 0, st>>>(cells, P, xh, xws, ld, C, Kq, eps, qa, sx);
   return cudaGetLastError();
 }
 

@@ -883,6 +883,7 @@ void bnn_logmel_free(bnn_logmel *o) {
 struct bnn_proto_s8 {
   bnn_devop op;
   int N, K, Kp, Np, nc, ppc, P, batch_cap;
+  int half;  /* PROTO variant 2: fp16 cells, SDOT panels, no -127 clamp (bnn_proto_s8h_*) */
   int8_t *qa;
   float *sx;
   int *err;
@@ -935,9 +936,68 @@ bnn_proto_s8 *bnn_proto_s8_new(int N, int K, int Kp, int Np, const int8_t *qw, c
   return o;
 }
 
+/* PROTO variant 2 (proto8_init, src/rt_ops_f16.c:252-271, after rt_proto_geom): K % 8 == 0, P % 8 == 0,
+ * Np % 12 == 0 and Np >= N, K <= 2^17 */
+bnn_proto_s8 *bnn_proto_s8h_new(int N, int K, int Np, const int8_t *qw, const float *sw, const float *cls_w,
+                                const float *cls_b, int nc, int ppc, float eps, int P, int batch_cap) {
+  if (!qw || !sw || !cls_w || !cls_b || P <= 0 || P > 65536 || P % 8 || nc <= 0 || ppc < 1 || N <= 0 ||
+      N > (1 << 26) || K <= 0 || K > (1 << 17) || K % 8 || (long long)nc * ppc != N || Np % 12 || Np < N ||
+      batch_cap <= 0) {
+    ERR(BNN_ERR_USAGE, "bnn_proto_s8h_new: N %d K %d Np %d P %d classes %d x %d batch %d (expected K %% 8 == 0, "
+        "K <= 2^17, Np %% 12 == 0, Np >= N = classes x prototypes per class, P %% 8 == 0)", N, K, Np, P, nc, ppc,
+        batch_cap);
+    return NULL;
+  }
+  bnn_proto_s8 *o = calloc(1, sizeof *o);
+  if (!o) { ERR(BNN_ERR_OOM, "out of memory"); return NULL; }
+  const int Kq = (K + 15) & ~15;
+  o->N = N; o->K = K; o->Kp = Kq; o->Np = Np; o->nc = nc; o->ppc = ppc; o->P = P; o->batch_cap = batch_cap;
+  o->half = 1;
+  char err[512];
+  int kind = BNN_ERR_CPU;
+  if (bnn_proto_weights_l(&o->op, 1, N, K, Kq, Np, qw, sw, cls_w, cls_b, nc, eps, err, sizeof err, &kind)) {
+    ERR(kind, "bnn_proto_s8h_new: %s", err);
+    bnn_proto_s8_free(o);
+    return NULL;
+  }
+  const size_t cells = (size_t)batch_cap * P;
+  cudaError_t e = cudaMalloc((void **)&o->qa, cells * Kq);
+  if (!e) e = cudaMemset(o->qa, 0, cells * Kq);
+  if (!e) e = cudaMalloc((void **)&o->sx, sizeof(float) * cells);
+  if (!e) e = cudaMalloc((void **)&o->err, sizeof(int));
+  if (!e) e = cudaMemset(o->err, 0, sizeof(int));
+  if (!e) e = (cudaError_t)bnnk_proto_plan_init(&o->op.pplan, o->op.w, Np, Kq, o->qa, batch_cap, P);
+  if (!e && !o->op.pplan.wt)
+    e = cudaMalloc((void **)&o->op.f[0], sizeof(float) * (size_t)batch_cap * o->op.pplan.nch * Np);
+  if (e) {
+    ERR(e == cudaErrorMemoryAllocation ? BNN_ERR_OOM : BNN_ERR_CPU, "bnn_proto_s8h_new: CUDA error %d (%s)", (int)e,
+        cudaGetErrorString(e));
+    bnn_proto_s8_free(o);
+    return NULL;
+  }
+  return o;
+}
+
+int bnn_proto_s8h_run(bnn_proto_s8 *o, int B, const uint16_t *d_x, long long xws, int ld, float *d_logits,
+                      long long lws, float *d_colmax, long long cws, int *d_status, void *stream) {
+  if (!o || !o->half || B < 0 || B > o->batch_cap || !d_x || !d_logits || !d_colmax || ld < o->K || lws < o->nc ||
+      cws < o->Np || (B > 1 && xws < (long long)o->P * ld)) {
+    ERR(BNN_ERR_USAGE, "bnn_proto_s8h_run: not a variant-2 head, or B %d (capacity %d) ld %d logits stride %lld "
+        "colmax stride %lld (expected ld >= K, strides >= classes / Np, window stride >= P ld)", B,
+        o ? o->batch_cap : 0, ld, lws, cws);
+    return -1;
+  }
+  bnn_stream_t st = (bnn_stream_t)stream;
+  int e = bnnk_proto_quant_h(B, o->P, d_x, xws, ld, o->K, o->Kp, o->op.eps, o->qa, o->sx, st);
+  if (!e) e = bnnk_proto_colmax(&o->op.pplan, B, o->sx, o->op.sw, d_colmax, cws, o->op.f[0], o->err, st);
+  if (!e) e = bnnk_proto_logits(B, o->nc, o->ppc, d_colmax, cws, o->op.f[1], o->op.f[2], d_logits, lws, d_status, NULL, 0,
+                                st);
+  return launch_rc("bnn_proto_s8h_run", e);
+}
+
 int bnn_proto_s8_run(bnn_proto_s8 *o, int B, const float *d_x, long long xws, int ld, float *d_logits, long long lws,
                      float *d_colmax, long long cws, int *d_status, void *stream) {
-  if (!o || B < 0 || B > o->batch_cap || !d_x || !d_logits || !d_colmax || ld < o->K || lws < o->nc ||
+  if (!o || o->half || B < 0 || B > o->batch_cap || !d_x || !d_logits || !d_colmax || ld < o->K || lws < o->nc ||
       cws < o->Np || (B > 1 && xws < (long long)o->P * ld)) {
     ERR(BNN_ERR_USAGE, "bnn_proto_s8_run: B %d (capacity %d) ld %d logits stride %lld colmax stride %lld (expected "
         "ld >= K, strides >= classes / Np, window stride >= P ld)", B, o ? o->batch_cap : 0, ld, lws, cws);

@@ -144,6 +144,8 @@ int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src
                    const int32_t *cs_src, const float *b_src, int rows_cap, char *err, size_t errlen, int *kind);
 int bnn_proto_weights(bnn_devop *d, int N, int Kp, int Np, const int8_t *src, const float *sw_src, const float *cw,
                       const float *cb, int nc, float eps, char *err, size_t errlen, int *kind);
+int bnn_proto_weights_l(bnn_devop *d, int layout, int N, int K, int Kq, int Np, const int8_t *src, const float *sw_src,
+                        const float *cw, const float *cb, int nc, float eps, char *err, size_t errlen, int *kind);
 int bnn_proto_n4_check(const int8_t *qw, int Kp, const uint8_t *n4, int npanels);
 /* pc_logmel_new's tables on the current device (t points into d->lm_mem); -1 with err set on failure */
 int bnn_logmel_build(bnn_devop *d, int nsamp, int frame, int hop, int pad, int nfft, int nmel, const float *window,

@@ -660,21 +660,30 @@ int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src
  * proto_s8n) as rows [Np][Kp]; sw [Np]; class weights [N], biases [nc]; eps */
 int bnn_proto_weights(bnn_devop *d, int N, int Kp, int Np, const int8_t *src, const float *sw_src, const float *cw,
                       const float *cb, int nc, float eps, char *err, size_t errlen, int *kind) {
-  int8_t *w = malloc((size_t)Np * Kp);
+  return bnn_proto_weights_l(d, 0, N, Kp, Kp, Np, src, sw_src, cw, cb, nc, eps, err, errlen, kind);
+}
+
+/* layout 0: the neon-int8 head's panels [Np/4][Kp/16][4][16] (K = Kp); layout 1: the SDOT head's [Np/12][K/4][12][4]
+ * (python/bnneon/compiler/lower.py proto_s8). Rows [Np][Kq], Kq >= K a multiple of 16, zero past K. */
+int bnn_proto_weights_l(bnn_devop *d, int layout, int N, int K, int Kq, int Np, const int8_t *src, const float *sw_src,
+                        const float *cw, const float *cb, int nc, float eps, char *err, size_t errlen, int *kind) {
+  const int Kp = Kq;
+  int8_t *w = calloc((size_t)Np * Kq, 1);
   if (!w) {
     *kind = BNN_ERR_OOM;
-    snprintf(err, errlen, "out of memory (prototypes, %d x %d)", Np, Kp);
+    snprintf(err, errlen, "out of memory (prototypes, %d x %d)", Np, Kq);
     return -1;
   }
   for (int j = 0; j < Np; j++)
-    for (int k = 0; k < Kp; k++)
-      w[(size_t)j * Kp + k] = src[(((size_t)(j / 4) * (Kp / 16) + k / 16) * 4 + j % 4) * 16 + k % 16];
-  int rc = upload((void **)&d->w, w, (size_t)Np * Kp, err, errlen, kind);
+    for (int k = 0; k < K; k++)
+      w[(size_t)j * Kq + k] = layout == 0 ? src[(((size_t)(j / 4) * (Kp / 16) + k / 16) * 4 + j % 4) * 16 + k % 16]
+                                          : src[(((size_t)(j / 12) * (K / 4) + k / 4) * 12 + j % 12) * 4 + k % 4];
+  int rc = upload((void **)&d->w, w, (size_t)Np * Kq, err, errlen, kind);
   free(w);
   if (!rc) rc = upload((void **)&d->sw, sw_src, sizeof(float) * Np, err, errlen, kind);
   if (!rc) rc = upload((void **)&d->f[1], cw, sizeof(float) * N, err, errlen, kind);
   if (!rc) rc = upload((void **)&d->f[2], cb, sizeof(float) * nc, err, errlen, kind);
-  d->kq = Kp;
+  d->kq = Kq;
   d->eps = eps;
   return rc;
 }

@@ -132,9 +132,18 @@ bnn_proto_s8 *bnn_proto_s8_new(int N, int K, int Kp, int Np, const int8_t *qw, c
  * finite check (where pc_proto_logits returns -2), else 0. */
 int bnn_proto_s8_run(bnn_proto_s8 *op, int B, const float *d_x, long long xws, int ld, float *d_logits, long long lws,
                      float *d_colmax, long long cws, int *d_status, void *stream);
+/* PROTO variant 2 (the neon-fp16 path's SDOT head, src/rt_ops_f16.c:252-283: pc_quant_cells_f16, src/pc_proto_s8.c:
+ * 13-45, pc_proto_colmax_s8, then pc_proto_logits), batched: prototypes qw [Np/12][K/4][12][4] int8 (Np % 12 == 0,
+ * Np >= N, K % 8 == 0), sw [Np], cls_w, cls_b, eps as above; P % 8 == 0 cells of IEEE-half channels per window. Run
+ * with bnn_proto_s8h_run (fp16 cells d_x [B][P][ld], as uint16 bits); the rest of the API (read_scratch, error, free)
+ * is shared. The quantized bytes saturate to [-128, 127] (the fp16 quantizer has no -127 clamp). */
+bnn_proto_s8 *bnn_proto_s8h_new(int N, int K, int Np, const int8_t *qw, const float *sw, const float *cls_w,
+                                const float *cls_b, int nc, int ppc, float eps, int P, int batch_cap);
+int bnn_proto_s8h_run(bnn_proto_s8 *op, int B, const uint16_t *d_x, long long xws, int ld, float *d_logits,
+                      long long lws, float *d_colmax, long long cws, int *d_status, void *stream);
 /* copies the op's own device scratch as the last run of B windows left it to host memory (synchronous; either pointer
- * may be NULL): the quantized cells qa [B * P][Kp] int8 and their scales sx [B * P] (the reference's qa buffer and
- * per-cell scale state) */
+ * may be NULL): the quantized cells qa [B * P][Kp] int8 (for a variant-2 head [B * P][K rounded up to 16], zero past
+ * K) and their scales sx [B * P] (the reference's qa buffer and per-cell scale state) */
 int bnn_proto_s8_read_scratch(bnn_proto_s8 *op, int B, int8_t *qa, float *sx);
 /* the device error word of the op's GEMM (0 = no bounded wait ran out) */
 int bnn_proto_s8_error(bnn_proto_s8 *op);

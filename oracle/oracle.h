@@ -77,6 +77,11 @@ void bnno_logmel_free(bnno_logmel *f);
 /* ---- the int8 prototype head PROTO_S8 (src/proto_s8n.c, src/rt_ops_s8n.c:212-250, src/pc_kern_f32.c:364-376) */
 /* pc_quant_cells_f32: x [P][ld] -> qa [P][Kp] (ties away, never -128, zero past C), sx [P]; C % 8 == 0 */
 void bnno_proto_quant_cells(const float *x, int P, int C, int ld, float eps, int8_t *qa, int Kp, float *sx);
+/* pc_quant_cells_f16 (PROTO variant 2, the SDOT head of the neon-fp16 path): fp16 cells x [P][ld] (IEEE half bits)
+ * -> rows qa [P][C] (saturated to [-128, 127], no -127 clamp), sx [P]; C % 8 == 0 */
+void bnno_proto_quant_cells_f16(const uint16_t *x, int P, int C, int ld, float eps, int8_t *qa, float *sx);
+/* the SDOT head's prototype panels [Np/12][K/4][12][4] -> rows [Np][K] */
+void bnno_proto_unpack12(const int8_t *qw, int Np, int K, int8_t *rows);
 /* the package's prototype bytes [Np/4][Kp/16][4][16] -> rows [Np][Kp] */
 void bnno_proto_unpack(const int8_t *qw, int Np, int Kp, int8_t *rows);
 /* pc_proto_colmax_s8n: colmax[j] = sw[j] * max_p (float)(qa[p] . w[j]) * sx[p]; packed or unpacked prototypes */

@@ -26,6 +26,8 @@ SIGS = {
     "bnno_logmel_frames": (_I, [_P]), "bnno_logmel_run": (None, [_P, _P, _P]), "bnno_logmel_free": (None, [_P]),
     "bnno_proto_quant_cells": (None, [_P, _I, _I, _I, _F, _P, _I, _P]),
     "bnno_proto_unpack": (None, [_P, _I, _I, _P]),
+    "bnno_proto_quant_cells_f16": (None, [_P, _I, _I, _I, _F, _P, _P]),
+    "bnno_proto_unpack12": (None, [_P, _I, _I, _P]),
     "bnno_proto_colmax": (None, [_P, _I, _P, _I, _P, _P, _I, _P]),
     "bnno_proto_colmax_rows": (None, [_P, _I, _P, _I, _P, _P, _I, _P]),
     "bnno_proto_logits": (_I, [_P, _P, _P, _I, _I, _P]),
@@ -116,6 +118,31 @@ def proto_s8(x, rows, sw, cls_w, cls_b, eps, C, Kp):
     for w in range(B):
         h.bnno_proto_quant_cells(ptr(x[w]), P, C, ld, float(eps), ptr(qa[w]), Kp, ptr(sx[w]))
         h.bnno_proto_colmax_rows(ptr(qa[w]), Kp, ptr(sx[w]), P, ptr(rows), ptr(sw), Np, ptr(cm[w]))
+        st[w] = h.bnno_proto_logits(ptr(cm[w]), ptr(cls_w), ptr(cls_b), nc, ppc, ptr(lg[w]))
+    return qa, sx, cm, lg, st
+
+
+def proto_s8h(x16, rows, sw, cls_w, cls_b, eps, C):
+    """PROTO variant 2 on fp16 windows x16 [B][P][ld] (numpy float16) with prototype rows [Np][K]: (qa [B][P][K],
+    sx [B][P], colmax [B][Np], logits [B][nc], status [B])."""
+    x16 = np.ascontiguousarray(x16, np.float16)
+    B, P, ld = x16.shape
+    rows = np.ascontiguousarray(rows, np.int8)
+    Np, K = rows.shape
+    sw = np.ascontiguousarray(sw, np.float32)
+    cls_w = np.ascontiguousarray(cls_w, np.float32).reshape(-1)
+    cls_b = np.ascontiguousarray(cls_b, np.float32)
+    nc = cls_b.shape[0]
+    ppc = cls_w.shape[0] // nc
+    qa = np.zeros((B, P, K), np.int8)
+    sx = np.zeros((B, P), np.float32)
+    cm = np.zeros((B, Np), np.float32)
+    lg = np.zeros((B, nc), np.float32)
+    st = np.zeros(B, np.int32)
+    h = lib()
+    for w in range(B):
+        h.bnno_proto_quant_cells_f16(ptr(x16[w]), P, C, ld, float(eps), ptr(qa[w]), ptr(sx[w]))
+        h.bnno_proto_colmax_rows(ptr(qa[w]), K, ptr(sx[w]), P, ptr(rows), ptr(sw), Np, ptr(cm[w]))
         st[w] = h.bnno_proto_logits(ptr(cm[w]), ptr(cls_w), ptr(cls_b), nc, ppc, ptr(lg[w]))
     return qa, sx, cm, lg, st
 

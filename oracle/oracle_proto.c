@@ -41,6 +41,58 @@ void bnno_proto_quant_cells(const float *x, int P, int C, int ld, float eps, int
   }
 }
 
+/* an IEEE half (fp16 bits) as a float: exact (vcvt_f32_f16); a NaN keeps its payload, quieted */
+static float half_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1fu, m = h & 0x3ffu;
+  uint32_t u;
+  if (e == 0x1f) u = sign | 0x7f800000u | (m << 13) | (m ? 0x400000u : 0u);
+  else if (e) u = sign | ((e + 112u) << 23) | (m << 13);
+  else if (!m) u = sign;
+  else { /* subnormal: normalise */
+    int sh = 0;
+    uint32_t mm = m;
+    while (!(mm & 0x400u)) { mm <<= 1; sh++; }
+    u = sign | ((uint32_t)(113 - sh) << 23) | ((mm & 0x3ffu) << 13);
+  }
+  return emu_float(u);
+}
+
+/* pc_quant_cells_f16 (src/pc_proto_s8.c:13-45): as the fp32 quantizer on the fp16 cells converted exactly to fp32,
+ * but the bytes are only narrowed with saturation (no clamp to -127: an infinite cell value gives -128); rows qa [P][K]
+ * (the reference packs them [P/8][K/4][8][4] for SDOT; the bytes are the same) */
+void bnno_proto_quant_cells_f16(const uint16_t *x, int P, int C, int ld, float eps, int8_t *qa, float *sx) {
+  for (int p = 0; p < P; p++) {
+    const uint16_t *r = x + (size_t)p * ld;
+    float s[8] = {0}, m[8] = {0};
+    for (int c = 0; c < C; c += 8)
+      for (int l = 0; l < 8; l++) {
+        const float u = half_to_float(r[c + l]);
+        s[l] = fmaf(u, u, s[l]);
+        m[l] = emu_fmax(m[l], fabsf(u));
+      }
+    const float v[4] = {s[0] + s[4], s[1] + s[5], s[2] + s[6], s[3] + s[7]};
+    const float den = sqrtf(emu_addv4(v)) + eps;
+    float mx = emu_fmax(emu_fmax(emu_fmax(m[0], m[4]), emu_fmax(m[1], m[5])),
+                        emu_fmax(emu_fmax(m[2], m[6]), emu_fmax(m[3], m[7])));
+    if (!(mx > 0)) mx = 1e-30f;
+    sx[p] = mx / (127.f * den);
+    const float inv = 127.f / mx;
+    for (int c = 0; c < C; c++) {
+      int32_t i = emu_cvtas(half_to_float(r[c]) * inv);
+      if (i > 127) i = 127;
+      if (i < -128) i = -128;
+      qa[(size_t)p * C + c] = (int8_t)i;
+    }
+  }
+}
+
+/* the SDOT head's prototype panels [Np/12][K/4][12][4] (python/bnneon/compiler/lower.py proto_s8) -> rows [Np][K] */
+void bnno_proto_unpack12(const int8_t *qw, int Np, int K, int8_t *rows) {
+  for (int j = 0; j < Np; j++)
+    for (int k = 0; k < K; k++)
+      rows[(size_t)j * K + k] = qw[(((size_t)(j / 12) * (size_t)(K / 4) + (size_t)(k / 4)) * 12 + (size_t)(j % 12)) * 4 + (size_t)(k % 4)];
+}
+
 /* the byte of prototype j, channel k in the package layout [Np/4][Kp/16][4][16] (python/bnneon/compiler/lower.py
  * proto_s8n: rows of 4-prototype panels, 16 channels per step) */
 static inline int8_t wbyte(const int8_t *qw, int Kp, int j, int k) {

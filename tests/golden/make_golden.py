@@ -81,7 +81,7 @@ def reference_proto_package(ref_root, head, ld, dst):
 
 def proto_fixtures(ref_root):
     sys.path.insert(0, os.path.join(ref_root, "python"))
-    from bnneon.compiler import lower  # pylint: disable=import-outside-toplevel
+    from bnneon.compiler import lower, pkgfmt  # pylint: disable=import-outside-toplevel
     out = {}
     with tempfile.TemporaryDirectory() as td:
         for name, seed, p_cells, c, nc, ppc, ld, eps in PROTO_HEADS:
@@ -119,6 +119,17 @@ def proto_fixtures(ref_root):
         arrays[f"sw{i}"] = sw
         arrays[f"n4_{i}"] = lower.n4_panel_flags(q)
         arrays[f"qp{i}"] = q.reshape(n_pad // 4, 4, k_pad // 16, 16).transpose(0, 2, 1, 3).copy()
+    # the SDOT head's packer (lower.py proto_s8, PROTO variant 2 of the neon-fp16 path) on two of the matrices
+    for i in (0, 4):
+        w = mats[i]
+        n, c = w.shape
+        lw = lower.Lowering(pkgfmt.Package(), [], "neon-fp16", 16)
+        head = {"P": w, "cw": np.ones((n, 1), np.float32), "cb": np.zeros(n, np.float32), "eps": 1e-6,
+                "out": "lg"}
+        lw.proto_s8(0, head, 0, 8, c, c, n, n, 1)
+        names = [t[0] for t in lw.pkg.tensors]
+        arrays[f"sdot_qp{i}"] = lw.pkg.tensors[names.index("s8/proto.0.q")][1]
+        arrays[f"sdot_sw{i}"] = lw.pkg.tensors[names.index("s8/proto.0.s")][1]
     np.savez(os.path.join(HERE, "proto_packing.npz"), **arrays)
     print("wrote proto_packages.json and proto_packing.npz")
 

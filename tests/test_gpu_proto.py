@@ -1,7 +1,8 @@
 """GPU parity of the int8 prototype head (PROTO_S8) against the CPU oracle, bit for bit, through the C ABI: the per-op
 entry point (include/bnneon_cuda.h bnn_proto_s8_*) on edge shapes and values, one-op packages written as the
-reference compiler writes them (tests/golden/proto_packages.json) through bnn_infer_batch, and the Perch v2 head
-shape (64 cells x 1536 channels -> 59180 prototypes) on sampled windows of a larger batch."""
+reference compiler writes them (tests/golden/proto_packages.json) through bnn_infer_batch, the Perch v2 head shape
+(64 cells x 1536 channels -> 59180 prototypes) on sampled windows of a larger batch, and PROTO variant 2 (fp16 cells,
+SDOT-packed prototypes, bnn_proto_s8h_*)."""
 import ctypes
 
 import numpy as np
@@ -201,6 +202,66 @@ def proto_args(head, g):
     qp, sw, _, rows = synth.pack_proto_s8(head["P"])
     del qp
     return rows, sw, head["cw"], head["cb"], np.float32(head["eps"]), g["channels"], rows.shape[1]
+
+
+class ProtoOpH(ProtoOp):
+    """bnn_proto_s8h_new on the SDOT-packed head (PROTO variant 2); run() takes fp16 cells."""
+
+    def __init__(self, h, head, P, C, cap):  # pylint: disable=super-init-not-called
+        self.h = h
+        self.qp, self.sw, self.rows = synth.pack_proto_s8_sdot(head["P"])
+        self.cw = np.ascontiguousarray(head["cw"], np.float32)
+        self.cb = np.ascontiguousarray(head["cb"], np.float32)
+        self.nc, self.ppc = self.cw.shape
+        self.Np, self.K = self.rows.shape
+        self.Kq = (self.K + 15) // 16 * 16
+        self.P, self.C, self.eps = P, C, np.float32(head["eps"])
+        self.op = h.bnn_proto_s8h_new(self.nc * self.ppc, C, self.Np, p(self.qp), p(self.sw), p(self.cw), p(self.cb),
+                                      self.nc, self.ppc, float(self.eps), P, cap)
+        assert self.op, h.bnn_last_error()
+
+    def run(self, x, colmax_stride=None):
+        B, P, ld = x.shape
+        d_x = dev(np.ascontiguousarray(x, np.float16).view(np.uint16))
+        d_lg = torch.full((B, self.nc), 7.0, dtype=torch.float32, device="cuda")
+        d_cm = torch.full((B, self.Np), 7.0, dtype=torch.float32, device="cuda")
+        d_st = torch.full((B,), 7, dtype=torch.int32, device="cuda")
+        rc = self.h.bnn_proto_s8h_run(self.op, B, d_x.data_ptr(), P * ld, ld, d_lg.data_ptr(), self.nc,
+                                      d_cm.data_ptr(), self.Np, d_st.data_ptr(), None)
+        assert rc == 0, self.h.bnn_last_error()
+        torch.cuda.synchronize()
+        qa = np.zeros((B, P, self.Kq), np.int8)
+        sx = np.zeros((B, P), np.float32)
+        assert self.h.bnn_proto_s8_read_scratch(self.op, B, p(qa), p(sx)) == 0
+        assert self.h.bnn_proto_s8_error(self.op) == 0
+        assert (qa[:, :, self.K:] == 0).all()
+        return qa[:, :, :self.K], sx, host(d_cm), host(d_lg), host(d_st)
+
+
+# (B, P, C, ld, classes, prototypes per class, what it covers) for PROTO variant 2
+CASES_H = [
+    (3, 8, 40, 40, 10, 3, "K 40 (rows padded to 48), Np 36 > N 30"),
+    (4, 16, 64, 72, 25, 4, "ld > C"),
+    (2, 264, 96, 96, 9, 2, "P > 256: chunked windows"),
+    (9, 64, 256, 256, 130, 4, "Np 528, 4 windows per cell tile"),
+]
+
+
+@pytest.mark.parametrize("case", CASES_H, ids=[c[-1].split(":")[0] for c in CASES_H])
+def test_proto_variant2(lib, case):
+    B, P, C, ld, nc, ppc, what = case
+    head = synth.proto_head(len(what) + 100, P, C, nc, ppc, 1e-6)
+    x = synth.cells(B, P, ld, seed=B * 7 + P).astype(np.float16)
+    x[0, 1, 3] = np.float16(-np.inf)  # a cell with -inf: its bytes saturate to -128 (no -127 clamp here)
+    x[0, 2, :] = 0                     # a zero cell
+    op = ProtoOpH(lib, head, P, C, B)
+    try:
+        got = op.run(x)
+    finally:
+        op.close()
+    want = oracle.proto_s8h(x, op.rows, op.sw, op.cw, op.cb, op.eps, C)
+    check(got, want, what)
+    assert got[0][0, 1].min() == -128 or got[0][0, 1].min() == 0  # -inf: -128 unless the cell's scale is infinite
 
 
 def test_perch_head_shape(lib):

@@ -38,6 +38,17 @@ def test_proto_packing_matches_reference_packer(i):
     assert np.array_equal(oracle.proto_unpack(PACKING[f"qp{i}"]), PACKING[f"q{i}"])
 
 
+@pytest.mark.parametrize("i", (0, 4))
+def test_sdot_packing_matches_reference_packer(i):
+    """PROTO variant 2's prototype tensors (lower.py proto_s8: [Np/12][K/4][12][4], Np = N rounded up to 12)."""
+    qp, sw, q = synth.pack_proto_s8_sdot(PACKING[f"w{i}"])
+    assert np.array_equal(qp, PACKING[f"sdot_qp{i}"])
+    assert np.array_equal(sw.view(np.int32), PACKING[f"sdot_sw{i}"].view(np.int32))
+    rows = np.empty(q.shape, np.int8)
+    oracle.lib().bnno_proto_unpack12(oracle.ptr(np.ascontiguousarray(qp)), q.shape[0], q.shape[1], oracle.ptr(rows))
+    assert np.array_equal(rows, q)
+
+
 def test_proto_rounding_reference_vectors():
     """Ties go away from zero and nothing maps to -128 (the reference's tests/test_lower_s8.py rules)."""
     q = PACKING["q2"]
