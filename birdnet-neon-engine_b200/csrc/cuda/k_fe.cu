@@ -280,41 +280,47 @@ __global__ void __launch_bounds__(512) k_fe_minmax(const float *__restrict__ pcm
 
 constexpr int kLmFrames = 2, kLmThreads = 128;
 
+// the points' shared-memory index, one pad word per 32: the butterfly passes' short strides and the 4-point groups
+// of the first pass fall in distinct banks
+__device__ __forceinline__ int lp(int i) { return i + (i >> 5); }
+
 __global__ void __launch_bounds__(kLmFrames * kLmThreads) k_logmel(const float *__restrict__ pcm, long long pws,
                                                                  const bnnk_logmel_tables t, float *__restrict__ spec,
                                                                  long long sws) {
   extern __shared__ float lsm[];
-  const int M = t.M, lg = t.lg;
+  const int M = t.M, lg = t.lg, MP = M + M / 32;
   const int fl = threadIdx.x / kLmThreads, lt = threadIdx.x % kLmThreads;
   const int f = blockIdx.x * kLmFrames + fl, win = blockIdx.y;
-  float *re = lsm + fl * (3 * M + 2), *im = re + M, *mag = im + M;
+  float *re = lsm + fl * (2 * MP + M + 2), *im = re + MP, *mag = im + MP;
   const float *x = pcm + win * pws;
   const bool live = f < t.nfr;
   {
-    // z[n] = w[2n] y[st + 2n] + i w[2n + 1] y[st + 2n + 1] (y: pad zeros, the window's samples, zeros); 0 past the
-    // frame's (frame + 1) / 2 points
+    // levels 1-2 (fft_tab.h:28-38) on the 4 consecutive bit-reversed positions 4g .. 4g + 3, gathered straight from
+    // the samples: z[n] = w[2n] y[st + 2n] + i w[2n + 1] y[st + 2n + 1] (y: pad zeros, the window's samples, zeros),
+    // 0 past the frame's (frame + 1) / 2 points
     const int st = f * t.hop - t.pad;
-    for (int n = lt; n < M; n += kLmThreads) {
-      float vr = 0.f, vi = 0.f;
-      if (live && n < t.nz) {
-        const int i0 = st + 2 * n, i1 = i0 + 1;
-        const float y0 = (i0 >= 0 && i0 < t.nsamp) ? __ldg(x + i0) : 0.f;
-        const float y1 = (i1 >= 0 && i1 < t.nsamp) ? __ldg(x + i1) : 0.f;
-        vr = __fmul_rn(y0, __ldg(t.win + 2 * n));
-        vi = __fmul_rn(y1, __ldg(t.win + 2 * n + 1));
+    for (int g = lt; g < M / 4; g += kLmThreads) {
+      cpx z[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int n = (int)(__brev((unsigned)(4 * g + e)) >> (32 - lg));
+        float vr = 0.f, vi = 0.f;
+        if (live && n < t.nz) {
+          const int i0 = st + 2 * n, i1 = i0 + 1;
+          const float y0 = (i0 >= 0 && i0 < t.nsamp) ? __ldg(x + i0) : 0.f;
+          const float y1 = (i1 >= 0 && i1 < t.nsamp) ? __ldg(x + i1) : 0.f;
+          vr = __fmul_rn(y0, __ldg(t.win + 2 * n));
+          vi = __fmul_rn(y1, __ldg(t.win + 2 * n + 1));
+        }
+        z[e] = {vr, vi};
       }
-      const int r = (int)(__brev((unsigned)n) >> (32 - lg));
-      re[r] = vr;
-      im[r] = vi;
+      r4first(z[0], z[1], z[2], z[3]);
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        re[lp(4 * g + e)] = z[e].r;
+        im[lp(4 * g + e)] = z[e].i;
+      }
     }
-  }
-  __syncthreads();
-  for (int g = lt; g < M / 4; g += kLmThreads) {  // levels 1-2 (fft_tab.h:28-38)
-    const int i = 4 * g;
-    cpx a = {re[i], im[i]}, b = {re[i + 1], im[i + 1]}, c = {re[i + 2], im[i + 2]}, d = {re[i + 3], im[i + 3]};
-    r4first(a, b, c, d);
-    re[i] = a.r; im[i] = a.i; re[i + 1] = b.r; im[i + 1] = b.i;
-    re[i + 2] = c.r; im[i + 2] = c.i; re[i + 3] = d.r; im[i + 3] = d.i;
   }
   __syncthreads();
   int len = 8;
@@ -322,12 +328,12 @@ __global__ void __launch_bounds__(kLmFrames * kLmThreads) k_logmel(const float *
     const int h = len / 2, st1 = M / len, st2 = M / (2 * len);
     for (int q = lt; q < M / 4; q += kLmThreads) {
       const int j = q % h, i = (q / h) * 2 * len + j;
-      cpx a = {re[i], im[i]}, b = {re[i + h], im[i + h]}, c = {re[i + 2 * h], im[i + 2 * h]},
-          d = {re[i + 3 * h], im[i + 3 * h]};
+      const int ia = lp(i), ib = lp(i + h), ic = lp(i + 2 * h), id = lp(i + 3 * h);
+      cpx a = {re[ia], im[ia]}, b = {re[ib], im[ib]}, c = {re[ic], im[ic]}, d = {re[id], im[id]};
       r22(a, b, c, d, __ldg(t.tw_re + j * st1), __ldg(t.tw_im + j * st1), __ldg(t.tw_re + j * st2),
           __ldg(t.tw_im + j * st2));
-      re[i] = a.r; im[i] = a.i; re[i + h] = b.r; im[i + h] = b.i;
-      re[i + 2 * h] = c.r; im[i + 2 * h] = c.i; re[i + 3 * h] = d.r; im[i + 3 * h] = d.i;
+      re[ia] = a.r; im[ia] = a.i; re[ib] = b.r; im[ib] = b.i;
+      re[ic] = c.r; im[ic] = c.i; re[id] = d.r; im[id] = d.i;
     }
     __syncthreads();
   }
@@ -335,17 +341,18 @@ __global__ void __launch_bounds__(kLmFrames * kLmThreads) k_logmel(const float *
     const int half = len / 2, step = M / len;
     for (int q = lt; q < M / 2; q += kLmThreads) {
       const int j = q % half, i = (q / half) * len + j;
-      const cpx v = cmul({re[i + half], im[i + half]}, __ldg(t.tw_re + j * step), __ldg(t.tw_im + j * step));
-      const float ur = re[i], ui = im[i];
-      re[i] = __fadd_rn(ur, v.r); im[i] = __fadd_rn(ui, v.i);
-      re[i + half] = __fsub_rn(ur, v.r); im[i + half] = __fsub_rn(ui, v.i);
+      const int iu = lp(i), iv = lp(i + half);
+      const cpx v = cmul({re[iv], im[iv]}, __ldg(t.tw_re + j * step), __ldg(t.tw_im + j * step));
+      const float ur = re[iu], ui = im[iu];
+      re[iu] = __fadd_rn(ur, v.r); im[iu] = __fadd_rn(ui, v.i);
+      re[iv] = __fsub_rn(ur, v.r); im[iv] = __fsub_rn(ui, v.i);
     }
     __syncthreads();
   }
   // |X_k|: A = Z_k, B = conj Z_{M-k}; E = (A + B) / 2, O = (A - B) / (2i); X = E + W^k O
   for (int k = t.klo + lt; k < t.khi; k += kLmThreads) {
     const int k2 = (k == 0 || k == M) ? 0 : M - k, ka = k == M ? 0 : k;
-    const float Ar = re[ka], Ai = im[ka], Br = re[k2], Bi = -im[k2];
+    const float Ar = re[lp(ka)], Ai = im[lp(ka)], Br = re[lp(k2)], Bi = -im[lp(k2)];
     const float Er = __fmul_rn(__fadd_rn(Ar, Br), 0.5f), Ei = __fmul_rn(__fadd_rn(Ai, Bi), 0.5f);
     const float Or = __fmul_rn(__fsub_rn(Ai, Bi), 0.5f), Oi = __fmul_rn(__fsub_rn(Br, Ar), 0.5f);
     const float c = __ldg(t.pc + k), sn = __ldg(t.ps + k);
@@ -400,7 +407,7 @@ extern "C" int bnnk_logmel(int B, const float *pcm, long long pws, const bnnk_lo
                            long long sws, bnn_stream_t st) {
   if (B <= 0 || t->nfr <= 0) return 0;
   if (B > 65535) return cudaErrorInvalidValue;
-  const size_t smem = sizeof(float) * (size_t)kLmFrames * (3 * t->M + 2);
+  const size_t smem = sizeof(float) * (size_t)kLmFrames * (2 * (t->M + t->M / 32) + t->M + 2);
   const dim3 grid((t->nfr + kLmFrames - 1) / kLmFrames, B);
   k_logmel<<<grid, kLmFrames * kLmThreads, smem, st>>>(pcm, pws, *t, spec, sws);
   return cudaGetLastError();

@@ -38,6 +38,12 @@ def full_pkg(pkg_dir):
     return path
 
 
+def gpu_visible():
+    """A GPU device node exists (any index: a GPU box may expose only, say, /dev/nvidia3)."""
+    import glob  # pylint: disable=import-outside-toplevel
+    return bool(glob.glob("/dev/nvidia[0-9]*"))
+
+
 def bits_equal(a, b):
     """Bit-exact equality of float arrays; any NaN equals any NaN (payloads are not modelled)."""
     a = np.ascontiguousarray(a, np.float32)

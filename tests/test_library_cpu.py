@@ -7,7 +7,7 @@ import struct
 
 import pytest
 
-from conftest import REPO
+from conftest import REPO, gpu_visible
 from bnneon_b200 import BnnError, Model, load_library, pkgread, probe, probe_meta, synth, verify_labels
 
 
@@ -79,7 +79,7 @@ def init_error(path, mode=0):
 
 def test_valid_package_stops_at_device_check(mini_pkg):
     """On a machine without a GPU a valid package passes every check and then reports the missing device."""
-    if os.path.exists("/dev/nvidia0"):
+    if gpu_visible():
         pytest.skip("a GPU is present")
     e = init_error(mini_pkg)
     assert e.kind == "CPU" and "no CUDA device" in str(e)

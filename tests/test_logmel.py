@@ -10,7 +10,7 @@ import struct
 import numpy as np
 import pytest
 
-from conftest import bits_equal, mismatch_report
+from conftest import bits_equal, mismatch_report, gpu_visible
 from bnneon_b200 import BnnError, Model, load_library, pkgread, synth
 from oracle import oracle
 
@@ -79,7 +79,7 @@ def test_logmel_validation_errors(tmp_path):
     g = PACKAGES["logmel_small"]
     path = str(tmp_path / "lm.bnpk")
     synth.write_logmel_package(path, frontend(g))
-    if not os.path.exists("/dev/nvidia0"):
+    if not gpu_visible():
         e = init_error(path)
         assert e.kind == "CPU" and "no CUDA device" in str(e)
     off = pkgread.op_offsets(path)[0]

@@ -9,6 +9,8 @@ import struct
 import numpy as np
 import pytest
 
+from conftest import gpu_visible
+
 from bnneon_b200 import BnnError, Model, pkgread, synth
 from oracle import oracle
 
@@ -131,7 +133,7 @@ def init_error(path):
 
 
 def test_proto_package_loads_until_device_check(tmp_path):
-    if os.path.exists("/dev/nvidia0"):
+    if gpu_visible():
         pytest.skip("a GPU is present")
     path, _, _ = proto_pkg(tmp_path, "proto_small")
     e = init_error(path)
