@@ -358,6 +358,124 @@ class _Int8Lowering:
         return i + 1
 
 
+OPC_F16 = dict(C0POOL=0x102, PW=0x103, DW3=0x104, SE=0x105, POSTPC=0x106, DENSE=0x107)
+OPC_DENSE_F32 = 7
+PATH_F16 = "neon-fp16"
+
+
+def pack_h16(w, b, kp):
+    """hp_pack (src/gemm_f16.c:17-40, lower.py pack_h16): fp16 panels [Np/16][Kp][16] and, when Np % 16, a [Kp][8] tail
+    panel; the bias as fp32 and as fp16, [Np + 16] each."""
+    n, k = w.shape
+    np_ = _r8(n)
+    n16 = np_ // 16
+    panels = np.zeros((((np_ * kp * 2) + 127) & ~63) // 2, np.float16)
+    w16 = np.zeros((np_, k), np.float16)
+    w16[:n] = w
+    panels[:n16 * kp * 16].reshape(n16, kp, 16)[:, :k, :] = w16[:n16 * 16].reshape(n16, 16, k).transpose(0, 2, 1)
+    if np_ > n16 * 16:
+        at = n16 * kp * 16
+        panels[at:at + kp * 8].reshape(kp, 8)[:k, :] = w16[n16 * 16:].T
+    b32 = np.zeros(np_ + 16, np.float32)
+    b32[:n] = b
+    return panels, b32, b32.astype(np.float16), (n, k, kp, np_)
+
+
+class _F16Lowering(_Int8Lowering):
+    """The neon-fp16 lowering of the v2.4 IR: fp16 activations, fp16 GEMM panels (hp_pack), fp16 depthwise weights,
+    the SE applied in place, the fp16 post conv and an fp16 head (fp32 for heads of 64 classes or fewer).
+
+    Follows python/bnneon/compiler/lower.py for the "neon-fp16" path (PathInfo act fp16, variant 1, prefix "f16/";
+    l_conv, pw, out_for_dw, l_dwconv, l_se, l_affine, l_dense), so the package it writes is the reference compiler's.
+    """
+
+    def gemm_tensors(self, tag, w, b, kp):
+        panels, b32, b16, shp = pack_h16(w, b, kp)
+        return [self.tensor(f"f16/{tag}.w", panels), self.tensor(f"f16/{tag}.b32", b32),
+                self.tensor(f"f16/{tag}.b16", b16)], shp
+
+    def l_conv(self, i, o, k):
+        w, b = o["w"], o["b"]
+        co = w.shape[0]
+        ib = self.vbuf[o["ins"][0]]
+        if o["k"] == [4, 8]:  # c0 + ReLU + max|avg pool
+            tl, shp = self.gemm_tensors(f"c0.{k}", w.transpose(0, 2, 3, 1).reshape(co, -1), b, 64)
+            ob = self.buf(F16, 48, 128, 48)
+            self.emit(OPC_F16["C0POOL"], [ib, ob], tl, list(shp), o)
+            self.vbuf[o["out"]] = ob
+            return i + 1
+        _, h_in, w_in, _, ld, _, _ = self.bufs[ib]
+        tl, shp = self.gemm_tensors(f"pw.{k}", w[:, :, 0, 0], b, _r8(w.shape[1]))
+        cons = self.uses.get(o["out"], [])
+        if len(cons) == 1 and cons[0]["op"] == "DWCONV" and co % 8 == 0:
+            ob, ow, opad, ldo = self.buf(F16, h_in, w_in, co, ld=co, halo=1), w_in, 1, co
+        else:
+            ldo = _r8(co)
+            ob, ow, opad = self.buf(F16, h_in, w_in, co, ld=ldo), 0, 0
+        rb, ldr = -1, 0
+        if o.get("res"):
+            rb = self.vbuf[o["res"]]
+            ldr = self.bufs[rb][4]
+        act = {None: 0, "swish": 1, "relu": 2}[o.get("act")]
+        self.emit(OPC_F16["PW"], [ib, ob, rb], tl, list(shp) + [h_in * w_in, ld, act, ldo, ow, opad, ldr], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+    def l_dwconv(self, i, o, k):
+        ib = self.vbuf[o["ins"][0]]
+        _, h, w, c, _, _, _ = self.bufs[ib]
+        ho, wo = self.vshape[o["out"]]
+        self.bufs.append((F32, 1, 1, c, c, 0, c))
+        cs = len(self.bufs) - 1
+        ob = self.buf(F16, ho, wo, c)
+        w9 = o["w"][:, 0].transpose(1, 2, 0).reshape(9, c)
+        tl = [self.tensor(f"f16/dw.{k}.w", w9.astype(np.float16)),
+              self.tensor(f"f16/dw.{k}.b", o["b"].astype(np.float16))]
+        pt, pl = o["pads"][0], o["pads"][1]
+        self.emit(OPC_F16["DW3"], [ib, ob, cs], tl, [h, w, c, o["s"][0], ho, wo, pt, pl], o)
+        self.vbuf[o["out"]] = ob
+        self.chsum = (ob, cs)
+        return i + 1
+
+    def l_se(self, i, o, k):
+        ib = self.vbuf[o["ins"][0]]
+        cs = self.chsum[1]
+        _, h, w, c, _, _, _ = self.bufs[ib]
+        rd = o["w1"].shape[0]
+        tl = [self.tensor(f"f16/se.{k}.w1", o["w1"]), self.tensor(f"f16/se.{k}.b1", o["b1"]),
+              self.tensor(f"f16/se.{k}.w2t", np.ascontiguousarray(o["w2"].T)),
+              self.tensor(f"f16/se.{k}.b2", o["b2"])]
+        self.emit(OPC_F16["SE"], [ib, cs], tl, [c, rd, h * w], o)
+        self.vbuf[o["out"]] = ib
+        return i + 1
+
+    def l_affine(self, i, o, k):
+        nx, mn = self.ops[i + 1], self.ops[i + 2]
+        ib = self.vbuf[o["ins"][0]]
+        w = nx["w"].transpose(0, 2, 3, 1).reshape(1024, 1728)
+        tl, shp = self.gemm_tensors(f"pc.{k}", w, nx["b"], 1728)
+        tl = [self.tensor(f"f16/post.{k}.s", o["s"]), self.tensor(f"f16/post.{k}.t", o["t"])] + tl
+        fb = self.buf(F32, 1, 1, 1024)
+        pin = self.buf(F16, 8, 1, 1728)
+        pout = self.buf(F16, 8, 1, 1024)
+        self.emit(OPC_F16["POSTPC"], [ib, fb, pin, pout], tl, list(shp), o)
+        self.vbuf[mn["out"]] = fb
+        return i + 3
+
+    def l_dense(self, i, o, k):
+        ib = self.vbuf[o["ins"][0]]
+        n = o["w"].shape[0]
+        ob = self.buf(F32, 1, 1, n)
+        if n > 64:  # the compiler's default policy: an fp16 head above 64 classes
+            tl = [self.tensor(f"f16/dense.{k}.w", o["w"].astype(np.float16)), self.tensor(f"f16/dense.{k}.b", o["b"])]
+            self.emit(OPC_F16["DENSE"], [ib, ob], tl, [n], o)
+        else:  # small heads: the exact fp32 GEMV (variant 0) on both paths
+            tl = [self.tensor(f"f32/dense.{k}.w", o["w"].astype(np.float32)), self.tensor(f"f32/dense.{k}.b", o["b"])]
+            self.emit(OPC_DENSE_F32, [ib, ob], tl, [n], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+
 def plan_slots(bufs, records, pinned):
     """Memory slots: buffers with disjoint op lifetimes and one dtype share a slot (best fit); buffer 0 and the pinned
     outputs get their own (lower.py plan_slots rules)."""
@@ -479,10 +597,27 @@ def write_int8_package(dst, ir):
     return n_classes, emb_dim
 
 
-def make_package(dst, seed=0, mini=False, n_classes=None):
-    """A synthetic v2.4-architecture neon-int8 package at dst; returns (n_classes, emb_dim)."""
+def write_f16_package(dst, ir):
+    """Lowers v24_ir()'s result for the neon-fp16 path (bnc.py compile --paths neon-fp16) and writes the package;
+    returns (n_classes, emb_dim)."""
+    ops, vshape, logits, feat = ir
+    lw = _F16Lowering(ops)
+    lw.vshape = vshape
+    lw.run()
+    ob, eb = lw.vbuf[logits], lw.vbuf[feat]
+    n_classes, emb_dim = lw.bufs[ob][3], lw.bufs[eb][3]
+    bufs = plan_slots(lw.bufs, lw.records, [ob, eb])
+    meta = [(f"src_nodes/{PATH_F16}", "\n".join(lw.src))] + metadata(n_classes, emb_dim, labels_for(n_classes))
+    write_package(dst, meta, lw.tensors, [(PATH_F16, 1, bufs, lw.records, 0, ob, eb)])
+    return n_classes, emb_dim
+
+
+def make_package(dst, seed=0, mini=False, n_classes=None, path=PATH):
+    """A synthetic v2.4-architecture package (path "neon-int8" or "neon-fp16") at dst; returns (n_classes,
+    emb_dim)."""
     nc = n_classes if n_classes is not None else (61 if mini else 6522)
-    return write_int8_package(dst, v24_ir(seed, nc, MINI_BLOCKS if mini else V24_BLOCKS))
+    ir = v24_ir(seed, nc, MINI_BLOCKS if mini else V24_BLOCKS)
+    return (write_f16_package if path == PATH_F16 else write_int8_package)(dst, ir)
 
 
 # ------------------------------------------------------------------ the int8 prototype head (PROTO_S8)

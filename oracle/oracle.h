@@ -102,6 +102,39 @@ int bnno_proto_s8_many(int n, int threads, const float *x, long long xws, int P,
                        const int8_t *rows, const float *sw, int Np, int Kp, const float *cls_w, const float *cls_b,
                        int nc, int ppc, float *logits);
 
+/* ---- the neon-fp16 path's ops (variant 1; oracle_f16.c). fp16 values are IEEE half bits (uint16_t). */
+double bnno_h2d(uint16_t h);
+float bnno_h2f(uint16_t h);
+uint16_t bnno_d2h(double x);          /* one rounding, nearest even */
+uint16_t bnno_f2h(float x);
+uint16_t bnno_h_add(uint16_t a, uint16_t b);
+uint16_t bnno_h_mul(uint16_t a, uint16_t b);
+uint16_t bnno_h_fma(uint16_t a, uint16_t b, uint16_t c); /* a * b + c, one rounding */
+uint16_t bnno_h_silu(uint16_t x);     /* src/silu_lut.h */
+extern const uint16_t BNNO_SILU_C0[16], BNNO_SILU_C1[16], BNNO_SILU_C2[16];
+float bnno_sigm_f16path(float a);     /* sigm4, src/v24_fast.c:173-185 */
+/* the SE's two FCs before the sigmoid: g [C] */
+void bnno_se_fc(int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2, const float *chsum,
+                int P, float *g);
+/* PW f16 / any hp_pack GEMM (src/gemm_f16.c): A [M][lda] -> out (padded rows when opad); act 0 none, 1 SiLU, 2 ReLU;
+ * w: panels [Np/16][Kp][16] + tail [Kp][8]; b32 / b16 [>= Np] */
+void bnno_gemm_f16(const uint16_t *A, int lda, int M, const uint16_t *w, const float *b32, const uint16_t *b16, int Kp,
+                   int Np, int act, uint16_t *out, int ldo, int ow, int opad, const uint16_t *res, int ldr);
+/* C0POOL f16: img [96][511][2] fp32 -> pin [48*128][48] fp16 (w: panels Kp 64 Np 24, b16) */
+void bnno_c0pool_f16(const float *img, const uint16_t *w, const uint16_t *b16, uint16_t *pin);
+/* DW3 f16: xp haloed [H+2][W+2][C] -> out [Ho][Wo][C], chsum [C] */
+void bnno_dw3_f16(const uint16_t *xp, int H, int W, int C, int s, int pt, int pl, const uint16_t *w, const uint16_t *b,
+                  uint16_t *out, int Ho, int Wo, float *chsum);
+/* SE f16: D [P][C] scaled in place */
+void bnno_se_f16(int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,
+                 const float *chsum, int P, uint16_t *D);
+/* POSTPC f16: X [24][192] -> feat [1024]; 0, or -2 when a feature is not finite (src/v24_fast.c:305-310) */
+int bnno_postpc_f16(const uint16_t *X, const float *post_s, const float *post_b, const uint16_t *w, const float *b32,
+                    const uint16_t *b16, float *feat);
+/* DENSE f16 (W fp16 [N][1024]) and DENSE f32 (W fp32 [N][1024]): feat [1024] -> out [N] */
+void bnno_dense_f16(const uint16_t *W, const float *bias, int N, const float *feat, float *out);
+void bnno_dense_f32(const float *W, const float *bias, int N, const float *feat, float *out);
+
 /* ---- a .bnpk package run on the CPU, window by window (the executor of src/rt_pkg.c:528-542) */
 typedef struct bnno_pkg bnno_pkg;
 /* path: the package; path_name: the package path to run ("neon-int8"). NULL on failure (err filled). */

@@ -1,4 +1,5 @@
-"""ctypes wrapper of liboracle.so, the CPU restatement of the reference's v2.4 neon-int8 path (TEST INFRASTRUCTURE).
+"""ctypes wrapper of liboracle.so, the CPU restatement of the reference's v2.4 neon-int8 and neon-fp16 paths (TEST
+INFRASTRUCTURE).
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs use this module; the product library never
 does. `make -C oracle` builds liboracle.so.
@@ -11,6 +12,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 _P, _I, _F, _L, _SZ, _S = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_long, ctypes.c_size_t, ctypes.c_char_p
+_H = ctypes.c_uint16
 SIGS = {
     "bnno_silu": (_F, [_F]), "bnno_sigmoid": (_F, [_F]), "bnno_frecpe": (_F, [_F]), "bnno_log2_acc": (_F, [_F]),
     "bnno_exp2_acc": (_F, [_F]), "bnno_expf": (_F, [_F]),
@@ -39,6 +41,15 @@ SIGS = {
     "bnno_pkg_run_range": (_I, [_P, _P, _I, _I]), "bnno_pkg_run": (_I, [_P, _P, _P, _P]),
     "bnno_pkg_get_buf": (_I, [_P, _I, _P, _SZ]), "bnno_pkg_set_buf": (_I, [_P, _I, _P, _SZ]),
     "bnno_pkg_run_many": (_I, [_S, _S, _I, _P, _P, _P, _I]),
+    "bnno_h_fma": (_H, [_H, _H, _H]), "bnno_h_add": (_H, [_H, _H]), "bnno_h_mul": (_H, [_H, _H]),
+    "bnno_h_silu": (_H, [_H]), "bnno_d2h": (_H, [ctypes.c_double]), "bnno_h2d": (ctypes.c_double, [_H]),
+    "bnno_sigm_f16path": (_F, [_F]),
+    "bnno_gemm_f16": (None, [_P, _I, _I, _P, _P, _P, _I, _I, _I, _P, _I, _I, _I, _P, _I]),
+    "bnno_c0pool_f16": (None, [_P, _P, _P, _P]),
+    "bnno_dw3_f16": (None, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
+    "bnno_se_f16": (None, [_I, _I, _P, _P, _P, _P, _P, _I, _P]),
+    "bnno_postpc_f16": (_I, [_P, _P, _P, _P, _P, _P, _P]),
+    "bnno_dense_f16": (None, [_P, _P, _I, _P, _P]), "bnno_dense_f32": (None, [_P, _P, _I, _P, _P]),
 }
 DTYPES = {0: np.float32, 1: np.float16, 2: np.int8, 3: np.int32}
 _LIB = None
@@ -145,6 +156,31 @@ def proto_s8h(x16, rows, sw, cls_w, cls_b, eps, C):
         h.bnno_proto_colmax_rows(ptr(qa[w]), K, ptr(sx[w]), P, ptr(rows), ptr(sw), Np, ptr(cm[w]))
         st[w] = h.bnno_proto_logits(ptr(cm[w]), ptr(cls_w), ptr(cls_b), nc, ppc, ptr(lg[w]))
     return qa, sx, cm, lg, st
+
+
+def h_op(name, *xs):
+    """An elementwise fp16 oracle operation over uint16 (IEEE half bit) arrays of one shape."""
+    f = getattr(lib(), name)
+    xs = [np.asarray(x, np.uint16).reshape(-1) for x in xs]
+    return np.array([f(*(int(x[i]) for x in xs)) for i in range(xs[0].size)], np.uint16)
+
+
+def silu_table():
+    """The oracle's fp16 SiLU coefficient table: {"c0": [16], "c1": [16], "c2": [16]} as 16-bit values."""
+    return {k: list((_H * 16).in_dll(lib(), f"BNNO_SILU_{k.upper()}")) for k in ("c0", "c1", "c2")}
+
+
+def gemm_f16(A, w, b32, b16, Kp, Np, act, M, ldo=None, ow=0, opad=0, res=None, ldr=0, out_rows=None):
+    """src/gemm_f16.c on fp16 arrays (uint16 views): A [M][lda] -> out [out_rows][ldo]."""
+    A = np.ascontiguousarray(A).view(np.uint16)
+    ldo = ldo or Np
+    rows = out_rows or (((M // ow) + 2 * opad) * (ow + 2 * opad) if opad else M)
+    out = np.zeros((rows, ldo), np.uint16)
+    r = None if res is None else np.ascontiguousarray(res).view(np.uint16)
+    lib().bnno_gemm_f16(ptr(A), A.shape[1], M, ptr(np.ascontiguousarray(w).view(np.uint16)), ptr(b32),
+                        ptr(np.ascontiguousarray(b16).view(np.uint16)), Kp, Np, act, ptr(out), ldo, ow, opad, ptr(r),
+                        ldr)
+    return out.view(np.float16)
 
 
 class Package:

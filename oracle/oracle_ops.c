@@ -234,8 +234,10 @@ void bnno_dw3(const float *xp, int H, int W, int C, int s, const float *w, const
 /* ------------------------------------------------------------------ squeeze-excitation gate */
 
 /* v24k32_se_fc1 (src/v24_f32.c:164-179) then se_gate_range (src/rt_ops_f32.c:272-283) */
-void bnno_se_gate(int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,
-                  const float *chsum, int P, float *gate) {
+/* the SE's two fully connected layers (v24k32_se_fc1, src/v24_f32.c:164-179, and se_gate_range, src/rt_ops_f32.c:
+ * 272-283): g [C] before the sigmoid. Shared by SE_GATE and the fp16 path's SE (src/v24_fast.c:188-210). */
+void bnno_se_fc(int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2, const float *chsum,
+                int P, float *g) {
   float *mean = malloc(sizeof(float) * (size_t)C), *s1 = malloc(sizeof(float) * (size_t)rd);
   const float inv = 1.f / (float)P;
   for (int c = 0; c < C; c++) mean[c] = chsum[c] * inv;
@@ -256,12 +258,18 @@ void bnno_se_gate(int C, int rd, const float *w1, const float *b1, const float *
     s1[r] = xr / (1.f + expf(-xr)); /* silu_s (src/v24_f32.c:160): libm expf, IEEE division */
   }
   for (int c = 0; c < C; c++) {
-    float g = b2[c];
-    for (int r = 0; r < rd; r++) g = fmaf(w2t[(size_t)r * C + c], s1[r], g);
-    gate[c] = bnno_sigmoid(g);
+    float a = b2[c];
+    for (int r = 0; r < rd; r++) a = fmaf(w2t[(size_t)r * C + c], s1[r], a);
+    g[c] = a;
   }
   free(mean);
   free(s1);
+}
+
+void bnno_se_gate(int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,
+                  const float *chsum, int P, float *gate) {
+  bnno_se_fc(C, rd, w1, b1, w2t, b2, chsum, P, gate);
+  for (int c = 0; c < C; c++) gate[c] = bnno_sigmoid(gate[c]);
 }
 
 /* ------------------------------------------------------------------ c0 conv + pool */

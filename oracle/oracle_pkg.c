@@ -2,8 +2,8 @@
  *
  * Reads the package format the reference compiler writes (python/bnneon/compiler/pkgfmt.py:1-22) and runs the op
  * list in order (rt_run, src/rt_pkg.c:528-542) with the oracle's per-op restatements. Buffers get memory of their
- * own instead of the reference's shared slots: no op of the v2.4 int8 path reads a value it did not write in the
- * same window (halos are re-zeroed by the producing PW_S8, every other buffer is written in full), so the results
+ * own instead of the reference's shared slots: no op of the v2.4 int8 and fp16 paths reads a value it did not write
+ * in the same window (halos are re-zeroed by the producing PW, every other buffer is written in full), so the results
  * are the same. Package validation is minimal here; the product loader does the full checks. */
 #include <pthread.h>
 #include <stdio.h>
@@ -202,6 +202,30 @@ static int run_op(bnno_pkg *p, const o_op *op) {
     free(sx);
     return bnno_proto_logits(bptr(p, op, 3), tdata(p, op, 3), tdata(p, op, 4), P[7], P[8], bptr(p, op, 1));
   }
+  case 0x102: /* C0POOL f16: b = [img f32, pin f16]; t = [w b32 b16] */
+    bnno_c0pool_f16(bptr(p, op, 0), tdata(p, op, 0), tdata(p, op, 2), bptr(p, op, 1));
+    return 0;
+  case 0x103: /* PW f16: b = [in, out, res|-1]; t = [w b32 b16]; p = [N K Kp Np M lda act ldo ow opad ldr] */
+    bnno_gemm_f16(bptr(p, op, 0), P[5], P[4], tdata(p, op, 0), tdata(p, op, 1), tdata(p, op, 2), P[2], P[3], P[6],
+                  bptr(p, op, 1), P[7], P[8], P[9], bptr(p, op, 2), P[10]);
+    return 0;
+  case 0x104: /* DW3 f16: b = [xp, out, chsum]; p = [H W C s Ho Wo pt pl] */
+    bnno_dw3_f16(bptr(p, op, 0), P[0], P[1], P[2], P[3], P[6], P[7], tdata(p, op, 0), tdata(p, op, 1), bptr(p, op, 1),
+                 P[4], P[5], bptr(p, op, 2));
+    return 0;
+  case 0x105: /* SE f16: b = [D, chsum]; p = [C rd P] */
+    bnno_se_f16(P[0], P[1], tdata(p, op, 0), tdata(p, op, 1), tdata(p, op, 2), tdata(p, op, 3), bptr(p, op, 1), P[2],
+                bptr(p, op, 0));
+    return 0;
+  case 0x106: /* POSTPC f16: b = [X, feat, pcin, pcout]; t = [post_s post_b w b32 b16] */
+    return bnno_postpc_f16(bptr(p, op, 0), tdata(p, op, 0), tdata(p, op, 1), tdata(p, op, 2), tdata(p, op, 3),
+                           tdata(p, op, 4), bptr(p, op, 1));
+  case 0x107: /* DENSE f16: b = [feat, out]; t = [w f16 [N][1024], b]; p = [N] */
+    bnno_dense_f16(tdata(p, op, 0), tdata(p, op, 1), P[0], bptr(p, op, 0), bptr(p, op, 1));
+    return 0;
+  case 7: /* DENSE f32 */
+    bnno_dense_f32(tdata(p, op, 0), tdata(p, op, 1), P[0], bptr(p, op, 0), bptr(p, op, 1));
+    return 0;
   default:
     return -1;
   }

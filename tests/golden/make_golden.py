@@ -14,7 +14,8 @@ s8_packing.npz, and for the int8 prototype head (PROTO_S8): the reference loweri
 prototype heads into one-op neon-int8 packages (sha256 in proto_packages.json; bnneon_b200.synth.write_proto_package
 must write the same bytes) and its packer (quant_rows_s8, n4_panel_flags, the [Np/4][Kp/16][4][16] layout) runs on
 fixed matrices (proto_packing.npz); and the reference lowering's l_fe_logmel writes one-op log-mel front-end packages
-(logmel_packages.json).
+(logmel_packages.json); and the reference lowering writes the same v2.4 models for the neon-fp16 path (sha256 in
+f16_packages.json, with the reference's fp16 SiLU coefficient table read from its source).
 """
 import hashlib
 import json
@@ -178,6 +179,61 @@ def logmel_fixtures(ref_root):
         f.write("\n")
 
 
+# the neon-fp16 packages: (name, seed, blocks, head classes); 61 classes give the fp32 head (DENSE variant 0)
+F16_MODELS = (("v24_full_f16", 0, "full", 6522), ("v24_mini_f16", 1, "mini", 100), ("v24_mini_f16_h32", 1, "mini", 61))
+
+
+def reference_f16_package(ref_root, ir, dst):
+    """The reference lowering of the v2.4 IR for the neon-fp16 path (bnc.py compile --paths neon-fp16)."""
+    sys.path.insert(0, os.path.join(ref_root, "python"))
+    from bnneon.compiler import lower, pkgfmt  # pylint: disable=import-outside-toplevel
+    ops, vshape, lv, ev = ir
+    pkg = pkgfmt.Package()
+    lw = lower.Lowering(pkg, ops, synth.PATH_F16, synth.NSAMP)
+    bufs, rops = lw.run(vshape)
+    ob, eb = lw.vbuf[lv], lw.vbuf.get(ev)
+    n_classes, emb_dim = bufs[ob][3], bufs[eb][3]
+    bufs, _ = lower.plan_slots(bufs, rops, [ob, eb])
+    pkg.add_path(synth.PATH_F16, lower.path_info(synth.PATH_F16).hwcap, bufs, rops, 0, ob, eb)
+    pkg.set(f"src_nodes/{synth.PATH_F16}", "\n".join(lw.src))
+    for k, v in synth.metadata(n_classes, emb_dim, synth.labels_for(n_classes)):
+        pkg.set(k, v)
+    pkg.write(dst)
+    return n_classes, emb_dim
+
+
+def silu_table(ref_root):
+    """The fp16 SiLU table of the reference (src/silu_lut_tables_deg2.h: low bytes then high bytes of 16 fp16
+    coefficients per array) as 16-bit values."""
+    import re  # pylint: disable=import-outside-toplevel
+    with open(os.path.join(ref_root, "src", "silu_lut_tables_deg2.h"), encoding="utf-8") as f:
+        text = f.read()
+    out = {}
+    for name in ("C0", "C1", "C2"):
+        body = re.search(r"SILU_LUT_%s\[32\][^{]*\{([^}]*)\}" % name, text).group(1)
+        b = [int(x, 16) for x in re.findall(r"0x[0-9a-fA-F]+", body)]
+        out[name.lower()] = [b[i] | b[16 + i] << 8 for i in range(16)]
+    return out
+
+
+def f16_fixtures(ref_root):
+    out = {}
+    with tempfile.TemporaryDirectory() as td:
+        for name, seed, kind, nc in F16_MODELS:
+            blocks = synth.V24_BLOCKS if kind == "full" else synth.MINI_BLOCKS
+            ref = os.path.join(td, name + ".ref.bnpk")
+            n_classes, emb_dim = reference_f16_package(ref_root, synth.v24_ir(seed, nc, blocks), ref)
+            mine = os.path.join(td, name + ".mine.bnpk")
+            synth.write_f16_package(mine, synth.v24_ir(seed, nc, blocks))
+            out[name] = dict(seed=seed, blocks=kind, head_classes=nc, n_classes=n_classes, emb_dim=emb_dim,
+                             size=os.path.getsize(ref), sha256=sha(ref))
+            print(name, out[name], "writer matches" if sha(mine) == sha(ref) else "WRITER DIFFERS")
+    out["silu_lut"] = silu_table(ref_root)
+    with open(os.path.join(HERE, "f16_packages.json"), "w", encoding="utf-8") as f:
+        json.dump(out, f, indent=1, sort_keys=True)
+        f.write("\n")
+
+
 def sha(path):
     with open(path, "rb") as f:
         return hashlib.sha256(f.read()).hexdigest()
@@ -221,6 +277,7 @@ def main():
     print("wrote packages.json and s8_packing.npz")
     proto_fixtures(ref_root)
     logmel_fixtures(ref_root)
+    f16_fixtures(ref_root)
 
 
 if __name__ == "__main__":
