@@ -1,0 +1,743 @@
+// The neon-fp16 path's kernels (the variant-1 ops of src/rt_ops_f16.c for the v2.4 architecture), bit for bit.
+//
+// The reference computes these layers with ARMv8.2 fp16 arithmetic in a fixed order: every multiply-add of its GEMMs
+// and depthwise convs is one fused fp16 FMLA lane operation, rounded once (src/gemm_f16.c, src/gemm_f16_kblock.h,
+// src/kern_f16.c, src/v24_fast.c). The B200's fp16 pipe executes exactly that operation -- PTX fma.rn.f16x2: fused,
+// round to nearest even, fp16 subnormals kept -- two lanes per instruction, so these kernels run the reference's
+// chains as they are, on CUDA cores. (The tensor cores accumulate in another order and precision and cannot reproduce
+// an fp16 FMA chain.) Every fp16 add, subtract, multiply and FMA is explicit PTX with .rn, which is never contracted;
+// the fp32 steps use the __f*_rn intrinsics. NaN results are the canonical NaN; payloads are not modelled.
+//
+// Layouts: activations are the package's fp16 NHWC buffers, B windows at a fixed window stride (elements). GEMM
+// weights are uploaded k-major, [Kp][Np] fp16 (row k holds the Np output channels), from the package's hp_pack panels.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "bnn_kernels.h"
+#include "emu.cuh"
+
+namespace bnn {
+
+// ------------------------------------------------------------------ fp16 pairs (two IEEE halves in a 32-bit word)
+
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {  // a * b + c, lane-wise
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ float h_lo(uint32_t x) { return __half2float(__ushort_as_half((unsigned short)(x & 0xffffu))); }
+__device__ __forceinline__ float h_hi(uint32_t x) { return __half2float(__ushort_as_half((unsigned short)(x >> 16))); }
+// fp32 -> fp16, nearest even (cvt.rn.f16.f32)
+__device__ __forceinline__ uint32_t f2h(float x) { return __half_as_ushort(__float2half_rn(x)); }
+__device__ __forceinline__ uint32_t pack2(uint32_t lo, uint32_t hi) { return lo | (hi << 16); }
+
+// FMAX(x, +0) lane-wise, as NEON vmaxq_f16(x, 0): negative values and -0 give +0, NaN stays NaN
+__device__ __forceinline__ uint32_t relu2(uint32_t x) {
+  const uint32_t nan = __vcmpgtu2(x & 0x7fff7fffu, 0x7c007c00u), neg = __vcmpgeu2(x, 0x80008000u);
+  return x & ~(neg & ~nan);
+}
+
+// The SiLU of the fp16 kernels (src/silu_lut.h:23-38): silu(x) = FMAX(x, 0) - |x| q(|x|), q a quadratic per unit
+// segment n = round(min(|x|, 15.4)) of the reference's coefficient table, at f = u - n. The clamp is an unsigned
+// lane minimum, which equals FMIN for the non-negative |x| except that a NaN lane becomes 15.4: its result is NaN
+// all the same, through FMAX(x, 0). tab01[n] = c0 | c1 << 16, tab2[n] = c2 (in shared memory).
+__device__ __forceinline__ uint32_t silu2(uint32_t x, const uint32_t *tab01, const uint32_t *tab2) {
+  const uint32_t u = x & 0x7fff7fffu;
+  const uint32_t uc = __vminu2(u, 0x4bb34bb3u);      // (fp16)15.4
+  const uint32_t tm = hadd2(uc, 0x66006600u);        // 1536 + round(uc): its low byte is the segment
+  const uint32_t f = hsub2(uc, hsub2(tm, 0x66006600u));
+  const uint32_t n0 = tm & 15u, n1 = (tm >> 16) & 15u;
+  const uint32_t t0 = tab01[n0], t1 = tab01[n1];
+  const uint32_t c0 = __byte_perm(t0, t1, 0x5410), c1 = __byte_perm(t0, t1, 0x7632);
+  const uint32_t c2 = __byte_perm(tab2[n0], tab2[n1], 0x5410);
+  uint32_t p = hfma2(c2, f, c1);
+  p = hfma2(p, f, c0);
+  return hfma2(u ^ 0x80008000u, p, relu2(x));  // FMLS: FMAX(x, 0) - u * p, one rounding
+}
+
+// The coefficient table of src/silu_lut_tables_deg2.h (there split into low and high bytes for a 2-register TBL):
+// c0 | c1 << 16 and c2, per segment n = 0..15.
+__constant__ uint32_t c_silu01[16] = {
+    0xb40b3800u, 0xb242344eu, 0xaecc2fa1u, 0xa9ea2a12u, 0xa4a6249au, 0x9f031ed9u, 0x99351910u, 0x93b11375u,
+    0x8daa0d7eu, 0x882c080au, 0x831202f9u, 0x81210118u, 0x806a0067u, 0x80270026u, 0x800e000eu, 0x80050005u};
+__constant__ uint32_t c_silu2[16] = {0x23bd, 0x299d, 0x2915, 0x254c, 0x2073, 0x1ae1, 0x1528, 0x0fa3,
+                                     0x09a2, 0x0426, 0x0187, 0x0090, 0x0035, 0x0013, 0x0007, 0x0003};
+
+__device__ __forceinline__ void load_silu_tab(uint32_t *tab01, uint32_t *tab2) {
+  for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 16; i += blockDim.x * blockDim.y) {
+    tab01[i] = c_silu01[i];
+    tab2[i] = c_silu2[i];
+  }
+}
+
+// ------------------------------------------------------------------ GEMM (PW f16, the pc conv)
+//
+// gemm_f16_range (src/gemm_f16.c:109-169) per output (row m, channel n): K in blocks of bs k-steps (kblocks: as few
+// blocks of <= 128 as possible, balanced, multiples of 8), in each block one fp16 FMA chain from +0 in k order; with
+// two or more blocks the chains are summed in fp32 from 0 and the bias is added in fp32 (b32) before one rounding to
+// fp16, else the bias is an fp16 add (b16). Epilogue: SiLU (table) or FMAX(x, 0), then the fp16 residual add, stored
+// at the pixel's padded row.
+//
+// CTA tile: BM = 8 RT rows x BN = 8 NT channels (NT threads across the channels, RT across the rows); each thread
+// holds 8 rows x 8 channels as 32 fp16 pairs, a pair being two ROWS of one channel, so that an FMA takes the rows'
+// activations as they lie in the transposed shared tile and the channel's weight duplicated into both lanes. Shared
+// memory per stage of kGS k-steps: At [kGS][BM] fp16 (the activations transposed), Wd [kGS][BN] u32 (the weights,
+// duplicated). Per k a thread issues 3 16-byte shared loads for 32 fp16x2 FMAs.
+constexpr int kGS = 32;
+
+struct GemmF16Args {
+  const uint16_t *A;
+  long long aws;
+  int lda, Mw, rows;
+  const uint16_t *W;  // [Kp][Np]
+  int Kp, Np, bs;
+  const uint16_t *b16;
+  const float *b32;
+  int act;
+  uint16_t *out;
+  long long ows;
+  int ldo, ow, opad;
+  const uint16_t *res;
+  long long rws;
+  int ldr;
+  int NT, RT;
+};
+
+template <bool kFlush>
+__global__ void __launch_bounds__(256, 1) k_gemm_f16(const GemmF16Args g) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int NT = g.NT, RT = g.RT, BM = 8 * RT, BN = 8 * NT;
+  uint16_t *At = reinterpret_cast<uint16_t *>(sm);
+  uint32_t *Wd = reinterpret_cast<uint32_t *>(sm + (size_t)kGS * BM * 2);
+  uint32_t *tab01 = Wd + (size_t)kGS * BN, *tab2 = tab01 + 16;
+  const int tid = threadIdx.x, nthr = NT * RT;
+  const int tn = tid % NT, tr = tid / NT;
+  const long long m0 = (long long)blockIdx.x * BM;
+  const int n0 = blockIdx.y * BN;
+  load_silu_tab(tab01, tab2);
+
+  uint32_t acc[4][8];
+  float2 fb[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      acc[i][j] = 0u;
+      fb[i][j] = make_float2(0.f, 0.f);
+    }
+
+  for (int ks = 0; ks < g.Kp; ks += kGS) {
+    const int kn = min(kGS, g.Kp - ks), kc = kn / 8;
+    __syncthreads();
+    // activations: 16-byte chunks (row, 8 k-steps); a warp covers 32 consecutive rows of one chunk column, so that
+    // the transposed stores of each of the 8 halves are 32 consecutive shared halves
+    for (int idx = tid; idx < BM * kc; idx += nthr) {
+      const int ml = idx % BM, c = idx / BM;
+      const long long r = m0 + ml;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < g.rows) {
+        const long long w = r / g.Mw, m = r - w * g.Mw;
+        v = __ldg(reinterpret_cast<const uint4 *>(g.A + w * g.aws + m * g.lda + ks + 8 * c));
+      }
+      uint16_t *d = At + (size_t)(8 * c) * BM + ml;
+      const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        d[(2 * j) * BM] = (uint16_t)(vv[j] & 0xffffu);
+        d[(2 * j + 1) * BM] = (uint16_t)(vv[j] >> 16);
+      }
+    }
+    // weights: 8 channels of one k-step per chunk, duplicated into both lanes of a word
+    for (int idx = tid; idx < kn * NT; idx += nthr) {
+      const int kk = idx / NT, c8 = idx % NT, n = n0 + 8 * c8;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (n < g.Np) v = __ldg(reinterpret_cast<const uint4 *>(g.W + (size_t)(ks + kk) * g.Np + n));
+      uint4 *d = reinterpret_cast<uint4 *>(Wd + (size_t)kk * BN + 8 * c8);
+      d[0] = make_uint4(__byte_perm(v.x, 0, 0x1010), __byte_perm(v.x, 0, 0x3232), __byte_perm(v.y, 0, 0x1010),
+                        __byte_perm(v.y, 0, 0x3232));
+      d[1] = make_uint4(__byte_perm(v.z, 0, 0x1010), __byte_perm(v.z, 0, 0x3232), __byte_perm(v.w, 0, 0x1010),
+                        __byte_perm(v.w, 0, 0x3232));
+    }
+    __syncthreads();
+    for (int kk = 0; kk < kn; kk += 8) {
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const uint4 a = *reinterpret_cast<const uint4 *>(At + (size_t)(kk + u) * BM + tr * 8);
+        const uint4 w0 = *reinterpret_cast<const uint4 *>(Wd + (size_t)(kk + u) * BN + tn * 8);
+        const uint4 w1 = *reinterpret_cast<const uint4 *>(Wd + (size_t)(kk + u) * BN + tn * 8 + 4);
+        const uint32_t av[4] = {a.x, a.y, a.z, a.w};
+        const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[i][j] = hfma2(av[i], wv[j], acc[i][j]);
+      }
+      if (kFlush) {
+        const int kg = ks + kk + 8;
+        if (kg % g.bs == 0 || kg == g.Kp) {  // the end of a K block: flush the chains to fp32, restart from +0
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              fb[i][j].x = __fadd_rn(fb[i][j].x, h_lo(acc[i][j]));
+              fb[i][j].y = __fadd_rn(fb[i][j].y, h_hi(acc[i][j]));
+              acc[i][j] = 0u;
+            }
+        }
+      }
+    }
+  }
+
+  // epilogue
+  const int nb = n0 + tn * 8;
+  if (nb >= g.Np) return;
+  uint32_t bias16[4];
+  float bias32[8];
+  {
+    const uint4 b = __ldg(reinterpret_cast<const uint4 *>(g.b16 + nb));
+    bias16[0] = b.x; bias16[1] = b.y; bias16[2] = b.z; bias16[3] = b.w;
+#pragma unroll
+    for (int j = 0; j < 8; j++) bias32[j] = __ldg(g.b32 + nb + j);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int l = 0; l < 2; l++) {
+      const long long r = m0 + tr * 8 + 2 * i + l;
+      if (r >= g.rows) continue;
+      const long long w = r / g.Mw, m = r - w * g.Mw;
+      uint32_t v[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        if (kFlush) {
+          const float x0 = l ? fb[i][2 * q].y : fb[i][2 * q].x, x1 = l ? fb[i][2 * q + 1].y : fb[i][2 * q + 1].x;
+          v[q] = pack2(f2h(__fadd_rn(x0, bias32[2 * q])), f2h(__fadd_rn(x1, bias32[2 * q + 1])));
+        } else {
+          v[q] = hadd2(__byte_perm(acc[i][2 * q], acc[i][2 * q + 1], l ? 0x7632 : 0x5410), bias16[q]);
+        }
+        if (g.act == 1) v[q] = silu2(v[q], tab01, tab2);
+        else if (g.act == 2) v[q] = relu2(v[q]);
+      }
+      if (g.res) {
+        const uint4 rv = __ldg(reinterpret_cast<const uint4 *>(g.res + w * g.rws + m * g.ldr + nb));
+        v[0] = hadd2(v[0], rv.x); v[1] = hadd2(v[1], rv.y); v[2] = hadd2(v[2], rv.z); v[3] = hadd2(v[3], rv.w);
+      }
+      const long long orow = g.opad ? (m / g.ow + g.opad) * (g.ow + 2 * g.opad) + m % g.ow + g.opad : m;
+      *reinterpret_cast<uint4 *>(g.out + w * g.ows + orow * g.ldo + nb) = make_uint4(v[0], v[1], v[2], v[3]);
+    }
+}
+
+// ------------------------------------------------------------------ C0POOL f16 (src/v24_fast.c:150-164)
+//
+// One CTA per (output row oy, window), thread qx = the pooled pixel: conv pixels 2qx and 2qx + 1 as the two lanes of
+// 24 fp16 pairs (one per channel), K = 64 FMAs in (ky, kx, ci) order from +0 (gemm_f16_rows: the 4 segments continue
+// one chain), + b16, ReLU, [max | avg] of the pair. The 4 padded image rows are staged in shared memory as fp16
+// (the reference rounds the image to fp16 first), pre-paired: word (ky, ci, col) = (img16[col], img16[col + 2]),
+// stored by col % 4 so that the 32 threads of a warp (columns 4 qx + kx) read consecutive words.
+__global__ void __launch_bounds__(128) k_c0pool_f16(const float *__restrict__ img, long long iws,
+                                                    const uint16_t *__restrict__ W /* [64][24] */,
+                                                    const uint16_t *__restrict__ b16, uint16_t *__restrict__ pin,
+                                                    long long pws) {
+  constexpr int NJ = 130;  // words per (ky, ci, col % 4) run: columns 0..519
+  __shared__ uint32_t P[4][2][4][NJ];
+  __shared__ __align__(16) uint32_t wd[64][24];
+  __shared__ uint16_t sh[4][520][2];
+  const int oy = blockIdx.x, win = blockIdx.y, tid = threadIdx.x;
+  const float *im = img + (long long)win * iws;
+  for (int i = tid; i < 4 * 520 * 2; i += 128) {
+    const int ky = i / 1040, col = (i / 2) % 520, ci = i & 1;
+    const int y = 2 * oy + ky - 1, x = col - 3;
+    sh[ky][col][ci] = (y >= 0 && y < 96 && x >= 0 && x < 511) ? (uint16_t)f2h(im[(y * 511 + x) * 2 + ci]) : 0;
+  }
+  for (int i = tid; i < 64 * 24; i += 128) {
+    const uint32_t h = __ldg(W + i);
+    wd[i / 24][i % 24] = h | (h << 16);
+  }
+  __syncthreads();
+  for (int i = tid; i < 4 * 2 * 518; i += 128) {
+    const int ky = i / (2 * 518), ci = (i / 518) & 1, col = i % 518;
+    P[ky][ci][col & 3][col >> 2] = pack2(sh[ky][col][ci], sh[ky][col + 2][ci]);
+  }
+  __syncthreads();
+  const int qx = tid;
+  uint32_t acc[24];
+#pragma unroll
+  for (int n = 0; n < 24; n++) acc[n] = 0u;
+#pragma unroll 1
+  for (int ky = 0; ky < 4; ky++)
+#pragma unroll
+    for (int kx = 0; kx < 8; kx++)
+#pragma unroll
+      for (int ci = 0; ci < 2; ci++) {
+        const uint32_t a = P[ky][ci][kx & 3][qx + (kx >> 2)];
+        const uint4 *wr = reinterpret_cast<const uint4 *>(wd[ky * 16 + kx * 2 + ci]);
+#pragma unroll
+        for (int q = 0; q < 6; q++) {
+          const uint4 w = wr[q];
+          acc[4 * q] = hfma2(a, w.x, acc[4 * q]);
+          acc[4 * q + 1] = hfma2(a, w.y, acc[4 * q + 1]);
+          acc[4 * q + 2] = hfma2(a, w.z, acc[4 * q + 2]);
+          acc[4 * q + 3] = hfma2(a, w.w, acc[4 * q + 3]);
+        }
+      }
+  uint32_t mx[12], av[12];
+#pragma unroll
+  for (int q = 0; q < 12; q++) {
+    uint32_t m[2], a[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint32_t b = __ldg(b16 + 2 * q + h);
+      const uint32_t v = relu2(hadd2(acc[2 * q + h], b | (b << 16)));  // lanes: the two conv pixels
+      m[h] = max(v & 0xffffu, v >> 16);                                 // FMAX of values >= +0 (or NaN): bit order
+      a[h] = hmul2(hadd2(v, __byte_perm(v, 0, 0x1032)), 0x38003800u) & 0xffffu;  // (a + b) * 0.5
+    }
+    mx[q] = pack2(m[0], m[1]);
+    av[q] = pack2(a[0], a[1]);
+  }
+  uint4 *o = reinterpret_cast<uint4 *>(pin + (long long)win * pws + ((long long)oy * 128 + qx) * 48);
+  o[0] = make_uint4(mx[0], mx[1], mx[2], mx[3]);
+  o[1] = make_uint4(mx[4], mx[5], mx[6], mx[7]);
+  o[2] = make_uint4(mx[8], mx[9], mx[10], mx[11]);
+  o[3] = make_uint4(av[0], av[1], av[2], av[3]);
+  o[4] = make_uint4(av[4], av[5], av[6], av[7]);
+  o[5] = make_uint4(av[8], av[9], av[10], av[11]);
+}
+
+// ------------------------------------------------------------------ DW3 f16 (src/kern_f16.c:83-155)
+//
+// Thread (channel pair, output row): the row's pixels in order, per pixel two FMA chains over the taps (a from the
+// bias: taps 0, 2, 4, 6, 8; a2 from the product of tap 1: taps 3, 5, 7), y = SiLU(a + a2), the fp16 row sum of y in
+// pixel order; then one thread per pair adds the row sums in row order in fp32 (chsum).
+__global__ void __launch_bounds__(1024) k_dw3_f16(const uint16_t *__restrict__ xp, long long xws, int W, int C, int s,
+                                                  int pt, int pl, const uint16_t *__restrict__ wt,
+                                                  const uint16_t *__restrict__ bt, uint16_t *__restrict__ out,
+                                                  long long ows, int Ho, int Wo, float *__restrict__ chsum,
+                                                  long long cws) {
+  extern __shared__ uint32_t srs[];  // [Ho][Lc] row sums
+  __shared__ uint32_t tab01[16], tab2[16];
+  const int Lc = blockDim.x, lane = threadIdx.x, win = blockIdx.y;
+  const int c2 = blockIdx.x * Lc + lane, C2 = C / 2;
+  load_silu_tab(tab01, tab2);
+  __syncthreads();
+  const bool on = c2 < C2;
+  uint32_t w[9], b = 0;
+  if (on) {
+    const uint32_t *w32 = reinterpret_cast<const uint32_t *>(wt);
+#pragma unroll
+    for (int t = 0; t < 9; t++) w[t] = __ldg(w32 + t * C2 + c2);
+    b = __ldg(reinterpret_cast<const uint32_t *>(bt) + c2);
+  }
+  const uint32_t *x = reinterpret_cast<const uint32_t *>(xp + (long long)win * xws);
+  uint32_t *o = reinterpret_cast<uint32_t *>(out + (long long)win * ows);
+  const int Wp = W + 2;
+  for (int oy = threadIdx.y; oy < Ho; oy += blockDim.y) {
+    uint32_t rs = 0u;
+    if (on) {
+      const int iy0 = oy * s - pt + 1;
+      for (int ox = 0; ox < Wo; ox++) {
+        const int ix0 = ox * s - pl + 1;
+        const uint32_t *r0 = x + ((long long)iy0 * Wp + ix0) * C2 + c2, *r1 = r0 + (long long)Wp * C2,
+                       *r2 = r1 + (long long)Wp * C2;
+        const uint32_t x00 = __ldg(r0), x01 = __ldg(r0 + C2), x02 = __ldg(r0 + 2 * C2);
+        const uint32_t x10 = __ldg(r1), x11 = __ldg(r1 + C2), x12 = __ldg(r1 + 2 * C2);
+        const uint32_t x20 = __ldg(r2), x21 = __ldg(r2 + C2), x22 = __ldg(r2 + 2 * C2);
+        uint32_t a = hfma2(x00, w[0], b);
+        uint32_t a2 = hmul2(x01, w[1]);
+        a = hfma2(x02, w[2], a);
+        a2 = hfma2(x10, w[3], a2);
+        a = hfma2(x11, w[4], a);
+        a2 = hfma2(x12, w[5], a2);
+        a = hfma2(x20, w[6], a);
+        a2 = hfma2(x21, w[7], a2);
+        a = hfma2(x22, w[8], a);
+        const uint32_t y = silu2(hadd2(a, a2), tab01, tab2);
+        o[((long long)oy * Wo + ox) * C2 + c2] = y;
+        rs = hadd2(rs, y);
+      }
+    }
+    srs[oy * Lc + lane] = rs;
+  }
+  __syncthreads();
+  if (threadIdx.y == 0 && on) {
+    float s0 = 0.f, s1 = 0.f;
+    for (int oy = 0; oy < Ho; oy++) {
+      const uint32_t r = srs[oy * Lc + lane];
+      s0 = __fadd_rn(s0, h_lo(r));
+      s1 = __fadd_rn(s1, h_hi(r));
+    }
+    *reinterpret_cast<float2 *>(chsum + (long long)win * cws + 2 * c2) = make_float2(s0, s1);
+  }
+}
+
+// ------------------------------------------------------------------ SE f16 (src/v24_fast.c:186-235)
+
+// sigm4 (src/v24_fast.c:173-185): 1 / (1 + 2^t), t = -a log2 e clamped to [-126, 126], 2^t as a degree-6 polynomial
+// of the fraction (FMA chain) with the integer part added to the exponent bits, an IEEE division
+__device__ __forceinline__ float sigm_f16path(float a) {
+  float t = __fmul_rn(a, -1.44269504f);
+  t = fmin_nan(fmax_nan(t, -126.f), 126.f);
+  const float n = rintf(t), f = __fsub_rn(t, n);
+  float p = 1.5403530e-4f;
+  p = __fmaf_rn(p, f, 1.3333558e-3f);
+  p = __fmaf_rn(p, f, 9.6181291e-3f);
+  p = __fmaf_rn(p, f, 5.5504109e-2f);
+  p = __fmaf_rn(p, f, 2.4022651e-1f);
+  p = __fmaf_rn(p, f, 6.9314718e-1f);
+  p = __fmaf_rn(p, f, 1.f);
+  const float e = __int_as_float((int)((uint32_t)__float_as_int(p) + ((uint32_t)cvtzs(n) << 23)));
+  return __fdiv_rn(1.f, __fadd_rn(1.f, e));
+}
+
+// One CTA per window: the gate as SE_GATE computes it (mean, fc1 in the NEON lane order, SiLU with glibc expf, fc2
+// from the bias in r order), then sigm4, rounded to fp16 -> g16 [C]
+constexpr int kSe16Threads = 512;
+__global__ void __launch_bounds__(kSe16Threads) k_se_gate_f16(int C, int rd, const float *__restrict__ w1,
+                                                              const float *__restrict__ b1,
+                                                              const float *__restrict__ w2t,
+                                                              const float *__restrict__ b2,
+                                                              const float *__restrict__ chsum, long long cws, int P,
+                                                              uint16_t *__restrict__ g16) {
+  extern __shared__ float sm_se[];
+  float *mean = sm_se, *s1 = sm_se + C;
+  const int win = blockIdx.x, tid = threadIdx.x;
+  const float inv = __fdiv_rn(1.f, __int2float_rn(P));
+  for (int c = tid; c < C; c += kSe16Threads) mean[c] = __fmul_rn(chsum[win * cws + c], inv);
+  __syncthreads();
+  const int lane8 = tid & 7, C8 = C >> 3;
+  for (int r0 = 0; r0 < rd; r0 += kSe16Threads / 8) {
+    const int r = r0 + tid / 8;
+    float a = 0.f;
+    if (r < rd) {
+      const float *wr = w1 + (long long)r * C + lane8;
+      const float *mr = mean + lane8;
+      for (int i = 0; i < C8; i++) a = __fmaf_rn(__ldg(wr + 8 * i), mr[8 * i], a);
+    }
+    const float other = __shfl_down_sync(0xffffffffu, a, 4, 8);
+    const float v = __fadd_rn(a, other);
+    const float v1 = __shfl_down_sync(0xffffffffu, v, 1, 8), v2 = __shfl_down_sync(0xffffffffu, v, 2, 8),
+                v3 = __shfl_down_sync(0xffffffffu, v, 3, 8);
+    if (r < rd && lane8 == 0) {
+      const float xr = __fadd_rn(__fadd_rn(__fadd_rn(v, v1), __fadd_rn(v2, v3)), b1[r]);
+      s1[r] = __fdiv_rn(xr, __fadd_rn(1.f, glibc_expf(-xr, c_expf_tab)));
+    }
+  }
+  __syncthreads();
+  for (int c = tid; c < C; c += kSe16Threads) {
+    float gv = b2[c];
+    for (int r = 0; r < rd; r++) gv = __fmaf_rn(__ldg(w2t + (long long)r * C + c), s1[r], gv);
+    g16[(long long)win * C + c] = (uint16_t)f2h(sigm_f16path(gv));
+  }
+}
+
+// D [P][C] *= g16 [C] in place (an fp16 multiply per element), 8 halves per thread
+__global__ void k_se_scale_f16(int B, int P, int C, uint16_t *__restrict__ D, long long dws,
+                               const uint16_t *__restrict__ g16) {
+  const long long per = (long long)P * (C / 8), total = per * B;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long win = i / per, rem = i - win * per;
+    const int c8 = (int)(rem % (C / 8));
+    uint4 *d = reinterpret_cast<uint4 *>(D + win * dws) + rem;
+    const uint4 g = __ldg(reinterpret_cast<const uint4 *>(g16 + win * C) + c8);
+    uint4 v = *d;
+    v.x = hmul2(v.x, g.x); v.y = hmul2(v.y, g.y); v.z = hmul2(v.z, g.z); v.w = hmul2(v.w, g.w);
+    *d = v;
+  }
+}
+
+// ------------------------------------------------------------------ POSTPC f16 (src/v24_fast.c:273-311)
+
+// post = fp16(FMAX(fma(X, s, b), 0)) and the 3x3 valid im2col: pcin [6][1728] per window, k = (ky 3 + kx) 192 + c
+__global__ void k_postpc_f16_im2col(const uint16_t *__restrict__ X, long long xws, const float *__restrict__ ps,
+                                    const float *__restrict__ pb, uint16_t *__restrict__ pcin, long long pws) {
+  const int win = blockIdx.y;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 6 * 1728; i += gridDim.x * blockDim.x) {
+    const int ox = i / 1728, k = i % 1728, t = k / 192, c = k % 192, ky = t / 3, kx = t % 3;
+    const int p = ky * 8 + ox + kx;
+    const float x = __half2float(__ushort_as_half(X[(long long)win * xws + p * 192 + c]));
+    pcin[(long long)win * pws + i] = (uint16_t)f2h(fmax_nan(__fmaf_rn(x, ps[c], pb[c]), 0.f));
+  }
+}
+
+// feat [1024] = (sum of the 6 positions in fp32, in order) * (1 / 6); a window with a feature that is not finite or
+// above 3e38 in magnitude failed (v24k16_postpc returns -2): fail holds the smallest failed w_base + window
+__global__ void k_postpc_f16_mean(const uint16_t *__restrict__ pcout, long long pws, float *__restrict__ feat,
+                                  long long fws, int *fail, int w_base) {
+  const int win = blockIdx.x;
+  bool bad = false;
+  for (int c = threadIdx.x; c < 1024; c += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int ox = 0; ox < 6; ox++)
+      s = __fadd_rn(s, __half2float(__ushort_as_half(pcout[(long long)win * pws + ox * 1024 + c])));
+    const float v = __fmul_rn(s, 1.f / 6.f);
+    feat[(long long)win * fws + c] = v;
+    bad |= !(fabsf(v) <= 3.0e38f);
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0 && fail) atomicMin(fail, w_base + win);
+}
+
+// ------------------------------------------------------------------ DENSE f16 (src/v24_fast.c:237-270)
+//
+// The 4-row path of v24k16_head for every class o < N & ~3: x = fp16(feat); per 128-k block 8 fp16 lanes, lane j
+// the FMA chain over k = j mod 8 from +0; the lanes flushed into 8 fp32 sums; out = FADDP((s_j + s_{j+4})_j) + b.
+// A thread holds 2 windows x 4 classes; a lane pair (2q, 2q + 1) is one fp16x2 chain over k-step pairs. Shared
+// tiles per block: X [32 windows][128 + 8] and W [64 classes][128 + 8] fp16 (rows padded against bank conflicts).
+constexpr int kDnW = 32, kDnC = 64, kDnLd = 136;
+__global__ void __launch_bounds__(256) k_dense_f16(int B, int N4, const float *__restrict__ feat, long long fws,
+                                                   const uint16_t *__restrict__ W, const float *__restrict__ bias,
+                                                   float *__restrict__ out, long long ows) {
+  __shared__ __align__(16) uint16_t xs[kDnW][kDnLd];
+  __shared__ __align__(16) uint16_t ws[kDnC][kDnLd];
+  const int tid = threadIdx.x, tw = tid / 16, tc = tid % 16;
+  const int w0 = blockIdx.y * kDnW, c0 = blockIdx.x * kDnC;
+  uint32_t acc[2][4][4];
+  float fs[2][4][8];
+#pragma unroll
+  for (int a = 0; a < 2; a++)
+#pragma unroll
+    for (int b = 0; b < 4; b++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) fs[a][b][j] = 0.f;
+  for (int kb = 0; kb < 1024; kb += 128) {
+    __syncthreads();
+    for (int i = tid; i < kDnW * 32; i += 256) {  // 4 features per step
+      const int r = i / 32, k4 = i % 32;
+      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (w0 + r < B) f = *reinterpret_cast<const float4 *>(feat + (long long)(w0 + r) * fws + kb + 4 * k4);
+      *reinterpret_cast<uint2 *>(&xs[r][4 * k4]) = make_uint2(pack2(f2h(f.x), f2h(f.y)), pack2(f2h(f.z), f2h(f.w)));
+    }
+    for (int i = tid; i < kDnC * 16; i += 256) {
+      const int r = i / 16, k8 = i % 16;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (c0 + r < N4) v = __ldg(reinterpret_cast<const uint4 *>(W + (long long)(c0 + r) * 1024 + kb + 8 * k8));
+      *reinterpret_cast<uint4 *>(&ws[r][8 * k8]) = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int a = 0; a < 2; a++)
+#pragma unroll
+      for (int b = 0; b < 4; b++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) acc[a][b][q] = 0u;
+#pragma unroll 4
+    for (int k = 0; k < 128; k += 8) {
+      uint4 xv[2], wv[4];
+#pragma unroll
+      for (int a = 0; a < 2; a++) xv[a] = *reinterpret_cast<const uint4 *>(&xs[tw * 2 + a][k]);
+#pragma unroll
+      for (int b = 0; b < 4; b++) wv[b] = *reinterpret_cast<const uint4 *>(&ws[tc * 4 + b][k]);
+#pragma unroll
+      for (int a = 0; a < 2; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+          acc[a][b][0] = hfma2(wv[b].x, xv[a].x, acc[a][b][0]);
+          acc[a][b][1] = hfma2(wv[b].y, xv[a].y, acc[a][b][1]);
+          acc[a][b][2] = hfma2(wv[b].z, xv[a].z, acc[a][b][2]);
+          acc[a][b][3] = hfma2(wv[b].w, xv[a].w, acc[a][b][3]);
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 2; a++)
+#pragma unroll
+      for (int b = 0; b < 4; b++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          fs[a][b][2 * q] = __fadd_rn(fs[a][b][2 * q], h_lo(acc[a][b][q]));
+          fs[a][b][2 * q + 1] = __fadd_rn(fs[a][b][2 * q + 1], h_hi(acc[a][b][q]));
+        }
+  }
+#pragma unroll
+  for (int a = 0; a < 2; a++)
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+      const int w = w0 + tw * 2 + a, o = c0 + tc * 4 + b;
+      if (w >= B || o >= N4) continue;
+      float v[4];
+#pragma unroll
+      for (int l = 0; l < 4; l++) v[l] = __fadd_rn(fs[a][b][l], fs[a][b][l + 4]);
+      out[(long long)w * ows + o] = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])), bias[o]);
+    }
+}
+
+// the scalar tail of v24k16_head (classes N & ~3 .. N - 1): fp32 products and sums in k order, + b
+__global__ void k_dense_f16_tail(int B, int N4, int N, const float *__restrict__ feat, long long fws,
+                                 const uint16_t *__restrict__ W, const float *__restrict__ bias,
+                                 float *__restrict__ out, long long ows) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x, nt = N - N4;
+  if (i >= B * nt) return;
+  const int w = i / nt, o = N4 + i % nt;
+  float s = 0.f;
+  for (int k = 0; k < 1024; k++) {
+    const float x = __half2float(__float2half_rn(feat[(long long)w * fws + k]));
+    s = __fadd_rn(s, __fmul_rn(__half2float(__ushort_as_half(W[(long long)o * 1024 + k])), x));
+  }
+  out[(long long)w * ows + o] = __fadd_rn(s, bias[o]);
+}
+
+// DENSE variant 0 (v24k32_head, src/v24_f32.c:213-243; the head of small models on every path): per class 8 fp32
+// FMA chains over k = j mod 8, out = FADDP((a_l + c_l)_l) + b
+__global__ void k_dense_f32(int B, int N, const float *__restrict__ feat, long long fws, const float *__restrict__ W,
+                            const float *__restrict__ bias, float *__restrict__ out, long long ows) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * N) return;
+  const int w = i / N, o = i % N;
+  const float *x = feat + (long long)w * fws, *wr = W + (long long)o * 1024;
+  float a[4] = {0.f, 0.f, 0.f, 0.f}, c[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k = 0; k < 1024; k += 8)
+#pragma unroll
+    for (int l = 0; l < 4; l++) {
+      a[l] = __fmaf_rn(wr[k + l], x[k + l], a[l]);
+      c[l] = __fmaf_rn(wr[k + 4 + l], x[k + 4 + l], c[l]);
+    }
+  float v[4];
+#pragma unroll
+  for (int l = 0; l < 4; l++) v[l] = __fadd_rn(a[l], c[l]);
+  out[(long long)w * ows + o] = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])), bias[o]);
+}
+
+}  // namespace bnn
+
+using namespace bnn;
+
+// ------------------------------------------------------------------ launchers
+
+extern "C" int bnnk_f16_tables_init(const unsigned long long *tab) {
+  return cudaMemcpyToSymbol(c_expf_tab, tab, sizeof(unsigned long long) * 32);
+}
+
+// K blocks (kblocks, src/gemm_f16.c:58-62)
+static void kblocks(int Kp, int *nblk, int *bs) {
+  *nblk = (Kp + 127) / 128;
+  *bs = ((Kp + *nblk - 1) / *nblk + 7) & ~7;
+}
+
+// the channel tile: all of Np up to 128, else the widest multiple of 8 up to 128 that divides Np (else 128)
+static int gemm_bn(int Np) {
+  if (Np <= 128) return Np;
+  for (int bn = 128; bn >= 64; bn -= 8)
+    if (Np % bn == 0) return bn;
+  return 128;
+}
+
+extern "C" int bnnk_gemm_f16(int rows, int Mw, const uint16_t *A, long long aws, int lda, const uint16_t *W, int Kp,
+                             int Np, const uint16_t *b16, const float *b32, int act, uint16_t *out, long long ows,
+                             int ldo, int ow, int opad, const uint16_t *res, long long rws, int ldr, bnn_stream_t st) {
+  if (rows <= 0) return 0;
+  if (Kp % 8 || Np % 8 || lda % 8 || aws % 8 || ldo % 8 || ows % 8 || (res && (ldr % 8 || rws % 8)) ||
+      ((uintptr_t)A & 15) || ((uintptr_t)W & 15) || ((uintptr_t)out & 15) || (res && ((uintptr_t)res & 15)))
+    return cudaErrorInvalidValue;
+  int nblk, bs;
+  kblocks(Kp, &nblk, &bs);
+  GemmF16Args g;
+  g.A = A; g.aws = aws; g.lda = lda; g.Mw = Mw; g.rows = rows;
+  g.W = W; g.Kp = Kp; g.Np = Np; g.bs = bs; g.b16 = b16; g.b32 = b32; g.act = act;
+  g.out = out; g.ows = ows; g.ldo = ldo; g.ow = ow; g.opad = opad; g.res = res; g.rws = rws; g.ldr = ldr;
+  const int BN = gemm_bn(Np);
+  g.NT = BN / 8;
+  g.RT = 256 / g.NT < 32 ? 256 / g.NT : 32;
+  const int BM = 8 * g.RT;
+  const size_t smem = (size_t)kGS * BM * 2 + (size_t)kGS * BN * 4 + 32 * 4;
+  const dim3 grid((unsigned)((rows + BM - 1) / BM), (unsigned)((Np + BN - 1) / BN));
+  cudaError_t e;
+  if (nblk > 1) {
+    e = cudaFuncSetAttribute(k_gemm_f16<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (!e) k_gemm_f16<true><<<grid, g.NT * g.RT, smem, st>>>(g);
+  } else {
+    e = cudaFuncSetAttribute(k_gemm_f16<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (!e) k_gemm_f16<false><<<grid, g.NT * g.RT, smem, st>>>(g);
+  }
+  return e ? e : cudaGetLastError();
+}
+
+extern "C" int bnnk_c0pool_f16(int B, const float *img, long long iws, const uint16_t *W, const uint16_t *b16,
+                               uint16_t *pin, long long pws, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  if (pws % 8 || ((uintptr_t)pin & 15)) return cudaErrorInvalidValue;
+  k_c0pool_f16<<<dim3(48, B), 128, 0, st>>>(img, iws, W, b16, pin, pws);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_dw3_f16(int B, const uint16_t *xp, long long xws, int H, int W, int C, int s, int pt, int pl,
+                            const uint16_t *w, const uint16_t *b, uint16_t *out, long long ows, int Ho, int Wo,
+                            float *chsum, long long cws, bnn_stream_t st) {
+  (void)H;
+  if (B <= 0) return 0;
+  if (C % 2 || xws % 2 || ows % 2 || cws % 2) return cudaErrorInvalidValue;
+  const int C2 = C / 2;
+  int Lc = C2 <= 64 ? C2 : 64;
+  for (int l = 64; l >= 32; l -= 8)  // a lane count that divides the channel pairs, if there is one
+    if (C2 > 64 && C2 % l == 0) { Lc = l; break; }
+  const int Ry = Ho < 1024 / Lc ? Ho : 1024 / Lc;
+  const size_t smem = sizeof(uint32_t) * (size_t)Ho * Lc;
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  k_dw3_f16<<<dim3((C2 + Lc - 1) / Lc, B), dim3(Lc, Ry), smem, st>>>(xp, xws, W, C, s, pt, pl, w, b, out, ows, Ho,
+                                                                     Wo, chsum, cws);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_se_f16(int B, int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,
+                           const float *chsum, long long cws, int P, uint16_t *D, long long dws, uint16_t *g16,
+                           bnn_stream_t st) {
+  if (B <= 0) return 0;
+  if (C % 8 || dws % 8 || ((uintptr_t)D & 15) || ((uintptr_t)g16 & 15)) return cudaErrorInvalidValue;
+  k_se_gate_f16<<<B, kSe16Threads, sizeof(float) * (size_t)(C + rd), st>>>(C, rd, w1, b1, w2t, b2, chsum, cws, P, g16);
+  cudaError_t e = cudaGetLastError();
+  if (e) return e;
+  const long long total = (long long)B * P * (C / 8);
+  const int blocks = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+  k_se_scale_f16<<<blocks, 256, 0, st>>>(B, P, C, D, dws, g16);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_postpc_f16(int B, const uint16_t *X, long long xws, const float *ps, const float *pb,
+                               const uint16_t *W, const uint16_t *b16, const float *b32, uint16_t *pcin,
+                               long long pinws, uint16_t *pcout, long long poutws, float *feat, long long fws,
+                               int *fail, int w_base, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  k_postpc_f16_im2col<<<dim3(12, B), 256, 0, st>>>(X, xws, ps, pb, pcin, pinws);
+  cudaError_t e = cudaGetLastError();
+  if (e) return e;
+  e = (cudaError_t)bnnk_gemm_f16(6 * B, 6, pcin, pinws, 1728, W, 1728, 1024, b16, b32, 2, pcout, poutws, 1024, 0, 0,
+                                 NULL, 0, 0, st);
+  if (e) return e;
+  k_postpc_f16_mean<<<B, 256, 0, st>>>(pcout, poutws, feat, fws, fail, w_base);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_dense_f16(int B, int N, const float *feat, long long fws, const uint16_t *W, const float *bias,
+                              float *out, long long ows, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  if (fws % 4 || ((uintptr_t)feat & 15) || ((uintptr_t)W & 15)) return cudaErrorInvalidValue;
+  const int N4 = N & ~3;
+  if (N4)
+    k_dense_f16<<<dim3((N4 + kDnC - 1) / kDnC, (B + kDnW - 1) / kDnW), 256, 0, st>>>(B, N4, feat, fws, W, bias, out,
+                                                                                    ows);
+  cudaError_t e = cudaGetLastError();
+  if (e || N4 == N) return e;
+  k_dense_f16_tail<<<(B * (N - N4) + 127) / 128, 128, 0, st>>>(B, N4, N, feat, fws, W, bias, out, ows);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_dense_f32(int B, int N, const float *feat, long long fws, const float *W, const float *bias,
+                              float *out, long long ows, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  k_dense_f32<<<(B * N + 127) / 128, 128, 0, st>>>(B, N, feat, fws, W, bias, out, ows);
+  return cudaGetLastError();
+}

@@ -457,7 +457,8 @@ extern "C" int bnnk_device_init(void) {
   }
   e = cudaMemcpyToSymbol(g_frecpe_lut, lut, sizeof lut);
   if (e) return e;
-  return bnnk_fp32_tables_init(tab, lut);
+  e = (cudaError_t)bnnk_fp32_tables_init(tab, lut);
+  return e ? e : bnnk_f16_tables_init(tab);
 }
 
 extern "C" int bnnk_quant(int rows, int Mw, const float *x, long long xws, int lda, int K, int Kq, const float *gate,

@@ -49,10 +49,13 @@ static const struct { int mode; const char *name, *precision; } PATHS[] = {
     {BNN_MODE_FP32, "neon-fp32", "fp32"},
 };
 
-/* 1 when every op of path i has a GPU kernel here (the int8 path's ops, variant 0) */
+/* 1 when every op of path i has a GPU kernel here (the neon-int8 path's ops, variant 0, and the neon-fp16 path's,
+ * variant 1) */
 static int path_runs_here(const bnn_pkg *p, int i) {
   static const int codes[] = {BNN_OP_FE_STFT2, BNN_OP_C0POOL, BNN_OP_PW_S8, BNN_OP_DW3, BNN_OP_SE_GATE,
-                              BNN_OP_POSTPC, BNN_OP_GEMV_S8, BNN_OP_PROTO_S8, BNN_OP_FE_LOGMEL};
+                              BNN_OP_POSTPC, BNN_OP_GEMV_S8, BNN_OP_PROTO_S8, BNN_OP_FE_LOGMEL, BNN_OP_DENSE,
+                              BNN_OP_C0POOL_F16, BNN_OP_PW_F16, BNN_OP_DW3_F16, BNN_OP_SE_F16, BNN_OP_POSTPC_F16,
+                              BNN_OP_DENSE_F16};
   const bnn_path_rec *d = &p->paths[i];
   const uint8_t *q = p->map + d->ops_off, *end = q + d->ops_bytes;
   for (uint32_t k = 0; k < d->n_ops; k++) {
@@ -91,8 +94,8 @@ static void no_path_error(const char *path, const bnn_pkg *p, const char *want) 
         "package of this model compiled for %s (%s-%s.bnpk)", path, want, list, want, id[0] ? id : "<model_id>", want);
   else
     ERR(BNN_ERR_CPU, "%s: this GPU library runs none of the package's paths%s%s (it has: %s; B200 kernels exist for the "
-        "neon-int8 path); hint: use the neon-int8 package of this model (%s-neon-int8.bnpk) or compile one with "
-        "--paths neon-int8", path, want[0] ? " named " : "", want, list, id[0] ? id : "<model_id>");
+        "neon-int8 and neon-fp16 paths); hint: use the neon-int8 package of this model (%s-neon-int8.bnpk) or compile "
+        "one with --paths neon-int8", path, want[0] ? " named " : "", want, list, id[0] ? id : "<model_id>");
 }
 
 static void pkg_info(const bnn_pkg *p, int pi, bnn_info *info) {
@@ -348,11 +351,10 @@ static int check_err_word(bnn_ctx *c, int di) {
     const int w = dv->err_host[1];
     dv->err_host[1] = BNNK_NO_FAIL;
     cudaMemsetAsync(dv->err + 1, 0x7f, sizeof(int), (cudaStream_t)dv->stream);
-    int i = 0;
-    while (i < c->n_ops && c->ops[i].code != BNN_OP_PROTO_S8) i++;
+    const int i = bnn_window_fail_op(c);
     ERR(BNN_ERR_WINDOW, "window not scored: op %d %s reported a failed window (code -2: non-finite values on the %s "
         "path) for window %d of the call; hint: skip this window (the input itself is probably non-finite or extreme)",
-        i, i < c->n_ops ? c->ops[i].kname : "?", c->info.path, w);
+        i, i >= 0 ? c->ops[i].kname : "?", c->info.path, w);
     return -2;
   }
   if (*dv->err_host) {

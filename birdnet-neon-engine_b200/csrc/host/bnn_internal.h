@@ -49,6 +49,11 @@ enum {
   BNN_OP_FE_STFT2 = 1, BNN_OP_C0POOL = 2, BNN_OP_PW = 3, BNN_OP_DW3 = 4, BNN_OP_SE = 5, BNN_OP_POSTPC = 6,
   BNN_OP_DENSE = 7, BNN_OP_FE_LOGMEL = 8, BNN_OP_PW_S8 = 22, BNN_OP_GEMV_S8 = 23, BNN_OP_SE_GATE = 25, BNN_OP_PROTO_S8 = 35, BNN_OP_N = 36
 };
+/* the fp16 kernels of the neon-fp16 path: base | variant 1 << 8 (src/rt_pkg.c:320-331, src/rt_ops_f16.c:286-299) */
+enum {
+  BNN_OP_C0POOL_F16 = 0x102, BNN_OP_PW_F16 = 0x103, BNN_OP_DW3_F16 = 0x104, BNN_OP_SE_F16 = 0x105,
+  BNN_OP_POSTPC_F16 = 0x106, BNN_OP_DENSE_F16 = 0x107
+};
 enum { BNN_ACT_NONE = 0, BNN_ACT_SILU = 1, BNN_ACT_RELU = 2 };
 
 /* one decoded op record (pointers into the package) */
@@ -74,6 +79,8 @@ typedef struct {
   /* FE_LOGMEL: the device tables and their allocations */
   bnnk_logmel_tables lm;
   void *lm_mem[8];
+  /* fp16 ops: hw the fp16 weights (GEMMs k-major [Kp][Np], DW3 [9][C], DENSE [N][1024]), hb the fp16 bias */
+  uint16_t *hw, *hb;
 } bnn_devop;
 
 typedef struct {
@@ -88,8 +95,9 @@ typedef struct {
   int8_t *q;            /* int8 GEMM scratch: [batch * rows][kq] */
   float *sa, *fe_minmax, *pcin;
   int32_t *za;
+  uint16_t *g16;        /* SE f16: the fp16 gates [batch][C] */
   int *err;             /* device words: [0] the error word of the bounded waits, [1] the smallest failed window index
-                         * of the call (BNNK_NO_FAIL if none; set by PROTO_S8's logits) */
+                         * of the call (BNNK_NO_FAIL if none; set by PROTO_S8's logits and POSTPC f16's features) */
   int *err_host;        /* pinned copy of both */
   int w_base;           /* index of the launch's first window in the caller's call (failed-window reports) */
   bnnk_fe_tables fe;
@@ -139,6 +147,8 @@ int bnn_rt_launch(bnn_ctx *c, int i, int n, const float *d_pcm, int op0, int op1
 /* the whole op list on n windows, replayed from a CUDA graph when the same (n, d_pcm, w_base) ran before */
 int bnn_rt_run(bnn_ctx *c, int i, int n, const float *d_pcm, void *stream);
 int c0_quantizes_next(const bnn_ctx *c, int i);
+/* the op that reports failed windows (-2) through the failed-window word (PROTO_S8, POSTPC f16), or -1 */
+int bnn_window_fail_op(const bnn_ctx *c);
 void bnn_rt_close(bnn_ctx *c);
 int bnn_s8_weights(bnn_devop *d, int N, int K, int Kp, int Np, const int8_t *src, const float *sw_src,
                    const int32_t *cs_src, const float *b_src, int rows_cap, char *err, size_t errlen, int *kind);

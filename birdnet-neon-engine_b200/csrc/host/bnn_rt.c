@@ -316,8 +316,106 @@ static int init_proto_s8(vctx *v) { /* proto8n_init (src/rt_ops_s8n.c:220-240) a
   return 0;
 }
 
-/* the registry of this library: (base opcode, variant 0) -> kernel; outmask / optmask as the reference's
- * (src/rt_ops_f32.c:620-637, src/rt_ops_s8n.c:255-260) */
+/* ---- the neon-fp16 path (src/rt_ops_f16.c, with the shared checks of src/rt_ops_f32.c) */
+
+/* packed fp16 GEMM weights (hpack_view, src/rt_ops_f16.c:14-27): t = [w (panels), b32, b16], p = [N K Kp Np] at po */
+static int v_hpack(vctx *v, int ti, int po) {
+  const int *p = v->op->p;
+  if (v->op->ni < po + 4)
+    return vbad(v, "GEMM shape [N K Kp Np] expected at int params %d..%d, the op has %d ints", po, po + 3, v->op->ni);
+  const int N = p[po], K = p[po + 1], Kp = p[po + 2], Np = p[po + 3];
+  if (N <= 0 || K <= 0 || Np != R8(N) || Kp < K || Kp % 8)
+    return vbad(v, "GEMM shape N %d K %d Kp %d Np %d: expected Np = N rounded up to 8, Kp >= K, Kp %% 8 == 0", N, K, Kp, Np);
+  return vneed_t(v, ti, (size_t)Np * Kp * 2, 1) || vneed_t(v, ti + 1, ((size_t)Np + 16) * 4, 1) ||
+                 vneed_t(v, ti + 2, ((size_t)Np + 16) * 2, 1)
+             ? -1
+             : 0;
+}
+static int init_c0pool_f16(vctx *v) { /* c0_init, src/rt_ops_f16.c:31-42 */
+  if (vneed_args(v, 2, 3, 4) || v_hpack(v, 0, 0)) return -1;
+  const int *p = v->op->p;
+  VREQ(v, p[0] == 24 && p[1] == 64 && p[2] == 64);
+  return vneed(v, 0, BNN_F32, (size_t)96 * 511 * 2) || vneed(v, 1, BNN_F16, (size_t)48 * 128 * 48) ? -1 : 0;
+}
+static int init_pw_f16(vctx *v) { /* pw_init + rt_pw_check, src/rt_ops_f16.c:54-61, src/rt_ops_f32.c:129-150 */
+  if (vneed_args(v, 3, 3, 11) || v_hpack(v, 0, 0)) return -1;
+  const int *p = v->op->p;
+  const int Kp = p[2], Np = p[3], M = p[4], lda = p[5], act = p[6], ldo = p[7], opad = p[9], ldr = p[10];
+  VREQ(v, M > 0);
+  VREQ(v, lda >= Kp);
+  VREQ(v, ldo >= Np);
+  VREQ(v, act >= 0 && act <= 2);
+  VREQ(v, opad >= 0 && opad <= 3);
+  if (vneed(v, 0, BNN_F16, (size_t)R8(M) * lda) || v_pw_out(v, BNN_F16)) return -1;
+  const bnn_buf_rec *r = vbd(v, 2);
+  if (r) {
+    VREQ(v, ldr >= Np);
+    if (r->halo)
+      return vbad(v, "buffer argument 2 (buffer #%d, residual): halo %u needs an fp32 buffer with ld %d and H x W = %d "
+                  "rows, found %s ld %u %ux%u", v->op->b[2], r->halo, ldr, M, bnn_dtype_name(r->dtype), r->ld, r->H, r->W);
+    if (vneed(v, 2, BNN_F16, (size_t)M * ldr)) return -1;
+  }
+  /* this library's GEMM moves 8 fp16 channels at a time: strides of whole 16-byte groups (every compiled package) */
+  if (lda % 8 || ldo % 8 || (r && ldr % 8))
+    return vbad(v, "channel strides lda %d, ldo %d, ldr %d: the B200 fp16 GEMM needs multiples of 8", lda, ldo, ldr);
+  return 0;
+}
+static int init_dw3_f16(vctx *v) { /* dw3_init + rt_dw3_check, src/rt_ops_f16.c:64-68, src/rt_ops_f32.c:216-230 */
+  if (vneed_args(v, 3, 2, 8)) return -1;
+  const int *p = v->op->p;
+  VREQ(v, p[2] <= 2048);
+  const int H = p[0], W = p[1], C = p[2], s = p[3], Ho = p[4], Wo = p[5], pt = p[6], pl = p[7];
+  VREQ(v, H > 0 && W > 0 && Ho > 0 && Wo > 0 && C > 0);
+  VREQ(v, C % 8 == 0);
+  VREQ(v, s == 1 || s == 2);
+  VREQ(v, pt >= 0 && pt <= 1 && pl >= 0 && pl <= 1);
+  if (vneed_t(v, 0, (size_t)9 * C * 2, 0) || vneed_t(v, 1, (size_t)C * 2, 0)) return -1;
+  VREQ(v, (Ho - 1) * s - pt + 1 + 3 <= H + 2);
+  VREQ(v, (Wo - 1) * s - pl + 1 + 3 <= W + 2);
+  if (vneed_haloed(v, 0, BNN_F16, H, W, C, 1)) return -1;
+  if (vneed(v, 1, BNN_F16, (size_t)Ho * Wo * C) || vneed(v, 2, BNN_F32, (size_t)C)) return -1;
+  if (Ho > 192) return vbad(v, "%d output rows: the B200 fp16 depthwise kernel takes at most 192", Ho);
+  return 0;
+}
+static int init_se_f16(vctx *v) { /* se_init = rt_se_check(F16), src/rt_ops_f16.c:115, src/rt_ops_f32.c:256-266 */
+  if (vneed_args(v, 2, 4, 3)) return -1;
+  const int C = v->op->p[0], rd = v->op->p[1], P = v->op->p[2];
+  VREQ(v, C > 0 && C % 8 == 0 && C <= 4096);
+  VREQ(v, rd > 0 && rd <= 512);
+  VREQ(v, P > 0);
+  const size_t want[4] = {(size_t)rd * C, (size_t)rd, (size_t)rd * C, (size_t)C};
+  for (int i = 0; i < 4; i++)
+    if (vneed_t(v, i, want[i] * 4, 0)) return -1;
+  return vneed(v, 0, BNN_F16, (size_t)P * C) || vneed(v, 1, BNN_F32, (size_t)C) ? -1 : 0;
+}
+static int init_postpc_f16(vctx *v) { /* postpc_init + rt_postpc_check, src/rt_ops_f16.c:136-143, rt_ops_f32.c:329-336 */
+  if (vneed_args(v, 4, 5, 4) || v_hpack(v, 2, 0)) return -1;
+  VREQ(v, v->op->p[0] == 1024 && v->op->p[1] == 1728);
+  if (vneed_t(v, 0, 192 * 4, 1) || vneed_t(v, 1, 192 * 4, 1)) return -1;
+  if (vneed(v, 0, BNN_F16, 24 * 192) || vneed(v, 1, BNN_F32, 1024) || vneed(v, 2, BNN_F16, 8 * 1728) ||
+      vneed(v, 3, BNN_F16, 8 * 1024))
+    return -1;
+  VREQ(v, v->op->p[2] == 1728); /* im2col rows of 1728 (v24k16_postpc): the GEMM's K is the row */
+  return 0;
+}
+static int init_dense(vctx *v, size_t wsize) { /* dense_init, src/rt_ops_f16.c:156-161, src/rt_ops_f32.c:351-356 */
+  if (vneed_args(v, 2, 2, 1)) return -1;
+  const int N = v->op->p[0];
+  VREQ(v, N > 0);
+  if (vneed(v, 0, BNN_F32, 1024) || vneed(v, 1, BNN_F32, (size_t)N)) return -1;
+  if (vneed_t(v, 0, (size_t)N * 1024 * wsize, 0) || vneed_t(v, 1, (size_t)N * 4, 0)) return -1;
+  return 0;
+}
+static int init_dense_f16(vctx *v) {
+  if (init_dense(v, 2)) return -1;
+  if (v->op->p[0] % 4) v->c->launches += 1; /* the scalar tail */
+  return 0;
+}
+static int init_dense_f32(vctx *v) { return init_dense(v, 4); }
+
+/* the registry of this library: opcode (base | variant << 8) -> kernel; outmask / optmask as the reference's
+ * (src/rt_ops_f32.c:620-637, src/rt_ops_s8n.c:255-260, src/rt_ops_f16.c:286-299). Variant 0: the neon-int8 path's
+ * ops (and the fp32 head of small models); variant 1: the neon-fp16 path's. The dotprod variant (2) has none. */
 typedef struct {
   int code;
   const char *name;
@@ -335,9 +433,15 @@ static const kdesc KERNELS[] = {
     {BNN_OP_GEMV_S8, "gemv_s8n", init_gemv_s8, 0x1e, 0, 2},
     {BNN_OP_PROTO_S8, "proto_s8n", init_proto_s8, 0xe, 0, 3},
     {BNN_OP_FE_LOGMEL, "fe_logmel", init_fe_logmel, 0x2, 0, 1},
+    {BNN_OP_DENSE, "dense_f32", init_dense_f32, 0x2, 0, 1},
+    {BNN_OP_C0POOL_F16, "c0pool_f16", init_c0pool_f16, 0x2, 0, 1},
+    {BNN_OP_PW_F16, "pw_f16", init_pw_f16, 0x2, 0x4, 1},
+    {BNN_OP_DW3_F16, "dw3_f16", init_dw3_f16, 0x6, 0, 1},
+    {BNN_OP_SE_F16, "se_f16", init_se_f16, 0x1, 0, 2},
+    {BNN_OP_POSTPC_F16, "postpc_f16", init_postpc_f16, 0xe, 0, 3},
+    {BNN_OP_DENSE_F16, "dense_f16", init_dense_f16, 0x2, 0, 1},
 };
 static const kdesc *kernel_for(int code) {
-  if (code >> 8) return NULL; /* variants 1 and 2 are the fp16 / dotprod CPU paths: no GPU kernels */
   for (size_t i = 0; i < sizeof KERNELS / sizeof KERNELS[0]; i++)
     if (KERNELS[i].code == code) return &KERNELS[i];
   return NULL;
@@ -437,8 +541,9 @@ int bnn_rt_open(bnn_ctx *c, char *err, size_t errlen, int *kind) {
       if (bnn_meta_str(c->pkg, "compiler", comp, sizeof comp) < 0) snprintf(comp, sizeof comp, "unknown");
       *kind = BNN_ERR_CPU;
       return vbad(&v, "opcode 0x%x (base %d variant %d) has no B200 kernel in this library (it runs the neon-int8 ops "
-                  "FE_STFT2, C0POOL, PW_S8, DW3, SE_GATE, POSTPC, GEMV_S8, PROTO_S8 and FE_LOGMEL; the package was "
-                  "written by compiler '%s')",
+                  "FE_STFT2, C0POOL, PW_S8, DW3, SE_GATE, POSTPC, GEMV_S8, PROTO_S8, FE_LOGMEL and DENSE, and the "
+                  "neon-fp16 ops C0POOL, PW, DW3, SE, POSTPC and DENSE of variant 1; the package was written by "
+                  "compiler '%s')",
                   op->code, op->code & 0xff, var, comp);
     }
     op->kname = k->name;
@@ -755,6 +860,24 @@ void bnn_logmel_release(bnn_devop *d) {
   }
 }
 
+/* hp_pack panels (src/gemm_f16.c:17-40: [Np/16][Kp][16], then a [Kp][8] tail panel when Np % 16) as the k-major
+ * [Kp][Np] fp16 matrix of the B200 GEMM, uploaded to d->hw; b16 [Np] to d->hb; b32 [Np] to *b32 unless NULL */
+static int hpack_upload(bnn_devop *d, const uint16_t *panels, const float *b32src, const uint16_t *b16src, int Kp,
+                        int Np, float **b32, char *err, size_t errlen, int *kind) {
+  uint16_t *wt = malloc(sizeof(uint16_t) * (size_t)Kp * Np);
+  if (!wt) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory (fp16 weights, %d x %d)", Kp, Np); return -1; }
+  const int n16 = Np / 16;
+  for (int n = 0; n < Np; n++)
+    for (int k = 0; k < Kp; k++)
+      wt[(size_t)k * Np + n] = n / 16 < n16 ? panels[((size_t)(n / 16) * Kp + k) * 16 + n % 16]
+                                            : panels[(size_t)n16 * Kp * 16 + (size_t)k * 8 + n % 16];
+  int rc = upload((void **)&d->hw, wt, sizeof(uint16_t) * (size_t)Kp * Np, err, errlen, kind);
+  free(wt);
+  if (!rc) rc = upload((void **)&d->hb, b16src, sizeof(uint16_t) * (size_t)Np, err, errlen, kind);
+  if (!rc && b32) rc = upload((void **)b32, b32src, sizeof(float) * (size_t)Np, err, errlen, kind);
+  return rc;
+}
+
 /* the weights of op i in the kernels' layouts */
 static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, int *kind) {
   const bnn_op *op = &c->ops[i];
@@ -808,6 +931,32 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
   case BNN_OP_PROTO_S8:
     return bnn_proto_weights(d, p[0], p[2], p[3], tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 3), tptr(c, op, 4),
                              p[7], ((const float *)tptr(c, op, 5))[0], err, errlen, kind);
+  case BNN_OP_C0POOL_F16: /* t = [w b32 b16]; p = [24 64 64 24] */
+    return hpack_upload(d, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), 64, 24, NULL, err, errlen, kind);
+  case BNN_OP_PW_F16:
+    return hpack_upload(d, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), p[2], p[3], &d->f[0], err, errlen, kind);
+  case BNN_OP_DW3_F16: {
+    const int C = p[2];
+    return upload((void **)&d->hw, tptr(c, op, 0), sizeof(uint16_t) * 9 * C, err, errlen, kind) ||
+           upload((void **)&d->hb, tptr(c, op, 1), sizeof(uint16_t) * C, err, errlen, kind);
+  }
+  case BNN_OP_SE_F16: {
+    const int C = p[0], rd = p[1];
+    return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * rd * C, err, errlen, kind) ||
+           upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * rd, err, errlen, kind) ||
+           upload((void **)&d->f[2], tptr(c, op, 2), sizeof(float) * rd * C, err, errlen, kind) ||
+           upload((void **)&d->f[3], tptr(c, op, 3), sizeof(float) * C, err, errlen, kind);
+  }
+  case BNN_OP_POSTPC_F16: /* t = [post_s post_b w b32 b16] */
+    return hpack_upload(d, tptr(c, op, 2), tptr(c, op, 3), tptr(c, op, 4), 1728, 1024, &d->f[1], err, errlen, kind) ||
+           upload((void **)&d->f[2], tptr(c, op, 0), sizeof(float) * 192, err, errlen, kind) ||
+           upload((void **)&d->f[3], tptr(c, op, 1), sizeof(float) * 192, err, errlen, kind);
+  case BNN_OP_DENSE_F16:
+    return upload((void **)&d->hw, tptr(c, op, 0), sizeof(uint16_t) * 1024 * (size_t)p[0], err, errlen, kind) ||
+           upload((void **)&d->f[0], tptr(c, op, 1), sizeof(float) * (size_t)p[0], err, errlen, kind);
+  case BNN_OP_DENSE:
+    return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * 1024 * (size_t)p[0], err, errlen, kind) ||
+           upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * (size_t)p[0], err, errlen, kind);
   default:
     return 0;
   }
@@ -889,6 +1038,10 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
   CK(cudaMalloc((void **)&dv->za, sizeof(int32_t) * rows), "int8 zero-point scratch");
   CK(cudaMalloc((void **)&dv->fe_minmax, sizeof(float) * 2 * B), "front-end scratch");
   CK(cudaMalloc((void **)&dv->pcin, sizeof(float) * 6 * 1728 * B), "post-conv scratch");
+  size_t gate_elems = 8;
+  for (int i = 0; i < c->n_ops; i++)
+    if (c->ops[i].code == BNN_OP_SE_F16 && (size_t)B * c->ops[i].p[0] > gate_elems) gate_elems = (size_t)B * c->ops[i].p[0];
+  CK(cudaMalloc((void **)&dv->g16, sizeof(uint16_t) * gate_elems), "SE gate scratch");
   CK(cudaMalloc((void **)&dv->err, 2 * sizeof(int)), "error word");
   CK(cudaMemset(dv->err, 0, sizeof(int)), "error word");
   CK(cudaMemset(dv->err + 1, 0x7f, sizeof(int)), "error word");
@@ -933,6 +1086,7 @@ void bnn_rt_device_free(bnn_ctx *c, int di) {
       bnn_devop *o = &dv->ops[i];
       cudaFree(o->w); cudaFree(o->sw); cudaFree(o->bias); cudaFree(o->cs);
       for (int k = 0; k < 6; k++) cudaFree(o->f[k]);
+      cudaFree(o->hw); cudaFree(o->hb);
       bnn_logmel_release(o);
     }
   for (int k = 0; k < dv->n_fe_mem; k++) cudaFree(dv->fe_mem[k]);
@@ -945,6 +1099,7 @@ void bnn_rt_device_free(bnn_ctx *c, int di) {
     for (uint32_t i = 0; i < c->path->n_buf; i++) cudaFree(dv->priv[i]);
   cudaFree(dv->arena);
   cudaFree(dv->q); cudaFree(dv->sa); cudaFree(dv->za); cudaFree(dv->fe_minmax); cudaFree(dv->pcin); cudaFree(dv->err);
+  cudaFree(dv->g16);
   if (dv->err_host) cudaFreeHost(dv->err_host);
   cudaFree(dv->up[0]); cudaFree(dv->up[1]);
   for (int k = 0; k < 2; k++) {
@@ -1057,6 +1212,33 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
         rc = bnnk_proto_logits(n, p[7], p[8], B_(3), WS(3), o->f[1], o->f[2], B_(1), WS(1), NULL, dv->err + 1,
                                dv->w_base, st);
       break;
+    case BNN_OP_C0POOL_F16:
+      rc = bnnk_c0pool_f16(n, IN_(0), INWS(0), o->hw, o->hb, B_(1), WS(1), st);
+      break;
+    case BNN_OP_PW_F16: {
+      const int M = p[4];
+      rc = bnnk_gemm_f16(n * M, M, B_(0), WS(0), p[5], o->hw, p[2], p[3], o->hb, o->f[0], p[6], B_(1), WS(1), p[7],
+                         p[8], p[9], B_(2), WS(2), p[10], st);
+      break;
+    }
+    case BNN_OP_DW3_F16:
+      rc = bnnk_dw3_f16(n, B_(0), WS(0), p[0], p[1], p[2], p[3], p[6], p[7], o->hw, o->hb, B_(1), WS(1), p[4], p[5],
+                        B_(2), WS(2), st);
+      break;
+    case BNN_OP_SE_F16:
+      rc = bnnk_se_f16(n, p[0], p[1], o->f[0], o->f[1], o->f[2], o->f[3], B_(1), WS(1), p[2], B_(0), WS(0), dv->g16,
+                       st);
+      break;
+    case BNN_OP_POSTPC_F16:
+      rc = bnnk_postpc_f16(n, B_(0), WS(0), o->f[2], o->f[3], o->hw, o->hb, o->f[1], B_(2), WS(2), B_(3), WS(3), B_(1),
+                           WS(1), dv->err + 1, dv->w_base, st);
+      break;
+    case BNN_OP_DENSE_F16:
+      rc = bnnk_dense_f16(n, p[0], B_(0), WS(0), o->hw, o->f[0], B_(1), WS(1), st);
+      break;
+    case BNN_OP_DENSE:
+      rc = bnnk_dense_f32(n, p[0], B_(0), WS(0), o->f[0], o->f[1], B_(1), WS(1), st);
+      break;
     default:
       rc = cudaErrorNotSupported;
     }
@@ -1075,14 +1257,15 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
 
 /* Whole launch sequences as CUDA graphs. A 16-window sequence costs 1.4 ms against 5.2 ms for 256 windows: most of
  * it is the host side of 101 kernel launches, which a graph replays in one call. The graph bakes in every pointer,
- * grid and parameter of the sequence, so it is keyed by the window count, the input buffer and (for packages with a
- * prototype head, whose logits kernel reports failed windows relative to the call) the first window of the chunk.
+ * grid and parameter of the sequence, so it is keyed by the window count, the input buffer and (for packages with an
+ * op that reports failed windows relative to the call: a prototype head, the fp16 post conv) the first window of the
+ * chunk.
  * The first run of a key is eager (it also sets the kernels' shared-memory attributes outside any capture); the
  * second is captured on the context's own stream, thread-locally, then launched on the caller's stream. */
-static int has_proto(const bnn_ctx *c) {
+int bnn_window_fail_op(const bnn_ctx *c) {
   for (int i = 0; i < c->n_ops; i++)
-    if (c->ops[i].code == BNN_OP_PROTO_S8) return 1;
-  return 0;
+    if (c->ops[i].code == BNN_OP_PROTO_S8 || c->ops[i].code == BNN_OP_POSTPC_F16) return i;
+  return -1;
 }
 
 int bnn_rt_run(bnn_ctx *c, int di, int n, const float *d_pcm, void *stream) {
@@ -1093,7 +1276,7 @@ int bnn_rt_run(bnn_ctx *c, int di, int n, const float *d_pcm, void *stream) {
     env = !(e && atoi(e) == 0);
   }
   if (!env || dv->graphs_off || dv->prof_on) return bnn_rt_launch(c, di, n, d_pcm, 0, c->n_ops, stream);
-  const int wb = has_proto(c) ? dv->w_base : 0;
+  const int wb = bnn_window_fail_op(c) >= 0 ? dv->w_base : 0;
   int k = 0;
   while (k < dv->n_graphs && !(dv->graphs[k].n == n && dv->graphs[k].in == d_pcm && dv->graphs[k].w_base == wb)) k++;
   if (k == dv->n_graphs) {

@@ -225,3 +225,44 @@ def test_f16_oracle_runs_the_fp32_head(tmp_path):
     assert p.op_code(p.n_ops - 1) == 7
     out, emb = p.run(synth.audio(1, seed=4)[0])
     assert out.shape == (61,) and np.isfinite(out).all() and np.isfinite(emb).all()
+
+
+# ------------------------------------------------------------------ the library's loader on the fp16 path
+
+def test_f16_path_selection_and_validation(tmp_path, f16_mini):
+    """Mode 4 names a path the package does not have; the fp16 records are checked as rt_ops_f16.c checks them (the
+    same messages), before any device is touched."""
+    from conftest import gpu_visible  # pylint: disable=import-outside-toplevel
+    from bnneon_b200 import BnnError, Model  # pylint: disable=import-outside-toplevel
+    import struct  # pylint: disable=import-outside-toplevel
+    from bnneon_b200 import pkgread  # pylint: disable=import-outside-toplevel
+    with pytest.raises(BnnError) as e:
+        Model(f16_mini, mode=4)
+    assert e.value.kind == "CPU" and "path neon-int8 is not in this package" in str(e.value)
+    if not gpu_visible():
+        with pytest.raises(BnnError) as e:
+            Model(f16_mini, mode=3)
+        assert e.value.kind == "CPU" and "no CUDA device" in str(e.value)
+    ops, _ = pkgread.read_ops(f16_mini, synth.PATH_F16)
+    offs = pkgread.op_offsets(f16_mini, synth.PATH_F16)
+    with open(f16_mini, "rb") as f:
+        data = f.read()
+    first = {code: i for i, (code, _, _, _) in reversed(list(enumerate(ops)))}
+    cases = [(0x103, 5, 16, "lda >= Kp", "pw_f16"), (0x103, 6, 3, "act >= 0 && act <= 2", "pw_f16"),
+             (0x104, 6, 2, "pt >= 0 && pt <= 1 && pl >= 0 && pl <= 1", "dw3_f16"),
+             (0x104, 2, 4096, "p[2] <= 2048", "dw3_f16"),
+             (0x105, 0, 12, "C > 0 && C % 8 == 0 && C <= 4096", "se_f16"),
+             (0x102, 0, 16, "GEMM shape N 16 K 64 Kp 64 Np 24", "c0pool_f16"),
+             (0x106, 0, 512, "GEMM shape N 512", "postpc_f16"),
+             (0x107, 0, 0, "N > 0", "dense_f16")]
+    for code, k, val, text, kname in cases:
+        i = first[code]
+        _, _, nb, nt, _, _ = struct.unpack_from("<6H", data, offs[i])
+        at = offs[i] + 12 + 4 * (nb + nt + k)
+        d = bytearray(data)
+        d[at:at + 4] = struct.pack("<i", val)
+        p = tmp_path / f"c{code:x}_{k}.bnpk"
+        p.write_bytes(bytes(d))
+        with pytest.raises(BnnError) as e:
+            Model(str(p), mode=3)
+        assert e.value.kind == "PACKAGE" and text in str(e.value) and f"op {i} {kname}" in str(e.value), str(e.value)
