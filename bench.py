@@ -390,6 +390,114 @@ def logmel_perch(h, torch, stream, hbm_peak, cpu=True, batch=512):
             "cpu_baseline": base}
 
 
+def hfma2_peak(h, torch, stream):
+    """The fp16 FMA pipe's throughput measured here (bnn_cuda_peak_hfma2: 148 x 8 CTAs of 256 threads, 8 independent
+    fma.rn.f16x2 chains each), TFLOP/s: the roofline of the neon-fp16 path's CUDA-core kernels."""
+    word = torch.zeros(4, dtype=torch.int32, device="cuda")
+    blocks, iters, sp = 148 * 8, 20000, stream.cuda_stream
+    for _ in range(2):
+        assert h.bnn_cuda_peak_hfma2(blocks, iters, word.data_ptr(), sp) == 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(5):
+        h.bnn_cuda_peak_hfma2(blocks, iters, word.data_ptr(), sp)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / 5
+    return 2.0 * blocks * 256 * iters * 16 / (ms * 1e-3) / 1e12
+
+
+def v24_fp16_c3(torch, stream, batch=1024, steps=10, cpu=True):
+    """the v2.4-architecture neon-fp16 package (the reference compiler's bytes for the same synthetic IR)
+    on `batch` windows: device-resident windows/s (bnn_infer_device, CUDA events over `steps` steps after 3
+    warm-ups), end to end through bnn_infer_batch with pinned host buffers, the per-op-class device time, and the
+    fp16 GEMMs' FLOP/s against the measured fp16 FMA pipe peak. Every kernel is bit-exact against the oracle (the
+    reference's fp16 FMA chains on CUDA cores; the tensor cores cannot reproduce them)."""
+    from bnneon_b200 import Model, pkgread, synth  # pylint: disable=import-outside-toplevel
+    td = tempfile.mkdtemp()
+    pkg = os.path.join(td, "v24_full_f16.bnpk")
+    synth.make_package(pkg, seed=0, path=synth.PATH_F16)
+    pcm = synth.audio(batch, seed=4000)
+    m = Model(pkg, mode=3, batch=batch)
+    try:
+        nc, ne = m.info.n_classes, m.info.emb_dim
+        d_pcm = torch.from_numpy(pcm).cuda()
+        d_out = torch.empty((batch, nc), dtype=torch.float32, device="cuda")
+        d_emb = torch.empty((batch, ne), dtype=torch.float32, device="cuda")
+        sp = stream.cuda_stream
+
+        def run():
+            m.infer_device(batch, d_pcm.data_ptr(), d_out.data_ptr(), d_emb.data_ptr(), sp)
+        for _ in range(3):
+            run()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            run()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        # end to end
+        h_pcm = torch.from_numpy(pcm).pin_memory()
+        h_out = torch.empty((batch, nc), dtype=torch.float32).pin_memory()
+        h_emb = torch.empty((batch, ne), dtype=torch.float32).pin_memory()
+        m.infer_batch(h_pcm.numpy(), h_out.numpy(), h_emb.numpy())
+        t0 = time.perf_counter()
+        for _ in range(3):
+            m.infer_batch(h_pcm.numpy(), h_out.numpy(), h_emb.numpy())
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / 3
+        # per-op classes
+        ops, _ = pkgread.read_ops(pkg, synth.PATH_F16)
+        m.h.bnn_profile_begin(m.ctx)
+        for _ in range(2):
+            run()
+            m.h.bnn_profile_collect(m.ctx)
+        m.h.bnn_profile_end(m.ctx)
+        cls = {}
+        for i, (code, _, _, p) in enumerate(ops):
+            c = cls.setdefault(pkgread.NAMES.get(code, str(code)).lower(), {"ms": 0.0, "flop": 0.0, "ops": 0})
+            c["ms"] += m.h.bnn_profile_op_ms(m.ctx, i) / 2
+            c["ops"] += 1
+            if code == 0x103:
+                c["flop"] += 2.0 * batch * p[4] * p[2] * p[3]
+        launches = m.launches_per_batch
+    finally:
+        m.close()
+    peak = hfma2_peak(m.h, torch, stream)
+    pw = cls["pw_f16"]
+    tflops = pw["flop"] / (pw["ms"] * 1e-3) / 1e12
+    base = None
+    if cpu:
+        from oracle import oracle  # pylint: disable=import-outside-toplevel
+        cores = os.cpu_count() or 1
+        n = min(batch, cores)
+        t0 = time.perf_counter()
+        oracle.run_many(pkg, pcm[:n], threads=cores, path_name=synth.PATH_F16)
+        dt = time.perf_counter() - t0
+        base = {"value": round(n / dt, 3), "unit": "windows/s", "cores": cores, "kind": "port",
+                "sample": f"{n} windows, one per thread: oracle/liboracle.so (the C restatement of the reference's "
+                          f"neon-fp16 path, every fp16 operation emulated exactly in software), {dt:.1f} s"}
+    total = sum(v["ms"] for v in cls.values())
+    return {"workload": "BirdNET-v2.4-architecture neon-fp16 package (config 3): 144000-sample windows, fp16 "
+                        "activations and weights, 6522-class fp16 head",
+            "batch": batch, "ms_per_step": round(ms, 3), "windows_per_s": round(batch / (ms * 1e-3), 1),
+            "e2e": {"value": round(batch / (e2e_ms * 1e-3), 1), "unit": "windows/s",
+                    "h2d_bytes_per_step": batch * 144000 * 4, "d2h_bytes_per_step": batch * (nc + ne) * 4,
+                    "path": "bnn_infer_batch (C ABI), pinned host buffers, wall clock"},
+            "gpu_launches_per_step": launches,
+            "roofline": {"bound": "fp16 FMA pipe (CUDA cores)", "kernel": f"pw_f16 ({pw['ops']} GEMMs per step)",
+                         "achieved": round(tflops, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                         "frac": round(tflops / peak, 4),
+                         "peak_source": "measured here: bnn_cuda_peak_hfma2 (fma.rn.f16x2 chains on every SM)",
+                         "note": "achieved = 2 M K N of the 1x1 convs (Kp, Np as packed) / their CUDA-event time"},
+            "ops": {k: {"ms": round(v["ms"], 4), "share": round(v["ms"] / total, 4), "ops": v["ops"]}
+                    for k, v in sorted(cls.items(), key=lambda kv: -kv[1]["ms"])},
+            "parity": "bit-exact against the oracle (tests/test_gpu_f16.py); the oracle within 50 dB SQNR of a "
+                      "float64 model (tests/test_f16_cpu.py)",
+            "cpu_baseline": base}
+
+
 def load_peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json"), encoding="utf-8") as f:
@@ -545,7 +653,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-summary", metavar="CSV",
                     help="write profiles/launch_list_v24_int8_b256.md from an ncu launch-list CSV (no GPU needed)")
-    ap.add_argument("--no-proto", action="store_true", help="skip the prototype-head (C4 int8 head) line")
+    ap.add_argument("--no-proto", action="store_true",
+                    help="skip the secondary lines (C4 int8 head, Perch log-mel front end, C3 fp16 package)")
     ap.add_argument("--proto-ncu", type=int, metavar="B", default=0,
                     help="for profiler captures: the prototype head on B windows, 3 warm-ups + 1 run, no timing")
     ap.add_argument("--logmel-ncu", type=int, metavar="B", default=0,
@@ -727,6 +836,8 @@ def main():
              if rank == 0 and not args.no_proto else None)
     logmel = (logmel_perch(m.h, torch, stream, load_peaks()[0], cpu=not args.no_cpu_baseline and world == 1)
               if rank == 0 and not args.no_proto else None)
+    fp16 = (v24_fp16_c3(torch, stream, cpu=not args.no_cpu_baseline and world == 1)
+            if rank == 0 and not args.no_proto else None)
 
     line = None
     if rank == 0:
@@ -744,7 +855,7 @@ def main():
                             "note": "int8 ops of PW_S8 + GEMV_S8 (quantizer + tcgen05 GEMM) per second; these GEMMs "
                                     "are HBM-bound (AI far below the int8 ridge)"},
                 "ops": ops_summary, "clocks": clocks, "s8_gemm_c1": c1, "proto_s8_c4": proto,
-                "fe_logmel_perch": logmel}
+                "fe_logmel_perch": logmel, "v24_fp16_c3": fp16}
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(pkg, pcm)
     m.close()

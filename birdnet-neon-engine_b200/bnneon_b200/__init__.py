@@ -69,6 +69,7 @@ SIGNATURES = {
     "bnn_profile_collect": (_I, [_P]),
     "bnn_profile_op_ms": (ctypes.c_double, [_P, _I]),
     "bnn_profile_end": (_I, [_P]),
+    "bnn_cuda_peak_hfma2": (_I, [_I, _I, _P, _P]),
     "bnn_debug_n_ops": (_I, [_P]),
     "bnn_debug_op_code": (_I, [_P, _I]),
     "bnn_debug_run_ops": (_I, [_P, _I, _P, _I, _I]),

@@ -173,10 +173,12 @@ int bnnk_test_fn(int fn, int n, const float *x, float *y, bnn_stream_t st);
  * elements. Every fp16 operation is the reference's, in its order (src/gemm_f16.c, src/kern_f16.c, src/v24_fast.c). */
 /* the glibc expf table of k_f16.cu's SE gate (per device, once) */
 int bnnk_f16_tables_init(const unsigned long long *tab);
-/* PW f16 / any hp_pack GEMM: rows r = w * Mw + m of A (window stride aws, row stride lda); W [Kp][Np] k-major;
+/* PW f16 / any hp_pack GEMM: rows r = w * Mw + m of A (window stride aws, row stride lda); Wd [Kp][Np] k-major, each
+ * weight duplicated into both halves of a 32-bit word;
  * K blocks of <= 128 (fp16 chains, fp32 flushes), bias b16 / b32, act (0 none, 1 SiLU, 2 ReLU), + residual, stored
- * at the padded row (ow, opad). Strides and Kp, Np multiples of 8, pointers 16-byte aligned. */
-int bnnk_gemm_f16(int rows, int Mw, const uint16_t *A, long long aws, int lda, const uint16_t *W, int Kp, int Np,
+ * at the padded row (ow, opad). Kp, Np, lda and aws multiples of 8, ldo / ldr and their window strides of 4; A and Wd
+ * 16-byte aligned, out and res 8. */
+int bnnk_gemm_f16(int rows, int Mw, const uint16_t *A, long long aws, int lda, const uint32_t *Wd, int Kp, int Np,
                   const uint16_t *b16, const float *b32, int act, uint16_t *out, long long ows, int ldo, int ow,
                   int opad, const uint16_t *res, long long rws, int ldr, bnn_stream_t st);
 /* C0POOL f16: img [B][96][511][2] fp32 -> pin [B][48 * 128][48] fp16; W [64][24] k-major, b16 [24] */
@@ -191,12 +193,14 @@ int bnnk_se_f16(int B, int C, int rd, const float *w1, const float *b1, const fl
                 const float *chsum, long long cws, int P, uint16_t *D, long long dws, uint16_t *g16, bnn_stream_t st);
 /* POSTPC f16: X [B][24][192] -> pcin [B][6][1728] -> pcout [B][6][1024] -> feat [B][1024]; a window whose features
  * are not finite sets fail (atomic minimum of w_base + window) */
-int bnnk_postpc_f16(int B, const uint16_t *X, long long xws, const float *ps, const float *pb, const uint16_t *W,
+int bnnk_postpc_f16(int B, const uint16_t *X, long long xws, const float *ps, const float *pb, const uint32_t *W,
                     const uint16_t *b16, const float *b32, uint16_t *pcin, long long pinws, uint16_t *pcout,
                     long long poutws, float *feat, long long fws, int *fail, int w_base, bnn_stream_t st);
 /* DENSE f16 (v24k16_head): feat [B][1024] fp32, W [N][1024] fp16, bias [N] -> out [B][N] */
 int bnnk_dense_f16(int B, int N, const float *feat, long long fws, const uint16_t *W, const float *bias, float *out,
                    long long ows, bnn_stream_t st);
+/* the fp16 FMA pipe's peak for the roofline: blocks x 256 threads x iters x 16 fp16 FMAs (out: one word, kept live) */
+int bnnk_peak_hfma2(int blocks, int iters, uint32_t *out, bnn_stream_t st);
 /* DENSE variant 0 (v24k32_head): W [N][1024] fp32 */
 int bnnk_dense_f32(int B, int N, const float *feat, long long fws, const float *W, const float *bias, float *out,
                    long long ows, bnn_stream_t st);

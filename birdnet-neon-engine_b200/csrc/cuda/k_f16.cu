@@ -16,6 +16,7 @@
 
 #include "bnn_kernels.h"
 #include "emu.cuh"
+#include "tc.cuh"
 
 namespace bnn {
 
@@ -94,18 +95,42 @@ __device__ __forceinline__ void load_silu_tab(uint32_t *tab01, uint32_t *tab2) {
 // fp16, else the bias is an fp16 add (b16). Epilogue: SiLU (table) or FMAX(x, 0), then the fp16 residual add, stored
 // at the pixel's padded row.
 //
-// CTA tile: BM = 8 RT rows x BN = 8 NT channels (NT threads across the channels, RT across the rows); each thread
-// holds 8 rows x 8 channels as 32 fp16 pairs, a pair being two ROWS of one channel, so that an FMA takes the rows'
-// activations as they lie in the transposed shared tile and the channel's weight duplicated into both lanes. Shared
-// memory per stage of kGS k-steps: At [kGS][BM] fp16 (the activations transposed), Wd [kGS][BN] u32 (the weights,
-// duplicated). Per k a thread issues 3 16-byte shared loads for 32 fp16x2 FMAs.
+// CTA tile: BM = 8 RT rows x BN = TN NT channels (NT threads across the channels, RT across the rows); each thread
+// holds 8 rows x TN channels (TN = 4 or 8) as 4 TN fp16 pairs, a pair being two ROWS of one channel, so that an FMA
+// takes the rows' activations as they lie in the transposed shared tile and the channel's weight duplicated into both
+// lanes (the weights are uploaded duplicated, [Kp][Np] words). Per k a thread issues 1 + TN / 4 16-byte shared loads
+// for 4 TN fp16x2 FMAs, which occupy the FMA pipe twice as many cycles (fp16x2 issues at half rate).
+//
+// The CTAs are persistent, as many as fit on the GPU at once: CTA b takes tiles b, b + grid, ... of the (M tile,
+// channel tile) space, channel tile fastest (neighbouring CTAs share the activation rows); a tile is ceil(Kp / kGS) stages of
+// kGS k-steps, and the (tile, stage) steps run as one pipeline over two shared-memory buffers: while step j is
+// computed, step j + 1's weights arrive by cp.async and its activations are loaded into registers, then stored
+// transposed into the other buffer; one barrier per step.
 constexpr int kGS = 32;
+
+// n / d for 0 <= n < 2^31 and 1 <= d < 2^31 by a multiply-high and a shift (Granlund and Montgomery, "Division by
+// invariant integers using multiplication", 1994): with l = ceil(log2 d), mul = ceil(2^(31 + l) / d) < 2^32 and
+// n / d = (n mul) >> (31 + l), exact because n (mul - 2^(31 + l) / d) / 2^(31 + l) < 2^-l <= 1 / d; d = 1 is mul = 0
+struct FastDiv {
+  uint32_t d, mul, shr;
+};
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) { return f.mul ? __umulhi(n, f.mul) >> f.shr : n; }
+static FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f = {d, 0u, 0u};
+  if (d > 1) {
+    uint32_t l = 0;
+    while ((1u << l) < d) l++;
+    f.mul = (uint32_t)(((1ull << (31 + l)) + d - 1) / d);
+    f.shr = l - 1;  // the multiply-high already divides by 2^32
+  }
+  return f;
+}
 
 struct GemmF16Args {
   const uint16_t *A;
   long long aws;
-  int lda, Mw, rows;
-  const uint16_t *W;  // [Kp][Np]
+  int lda, Mw, rows, n_mtiles;
+  const uint32_t *Wd;  // [Kp][Np], each weight in both halves
   int Kp, Np, bs;
   const uint16_t *b16;
   const float *b32;
@@ -117,76 +142,118 @@ struct GemmF16Args {
   long long rws;
   int ldr;
   int NT, RT;
+  int ntn;               // channel tiles: the CTAs take the tiles (M tile, channel tile) in M-major order
+  FastDiv mw, owd, ntd;  // rows per window, padded output width, channel tiles
 };
 
-template <bool kFlush>
-__global__ void __launch_bounds__(256, 1) k_gemm_f16(const GemmF16Args g) {
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gmem), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// kA: activation chunks (16 bytes) per thread per stage, >= ceil(32 / NT); TN: channels per thread
+template <bool kFlush, int kA, int TN>
+__global__ void __launch_bounds__(256, TN == 8 ? 2 : kA > 4 ? 2 : 4) k_gemm_f16(const GemmF16Args g) {
   extern __shared__ __align__(16) uint8_t sm[];
-  const int NT = g.NT, RT = g.RT, BM = 8 * RT, BN = 8 * NT;
-  uint16_t *At = reinterpret_cast<uint16_t *>(sm);
-  uint32_t *Wd = reinterpret_cast<uint32_t *>(sm + (size_t)kGS * BM * 2);
-  uint32_t *tab01 = Wd + (size_t)kGS * BN, *tab2 = tab01 + 16;
-  const int tid = threadIdx.x, nthr = NT * RT;
-  const int tn = tid % NT, tr = tid / NT;
-  const long long m0 = (long long)blockIdx.x * BM;
-  const int n0 = blockIdx.y * BN;
+  const int NT = g.NT, RT = g.RT, BM = 8 * RT, BN = TN * NT, nthr = NT * RT;
+  uint16_t *At = reinterpret_cast<uint16_t *>(sm);                                    // [2][kGS][BM]
+  uint32_t *Ws = reinterpret_cast<uint32_t *>(sm + (size_t)2 * kGS * BM * 2);         // [2][kGS][BN]
+  uint32_t *tab01 = Ws + (size_t)2 * kGS * BN, *tab2 = tab01 + 16;
+  float *fbs = reinterpret_cast<float *>(tab2 + 16);  // kFlush: the 8 TN fp32 block sums of each thread, [8 TN][nthr]
+  const int tid = threadIdx.x, tn = tid % NT, tr = tid / NT;
+  const int nst = (g.Kp + kGS - 1) / kGS;
+  const int mine = (g.n_mtiles * g.ntn - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int nsteps = mine * nst;
   load_silu_tab(tab01, tab2);
 
-  uint32_t acc[4][8];
-  float2 fb[4][8];
+  // this thread's activation chunks of a stage: chunk i is (row ml[i], 8 k-steps c[i]) of the tile
+  int cml[kA], cc[kA];
+#pragma unroll
+  for (int i = 0; i < kA; i++) {
+    const int idx = tid + i * nthr;
+    cml[i] = idx % BM;
+    cc[i] = idx / BM;
+  }
+  uint4 pa[kA];
+  // issue step j's loads: weights by cp.async into buffer j & 1, activations into registers
+  auto issue = [&](int j) {
+    const int tf = blockIdx.x + (j / nst) * gridDim.x, ks = (j % nst) * kGS;
+    const int t = (int)fdiv((uint32_t)tf, g.ntd), n0 = (tf - t * g.ntn) * BN;
+    const int kn = min(kGS, g.Kp - ks), kc = kn / 8;
+    uint32_t *W = Ws + (size_t)(j & 1) * kGS * BN;
+#pragma unroll
+    for (int h = 0; h < TN / 4; h++) {
+      const int n = n0 + TN * tn + 4 * h;
+      const uint32_t *src = g.Wd + (size_t)ks * g.Np + (n < g.Np ? n : 0);
+      for (int kk = tr; kk < kn; kk += RT)
+        cp_async16(W + (size_t)kk * BN + TN * tn + 4 * h, src + (size_t)kk * g.Np, n < g.Np);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < kA; i++) {
+      pa[i] = make_uint4(0u, 0u, 0u, 0u);
+      const int r = t * BM + cml[i];
+      if (cc[i] < kc && r < g.rows) {
+        const int w = (int)fdiv((uint32_t)r, g.mw), m = r - w * g.Mw;
+        pa[i] = __ldg(reinterpret_cast<const uint4 *>(g.A + (size_t)w * g.aws + (size_t)m * g.lda + ks + 8 * cc[i]));
+      }
+    }
+  };
+  // store the registers of step j transposed into buffer j & 1 (a warp: 32 consecutive rows of one chunk column)
+  auto store = [&](int j) {
+    const int ks = (j % nst) * kGS, kc = min(kGS, g.Kp - ks) / 8;
+    uint16_t *A = At + (size_t)(j & 1) * kGS * BM;
+#pragma unroll
+    for (int i = 0; i < kA; i++) {
+      if (cc[i] < kc) {
+        uint16_t *d = A + (size_t)(8 * cc[i]) * BM + cml[i];
+        const uint32_t vv[4] = {pa[i].x, pa[i].y, pa[i].z, pa[i].w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          d[(2 * q) * BM] = (uint16_t)(vv[q] & 0xffffu);
+          d[(2 * q + 1) * BM] = (uint16_t)(vv[q] >> 16);
+        }
+      }
+    }
+  };
+
+  uint32_t acc[4][TN];
 #pragma unroll
   for (int i = 0; i < 4; i++)
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-      acc[i][j] = 0u;
-      fb[i][j] = make_float2(0.f, 0.f);
-    }
+    for (int q = 0; q < TN; q++) acc[i][q] = 0u;
+  if (kFlush)
+    for (int e = 0; e < 8 * TN; e++) fbs[e * nthr + tid] = 0.f;
 
-  for (int ks = 0; ks < g.Kp; ks += kGS) {
-    const int kn = min(kGS, g.Kp - ks), kc = kn / 8;
-    __syncthreads();
-    // activations: 16-byte chunks (row, 8 k-steps); a warp covers 32 consecutive rows of one chunk column, so that
-    // the transposed stores of each of the 8 halves are 32 consecutive shared halves
-    for (int idx = tid; idx < BM * kc; idx += nthr) {
-      const int ml = idx % BM, c = idx / BM;
-      const long long r = m0 + ml;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (r < g.rows) {
-        const long long w = r / g.Mw, m = r - w * g.Mw;
-        v = __ldg(reinterpret_cast<const uint4 *>(g.A + w * g.aws + m * g.lda + ks + 8 * c));
-      }
-      uint16_t *d = At + (size_t)(8 * c) * BM + ml;
-      const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        d[(2 * j) * BM] = (uint16_t)(vv[j] & 0xffffu);
-        d[(2 * j + 1) * BM] = (uint16_t)(vv[j] >> 16);
-      }
-    }
-    // weights: 8 channels of one k-step per chunk, duplicated into both lanes of a word
-    for (int idx = tid; idx < kn * NT; idx += nthr) {
-      const int kk = idx / NT, c8 = idx % NT, n = n0 + 8 * c8;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (n < g.Np) v = __ldg(reinterpret_cast<const uint4 *>(g.W + (size_t)(ks + kk) * g.Np + n));
-      uint4 *d = reinterpret_cast<uint4 *>(Wd + (size_t)kk * BN + 8 * c8);
-      d[0] = make_uint4(__byte_perm(v.x, 0, 0x1010), __byte_perm(v.x, 0, 0x3232), __byte_perm(v.y, 0, 0x1010),
-                        __byte_perm(v.y, 0, 0x3232));
-      d[1] = make_uint4(__byte_perm(v.z, 0, 0x1010), __byte_perm(v.z, 0, 0x3232), __byte_perm(v.w, 0, 0x1010),
-                        __byte_perm(v.w, 0, 0x3232));
-    }
-    __syncthreads();
+  if (nsteps > 0) {
+    issue(0);
+    store(0);
+    cp_async_wait_all();
+  }
+  __syncthreads();
+  for (int j = 0; j < nsteps; j++) {
+    if (j + 1 < nsteps) issue(j + 1);
+    const int tf = blockIdx.x + (j / nst) * gridDim.x, st = j % nst, ks = st * kGS;
+    const int t = (int)fdiv((uint32_t)tf, g.ntd), n0 = (tf - t * g.ntn) * BN;
+    const int kn = min(kGS, g.Kp - ks);
+    const uint16_t *A = At + (size_t)(j & 1) * kGS * BM;
+    const uint32_t *W = Ws + (size_t)(j & 1) * kGS * BN;
     for (int kk = 0; kk < kn; kk += 8) {
 #pragma unroll
       for (int u = 0; u < 8; u++) {
-        const uint4 a = *reinterpret_cast<const uint4 *>(At + (size_t)(kk + u) * BM + tr * 8);
-        const uint4 w0 = *reinterpret_cast<const uint4 *>(Wd + (size_t)(kk + u) * BN + tn * 8);
-        const uint4 w1 = *reinterpret_cast<const uint4 *>(Wd + (size_t)(kk + u) * BN + tn * 8 + 4);
+        const uint4 a = *reinterpret_cast<const uint4 *>(A + (size_t)(kk + u) * BM + tr * 8);
+        uint32_t wv[TN];
+#pragma unroll
+        for (int h = 0; h < TN / 4; h++) {
+          const uint4 w = *reinterpret_cast<const uint4 *>(W + (size_t)(kk + u) * BN + tn * TN + 4 * h);
+          wv[4 * h] = w.x; wv[4 * h + 1] = w.y; wv[4 * h + 2] = w.z; wv[4 * h + 3] = w.w;
+        }
         const uint32_t av[4] = {a.x, a.y, a.z, a.w};
-        const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
-          for (int j = 0; j < 8; j++) acc[i][j] = hfma2(av[i], wv[j], acc[i][j]);
+          for (int q = 0; q < TN; q++) acc[i][q] = hfma2(av[i], wv[q], acc[i][q]);
       }
       if (kFlush) {
         const int kg = ks + kk + 8;
@@ -194,53 +261,82 @@ __global__ void __launch_bounds__(256, 1) k_gemm_f16(const GemmF16Args g) {
 #pragma unroll
           for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-              fb[i][j].x = __fadd_rn(fb[i][j].x, h_lo(acc[i][j]));
-              fb[i][j].y = __fadd_rn(fb[i][j].y, h_hi(acc[i][j]));
-              acc[i][j] = 0u;
+            for (int q = 0; q < TN; q++) {
+              float *f = fbs + (size_t)((i * TN + q) * 2) * nthr + tid;
+              f[0] = __fadd_rn(f[0], h_lo(acc[i][q]));
+              f[nthr] = __fadd_rn(f[nthr], h_hi(acc[i][q]));
+              acc[i][q] = 0u;
             }
         }
       }
     }
-  }
-
-  // epilogue
-  const int nb = n0 + tn * 8;
-  if (nb >= g.Np) return;
-  uint32_t bias16[4];
-  float bias32[8];
-  {
-    const uint4 b = __ldg(reinterpret_cast<const uint4 *>(g.b16 + nb));
-    bias16[0] = b.x; bias16[1] = b.y; bias16[2] = b.z; bias16[3] = b.w;
+    if (st == nst - 1) {  // the tile's epilogue
+      const int nb = n0 + tn * TN;
+      if (nb < g.Np) {
+        uint32_t bias16[TN / 2];
+        float bias32[TN];
 #pragma unroll
-    for (int j = 0; j < 8; j++) bias32[j] = __ldg(g.b32 + nb + j);
-  }
-#pragma unroll
-  for (int i = 0; i < 4; i++)
-#pragma unroll
-    for (int l = 0; l < 2; l++) {
-      const long long r = m0 + tr * 8 + 2 * i + l;
-      if (r >= g.rows) continue;
-      const long long w = r / g.Mw, m = r - w * g.Mw;
-      uint32_t v[4];
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        if (kFlush) {
-          const float x0 = l ? fb[i][2 * q].y : fb[i][2 * q].x, x1 = l ? fb[i][2 * q + 1].y : fb[i][2 * q + 1].x;
-          v[q] = pack2(f2h(__fadd_rn(x0, bias32[2 * q])), f2h(__fadd_rn(x1, bias32[2 * q + 1])));
-        } else {
-          v[q] = hadd2(__byte_perm(acc[i][2 * q], acc[i][2 * q + 1], l ? 0x7632 : 0x5410), bias16[q]);
+        for (int h = 0; h < TN / 4; h++) {
+          const uint2 b = __ldg(reinterpret_cast<const uint2 *>(g.b16 + nb + 4 * h));
+          const float4 b32 = __ldg(reinterpret_cast<const float4 *>(g.b32 + nb + 4 * h));
+          bias16[2 * h] = b.x; bias16[2 * h + 1] = b.y;
+          bias32[4 * h] = b32.x; bias32[4 * h + 1] = b32.y; bias32[4 * h + 2] = b32.z; bias32[4 * h + 3] = b32.w;
         }
-        if (g.act == 1) v[q] = silu2(v[q], tab01, tab2);
-        else if (g.act == 2) v[q] = relu2(v[q]);
+        int r = t * BM + tr * 8;
+        int w = (int)fdiv((uint32_t)r, g.mw), m = r - w * g.Mw;  // the row's window and pixel, advanced row by row
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+          for (int l = 0; l < 2; l++) {
+            if (r < g.rows) {
+              uint32_t v[TN / 2];
+#pragma unroll
+              for (int q = 0; q < TN / 2; q++) {
+                if (kFlush) {
+                  const float x0 = fbs[(size_t)((i * TN + 2 * q) * 2 + l) * nthr + tid],
+                              x1 = fbs[(size_t)((i * TN + 2 * q + 1) * 2 + l) * nthr + tid];
+                  v[q] = pack2(f2h(__fadd_rn(x0, bias32[2 * q])), f2h(__fadd_rn(x1, bias32[2 * q + 1])));
+                } else {
+                  v[q] = hadd2(__byte_perm(acc[i][2 * q], acc[i][2 * q + 1], l ? 0x7632 : 0x5410), bias16[q]);
+                }
+                if (g.act == 1) v[q] = silu2(v[q], tab01, tab2);
+                else if (g.act == 2) v[q] = relu2(v[q]);
+              }
+              if (g.res) {
+#pragma unroll
+                for (int h = 0; h < TN / 4; h++) {
+                  const uint2 rv = __ldg(
+                      reinterpret_cast<const uint2 *>(g.res + (size_t)w * g.rws + (size_t)m * g.ldr + nb + 4 * h));
+                  v[2 * h] = hadd2(v[2 * h], rv.x);
+                  v[2 * h + 1] = hadd2(v[2 * h + 1], rv.y);
+                }
+              }
+              int orow = m;
+              if (g.opad) {
+                const int y = (int)fdiv((uint32_t)m, g.owd);
+                orow = (y + g.opad) * (g.ow + 2 * g.opad) + (m - y * g.ow) + g.opad;
+              }
+              uint16_t *o = g.out + (size_t)w * g.ows + (size_t)orow * g.ldo + nb;
+              if (TN == 8) *reinterpret_cast<uint4 *>(o) = make_uint4(v[0], v[1], v[2 % (TN / 2)], v[3 % (TN / 2)]);
+              else *reinterpret_cast<uint2 *>(o) = make_uint2(v[0], v[1]);
+            }
+            r++;
+            if (++m == g.Mw) { m = 0; w++; }
+          }
       }
-      if (g.res) {
-        const uint4 rv = __ldg(reinterpret_cast<const uint4 *>(g.res + w * g.rws + m * g.ldr + nb));
-        v[0] = hadd2(v[0], rv.x); v[1] = hadd2(v[1], rv.y); v[2] = hadd2(v[2], rv.z); v[3] = hadd2(v[3], rv.w);
-      }
-      const long long orow = g.opad ? (m / g.ow + g.opad) * (g.ow + 2 * g.opad) + m % g.ow + g.opad : m;
-      *reinterpret_cast<uint4 *>(g.out + w * g.ows + orow * g.ldo + nb) = make_uint4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int q = 0; q < TN; q++) acc[i][q] = 0u;
+      if (kFlush)
+        for (int e = 0; e < 8 * TN; e++) fbs[e * nthr + tid] = 0.f;
     }
+    if (j + 1 < nsteps) {
+      store(j + 1);
+      cp_async_wait_all();
+    }
+    __syncthreads();
+  }
 }
 
 // ------------------------------------------------------------------ C0POOL f16 (src/v24_fast.c:150-164)
@@ -612,6 +708,22 @@ __global__ void k_dense_f32(int B, int N, const float *__restrict__ feat, long l
   out[(long long)w * ows + o] = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])), bias[o]);
 }
 
+// The fp16 FMA pipe's throughput, for the roofline of the kernels above: every thread runs 8 independent
+// fma.rn.f16x2 chains for iters rounds (16 fp16 FMAs per thread per round); out keeps the chains live.
+__global__ void __launch_bounds__(256) k_peak_hfma2(int iters, uint32_t seed, uint32_t *out) {
+  uint32_t a[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) a[j] = 0x3c003c00u ^ (seed + j + threadIdx.x);
+  const uint32_t m = 0x3bff3bffu, c = 0x1c001c00u;  // x * (1 - 2^-11) + 2^-8: stays finite
+  for (int i = 0; i < iters; i++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) a[j] = hfma2(a[j], m, c);
+  uint32_t r = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) r ^= a[j];
+  if (r == 0x12345678u) out[0] = r;
+}
+
 }  // namespace bnn
 
 using namespace bnn;
@@ -628,42 +740,59 @@ static void kblocks(int Kp, int *nblk, int *bs) {
   *bs = ((Kp + *nblk - 1) / *nblk + 7) & ~7;
 }
 
-// the channel tile: all of Np up to 128, else the widest multiple of 8 up to 128 that divides Np (else 128)
+// the channel tile: all of Np up to 128 (at least 16), else the widest multiple of 8 up to 128 that divides Np (else
+// 128); columns past Np are zero-filled and not stored
 static int gemm_bn(int Np) {
-  if (Np <= 128) return Np;
+  if (Np <= 128) return Np < 16 ? 16 : Np;
   for (int bn = 128; bn >= 64; bn -= 8)
     if (Np % bn == 0) return bn;
   return 128;
 }
 
-extern "C" int bnnk_gemm_f16(int rows, int Mw, const uint16_t *A, long long aws, int lda, const uint16_t *W, int Kp,
+extern "C" int bnnk_gemm_f16(int rows, int Mw, const uint16_t *A, long long aws, int lda, const uint32_t *Wd, int Kp,
                              int Np, const uint16_t *b16, const float *b32, int act, uint16_t *out, long long ows,
                              int ldo, int ow, int opad, const uint16_t *res, long long rws, int ldr, bnn_stream_t st) {
   if (rows <= 0) return 0;
-  if (Kp % 8 || Np % 8 || lda % 8 || aws % 8 || ldo % 8 || ows % 8 || (res && (ldr % 8 || rws % 8)) ||
-      ((uintptr_t)A & 15) || ((uintptr_t)W & 15) || ((uintptr_t)out & 15) || (res && ((uintptr_t)res & 15)))
+  if (Kp % 8 || Np % 8 || lda % 8 || aws % 8 || ldo % 4 || ows % 4 || (res && (ldr % 4 || rws % 4)) ||
+      ((uintptr_t)A & 15) || ((uintptr_t)Wd & 15) || ((uintptr_t)out & 7) || (res && ((uintptr_t)res & 7)) ||
+      ((uintptr_t)b32 & 15) || ((uintptr_t)b16 & 7))
     return cudaErrorInvalidValue;
   int nblk, bs;
   kblocks(Kp, &nblk, &bs);
   GemmF16Args g;
   g.A = A; g.aws = aws; g.lda = lda; g.Mw = Mw; g.rows = rows;
-  g.W = W; g.Kp = Kp; g.Np = Np; g.bs = bs; g.b16 = b16; g.b32 = b32; g.act = act;
+  g.Wd = Wd; g.Kp = Kp; g.Np = Np; g.bs = bs; g.b16 = b16; g.b32 = b32; g.act = act;
   g.out = out; g.ows = ows; g.ldo = ldo; g.ow = ow; g.opad = opad; g.res = res; g.rws = rws; g.ldr = ldr;
-  const int BN = gemm_bn(Np);
-  g.NT = BN / 8;
+  g.mw = make_fastdiv((uint32_t)Mw);
+  g.owd = make_fastdiv((uint32_t)(ow > 0 ? ow : 1));
+  // the channel tile and the channels per thread: 8 when the tile has at least 64 channels, else 4
+  const int BN = gemm_bn(Np), TN = BN >= 64 && BN % 8 == 0 ? 8 : 4;
+  g.NT = BN / TN;
   g.RT = 256 / g.NT < 32 ? 256 / g.NT : 32;
-  const int BM = 8 * g.RT;
-  const size_t smem = (size_t)kGS * BM * 2 + (size_t)kGS * BN * 4 + 32 * 4;
-  const dim3 grid((unsigned)((rows + BM - 1) / BM), (unsigned)((Np + BN - 1) / BN));
-  cudaError_t e;
-  if (nblk > 1) {
-    e = cudaFuncSetAttribute(k_gemm_f16<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (!e) k_gemm_f16<true><<<grid, g.NT * g.RT, smem, st>>>(g);
-  } else {
-    e = cudaFuncSetAttribute(k_gemm_f16<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (!e) k_gemm_f16<false><<<grid, g.NT * g.RT, smem, st>>>(g);
-  }
-  return e ? e : cudaGetLastError();
+  const int BM = 8 * g.RT, threads = g.NT * g.RT;
+  const int ka = (32 + g.NT - 1) / g.NT;  // activation chunks per thread per stage (NT >= 4: at most 8)
+  g.n_mtiles = (int)((rows + BM - 1) / BM);
+  const int ntn = (Np + BN - 1) / BN;
+  const size_t smem = (size_t)2 * kGS * BM * 2 + (size_t)2 * kGS * BN * 4 + 32 * 4 +
+                      (nblk > 1 ? sizeof(float) * 8 * TN * (size_t)threads : 0);
+  void (*kern)(GemmF16Args);
+  if (TN == 8)
+    kern = nblk > 1 ? (ka <= 2 ? k_gemm_f16<true, 2, 8> : ka <= 4 ? k_gemm_f16<true, 4, 8> : k_gemm_f16<true, 8, 8>)
+                    : (ka <= 2 ? k_gemm_f16<false, 2, 8> : ka <= 4 ? k_gemm_f16<false, 4, 8> : k_gemm_f16<false, 8, 8>);
+  else
+    kern = nblk > 1 ? (ka <= 2 ? k_gemm_f16<true, 2, 4> : ka <= 4 ? k_gemm_f16<true, 4, 4> : k_gemm_f16<true, 8, 4>)
+                    : (ka <= 2 ? k_gemm_f16<false, 2, 4> : ka <= 4 ? k_gemm_f16<false, 4, 4> : k_gemm_f16<false, 8, 4>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int per_sm = 0;
+  if (!e) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+  if (e) return e;
+  g.ntn = ntn;
+  g.ntd = make_fastdiv((uint32_t)ntn);
+  const long long tiles = (long long)g.n_mtiles * ntn;
+  long long gx = (long long)(per_sm > 0 ? per_sm : 1) * num_sms();  // resident CTAs only: none waits for a slot
+  if (gx > tiles) gx = tiles;
+  kern<<<(unsigned)gx, threads, smem, st>>>(g);
+  return cudaGetLastError();
 }
 
 extern "C" int bnnk_c0pool_f16(int B, const float *img, long long iws, const uint16_t *W, const uint16_t *b16,
@@ -707,7 +836,7 @@ extern "C" int bnnk_se_f16(int B, int C, int rd, const float *w1, const float *b
 }
 
 extern "C" int bnnk_postpc_f16(int B, const uint16_t *X, long long xws, const float *ps, const float *pb,
-                               const uint16_t *W, const uint16_t *b16, const float *b32, uint16_t *pcin,
+                               const uint32_t *W, const uint16_t *b16, const float *b32, uint16_t *pcin,
                                long long pinws, uint16_t *pcout, long long poutws, float *feat, long long fws,
                                int *fail, int w_base, bnn_stream_t st) {
   if (B <= 0) return 0;
@@ -732,6 +861,11 @@ extern "C" int bnnk_dense_f16(int B, int N, const float *feat, long long fws, co
   cudaError_t e = cudaGetLastError();
   if (e || N4 == N) return e;
   k_dense_f16_tail<<<(B * (N - N4) + 127) / 128, 128, 0, st>>>(B, N4, N, feat, fws, W, bias, out, ows);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_peak_hfma2(int blocks, int iters, uint32_t *out, bnn_stream_t st) {
+  k_peak_hfma2<<<blocks, 256, 0, st>>>(iters, 0x9e37u, out);
   return cudaGetLastError();
 }
 

@@ -1051,6 +1051,14 @@ int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, i
                                              op_err_word(), (bnn_stream_t)stream));
 }
 
+int bnn_cuda_peak_hfma2(int blocks, int iters, void *d_word, void *stream) {
+  if (blocks <= 0 || iters <= 0 || !d_word) {
+    ERR(BNN_ERR_USAGE, "bnn_cuda_peak_hfma2: blocks %d iters %d word %p", blocks, iters, d_word);
+    return -1;
+  }
+  return launch_rc("bnn_cuda_peak_hfma2", bnnk_peak_hfma2(blocks, iters, d_word, (bnn_stream_t)stream));
+}
+
 int bnn_cuda_fn(int fn, int n, const float *d_x, float *d_y, void *stream) {
   if (fn < 0 || fn > 8 || n < 0) { ERR(BNN_ERR_USAGE, "bnn_cuda_fn: fn %d n %d", fn, n); return -1; }
   return launch_rc("bnn_cuda_fn", bnnk_test_fn(fn, n, d_x, d_y, (bnn_stream_t)stream));

@@ -79,8 +79,10 @@ typedef struct {
   /* FE_LOGMEL: the device tables and their allocations */
   bnnk_logmel_tables lm;
   void *lm_mem[8];
-  /* fp16 ops: hw the fp16 weights (GEMMs k-major [Kp][Np], DW3 [9][C], DENSE [N][1024]), hb the fp16 bias */
+  /* fp16 ops: hw the fp16 weights (C0POOL k-major [64][24], DW3 [9][C], DENSE [N][1024]), hwd the GEMM weights
+   * k-major [Kp][Np] with each weight in both halves of a word, hb the fp16 bias */
   uint16_t *hw, *hb;
+  uint32_t *hwd;
 } bnn_devop;
 
 typedef struct {

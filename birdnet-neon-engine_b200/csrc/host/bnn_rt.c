@@ -355,9 +355,10 @@ static int init_pw_f16(vctx *v) { /* pw_init + rt_pw_check, src/rt_ops_f16.c:54-
                   "rows, found %s ld %u %ux%u", v->op->b[2], r->halo, ldr, M, bnn_dtype_name(r->dtype), r->ld, r->H, r->W);
     if (vneed(v, 2, BNN_F16, (size_t)M * ldr)) return -1;
   }
-  /* this library's GEMM moves 8 fp16 channels at a time: strides of whole 16-byte groups (every compiled package) */
-  if (lda % 8 || ldo % 8 || (r && ldr % 8))
-    return vbad(v, "channel strides lda %d, ldo %d, ldr %d: the B200 fp16 GEMM needs multiples of 8", lda, ldo, ldr);
+  /* this library's GEMM reads 8 fp16 channels and writes 4 at a time (every compiled package's strides qualify) */
+  if (lda % 8 || ldo % 4 || (r && ldr % 4))
+    return vbad(v, "channel strides lda %d, ldo %d, ldr %d: the B200 fp16 GEMM needs lda a multiple of 8 and ldo, ldr "
+                "multiples of 4", lda, ldo, ldr);
   return 0;
 }
 static int init_dw3_f16(vctx *v) { /* dw3_init + rt_dw3_check, src/rt_ops_f16.c:64-68, src/rt_ops_f32.c:216-230 */
@@ -861,17 +862,22 @@ void bnn_logmel_release(bnn_devop *d) {
 }
 
 /* hp_pack panels (src/gemm_f16.c:17-40: [Np/16][Kp][16], then a [Kp][8] tail panel when Np % 16) as the k-major
- * [Kp][Np] fp16 matrix of the B200 GEMM, uploaded to d->hw; b16 [Np] to d->hb; b32 [Np] to *b32 unless NULL */
-static int hpack_upload(bnn_devop *d, const uint16_t *panels, const float *b32src, const uint16_t *b16src, int Kp,
-                        int Np, float **b32, char *err, size_t errlen, int *kind) {
-  uint16_t *wt = malloc(sizeof(uint16_t) * (size_t)Kp * Np);
+ * [Kp][Np] matrix of the B200 fp16 GEMM, each weight in both halves of a 32-bit word (dup != 0, to d->hwd) or plain
+ * fp16 (to d->hw); b16 [Np] to d->hb; b32 [Np] to *b32 unless NULL */
+static int hpack_upload(bnn_devop *d, int dup, const uint16_t *panels, const float *b32src, const uint16_t *b16src,
+                        int Kp, int Np, float **b32, char *err, size_t errlen, int *kind) {
+  const size_t es = dup ? 4 : 2;
+  uint8_t *wt = malloc(es * (size_t)Kp * Np);
   if (!wt) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory (fp16 weights, %d x %d)", Kp, Np); return -1; }
   const int n16 = Np / 16;
   for (int n = 0; n < Np; n++)
-    for (int k = 0; k < Kp; k++)
-      wt[(size_t)k * Np + n] = n / 16 < n16 ? panels[((size_t)(n / 16) * Kp + k) * 16 + n % 16]
-                                            : panels[(size_t)n16 * Kp * 16 + (size_t)k * 8 + n % 16];
-  int rc = upload((void **)&d->hw, wt, sizeof(uint16_t) * (size_t)Kp * Np, err, errlen, kind);
+    for (int k = 0; k < Kp; k++) {
+      const uint16_t h = n / 16 < n16 ? panels[((size_t)(n / 16) * Kp + k) * 16 + n % 16]
+                                      : panels[(size_t)n16 * Kp * 16 + (size_t)k * 8 + n % 16];
+      if (dup) ((uint32_t *)wt)[(size_t)k * Np + n] = (uint32_t)h | ((uint32_t)h << 16);
+      else ((uint16_t *)wt)[(size_t)k * Np + n] = h;
+    }
+  int rc = upload(dup ? (void **)&d->hwd : (void **)&d->hw, wt, es * (size_t)Kp * Np, err, errlen, kind);
   free(wt);
   if (!rc) rc = upload((void **)&d->hb, b16src, sizeof(uint16_t) * (size_t)Np, err, errlen, kind);
   if (!rc && b32) rc = upload((void **)b32, b32src, sizeof(float) * (size_t)Np, err, errlen, kind);
@@ -932,9 +938,9 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
     return bnn_proto_weights(d, p[0], p[2], p[3], tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 3), tptr(c, op, 4),
                              p[7], ((const float *)tptr(c, op, 5))[0], err, errlen, kind);
   case BNN_OP_C0POOL_F16: /* t = [w b32 b16]; p = [24 64 64 24] */
-    return hpack_upload(d, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), 64, 24, NULL, err, errlen, kind);
+    return hpack_upload(d, 0, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), 64, 24, NULL, err, errlen, kind);
   case BNN_OP_PW_F16:
-    return hpack_upload(d, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), p[2], p[3], &d->f[0], err, errlen, kind);
+    return hpack_upload(d, 1, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), p[2], p[3], &d->f[0], err, errlen, kind);
   case BNN_OP_DW3_F16: {
     const int C = p[2];
     return upload((void **)&d->hw, tptr(c, op, 0), sizeof(uint16_t) * 9 * C, err, errlen, kind) ||
@@ -948,7 +954,7 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
            upload((void **)&d->f[3], tptr(c, op, 3), sizeof(float) * C, err, errlen, kind);
   }
   case BNN_OP_POSTPC_F16: /* t = [post_s post_b w b32 b16] */
-    return hpack_upload(d, tptr(c, op, 2), tptr(c, op, 3), tptr(c, op, 4), 1728, 1024, &d->f[1], err, errlen, kind) ||
+    return hpack_upload(d, 1, tptr(c, op, 2), tptr(c, op, 3), tptr(c, op, 4), 1728, 1024, &d->f[1], err, errlen, kind) ||
            upload((void **)&d->f[2], tptr(c, op, 0), sizeof(float) * 192, err, errlen, kind) ||
            upload((void **)&d->f[3], tptr(c, op, 1), sizeof(float) * 192, err, errlen, kind);
   case BNN_OP_DENSE_F16:
@@ -1086,7 +1092,7 @@ void bnn_rt_device_free(bnn_ctx *c, int di) {
       bnn_devop *o = &dv->ops[i];
       cudaFree(o->w); cudaFree(o->sw); cudaFree(o->bias); cudaFree(o->cs);
       for (int k = 0; k < 6; k++) cudaFree(o->f[k]);
-      cudaFree(o->hw); cudaFree(o->hb);
+      cudaFree(o->hw); cudaFree(o->hb); cudaFree(o->hwd);
       bnn_logmel_release(o);
     }
   for (int k = 0; k < dv->n_fe_mem; k++) cudaFree(dv->fe_mem[k]);
@@ -1217,7 +1223,7 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
       break;
     case BNN_OP_PW_F16: {
       const int M = p[4];
-      rc = bnnk_gemm_f16(n * M, M, B_(0), WS(0), p[5], o->hw, p[2], p[3], o->hb, o->f[0], p[6], B_(1), WS(1), p[7],
+      rc = bnnk_gemm_f16(n * M, M, B_(0), WS(0), p[5], o->hwd, p[2], p[3], o->hb, o->f[0], p[6], B_(1), WS(1), p[7],
                          p[8], p[9], B_(2), WS(2), p[10], st);
       break;
     }
@@ -1230,7 +1236,7 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
                        st);
       break;
     case BNN_OP_POSTPC_F16:
-      rc = bnnk_postpc_f16(n, B_(0), WS(0), o->f[2], o->f[3], o->hw, o->hb, o->f[1], B_(2), WS(2), B_(3), WS(3), B_(1),
+      rc = bnnk_postpc_f16(n, B_(0), WS(0), o->f[2], o->f[3], o->hwd, o->hb, o->f[1], B_(2), WS(2), B_(3), WS(3), B_(1),
                            WS(1), dv->err + 1, dv->w_base, st);
       break;
     case BNN_OP_DENSE_F16:

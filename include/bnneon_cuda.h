@@ -164,6 +164,10 @@ int bnn_cuda_op_error(void);
  * 8 fma(x, 1.7f, 0.3f) on paired fp32 lanes */
 int bnn_cuda_fn(int fn, int n, const float *d_x, float *d_y, void *stream);
 
+/* the fp16 FMA pipe's throughput, for a roofline: blocks x 256 threads each run iters x 16 fp16 FMAs (8 chains of
+ * fma.rn.f16x2); d_word: one device word the result is kept live in. Time it with events on the stream. */
+int bnn_cuda_peak_hfma2(int blocks, int iters, void *d_word, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
