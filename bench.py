@@ -659,6 +659,8 @@ def main():
                     help="for profiler captures: the prototype head on B windows, 3 warm-ups + 1 run, no timing")
     ap.add_argument("--logmel-ncu", type=int, metavar="B", default=0,
                     help="for profiler captures: the Perch-like log-mel front end on B windows, 3 warm-ups + 1 run")
+    ap.add_argument("--f16-ncu", type=int, metavar="B", default=0,
+                    help="for profiler captures: the v2.4 neon-fp16 package on B windows, 3 warm-ups + 1 step")
     ap.add_argument("--ncu", action="store_true",
                     help="for profiler captures: warm-up steps + one step through bnn_infer_device, no timing, no JSON")
     args = ap.parse_args()
@@ -672,7 +674,7 @@ def main():
     if args.impl == "reference":
         reference_arm(args, rank)
         return
-    if args.ncu or args.proto_ncu or args.logmel_ncu:
+    if args.ncu or args.proto_ncu or args.logmel_ncu or args.f16_ncu:
         # profiler captures use eager launches: a run that replays the op list from CUDA graphs stopped with a driver
         # LaunchFailed under ncu (the same command exits 0 without ncu)
         os.environ["BNN_GRAPHS"] = "0"
@@ -702,6 +704,21 @@ def main():
         torch.cuda.synchronize()
         h.bnn_logmel_free(op)
         print(f"logmel ncu mode: 4 runs of {B} windows", flush=True)
+        return
+    if args.f16_ncu:  # the fp16 package alone, for a profiler; nothing is timed or printed as a result
+        B = args.f16_ncu
+        td = tempfile.mkdtemp()
+        pkg = os.path.join(td, "v24_full_f16.bnpk")
+        synth.make_package(pkg, seed=0, path=synth.PATH_F16)
+        m = Model(pkg, mode=3, batch=B)
+        d_pcm = torch.from_numpy(synth.audio(B, seed=4000)).cuda()
+        d_out = torch.empty((B, m.info.n_classes), dtype=torch.float32, device="cuda")
+        d_emb = torch.empty((B, m.info.emb_dim), dtype=torch.float32, device="cuda")
+        for _ in range(4):
+            m.infer_device(B, d_pcm.data_ptr(), d_out.data_ptr(), d_emb.data_ptr(), None)
+        torch.cuda.synchronize()
+        print(f"f16 ncu mode: 4 steps of {m.launches_per_batch} launches on {B} windows", flush=True)
+        m.close()
         return
     if args.proto_ncu:  # the prototype head alone, for a profiler; nothing is timed or printed as a result
         from bnneon_b200 import load_library  # pylint: disable=import-outside-toplevel
