@@ -2,8 +2,9 @@
  * launch sequence of one batch.
  *
  * Replaces src/rt_pkg.c:168-542 (executor, arena, registry) and the inits / runs of the registry kernels the v2.4
- * neon-int8 package uses (src/rt_ops_f32.c FE_STFT2 / C0POOL / DW3 / SE_GATE / POSTPC, src/rt_ops_s8n.c PW_S8 /
- * GEMV_S8). The validation is the reference's: the same records are accepted and refused with the same messages
+ * neon-int8 package uses (src/rt_ops_f32.c FE_STFT2 / C0POOL / DW3 / SE_GATE / POSTPC / DENSE, src/rt_ops_s8n.c
+ * PW_S8 / GEMV_S8 / PROTO_S8, FE_LOGMEL) and the v2.4 neon-fp16 package uses (src/rt_ops_f16.c C0POOL / PW / DW3 / SE
+ * / POSTPC / DENSE). The validation is the reference's: the same records are accepted and refused with the same messages
  * (op index, kernel, source node, expected and found values, hint), so a package that loads on the reference loads
  * here and a bad one fails the same way.
  *
