@@ -144,6 +144,7 @@ struct GemmF16Args {
   int NT, RT;
   int ntn;               // channel tiles: the CTAs take the tiles (M tile, channel tile) in M-major order
   FastDiv mw, owd, ntd;  // rows per window, padded output width, channel tiles
+  int st16;  // the output rows are 16-byte aligned (out, ldo and ows): 8-channel groups store in one instruction
 };
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
@@ -317,8 +318,13 @@ __global__ void __launch_bounds__(256, TN == 8 ? 2 : kA > 4 ? 2 : 4) k_gemm_f16(
                 orow = (y + g.opad) * (g.ow + 2 * g.opad) + (m - y * g.ow) + g.opad;
               }
               uint16_t *o = g.out + (size_t)w * g.ows + (size_t)orow * g.ldo + nb;
-              if (TN == 8) *reinterpret_cast<uint4 *>(o) = make_uint4(v[0], v[1], v[2 % (TN / 2)], v[3 % (TN / 2)]);
-              else *reinterpret_cast<uint2 *>(o) = make_uint2(v[0], v[1]);
+              if (TN == 8 && g.st16) {  // 16-byte rows: one store
+                *reinterpret_cast<uint4 *>(o) = make_uint4(v[0], v[1], v[2 % (TN / 2)], v[3 % (TN / 2)]);
+              } else {  // 8-byte aligned rows
+#pragma unroll
+                for (int h = 0; h < TN / 4; h++)
+                  *reinterpret_cast<uint2 *>(o + 4 * h) = make_uint2(v[2 * h], v[2 * h + 1]);
+              }
             }
             r++;
             if (++m == g.Mw) { m = 0; w++; }
@@ -763,6 +769,7 @@ extern "C" int bnnk_gemm_f16(int rows, int Mw, const uint16_t *A, long long aws,
   g.A = A; g.aws = aws; g.lda = lda; g.Mw = Mw; g.rows = rows;
   g.Wd = Wd; g.Kp = Kp; g.Np = Np; g.bs = bs; g.b16 = b16; g.b32 = b32; g.act = act;
   g.out = out; g.ows = ows; g.ldo = ldo; g.ow = ow; g.opad = opad; g.res = res; g.rws = rws; g.ldr = ldr;
+  g.st16 = ((uintptr_t)out & 15) == 0 && ldo % 8 == 0 && ows % 8 == 0;
   g.mw = make_fastdiv((uint32_t)Mw);
   g.owd = make_fastdiv((uint32_t)(ow > 0 ? ow : 1));
   // the channel tile and the channels per thread: 8 when the tile has at least 64 channels, else 4

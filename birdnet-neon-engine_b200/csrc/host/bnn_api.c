@@ -1039,6 +1039,58 @@ void bnn_proto_s8_free(bnn_proto_s8 *o) {
   free(o);
 }
 
+/* ------------------------------------------------------------------ PW f16 */
+
+struct bnn_pw_f16 {
+  bnn_devop op;
+  int N, K, Kp, Np;
+};
+
+bnn_pw_f16 *bnn_pw_f16_new(int N, int K, int Kp, int Np, const uint16_t *panels, const float *b32,
+                           const uint16_t *b16) {
+  if (N <= 0 || K <= 0 || Np != ((N + 7) & ~7) || Kp < K || Kp % 8 || !panels || !b32 || !b16) {
+    ERR(BNN_ERR_USAGE, "bnn_pw_f16_new: N %d K %d Kp %d Np %d (expected Np = N rounded up to 8, Kp >= K, Kp %% 8 == 0)",
+        N, K, Kp, Np);
+    return NULL;
+  }
+  bnn_pw_f16 *o = calloc(1, sizeof *o);
+  if (!o) { ERR(BNN_ERR_OOM, "out of memory"); return NULL; }
+  o->N = N; o->K = K; o->Kp = Kp; o->Np = Np;
+  char err[512];
+  int kind = BNN_ERR_CPU;
+  if (bnn_hpack_weights(&o->op, 1, panels, b32, b16, Kp, Np, &o->op.f[0], err, sizeof err, &kind)) {
+    ERR(kind, "bnn_pw_f16_new: %s", err);
+    bnn_pw_f16_free(o);
+    return NULL;
+  }
+  return o;
+}
+
+int bnn_pw_f16_run(bnn_pw_f16 *o, int B, int Mw, const void *d_x, long long xws, int lda, int act, void *d_out,
+                   long long ows, int ldo, int ow, int opad, const void *d_res, long long rws, int ldr, void *stream) {
+  if (!o || B < 0 || Mw < 1 || (long long)B * Mw >= (1ll << 31) || !d_x || !d_out || lda < o->Kp || lda % 8 ||
+      xws % 8 || ldo < o->Np || ldo % 4 || ows % 4 || act < 0 || act > 2 || opad < 0 ||
+      (opad && (ow <= 0 || Mw % ow)) || (d_res && (ldr < o->Np || ldr % 4 || rws % 4)) || ((uintptr_t)d_x & 15) ||
+      ((uintptr_t)d_out & 7) || ((uintptr_t)d_res & 7)) {
+    ERR(BNN_ERR_USAGE, "bnn_pw_f16_run: B %d Mw %d lda %d (>= Kp %d, a multiple of 8) xws %lld ldo %d (>= Np %d, a "
+        "multiple of 4) act %d ow %d opad %d ldr %d, or a misaligned pointer", B, Mw, lda, o ? o->Kp : 0, xws, ldo,
+        o ? o->Np : 0, act, ow, opad, ldr);
+    return -1;
+  }
+  if (B == 0) return 0;
+  return launch_rc("bnn_pw_f16_run", bnnk_gemm_f16(B * Mw, Mw, d_x, xws, lda, o->op.hwd, o->Kp, o->Np, o->op.hb,
+                                                   o->op.f[0], act, d_out, ows, ldo, ow, opad, d_res, rws, ldr,
+                                                   (bnn_stream_t)stream));
+}
+
+void bnn_pw_f16_free(bnn_pw_f16 *o) {
+  if (!o) return;
+  cudaFree(o->op.hwd);
+  cudaFree(o->op.hb);
+  cudaFree(o->op.f[0]);
+  free(o);
+}
+
 int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, int s, const float *d_w, const float *d_b,
                  float *d_out, long long ows, int Ho, int Wo, float *d_chsum, long long cws, void *stream) {
   if (B < 0 || H <= 0 || W <= 0 || C <= 0 || C % 8 || (s != 1 && s != 2) || Ho <= 0 || Wo <= 0 ||

@@ -159,6 +159,10 @@ int bnn_proto_weights(bnn_devop *d, int N, int Kp, int Np, const int8_t *src, co
 int bnn_proto_weights_l(bnn_devop *d, int layout, int N, int K, int Kq, int Np, const int8_t *src, const float *sw_src,
                         const float *cw, const float *cb, int nc, float eps, char *err, size_t errlen, int *kind);
 int bnn_proto_n4_check(const int8_t *qw, int Kp, const uint8_t *n4, int npanels);
+/* hp_pack panels as the fp16 GEMM's k-major [Kp][Np] weights (dup: each in both halves of a word, to d->hwd; else
+ * plain fp16, to d->hw), b16 to d->hb, b32 to *b32 unless NULL */
+int bnn_hpack_weights(bnn_devop *d, int dup, const uint16_t *panels, const float *b32src, const uint16_t *b16src,
+                      int Kp, int Np, float **b32, char *err, size_t errlen, int *kind);
 /* pc_logmel_new's tables on the current device (t points into d->lm_mem); -1 with err set on failure */
 int bnn_logmel_build(bnn_devop *d, int nsamp, int frame, int hop, int pad, int nfft, int nmel, const float *window,
                      const float *mel, float floor_, float scale, char *err, size_t errlen, int *kind);

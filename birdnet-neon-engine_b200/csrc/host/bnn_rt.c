@@ -865,8 +865,8 @@ void bnn_logmel_release(bnn_devop *d) {
 /* hp_pack panels (src/gemm_f16.c:17-40: [Np/16][Kp][16], then a [Kp][8] tail panel when Np % 16) as the k-major
  * [Kp][Np] matrix of the B200 fp16 GEMM, each weight in both halves of a 32-bit word (dup != 0, to d->hwd) or plain
  * fp16 (to d->hw); b16 [Np] to d->hb; b32 [Np] to *b32 unless NULL */
-static int hpack_upload(bnn_devop *d, int dup, const uint16_t *panels, const float *b32src, const uint16_t *b16src,
-                        int Kp, int Np, float **b32, char *err, size_t errlen, int *kind) {
+int bnn_hpack_weights(bnn_devop *d, int dup, const uint16_t *panels, const float *b32src, const uint16_t *b16src,
+                      int Kp, int Np, float **b32, char *err, size_t errlen, int *kind) {
   const size_t es = dup ? 4 : 2;
   uint8_t *wt = malloc(es * (size_t)Kp * Np);
   if (!wt) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory (fp16 weights, %d x %d)", Kp, Np); return -1; }
@@ -939,9 +939,9 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
     return bnn_proto_weights(d, p[0], p[2], p[3], tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 3), tptr(c, op, 4),
                              p[7], ((const float *)tptr(c, op, 5))[0], err, errlen, kind);
   case BNN_OP_C0POOL_F16: /* t = [w b32 b16]; p = [24 64 64 24] */
-    return hpack_upload(d, 0, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), 64, 24, NULL, err, errlen, kind);
+    return bnn_hpack_weights(d, 0, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), 64, 24, NULL, err, errlen, kind);
   case BNN_OP_PW_F16:
-    return hpack_upload(d, 1, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), p[2], p[3], &d->f[0], err, errlen, kind);
+    return bnn_hpack_weights(d, 1, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), p[2], p[3], &d->f[0], err, errlen, kind);
   case BNN_OP_DW3_F16: {
     const int C = p[2];
     return upload((void **)&d->hw, tptr(c, op, 0), sizeof(uint16_t) * 9 * C, err, errlen, kind) ||
@@ -955,7 +955,7 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
            upload((void **)&d->f[3], tptr(c, op, 3), sizeof(float) * C, err, errlen, kind);
   }
   case BNN_OP_POSTPC_F16: /* t = [post_s post_b w b32 b16] */
-    return hpack_upload(d, 1, tptr(c, op, 2), tptr(c, op, 3), tptr(c, op, 4), 1728, 1024, &d->f[1], err, errlen, kind) ||
+    return bnn_hpack_weights(d, 1, tptr(c, op, 2), tptr(c, op, 3), tptr(c, op, 4), 1728, 1024, &d->f[1], err, errlen, kind) ||
            upload((void **)&d->f[2], tptr(c, op, 0), sizeof(float) * 192, err, errlen, kind) ||
            upload((void **)&d->f[3], tptr(c, op, 1), sizeof(float) * 192, err, errlen, kind);
   case BNN_OP_DENSE_F16:

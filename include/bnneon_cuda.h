@@ -149,6 +149,22 @@ int bnn_proto_s8_read_scratch(bnn_proto_s8 *op, int B, int8_t *qa, float *sx);
 int bnn_proto_s8_error(bnn_proto_s8 *op);
 void bnn_proto_s8_free(bnn_proto_s8 *op);
 
+/* ---- PW f16: the neon-fp16 path's 1x1 conv (gemm_f16, src/gemm_f16.c:109-169; record src/rt_ops_f16.c:53-82).
+ * Weights as the package stores them: hp_pack panels [Np/16][Kp][16] then, when Np % 16, a [Kp][8] tail panel, b32
+ * [Np] and b16 [Np] (fp16 values are IEEE half bits); Np = N rounded up to 8, Kp >= K a multiple of 8. A run scores B
+ * windows of Mw rows: d_x rows of Kp fp16 values at row stride lda (a multiple of 8, >= Kp; window stride xws, a
+ * multiple of 8; 16-byte aligned) -> d_out fp16 rows of Np values at stride ldo (>= Np, a multiple of 4; window stride
+ * ows), stored at the padded row when opad (ow pixels a row, zero halo opad: the buffer's halo is not written);
+ * act 0 none, 1 SiLU (the reference's table form), 2 ReLU; d_res (or NULL): fp16 rows at stride ldr added after
+ * the activation. Bit-identical to the reference's fp16 arithmetic (fp16 FMA chains over K blocks of <= 128,
+ * fp32 flushes). */
+typedef struct bnn_pw_f16 bnn_pw_f16;
+bnn_pw_f16 *bnn_pw_f16_new(int N, int K, int Kp, int Np, const uint16_t *panels, const float *b32,
+                           const uint16_t *b16);
+int bnn_pw_f16_run(bnn_pw_f16 *op, int B, int Mw, const void *d_x, long long xws, int lda, int act, void *d_out,
+                   long long ows, int ldo, int ow, int opad, const void *d_res, long long rws, int ldr, void *stream);
+void bnn_pw_f16_free(bnn_pw_f16 *op);
+
 /* DW3 (src/gemm_f32.c:398-411, dw3x3_f32), batched: d_xp [B][(H+2)(W+2)][C] (zero halo 1), d_w [9][C], d_b [C] ->
  * d_out [B][Ho Wo][C], d_chsum [B][C]. A bounded device wait that ran out is reported by bnn_cuda_op_error. */
 int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, int s, const float *d_w,

@@ -115,3 +115,88 @@ def test_f16_overflow_fails_the_window(lib, tmp_path):
         with pytest.raises(BnnError) as e:
             m.infer_batch(pcm)
         assert e.value.kind == "WINDOW" and "postpc_f16" in str(e.value) and "window 0" in str(e.value)
+
+
+# ------------------------------------------------------------------ the fp16 1x1 conv through its own C ABI
+
+PW_CASES = [  # (Mw, B, N, K, act, ow, opad, residual): shapes the v2.4 model never has, and its own
+    (37, 3, 24, 48, 0, 0, 0, False),      # ragged row tiles, N 24 (4-channel thread tiles)
+    (100, 2, 8, 8, 1, 0, 0, False),       # N 8: a channel tile wider than N
+    (64, 2, 72, 24, 1, 16, 1, False),     # padded output rows (the depthwise conv's input)
+    (50, 2, 40, 136, 2, 0, 0, True),      # two K blocks of 72 and 64, ReLU, residual
+    (20, 5, 136, 264, 1, 0, 0, False),    # N 136 (a ragged second channel tile), three K blocks of 88
+    (33, 2, 288, 72, 1, 11, 2, False),    # halo 2
+    (7, 3, 1536, 1536, 0, 0, 0, True),    # twelve K blocks of 128
+    (6, 4, 1024, 1728, 2, 0, 0, False),   # the pc conv's shape: fourteen blocks
+    (1, 9, 16, 1000, 1, 0, 0, False),     # K not a multiple of 8: Kp 1000 -> 1000, 8 K blocks of 128 - (ragged 104)
+]
+
+
+def half_bits(a):
+    return np.ascontiguousarray(a, np.float16).view(np.uint16)
+
+
+def f16_equal(got, want):
+    g, w = np.asarray(got, np.uint16), np.asarray(want, np.uint16)
+    gn = (g & 0x7C00) == 0x7C00
+    gn &= (g & 0x3FF) != 0
+    wn = ((w & 0x7C00) == 0x7C00) & ((w & 0x3FF) != 0)
+    return np.array_equal(gn, wn) and np.array_equal(g[~gn], w[~wn])
+
+
+@pytest.mark.parametrize("case", PW_CASES, ids=[f"M{c[0]}xB{c[1]}_N{c[2]}_K{c[3]}_act{c[4]}" for c in PW_CASES])
+def test_pw_f16_op(lib, case):
+    Mw, B, N, K, act, ow, opad, residual = case
+    rng = np.random.default_rng(N * 31 + K)
+    Kp = (K + 7) & ~7
+    w = (rng.standard_normal((N, K)) * (2.0 / np.sqrt(K))).astype(np.float32)
+    w[0, :] = 0.0  # a zero channel
+    b = (rng.standard_normal(N) * 0.2).astype(np.float32)
+    panels, b32, b16, shp = synth.pack_h16(w, b, Kp)
+    Np = shp[3]
+    lda, ldo, ldr = Kp + 8, Np + 4, Np + 8
+    x = (rng.standard_normal((B, Mw, lda)) * 3.0).astype(np.float16)
+    x[:, :, Kp:] = 0
+    x[0, 0, :4] = [60000.0, -60000.0, 6e-8, -0.0]  # overflow toward infinity, a subnormal, -0
+    res = (rng.standard_normal((B, Mw, ldr)) * 0.5).astype(np.float16) if residual else None
+    orows = ((Mw // ow) + 2 * opad) * (ow + 2 * opad) if opad else Mw
+    op = lib.bnn_pw_f16_new(N, K, Kp, Np, panels.ctypes.data, b32.ctypes.data, b16.ctypes.data)
+    assert op, lib.bnn_last_error()
+    try:
+        d_x = torch.from_numpy(half_bits(x).astype(np.int16)).cuda()
+        d_out = torch.full((B, orows, ldo), 0x7777, dtype=torch.int16, device="cuda")
+        d_res = torch.from_numpy(half_bits(res).astype(np.int16)).cuda() if residual else None
+        rc = lib.bnn_pw_f16_run(op, B, Mw, d_x.data_ptr(), Mw * lda, lda, act, d_out.data_ptr(), orows * ldo, ldo, ow,
+                                opad, d_res.data_ptr() if residual else None, Mw * ldr if residual else 0,
+                                ldr if residual else 0, None)
+        assert rc == 0, lib.bnn_last_error()
+        torch.cuda.synchronize()
+        got = d_out.cpu().numpy().view(np.uint16)
+    finally:
+        lib.bnn_pw_f16_free(op)
+    for wi in range(B):
+        want = oracle.gemm_f16(x[wi], panels, b32, b16, Kp, Np, act, Mw, ldo=ldo, ow=ow, opad=opad,
+                               res=None if res is None else res[wi], ldr=ldr).view(np.uint16)
+        if opad:  # the halo is not written: the sentinel stays
+            keep = np.zeros((orows,), bool)
+            for m in range(Mw):
+                keep[((m // ow) + opad) * (ow + 2 * opad) + m % ow + opad] = True
+            assert (got[wi][~keep] == 0x7777).all()
+            g, wv = got[wi][keep][:, :Np], want[keep][:, :Np]
+        else:
+            g, wv = got[wi][:, :Np], want[:, :Np]
+        assert (got[wi][:, Np:] == 0x7777).all()
+        assert f16_equal(g, wv), (wi, int(np.sum(g != wv)))
+
+
+def test_pw_f16_op_refuses_bad_arguments(lib):
+    panels, b32, b16, _ = synth.pack_h16(np.ones((8, 8), np.float32), np.zeros(8, np.float32), 8)
+    assert not lib.bnn_pw_f16_new(8, 8, 12, 8, panels.ctypes.data, b32.ctypes.data, b16.ctypes.data)
+    assert "Kp % 8 == 0" in lib.bnn_last_error().decode()
+    op = lib.bnn_pw_f16_new(8, 8, 8, 8, panels.ctypes.data, b32.ctypes.data, b16.ctypes.data)
+    try:
+        d = torch.zeros(64, dtype=torch.int16, device="cuda")
+        assert lib.bnn_pw_f16_run(op, 1, 4, d.data_ptr(), 32, 4, 0, d.data_ptr(), 32, 8, 0, 0, None, 0, 0, None) == -1
+        assert "lda 4" in lib.bnn_last_error().decode()
+    finally:
+        lib.bnn_pw_f16_free(op)
