@@ -184,10 +184,11 @@ int bnnk_gemm_f16(int rows, int Mw, const uint16_t *A, long long aws, int lda, c
 /* C0POOL f16: img [B][96][511][2] fp32 -> pin [B][48 * 128][48] fp16; W [64][24] k-major, b16 [24] */
 int bnnk_c0pool_f16(int B, const float *img, long long iws, const uint16_t *W, const uint16_t *b16, uint16_t *pin,
                     long long pws, bnn_stream_t st);
-/* DW3 f16: xp [B][(H+2)(W+2)][C] haloed -> out [B][Ho Wo][C], chsum [B][C]; w [9][C], b [C] fp16 */
+/* DW3 f16: xp [B][(H+2)(W+2)][C] haloed -> out [B][Ho Wo][C], chsum [B][C]; w [9][C], b [C] fp16; err: the device
+ * error word a timed-out input wait is reported in (NULL: not reported) */
 int bnnk_dw3_f16(int B, const uint16_t *xp, long long xws, int H, int W, int C, int s, int pt, int pl,
                  const uint16_t *w, const uint16_t *b, uint16_t *out, long long ows, int Ho, int Wo, float *chsum,
-                 long long cws, bnn_stream_t st);
+                 long long cws, int *err, bnn_stream_t st);
 /* SE f16: the gate from chsum [B][C] (fp32 FCs, sigm4, rounded to fp16 into g16 [B][C]), D [B][P][C] scaled in place */
 int bnnk_se_f16(int B, int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,
                 const float *chsum, long long cws, int P, uint16_t *D, long long dws, uint16_t *g16, bnn_stream_t st);

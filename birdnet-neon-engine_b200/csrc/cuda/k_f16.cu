@@ -14,8 +14,14 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "bnn_kernels.h"
 #include "emu.cuh"
+#include "sync.cuh"
 #include "tc.cuh"
 
 namespace bnn {
@@ -487,6 +493,130 @@ __global__ void __launch_bounds__(1024) k_dw3_f16(const uint16_t *__restrict__ x
   }
 }
 
+// The same DW3 with the input streamed by TMA (the fp32 path's k_dw3t schedule in fp16 arithmetic). One CTA per
+// (window, group of CG channels) walks the output rows: the haloed input rows (W + 2 pixels x CG channels, one 3-D
+// tensor-map box) pass through a ring of NR = S + 3 slots in shared memory, loaded one row step ahead, so every
+// input byte is read from HBM once and no thread waits on a global load. Thread (lane, channel octet) keeps its
+// octet's weights in registers and computes pixel groups lane, lane + NL, ... of the row (R consecutive pixels per
+// group share their input columns) with the reference's two tap chains, stores them and leaves them in a
+// double-buffered row tile; after the step's barrier the first CG / 2 threads add their channel pair's outputs over
+// the row in pixel order (the fp16 row sum) and flush it to their fp32 channel sums. Row v of the ring is input row
+// v + 1 - pt; pixel x of an output group reads input columns x S + 1 - pl ...
+template <int S, int R>
+__global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtensorMap tmx, int W, int C, int CG,
+                                                  int pt, int pl, int Ho, int Wo, const uint16_t *__restrict__ wt,
+                                                  const uint16_t *__restrict__ bt, uint16_t *__restrict__ out,
+                                                  long long ows, float *__restrict__ chsum, long long cws, int *err) {
+  constexpr int NR = S + 3, NX = (R - 1) * S + 3;
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ __align__(8) unsigned long long bar[NR];
+  __shared__ uint32_t tab01[16], tab2[16];
+  const int tid = threadIdx.x, nt = blockDim.x;
+  load_silu_tab(tab01, tab2);
+  const int ngroups = C / CG;
+  const int win = blockIdx.x / ngroups, grp = blockIdx.x - win * ngroups;
+  const int Wp = W + 2, Q = CG >> 3, NL = nt / Q, ngrp = Wo / R, ro = 1 - pt, co = 1 - pl;
+  const uint32_t row_bytes = (uint32_t)Wp * CG * 2, row_stride = (row_bytes + 127u) & ~127u;
+  const uint32_t ring = smem_u32(dsm);
+  uint16_t *obuf = reinterpret_cast<uint16_t *>(dsm + NR * row_stride);  // [2][Wo][CG]
+  const int q = tid % Q, lane = tid / Q;  // lanes >= NL (the last nt % Q threads) only sum
+  const bool comp = lane < NL;
+  const int c = grp * CG + 8 * q;
+  uint32_t w[9][4], b[4];
+#pragma unroll
+  for (int t = 0; t < 9; t++) {
+    const uint4 v = comp ? __ldg(reinterpret_cast<const uint4 *>(wt + (size_t)t * C + c)) : make_uint4(0u, 0u, 0u, 0u);
+    w[t][0] = v.x; w[t][1] = v.y; w[t][2] = v.z; w[t][3] = v.w;
+  }
+  {
+    const uint4 v = comp ? __ldg(reinterpret_cast<const uint4 *>(bt + c)) : make_uint4(0u, 0u, 0u, 0u);
+    b[0] = v.x; b[1] = v.y; b[2] = v.z; b[3] = v.w;
+  }
+  if (tid == 0) {
+    for (int i = 0; i < NR; i++) mbar_init(smem_u32(&bar[i]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int rows_in = (Ho - 1) * S + 3;  // ring rows the outputs read
+  int issued = 0;                        // ring rows whose load thread 0 has issued
+  auto issue_to = [&](int last) {        // thread 0: load ring rows issued .. last
+    for (; issued <= last && issued < rows_in; issued++) {
+      const int sl = issued % NR;
+      mbar_expect_tx(smem_u32(&bar[sl]), row_bytes);
+      tma_load_3d(ring + sl * row_stride, &tmx, smem_u32(&bar[sl]), grp * CG, (issued + ro) * Wp, win);
+    }
+  };
+  if (tid == 0) issue_to(S + 2);  // the rows of steps 0 and 1
+  float2 cs = make_float2(0.f, 0.f);
+  int oy = 0;
+  for (; oy < Ho; oy++) {
+    bool ok = true;
+#pragma unroll
+    for (int ky = 0; ky < 3; ky++) {
+      const int iy = oy * S + ky;
+      ok = ok && mbar_wait(smem_u32(&bar[iy % NR]), (uint32_t)(iy / NR) & 1u);
+    }
+    uint16_t *ob = obuf + (size_t)(oy & 1) * Wo * CG;
+    if (comp) {
+      for (int g = lane; g < ngrp; g += NL) {
+        const int x0 = g * R;
+        uint32_t a[R][4], a2[R][4];
+#pragma unroll
+        for (int ky = 0; ky < 3; ky++) {
+          const uint16_t *rw = reinterpret_cast<const uint16_t *>(dsm + ((oy * S + ky) % NR) * row_stride) +
+                               (size_t)(x0 * S + co) * CG + 8 * q;
+          uint4 xin[NX];
+#pragma unroll
+          for (int j = 0; j < NX; j++) xin[j] = *reinterpret_cast<const uint4 *>(rw + (size_t)j * CG);
+#pragma unroll
+          for (int r = 0; r < R; r++) {
+#pragma unroll
+            for (int kx = 0; kx < 3; kx++) {
+              const uint4 xv = xin[r * S + kx];
+              const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+              const int t = 3 * ky + kx;  // taps 0, 2, 4, 6, 8 chain a (from the bias), 1, 3, 5, 7 chain a2
+#pragma unroll
+              for (int h = 0; h < 4; h++) {
+                if (t == 0) a[r][h] = hfma2(xs[h], w[0][h], b[h]);
+                else if (t == 1) a2[r][h] = hmul2(xs[h], w[1][h]);
+                else if (t % 2 == 0) a[r][h] = hfma2(xs[h], w[t][h], a[r][h]);
+                else a2[r][h] = hfma2(xs[h], w[t][h], a2[r][h]);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          uint32_t y[4];
+#pragma unroll
+          for (int h = 0; h < 4; h++) y[h] = silu2(hadd2(a[r][h], a2[r][h]), tab01, tab2);
+          const uint4 v = make_uint4(y[0], y[1], y[2], y[3]);
+          *reinterpret_cast<uint4 *>(out + (size_t)win * ows + ((size_t)oy * Wo + x0 + r) * C + c) = v;
+          *reinterpret_cast<uint4 *>(ob + (size_t)(x0 + r) * CG + 8 * q) = v;
+        }
+      }
+    }
+    if (!__syncthreads_and(ok)) break;  // every thread has left this step's rows and written its outputs
+    if (tid == 0) issue_to((oy + 2) * S + 2);
+    if (tid < CG / 2) {  // channel pair tid: the fp16 row sum in pixel order, then the fp32 channel sums
+      const uint32_t *o32 = reinterpret_cast<const uint32_t *>(ob);
+      uint32_t rs = 0u;
+      for (int x = 0; x < Wo; x++) rs = hadd2(rs, o32[(size_t)x * (CG / 2) + tid]);
+      cs.x = __fadd_rn(cs.x, h_lo(rs));
+      cs.y = __fadd_rn(cs.y, h_hi(rs));
+    }
+  }
+  if (oy < Ho) {  // a load never arrived: report it, then let the loads still in flight land before leaving
+    if (tid == 0) {
+      if (err) atomicExch(err, BNNK_ERR_DW3_WAIT);
+      for (int iy = oy * S; iy < issued; iy++) mbar_wait(smem_u32(&bar[iy % NR]), (uint32_t)(iy / NR) & 1u);
+    }
+    __syncthreads();
+    return;
+  }
+  if (tid < CG / 2) *reinterpret_cast<float2 *>(chsum + (size_t)win * cws + grp * CG + 2 * tid) = cs;
+}
+
 // ------------------------------------------------------------------ SE f16 (src/v24_fast.c:186-235)
 
 // sigm4 (src/v24_fast.c:173-185): 1 / (1 + 2^t), t = -a log2 e clamped to [-126, 126], 2^t as a degree-6 polynomial
@@ -810,11 +940,67 @@ extern "C" int bnnk_c0pool_f16(int B, const float *img, long long iws, const uin
   return cudaGetLastError();
 }
 
+static PFN_cuTensorMapEncodeTiled_v12000 f16_encode_fn(void) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult qr;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+// shared memory of the TMA form for CG channels: the ring of S + 3 input rows and the two output-row tiles
+static size_t dw3t_f16_smem(int W, int Wo, int s, int cg) {
+  const size_t row_stride = ((size_t)(W + 2) * cg * 2 + 127) & ~(size_t)127;
+  return (size_t)(s + 3) * row_stride + 2 * 2 * (size_t)Wo * cg;
+}
+
 extern "C" int bnnk_dw3_f16(int B, const uint16_t *xp, long long xws, int H, int W, int C, int s, int pt, int pl,
                             const uint16_t *w, const uint16_t *b, uint16_t *out, long long ows, int Ho, int Wo,
-                            float *chsum, long long cws, bnn_stream_t st) {
-  (void)H;
+                            float *chsum, long long cws, int *err, bnn_stream_t st) {
   if (B <= 0) return 0;
+  // the TMA form: channels per CTA the largest multiple of 8 dividing C, at most 256 (one box dimension), with at
+  // most 113 KB of shared memory (two CTAs per SM)
+  int cg = 0;
+  for (int g = 8; g <= C && g <= 256; g += 8)
+    if (C % g == 0 && dw3t_f16_smem(W, Wo, s, g) <= 113 * 1024) cg = g;
+  PFN_cuTensorMapEncodeTiled_v12000 enc = f16_encode_fn();
+  if (cg && enc && ((uintptr_t)xp & 15) == 0 && xws % 8 == 0 && W + 2 <= 256 && (s == 1 || s == 2) &&
+      ((uintptr_t)out & 15) == 0 && ows % 8 == 0 && ((uintptr_t)w & 15) == 0 && ((uintptr_t)b & 15) == 0 &&
+      cws % 2 == 0 && (Ho - 1) * s - pt + 1 + 3 <= H + 2 && (Wo - 1) * s - pl + 1 + 3 <= W + 2) {
+    CUtensorMap map;
+    cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)(H + 2) * (W + 2), (cuuint64_t)B};
+    cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)xws * 2};
+    cuuint32_t box[3] = {(cuuint32_t)cg, (cuuint32_t)(W + 2), 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t *>(xp), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+      const size_t smem = dw3t_f16_smem(W, Wo, s, cg);
+      const unsigned grid = (unsigned)B * (unsigned)(C / cg);
+      const int Q = cg / 8;  // threads: whole channel octets up to 256, at least the CG / 2 summing threads
+      int nt = (256 / Q) * Q;
+      if (nt < cg / 2) nt = cg / 2;
+      nt = (nt + 31) / 32 * 32;
+      const bool pair = Wo % 2 == 0;
+#define BNN_DW3T16(SS, RR)                                                                                     \
+  do {                                                                                                        \
+    cudaError_t e_ = cudaFuncSetAttribute(k_dw3t_f16<SS, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
+                                          (int)smem);                                                         \
+    if (e_) return e_;                                                                                        \
+    k_dw3t_f16<SS, RR><<<grid, nt, smem, st>>>(map, W, C, cg, pt, pl, Ho, Wo, w, b, out, ows, chsum, cws, err); \
+  } while (0)
+      if (s == 1) { if (pair) BNN_DW3T16(1, 2); else BNN_DW3T16(1, 1); }
+      else { if (pair) BNN_DW3T16(2, 2); else BNN_DW3T16(2, 1); }
+#undef BNN_DW3T16
+      return cudaGetLastError();
+    }
+  }
+  // the general form: taps loaded straight from global memory
   if (C % 2 || xws % 2 || ows % 2 || cws % 2) return cudaErrorInvalidValue;
   const int C2 = C / 2;
   int Lc = C2 <= 64 ? C2 : 64;

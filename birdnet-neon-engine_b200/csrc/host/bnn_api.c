@@ -1103,6 +1103,21 @@ int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, i
                                              op_err_word(), (bnn_stream_t)stream));
 }
 
+int bnn_cuda_dw3_f16(int B, const void *d_xp, long long xws, int H, int W, int C, int s, int pt, int pl,
+                     const void *d_w, const void *d_b, void *d_out, long long ows, int Ho, int Wo, float *d_chsum,
+                     long long cws, void *stream) {
+  if (B < 0 || H <= 0 || W <= 0 || C <= 0 || C % 8 || C > 2048 || (s != 1 && s != 2) || pt < 0 || pt > 1 || pl < 0 ||
+      pl > 1 || Ho <= 0 || Wo <= 0 || Ho > 192 || (Ho - 1) * s - pt + 1 + 3 > H + 2 ||
+      (Wo - 1) * s - pl + 1 + 3 > W + 2 || xws % 2 || ows % 2 || cws % 2 || !d_xp || !d_w || !d_b || !d_out ||
+      !d_chsum) {
+    ERR(BNN_ERR_USAGE, "bnn_cuda_dw3_f16: H %d W %d C %d s %d pt %d pl %d Ho %d Wo %d (C %% 8 == 0 and <= 2048, s 1|2, "
+        "pt and pl 0|1, Ho <= 192, taps inside the halo, even strides)", H, W, C, s, pt, pl, Ho, Wo);
+    return -1;
+  }
+  return launch_rc("bnn_cuda_dw3_f16", bnnk_dw3_f16(B, d_xp, xws, H, W, C, s, pt, pl, d_w, d_b, d_out, ows, Ho, Wo,
+                                                    d_chsum, cws, op_err_word(), (bnn_stream_t)stream));
+}
+
 int bnn_cuda_peak_hfma2(int blocks, int iters, void *d_word, void *stream) {
   if (blocks <= 0 || iters <= 0 || !d_word) {
     ERR(BNN_ERR_USAGE, "bnn_cuda_peak_hfma2: blocks %d iters %d word %p", blocks, iters, d_word);

@@ -1230,7 +1230,7 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
     }
     case BNN_OP_DW3_F16:
       rc = bnnk_dw3_f16(n, B_(0), WS(0), p[0], p[1], p[2], p[3], p[6], p[7], o->hw, o->hb, B_(1), WS(1), p[4], p[5],
-                        B_(2), WS(2), st);
+                        B_(2), WS(2), dv->err, st);
       break;
     case BNN_OP_SE_F16:
       rc = bnnk_se_f16(n, p[0], p[1], o->f[0], o->f[1], o->f[2], o->f[3], B_(1), WS(1), p[2], B_(0), WS(0), dv->g16,

@@ -171,6 +171,14 @@ int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, i
                  const float *d_b, float *d_out, long long ows, int Ho, int Wo, float *d_chsum, long long cws,
                  void *stream);
 
+/* DW3 f16 (dw3x3_f16_cr, src/kern_f16.c:83-155; record src/rt_ops_f16.c:64-103), batched: d_xp [B][(H+2)(W+2)][C]
+ * fp16 (zero halo 1; window stride xws), d_w [9][C], d_b [C] fp16 -> d_out [B][Ho Wo][C] fp16, d_chsum [B][C] fp32;
+ * stride s 1 | 2, output pixel (oy, ox) reads input rows oy s - pt + 1 .. + 2 and columns ox s - pl + 1 .. + 2 of the
+ * haloed image (pt, pl in {0, 1}). A bounded device wait that ran out is reported by bnn_cuda_op_error. */
+int bnn_cuda_dw3_f16(int B, const void *d_xp, long long xws, int H, int W, int C, int s, int pt, int pl,
+                     const void *d_w, const void *d_b, void *d_out, long long ows, int Ho, int Wo, float *d_chsum,
+                     long long cws, void *stream);
+
 /* the current device's error word of the per-op entry points (0 = no bounded device wait ran out; then reset to 0;
  * -1 if it cannot be read); synchronous */
 int bnn_cuda_op_error(void);

@@ -200,3 +200,45 @@ def test_pw_f16_op_refuses_bad_arguments(lib):
         assert "lda 4" in lib.bnn_last_error().decode()
     finally:
         lib.bnn_pw_f16_free(op)
+
+
+# ------------------------------------------------------------------ the fp16 depthwise conv through its own C ABI
+
+DW_CASES = [  # (B, H, W, C, s, pt, pl): the v2.4 shapes and the record's other geometries
+    (2, 24, 64, 72, 1, 1, 1), (2, 48, 128, 72, 2, 1, 1), (3, 12, 32, 288, 1, 1, 1), (2, 6, 16, 864, 2, 1, 1),
+    (2, 3, 8, 1536, 1, 1, 1),
+    (2, 9, 14, 16, 1, 0, 0),    # pt = pl = 0 and an odd output width (one pixel per group)
+    (3, 10, 11, 8, 2, 0, 1),    # stride 2, pt 0, C 8
+    (1, 5, 7, 2048, 2, 1, 0),   # the widest C the record allows
+]
+
+
+@pytest.mark.parametrize("case", DW_CASES, ids=[f"H{c[1]}W{c[2]}C{c[3]}s{c[4]}pt{c[5]}pl{c[6]}" for c in DW_CASES])
+def test_dw3_f16_op(lib, case):
+    B, H, W, C, s, pt, pl = case
+    # the largest output the taps allow: (Ho - 1) s - pt + 1 + 3 <= H + 2
+    Ho, Wo = (H + 2 - 4 + pt) // s + 1, (W + 2 - 4 + pl) // s + 1
+    rng = np.random.default_rng(H * 7 + C)
+    xp = np.zeros((B, H + 2, W + 2, C), np.float16)
+    xp[:, 1:H + 1, 1:W + 1] = (rng.standard_normal((B, H, W, C)) * 2.0).astype(np.float16)
+    xp[0, 1, 1, :2] = [60000.0, -0.0]
+    w = (rng.standard_normal((9, C)) * 0.5).astype(np.float16)
+    bias = (rng.standard_normal(C) * 0.1).astype(np.float16)
+    xws, ows = (H + 2) * (W + 2) * C, Ho * Wo * C
+    d_x = torch.from_numpy(half_bits(xp).astype(np.int16)).cuda()
+    d_w = torch.from_numpy(half_bits(w).astype(np.int16)).cuda()
+    d_b = torch.from_numpy(half_bits(bias).astype(np.int16)).cuda()
+    d_o = torch.full((B, ows), 0x7777, dtype=torch.int16, device="cuda")
+    d_c = torch.full((B, C), 7.0, dtype=torch.float32, device="cuda")
+    assert lib.bnn_cuda_dw3_f16(B, d_x.data_ptr(), xws, H, W, C, s, pt, pl, d_w.data_ptr(), d_b.data_ptr(),
+                                d_o.data_ptr(), ows, Ho, Wo, d_c.data_ptr(), C, None) == 0, lib.bnn_last_error()
+    torch.cuda.synchronize()
+    assert lib.bnn_cuda_op_error() == 0
+    got, chs = d_o.cpu().numpy().view(np.uint16), d_c.cpu().numpy()
+    for wi in range(B):
+        out = np.zeros((Ho * Wo, C), np.uint16)
+        cs = np.zeros(C, np.float32)
+        oracle.lib().bnno_dw3_f16(half_bits(xp[wi]).ctypes.data, H, W, C, s, pt, pl, half_bits(w).ctypes.data,
+                                  half_bits(bias).ctypes.data, out.ctypes.data, Ho, Wo, cs.ctypes.data)
+        assert f16_equal(got[wi].reshape(Ho * Wo, C), out), (wi, int(np.sum(got[wi].reshape(Ho * Wo, C) != out)))
+        assert bits_equal(chs[wi], cs), mismatch_report(chs[wi], cs)
