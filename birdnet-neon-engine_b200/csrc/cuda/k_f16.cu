@@ -729,8 +729,9 @@ __global__ void k_postpc_f16_mean(const uint16_t *__restrict__ pcout, long long 
 //
 // The 4-row path of v24k16_head for every class o < N & ~3: x = fp16(feat); per 128-k block 8 fp16 lanes, lane j
 // the FMA chain over k = j mod 8 from +0; the lanes flushed into 8 fp32 sums; out = FADDP((s_j + s_{j+4})_j) + b.
-// A thread holds 2 windows x 4 classes; a lane pair (2q, 2q + 1) is one fp16x2 chain over k-step pairs. Shared
-// tiles per block: X [32 windows][128 + 8] and W [64 classes][128 + 8] fp16 (rows padded against bank conflicts).
+// A thread holds 2 windows x 4 classes (tc, tc + 16, tc + 32, tc + 48 of the CTA's 64: a warp's weight rows are then
+// consecutive, 4 banks apart); a lane pair (2q, 2q + 1) is one fp16x2 chain over k-step pairs. Shared tiles per
+// block: X [32 windows][128 + 8] and W [64 classes][128 + 8] fp16 (rows padded against bank conflicts).
 constexpr int kDnW = 32, kDnC = 64, kDnLd = 136;
 __global__ void __launch_bounds__(256) k_dense_f16(int B, int N4, const float *__restrict__ feat, long long fws,
                                                    const uint16_t *__restrict__ W, const float *__restrict__ bias,
@@ -774,7 +775,7 @@ __global__ void __launch_bounds__(256) k_dense_f16(int B, int N4, const float *_
 #pragma unroll
       for (int a = 0; a < 2; a++) xv[a] = *reinterpret_cast<const uint4 *>(&xs[tw * 2 + a][k]);
 #pragma unroll
-      for (int b = 0; b < 4; b++) wv[b] = *reinterpret_cast<const uint4 *>(&ws[tc * 4 + b][k]);
+      for (int b = 0; b < 4; b++) wv[b] = *reinterpret_cast<const uint4 *>(&ws[tc + 16 * b][k]);
 #pragma unroll
       for (int a = 0; a < 2; a++)
 #pragma unroll
@@ -799,7 +800,7 @@ __global__ void __launch_bounds__(256) k_dense_f16(int B, int N4, const float *_
   for (int a = 0; a < 2; a++)
 #pragma unroll
     for (int b = 0; b < 4; b++) {
-      const int w = w0 + tw * 2 + a, o = c0 + tc * 4 + b;
+      const int w = w0 + tw * 2 + a, o = c0 + tc + 16 * b;
       if (w >= B || o >= N4) continue;
       float v[4];
 #pragma unroll
