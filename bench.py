@@ -407,17 +407,13 @@ def hfma2_peak(h, torch, stream):
     return 2.0 * blocks * 256 * iters * 16 / (ms * 1e-3) / 1e12
 
 
-def v24_fp16_c3(torch, stream, batch=1024, steps=10, cpu=True):
-    """SURVEY C3: the v2.4-architecture neon-fp16 package (the reference compiler's bytes for the same synthetic IR)
-    on `batch` windows: device-resident windows/s (bnn_infer_device, CUDA events over `steps` steps after 3
-    warm-ups), end to end through bnn_infer_batch with pinned host buffers, the per-op-class device time, and the
-    fp16 GEMMs' FLOP/s against the measured fp16 FMA pipe peak. Every kernel is bit-exact against the oracle (the
-    reference's fp16 FMA chains on CUDA cores; the tensor cores cannot reproduce them)."""
+def fp16_package_leg(torch, stream, pkg, pcm, batch, steps, cpu, workload, parity):
+    """One neon-fp16 package on `batch` windows: device-resident windows/s (bnn_infer_device, CUDA events over `steps`
+    steps after 3 warm-ups), end to end through bnn_infer_batch with pinned host buffers, the per-op-class device
+    time, and the fp16 GEMMs' FLOP/s against the measured fp16 FMA pipe peak. Every kernel is bit-exact against the
+    oracle (the reference's fp16 FMA chains on CUDA cores; the tensor cores cannot reproduce them)."""
     from bnneon_b200 import Model, pkgread, synth  # pylint: disable=import-outside-toplevel
-    td = tempfile.mkdtemp()
-    pkg = os.path.join(td, "v24_full_f16.bnpk")
-    synth.make_package(pkg, seed=0, path=synth.PATH_F16)
-    pcm = synth.audio(batch, seed=4000)
+    nsamp = pcm.shape[1]
     m = Model(pkg, mode=3, batch=batch)
     try:
         nc, ne = m.info.n_classes, m.info.emb_dim
@@ -479,11 +475,10 @@ def v24_fp16_c3(torch, stream, batch=1024, steps=10, cpu=True):
                 "sample": f"{n} windows, one per thread: oracle/liboracle.so (the C restatement of the reference's "
                           f"neon-fp16 path, every fp16 operation emulated exactly in software), {dt:.1f} s"}
     total = sum(v["ms"] for v in cls.values())
-    return {"workload": "BirdNET-v2.4-architecture neon-fp16 package (config 3): 144000-sample windows, fp16 "
-                        "activations and weights, 6522-class fp16 head",
+    return {"workload": workload,
             "batch": batch, "ms_per_step": round(ms, 3), "windows_per_s": round(batch / (ms * 1e-3), 1),
             "e2e": {"value": round(batch / (e2e_ms * 1e-3), 1), "unit": "windows/s",
-                    "h2d_bytes_per_step": batch * 144000 * 4, "d2h_bytes_per_step": batch * (nc + ne) * 4,
+                    "h2d_bytes_per_step": batch * nsamp * 4, "d2h_bytes_per_step": batch * (nc + ne) * 4,
                     "path": "bnn_infer_batch (C ABI), pinned host buffers, wall clock"},
             "gpu_launches_per_step": launches,
             "roofline": {"bound": "fp16 FMA pipe (CUDA cores)", "kernel": f"pw_f16 ({pw['ops']} GEMMs per step)",
@@ -493,9 +488,36 @@ def v24_fp16_c3(torch, stream, batch=1024, steps=10, cpu=True):
                          "note": "achieved = 2 M K N of the 1x1 convs (Kp, Np as packed) / their CUDA-event time"},
             "ops": {k: {"ms": round(v["ms"], 4), "share": round(v["ms"] / total, 4), "ops": v["ops"]}
                     for k, v in sorted(cls.items(), key=lambda kv: -kv[1]["ms"])},
-            "parity": "bit-exact against the oracle (tests/test_gpu_f16.py); the oracle within 50 dB SQNR of a "
-                      "float64 model (tests/test_f16_cpu.py)",
-            "cpu_baseline": base}
+            "parity": parity, "cpu_baseline": base}
+
+
+def v24_fp16_c3(torch, stream, batch=1024, steps=10, cpu=True):
+    """SURVEY C3: the v2.4-architecture neon-fp16 package (the reference compiler's bytes for the same synthetic IR)
+    on `batch` windows."""
+    from bnneon_b200 import synth  # pylint: disable=import-outside-toplevel
+    pkg = os.path.join(tempfile.mkdtemp(), "v24_full_f16.bnpk")
+    synth.make_package(pkg, seed=0, path=synth.PATH_F16)
+    return fp16_package_leg(
+        torch, stream, pkg, synth.audio(batch, seed=4000), batch, steps, cpu,
+        "BirdNET-v2.4-architecture neon-fp16 package (config 3): 144000-sample windows, fp16 activations and weights, "
+        "6522-class fp16 head",
+        "bit-exact against the oracle (tests/test_gpu_f16.py); the oracle within 50 dB SQNR of a float64 model "
+        "(tests/test_f16_cpu.py)")
+
+
+def perch_c4(torch, stream, batch=512, steps=5, cpu=True):
+    """a Perch-v2-architecture package, neon-fp16 body + the int8 SDOT prototype head (bnc.py compile
+    --paths neon-fp16 --proto-s8), 160000-sample windows at 32 kHz, 59180 prototypes, on `batch` windows."""
+    from bnneon_b200 import synth  # pylint: disable=import-outside-toplevel
+    pkg = os.path.join(tempfile.mkdtemp(), "perch_v2_f16s8.bnpk")
+    _, _, ns = synth.make_perch_package(pkg, seed=0)
+    pcm = synth.audio(batch, seed=4100, n_samples=ns, rate=synth.PERCH_SAMPLE_RATE)
+    return fp16_package_leg(
+        torch, stream, pkg, pcm, batch, steps, cpu,
+        "Perch-v2-architecture neon-fp16 package with the int8 prototype head (config 4): 160000-sample windows, "
+        "log-mel front end, fp32 stem, 26 fp16 MBConv blocks, 14795 x 4 int8 prototypes on 64 cells, 1536-d embedding",
+        "bit-exact against the oracle (tests/test_gpu_perch.py); the oracle within 50 dB SQNR of a float64 model on "
+        "the embedding (tests/test_perch_cpu.py)")
 
 
 def load_peaks():
@@ -855,6 +877,8 @@ def main():
               if rank == 0 and not args.no_proto else None)
     fp16 = (v24_fp16_c3(torch, stream, cpu=not args.no_cpu_baseline and world == 1)
             if rank == 0 and not args.no_proto else None)
+    perch = (perch_c4(torch, stream, cpu=not args.no_cpu_baseline and world == 1)
+             if rank == 0 and not args.no_proto else None)
 
     line = None
     if rank == 0:
@@ -872,7 +896,7 @@ def main():
                             "note": "int8 ops of PW_S8 + GEMV_S8 (quantizer + tcgen05 GEMM) per second; these GEMMs "
                                     "are HBM-bound (AI far below the int8 ridge)"},
                 "ops": ops_summary, "clocks": clocks, "s8_gemm_c1": c1, "proto_s8_c4": proto,
-                "fe_logmel_perch": logmel, "v24_fp16_c3": fp16}
+                "fe_logmel_perch": logmel, "v24_fp16_c3": fp16, "perch_v2_fp16_s8_c4": perch}
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(pkg, pcm)
     m.close()

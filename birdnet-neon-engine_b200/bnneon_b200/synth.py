@@ -770,6 +770,243 @@ def write_logmel_package(dst, fe, model_id="perch_v2_frontend_synthetic"):
     return nfr, nmel
 
 
+# ------------------------------------------------------------------ a Perch-v2-architecture model (neon-fp16 + int8 head)
+
+OPC_PERCH = dict(STEM=0x109, DWK=0x10a, PAD=0x10b, MEAN=0x10c, PROTO_F16S8=0x20d)
+# the EfficientNet-B3 stages of Perch v2's backbone (results/perch_graph_compact.txt, results/perch_mac_table.txt):
+# (blocks, depthwise k, first block's stride and pads [top, left, bottom, right], c_in, expansion, c_out)
+PERCH_STAGES = ((2, 3, 1, [1, 1, 1, 1], 40, 1, 24), (3, 3, 2, [1, 1, 1, 1], 24, 6, 32),
+                (3, 5, 2, [2, 1, 2, 2], 32, 6, 48), (5, 3, 2, [1, 0, 1, 1], 48, 6, 96),
+                (5, 5, 1, [2, 2, 2, 2], 96, 6, 136), (6, 5, 2, [1, 1, 2, 2], 136, 6, 232),
+                (2, 3, 1, [1, 1, 1, 1], 232, 6, 384))
+# one block per stage, but both blocks of the first and the last stage: every op kind and geometry of the full
+# model (DW3 on the stem output, PAD + DWK k3 of an unexpanded residual block, every strided depthwise form, DWK k3
+# above 2048 channels)
+PERCH_MINI_COUNTS = (2, 1, 1, 1, 1, 1, 2)
+PERCH_MINI_FE = dict(PERCH_FE, nsamp=80000)  # 249 frames: 124 x 63 after the stem, 8 x 4 cells
+PERCH_STEM = 40
+PERCH_TOP = 1536
+PERCH_HEAD = (14795, 4)  # classes x prototypes per class: 59180 prototypes (results/perch_graph_compact.txt:1129-1135)
+
+
+def perch_ir(seed=0, mini=False, n_classes=None, ppc=None, fe=None):
+    """The fused IR of a Perch-v2-architecture model with seeded random weights: FE_LOGMEL (a Perch-like log-mel
+    front end), the 3x3 stride-2 stem, 26 MBConv blocks (SE on every block) in the stages of PERCH_STAGES, the
+    1x1 top conv to 1536 channels, the prototype head on the 16 x 4 cells and the spatial mean (the embedding).
+    mini: one block per inner stage (PERCH_MINI_COUNTS), 61 classes and 2.5 s windows (8 x 4 cells), for tests.
+
+    Returns:
+        (ops, vshape, logits_value, embedding_value, fe)
+    """
+    rng = np.random.default_rng(seed)
+    f32 = np.float32
+    nc = n_classes if n_classes is not None else (61 if mini else PERCH_HEAD[0])
+    ppc = ppc or PERCH_HEAD[1]
+    fe = fe or logmel_frontend(**(PERCH_MINI_FE if mini else PERCH_FE))
+
+    def he(*shape, fan_in, scale=1.0):
+        return (rng.standard_normal(shape) * (scale * np.sqrt(2.0 / fan_in))).astype(f32)
+
+    def bias(n, sd=0.02):
+        return (rng.standard_normal(n) * sd).astype(f32)
+
+    ops, vshape = [], {}
+    nid = [0]
+
+    def val(h, w):
+        nid[0] += 1
+        vshape[nid[0]] = (h, w)
+        return nid[0]
+
+    nmel = fe["mel"].shape[0]
+    h, w = logmel_frames(fe), nmel
+    spec = val(h, w)
+    ops.append(dict(op="FE_LOGMEL", ins=[], out=spec, fe=fe, nodes=["perch/frontend"]))
+    h, w = (h - 3) // 2 + 1, (w - 3) // 2 + 1
+    x = val(h, w)
+    ops.append(dict(op="CONV", ins=[spec], out=x, w=he(PERCH_STEM, 1, 3, 3, fan_in=9), b=bias(PERCH_STEM), k=[3, 3],
+                    s=[2, 2], pads=[0, 0, 0, 0], act="swish", nodes=["perch/stem"]))
+    blk = 0
+    for si, (n, k, st0, pads0, cin0, ex, cout) in enumerate(PERCH_STAGES):
+        for j in range(PERCH_MINI_COUNTS[si] if mini else n):
+            cin = cin0 if j == 0 else cout
+            st = st0 if j == 0 else 1
+            pads = pads0 if j == 0 else [(k - 1) // 2] * 4
+            cm = cin * ex
+            rd = max(1, cin // 4)
+            tag = f"perch/block{blk}"
+            e = x
+            if ex != 1:
+                e = val(h, w)
+                ops.append(dict(op="CONV", ins=[x], out=e, w=he(cm, cin, 1, 1, fan_in=cin), b=bias(cm), k=[1, 1],
+                                s=[1, 1], pads=[0, 0, 0, 0], act="swish", nodes=[f"{tag}/expand"]))
+            ho = (h + pads[0] + pads[2] - k) // st + 1
+            wo = (w + pads[1] + pads[3] - k) // st + 1
+            d = val(ho, wo)
+            ops.append(dict(op="DWCONV", ins=[e], out=d, w=he(cm, 1, k, k, fan_in=k * k), b=bias(cm), k=[k, k],
+                            s=[st, st], pads=list(pads), act="swish", nodes=[f"{tag}/dw"]))
+            g = val(ho, wo)
+            ops.append(dict(op="SE", ins=[d], out=g, w1=he(rd, cm, fan_in=cm), b1=bias(rd), act1="swish",
+                            w2=he(cm, rd, fan_in=rd), b2=bias(cm, 0.5), nodes=[f"{tag}/se"]))
+            y = val(ho, wo)
+            proj = dict(op="CONV", ins=[g], out=y, w=he(cout, cm, 1, 1, fan_in=cm, scale=0.35), b=bias(cout),
+                        k=[1, 1], s=[1, 1], pads=[0, 0, 0, 0], act=None, nodes=[f"{tag}/project"])
+            if st == 1 and cin == cout:
+                proj["res"] = x
+            ops.append(proj)
+            x, h, w = y, ho, wo
+            blk += 1
+    top = val(h, w)
+    c_last = PERCH_STAGES[-1][6]
+    ops.append(dict(op="CONV", ins=[x], out=top, w=he(PERCH_TOP, c_last, 1, 1, fan_in=c_last), b=bias(PERCH_TOP),
+                    k=[1, 1], s=[1, 1], pads=[0, 0, 0, 0], act="swish", nodes=["perch/top"]))
+    head = proto_head(seed + 1, h * w, PERCH_TOP, nc, ppc, scale=1.0)
+    logits = val(1, 1)
+    ops.append(dict(op="PROTO", ins=[top], out=logits, P=head["P"], cw=head["cw"], cb=head["cb"], eps=head["eps"],
+                    nodes=["perch/protopnet"]))
+    emb = val(1, 1)
+    ops.append(dict(op="MEAN", ins=[top], out=emb, nodes=["perch/embedding"]))
+    return ops, vshape, logits, emb, fe
+
+
+class _PerchF16Lowering(_F16Lowering):
+    """The neon-fp16 lowering of a compiled model's IR with the int8 SDOT prototype head (bnc.py compile --paths
+    neon-fp16 --proto-s8), for the op kinds of Perch v2. Follows python/bnneon/compiler/lower.py: l_fe_logmel, stem
+    (im2col fp32 GEMM to fp16), pw / out_for_dw (a zero halo of (k - 1) / 2 for a lone depthwise consumer),
+    l_dwconv / dw_input (DW3 for a 3x3 on a halo-1 buffer with pads <= 1 and C <= 2048, else PAD when needed + DWK),
+    l_se (in place), l_mean, proto_s8 / emit_proto / cls_tensors."""
+
+    def __init__(self, ops, nsamp):
+        super().__init__(ops)
+        self.bufs = [(F32, 1, 1, nsamp, nsamp, 0, nsamp)]
+
+    def l_fe_logmel(self, i, o, k):
+        fe = o["fe"]
+        nmel = fe["mel"].shape[0]
+        tl = [self.tensor("fe/window", fe["window"]), self.tensor("fe/mel", fe["mel"]),
+              self.tensor("fe/consts", np.array([fe["floor"], fe["scale"]], np.float32))]
+        ob = self.buf(F32, logmel_frames(fe), nmel, 1)
+        self.emit(OPC_FE_LOGMEL, [0, ob], tl, [fe["nsamp"], fe["frame"], fe["hop"], fe["pad"], fe["nfft"], nmel], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+    def out_for_dw(self, o, ho, wo, co):
+        cons = self.uses.get(o["out"], [])
+        if len(cons) == 1 and cons[0]["op"] == "DWCONV" and co % 8 == 0:
+            hk = (cons[0]["k"][0] - 1) // 2
+            return self.buf(F16, ho, wo, co, ld=co, halo=hk), wo, hk, co
+        ldo = _r8(co)
+        return self.buf(F16, ho, wo, co, ld=ldo), 0, 0, ldo
+
+    def l_conv(self, i, o, k):
+        w, b = o["w"], o["b"]
+        co = w.shape[0]
+        ib = self.vbuf[o["ins"][0]]
+        dt, h_in, w_in, _, ld, _, _ = self.bufs[ib]
+        if o["k"] != [1, 1]:  # the stem: dense k x k VALID conv on the 1-channel fp32 image
+            kk, st = o["k"][0], o["s"][0]
+            ho, wo = self.vshape[o["out"]]
+            taps = kk * kk
+            k_pad = (taps + 3) & ~3
+            panels, bb, shp = self.pack_f32(w.reshape(co, taps), b, k_pad)
+            tl = [self.tensor(f"f32/stem.{k}.w", panels), self.tensor(f"f32/stem.{k}.b", bb)]
+            ob, _, opad, ldo = self.out_for_dw(o, ho, wo, co)
+            col = self.buf(F32, _r8(ho * wo), 1, k_pad)
+            tmp = self.buf(F32, ho * wo, 1, shp[3])
+            act = {None: 0, "swish": 1, "relu": 2}[o.get("act")]
+            self.emit(OPC_PERCH["STEM"], [ib, ob, col, tmp], tl,
+                      list(shp) + [h_in, w_in, ho, wo, kk, st, act, ldo, opad], o)
+            self.vbuf[o["out"]] = ob
+            return i + 1
+        tl, shp = self.gemm_tensors(f"pw.{k}", w[:, :, 0, 0], b, _r8(w.shape[1]))
+        ob, ow, opad, ldo = self.out_for_dw(o, h_in, w_in, co)
+        rb, ldr = -1, 0
+        if o.get("res"):
+            rb = self.vbuf[o["res"]]
+            ldr = self.bufs[rb][4]
+        act = {None: 0, "swish": 1, "relu": 2}[o.get("act")]
+        self.emit(OPC_F16["PW"], [ib, ob, rb], tl, list(shp) + [h_in * w_in, ld, act, ldo, ow, opad, ldr], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+    def l_dwconv(self, i, o, k):
+        kk, st, pads = o["k"][0], o["s"][0], o["pads"]
+        ib = self.vbuf[o["ins"][0]]
+        _, h, w, c, ld, halo, _ = self.bufs[ib]
+        pt, pl, pb, pr = pads
+        ho, wo = self.vshape[o["out"]]
+        self.bufs.append((F32, 1, 1, c, c, 0, c))
+        cs = len(self.bufs) - 1
+        ob = self.buf(F16, ho, wo, c)
+        w9 = o["w"][:, 0].transpose(1, 2, 0).reshape(kk * kk, c)
+        if kk == 3 and halo == 1 and ld == c and max(pads) <= 1 and c <= 2048:
+            tl = [self.tensor(f"f16/dw.{k}.w", w9.astype(np.float16)),
+                  self.tensor(f"f16/dw.{k}.b", o["b"].astype(np.float16))]
+            self.emit(OPC_F16["DW3"], [ib, ob, cs], tl, [h, w, c, st, ho, wo, pt, pl], o)
+        else:
+            hk = (kk - 1) // 2
+            if halo != hk or ld != c:  # dw_input: a PAD into a buffer with halo hk and ld == C
+                pb_ = self.buf(F16, h, w, c, ld=c, halo=hk)
+                self.emit(OPC_PERCH["PAD"], [ib, pb_], [], [h, w, c, ld, hk], o)
+                ib = pb_
+            tl = [self.tensor(f"f16/dw.{k}.w", w9.astype(np.float16)),
+                  self.tensor(f"f16/dw.{k}.b", o["b"].astype(np.float16))]
+            self.emit(OPC_PERCH["DWK"], [ib, ob, cs], tl, [h, w, c, kk, st, pt, pl, ho, wo, 1], o)
+        self.vbuf[o["out"]] = ob
+        self.chsum = (ob, cs)
+        return i + 1
+
+    def l_mean(self, i, o, k):
+        ib = self.vbuf[o["ins"][0]]
+        _, h, w, c, ld, _, _ = self.bufs[ib]
+        ob = self.buf(F32, 1, 1, c)
+        self.emit(OPC_PERCH["MEAN"], [ib, ob], [], [h * w, c, ld], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+    def l_proto(self, i, o, k):
+        ib = self.vbuf[o["ins"][0]]
+        _, h, w, c, ld, _, _ = self.bufs[ib]
+        n_proto = o["P"].shape[0]
+        nc, ppc = o["cw"].shape
+        qp, sw, _ = pack_proto_s8_sdot(o["P"])
+        n_pad = qp.shape[0] * 12
+        tl = [self.tensor(f"s8/proto.{k}.q", qp), self.tensor(f"s8/proto.{k}.s", sw),
+              self.tensor(f"cls.{k}.w", o["cw"]), self.tensor(f"cls.{k}.b", o["cb"]),
+              self.tensor(f"cls.{k}.eps", np.array([o["eps"]], np.float32))]
+        ob = self.buf(F32, 1, 1, nc)
+        ab = self.buf(I8, h * w, 1, c)
+        cm = self.buf(F32, 1, 1, n_pad)
+        self.emit(OPC_PERCH["PROTO_F16S8"], [ib, ob, ab, cm], tl, [n_proto, c, n_pad, h * w, c, ld, nc, ppc], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+
+def write_perch_package(dst, ir):
+    """Lowers perch_ir()'s result for the neon-fp16 path with the int8 SDOT prototype head and writes the package
+    (hwcap fp16 | dotprod, as the reference compiler sets it for a path with variant-2 ops); returns (n_classes,
+    emb_dim, n_samples)."""
+    ops, vshape, logits, emb, fe = ir
+    lw = _PerchF16Lowering(ops, fe["nsamp"])
+    lw.vshape = vshape
+    lw.run()
+    ob, eb = lw.vbuf[logits], lw.vbuf[emb]
+    n_classes, emb_dim = lw.bufs[ob][3], lw.bufs[eb][3]
+    bufs = plan_slots(lw.bufs, lw.records, [ob, eb])
+    meta = [(f"src_nodes/{PATH_F16}", "\n".join(lw.src))] + metadata(
+        n_classes, emb_dim, labels_for(n_classes), model_id="perch_v2_synthetic", family=BNN_MODEL_PERCH_V2,
+        sample_rate=PERCH_SAMPLE_RATE, n_samples=fe["nsamp"],
+        attribution="synthetic Perch-v2-architecture model (random weights)")
+    write_package(dst, meta, lw.tensors, [(PATH_F16, 3, bufs, lw.records, 0, ob, eb)])
+    return n_classes, emb_dim, fe["nsamp"]
+
+
+def make_perch_package(dst, seed=0, mini=False, n_classes=None, ppc=None):
+    """A synthetic Perch-v2-architecture neon-fp16 package with the int8 prototype head at dst; returns (n_classes,
+    emb_dim, n_samples)."""
+    return write_perch_package(dst, perch_ir(seed, mini, n_classes, ppc))
+
+
 # ------------------------------------------------------------------ audio
 
 def audio(n, seed=0, n_samples=NSAMP, rate=SAMPLE_RATE):

@@ -206,6 +206,24 @@ int bnnk_peak_hfma2(int blocks, int iters, uint32_t *out, bnn_stream_t st);
 int bnnk_dense_f32(int B, int N, const float *feat, long long fws, const float *W, const float *bias, float *out,
                    long long ows, bnn_stream_t st);
 
+/* ---- compiled models' fp16 bodies (Perch v2) */
+/* STEM f32 -> f16: img [B][H][W] fp32 (window stride iws), w the fp32 GEMM panels [Np/8][Kp][8], b [Np]; out fp16
+ * at the padded position (halo opad, channel stride ldo, window stride ows) */
+int bnnk_stem_f16(int B, const float *img, long long iws, int W, int k, int s, int Ho, int Wo, const float *w,
+                  const float *b, int N, int Kp, int Np, int act, uint16_t *out, long long ows, int ldo, int opad,
+                  bnn_stream_t st);
+/* DWK f16: xp [B] zero-haloed by (k - 1) / 2 with channel stride C, w [k*k][C], b [C] fp16 -> out [B][Ho][Wo][C],
+ * chsum [B][C] fp32 */
+int bnnk_dwk_f16(int B, const uint16_t *xp, long long xws, int W, int C, int k, int s, int pt, int pl,
+                 const uint16_t *w, const uint16_t *b, int act, uint16_t *out, long long ows, int Ho, int Wo,
+                 float *chsum, long long cws, bnn_stream_t st);
+/* PAD f16: x [B][H][W] (channel stride ld) into the interior of xp [B][H+2h][W+2h][C] */
+int bnnk_pad_f16(int B, int H, int W, int C, int ld, int h, const uint16_t *x, long long xws, uint16_t *xp,
+                 long long pws, bnn_stream_t st);
+/* MEAN f16: x [B][P][ld] -> out [B][C] fp32 */
+int bnnk_mean_f16(int B, int P, int C, int ld, const uint16_t *x, long long xws, float *out, long long ows,
+                  bnn_stream_t st);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,6 +4,7 @@
 // rounded where it rounds), so the values are bit-identical; only the parallel schedule is ours, and no reference
 // reduction is split across threads except where its order is restated exactly.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <stdint.h>
@@ -491,6 +492,57 @@ __global__ void __launch_bounds__(kPcThreads) k_postpc_gemm(int B, const float *
       make_float4(__fmul_rn(s[0], k6), __fmul_rn(s[1], k6), __fmul_rn(s[2], k6), __fmul_rn(s[3], k6));
 }
 
+// ------------------------------------------------------------------ STEM, fp32 math to fp16 (src/rt_ops_f16.c:175-190)
+//
+// The dense k x k VALID conv of compiled models on a 1-channel fp32 image (Perch's stem): the reference builds the
+// im2col rows (taps (ky, kx) in order, zeros up to Kp; src/pc_kern_f32.c:151-161) and runs its fp32 GEMM (one
+// accumulator per output from +0, fused multiply-adds over all Kp taps in order, + bias, SiLU polynomial or FMAX(x, 0);
+// src/gemm_f32.c:100-132), then rounds the outputs to fp16 into the zero-haloed buffer (pc_cvt_pad_f16,
+// src/pc_kern_f16.c:104-113). Thread (pixel, 8-channel panel): the taps are read from the image as the GEMM consumes
+// them (no im2col buffer), the panel's weights and bias sit in shared memory.
+__global__ void __launch_bounds__(256) k_stem_f16(const float *__restrict__ img, long long iws, int W, int k, int s,
+                                                  int Ho, int Wo, const float *__restrict__ wt,
+                                                  const float *__restrict__ bias, int N, int Kp, int Np, int act,
+                                                  uint16_t *__restrict__ out, long long ows, int ldo, int opad) {
+  extern __shared__ float sw[];  // [Np/8][Kp][8] weights, then [Np] bias
+  __shared__ uint32_t lut[256];
+  const int tid = threadIdx.x;
+  for (int i = tid; i < 256; i += blockDim.x) lut[i] = g_frecpe_lut[i];
+  for (int i = tid; i < Np * Kp; i += blockDim.x) sw[i] = wt[i];
+  for (int i = tid; i < Np; i += blockDim.x) sw[Np * Kp + i] = bias[i];
+  __syncthreads();
+  const int npan = Np / 8, M = Ho * Wo, K = k * k;
+  const long long win = blockIdx.y;
+  const int item = blockIdx.x * blockDim.x + tid;
+  if (item >= M * npan) return;
+  const int m = item / npan, nb = item - m * npan;
+  const int oy = m / Wo, ox = m - oy * Wo;
+  const float *x = img + win * iws + (long long)(oy * s) * W + ox * s;
+  const float *wp = sw + (size_t)nb * Kp * 8;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) acc[j] = 0.f;
+  int ky = 0, kx = 0;
+  for (int t = 0; t < Kp; t++) {
+    float v = 0.f;
+    if (t < K) {
+      v = __ldg(x + ky * W + kx);
+      if (++kx == k) { kx = 0; ky++; }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc[j] = __fmaf_rn(v, wp[t * 8 + j], acc[j]);
+  }
+  uint16_t *o = out + win * ows + ((long long)(oy + opad) * (Wo + 2 * opad) + ox + opad) * ldo + nb * 8;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    if (nb * 8 + j >= N) break;
+    float y = __fadd_rn(acc[j], sw[Np * Kp + nb * 8 + j]);
+    if (act == 1) y = silu<true>(y, lut);
+    else if (act == 2) y = fmax_nan(y, 0.f);
+    o[j] = __half_as_ushort(__float2half_rn(y));
+  }
+}
+
 }  // namespace bnn
 
 using namespace bnn;
@@ -613,5 +665,17 @@ extern "C" int bnnk_postpc(int B, const float *X, long long xws, const float *po
   if (B <= 0) return 0;
   k_postpc_im2col<<<B, 256, 0, st>>>(X, xws, post_s, post_b, pcin);
   k_postpc_gemm<<<dim3(1024 / kPcN, (6 * B + kPcM - 1) / kPcM), kPcThreads, 0, st>>>(B, pcin, wt, b, feat, fws);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_stem_f16(int B, const float *img, long long iws, int W, int k, int s, int Ho, int Wo,
+                             const float *w, const float *b, int N, int Kp, int Np, int act, uint16_t *out,
+                             long long ows, int ldo, int opad, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  const size_t smem = sizeof(float) * ((size_t)Np * Kp + Np);
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  const long long items = (long long)Ho * Wo * (Np / 8);
+  k_stem_f16<<<dim3((unsigned)((items + 255) / 256), (unsigned)B), 256, smem, st>>>(img, iws, W, k, s, Ho, Wo, w, b, N,
+                                                                                  Kp, Np, act, out, ows, ldo, opad);
   return cudaGetLastError();
 }

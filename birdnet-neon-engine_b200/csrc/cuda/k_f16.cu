@@ -861,6 +861,128 @@ __global__ void __launch_bounds__(256) k_peak_hfma2(int iters, uint32_t seed, ui
   if (r == 0x12345678u) out[0] = r;
 }
 
+// ------------------------------------------------------------------ DWK f16 (pc_dwk_f16_cr, src/pc_kern_f16.c:16-96)
+//
+// Depthwise k x k (k odd <= 7) on the input zero-haloed by h = (k - 1) / 2, output pixel (oy, ox) reading rows
+// oy s - pt + h + ky and columns ox s - pl + h + kx. The reference walks each output row in groups: four pixels (two
+// chains per pixel, even taps from the bias and odd taps from +0 in (ky, kx) order, then one fp16 add), then a pair,
+// then a single pixel (one chain from the bias); activation 1 = the SiLU table; the group's fp16 sum ((v0 + v1) +
+// (v2 + v3), v0 + v1 or v0) is added to the fp32 channel sum in group order.
+// Thread (channel pair, output row): the row's groups in order, each group's fp16 sum kept in shared memory; after
+// the barrier one thread per pair adds the sums of all rows' groups in order in fp32.
+template <int K, int G>
+__device__ __forceinline__ uint32_t dwk_group(const uint32_t *xr, long long rs, long long cs, int s, const uint32_t *w,
+                                              uint32_t b, int act, const uint32_t *tab01, const uint32_t *tab2,
+                                              uint32_t *o, long long os) {
+  uint32_t a[G], e[G];
+#pragma unroll
+  for (int q = 0; q < G; q++) { a[q] = b; e[q] = 0u; }
+#pragma unroll
+  for (int ky = 0; ky < K; ky++)
+#pragma unroll
+    for (int kx = 0; kx < K; kx++) {
+      const int t = ky * K + kx;
+#pragma unroll
+      for (int q = 0; q < G; q++) {
+        const uint32_t xv = __ldg(xr + ky * rs + ((long long)q * s + kx) * cs);
+        if (G == 4 && (t & 1)) e[q] = hfma2(xv, w[t], e[q]);
+        else a[q] = hfma2(xv, w[t], a[q]);
+      }
+    }
+  uint32_t v[G];
+#pragma unroll
+  for (int q = 0; q < G; q++) {
+    v[q] = G == 4 ? hadd2(a[q], e[q]) : a[q];
+    if (act == 1) v[q] = silu2(v[q], tab01, tab2);
+    o[q * os] = v[q];
+  }
+  if (G == 4) return hadd2(hadd2(v[0], v[1]), hadd2(v[2], v[3]));
+  if (G == 2) return hadd2(v[0], v[1]);
+  return v[0];
+}
+
+template <int K>
+__global__ void __launch_bounds__(256) k_dwk_f16(const uint16_t *__restrict__ xp, long long xws, int W, int C, int s,
+                                                  int pt, int pl, const uint16_t *__restrict__ wt,
+                                                  const uint16_t *__restrict__ bt, int act, uint16_t *__restrict__ out,
+                                                  long long ows, int Ho, int Wo, int ngr, float *__restrict__ chsum,
+                                                  long long cws) {
+  extern __shared__ uint32_t sgs[];  // [Ho * ngr][Lc] group sums
+  __shared__ uint32_t tab01[16], tab2[16];
+  constexpr int KK = K * K, h = (K - 1) / 2;
+  const int Lc = blockDim.x, lane = threadIdx.x, win = blockIdx.y;
+  const int c2 = blockIdx.x * Lc + lane, C2 = C / 2;
+  load_silu_tab(tab01, tab2);
+  __syncthreads();
+  const bool on = c2 < C2;
+  uint32_t w[KK], b = 0u;
+  if (on) {
+    const uint32_t *w32 = reinterpret_cast<const uint32_t *>(wt);
+#pragma unroll
+    for (int t = 0; t < KK; t++) w[t] = __ldg(w32 + t * C2 + c2);
+    b = __ldg(reinterpret_cast<const uint32_t *>(bt) + c2);
+  }
+  const uint32_t *x = reinterpret_cast<const uint32_t *>(xp + (long long)win * xws) + c2;
+  uint32_t *o = reinterpret_cast<uint32_t *>(out + (long long)win * ows) + c2;
+  const long long cs = C2, rs = (long long)(W + 2 * h) * C2;
+  for (int oy = threadIdx.y; oy < Ho; oy += blockDim.y) {
+    if (!on) continue;
+    const uint32_t *xr = x + (long long)(oy * s - pt + h) * rs;
+    uint32_t *orow = o + (long long)oy * Wo * cs;
+    int ox = 0, gi = 0;
+    for (; ox + 4 <= Wo; ox += 4, gi++)
+      sgs[(oy * ngr + gi) * Lc + lane] = dwk_group<K, 4>(xr + (long long)(ox * s - pl + h) * cs, rs, cs, s, w, b, act,
+                                                         tab01, tab2, orow + ox * cs, cs);
+    if (ox + 2 <= Wo) {
+      sgs[(oy * ngr + gi) * Lc + lane] = dwk_group<K, 2>(xr + (long long)(ox * s - pl + h) * cs, rs, cs, s, w, b, act,
+                                                         tab01, tab2, orow + ox * cs, cs);
+      ox += 2;
+      gi++;
+    }
+    if (ox < Wo)
+      sgs[(oy * ngr + gi) * Lc + lane] = dwk_group<K, 1>(xr + (long long)(ox * s - pl + h) * cs, rs, cs, s, w, b, act,
+                                                         tab01, tab2, orow + ox * cs, cs);
+  }
+  __syncthreads();
+  if (threadIdx.y == 0 && on) {
+    float s0 = 0.f, s1 = 0.f;
+    const int n = Ho * ngr;
+    for (int i = 0; i < n; i++) {
+      const uint32_t r = sgs[i * Lc + lane];
+      s0 = __fadd_rn(s0, h_lo(r));
+      s1 = __fadd_rn(s1, h_hi(r));
+    }
+    chsum[(long long)win * cws + 2 * c2] = s0;
+    chsum[(long long)win * cws + 2 * c2 + 1] = s1;
+  }
+}
+
+// ------------------------------------------------------------------ PAD f16 (pc_pad_f16, src/pc_kern_f16.c:98-102)
+// x [H][W] (channel stride ld) into the interior of the zero-haloed xp [H + 2h][W + 2h][C]; the halo is never written
+// (the buffer is zeroed once when it is allocated).
+__global__ void k_pad_f16(int H, int W, int C, int ld, int h, const uint16_t *__restrict__ x, long long xws,
+                          uint16_t *__restrict__ xp, long long pws) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x, n = (long long)H * W * C;
+  if (i >= n) return;
+  const int c = (int)(i % C);
+  const long long pix = i / C;
+  const int y = (int)(pix / W), xx = (int)(pix - (long long)y * W);
+  xp[(long long)blockIdx.y * pws + ((long long)(y + h) * (W + 2 * h) + xx + h) * C + c] =
+      x[(long long)blockIdx.y * xws + pix * ld + c];
+}
+
+// ------------------------------------------------------------------ MEAN f16 (pc_mean_f16, src/pc_kern_f16.c:115-121)
+// per channel: the P pixels converted to fp32 and summed in pixel order from +0, then one IEEE division by P.
+__global__ void k_mean_f16(int P, int C, int ld, const uint16_t *__restrict__ x, long long xws,
+                           float *__restrict__ out, long long ows) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const uint16_t *xr = x + (long long)blockIdx.y * xws + c;
+  float s = 0.f;
+  for (int p = 0; p < P; p++) s = __fadd_rn(s, __half2float(__ushort_as_half(xr[(long long)p * ld])));
+  out[(long long)blockIdx.y * ows + c] = __fdiv_rn(s, (float)P);
+}
+
 }  // namespace bnn
 
 using namespace bnn;
@@ -1007,6 +1129,7 @@ extern "C" int bnnk_dw3_f16(int B, const uint16_t *xp, long long xws, int H, int
   int Lc = C2 <= 64 ? C2 : 64;
   for (int l = 64; l >= 32; l -= 8)  // a lane count that divides the channel pairs, if there is one
     if (C2 > 64 && C2 % l == 0) { Lc = l; break; }
+  while (Lc > 1 && sizeof(uint32_t) * (size_t)Ho * Lc > 48 * 1024) Lc = (Lc + 1) / 2;  // tall maps: fewer lanes
   const int Ry = Ho < 1024 / Lc ? Ho : 1024 / Lc;
   const size_t smem = sizeof(uint32_t) * (size_t)Ho * Lc;
   if (smem > 48 * 1024) return cudaErrorInvalidValue;
@@ -1067,5 +1190,54 @@ extern "C" int bnnk_dense_f32(int B, int N, const float *feat, long long fws, co
                               float *out, long long ows, bnn_stream_t st) {
   if (B <= 0) return 0;
   k_dense_f32<<<(B * N + 127) / 128, 128, 0, st>>>(B, N, feat, fws, W, bias, out, ows);
+  return cudaGetLastError();
+}
+
+// groups per output row of the DWK walk: fours, then a pair, then a single pixel
+static int dwk_groups(int Wo) { return Wo / 4 + (Wo % 4 >= 2) + (Wo % 2); }
+
+extern "C" int bnnk_dwk_f16(int B, const uint16_t *xp, long long xws, int W, int C, int k, int s, int pt, int pl,
+                            const uint16_t *w, const uint16_t *b, int act, uint16_t *out, long long ows, int Ho, int Wo,
+                            float *chsum, long long cws, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  if (C % 2 || xws % 2 || ows % 2 || ((uintptr_t)xp & 3) || ((uintptr_t)out & 3) || ((uintptr_t)w & 3) ||
+      ((uintptr_t)b & 3))
+    return cudaErrorInvalidValue;
+  const int C2 = C / 2, ngr = dwk_groups(Wo);
+  int Lc = C2 < 32 ? C2 : 32;
+  while (Lc > 8 && (size_t)Ho * ngr * Lc * 4 > 96 * 1024) Lc /= 2;
+  const size_t smem = (size_t)Ho * ngr * Lc * 4;
+  if (smem > 96 * 1024) return cudaErrorInvalidValue;
+  const int Ry = Ho < 256 / Lc ? Ho : 256 / Lc;
+  const dim3 grid((C2 + Lc - 1) / Lc, B), blk(Lc, Ry);
+#define BNN_DWK(KK)                                                                                              \
+  do {                                                                                                           \
+    cudaError_t e_ = cudaFuncSetAttribute(k_dwk_f16<KK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (e_) return e_;                                                                                           \
+    k_dwk_f16<KK><<<grid, blk, smem, st>>>(xp, xws, W, C, s, pt, pl, w, b, act, out, ows, Ho, Wo, ngr, chsum, cws); \
+  } while (0)
+  switch (k) {
+  case 1: BNN_DWK(1); break;
+  case 3: BNN_DWK(3); break;
+  case 5: BNN_DWK(5); break;
+  case 7: BNN_DWK(7); break;
+  default: return cudaErrorInvalidValue;
+  }
+#undef BNN_DWK
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_pad_f16(int B, int H, int W, int C, int ld, int h, const uint16_t *x, long long xws, uint16_t *xp,
+                            long long pws, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  const long long n = (long long)H * W * C;
+  k_pad_f16<<<dim3((unsigned)((n + 255) / 256), (unsigned)B), 256, 0, st>>>(H, W, C, ld, h, x, xws, xp, pws);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_mean_f16(int B, int P, int C, int ld, const uint16_t *x, long long xws, float *out, long long ows,
+                             bnn_stream_t st) {
+  if (B <= 0) return 0;
+  k_mean_f16<<<dim3((unsigned)((C + 127) / 128), (unsigned)B), 128, 0, st>>>(P, C, ld, x, xws, out, ows);
   return cudaGetLastError();
 }

@@ -55,7 +55,8 @@ static int path_runs_here(const bnn_pkg *p, int i) {
   static const int codes[] = {BNN_OP_FE_STFT2, BNN_OP_C0POOL, BNN_OP_PW_S8, BNN_OP_DW3, BNN_OP_SE_GATE,
                               BNN_OP_POSTPC, BNN_OP_GEMV_S8, BNN_OP_PROTO_S8, BNN_OP_FE_LOGMEL, BNN_OP_DENSE,
                               BNN_OP_C0POOL_F16, BNN_OP_PW_F16, BNN_OP_DW3_F16, BNN_OP_SE_F16, BNN_OP_POSTPC_F16,
-                              BNN_OP_DENSE_F16};
+                              BNN_OP_DENSE_F16, BNN_OP_STEM_F16, BNN_OP_DWK_F16, BNN_OP_PAD_F16, BNN_OP_MEAN_F16,
+                              BNN_OP_PROTO_F16S8};
   const bnn_path_rec *d = &p->paths[i];
   const uint8_t *q = p->map + d->ops_off, *end = q + d->ops_bytes;
   for (uint32_t k = 0; k < d->n_ops; k++) {

@@ -52,7 +52,11 @@ enum {
 /* the fp16 kernels of the neon-fp16 path: base | variant 1 << 8 (src/rt_pkg.c:320-331, src/rt_ops_f16.c:286-299) */
 enum {
   BNN_OP_C0POOL_F16 = 0x102, BNN_OP_PW_F16 = 0x103, BNN_OP_DW3_F16 = 0x104, BNN_OP_SE_F16 = 0x105,
-  BNN_OP_POSTPC_F16 = 0x106, BNN_OP_DENSE_F16 = 0x107
+  BNN_OP_POSTPC_F16 = 0x106, BNN_OP_DENSE_F16 = 0x107,
+  /* compiled models' fp16 bodies (Perch): STEM = 9, DWK = 10, PAD = 11, MEAN = 12 (src/rt.h:179-182) */
+  BNN_OP_STEM_F16 = 0x109, BNN_OP_DWK_F16 = 0x10a, BNN_OP_PAD_F16 = 0x10b, BNN_OP_MEAN_F16 = 0x10c,
+  /* PROTO = 13 variant 2: the int8 prototype head of the fp16 path (src/rt_ops_f16.c:280-283) */
+  BNN_OP_PROTO_F16S8 = 0x20d
 };
 enum { BNN_ACT_NONE = 0, BNN_ACT_SILU = 1, BNN_ACT_RELU = 2 };
 

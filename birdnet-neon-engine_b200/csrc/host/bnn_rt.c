@@ -376,7 +376,7 @@ static int init_dw3_f16(vctx *v) { /* dw3_init + rt_dw3_check, src/rt_ops_f16.c:
   VREQ(v, (Wo - 1) * s - pl + 1 + 3 <= W + 2);
   if (vneed_haloed(v, 0, BNN_F16, H, W, C, 1)) return -1;
   if (vneed(v, 1, BNN_F16, (size_t)Ho * Wo * C) || vneed(v, 2, BNN_F32, (size_t)C)) return -1;
-  if (Ho > 192) return vbad(v, "%d output rows: the B200 fp16 depthwise kernel takes at most 192", Ho);
+  if (Ho > 12288) return vbad(v, "%d output rows: the B200 fp16 depthwise kernel takes at most 12288", Ho);
   return 0;
 }
 static int init_se_f16(vctx *v) { /* se_init = rt_se_check(F16), src/rt_ops_f16.c:115, src/rt_ops_f32.c:256-266 */
@@ -415,9 +415,109 @@ static int init_dense_f16(vctx *v) {
 }
 static int init_dense_f32(vctx *v) { return init_dense(v, 4); }
 
+/* ---- compiled models' fp16 bodies (src/rt_ops_f16.c:175-218, with the shared checks of src/rt_ops_f32.c) */
+
+static int init_stem_f16(vctx *v) { /* stem_init + rt_stem_f32_check, src/rt_ops_f16.c:175-181, src/rt_ops_f32.c:390-408 */
+  if (vneed_args(v, 4, -1, -1) || vneed_args(v, -1, 2, 13) || v_fpack(v, 0, 0)) return -1;
+  const int *p = v->op->p;
+  const int K = p[1], Kp = p[2], Np = p[3], H = p[4], W = p[5], Ho = p[6], Wo = p[7], k = p[8], s = p[9];
+  const int ldo = p[11], h = p[12];
+  VREQ(v, k >= 1 && s >= 1 && Ho > 0 && Wo > 0);
+  VREQ(v, (Ho - 1) * s + k <= H && (Wo - 1) * s + k <= W); /* VALID conv */
+  VREQ(v, K == k * k);
+  VREQ(v, ldo >= Np);
+  VREQ(v, h >= 0 && h <= 3);
+  VREQ(v, p[10] >= 0 && p[10] <= 2);
+  if (vneed(v, 0, BNN_F32, (size_t)H * W) || vneed(v, 2, BNN_F32, (size_t)R8(Ho * Wo) * Kp)) return -1;
+  const bnn_buf_rec *o = vbd(v, 1);
+  if (!o) return vbad(v, "buffer argument 1 (output) is absent");
+  if (o->halo != (uint32_t)h || o->ld != (uint32_t)ldo || (h && (o->W != (uint32_t)Wo || o->H != (uint32_t)Ho)))
+    return vbad(v, "buffer argument 1 (buffer #%d, output): expected %d x %d, halo %d, ld %d; found %u x %u, halo %u, ld %u",
+                v->op->b[1], Ho, Wo, h, ldo, o->H, o->W, o->halo, o->ld);
+  if (vneed(v, 1, (int)o->dtype, (size_t)(Ho + 2 * h) * (Wo + 2 * h) * ldo) || vneed(v, 1, BNN_F16, 1)) return -1;
+  if (vneed(v, 3, BNN_F32, (size_t)Ho * Wo * Np)) return -1;
+  if (((size_t)Np * Kp + Np) * 4 > 48 * 1024)
+    return vbad(v, "stem GEMM %d x %d: the B200 stem kernel keeps the weights in 48 KB of shared memory", Np, Kp);
+  return 0;
+}
+static int init_dwk_f16(vctx *v) { /* dwk_init = rt_dwk_check(2), src/rt_ops_f16.c:192, src/rt_ops_f32.c:435-451 */
+  if (vneed_args(v, 3, 2, 10)) return -1;
+  const int *p = v->op->p;
+  const int H = p[0], W = p[1], C = p[2], k = p[3], s = p[4], pt = p[5], pl = p[6], Ho = p[7], Wo = p[8];
+  const int h = (k - 1) / 2;
+  VREQ(v, H > 0 && W > 0 && Ho > 0 && Wo > 0 && C > 0);
+  VREQ(v, C % 8 == 0);
+  VREQ(v, k % 2 == 1 && k >= 1 && k <= 7);
+  VREQ(v, s >= 1 && s <= 2);
+  VREQ(v, pt >= 0 && pt <= h && pl >= 0 && pl <= h);
+  VREQ(v, p[9] >= 0 && p[9] <= 1);
+  if (vneed_t(v, 0, (size_t)k * k * C * 2, 0) || vneed_t(v, 1, (size_t)C * 2, 0)) return -1;
+  /* the last tap of the last output stays inside the haloed input */
+  VREQ(v, (Ho - 1) * s - pt + k <= H + 2 * h - h);
+  VREQ(v, (Wo - 1) * s - pl + k <= W + 2 * h - h);
+  if (vneed_haloed(v, 0, BNN_F16, H, W, C, h)) return -1;
+  if (vneed(v, 1, BNN_F16, (size_t)Ho * Wo * C) || vneed(v, 2, BNN_F32, (size_t)C)) return -1;
+  const int groups = Wo / 4 + (Wo % 4 >= 2) + Wo % 2;
+  if ((long long)Ho * groups > 3072)
+    return vbad(v, "%d output rows of %d pixel groups: the B200 depthwise kernel keeps at most 3072 group sums", Ho,
+                groups);
+  return 0;
+}
+static int init_pad(vctx *v) { /* rt_pad_check, src/rt_ops_f32.c:474-492 (pad_f16: src/rt_ops_f16.c:204-208) */
+  if (vneed_args(v, 2, -1, 5)) return -1;
+  const int *p = v->op->p;
+  const bnn_buf_rec *x = vbd(v, 0), *o = vbd(v, 1);
+  if (!x || !o) return vbad(v, "buffer argument %d is absent", x ? 1 : 0);
+  VREQ(v, p[0] > 0 && p[1] > 0 && p[2] > 0);
+  VREQ(v, p[4] >= 1 && p[4] <= 3);
+  VREQ(v, p[3] >= p[2]);
+  if (x->dtype != o->dtype)
+    return vbad(v, "buffer argument 0 (buffer #%d, input) is %s but buffer argument 1 (buffer #%d, output) is %s",
+                v->op->b[0], bnn_dtype_name(x->dtype), v->op->b[1], bnn_dtype_name(o->dtype));
+  if (x->halo) return vbad(v, "buffer argument 0 (buffer #%d, input): expected no halo, found halo %u", v->op->b[0], x->halo);
+  if (o->ld != (uint32_t)p[2] || o->halo != (uint32_t)p[4])
+    return vbad(v, "buffer argument 1 (buffer #%d, output): expected ld %d halo %d, found ld %u halo %u", v->op->b[1],
+                p[2], p[4], o->ld, o->halo);
+  return vneed(v, 0, (int)x->dtype, (size_t)p[0] * p[1] * p[3]) ||
+                 vneed(v, 1, (int)o->dtype, (size_t)(p[0] + 2 * p[4]) * (p[1] + 2 * p[4]) * p[2])
+             ? -1
+             : 0;
+}
+static int init_mean(vctx *v) { /* rt_mean_check, src/rt_ops_f32.c:501-513 (mean_f16: src/rt_ops_f16.c:210-213) */
+  if (vneed_args(v, 2, -1, 3)) return -1;
+  const int *p = v->op->p;
+  VREQ(v, p[0] > 0 && p[1] > 0);
+  VREQ(v, p[1] % 4 == 0);
+  VREQ(v, p[2] >= p[1]);
+  const bnn_buf_rec *x = vbd(v, 0);
+  if (!x) return vbad(v, "buffer argument 0 (input) is absent");
+  if (x->halo) return vbad(v, "buffer argument 0 (buffer #%d, input): expected no halo, found halo %u", v->op->b[0], x->halo);
+  return vneed(v, 0, (int)x->dtype, (size_t)p[0] * p[2]) || vneed(v, 1, BNN_F32, (size_t)p[1]) ? -1 : 0;
+}
+static int init_proto_f16s8(vctx *v) { /* proto8_init (src/rt_ops_f16.c:254-267) after rt_proto_geom / rt_proto_io
+                                        * (src/rt_ops_f32.c:525-545) */
+  if (vneed_args(v, 4, 5, 8)) return -1;
+  const int *p = v->op->p;
+  const int N = p[0], K = p[1], Np = p[2], P = p[3], C = p[4], ld = p[5], nc = p[6], ppc = p[7];
+  VREQ(v, P > 0 && P <= 65536 && nc > 0 && ppc >= 1);
+  VREQ(v, N > 0 && N <= (1 << 26) && K > 0 && K <= (1 << 17));
+  VREQ(v, K == C);
+  VREQ(v, ld >= C);
+  VREQ(v, (size_t)nc * ppc == (size_t)N);
+  VREQ(v, K % 8 == 0);
+  VREQ(v, P % 8 == 0 && Np % 12 == 0 && Np >= N);
+  if (vneed_t(v, 0, (size_t)Np * K, 1) || vneed_t(v, 1, (size_t)Np * 4, 1)) return -1;
+  if (vneed_t(v, 2, (size_t)N * 4, 0) || vneed_t(v, 3, (size_t)nc * 4, 0) || vneed_t(v, 4, 4, 0)) return -1;
+  if (vneed_nohalo(v, 0, BNN_F16, (size_t)P * ld) || vneed(v, 1, BNN_F32, (size_t)nc)) return -1;
+  if (vneed(v, 2, BNN_I8, (size_t)P * K) || vneed(v, 3, BNN_F32, (size_t)Np)) return -1;
+  if (P > 256) v->c->launches += 1; /* the chunk maxima */
+  return 0;
+}
+
 /* the registry of this library: opcode (base | variant << 8) -> kernel; outmask / optmask as the reference's
- * (src/rt_ops_f32.c:620-637, src/rt_ops_s8n.c:255-260, src/rt_ops_f16.c:286-299). Variant 0: the neon-int8 path's
- * ops (and the fp32 head of small models); variant 1: the neon-fp16 path's. The dotprod variant (2) has none. */
+ * (src/rt_ops_f32.c:620-637, src/rt_ops_s8n.c:255-260, src/rt_ops_f16.c:280-299). Variant 0: the neon-int8 path's
+ * ops (and the fp32 head of small models); variant 1: the neon-fp16 path's; variant 2: the int8 prototype head of
+ * the neon-fp16 path (the reference's SDOT head, rt_k_f16_s8). */
 typedef struct {
   int code;
   const char *name;
@@ -442,6 +542,11 @@ static const kdesc KERNELS[] = {
     {BNN_OP_SE_F16, "se_f16", init_se_f16, 0x1, 0, 2},
     {BNN_OP_POSTPC_F16, "postpc_f16", init_postpc_f16, 0xe, 0, 3},
     {BNN_OP_DENSE_F16, "dense_f16", init_dense_f16, 0x2, 0, 1},
+    {BNN_OP_STEM_F16, "stem_f32to16", init_stem_f16, 0xe, 0, 1},
+    {BNN_OP_DWK_F16, "dwk_f16", init_dwk_f16, 0x6, 0, 1},
+    {BNN_OP_PAD_F16, "pad_f16", init_pad, 0x2, 0, 1},
+    {BNN_OP_MEAN_F16, "mean_f16", init_mean, 0x2, 0, 1},
+    {BNN_OP_PROTO_F16S8, "proto_s8", init_proto_f16s8, 0xe, 0, 3},
 };
 static const kdesc *kernel_for(int code) {
   for (size_t i = 0; i < sizeof KERNELS / sizeof KERNELS[0]; i++)
@@ -593,13 +698,15 @@ static int upload(void **dst, const void *src, size_t bytes, char *err, size_t e
   if (bytes) CK(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice), "weight upload (cudaMemcpy)");
   return 0;
 }
-/* the buffer arguments [lo, lo + n) of an op that the device scratch replaces: PW_S8 b[3..5], GEMV_S8 b[2..4] (q, sa,
- * za), PROTO_S8 b[2] (the quantized cells) */
+/* the buffer arguments [lo, lo + n) of an op that the device scratch replaces or that its kernels never touch:
+ * PW_S8 b[3..5], GEMV_S8 b[2..4] (q, sa, za), PROTO_S8 and PROTO variant 2 b[2] (the quantized cells), STEM f16 b[2..3]
+ * (the im2col rows and the fp32 GEMM output: the kernel reads the image and writes fp16 directly) */
 static void scratch_args(const bnn_op *op, int *lo, int *n) {
-  *lo = op->code == BNN_OP_PW_S8 ? 3 : op->code == BNN_OP_GEMV_S8 || op->code == BNN_OP_PROTO_S8 ? 2 : -1;
-  *n = op->code == BNN_OP_PROTO_S8 ? 1 : 3;
+  const int proto = op->code == BNN_OP_PROTO_S8 || op->code == BNN_OP_PROTO_F16S8;
+  *lo = op->code == BNN_OP_PW_S8 ? 3 : op->code == BNN_OP_GEMV_S8 || proto || op->code == BNN_OP_STEM_F16 ? 2 : -1;
+  *n = proto ? 1 : op->code == BNN_OP_STEM_F16 ? 2 : 3;
 }
-static int is_int8_scratch(const bnn_ctx *c, int buf) {
+static int is_scratch(const bnn_ctx *c, int buf) {
   for (int i = 0; i < c->n_ops; i++) {
     const bnn_op *op = &c->ops[i];
     int lo, n;
@@ -961,6 +1068,17 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
   case BNN_OP_DENSE_F16:
     return upload((void **)&d->hw, tptr(c, op, 0), sizeof(uint16_t) * 1024 * (size_t)p[0], err, errlen, kind) ||
            upload((void **)&d->f[0], tptr(c, op, 1), sizeof(float) * (size_t)p[0], err, errlen, kind);
+  case BNN_OP_STEM_F16: /* t = [w panels [Np/8][Kp][8], b [Np]] fp32, used as they are */
+    return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * (size_t)p[3] * p[2], err, errlen, kind) ||
+           upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * (size_t)p[3], err, errlen, kind);
+  case BNN_OP_DWK_F16: {
+    const int C = p[2], k = p[3];
+    return upload((void **)&d->hw, tptr(c, op, 0), sizeof(uint16_t) * (size_t)k * k * C, err, errlen, kind) ||
+           upload((void **)&d->hb, tptr(c, op, 1), sizeof(uint16_t) * C, err, errlen, kind);
+  }
+  case BNN_OP_PROTO_F16S8: /* t = [qw [Np/12][K/4][12][4], sw, cls w, cls b, eps]; p = [N K Np, P C ld nc ppc] */
+    return bnn_proto_weights_l(d, 1, p[0], p[1], R16(p[1]), p[2], tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2),
+                               tptr(c, op, 3), p[6], ((const float *)tptr(c, op, 4))[0], err, errlen, kind);
   case BNN_OP_DENSE:
     return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * 1024 * (size_t)p[0], err, errlen, kind) ||
            upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * (size_t)p[0], err, errlen, kind);
@@ -1000,7 +1118,7 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
   if (!slot_bytes || !slot_off) { free(slot_bytes); free(slot_off); *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory"); return -1; }
   for (uint32_t i = 0; i < d->n_buf; i++) {
     const bnn_buf_rec *b = &c->bufd[i];
-    if (i == d->in_buf || b->halo || is_int8_scratch(c, (int)i)) continue;
+    if (i == d->in_buf || b->halo || is_scratch(c, (int)i)) continue;
     const size_t bytes = ((size_t)b->elems * dsize(b->dtype) + 255) & ~(size_t)255;
     if (bytes > slot_bytes[b->slot]) slot_bytes[b->slot] = bytes;
   }
@@ -1021,7 +1139,7 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
       e = cudaMalloc(&dv->priv[i], (size_t)dv->ws[i] * es * B);
       if (!e) e = cudaMemset(dv->priv[i], 0, (size_t)dv->ws[i] * es * B);
       dv->buf[i] = dv->priv[i];
-    } else if (!is_int8_scratch(c, (int)i)) {
+    } else if (!is_scratch(c, (int)i)) {
       dv->ws[i] = (long long)(slot_bytes[b->slot] / es);
       dv->buf[i] = (uint8_t *)dv->arena + slot_off[b->slot];
     }
@@ -1033,6 +1151,12 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
   size_t qbytes = 256, rows = 8;
   for (int i = 0; i < c->n_ops; i++) {
     const bnn_op *op = &c->ops[i];
+    if (op->code == BNN_OP_PROTO_F16S8) { /* p = [N K Np, P C ld nc ppc]: cells of K rounded up to 16 */
+      const size_t r = (size_t)B * op->p[3], qb = r * (size_t)R16(op->p[1]);
+      if (qb > qbytes) qbytes = qb;
+      if (r > rows) rows = r;
+      continue;
+    }
     if (op->code != BNN_OP_PW_S8 && op->code != BNN_OP_GEMV_S8 && op->code != BNN_OP_PROTO_S8) continue;
     const size_t r = (size_t)B * (op->code == BNN_OP_GEMV_S8 ? 1 : (size_t)op->p[4]);
     const size_t qb = r * (op->code == BNN_OP_PROTO_S8 ? (size_t)op->p[2] : (size_t)R32(op->p[1]));
@@ -1068,15 +1192,17 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
         return -1;
       }
     }
-    if (op->code == BNN_OP_PROTO_S8) {
+    if (op->code == BNN_OP_PROTO_S8 || op->code == BNN_OP_PROTO_F16S8) {
       bnn_devop *o = &dv->ops[i];
-      if (bnnk_proto_plan_init(&o->pplan, o->w, op->p[3], op->p[2], dv->q, B, op->p[4])) {
+      const int v2 = op->code == BNN_OP_PROTO_F16S8;
+      const int np = v2 ? op->p[2] : op->p[3], kp = v2 ? R16(op->p[1]) : op->p[2], P = v2 ? op->p[3] : op->p[4];
+      if (bnnk_proto_plan_init(&o->pplan, o->w, np, kp, dv->q, B, P)) {
         *kind = BNN_ERR_CPU;
         snprintf(err, errlen, "op %d %s: TMA descriptors could not be made (driver too old?)", i, op->kname);
         return -1;
       }
       if (!o->pplan.wt)
-        CK(cudaMalloc((void **)&o->f[0], sizeof(float) * (size_t)B * o->pplan.nch * op->p[3]), "prototype scratch");
+        CK(cudaMalloc((void **)&o->f[0], sizeof(float) * (size_t)B * o->pplan.nch * np), "prototype scratch");
     }
   }
   CK(cudaDeviceSynchronize(), "device set-up");
@@ -1246,6 +1372,27 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
     case BNN_OP_DENSE:
       rc = bnnk_dense_f32(n, p[0], B_(0), WS(0), o->f[0], o->f[1], B_(1), WS(1), st);
       break;
+    case BNN_OP_STEM_F16:
+      rc = bnnk_stem_f16(n, B_(0), WS(0), p[5], p[8], p[9], p[6], p[7], o->f[0], o->f[1], p[0], p[2], p[3], p[10],
+                         B_(1), WS(1), p[11], p[12], st);
+      break;
+    case BNN_OP_DWK_F16:
+      rc = bnnk_dwk_f16(n, B_(0), WS(0), p[1], p[2], p[3], p[4], p[5], p[6], o->hw, o->hb, p[9], B_(1), WS(1), p[7],
+                        p[8], B_(2), WS(2), st);
+      break;
+    case BNN_OP_PAD_F16:
+      rc = bnnk_pad_f16(n, p[0], p[1], p[2], p[3], p[4], B_(0), WS(0), B_(1), WS(1), st);
+      break;
+    case BNN_OP_MEAN_F16:
+      rc = bnnk_mean_f16(n, p[0], p[1], p[2], B_(0), WS(0), B_(1), WS(1), st);
+      break;
+    case BNN_OP_PROTO_F16S8:
+      rc = bnnk_proto_quant_h(n, p[3], B_(0), WS(0), p[5], p[1], R16(p[1]), o->eps, dv->q, dv->sa, st);
+      if (!rc) rc = bnnk_proto_colmax(&o->pplan, n, dv->sa, o->sw, B_(3), WS(3), o->f[0], dv->err, st);
+      if (!rc)
+        rc = bnnk_proto_logits(n, p[6], p[7], B_(3), WS(3), o->f[1], o->f[2], B_(1), WS(1), NULL, dv->err + 1,
+                               dv->w_base, st);
+      break;
     default:
       rc = cudaErrorNotSupported;
     }
@@ -1271,7 +1418,8 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
  * second is captured on the context's own stream, thread-locally, then launched on the caller's stream. */
 int bnn_window_fail_op(const bnn_ctx *c) {
   for (int i = 0; i < c->n_ops; i++)
-    if (c->ops[i].code == BNN_OP_PROTO_S8 || c->ops[i].code == BNN_OP_POSTPC_F16) return i;
+    if (c->ops[i].code == BNN_OP_PROTO_S8 || c->ops[i].code == BNN_OP_PROTO_F16S8 || c->ops[i].code == BNN_OP_POSTPC_F16)
+      return i;
   return -1;
 }
 

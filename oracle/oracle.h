@@ -135,6 +135,14 @@ int bnno_postpc_f16(const uint16_t *X, const float *post_s, const float *post_b,
 void bnno_dense_f16(const uint16_t *W, const float *bias, int N, const float *feat, float *out);
 void bnno_dense_f32(const float *W, const float *bias, int N, const float *feat, float *out);
 
+/* ---- compiled models' fp16 bodies (oracle_perch.c) */
+void bnno_stem_f16(const float *img, int H, int W, int k, int s, int Ho, int Wo, const float *w, const float *b, int N,
+                   int Kp, int act, uint16_t *out, int ldo, int opad);
+void bnno_dwk_f16(const uint16_t *xp, int H, int W, int C, int k, int s, int pt, int pl, const uint16_t *w,
+                  const uint16_t *b, int act, uint16_t *out, int Ho, int Wo, float *chsum);
+void bnno_pad_f16(const uint16_t *x, int H, int W, int C, int ld, int h, uint16_t *xp);
+void bnno_mean_f16(const uint16_t *x, int P, int C, int ld, float *out);
+
 /* ---- a .bnpk package run on the CPU, window by window (the executor of src/rt_pkg.c:528-542) */
 typedef struct bnno_pkg bnno_pkg;
 /* path: the package; path_name: the package path to run ("neon-int8"). NULL on failure (err filled). */

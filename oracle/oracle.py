@@ -1,5 +1,5 @@
-"""ctypes wrapper of liboracle.so, the CPU restatement of the reference's v2.4 neon-int8 and neon-fp16 paths (TEST
-INFRASTRUCTURE).
+"""ctypes wrapper of liboracle.so, the CPU restatement of the reference's v2.4 neon-int8 and neon-fp16 paths and
+the fp16 bodies of compiled models (TEST INFRASTRUCTURE).
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs use this module; the product library never
 does. `make -C oracle` builds liboracle.so.
@@ -48,6 +48,10 @@ SIGS = {
     "bnno_c0pool_f16": (None, [_P, _P, _P, _P]),
     "bnno_dw3_f16": (None, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
     "bnno_se_f16": (None, [_I, _I, _P, _P, _P, _P, _P, _I, _P]),
+    "bnno_stem_f16": (None, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P, _I, _I]),
+    "bnno_dwk_f16": (None, [_P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _I, _I, _P]),
+    "bnno_pad_f16": (None, [_P, _I, _I, _I, _I, _I, _P]),
+    "bnno_mean_f16": (None, [_P, _I, _I, _I, _P]),
     "bnno_postpc_f16": (_I, [_P, _P, _P, _P, _P, _P, _P]),
     "bnno_dense_f16": (None, [_P, _P, _I, _P, _P]), "bnno_dense_f32": (None, [_P, _P, _I, _P, _P]),
 }

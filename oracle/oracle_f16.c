@@ -34,7 +34,7 @@ typedef uint16_t h16;
 
 /* ------------------------------------------------------------------ fp16 arithmetic */
 
-double bnno_h2d(h16 h) {
+static double h2d_calc(h16 h) {
   const int s = h >> 15, e = (h >> 10) & 31, m = h & 1023;
   double v;
   if (e == 31) v = m ? NAN : INFINITY;
@@ -42,6 +42,12 @@ double bnno_h2d(h16 h) {
   else v = ldexp((double)(m | 1024), e - 25);
   return s ? -v : v;
 }
+/* every fp16 value as a double (exact), filled once when the library loads */
+static double H2D[65536];
+__attribute__((constructor)) static void h2d_init(void) {
+  for (int i = 0; i < 65536; i++) H2D[i] = h2d_calc((h16)i);
+}
+double bnno_h2d(h16 h) { return H2D[h]; }
 float bnno_h2f(h16 h) { return (float)bnno_h2d(h); }
 
 /* one rounding of a double to fp16, nearest even; overflow to infinity; NaN -> the default NaN */
@@ -137,33 +143,55 @@ static void kblocks(int Kp, int *nblk, int *bs) {
   *bs = ((Kp + *nblk - 1) / *nblk + 7) & ~7;
 }
 
-/* the pre-activation value of output (row a, column n): K blocks, fp16 chains, fp32 flushes, bias */
-static h16 gemm_pre(const h16 *a, const h16 *w, const float *b32, const h16 *b16, int Kp, int Np, int n) {
+/* the pre-activation values of R outputs of one column from their input rows a[r] and the weight column wc [Kp]:
+ * K blocks, fp16 chains, fp32 flushes, bias (the R chains are independent: computed side by side for speed) */
+#define GEMM_R 4
+static void gemm_pre(const h16 *const *a, int R, const h16 *wc, float b32, h16 b16, int Kp, h16 *v) {
   int nblk, bs;
   kblocks(Kp, &nblk, &bs);
-  float fb = 0.f;
-  h16 cb = 0;
+  float fb[GEMM_R] = {0.f, 0.f, 0.f, 0.f};
+  h16 cb[GEMM_R] = {0, 0, 0, 0};
   for (int kb = 0; kb < Kp; kb += bs) {
     const int kn = Kp - kb < bs ? Kp - kb : bs;
-    cb = 0;
-    for (int k = kb; k < kb + kn; k++) cb = bnno_h_fma(hp_w(w, Kp, Np, n, k), a[k], cb);
-    if (nblk > 1) fb = fb + bnno_h2f(cb);
+    for (int r = 0; r < GEMM_R; r++) cb[r] = 0;
+    if (R == GEMM_R)
+      for (int k = kb; k < kb + kn; k++) {
+        const h16 wk = wc[k];
+        for (int r = 0; r < GEMM_R; r++) cb[r] = bnno_h_fma(wk, a[r][k], cb[r]);
+      }
+    else
+      for (int r = 0; r < R; r++)
+        for (int k = kb; k < kb + kn; k++) cb[r] = bnno_h_fma(wc[k], a[r][k], cb[r]);
+    if (nblk > 1)
+      for (int r = 0; r < R; r++) fb[r] = fb[r] + bnno_h2f(cb[r]);
   }
-  return nblk > 1 ? bnno_f2h(fb + b32[n]) : bnno_h_add(cb, b16[n]);
+  for (int r = 0; r < R; r++) v[r] = nblk > 1 ? bnno_f2h(fb[r] + b32) : bnno_h_add(cb[r], b16);
 }
 
 void bnno_gemm_f16(const h16 *A, int lda, int M, const h16 *w, const float *b32, const h16 *b16, int Kp, int Np,
                    int act, h16 *out, int ldo, int ow, int opad, const h16 *res, int ldr) {
-  for (int m = 0; m < M; m++) {
-    const size_t orow = opad ? (size_t)((m / ow) + opad) * (ow + 2 * opad) + (m % ow) + opad : (size_t)m;
-    for (int n = 0; n < Np; n++) {
-      h16 v = gemm_pre(A + (size_t)m * lda, w, b32, b16, Kp, Np, n);
-      if (act == 1) v = bnno_h_silu(v);
-      else if (act == 2) v = h_max(v, 0);
-      if (res) v = bnno_h_add(v, res[(size_t)m * ldr + n]);
-      out[orow * ldo + n] = v;
+  h16 *wc = malloc(sizeof(h16) * (size_t)Kp);
+  if (!wc) return;
+  for (int n = 0; n < Np; n++) { /* every output is computed on its own: column by column */
+    for (int k = 0; k < Kp; k++) wc[k] = hp_w(w, Kp, Np, n, k);
+    for (int m0 = 0; m0 < M; m0 += GEMM_R) {
+      const int R = M - m0 < GEMM_R ? M - m0 : GEMM_R;
+      const h16 *rows[GEMM_R];
+      h16 vv[GEMM_R];
+      for (int r = 0; r < R; r++) rows[r] = A + (size_t)(m0 + r) * lda;
+      gemm_pre(rows, R, wc, b32[n], b16[n], Kp, vv);
+      for (int r = 0; r < R; r++) {
+        const int m = m0 + r;
+        const size_t orow = opad ? (size_t)((m / ow) + opad) * (ow + 2 * opad) + (m % ow) + opad : (size_t)m;
+        h16 v = vv[r];
+        if (act == 1) v = bnno_h_silu(v);
+        else if (act == 2) v = h_max(v, 0);
+        if (res) v = bnno_h_add(v, res[(size_t)m * ldr + n]);
+        out[orow * ldo + n] = v;
+      }
     }
   }
+  free(wc);
 }
 
 /* ------------------------------------------------------------------ C0POOL f16 */

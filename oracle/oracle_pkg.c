@@ -226,6 +226,33 @@ static int run_op(bnno_pkg *p, const o_op *op) {
   case 7: /* DENSE f32 */
     bnno_dense_f32(tdata(p, op, 0), tdata(p, op, 1), P[0], bptr(p, op, 0), bptr(p, op, 1));
     return 0;
+  case 0x109: /* STEM f32 -> f16: b = [img, out, col, tmp]; t = [w, b]; p = [N K Kp Np H W Ho Wo k s act ldo opad] */
+    bnno_stem_f16(bptr(p, op, 0), P[4], P[5], P[8], P[9], P[6], P[7], tdata(p, op, 0), tdata(p, op, 1), P[0], P[2],
+                  P[10], bptr(p, op, 1), P[11], P[12]);
+    return 0;
+  case 0x10a: /* DWK f16: b = [xp, out, chsum]; t = [w, b]; p = [H W C k s pt pl Ho Wo act] */
+    bnno_dwk_f16(bptr(p, op, 0), P[0], P[1], P[2], P[3], P[4], P[5], P[6], tdata(p, op, 0), tdata(p, op, 1), P[9],
+                 bptr(p, op, 1), P[7], P[8], bptr(p, op, 2));
+    return 0;
+  case 0x10b: /* PAD f16: b = [x, xp]; p = [H W C ld h] */
+    bnno_pad_f16(bptr(p, op, 0), P[0], P[1], P[2], P[3], P[4], bptr(p, op, 1));
+    return 0;
+  case 0x10c: /* MEAN f16: b = [x, out f32]; p = [P C ld] */
+    bnno_mean_f16(bptr(p, op, 0), P[0], P[1], P[2], bptr(p, op, 1));
+    return 0;
+  case 0x20d: { /* PROTO, int8 SDOT head of the fp16 path: b = [x f16, logits, qa, colmax];
+                 * t = [qw [Np/12][K/4][12][4], sw, cls w, cls b, eps]; p = [N K Np, P C ld nc ppc] */
+    float *sx = malloc(sizeof(float) * (size_t)P[3]);
+    int8_t *rows = malloc((size_t)P[2] * (size_t)P[1]);
+    if (!sx || !rows) { free(sx); free(rows); return -1; }
+    const float *eps = tdata(p, op, 4);
+    bnno_proto_quant_cells_f16(bptr(p, op, 0), P[3], P[4], P[5], eps[0], bptr(p, op, 2), sx);
+    bnno_proto_unpack12(tdata(p, op, 0), P[2], P[1], rows);
+    bnno_proto_colmax_rows(bptr(p, op, 2), P[1], sx, P[3], rows, tdata(p, op, 1), P[2], bptr(p, op, 3));
+    free(sx);
+    free(rows);
+    return bnno_proto_logits(bptr(p, op, 3), tdata(p, op, 2), tdata(p, op, 3), P[6], P[7], bptr(p, op, 1));
+  }
   default:
     return -1;
   }
