@@ -868,8 +868,9 @@ __global__ void __launch_bounds__(256) k_peak_hfma2(int iters, uint32_t seed, ui
 // chains per pixel, even taps from the bias and odd taps from +0 in (ky, kx) order, then one fp16 add), then a pair,
 // then a single pixel (one chain from the bias); activation 1 = the SiLU table; the group's fp16 sum ((v0 + v1) +
 // (v2 + v3), v0 + v1 or v0) is added to the fp32 channel sum in group order.
-// Thread (channel pair, output row): the row's groups in order, each group's fp16 sum kept in shared memory; after
-// the barrier one thread per pair adds the sums of all rows' groups in order in fp32.
+// Thread (channel pair, output row): the row's groups in order, each group's fp16 sum kept in shared memory; the
+// block walks the rows in chunks of one row per thread row, and after each chunk's barrier one thread per pair adds
+// the chunk's group sums in row order, then group order, to its fp32 sums.
 template <int K, int G>
 __device__ __forceinline__ uint32_t dwk_group(const uint32_t *xr, long long rs, long long cs, int s, const uint32_t *w,
                                               uint32_t b, int act, const uint32_t *tab01, const uint32_t *tab2,
@@ -903,14 +904,14 @@ __device__ __forceinline__ uint32_t dwk_group(const uint32_t *xr, long long rs, 
 
 template <int K>
 __global__ void __launch_bounds__(256) k_dwk_f16(const uint16_t *__restrict__ xp, long long xws, int W, int C, int s,
-                                                  int pt, int pl, const uint16_t *__restrict__ wt,
-                                                  const uint16_t *__restrict__ bt, int act, uint16_t *__restrict__ out,
-                                                  long long ows, int Ho, int Wo, int ngr, float *__restrict__ chsum,
-                                                  long long cws) {
-  extern __shared__ uint32_t sgs[];  // [Ho * ngr][Lc] group sums
+                                                 int pt, int pl, const uint16_t *__restrict__ wt,
+                                                 const uint16_t *__restrict__ bt, int act, uint16_t *__restrict__ out,
+                                                 long long ows, int Ho, int Wo, int ngr, float *__restrict__ chsum,
+                                                 long long cws) {
+  extern __shared__ uint32_t sgs[];  // [Ry * ngr][Lc] group sums of the current chunk of rows
   __shared__ uint32_t tab01[16], tab2[16];
   constexpr int KK = K * K, h = (K - 1) / 2;
-  const int Lc = blockDim.x, lane = threadIdx.x, win = blockIdx.y;
+  const int Lc = blockDim.x, Ry = blockDim.y, lane = threadIdx.x, win = blockIdx.y;
   const int c2 = blockIdx.x * Lc + lane, C2 = C / 2;
   load_silu_tab(tab01, tab2);
   __syncthreads();
@@ -925,33 +926,39 @@ __global__ void __launch_bounds__(256) k_dwk_f16(const uint16_t *__restrict__ xp
   const uint32_t *x = reinterpret_cast<const uint32_t *>(xp + (long long)win * xws) + c2;
   uint32_t *o = reinterpret_cast<uint32_t *>(out + (long long)win * ows) + c2;
   const long long cs = C2, rs = (long long)(W + 2 * h) * C2;
-  for (int oy = threadIdx.y; oy < Ho; oy += blockDim.y) {
-    if (!on) continue;
-    const uint32_t *xr = x + (long long)(oy * s - pt + h) * rs;
-    uint32_t *orow = o + (long long)oy * Wo * cs;
-    int ox = 0, gi = 0;
-    for (; ox + 4 <= Wo; ox += 4, gi++)
-      sgs[(oy * ngr + gi) * Lc + lane] = dwk_group<K, 4>(xr + (long long)(ox * s - pl + h) * cs, rs, cs, s, w, b, act,
-                                                         tab01, tab2, orow + ox * cs, cs);
-    if (ox + 2 <= Wo) {
-      sgs[(oy * ngr + gi) * Lc + lane] = dwk_group<K, 2>(xr + (long long)(ox * s - pl + h) * cs, rs, cs, s, w, b, act,
-                                                         tab01, tab2, orow + ox * cs, cs);
-      ox += 2;
-      gi++;
+  float s0 = 0.f, s1 = 0.f;  // the channel pair's sums (kept by the threads of row 0 of the block)
+  for (int oy0 = 0; oy0 < Ho; oy0 += Ry) {
+    const int oy = oy0 + threadIdx.y;
+    if (on && oy < Ho) {
+      const uint32_t *xr = x + (long long)(oy * s - pt + h) * rs;
+      uint32_t *orow = o + (long long)oy * Wo * cs;
+      uint32_t *g = sgs + threadIdx.y * ngr * Lc + lane;
+      int ox = 0, gi = 0;
+      for (; ox + 4 <= Wo; ox += 4, gi++)
+        g[gi * Lc] = dwk_group<K, 4>(xr + (long long)(ox * s - pl + h) * cs, rs, cs, s, w, b, act, tab01, tab2,
+                                     orow + ox * cs, cs);
+      if (ox + 2 <= Wo) {
+        g[gi * Lc] = dwk_group<K, 2>(xr + (long long)(ox * s - pl + h) * cs, rs, cs, s, w, b, act, tab01, tab2,
+                                     orow + ox * cs, cs);
+        ox += 2;
+        gi++;
+      }
+      if (ox < Wo)
+        g[gi * Lc] = dwk_group<K, 1>(xr + (long long)(ox * s - pl + h) * cs, rs, cs, s, w, b, act, tab01, tab2,
+                                     orow + ox * cs, cs);
     }
-    if (ox < Wo)
-      sgs[(oy * ngr + gi) * Lc + lane] = dwk_group<K, 1>(xr + (long long)(ox * s - pl + h) * cs, rs, cs, s, w, b, act,
-                                                         tab01, tab2, orow + ox * cs, cs);
+    __syncthreads();
+    if (threadIdx.y == 0 && on) {  // the chunk's group sums in row order, then group order
+      const int n = min(Ry, Ho - oy0) * ngr;
+      for (int i = 0; i < n; i++) {
+        const uint32_t r = sgs[i * Lc + lane];
+        s0 = __fadd_rn(s0, h_lo(r));
+        s1 = __fadd_rn(s1, h_hi(r));
+      }
+    }
+    __syncthreads();
   }
-  __syncthreads();
   if (threadIdx.y == 0 && on) {
-    float s0 = 0.f, s1 = 0.f;
-    const int n = Ho * ngr;
-    for (int i = 0; i < n; i++) {
-      const uint32_t r = sgs[i * Lc + lane];
-      s0 = __fadd_rn(s0, h_lo(r));
-      s1 = __fadd_rn(s1, h_hi(r));
-    }
     chsum[(long long)win * cws + 2 * c2] = s0;
     chsum[(long long)win * cws + 2 * c2 + 1] = s1;
   }
@@ -1204,11 +1211,11 @@ extern "C" int bnnk_dwk_f16(int B, const uint16_t *xp, long long xws, int W, int
       ((uintptr_t)b & 3))
     return cudaErrorInvalidValue;
   const int C2 = C / 2, ngr = dwk_groups(Wo);
-  int Lc = C2 < 32 ? C2 : 32;
-  while (Lc > 8 && (size_t)Ho * ngr * Lc * 4 > 96 * 1024) Lc /= 2;
-  const size_t smem = (size_t)Ho * ngr * Lc * 4;
+  const int Lc = C2 < 32 ? C2 : 32;
+  int Ry = Ho < 256 / Lc ? Ho : 256 / Lc;  // rows per chunk: one per thread row
+  while (Ry > 1 && (size_t)Ry * ngr * Lc * 4 > 48 * 1024) Ry--;
+  const size_t smem = (size_t)Ry * ngr * Lc * 4;
   if (smem > 96 * 1024) return cudaErrorInvalidValue;
-  const int Ry = Ho < 256 / Lc ? Ho : 256 / Lc;
   const dim3 grid((C2 + Lc - 1) / Lc, B), blk(Lc, Ry);
 #define BNN_DWK(KK)                                                                                              \
   do {                                                                                                           \

@@ -458,8 +458,8 @@ static int init_dwk_f16(vctx *v) { /* dwk_init = rt_dwk_check(2), src/rt_ops_f16
   if (vneed_haloed(v, 0, BNN_F16, H, W, C, h)) return -1;
   if (vneed(v, 1, BNN_F16, (size_t)Ho * Wo * C) || vneed(v, 2, BNN_F32, (size_t)C)) return -1;
   const int groups = Wo / 4 + (Wo % 4 >= 2) + Wo % 2;
-  if ((long long)Ho * groups > 3072)
-    return vbad(v, "%d output rows of %d pixel groups: the B200 depthwise kernel keeps at most 3072 group sums", Ho,
+  if (groups > 768)
+    return vbad(v, "%d output columns (%d pixel groups): the B200 depthwise kernel takes at most 768 groups per row", Wo,
                 groups);
   return 0;
 }
