@@ -500,46 +500,70 @@ __global__ void __launch_bounds__(kPcThreads) k_postpc_gemm(int B, const float *
 // src/gemm_f32.c:100-132), then rounds the outputs to fp16 into the zero-haloed buffer (pc_cvt_pad_f16,
 // src/pc_kern_f16.c:104-113). Thread (pixel, 8-channel panel): the taps are read from the image as the GEMM consumes
 // them (no im2col buffer), the panel's weights and bias sit in shared memory.
+template <int KS>  // KS > 0: the kernel size known at compile time (taps unrolled); 0: any k
 __global__ void __launch_bounds__(256) k_stem_f16(const float *__restrict__ img, long long iws, int W, int k, int s,
                                                   int Ho, int Wo, const float *__restrict__ wt,
                                                   const float *__restrict__ bias, int N, int Kp, int Np, int act,
-                                                  uint16_t *__restrict__ out, long long ows, int ldo, int opad) {
-  extern __shared__ float sw[];  // [Np/8][Kp][8] weights, then [Np] bias
+                                                  uint16_t *__restrict__ out, long long ows, int ldo, int opad,
+                                                  int st16) {
+  extern __shared__ float sw[];  // [Kp][Np] weights (channel fastest: the panels of a warp hit distinct banks), [Np] bias
   __shared__ uint32_t lut[256];
   const int tid = threadIdx.x;
   for (int i = tid; i < 256; i += blockDim.x) lut[i] = g_frecpe_lut[i];
-  for (int i = tid; i < Np * Kp; i += blockDim.x) sw[i] = wt[i];
+  for (int i = tid; i < Np * Kp; i += blockDim.x) {  // from the package's panels [Np/8][Kp][8]
+    const int nb = i / (Kp * 8), r = i - nb * Kp * 8, t = r / 8, j = r - t * 8;
+    sw[t * Np + nb * 8 + j] = wt[i];
+  }
   for (int i = tid; i < Np; i += blockDim.x) sw[Np * Kp + i] = bias[i];
   __syncthreads();
-  const int npan = Np / 8, M = Ho * Wo, K = k * k;
+  const int npan = Np / 8, M = Ho * Wo, kk = KS > 0 ? KS : k, K = kk * kk;
   const long long win = blockIdx.y;
   const int item = blockIdx.x * blockDim.x + tid;
   if (item >= M * npan) return;
   const int m = item / npan, nb = item - m * npan;
   const int oy = m / Wo, ox = m - oy * Wo;
   const float *x = img + win * iws + (long long)(oy * s) * W + ox * s;
-  const float *wp = sw + (size_t)nb * Kp * 8;
+  const float *wp = sw + nb * 8;
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; j++) acc[j] = 0.f;
-  int ky = 0, kx = 0;
-  for (int t = 0; t < Kp; t++) {
-    float v = 0.f;
-    if (t < K) {
-      v = __ldg(x + ky * W + kx);
-      if (++kx == k) { kx = 0; ky++; }
-    }
+  if constexpr (KS > 0) {
+    constexpr int KP = ((KS * KS + 3) & ~3);
+    float v[KP];
 #pragma unroll
-    for (int j = 0; j < 8; j++) acc[j] = __fmaf_rn(v, wp[t * 8 + j], acc[j]);
+    for (int t = 0; t < KP; t++) v[t] = t < KS * KS ? __ldg(x + (t / KS) * W + t % KS) : 0.f;
+#pragma unroll
+    for (int t = 0; t < KP; t++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[j] = __fmaf_rn(v[t], wp[t * Np + j], acc[j]);
+  } else {
+    int ky = 0, kx = 0;
+    for (int t = 0; t < Kp; t++) {
+      float v = 0.f;
+      if (t < K) {
+        v = __ldg(x + ky * W + kx);
+        if (++kx == kk) { kx = 0; ky++; }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[j] = __fmaf_rn(v, wp[t * Np + j], acc[j]);
+    }
   }
   uint16_t *o = out + win * ows + ((long long)(oy + opad) * (Wo + 2 * opad) + ox + opad) * ldo + nb * 8;
+  uint32_t hv[8];
 #pragma unroll
   for (int j = 0; j < 8; j++) {
-    if (nb * 8 + j >= N) break;
     float y = __fadd_rn(acc[j], sw[Np * Kp + nb * 8 + j]);
     if (act == 1) y = silu<true>(y, lut);
     else if (act == 2) y = fmax_nan(y, 0.f);
-    o[j] = __half_as_ushort(__float2half_rn(y));
+    hv[j] = __half_as_ushort(__float2half_rn(y));
+  }
+  if (st16 && nb * 8 + 8 <= N) {  // a whole panel: one 16-byte store
+    *reinterpret_cast<uint4 *>(o) = make_uint4(hv[0] | hv[1] << 16, hv[2] | hv[3] << 16, hv[4] | hv[5] << 16,
+                                               hv[6] | hv[7] << 16);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (nb * 8 + j < N) o[j] = (uint16_t)hv[j];
   }
 }
 
@@ -675,7 +699,11 @@ extern "C" int bnnk_stem_f16(int B, const float *img, long long iws, int W, int 
   const size_t smem = sizeof(float) * ((size_t)Np * Kp + Np);
   if (smem > 48 * 1024) return cudaErrorInvalidValue;
   const long long items = (long long)Ho * Wo * (Np / 8);
-  k_stem_f16<<<dim3((unsigned)((items + 255) / 256), (unsigned)B), 256, smem, st>>>(img, iws, W, k, s, Ho, Wo, w, b, N,
-                                                                                  Kp, Np, act, out, ows, ldo, opad);
+  const int st16 = ldo % 8 == 0 && ows % 8 == 0 && ((uintptr_t)out & 15) == 0;
+  const dim3 grid((unsigned)((items + 255) / 256), (unsigned)B);
+  if (k == 3 && Kp == 12)
+    k_stem_f16<3><<<grid, 256, smem, st>>>(img, iws, W, k, s, Ho, Wo, w, b, N, Kp, Np, act, out, ows, ldo, opad, st16);
+  else
+    k_stem_f16<0><<<grid, 256, smem, st>>>(img, iws, W, k, s, Ho, Wo, w, b, N, Kp, Np, act, out, ows, ldo, opad, st16);
   return cudaGetLastError();
 }

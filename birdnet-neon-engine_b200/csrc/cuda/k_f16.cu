@@ -964,18 +964,135 @@ __global__ void __launch_bounds__(256) k_dwk_f16(const uint16_t *__restrict__ xp
   }
 }
 
+// The same DWK for channel quads (C % 4 == 0 with 8-byte aligned rows: every package buffer qualifies): a thread
+// holds 4 channels (two fp16 pairs, one 8-byte load per tap column), and with the stride S a template parameter the
+// NX = (G - 1) S + k input columns of a G-pixel group are loaded once per tap row and shared by the group's pixels.
+template <int K, int S, int G>
+__device__ __forceinline__ uint2 dwk4_group(const uint2 *xr, long long rs, long long cs, const uint32_t (&w)[K * K][2],
+                                            uint2 b, int act, const uint32_t *tab01, const uint32_t *tab2, uint2 *o,
+                                            long long os) {
+  constexpr int NX = (G - 1) * S + K;
+  uint32_t a[G][2], e[G][2];
+#pragma unroll
+  for (int q = 0; q < G; q++) { a[q][0] = b.x; a[q][1] = b.y; e[q][0] = 0u; e[q][1] = 0u; }
+#pragma unroll
+  for (int ky = 0; ky < K; ky++) {
+    uint2 xv[NX];
+#pragma unroll
+    for (int j = 0; j < NX; j++) xv[j] = __ldg(xr + ky * rs + j * cs);
+#pragma unroll
+    for (int kx = 0; kx < K; kx++) {
+      const int t = ky * K + kx;
+#pragma unroll
+      for (int q = 0; q < G; q++) {
+        const uint2 v = xv[q * S + kx];
+        if (G == 4 && (t & 1)) {
+          e[q][0] = hfma2(v.x, w[t][0], e[q][0]);
+          e[q][1] = hfma2(v.y, w[t][1], e[q][1]);
+        } else {
+          a[q][0] = hfma2(v.x, w[t][0], a[q][0]);
+          a[q][1] = hfma2(v.y, w[t][1], a[q][1]);
+        }
+      }
+    }
+  }
+  uint2 v[G];
+#pragma unroll
+  for (int q = 0; q < G; q++) {
+    v[q] = G == 4 ? make_uint2(hadd2(a[q][0], e[q][0]), hadd2(a[q][1], e[q][1])) : make_uint2(a[q][0], a[q][1]);
+    if (act == 1) v[q] = make_uint2(silu2(v[q].x, tab01, tab2), silu2(v[q].y, tab01, tab2));
+    o[q * os] = v[q];
+  }
+  if (G == 4)
+    return make_uint2(hadd2(hadd2(v[0].x, v[1].x), hadd2(v[2].x, v[3].x)),
+                      hadd2(hadd2(v[0].y, v[1].y), hadd2(v[2].y, v[3].y)));
+  if (G == 2) return make_uint2(hadd2(v[0].x, v[1].x), hadd2(v[0].y, v[1].y));
+  return v[0];
+}
+
+template <int K, int S>
+__global__ void __launch_bounds__(256) k_dwk4_f16(const uint16_t *__restrict__ xp, long long xws, int W, int C, int pt,
+                                                  int pl, const uint16_t *__restrict__ wt,
+                                                  const uint16_t *__restrict__ bt, int act, uint16_t *__restrict__ out,
+                                                  long long ows, int Ho, int Wo, int ngr, float *__restrict__ chsum,
+                                                  long long cws) {
+  extern __shared__ uint2 sg4[];  // [Ry * ngr][Lc] group sums of the current chunk of rows
+  __shared__ uint32_t tab01[16], tab2[16];
+  constexpr int KK = K * K, h = (K - 1) / 2;
+  const int Lc = blockDim.x, Ry = blockDim.y, lane = threadIdx.x, win = blockIdx.y;
+  const int c4 = blockIdx.x * Lc + lane, C4 = C / 4;
+  load_silu_tab(tab01, tab2);
+  __syncthreads();
+  const bool on = c4 < C4;
+  uint32_t w[KK][2];
+  uint2 b = make_uint2(0u, 0u);
+  if (on) {
+    const uint2 *w64 = reinterpret_cast<const uint2 *>(wt);
+#pragma unroll
+    for (int t = 0; t < KK; t++) {
+      const uint2 v = __ldg(w64 + t * C4 + c4);
+      w[t][0] = v.x;
+      w[t][1] = v.y;
+    }
+    b = __ldg(reinterpret_cast<const uint2 *>(bt) + c4);
+  }
+  const uint2 *x = reinterpret_cast<const uint2 *>(xp + (long long)win * xws) + c4;
+  uint2 *o = reinterpret_cast<uint2 *>(out + (long long)win * ows) + c4;
+  const long long cs = C4, rs = (long long)(W + 2 * h) * C4;
+  float sm[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int oy0 = 0; oy0 < Ho; oy0 += Ry) {
+    const int oy = oy0 + threadIdx.y;
+    if (on && oy < Ho) {
+      const uint2 *xr = x + (long long)(oy * S - pt + h) * rs;
+      uint2 *orow = o + (long long)oy * Wo * cs;
+      uint2 *g = sg4 + threadIdx.y * ngr * Lc + lane;
+      int ox = 0, gi = 0;
+      for (; ox + 4 <= Wo; ox += 4, gi++)
+        g[gi * Lc] = dwk4_group<K, S, 4>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, w, b, act, tab01, tab2,
+                                         orow + ox * cs, cs);
+      if (ox + 2 <= Wo) {
+        g[gi * Lc] = dwk4_group<K, S, 2>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, w, b, act, tab01, tab2,
+                                         orow + ox * cs, cs);
+        ox += 2;
+        gi++;
+      }
+      if (ox < Wo)
+        g[gi * Lc] = dwk4_group<K, S, 1>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, w, b, act, tab01, tab2,
+                                         orow + ox * cs, cs);
+    }
+    __syncthreads();
+    if (threadIdx.y == 0 && on) {  // the chunk's group sums in row order, then group order
+      const int n = min(Ry, Ho - oy0) * ngr;
+      for (int i = 0; i < n; i++) {
+        const uint2 r = sg4[i * Lc + lane];
+        sm[0] = __fadd_rn(sm[0], h_lo(r.x));
+        sm[1] = __fadd_rn(sm[1], h_hi(r.x));
+        sm[2] = __fadd_rn(sm[2], h_lo(r.y));
+        sm[3] = __fadd_rn(sm[3], h_hi(r.y));
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.y == 0 && on)
+    for (int j = 0; j < 4; j++) chsum[(long long)win * cws + 4 * c4 + j] = sm[j];
+}
+
 // ------------------------------------------------------------------ PAD f16 (pc_pad_f16, src/pc_kern_f16.c:98-102)
 // x [H][W] (channel stride ld) into the interior of the zero-haloed xp [H + 2h][W + 2h][C]; the halo is never written
 // (the buffer is zeroed once when it is allocated).
+template <int V>  // V fp16 values per thread (8: 16-byte copies, for aligned rows)
 __global__ void k_pad_f16(int H, int W, int C, int ld, int h, const uint16_t *__restrict__ x, long long xws,
                           uint16_t *__restrict__ xp, long long pws) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x, n = (long long)H * W * C;
+  const int CV = C / V;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x, n = (long long)H * W * CV;
   if (i >= n) return;
-  const int c = (int)(i % C);
-  const long long pix = i / C;
+  const int c = (int)(i % CV) * V;
+  const long long pix = i / CV;
   const int y = (int)(pix / W), xx = (int)(pix - (long long)y * W);
-  xp[(long long)blockIdx.y * pws + ((long long)(y + h) * (W + 2 * h) + xx + h) * C + c] =
-      x[(long long)blockIdx.y * xws + pix * ld + c];
+  uint16_t *d = xp + (long long)blockIdx.y * pws + ((long long)(y + h) * (W + 2 * h) + xx + h) * C + c;
+  const uint16_t *src = x + (long long)blockIdx.y * xws + pix * ld + c;
+  if (V == 8) *reinterpret_cast<uint4 *>(d) = __ldg(reinterpret_cast<const uint4 *>(src));
+  else *d = *src;
 }
 
 // ------------------------------------------------------------------ MEAN f16 (pc_mean_f16, src/pc_kern_f16.c:115-121)
@@ -1207,10 +1324,37 @@ extern "C" int bnnk_dwk_f16(int B, const uint16_t *xp, long long xws, int W, int
                             const uint16_t *w, const uint16_t *b, int act, uint16_t *out, long long ows, int Ho, int Wo,
                             float *chsum, long long cws, bnn_stream_t st) {
   if (B <= 0) return 0;
+  const int ngr = dwk_groups(Wo);
+  // the channel-quad form: 8-byte aligned rows, windows, weights and bias
+  if (C % 4 == 0 && xws % 4 == 0 && ows % 4 == 0 && ((uintptr_t)xp & 7) == 0 && ((uintptr_t)out & 7) == 0 &&
+      ((uintptr_t)w & 7) == 0 && ((uintptr_t)b & 7) == 0 && (s == 1 || s == 2) && (k == 3 || k == 5 || k == 7)) {
+    const int C4 = C / 4;
+    const int Lc = C4 < 32 ? C4 : 32;
+    int Ry = Ho < 256 / Lc ? Ho : 256 / Lc;
+    while (Ry > 1 && (size_t)Ry * ngr * Lc * 8 > 48 * 1024) Ry--;
+    const size_t smem = (size_t)Ry * ngr * Lc * 8;
+    if (smem <= 96 * 1024) {
+      const dim3 grid((C4 + Lc - 1) / Lc, B), blk(Lc, Ry);
+#define BNN_DWK4(KK, SS)                                                                                         \
+  do {                                                                                                           \
+    cudaError_t e_ = cudaFuncSetAttribute(k_dwk4_f16<KK, SS>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                                          (int)smem);                                                           \
+    if (e_) return e_;                                                                                           \
+    k_dwk4_f16<KK, SS><<<grid, blk, smem, st>>>(xp, xws, W, C, pt, pl, w, b, act, out, ows, Ho, Wo, ngr, chsum,  \
+                                                cws);                                                            \
+  } while (0)
+      if (k == 3) { if (s == 1) BNN_DWK4(3, 1); else BNN_DWK4(3, 2); }
+      else if (k == 5) { if (s == 1) BNN_DWK4(5, 1); else BNN_DWK4(5, 2); }
+      else { if (s == 1) BNN_DWK4(7, 1); else BNN_DWK4(7, 2); }
+#undef BNN_DWK4
+      return cudaGetLastError();
+    }
+  }
+  // the channel-pair form (any stride and k, 4-byte alignment)
   if (C % 2 || xws % 2 || ows % 2 || ((uintptr_t)xp & 3) || ((uintptr_t)out & 3) || ((uintptr_t)w & 3) ||
       ((uintptr_t)b & 3))
     return cudaErrorInvalidValue;
-  const int C2 = C / 2, ngr = dwk_groups(Wo);
+  const int C2 = C / 2;
   const int Lc = C2 < 32 ? C2 : 32;
   int Ry = Ho < 256 / Lc ? Ho : 256 / Lc;  // rows per chunk: one per thread row
   while (Ry > 1 && (size_t)Ry * ngr * Lc * 4 > 48 * 1024) Ry--;
@@ -1237,8 +1381,13 @@ extern "C" int bnnk_dwk_f16(int B, const uint16_t *xp, long long xws, int W, int
 extern "C" int bnnk_pad_f16(int B, int H, int W, int C, int ld, int h, const uint16_t *x, long long xws, uint16_t *xp,
                             long long pws, bnn_stream_t st) {
   if (B <= 0) return 0;
-  const long long n = (long long)H * W * C;
-  k_pad_f16<<<dim3((unsigned)((n + 255) / 256), (unsigned)B), 256, 0, st>>>(H, W, C, ld, h, x, xws, xp, pws);
+  if (C % 8 == 0 && ld % 8 == 0 && xws % 8 == 0 && pws % 8 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)xp & 15) == 0) {
+    const long long n = (long long)H * W * (C / 8);
+    k_pad_f16<8><<<dim3((unsigned)((n + 255) / 256), (unsigned)B), 256, 0, st>>>(H, W, C, ld, h, x, xws, xp, pws);
+  } else {
+    const long long n = (long long)H * W * C;
+    k_pad_f16<1><<<dim3((unsigned)((n + 255) / 256), (unsigned)B), 256, 0, st>>>(H, W, C, ld, h, x, xws, xp, pws);
+  }
   return cudaGetLastError();
 }
 
