@@ -1125,11 +1125,17 @@ static void kblocks(int Kp, int *nblk, int *bs) {
 
 // the channel tile: all of Np up to 128 (at least 16), else the widest multiple of 8 up to 128 that divides Np (else
 // 128); columns past Np are zero-filled and not stored
+// the channel tile: all Np channels up to 128, else the width in 64..128 (a multiple of 8) whose tiles cover Np with
+// the fewest padded channels, the widest of those (136 -> 2 x 72, 816 -> 8 x 104, 232 -> 2 x 120, 576 -> 6 x 96)
 static int gemm_bn(int Np) {
   if (Np <= 128) return Np < 16 ? 16 : Np;
-  for (int bn = 128; bn >= 64; bn -= 8)
-    if (Np % bn == 0) return bn;
-  return 128;
+  int best = 128;
+  long long cover = (long long)((Np + 127) / 128) * 128;
+  for (int bn = 120; bn >= 64; bn -= 8) {
+    const long long c = (long long)((Np + bn - 1) / bn) * bn;
+    if (c < cover) { best = bn; cover = c; }
+  }
+  return best;
 }
 
 extern "C" int bnnk_gemm_f16(int rows, int Mw, const uint16_t *A, long long aws, int lda, const uint32_t *Wd, int Kp,
