@@ -683,6 +683,9 @@ def main():
                     help="for profiler captures: the Perch-like log-mel front end on B windows, 3 warm-ups + 1 run")
     ap.add_argument("--f16-ncu", type=int, metavar="B", default=0,
                     help="for profiler captures: the v2.4 neon-fp16 package on B windows, 3 warm-ups + 1 step")
+    ap.add_argument("--perch-ncu", type=int, metavar="B", default=0,
+                    help="for profiler captures: the Perch-architecture neon-fp16 package on B windows, 3 warm-ups + 1 "
+                         "step")
     ap.add_argument("--ncu", action="store_true",
                     help="for profiler captures: warm-up steps + one step through bnn_infer_device, no timing, no JSON")
     args = ap.parse_args()
@@ -696,7 +699,7 @@ def main():
     if args.impl == "reference":
         reference_arm(args, rank)
         return
-    if args.ncu or args.proto_ncu or args.logmel_ncu or args.f16_ncu:
+    if args.ncu or args.proto_ncu or args.logmel_ncu or args.f16_ncu or args.perch_ncu:
         # profiler captures use eager launches: a run that replays the op list from CUDA graphs stopped with a driver
         # LaunchFailed under ncu (the same command exits 0 without ncu)
         os.environ["BNN_GRAPHS"] = "0"
@@ -727,13 +730,19 @@ def main():
         h.bnn_logmel_free(op)
         print(f"logmel ncu mode: 4 runs of {B} windows", flush=True)
         return
-    if args.f16_ncu:  # the fp16 package alone, for a profiler; nothing is timed or printed as a result
-        B = args.f16_ncu
+    if args.f16_ncu or args.perch_ncu:  # an fp16 package alone, for a profiler; nothing is timed or printed
+        B = args.f16_ncu or args.perch_ncu
         td = tempfile.mkdtemp()
-        pkg = os.path.join(td, "v24_full_f16.bnpk")
-        synth.make_package(pkg, seed=0, path=synth.PATH_F16)
+        if args.perch_ncu:
+            pkg = os.path.join(td, "perch_v2_f16s8.bnpk")
+            _, _, ns = synth.make_perch_package(pkg, seed=0)
+            pcm = synth.audio(B, seed=4100, n_samples=ns, rate=synth.PERCH_SAMPLE_RATE)
+        else:
+            pkg = os.path.join(td, "v24_full_f16.bnpk")
+            synth.make_package(pkg, seed=0, path=synth.PATH_F16)
+            pcm = synth.audio(B, seed=4000)
         m = Model(pkg, mode=3, batch=B)
-        d_pcm = torch.from_numpy(synth.audio(B, seed=4000)).cuda()
+        d_pcm = torch.from_numpy(pcm).cuda()
         d_out = torch.empty((B, m.info.n_classes), dtype=torch.float32, device="cuda")
         d_emb = torch.empty((B, m.info.emb_dim), dtype=torch.float32, device="cuda")
         for _ in range(4):
