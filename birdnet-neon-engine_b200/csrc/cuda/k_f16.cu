@@ -967,8 +967,12 @@ __global__ void __launch_bounds__(256) k_dwk_f16(const uint16_t *__restrict__ xp
 // The same DWK for channel quads (C % 4 == 0 with 8-byte aligned rows: every package buffer qualifies): a thread
 // holds 4 channels (two fp16 pairs, one 8-byte load per tap column), and with the stride S a template parameter the
 // NX = (G - 1) S + k input columns of a G-pixel group are loaded once per tap row and shared by the group's pixels.
+// The tap weights sit in shared memory (one 8-byte load feeds the group's 2 G fp16-pair FMAs of a tap), which keeps
+// the kernel near 70 registers. Thread rows 0 .. Ry - 1 compute a chunk of Ry output rows into one of two group-sum
+// tiles; the last thread row only adds the previous chunk's group sums (row order, then group order) into the fp32
+// channel sums, so the compute rows pass one barrier per chunk and never wait for the sums.
 template <int K, int S, int G>
-__device__ __forceinline__ uint2 dwk4_group(const uint2 *xr, long long rs, long long cs, const uint32_t (&w)[K * K][2],
+__device__ __forceinline__ uint2 dwk4_group(const uint2 *xr, long long rs, long long cs, const uint2 *ws, int wl,
                                             uint2 b, int act, const uint32_t *tab01, const uint32_t *tab2, uint2 *o,
                                             long long os) {
   constexpr int NX = (G - 1) * S + K;
@@ -983,15 +987,16 @@ __device__ __forceinline__ uint2 dwk4_group(const uint2 *xr, long long rs, long 
 #pragma unroll
     for (int kx = 0; kx < K; kx++) {
       const int t = ky * K + kx;
+      const uint2 wt = ws[t * wl];
 #pragma unroll
       for (int q = 0; q < G; q++) {
         const uint2 v = xv[q * S + kx];
         if (G == 4 && (t & 1)) {
-          e[q][0] = hfma2(v.x, w[t][0], e[q][0]);
-          e[q][1] = hfma2(v.y, w[t][1], e[q][1]);
+          e[q][0] = hfma2(v.x, wt.x, e[q][0]);
+          e[q][1] = hfma2(v.y, wt.y, e[q][1]);
         } else {
-          a[q][0] = hfma2(v.x, w[t][0], a[q][0]);
-          a[q][1] = hfma2(v.y, w[t][1], a[q][1]);
+          a[q][0] = hfma2(v.x, wt.x, a[q][0]);
+          a[q][1] = hfma2(v.y, wt.y, a[q][1]);
         }
       }
     }
@@ -1011,60 +1016,55 @@ __device__ __forceinline__ uint2 dwk4_group(const uint2 *xr, long long rs, long 
 }
 
 template <int K, int S>
-__global__ void __launch_bounds__(256) k_dwk4_f16(const uint16_t *__restrict__ xp, long long xws, int W, int C, int pt,
+__global__ void __launch_bounds__(256, 3) k_dwk4_f16(const uint16_t *__restrict__ xp, long long xws, int W, int C, int pt,
                                                   int pl, const uint16_t *__restrict__ wt,
                                                   const uint16_t *__restrict__ bt, int act, uint16_t *__restrict__ out,
                                                   long long ows, int Ho, int Wo, int ngr, float *__restrict__ chsum,
                                                   long long cws) {
-  extern __shared__ uint2 sg4[];  // [Ry * ngr][Lc] group sums of the current chunk of rows
+  extern __shared__ uint2 sd4[];  // [K * K][Lc] tap weights, then [2][Ry * ngr][Lc] group sums of two chunks
   __shared__ uint32_t tab01[16], tab2[16];
   constexpr int KK = K * K, h = (K - 1) / 2;
-  const int Lc = blockDim.x, Ry = blockDim.y, lane = threadIdx.x, win = blockIdx.y;
+  const int Lc = blockDim.x, Ry = blockDim.y - 1, lane = threadIdx.x, win = blockIdx.y;
   const int c4 = blockIdx.x * Lc + lane, C4 = C / 4;
+  const bool on = c4 < C4, summer = threadIdx.y == Ry;
+  uint2 *ws = sd4, *sg = sd4 + KK * Lc;
+  const int tile = Ry * ngr * Lc;
   load_silu_tab(tab01, tab2);
+  for (int t = threadIdx.y; t < KK; t += blockDim.y)
+    ws[t * Lc + lane] = on ? __ldg(reinterpret_cast<const uint2 *>(wt) + t * C4 + c4) : make_uint2(0u, 0u);
+  const uint2 b = on ? __ldg(reinterpret_cast<const uint2 *>(bt) + c4) : make_uint2(0u, 0u);
   __syncthreads();
-  const bool on = c4 < C4;
-  uint32_t w[KK][2];
-  uint2 b = make_uint2(0u, 0u);
-  if (on) {
-    const uint2 *w64 = reinterpret_cast<const uint2 *>(wt);
-#pragma unroll
-    for (int t = 0; t < KK; t++) {
-      const uint2 v = __ldg(w64 + t * C4 + c4);
-      w[t][0] = v.x;
-      w[t][1] = v.y;
-    }
-    b = __ldg(reinterpret_cast<const uint2 *>(bt) + c4);
-  }
   const uint2 *x = reinterpret_cast<const uint2 *>(xp + (long long)win * xws) + c4;
   uint2 *o = reinterpret_cast<uint2 *>(out + (long long)win * ows) + c4;
   const long long cs = C4, rs = (long long)(W + 2 * h) * C4;
   float sm[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int oy0 = 0; oy0 < Ho; oy0 += Ry) {
-    const int oy = oy0 + threadIdx.y;
-    if (on && oy < Ho) {
-      const uint2 *xr = x + (long long)(oy * S - pt + h) * rs;
-      uint2 *orow = o + (long long)oy * Wo * cs;
-      uint2 *g = sg4 + threadIdx.y * ngr * Lc + lane;
-      int ox = 0, gi = 0;
-      for (; ox + 4 <= Wo; ox += 4, gi++)
-        g[gi * Lc] = dwk4_group<K, S, 4>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, w, b, act, tab01, tab2,
-                                         orow + ox * cs, cs);
-      if (ox + 2 <= Wo) {
-        g[gi * Lc] = dwk4_group<K, S, 2>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, w, b, act, tab01, tab2,
-                                         orow + ox * cs, cs);
-        ox += 2;
-        gi++;
+  const int nch = (Ho + Ry - 1) / Ry;
+  for (int ci = 0; ci <= nch; ci++) {
+    if (!summer) {
+      const int oy = ci * Ry + threadIdx.y;
+      if (ci < nch && on && oy < Ho) {
+        const uint2 *xr = x + (long long)(oy * S - pt + h) * rs;
+        uint2 *orow = o + (long long)oy * Wo * cs;
+        uint2 *g = sg + (ci & 1) * tile + threadIdx.y * ngr * Lc + lane;
+        int ox = 0, gi = 0;
+        for (; ox + 4 <= Wo; ox += 4, gi++)
+          g[gi * Lc] = dwk4_group<K, S, 4>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, ws + lane, Lc, b, act,
+                                           tab01, tab2, orow + ox * cs, cs);
+        if (ox + 2 <= Wo) {
+          g[gi * Lc] = dwk4_group<K, S, 2>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, ws + lane, Lc, b, act,
+                                           tab01, tab2, orow + ox * cs, cs);
+          ox += 2;
+          gi++;
+        }
+        if (ox < Wo)
+          g[gi * Lc] = dwk4_group<K, S, 1>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, ws + lane, Lc, b, act,
+                                           tab01, tab2, orow + ox * cs, cs);
       }
-      if (ox < Wo)
-        g[gi * Lc] = dwk4_group<K, S, 1>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, w, b, act, tab01, tab2,
-                                         orow + ox * cs, cs);
-    }
-    __syncthreads();
-    if (threadIdx.y == 0 && on) {  // the chunk's group sums in row order, then group order
-      const int n = min(Ry, Ho - oy0) * ngr;
+    } else if (ci > 0 && on) {  // the previous chunk's group sums, row order then group order
+      const uint2 *gs = sg + ((ci - 1) & 1) * tile + lane;
+      const int n = min(Ry, Ho - (ci - 1) * Ry) * ngr;
       for (int i = 0; i < n; i++) {
-        const uint2 r = sg4[i * Lc + lane];
+        const uint2 r = gs[i * Lc];
         sm[0] = __fadd_rn(sm[0], h_lo(r.x));
         sm[1] = __fadd_rn(sm[1], h_hi(r.x));
         sm[2] = __fadd_rn(sm[2], h_lo(r.y));
@@ -1073,7 +1073,7 @@ __global__ void __launch_bounds__(256) k_dwk4_f16(const uint16_t *__restrict__ x
     }
     __syncthreads();
   }
-  if (threadIdx.y == 0 && on)
+  if (summer && on)
     for (int j = 0; j < 4; j++) chsum[(long long)win * cws + 4 * c4 + j] = sm[j];
 }
 
@@ -1336,11 +1336,14 @@ extern "C" int bnnk_dwk_f16(int B, const uint16_t *xp, long long xws, int W, int
       ((uintptr_t)w & 7) == 0 && ((uintptr_t)b & 7) == 0 && (s == 1 || s == 2) && (k == 3 || k == 5 || k == 7)) {
     const int C4 = C / 4;
     const int Lc = C4 < 32 ? C4 : 32;
-    int Ry = Ho < 256 / Lc ? Ho : 256 / Lc;
-    while (Ry > 1 && (size_t)Ry * ngr * Lc * 8 > 48 * 1024) Ry--;
-    const size_t smem = (size_t)Ry * ngr * Lc * 8;
-    if (smem <= 96 * 1024) {
-      const dim3 grid((C4 + Lc - 1) / Lc, B), blk(Lc, Ry);
+    int Ry = 256 / Lc - 1;  // computing thread rows; one more row adds the group sums
+    if (Ry > Ho) Ry = Ho;
+    if (Ry < 1) Ry = 1;
+    auto smem_of = [&](int ry) { return (size_t)(k * k + 2 * ry * ngr) * Lc * 8; };
+    while (Ry > 1 && smem_of(Ry) > 48 * 1024) Ry--;
+    const size_t smem = smem_of(Ry);
+    if (smem <= 96 * 1024 && (Ry + 1) * Lc <= 256) {
+      const dim3 grid((C4 + Lc - 1) / Lc, B), blk(Lc, Ry + 1);
 #define BNN_DWK4(KK, SS)                                                                                         \
   do {                                                                                                           \
     cudaError_t e_ = cudaFuncSetAttribute(k_dwk4_f16<KK, SS>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
