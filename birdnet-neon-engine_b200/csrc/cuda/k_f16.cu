@@ -1125,17 +1125,22 @@ static void kblocks(int Kp, int *nblk, int *bs) {
 
 // the channel tile: all of Np up to 128 (at least 16), else the widest multiple of 8 up to 128 that divides Np (else
 // 128); columns past Np are zero-filled and not stored
-// the channel tile: all Np channels up to 128, else the width in 64..128 (a multiple of 8) whose tiles cover Np with
-// the fewest padded channels, the widest of those (136 -> 2 x 72, 816 -> 8 x 104, 232 -> 2 x 120, 576 -> 6 x 96)
+// the channel tile: all Np channels up to 128; else the widest multiple of 8 in 64..128 that divides Np (576 -> 96);
+// else the width whose tiles cover Np with the fewest padded channels, if that saves at least 15 % of the 128-wide
+// tiles' width (136 -> 2 x 72 instead of 2 x 128), else 128 (816 and 232 ran 5-12 % slower on 104- and 120-wide
+// tiles than on 128-wide ones with a partly empty last tile)
 static int gemm_bn(int Np) {
   if (Np <= 128) return Np < 16 ? 16 : Np;
+  for (int bn = 128; bn >= 64; bn -= 8)
+    if (Np % bn == 0) return bn;
+  const long long c128 = (long long)((Np + 127) / 128) * 128;
   int best = 128;
-  long long cover = (long long)((Np + 127) / 128) * 128;
+  long long cover = c128;
   for (int bn = 120; bn >= 64; bn -= 8) {
     const long long c = (long long)((Np + bn - 1) / bn) * bn;
     if (c < cover) { best = bn; cover = c; }
   }
-  return best;
+  return cover * 100 <= c128 * 85 ? best : 128;
 }
 
 extern "C" int bnnk_gemm_f16(int rows, int Mw, const uint16_t *A, long long aws, int lda, const uint32_t *Wd, int Kp,
