@@ -74,6 +74,8 @@ SIGNATURES = {
     "bnn_pw_f16_run": (_I, [_P, _I, _I, _P, _LL, _I, _I, _P, _LL, _I, _I, _I, _P, _LL, _I, _P]),
     "bnn_pw_f16_free": (None, [_P]),
     "bnn_cuda_dw3_f16": (_I, [_I, _P, _LL, _I, _I, _I, _I, _I, _I, _P, _P, _P, _LL, _I, _I, _P, _LL, _P]),
+    "bnn_cuda_dwk_f16": (_I, [_I, _P, _LL, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _LL, _I, _I, _P, _LL, _P]),
+    "bnn_cuda_stem_f16": (_I, [_I, _P, _LL, _I, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P, _LL, _I, _I, _P]),
     "bnn_debug_n_ops": (_I, [_P]),
     "bnn_debug_op_code": (_I, [_P, _I]),
     "bnn_debug_run_ops": (_I, [_P, _I, _P, _I, _I]),

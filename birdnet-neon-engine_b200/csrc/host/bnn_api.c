@@ -1108,15 +1108,51 @@ int bnn_cuda_dw3_f16(int B, const void *d_xp, long long xws, int H, int W, int C
                      const void *d_w, const void *d_b, void *d_out, long long ows, int Ho, int Wo, float *d_chsum,
                      long long cws, void *stream) {
   if (B < 0 || H <= 0 || W <= 0 || C <= 0 || C % 8 || C > 2048 || (s != 1 && s != 2) || pt < 0 || pt > 1 || pl < 0 ||
-      pl > 1 || Ho <= 0 || Wo <= 0 || Ho > 192 || (Ho - 1) * s - pt + 1 + 3 > H + 2 ||
+      pl > 1 || Ho <= 0 || Wo <= 0 || Ho > 12288 || (Ho - 1) * s - pt + 1 + 3 > H + 2 ||
       (Wo - 1) * s - pl + 1 + 3 > W + 2 || xws % 2 || ows % 2 || cws % 2 || !d_xp || !d_w || !d_b || !d_out ||
       !d_chsum) {
     ERR(BNN_ERR_USAGE, "bnn_cuda_dw3_f16: H %d W %d C %d s %d pt %d pl %d Ho %d Wo %d (C %% 8 == 0 and <= 2048, s 1|2, "
-        "pt and pl 0|1, Ho <= 192, taps inside the halo, even strides)", H, W, C, s, pt, pl, Ho, Wo);
+        "pt and pl 0|1, Ho <= 12288, taps inside the halo, even strides)", H, W, C, s, pt, pl, Ho, Wo);
     return -1;
   }
   return launch_rc("bnn_cuda_dw3_f16", bnnk_dw3_f16(B, d_xp, xws, H, W, C, s, pt, pl, d_w, d_b, d_out, ows, Ho, Wo,
                                                     d_chsum, cws, op_err_word(), (bnn_stream_t)stream));
+}
+
+/* DWK f16 with the checks of rt_dwk_check (src/rt_ops_f32.c:435-451) and this library's limit of 768 pixel groups
+ * per output row */
+int bnn_cuda_dwk_f16(int B, const void *d_xp, long long xws, int H, int W, int C, int k, int s, int pt, int pl,
+                     const void *d_w, const void *d_b, int act, void *d_out, long long ows, int Ho, int Wo,
+                     float *d_chsum, long long cws, void *stream) {
+  const int h = (k - 1) / 2, groups = Wo / 4 + (Wo % 4 >= 2) + Wo % 2;
+  if (B < 0 || H <= 0 || W <= 0 || Ho <= 0 || Wo <= 0 || C <= 0 || C % 8 || k < 1 || k > 7 || k % 2 == 0 ||
+      (s != 1 && s != 2) || pt < 0 || pt > h || pl < 0 || pl > h || act < 0 || act > 1 ||
+      (Ho - 1) * s - pt + k > H + h || (Wo - 1) * s - pl + k > W + h || groups > 768 || xws % 2 || ows % 2 ||
+      !d_xp || !d_w || !d_b || !d_out || !d_chsum) {
+    ERR(BNN_ERR_USAGE, "bnn_cuda_dwk_f16: H %d W %d C %d k %d s %d pt %d pl %d act %d Ho %d Wo %d (C %% 8 == 0, k odd "
+        "1..7, s 1|2, pt and pl <= (k - 1) / 2, taps inside the halo, at most 768 pixel groups per row, even strides)",
+        H, W, C, k, s, pt, pl, act, Ho, Wo);
+    return -1;
+  }
+  return launch_rc("bnn_cuda_dwk_f16", bnnk_dwk_f16(B, d_xp, xws, W, C, k, s, pt, pl, d_w, d_b, act, d_out, ows, Ho,
+                                                    Wo, d_chsum, cws, (bnn_stream_t)stream));
+}
+
+/* STEM f32 -> f16 with the checks of rt_stem_f32_check (src/rt_ops_f32.c:390-408) and this library's 48 KB limit */
+int bnn_cuda_stem_f16(int B, const float *d_img, long long iws, int H, int W, int k, int s, int Ho, int Wo,
+                      const float *d_w, const float *d_b, int N, int Kp, int act, void *d_out, long long ows, int ldo,
+                      int opad, void *stream) {
+  const int Np = (N + 7) & ~7;
+  if (B < 0 || k < 1 || s < 1 || Ho <= 0 || Wo <= 0 || N <= 0 || (Ho - 1) * s + k > H || (Wo - 1) * s + k > W ||
+      Kp < k * k || Kp % 4 || ldo < Np || opad < 0 || opad > 3 || act < 0 || act > 2 ||
+      ((size_t)Np * Kp + Np) * 4 > 48 * 1024 || !d_img || !d_w || !d_b || !d_out) {
+    ERR(BNN_ERR_USAGE, "bnn_cuda_stem_f16: H %d W %d k %d s %d Ho %d Wo %d N %d Kp %d act %d ldo %d opad %d (VALID "
+        "conv, Kp >= k k and a multiple of 4, ldo >= N rounded up to 8, opad 0..3, act 0..2, weights within 48 KB)",
+        H, W, k, s, Ho, Wo, N, Kp, act, ldo, opad);
+    return -1;
+  }
+  return launch_rc("bnn_cuda_stem_f16", bnnk_stem_f16(B, d_img, iws, W, k, s, Ho, Wo, d_w, d_b, N, Kp, Np, act, d_out,
+                                                      ows, ldo, opad, (bnn_stream_t)stream));
 }
 
 int bnn_cuda_peak_hfma2(int blocks, int iters, void *d_word, void *stream) {

@@ -174,10 +174,29 @@ int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, i
 /* DW3 f16 (dw3x3_f16_cr, src/kern_f16.c:83-155; record src/rt_ops_f16.c:64-103), batched: d_xp [B][(H+2)(W+2)][C]
  * fp16 (zero halo 1; window stride xws), d_w [9][C], d_b [C] fp16 -> d_out [B][Ho Wo][C] fp16, d_chsum [B][C] fp32;
  * stride s 1 | 2, output pixel (oy, ox) reads input rows oy s - pt + 1 .. + 2 and columns ox s - pl + 1 .. + 2 of the
- * haloed image (pt, pl in {0, 1}). A bounded device wait that ran out is reported by bnn_cuda_op_error. */
+ * haloed image (pt, pl in {0, 1}); Ho <= 12288. A bounded device wait that ran out is reported by bnn_cuda_op_error. */
 int bnn_cuda_dw3_f16(int B, const void *d_xp, long long xws, int H, int W, int C, int s, int pt, int pl,
                      const void *d_w, const void *d_b, void *d_out, long long ows, int Ho, int Wo, float *d_chsum,
                      long long cws, void *stream);
+
+/* DWK f16 (pc_dwk_f16_cr, src/pc_kern_f16.c:16-96; record src/rt_ops_f16.c:192-202, checks src/rt_ops_f32.c:435-451),
+ * batched: d_xp [B][(H+2h)(W+2h)][C] fp16 zero-haloed by h = (k - 1) / 2 (window stride xws), d_w [k*k][C], d_b [C]
+ * fp16 -> d_out [B][Ho Wo][C] fp16, d_chsum [B][C] fp32; k odd 1..7, stride s 1 | 2, output pixel (oy, ox) reads
+ * rows oy s - pt + h + ky and columns ox s - pl + h + kx (pt, pl in 0..h); act 0 none | 1 the SiLU table; at most 768
+ * pixel groups (Wo / 4 fours, then a pair, then a single pixel) per output row. */
+int bnn_cuda_dwk_f16(int B, const void *d_xp, long long xws, int H, int W, int C, int k, int s, int pt, int pl,
+                     const void *d_w, const void *d_b, int act, void *d_out, long long ows, int Ho, int Wo,
+                     float *d_chsum, long long cws, void *stream);
+
+/* STEM f32 -> f16 (stem_run, src/rt_ops_f16.c:175-190: pc_im2col1 + gemm_f32 + pc_cvt_pad_f16), batched: the VALID
+ * k x k stride-s conv of the 1-channel image d_img [B][H][W] fp32 (window stride iws) with the package's fp32 GEMM
+ * panels d_w [Np/8][Kp][8] and bias d_b [Np] (Np = N rounded up to 8, Kp >= k k, a multiple of 4): one fp32
+ * accumulator per output over all Kp taps, + bias, act 0 none | 1 SiLU | 2 ReLU, rounded to fp16 into d_out at the
+ * padded position ((Ho + 2 opad) (Wo + 2 opad) pixels of ldo channels per window, window stride ows; channels N..ldo
+ * and the halo are not written). (Np Kp + Np) fp32 weights at most 48 KB. */
+int bnn_cuda_stem_f16(int B, const float *d_img, long long iws, int H, int W, int k, int s, int Ho, int Wo,
+                      const float *d_w, const float *d_b, int N, int Kp, int act, void *d_out, long long ows, int ldo,
+                      int opad, void *stream);
 
 /* the current device's error word of the per-op entry points (0 = no bounded device wait ran out; then reset to 0;
  * -1 if it cannot be read); synchronous */
