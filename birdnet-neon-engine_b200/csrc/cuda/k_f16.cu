@@ -506,12 +506,18 @@ template <int S, int R>
 __global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtensorMap tmx, int W, int C, int CG,
                                                   int pt, int pl, int Ho, int Wo, const uint16_t *__restrict__ wt,
                                                   const uint16_t *__restrict__ bt, uint16_t *__restrict__ out,
-                                                  long long ows, float *__restrict__ chsum, long long cws, int *err) {
+                                                  long long ows, float *__restrict__ chsum, long long cws, int *err,
+                                                  int SB) {
   constexpr int NR = S + 3, NX = (R - 1) * S + 3;
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ __align__(8) unsigned long long bar[NR];
   __shared__ uint32_t tab01[16], tab2[16];
-  const int tid = threadIdx.x, nt = blockDim.x;
+  // SB < blockDim.x: threads SB.. (whole warps) only sum, one step behind the others (row oy - 1 while row oy is
+  // computed); threads below SB compute (those past the last whole channel octet of lanes idle). SB == blockDim.x:
+  // the first CG / 2 threads also sum, after each step's barrier.
+  const int tid = threadIdx.x, nt = SB < (int)blockDim.x ? SB : (int)blockDim.x;
+  const bool summer = tid >= SB;
+  const int sp = tid - SB;  // a summer's channel pair
   load_silu_tab(tab01, tab2);
   const int ngroups = C / CG;
   const int win = blockIdx.x / ngroups, grp = blockIdx.x - win * ngroups;
@@ -519,8 +525,8 @@ __global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtens
   const uint32_t row_bytes = (uint32_t)Wp * CG * 2, row_stride = (row_bytes + 127u) & ~127u;
   const uint32_t ring = smem_u32(dsm);
   uint16_t *obuf = reinterpret_cast<uint16_t *>(dsm + NR * row_stride);  // [2][Wo][CG]
-  const int q = tid % Q, lane = tid / Q;  // lanes >= NL (the last nt % Q threads) only sum
-  const bool comp = lane < NL;
+  const int q = tid % Q, lane = tid / Q;  // lanes >= NL (the last nt % Q threads) do not compute
+  const bool comp = !summer && lane < NL;
   const int c = grp * CG + 8 * q;
   uint32_t w[9][4], b[4];
 #pragma unroll
@@ -551,13 +557,23 @@ __global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtens
   int oy = 0;
   for (; oy < Ho; oy++) {
     bool ok = true;
+    if (!summer) {
 #pragma unroll
-    for (int ky = 0; ky < 3; ky++) {
-      const int iy = oy * S + ky;
-      ok = ok && mbar_wait(smem_u32(&bar[iy % NR]), (uint32_t)(iy / NR) & 1u);
+      for (int ky = 0; ky < 3; ky++) {
+        const int iy = oy * S + ky;
+        ok = ok && mbar_wait(smem_u32(&bar[iy % NR]), (uint32_t)(iy / NR) & 1u);
+      }
     }
     uint16_t *ob = obuf + (size_t)(oy & 1) * Wo * CG;
-    if (comp) {
+    if (summer) {  // the previous row's fp16 row sum in pixel order, then the fp32 channel sums
+      if (oy > 0 && sp < CG / 2) {
+        const uint32_t *o32 = reinterpret_cast<const uint32_t *>(obuf + (size_t)((oy - 1) & 1) * Wo * CG);
+        uint32_t rs = 0u;
+        for (int x = 0; x < Wo; x++) rs = hadd2(rs, o32[(size_t)x * (CG / 2) + sp]);
+        cs.x = __fadd_rn(cs.x, h_lo(rs));
+        cs.y = __fadd_rn(cs.y, h_hi(rs));
+      }
+    } else if (comp) {
       for (int g = lane; g < ngrp; g += NL) {
         const int x0 = g * R;
         uint32_t a[R][4], a2[R][4];
@@ -598,7 +614,7 @@ __global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtens
     }
     if (!__syncthreads_and(ok)) break;  // every thread has left this step's rows and written its outputs
     if (tid == 0) issue_to((oy + 2) * S + 2);
-    if (tid < CG / 2) {  // channel pair tid: the fp16 row sum in pixel order, then the fp32 channel sums
+    if (SB >= (int)blockDim.x && tid < CG / 2) {  // channel pair tid: the fp16 row sum in pixel order, then fp32
       const uint32_t *o32 = reinterpret_cast<const uint32_t *>(ob);
       uint32_t rs = 0u;
       for (int x = 0; x < Wo; x++) rs = hadd2(rs, o32[(size_t)x * (CG / 2) + tid]);
@@ -614,7 +630,18 @@ __global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtens
     __syncthreads();
     return;
   }
-  if (tid < CG / 2) *reinterpret_cast<float2 *>(chsum + (size_t)win * cws + grp * CG + 2 * tid) = cs;
+  if (SB < (int)blockDim.x) {  // the summers add the last row (the compute threads are done with the tile)
+    if (summer && sp < CG / 2) {
+      const uint32_t *o32 = reinterpret_cast<const uint32_t *>(obuf + (size_t)((Ho - 1) & 1) * Wo * CG);
+      uint32_t rs = 0u;
+      for (int x = 0; x < Wo; x++) rs = hadd2(rs, o32[(size_t)x * (CG / 2) + sp]);
+      cs.x = __fadd_rn(cs.x, h_lo(rs));
+      cs.y = __fadd_rn(cs.y, h_hi(rs));
+      *reinterpret_cast<float2 *>(chsum + (size_t)win * cws + grp * CG + 2 * sp) = cs;
+    }
+  } else if (tid < CG / 2) {
+    *reinterpret_cast<float2 *>(chsum + (size_t)win * cws + grp * CG + 2 * tid) = cs;
+  }
 }
 
 // ------------------------------------------------------------------ SE f16 (src/v24_fast.c:186-235)
@@ -1244,13 +1271,23 @@ extern "C" int bnnk_dw3_f16(int B, const uint16_t *xp, long long xws, int H, int
       int nt = (256 / Q) * Q;
       if (nt < cg / 2) nt = cg / 2;
       nt = (nt + 31) / 32 * 32;
+      int sb = nt;
+      // rows of 16+ pixels: whole warps of summers, one row behind (the row sum is a chain of Wo dependent adds,
+      // which on the computing threads delayed every step), the computing threads within the rest of 256
+      const int ns = 32 * ((cg / 2 + 31) / 32);
+      if (Wo >= 16 && ((256 - ns) / Q) * Q >= Q) {
+        sb = ((256 - ns) / Q) * Q;
+        sb = (sb + 31) / 32 * 32;
+        nt = sb + ns;
+      }
       const bool pair = Wo % 2 == 0;
 #define BNN_DW3T16(SS, RR)                                                                                     \
   do {                                                                                                        \
     cudaError_t e_ = cudaFuncSetAttribute(k_dw3t_f16<SS, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
                                           (int)smem);                                                         \
     if (e_) return e_;                                                                                        \
-    k_dw3t_f16<SS, RR><<<grid, nt, smem, st>>>(map, W, C, cg, pt, pl, Ho, Wo, w, b, out, ows, chsum, cws, err); \
+    k_dw3t_f16<SS, RR><<<grid, nt, smem, st>>>(map, W, C, cg, pt, pl, Ho, Wo, w, b, out, ows, chsum, cws, err, \
+                                               sb);                                                            \
   } while (0)
       if (s == 1) { if (pair) BNN_DW3T16(1, 2); else BNN_DW3T16(1, 1); }
       else { if (pair) BNN_DW3T16(2, 2); else BNN_DW3T16(2, 1); }
