@@ -1272,10 +1272,12 @@ extern "C" int bnnk_dw3_f16(int B, const uint16_t *xp, long long xws, int H, int
       if (nt < cg / 2) nt = cg / 2;
       nt = (nt + 31) / 32 * 32;
       int sb = nt;
-      // rows of 16+ pixels: whole warps of summers, one row behind (the row sum is a chain of Wo dependent adds,
-      // which on the computing threads delayed every step), the computing threads within the rest of 256
+      // rows of 16+ pixels in groups of at most 64 channels: one warp of summers, one row behind (the row sum is a
+      // chain of Wo dependent adds, which on the computing threads delayed every step: Perch's 40-channel 249 x 63
+      // layer 0.95 -> 0.77 ms per 512 windows), the computing threads within the rest of 256. Wider groups need
+      // more summer warps, whose computing lanes cost more than the sums (144 and 192 channels: 8-10 % slower).
       const int ns = 32 * ((cg / 2 + 31) / 32);
-      if (Wo >= 16 && ((256 - ns) / Q) * Q >= Q) {
+      if (Wo >= 16 && cg <= 64 && ((256 - ns) / Q) * Q >= Q) {
         sb = ((256 - ns) / Q) * Q;
         sb = (sb + 31) / 32 * 32;
         nt = sb + ns;
