@@ -502,7 +502,7 @@ __global__ void __launch_bounds__(1024) k_dw3_f16(const uint16_t *__restrict__ x
 // double-buffered row tile; after the step's barrier the first CG / 2 threads add their channel pair's outputs over
 // the row in pixel order (the fp16 row sum) and flush it to their fp32 channel sums. Row v of the ring is input row
 // v + 1 - pt; pixel x of an output group reads input columns x S + 1 - pl ...
-template <int S, int R>
+template <int S, int R, bool kSum>
 __global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtensorMap tmx, int W, int C, int CG,
                                                   int pt, int pl, int Ho, int Wo, const uint16_t *__restrict__ wt,
                                                   const uint16_t *__restrict__ bt, uint16_t *__restrict__ out,
@@ -512,11 +512,11 @@ __global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtens
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ __align__(8) unsigned long long bar[NR];
   __shared__ uint32_t tab01[16], tab2[16];
-  // SB < blockDim.x: threads SB.. (whole warps) only sum, one step behind the others (row oy - 1 while row oy is
-  // computed); threads below SB compute (those past the last whole channel octet of lanes idle). SB == blockDim.x:
-  // the first CG / 2 threads also sum, after each step's barrier.
-  const int tid = threadIdx.x, nt = SB < (int)blockDim.x ? SB : (int)blockDim.x;
-  const bool summer = tid >= SB;
+  // kSum: threads SB.. (whole warps) only sum, one step behind the others (row oy - 1 while row oy is computed);
+  // threads below SB compute (those past the last whole channel octet of lanes idle). Otherwise the first CG / 2
+  // threads also sum, after each step's barrier.
+  const int tid = threadIdx.x, nt = kSum ? SB : (int)blockDim.x;
+  const bool summer = kSum && tid >= SB;
   const int sp = tid - SB;  // a summer's channel pair
   load_silu_tab(tab01, tab2);
   const int ngroups = C / CG;
@@ -565,7 +565,7 @@ __global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtens
       }
     }
     uint16_t *ob = obuf + (size_t)(oy & 1) * Wo * CG;
-    if (summer) {  // the previous row's fp16 row sum in pixel order, then the fp32 channel sums
+    if (kSum && summer) {  // the previous row's fp16 row sum in pixel order, then the fp32 channel sums
       if (oy > 0 && sp < CG / 2) {
         const uint32_t *o32 = reinterpret_cast<const uint32_t *>(obuf + (size_t)((oy - 1) & 1) * Wo * CG);
         uint32_t rs = 0u;
@@ -614,7 +614,7 @@ __global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtens
     }
     if (!__syncthreads_and(ok)) break;  // every thread has left this step's rows and written its outputs
     if (tid == 0) issue_to((oy + 2) * S + 2);
-    if (SB >= (int)blockDim.x && tid < CG / 2) {  // channel pair tid: the fp16 row sum in pixel order, then fp32
+    if (!kSum && tid < CG / 2) {  // channel pair tid: the fp16 row sum in pixel order, then fp32
       const uint32_t *o32 = reinterpret_cast<const uint32_t *>(ob);
       uint32_t rs = 0u;
       for (int x = 0; x < Wo; x++) rs = hadd2(rs, o32[(size_t)x * (CG / 2) + tid]);
@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtens
     __syncthreads();
     return;
   }
-  if (SB < (int)blockDim.x) {  // the summers add the last row (the compute threads are done with the tile)
+  if (kSum) {  // the summers add the last row (the compute threads are done with the tile)
     if (summer && sp < CG / 2) {
       const uint32_t *o32 = reinterpret_cast<const uint32_t *>(obuf + (size_t)((Ho - 1) & 1) * Wo * CG);
       uint32_t rs = 0u;
@@ -1283,17 +1283,20 @@ extern "C" int bnnk_dw3_f16(int B, const uint16_t *xp, long long xws, int H, int
         nt = sb + ns;
       }
       const bool pair = Wo % 2 == 0;
-#define BNN_DW3T16(SS, RR)                                                                                     \
+#define BNN_DW3T16_(SS, RR, KS)                                                                                \
   do {                                                                                                        \
-    cudaError_t e_ = cudaFuncSetAttribute(k_dw3t_f16<SS, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
+    cudaError_t e_ = cudaFuncSetAttribute(k_dw3t_f16<SS, RR, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                           (int)smem);                                                         \
     if (e_) return e_;                                                                                        \
-    k_dw3t_f16<SS, RR><<<grid, nt, smem, st>>>(map, W, C, cg, pt, pl, Ho, Wo, w, b, out, ows, chsum, cws, err, \
-                                               sb);                                                            \
+    k_dw3t_f16<SS, RR, KS><<<grid, nt, smem, st>>>(map, W, C, cg, pt, pl, Ho, Wo, w, b, out, ows, chsum, cws,  \
+                                                   err, sb);                                                  \
   } while (0)
+#define BNN_DW3T16(SS, RR) \
+  do { if (sb < nt) BNN_DW3T16_(SS, RR, true); else BNN_DW3T16_(SS, RR, false); } while (0)
       if (s == 1) { if (pair) BNN_DW3T16(1, 2); else BNN_DW3T16(1, 1); }
       else { if (pair) BNN_DW3T16(2, 2); else BNN_DW3T16(2, 1); }
 #undef BNN_DW3T16
+#undef BNN_DW3T16_
       return cudaGetLastError();
     }
   }
