@@ -1272,14 +1272,16 @@ extern "C" int bnnk_dw3_f16(int B, const uint16_t *xp, long long xws, int H, int
       if (nt < cg / 2) nt = cg / 2;
       nt = (nt + 31) / 32 * 32;
       int sb = nt;
-      // rows of 16+ pixels in groups of at most 64 channels: one warp of summers, one row behind (the row sum is a
-      // chain of Wo dependent adds, which on the computing threads delayed every step: Perch's 40-channel 249 x 63
-      // layer 0.95 -> 0.77 ms per 512 windows), the computing threads within the rest of 256. Wider groups need
-      // more summer warps, whose computing lanes cost more than the sums (144 and 192 channels: 8-10 % slower).
-      const int ns = 32 * ((cg / 2 + 31) / 32);
-      if (Wo >= 16 && cg <= 64 && ((256 - ns) / Q) * Q >= Q) {
-        sb = ((256 - ns) / Q) * Q;
-        sb = (sb + 31) / 32 * 32;
+      // rows of 16+ pixels: summer warps, one row behind (the row sum is a chain of Wo dependent adds, which on the
+      // computing threads delayed every step: Perch's 40-channel 249 x 63 layer 0.95 -> 0.77 ms per 512 windows,
+      // v2.4's 72-channel 24 x 64 layers 0.244 -> 0.206 ms per 1024), the computing threads within the rest of 256;
+      // only where the summers take at most two warps and leave the passes over a row's pixel groups as they were
+      // (144 and 192 channels, with three summer warps, ran 8-10 % slower)
+      const int ns = 32 * ((cg / 2 + 31) / 32), ngrp = Wo / (Wo % 2 == 0 ? 2 : 1);
+      const int sbc = ((256 - ns) / Q) * Q, nl_old = (256 / Q) * Q / Q, nl_new = sbc / Q;
+      if (Wo >= 16 && ns <= 64 && nl_new >= 1 &&
+          (ngrp + nl_new - 1) / nl_new == (ngrp + nl_old - 1) / nl_old) {
+        sb = (sbc + 31) / 32 * 32;
         nt = sb + ns;
       }
       const bool pair = Wo % 2 == 0;
