@@ -1,5 +1,6 @@
 // The fp32 ops of the v2.4 int8 package on CUDA cores: depthwise 3x3 + SiLU + channel sums (DW3), the SE gate
-// (SE_GATE), the c0 conv + pool (C0POOL) and the post BN + pc conv + mean (POSTPC); the front end is in k_fe.cu.
+// (SE_GATE), the c0 conv + pool (C0POOL) and the post BN + pc conv + mean (POSTPC); the front end is in k_fe.cu. Also
+// the fp32 stem of compiled models' fp16 path (STEM f16: fp32 math, fp16 output).
 // Each output is computed with the reference's operations in the reference's order (fused where the NEON code fuses,
 // rounded where it rounds), so the values are bit-identical; only the parallel schedule is ours, and no reference
 // reduction is split across threads except where its order is restated exactly.

@@ -1,4 +1,5 @@
-// The neon-fp16 path's kernels (the variant-1 ops of src/rt_ops_f16.c for the v2.4 architecture), bit for bit.
+// The neon-fp16 path's kernels (the variant-1 ops of src/rt_ops_f16.c: those of the v2.4 architecture and the DWK,
+// PAD and MEAN of compiled models such as Perch v2), bit for bit.
 //
 // The reference computes these layers with ARMv8.2 fp16 arithmetic in a fixed order: every multiply-add of its GEMMs
 // and depthwise convs is one fused fp16 FMLA lane operation, rounded once (src/gemm_f16.c, src/gemm_f16_kblock.h,

@@ -144,3 +144,25 @@ def test_perch_path_needs_dotprod_flag(tmp_path, perch_mini):
     with pytest.raises(BnnError) as e:
         Model(str(p), mode=3)
     assert "dotprod kernel (opcode 0x20d)" in str(e.value), str(e.value)
+
+
+def test_dwk_and_stem_entry_points_check_shapes_without_a_device():
+    """bnn_cuda_dwk_f16 / bnn_cuda_stem_f16 refuse shapes the reference's checks refuse before touching a device"""
+    from bnneon_b200 import load_library  # pylint: disable=import-outside-toplevel
+    h = load_library()
+    cases = [  # (args, text in the message)
+        ((1, 1, 0, 8, 8, 12, 3, 1, 1, 1, 1, 1, 1, 1, 0, 8, 8, 1, 0, None), "C % 8 == 0"),
+        ((1, 1, 0, 8, 8, 8, 4, 1, 1, 1, 1, 1, 1, 1, 0, 8, 8, 1, 0, None), "k odd"),
+        ((1, 1, 0, 8, 8, 8, 3, 3, 1, 1, 1, 1, 1, 1, 0, 3, 3, 1, 0, None), "s 1|2"),
+        ((1, 1, 0, 8, 8, 8, 3, 1, 2, 1, 1, 1, 1, 1, 0, 8, 8, 1, 0, None), "pt and pl"),
+        ((1, 1, 0, 8, 8, 8, 3, 1, 1, 1, 1, 1, 1, 1, 0, 9, 8, 1, 0, None), "taps inside the halo"),
+        ((1, 1, 0, 8, 4000, 8, 3, 1, 1, 1, 1, 1, 1, 1, 0, 8, 4000, 1, 0, None), "768 pixel groups"),
+    ]
+    for args, text in cases:
+        assert h.bnn_cuda_dwk_f16(*args) == -1
+        assert text in h.bnn_last_error().decode(), h.bnn_last_error()
+    assert h.bnn_cuda_stem_f16(1, 1, 0, 8, 8, 3, 1, 7, 6, 1, 1, 8, 12, 1, 1, 0, 8, 0, None) == -1
+    assert "VALID conv" in h.bnn_last_error().decode()
+    assert h.bnn_cuda_stem_f16(1, 1, 0, 8, 8, 3, 1, 6, 6, 1, 1, 8, 8, 1, 1, 0, 8, 0, None) == -1  # Kp < k k
+    assert h.bnn_cuda_stem_f16(1, 1, 0, 200, 200, 3, 1, 6, 6, 1, 1, 1024, 12, 1, 1, 0, 1024, 0, None) == -1  # > 48 KB
+    assert "48 KB" in h.bnn_last_error().decode()
