@@ -186,7 +186,9 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
     }
     float *ob = obuf + (oy & 1) * Wo * CG;
     if (comp) {
-      for (int g = lane; g < ngrp; g += NL) {
+      // groups in reverse lane order: when they do not divide evenly, the extra ones go to the high lanes, not to
+      // the low threads that also add the row sums after the barrier
+      for (int g = NL - 1 - lane; g < ngrp; g += NL) {
         const int x0 = g * R;
         float2 acc[R][2], acb[R][2], acd[R][2];
 #pragma unroll

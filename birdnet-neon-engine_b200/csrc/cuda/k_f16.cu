@@ -575,7 +575,9 @@ __global__ void __launch_bounds__(256) k_dw3t_f16(const __grid_constant__ CUtens
         cs.y = __fadd_rn(cs.y, h_hi(rs));
       }
     } else if (comp) {
-      for (int g = lane; g < ngrp; g += NL) {
+      // groups in reverse lane order: when they do not divide evenly, the extra ones go to the high lanes, not to
+      // the low threads that also add the row sums after the barrier
+      for (int g = NL - 1 - lane; g < ngrp; g += NL) {
         const int x0 = g * R;
         uint32_t a[R][4], a2[R][4];
 #pragma unroll
