@@ -463,6 +463,9 @@ static int init_dwk_f16(vctx *v) { /* dwk_init = rt_dwk_check(2), src/rt_ops_f16
                 groups);
   return 0;
 }
+/* PAD and MEAN of variant 1 take the shared checks as the reference registers them (rt_pad_check, rt_mean_check):
+ * sizes are checked in the buffers' own dtypes and the dtype itself is not pinned, while the kernels read 16-bit
+ * elements, as pc_pad_f16 / pc_mean_f16 do; the compiler only emits them on fp16 buffers */
 static int init_pad(vctx *v) { /* rt_pad_check, src/rt_ops_f32.c:474-492 (pad_f16: src/rt_ops_f16.c:204-208) */
   if (vneed_args(v, 2, -1, 5)) return -1;
   const int *p = v->op->p;
