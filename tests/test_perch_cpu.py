@@ -166,3 +166,41 @@ def test_dwk_and_stem_entry_points_check_shapes_without_a_device():
     assert h.bnn_cuda_stem_f16(1, 1, 0, 8, 8, 3, 1, 6, 6, 1, 1, 8, 8, 1, 1, 0, 8, 0, None) == -1  # Kp < k k
     assert h.bnn_cuda_stem_f16(1, 1, 0, 200, 200, 3, 1, 6, 6, 1, 1, 1024, 12, 1, 1, 0, 1024, 0, None) == -1  # > 48 KB
     assert "48 KB" in h.bnn_last_error().decode()
+
+
+
+def op_macs(code, p):
+    """(class, MACs per window) of one op record of the Perch package"""
+    if code == 0x103:  # PW: M K N
+        return "1x1", p[4] * p[1] * p[0]
+    if code == 0x104:  # DW3: Ho Wo C 9
+        return "dw3x3", p[4] * p[5] * p[2] * 9
+    if code == 0x10A:  # DWK: Ho Wo C k k
+        return f"dw{p[3]}x{p[3]}", p[7] * p[8] * p[2] * p[3] * p[3]
+    if code == 0x109:  # STEM: Ho Wo N K
+        return "stem", p[6] * p[7] * p[0] * p[1]
+    if code == 0x20D:  # PROTO: cells K prototypes
+        return "proto", p[3] * p[1] * p[0]
+    return None, 0
+
+
+def test_perch_package_has_perch_v2_work(tmp_path):
+    """The full synthetic package does Perch v2's work: per window, the MACs of its op records against the reference's
+    published table for the Perch v2 graph (results/perch_mac_table.txt:2-13: 1x1 convs 1096.3 + head conv 37.7, dw 5x5
+    56.2, dw 3x3 36.0, stem 5.6 MMAC, body 1233 MMAC, prototype head 5817.6 MMAC)."""
+    from bnneon_b200 import pkgread  # pylint: disable=import-outside-toplevel
+    path = str(tmp_path / "perch_full.bnpk")
+    synth.make_perch_package(path, seed=0)
+    ops, _ = pkgread.read_ops(path, synth.PATH_F16)
+    mac, body = {}, 0.0
+    for code, _, _, p in ops:
+        k, m = op_macs(code, p)
+        if k:
+            mac[k] = mac.get(k, 0.0) + m / 1e6
+            body += m / 1e6 if k != "proto" else 0.0
+    assert abs(mac["1x1"] - (1096.3 + 37.7)) / 1134.0 < 0.005, mac
+    assert abs(mac["dw5x5"] - 56.2) / 56.2 < 0.01, mac
+    assert abs(mac["dw3x3"] - 36.0) / 36.0 < 0.01, mac
+    assert abs(mac["stem"] - 5.6) / 5.6 < 0.02, mac
+    assert abs(body - 1233.0) / 1233.0 < 0.005, (body, mac)
+    assert abs(mac["proto"] - 5817.6) / 5817.6 < 1e-4, mac
