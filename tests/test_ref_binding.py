@@ -51,3 +51,36 @@ def test_reference_binding_infer_matches(refb, mini_pkg):
         assert bits_equal(got[i][0], out[i]), mismatch_report(got[i][0], out[i])
         assert bits_equal(got[i][1], emb[i]), mismatch_report(got[i][1], emb[i])
     assert labels is not None and len(labels) == 64
+
+
+@pytest.fixture(scope="module")
+def perch_mini_pkg(tmp_path_factory):
+    path = str(tmp_path_factory.mktemp("refb_perch") / "perch_mini.bnpk")
+    synth.make_perch_package(path, seed=3, mini=True)
+    return path
+
+
+def test_reference_binding_probes_a_perch_package(refb, perch_mini_pkg):
+    """the reference's binding probes a Perch-architecture fp16 package through this library (no GPU needed)"""
+    info = refb.probe(perch_mini_pkg, lib=DEFAULT_LIB)
+    assert info.n_samples == 80000 and info.n_classes == 61 and info.emb_dim == 1536
+    assert info.path == b"neon-fp16"
+
+
+@pytest.mark.gpu
+def test_reference_binding_runs_a_perch_package(refb, perch_mini_pkg):
+    """mode 3 (neon-fp16) through the reference's binding: logits and the 1536-d embedding bit for bit against this
+    repository's batched entry point"""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.fail("a GPU test ran without a visible CUDA device")
+    from bnneon_b200 import Model  # pylint: disable=import-outside-toplevel
+    pcm = synth.audio(2, seed=78, n_samples=80000, rate=synth.PERCH_SAMPLE_RATE)
+    with refb.Model(perch_mini_pkg, mode=3, lib=DEFAULT_LIB) as m:
+        assert m.info.path == b"neon-fp16"
+        got = [m.infer(pcm[i]) for i in range(2)]
+    with Model(perch_mini_pkg, mode=3, batch=2) as ours:
+        out, emb = ours.infer_batch(pcm)
+    for i in range(2):
+        assert bits_equal(got[i][0], out[i]), mismatch_report(got[i][0], out[i])
+        assert bits_equal(got[i][1], emb[i]), mismatch_report(got[i][1], emb[i])
