@@ -1128,10 +1128,11 @@ int bnn_cuda_dwk_f16(int B, const void *d_xp, long long xws, int H, int W, int C
   if (B < 0 || H <= 0 || W <= 0 || Ho <= 0 || Wo <= 0 || C <= 0 || C % 8 || k < 1 || k > 7 || k % 2 == 0 ||
       (s != 1 && s != 2) || pt < 0 || pt > h || pl < 0 || pl > h || act < 0 || act > 1 ||
       (Ho - 1) * s - pt + k > H + h || (Wo - 1) * s - pl + k > W + h || groups > 768 || xws % 2 || ows % 2 ||
+      (B > 1 && (xws < (long long)(H + 2 * h) * (W + 2 * h) * C || ows < (long long)Ho * Wo * C || cws < C)) ||
       !d_xp || !d_w || !d_b || !d_out || !d_chsum) {
     ERR(BNN_ERR_USAGE, "bnn_cuda_dwk_f16: H %d W %d C %d k %d s %d pt %d pl %d act %d Ho %d Wo %d (C %% 8 == 0, k odd "
-        "1..7, s 1|2, pt and pl <= (k - 1) / 2, taps inside the halo, at most 768 pixel groups per row, even strides)",
-        H, W, C, k, s, pt, pl, act, Ho, Wo);
+        "1..7, s 1|2, pt and pl <= (k - 1) / 2, taps inside the halo, at most 768 pixel groups per row, even window "
+        "strides of at least one window)", H, W, C, k, s, pt, pl, act, Ho, Wo);
     return -1;
   }
   return launch_rc("bnn_cuda_dwk_f16", bnnk_dwk_f16(B, d_xp, xws, W, C, k, s, pt, pl, d_w, d_b, act, d_out, ows, Ho,
@@ -1145,10 +1146,12 @@ int bnn_cuda_stem_f16(int B, const float *d_img, long long iws, int H, int W, in
   const int Np = (N + 7) & ~7;
   if (B < 0 || k < 1 || s < 1 || Ho <= 0 || Wo <= 0 || N <= 0 || (Ho - 1) * s + k > H || (Wo - 1) * s + k > W ||
       Kp < k * k || Kp % 4 || ldo < Np || opad < 0 || opad > 3 || act < 0 || act > 2 ||
-      ((size_t)Np * Kp + Np) * 4 > 48 * 1024 || !d_img || !d_w || !d_b || !d_out) {
+      ((size_t)Np * Kp + Np) * 4 > 48 * 1024 ||
+      (B > 1 && (iws < (long long)H * W || ows < (long long)(Ho + 2 * opad) * (Wo + 2 * opad) * ldo)) || !d_img ||
+      !d_w || !d_b || !d_out) {
     ERR(BNN_ERR_USAGE, "bnn_cuda_stem_f16: H %d W %d k %d s %d Ho %d Wo %d N %d Kp %d act %d ldo %d opad %d (VALID "
-        "conv, Kp >= k k and a multiple of 4, ldo >= N rounded up to 8, opad 0..3, act 0..2, weights within 48 KB)",
-        H, W, k, s, Ho, Wo, N, Kp, act, ldo, opad);
+        "conv, Kp >= k k and a multiple of 4, ldo >= N rounded up to 8, opad 0..3, act 0..2, weights within 48 KB, "
+        "window strides of at least one window)", H, W, k, s, Ho, Wo, N, Kp, act, ldo, opad);
     return -1;
   }
   return launch_rc("bnn_cuda_stem_f16", bnnk_stem_f16(B, d_img, iws, W, k, s, Ho, Wo, d_w, d_b, N, Kp, Np, act, d_out,

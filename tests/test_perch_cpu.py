@@ -166,6 +166,11 @@ def test_dwk_and_stem_entry_points_check_shapes_without_a_device():
     assert h.bnn_cuda_stem_f16(1, 1, 0, 8, 8, 3, 1, 6, 6, 1, 1, 8, 8, 1, 1, 0, 8, 0, None) == -1  # Kp < k k
     assert h.bnn_cuda_stem_f16(1, 1, 0, 200, 200, 3, 1, 6, 6, 1, 1, 1024, 12, 1, 1, 0, 1024, 0, None) == -1  # > 48 KB
     assert "48 KB" in h.bnn_last_error().decode()
+    # two windows whose strides are shorter than a window
+    assert h.bnn_cuda_dwk_f16(2, 1, 100, 8, 8, 8, 3, 1, 1, 1, 1, 1, 1, 1, 512, 8, 8, 1, 8, None) == -1
+    assert "at least one window" in h.bnn_last_error().decode()
+    assert h.bnn_cuda_stem_f16(2, 1, 50, 8, 8, 3, 1, 6, 6, 1, 1, 8, 12, 1, 1, 288, 8, 0, None) == -1
+    assert "at least one window" in h.bnn_last_error().decode()
 
 
 
