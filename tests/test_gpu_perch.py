@@ -195,3 +195,23 @@ def test_dwk_and_stem_refuse_bad_shapes(lib):
     assert lib.bnn_cuda_dwk_f16(1, 1, 0, 8, 8, 8, 4, 1, 1, 1, 1, 1, 1, 1, 0, 8, 8, 1, 0, None) == -1
     assert lib.bnn_cuda_stem_f16(1, 1, 0, 8, 8, 3, 1, 7, 6, 1, 1, 8, 12, 1, 1, 0, 8, 0, None) == -1
     assert "VALID conv" in lib.bnn_last_error().decode()
+
+
+def test_perch_nonfinite_logits_fail_the_window(lib, tmp_path):
+    """class weights of 1e38 send the logits past 3e38: pc_proto_logits returns -2 (src/pc_kern_f32.c:364-376), the
+    oracle refuses the window, and the library reports every window failed (BNN_ERR_WINDOW, the prototype head and
+    the first failed window named), as the reference's rt_run / bnn_infer report it"""
+    from bnneon_b200 import BnnError  # pylint: disable=import-outside-toplevel
+    ops, vshape, lv, ev, fe = synth.perch_ir(4, mini=True)
+    for o in ops:
+        if o["op"] == "PROTO":
+            o["cw"] = np.full_like(o["cw"], 1e38)
+    pkg = str(tmp_path / "perch_overflow.bnpk")
+    synth.write_perch_package(pkg, (ops, vshape, lv, ev, fe))
+    pcm = synth.audio(3, seed=6, n_samples=fe["nsamp"], rate=synth.PERCH_SAMPLE_RATE)
+    with pytest.raises(RuntimeError):
+        oracle.Package(pkg, PATH).run(pcm[0])
+    with Model(pkg, mode=3, batch=4) as m:
+        with pytest.raises(BnnError) as e:
+            m.infer_batch(pcm)
+        assert e.value.kind == "WINDOW" and "proto_s8" in str(e.value) and "window 0" in str(e.value), str(e.value)
