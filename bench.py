@@ -15,8 +15,10 @@ Printed (rank 0, one JSON line):
           embeddings inside the timed region;
   roofline  the op class with the most device time (per-op CUDA events): algorithmic bytes / its time vs the
           measured HBM copy bandwidth (MEASURED_PEAKS.json);
-  cpu_baseline  the CPU oracle (a C restatement of the reference's int8 path; the reference's NEON build does not
-          compile on x86) on this host's cores, a bounded sample of the same windows.
+  cpu_baseline  the reference's own C runtime (oracle/_ref: its unmodified sources compiled for x86, NEON intrinsics
+          through a scalar stand-in) on this host's cores, a bounded sample of the same windows; the C restatement
+          of the reference's path (oracle/liboracle.so) where that build is absent;
+  parity_checked  the timed calls' outputs against the CPU oracle, after timing.
 `--impl reference` times that CPU implementation alone on rank 0 (the reference arm).
 """
 import argparse
@@ -69,7 +71,7 @@ def op_cost(code, p, bufs, bl):
 
 PROFILE = os.path.join(REPO, "profiles", "launch_list_v24_int8_b256.md")
 NCU_CMD = ("ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum --clock-control none "
-           "-s {skip} -c {count} --csv --log-file gpurun_out/launches.csv python bench.py --ncu --warmup 3")
+           "-s {skip} -c {count} --csv --log-file <out>/launches.csv python bench.py --ncu --warmup 3")
 # the kernels each op launches, in order (the runtime's op registry)
 OP_KERNELS = {1: ("k_fe_minmax", "k_fe_spec"), 2: ("k_c0pool",), 22: ("k_quant", "k_gemm_s8"),
               23: ("k_quant", "k_gemm_s8"), 4: ("k_dw3",), 25: ("k_se_gate",), 6: ("k_postpc_im2col", "k_postpc_gemm")}
@@ -129,7 +131,7 @@ def ncu_summary(csv_path, batch):
            "Command (GPU box, after the same command line without `ncu` exited 0):", "",
            "    python bench.py --ncu --warmup 3 && \\",
            "    " + NCU_CMD.format(skip=3 * len(lst), count=len(lst)), "",
-           "then `python bench.py --ncu-summary gpurun_out/launches.csv` wrote this file. Per-launch times are",
+           "then `python bench.py --ncu-summary <out>/launches.csv` wrote this file. Per-launch times are",
            "serialised and cold-cache (ncu flushes caches between launches); the shares are what compare with the",
            "bench's per-op CUDA-event times. DRAM bytes are `dram__bytes_read.sum + dram__bytes_write.sum`.", "",
            "| kernel | launches | total µs | share | DRAM MB | GB/s |", "|---|---:|---:|---:|---:|---:|"]
@@ -162,7 +164,7 @@ def profile_traffic(cls_name, batch):
 
 
 def c1_gemm(m, torch, stream, peak_bf16):
-    """BASELINE config 1 timed: one int8 GEMM M 4096 x K 256 x N 512 on given int8 rows through
+    """Config 1 timed: one int8 GEMM M 4096 x K 256 x N 512 on given int8 rows through
     bnn_pw_s8_gemm, 50 launches back to back, CUDA events on their stream; fp32 outputs (the harness requant is in
     the parity test). int8 ops = 2 M N K per launch."""
     from bnneon_b200 import synth  # pylint: disable=import-outside-toplevel
@@ -235,7 +237,7 @@ def int8_peak(torch):
 
 
 def proto_setup(h, torch, batch, seed=2024):
-    """The Perch v2 prototype head (64 cells x 1536 channels -> 14795 classes x 4 prototypes) as a
+    """The Perch v2 prototype head (config 4: 64 cells x 1536 channels -> 14795 classes x 4 prototypes) as a
     bnn_proto_s8 op for `batch` windows, with seeded N(0, 1) cells resident on the device."""
     from bnneon_b200 import synth  # pylint: disable=import-outside-toplevel
     c = PROTO_C4
@@ -291,7 +293,7 @@ def proto_cpu_baseline(keep, n, seconds=15.0):
 
 
 def proto_head_c4(h, torch, stream, peak_bf16, cpu=True):
-    """SURVEY C4's int8 head timed: PROTO_S8 (per-cell quantizer, tcgen05 column-max GEMM, logits) on 512 windows
+    """Config 4's int8 head timed: PROTO_S8 (per-cell quantizer, tcgen05 column-max GEMM, logits) on 512 windows
     through bnn_proto_s8_run, inputs resident, 20 runs back to back after 3 warm-ups, CUDA events on their stream.
     The GEMM is tensor-core bound (M 32768 cells x N 59180 x K 1536: 5.96 T int8 ops per run)."""
     c = PROTO_C4
@@ -443,6 +445,9 @@ def fp16_package_leg(torch, stream, pkg, pcm, batch, steps, cpu, workload, parit
         for _ in range(3):
             m.infer_batch(h_pcm.numpy(), h_out.numpy(), h_emb.numpy())
         e2e_ms = (time.perf_counter() - t0) * 1e3 / 3
+        stream.synchronize()
+        timed_out = {"bnn_infer_batch": (h_out.numpy().copy(), h_emb.numpy().copy()),
+                     "bnn_infer_device": (d_out.cpu().numpy(), d_emb.cpu().numpy())}
         # per-op classes
         ops, _ = pkgread.read_ops(pkg, synth.PATH_F16)
         m.h.bnn_profile_begin(m.ctx)
@@ -465,15 +470,17 @@ def fp16_package_leg(torch, stream, pkg, pcm, batch, steps, cpu, workload, parit
     tflops = pw["flop"] / (pw["ms"] * 1e-3) / 1e12
     base = None
     if cpu:
-        from oracle import oracle  # pylint: disable=import-outside-toplevel
         cores = os.cpu_count() or 1
         n = min(batch, cores)
+        kind, crun, what = cpu_runner(pkg, mode=3)
         t0 = time.perf_counter()
-        oracle.run_many(pkg, pcm[:n], threads=cores, path_name=synth.PATH_F16)
+        crun(pcm[:n], cores)
         dt = time.perf_counter() - t0
-        base = {"value": round(n / dt, 3), "unit": "windows/s", "cores": cores, "kind": "port",
-                "sample": f"{n} windows, one per thread: oracle/liboracle.so (the C restatement of the reference's "
-                          f"neon-fp16 path, every fp16 operation emulated exactly in software), {dt:.1f} s"}
+        base = {"value": round(n / dt, 3), "unit": "windows/s", "cores": cores, "kind": kind,
+                "sample": f"{n} windows, one per thread, {dt:.1f} s: {what} (every fp16 operation emulated exactly "
+                          f"in software)"}
+    checked = (parity_check(pkg, pcm, timed_out, chunk_boundary_sample(batch, batch, 4), synth.PATH_F16,
+                            os.cpu_count() or 1) if cpu else None)
     total = sum(v["ms"] for v in cls.values())
     return {"workload": workload,
             "batch": batch, "ms_per_step": round(ms, 3), "windows_per_s": round(batch / (ms * 1e-3), 1),
@@ -488,11 +495,11 @@ def fp16_package_leg(torch, stream, pkg, pcm, batch, steps, cpu, workload, parit
                          "note": "achieved = 2 M K N of the 1x1 convs (Kp, Np as packed) / their CUDA-event time"},
             "ops": {k: {"ms": round(v["ms"], 4), "share": round(v["ms"] / total, 4), "ops": v["ops"]}
                     for k, v in sorted(cls.items(), key=lambda kv: -kv[1]["ms"])},
-            "parity": parity, "cpu_baseline": base}
+            "parity": parity, "parity_checked": checked, "cpu_baseline": base}
 
 
 def v24_fp16_c3(torch, stream, batch=1024, steps=10, cpu=True):
-    """the v2.4-architecture neon-fp16 package (the reference compiler's bytes for the same synthetic IR)
+    """Config 3: the v2.4-architecture neon-fp16 package (the reference compiler's bytes for the same synthetic IR)
     on `batch` windows."""
     from bnneon_b200 import synth  # pylint: disable=import-outside-toplevel
     pkg = os.path.join(tempfile.mkdtemp(), "v24_full_f16.bnpk")
@@ -506,7 +513,7 @@ def v24_fp16_c3(torch, stream, batch=1024, steps=10, cpu=True):
 
 
 def perch_c4(torch, stream, batch=512, steps=5, cpu=True):
-    """a Perch-v2-architecture package, neon-fp16 body + the int8 SDOT prototype head (bnc.py compile
+    """Config 4: a Perch-v2-architecture package, neon-fp16 body + the int8 SDOT prototype head (bnc.py compile
     --paths neon-fp16 --proto-s8), 160000-sample windows at 32 kHz, 59180 prototypes, on `batch` windows."""
     from bnneon_b200 import synth  # pylint: disable=import-outside-toplevel
     pkg = os.path.join(tempfile.mkdtemp(), "perch_v2_f16s8.bnpk")
@@ -616,51 +623,100 @@ class Clocks:
                 "reasons": reasons, "samples": len(sm), "source": "nvml" if self.nv else "nvidia-smi"}
 
 
+REF_SAMPLE = ("the reference's own C runtime (its src/*.c, unmodified) compiled for this x86 host by oracle/ref.mk: "
+              "NEON intrinsics through a scalar stand-in written from the Arm ARM, auto-vectorized by GCC; one "
+              "single-threaded bnn_init context per host thread (windows are independent)")
+PORT_SAMPLE = "oracle/liboracle.so, the C restatement of the reference's neon-int8 path"
+
+
+def cpu_runner(pkg, mode=4):
+    """The CPU implementation the baselines time: the reference build (oracle/_ref) when present, else the port.
+    Returns (kind, run(pcm, threads), description)."""
+    from oracle import oracle, ref  # pylint: disable=import-outside-toplevel
+    if ref.available():
+        def run(x, threads):
+            _, _, rc = ref.run_many(pkg, mode, x, threads=threads)
+            if rc.any():
+                raise RuntimeError("reference build: a window failed")
+        return "reference", run, REF_SAMPLE
+
+    def run_port(x, threads):
+        oracle.run_many(pkg, x, threads=threads, path_name="neon-int8" if mode == 4 else "neon-fp16")
+    return "port", run_port, PORT_SAMPLE
+
+
 def cpu_baseline(pkg, pcm, seconds=12.0):
-    """The CPU oracle on all host cores over a bounded sample: windows/s."""
-    from oracle import oracle  # pylint: disable=import-outside-toplevel
+    """The reference's CPU implementation on all host cores over a bounded sample: windows/s."""
     cores = os.cpu_count() or 1
+    kind, run, what = cpu_runner(pkg)
     t = time.time()
-    oracle.run_many(pkg, pcm[:cores], threads=cores)  # calibration round: one window per core
+    run(pcm[:cores], cores)  # calibration round: one window per core
     per_round = time.time() - t
     rounds = max(1, min(16, int(seconds / max(per_round, 1e-3))))
     n = min(pcm.shape[0], cores * rounds)
     reps = max(1, (cores * rounds) // n)
     t = time.time()
     for _ in range(reps):
-        oracle.run_many(pkg, pcm[:n], threads=cores)
+        run(pcm[:n], cores)
     dt = time.time() - t
-    return {"value": round(n * reps / dt, 3), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{n * reps} windows ({reps} x {n}) of the same synthetic batch, oracle/liboracle.so "
-                      f"(C restatement of the reference's neon-int8 path) on {cores} threads, {dt:.1f} s"}
+    return {"value": round(n * reps / dt, 3), "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{n * reps} windows ({reps} x {n}) of the same synthetic batch on {cores} threads, {dt:.1f} s: "
+                      f"{what}"}
+
+
+def parity_check(pkg, pcm, results, idx, path_name, threads):
+    """The checker, after the timed regions: the outputs the timed calls produced for the windows `idx` of the timed
+    batch against the CPU oracle (oracle/liboracle.so), bit for bit. results = {call name: (out, emb)}."""
+    from oracle import oracle  # pylint: disable=import-outside-toplevel
+    want, wemb = oracle.run_many(pkg, np.ascontiguousarray(pcm[idx]), threads=max(1, min(threads, len(idx))),
+                                 path_name=path_name)
+    bad = 0
+    for out, emb in results.values():
+        for j, w in enumerate(idx):
+            same = np.array_equal(np.asarray(out[w]).view(np.int32), want[j].view(np.int32))
+            if emb is not None:
+                same = same and np.array_equal(np.asarray(emb[w]).view(np.int32), wemb[j].view(np.int32))
+            bad += 0 if same else 1
+    return {"windows": len(idx), "calls": sorted(results), "mismatched": bad, "bit_exact": bad == 0,
+            "against": "oracle/liboracle.so (CPU restatement of the reference path), logits and embeddings"}
+
+
+def chunk_boundary_sample(n, batch, k):
+    """k windows of a batch of n: the first and last, both sides of the first chunk boundary of bnn_infer_batch (a
+    quarter of the batch, rounded up to 8) and evenly spaced ones"""
+    c = (min(n, batch) // 4 + 7) // 8 * 8 if min(n, batch) >= 64 else n
+    idx = {0, n - 1, min(c, n - 1), max(c - 1, 0)}
+    for w in np.linspace(0, n - 1, k).astype(int):
+        if len(idx) >= k:
+            break
+        idx.add(int(w))
+    return np.array(sorted(idx))
 
 
 def reference_arm(args, rank):
     if rank != 0:
         return
     from bnneon_b200 import synth  # pylint: disable=import-outside-toplevel
-    from oracle import oracle  # pylint: disable=import-outside-toplevel
     cores = os.cpu_count() or 1
     with tempfile.TemporaryDirectory() as td:
         pkg = os.path.join(td, "v24_full.bnpk")
         synth.make_package(pkg, seed=0)
+        kind, run, what = cpu_runner(pkg)
         n = 2 * cores  # a bounded sample per step
         pcm = synth.audio(n, seed=100)
         for _ in range(args.warmup):
-            oracle.run_many(pkg, pcm, threads=cores)
+            run(pcm, cores)
         t = time.time()
         for _ in range(args.steps):
-            oracle.run_many(pkg, pcm, threads=cores)
+            run(pcm, cores)
         dt = time.time() - t
     value = n * args.steps / dt
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic", "impl": "reference",
             "config": {"workload": WORKLOAD, "batch_per_gpu": args.batch, "cpu_sample_windows_per_step": n},
-            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": f"{n} windows per step on {cores} threads: oracle/liboracle.so, the C "
-                                       f"restatement of the reference's neon-int8 path (its NEON build does not "
-                                       f"compile on an x86 host)"},
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": kind,
+                             "sample": f"{n} windows per step on {cores} threads: {what}"},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -839,6 +895,19 @@ def main():
            "d2h_bytes_per_step": B * (nc + ne) * 4, "ms_per_step": round(e2e_ms, 3),
            "path": "bnn_infer_batch (C ABI), pinned host buffers"}
 
+    # ---- the checker: the timed calls' outputs against the CPU oracle (every window at N = 1, a sample per rank
+    # otherwise, so that N processes share the host cores)
+    torch.cuda.synchronize()
+    idx = np.arange(B) if world == 1 else chunk_boundary_sample(B, B, 16)
+    parity = parity_check(pkg, pcm, {"bnn_infer_batch": (out_np, emb_np),
+                                     "bnn_infer_device": (d_out.cpu().numpy(), d_emb.cpu().numpy())},
+                          idx, synth.PATH, max(1, (os.cpu_count() or 1) // world))
+    if world > 1:
+        t = torch.tensor([parity["mismatched"], parity["windows"]], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        parity.update({"mismatched": int(t[0].item()), "windows": int(t[1].item()), "bit_exact": int(t[0].item()) == 0,
+                       "scope": f"{len(idx)} windows per rank, {world} ranks"})
+
     # ---- per-op device times (CUDA events around every op on the launching stream)
     from bnneon_b200 import pkgread  # pylint: disable=import-outside-toplevel
     ops, bufs = pkgread.read_ops(pkg)
@@ -904,6 +973,7 @@ def main():
                             "ms_per_step": round(s8_ms, 4),
                             "note": "int8 ops of PW_S8 + GEMV_S8 (quantizer + tcgen05 GEMM) per second; these GEMMs "
                                     "are HBM-bound (AI far below the int8 ridge)"},
+                "parity_checked": parity,
                 "ops": ops_summary, "clocks": clocks, "s8_gemm_c1": c1, "proto_s8_c4": proto,
                 "fe_logmel_perch": logmel, "v24_fp16_c3": fp16, "perch_v2_fp16_s8_c4": perch}
         if not args.no_cpu_baseline and world == 1:

@@ -17,6 +17,7 @@
 #include <stdint.h>
 
 #include "bnn_kernels.h"
+#include "smem_attr.cuh"
 #include "emu.cuh"
 
 namespace bnn {
@@ -390,14 +391,9 @@ extern "C" int bnnk_fe_stft2(int B, const float *pcm, long long pws, const bnnk_
                                     ff * (t->khi[br] - t->klo[br]));
   };
   const size_t smem = need(10, 0) > need(9, 1) ? need(10, 0) : need(9, 1);
-  static size_t attr[64];  // per device: function attributes are per context
-  int dev = 0;
-  if (cudaGetDevice(&dev) || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (smem > attr[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(k_fe_spec, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e) return e;
-    attr[dev] = smem;
-  }
+  static SmemAttr attr;
+  const cudaError_t e = attr.ensure(k_fe_spec, smem);
+  if (e) return e;
   k_fe_minmax<<<B, 512, 0, st>>>(pcm, pws, minmax);
   k_fe_spec<<<dim3((kNfr + kFG - 1) / kFG, 2, B), 256, smem, st>>>(pcm, pws, minmax, *t, img, iws);
   return cudaGetLastError();

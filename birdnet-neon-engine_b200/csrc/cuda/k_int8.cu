@@ -26,6 +26,7 @@
 #include <mutex>
 
 #include "bnn_kernels.h"
+#include "smem_attr.cuh"
 #include "emu.cuh"
 #include "sync.cuh"
 #include "tc.cuh"
@@ -605,17 +606,10 @@ extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_
 
 template <int SW, bool kSP>
 static int launch_gemm(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
-  // the dynamic shared memory this instantiation may use so far, per device (function attributes are per context;
-  // static + dynamic <= 227 KB)
-  static size_t attr[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (p->smem > attr[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(k_gemm_s8<SW, kSP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)p->smem);
-    if (e) return e;
-    attr[dev] = p->smem;
-  }
+  // the dynamic shared memory this instantiation may use so far, per device (static + dynamic <= 227 KB)
+  static SmemAttr attr;
+  const cudaError_t e = attr.ensure(k_gemm_s8<SW, kSP>, p->smem);
+  if (e) return e;
   const int grid = a.tiles < num_sms() ? a.tiles : num_sms();
   k_gemm_s8<SW, kSP><<<grid, 64 + 128 * a.ne * a.nh, p->smem, st>>>(*(const CUtensorMap *)p->tma_a,
                                                                     *(const CUtensorMap *)p->tma_b, a);

@@ -28,6 +28,7 @@
 #include <string.h>
 
 #include "bnn_kernels.h"
+#include "smem_attr.cuh"
 #include "emu.cuh"
 #include "sync.cuh"
 #include "tc.cuh"
@@ -454,15 +455,9 @@ extern "C" int bnnk_proto_plan_init(bnnk_proto_plan *p, const int8_t *w, int np,
 
 template <int U, int MH>
 static int launch_colmax(const bnnk_proto_plan *p, const ProtoArgs &a, bnn_stream_t st) {
-  static size_t attr[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (p->smem > attr[dev]) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(k_proto_colmax<U, MH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p->smem);
-    if (e) return e;
-    attr[dev] = p->smem;
-  }
+  static SmemAttr attr;
+  const cudaError_t e = attr.ensure(k_proto_colmax<U, MH>, p->smem);
+  if (e) return e;
   const int grid = a.tiles < num_sms() ? a.tiles : num_sms();
   k_proto_colmax<U, MH><<<grid, 64 + 128 * a.ne * a.nh, p->smem, st>>>(*(const CUtensorMap *)p->tma_w,
                                                                       *(const CUtensorMap *)p->tma_q, a);

@@ -1,0 +1,31 @@
+// The dynamic shared memory a kernel may use above the 48 KB default, raised per device the first time a launch needs
+// more. Function attributes belong to the device's primary context: after a host calls cudaDeviceReset they are gone
+// (as is every other piece of module state, e.g. the address of a __device__ array) while the sizes recorded here
+// stay, so a process must not call this library on a device after resetting it.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+#include <mutex>
+
+namespace bnn {
+
+constexpr int kAttrDevices = 64;
+
+struct SmemAttr {
+  std::mutex mu;  // host threads of several contexts may launch the same kernel on one device at once
+  size_t cur[kAttrDevices] = {};
+
+  template <typename Kernel>
+  cudaError_t ensure(Kernel *kernel, size_t smem) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) || dev < 0 || dev >= kAttrDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (smem <= cur[dev]) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (!e) cur[dev] = smem;
+    return e;
+  }
+};
+
+}  // namespace bnn

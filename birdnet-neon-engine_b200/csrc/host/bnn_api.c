@@ -486,14 +486,18 @@ int bnn_infer_batch(bnn_ctx *c, int n, const float *pcm, float *out, float *emb)
   if (n == 0) return 0;
   dev_job jobs[64];
   pthread_t th[64];
+  char started[64] = {0};
   const int nd = c->n_dev < n ? c->n_dev : n;
   for (int i = 0; i < nd; i++) {
     jobs[i] = (dev_job){c, i, (int)((long long)n * i / nd), (int)((long long)n * (i + 1) / nd), 0, pcm, out, emb, "", 0};
-    if (nd > 1) pthread_create(&th[i], NULL, dev_worker, &jobs[i]);
-    else dev_worker(&jobs[i]);
+    /* one host thread per further GPU; a GPU whose thread cannot be created is driven from this thread instead, so
+     * every window is still scored */
+    if (i > 0 && nd > 1 && pthread_create(&th[i], NULL, dev_worker, &jobs[i]) == 0) started[i] = 1;
   }
-  if (nd > 1)
-    for (int i = 0; i < nd; i++) pthread_join(th[i], NULL);
+  for (int i = 0; i < nd; i++)
+    if (!started[i]) dev_worker(&jobs[i]);
+  for (int i = 1; i < nd; i++)
+    if (started[i]) pthread_join(th[i], NULL);
   for (int i = 0; i < nd; i++)
     if (jobs[i].rc) {
       ERR(jobs[i].kind ? jobs[i].kind : BNN_ERR_WINDOW, "%s", jobs[i].err);

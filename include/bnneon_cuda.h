@@ -10,7 +10,11 @@
  * taking device pointers, for hosts that run their own graphs and for the parity tests.
  *
  * Pointers named d_* are device pointers on the current CUDA device; `stream` is a cudaStream_t (NULL = the legacy
- * default stream). Functions return 0 on success, else -1 with bnn_last_error / bnn_last_error_kind set. */
+ * default stream). Functions return 0 on success, else -1 with bnn_last_error / bnn_last_error_kind set.
+ *
+ * Device reset: the library keeps per-device state for the life of the process (kernels' shared-memory limits, the
+ * address of bnn_pw_s8_run_static's array, every context's and op's device memory). cudaDeviceReset destroys all of
+ * it on the CUDA side, so a host that resets a device must not use this library on that device afterwards. */
 #ifndef BNNEON_CUDA_H
 #define BNNEON_CUDA_H
 #include <stddef.h>

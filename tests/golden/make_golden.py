@@ -6,7 +6,7 @@ For each synthetic model (bnneon_b200.synth.v24_ir: the full v2.4 architecture a
 reference's own lowering (python/bnneon/compiler/lower.py: Lowering, plan_slots) and package writer (pkgfmt.py)
 write the neon-int8 package exactly as `bnc.py compile --paths neon-int8 --int8 pw,pwl,head,lin` does after
 recognition (cmd_compile.py _lower_path + _set_metadata). The sha256 and size of those packages go into
-packages.json; tests/test_package_golden.py checks that bnneon_b200.synth writes byte-identical files, so the loader
+packages.json; tests/test_golden_cpu.py checks that bnneon_b200.synth writes byte-identical files, so the loader
 and kernels run on the reference compiler's bytes without the reference being present.
 
 It also records the reference packer's output for a few weight matrices (s8_tensors, quant_rows_s8) in
@@ -240,7 +240,9 @@ def sha(path):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <checkout of the reference repository>")
+    ref_root = sys.argv[1]
     out = {}
     with tempfile.TemporaryDirectory() as td:
         for name, seed, blocks, nc in (("v24_full", 0, synth.V24_BLOCKS, 6522),

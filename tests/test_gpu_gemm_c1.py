@@ -1,4 +1,4 @@
-"""one int8 pointwise GEMM on given int8 rows, through bnn_pw_s8_gemm (the reference's
+"""Config 1 of the benchmark: one int8 pointwise GEMM on given int8 rows, through bnn_pw_s8_gemm (the reference's
 s8n_gemm_range on the rows s8n_quant_rows writes), against the CPU oracle bit for bit.
 
 Inputs as the config states them: activations int8 [M = 4096][K = 256] seeded uniform in [-127, 127] with scale 0.05

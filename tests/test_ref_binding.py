@@ -1,6 +1,6 @@
 """The reference's own Python binding (python/bnneon/binding.py, installed unchanged under baseline/_ref) drives this
-libbnneon.so: the reference's compatibility check for hosts (SURVEY 8b "who calls it"). Skipped when the reference
-package is not installed in baseline/_ref.
+libbnneon.so: the reference's compatibility check for hosts (its binding is how Python hosts call the library).
+Skipped when the reference package is not installed in baseline/_ref.
 
 Probe, metadata and label checks need no GPU; inference through the reference binding is compared bit for bit with
 this repository's batched entry point.

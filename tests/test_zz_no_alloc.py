@@ -65,6 +65,9 @@ class Call:
 CALLS = [  # two layers of the v2.4 int8 path, run back to back on the shared static array
     (72, 288, 384, 3, 0, True, 0, True),     # b2.2 pwl: SE gate + residual
     (72, 24, 6144, 2, 1, False, 128, False),  # b1.1 pw: SiLU, haloed output, 12288 rows
+    # both limits reached exactly: 4 x 8192 = 32768 rows of Kq = 128 bytes = 4 MiB of quantized rows, so the q
+    # region's tensor map is used to its last row and the sa / za regions to their last entry
+    (36, 128, 8192, 4, 1, True, 0, False),
 ]
 
 
