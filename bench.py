@@ -70,7 +70,7 @@ def op_cost(code, p, bufs, bl):
 
 
 PROFILE = os.path.join(REPO, "profiles", "launch_list_v24_int8_b256.md")
-NCU_CMD = ("ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum --clock-control none "
+NCU_CMD = ("ncu --metrics gpu__time_duration.sum --clock-control none "
            "-s {skip} -c {count} --csv --log-file <out>/launches.csv python bench.py --ncu --warmup 3")
 # the kernels each op launches, in order (the runtime's op registry)
 OP_KERNELS = {1: ("k_fe_minmax", "k_fe_spec"), 2: ("k_c0pool",), 22: ("k_quant", "k_gemm_s8"),

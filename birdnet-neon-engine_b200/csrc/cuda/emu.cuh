@@ -109,10 +109,12 @@ __device__ __forceinline__ float frecpe(float x) {
 }
 
 // FRECPE for a normal d in [1, 2^126) (the SiLU denominators): exponent 253 - e, 8-bit estimate from the table
-// (lut[i] = estimate(256 + i) << 15)
+// (lut[i] = estimate(256 + i) << 15). The estimate bits and the exponent bits do not overlap, so the pseudocode's
+// OR is an add (one three-input integer add), and the table is read at a byte offset cut straight from the mantissa.
 __device__ __forceinline__ float frecpe_ge1(float d, const uint32_t *lut) {
-  uint32_t u = __float_as_uint(d);
-  return __uint_as_float((0x7e800000u - (u & 0x7f800000u)) | lut[(u >> 15) & 0xffu]);
+  const uint32_t u = __float_as_uint(d);
+  const uint32_t est = *reinterpret_cast<const uint32_t *>(reinterpret_cast<const char *>(lut) + ((u >> 13) & 0x3fcu));
+  return __uint_as_float(0x7e800000u - (u & 0x7f800000u) + est);
 }
 
 // FRECPS(a, b) = 2 - a * b fused (finite operands: the infinity x zero case cannot arise here)
@@ -183,7 +185,7 @@ __device__ __forceinline__ float2 silu2(float2 x, const uint32_t *lut) {
   t.x = fmin_nan(fmax_nan(t.x, -60.f), 60.f);
   t.y = fmin_nan(fmax_nan(t.y, -60.f), 60.f);
   const float2 tm = add2_rn(t, splat2(magic));
-  const float2 f = add2_rn(t, neg2(add2_rn(tm, splat2(-magic))));
+  const float2 f = sub2_rn(t, add2_rn(tm, splat2(-magic)));
   float2 p = fma2_rn(splat2(0x1.5d87fep-10f), f, splat2(0x1.3b2ab6p-7f));
   p = fma2_rn(p, f, splat2(0x1.c6b08ep-5f));
   p = fma2_rn(p, f, splat2(0x1.ebfbep-3f));
@@ -192,8 +194,9 @@ __device__ __forceinline__ float2 silu2(float2 x, const uint32_t *lut) {
   const float2 e = make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(tm.x) << 23)),
                                __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(tm.y) << 23)));
   const float2 d = add2_rn(splat2(1.f), e);
+  const float2 dn = sub2_rn(splat2(-1.f), e);  // -d exactly: rounding to nearest is symmetric in sign
   float2 r = make_float2(frecpe_ge1(d.x, lut), frecpe_ge1(d.y, lut));
-  r = mul2_rn(r, fma2_rn(neg2(d), r, splat2(2.f)));
+  r = mul2_rn(r, fma2_rn(dn, r, splat2(2.f)));  // FRECPS(d, r) = 2 - d r fused
   return mul2_rn(x, r);
 }
 

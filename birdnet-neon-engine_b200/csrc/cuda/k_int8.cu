@@ -109,6 +109,93 @@ __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__
   }
 }
 
+// Wide rows (K >= 128): one warp per row, lane l holding the float4 groups l, l + 32, ... (NG of them) of the row in
+// registers: fully coalesced 512-byte loads, the min / max reduced across the warp by shuffles, each group's 4
+// quantized bytes stored as one word (128-byte warp stores). A warp walks RPW consecutive rows and keeps the SE gate
+// of the current window in registers, reloading it only when the window changes.
+template <int NG, bool kGate>
+__global__ void __launch_bounds__(256) k_quant_w(int rows, int Mw, const float *__restrict__ x, long long xws, int lda,
+                                                 int K, int Kq, const float *__restrict__ gate, long long gws,
+                                                 int8_t *__restrict__ q, float *__restrict__ sa,
+                                                 int32_t *__restrict__ za, int rpw) {
+  const int lane = threadIdx.x % 32;
+  const int wrp = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) / 32);
+  const int r0 = wrp * rpw, r1 = min(rows, r0 + rpw);
+  const int K4 = K >> 2, Kq4 = Kq >> 2, K8 = K & ~7;
+  float4 gv[kGate ? NG : 1];
+  int gw = -1;
+  // the next row's loads are issued before the current row is reduced and quantized (one row in flight per warp
+  // behind the one being processed)
+  float4 vn[NG];
+  auto load_row = [&](int r) {
+    const int w = r / Mw, m = r - w * Mw;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + w * xws + (long long)m * lda);
+#pragma unroll
+    for (int i = 0; i < NG; i++) {
+      const int g = lane + 32 * i;
+      if (g < K4) vn[i] = __ldg(xr + g);
+    }
+  };
+  if (r0 < r1) load_row(r0);
+  for (int r = r0; r < r1; r++) {
+    const int w = r / Mw;
+    float4 v[NG];
+#pragma unroll
+    for (int i = 0; i < NG; i++) v[i] = vn[i];
+    if (r + 1 < r1) load_row(r + 1);
+    if (kGate && w != gw) {
+      gw = w;
+      const float4 *gp = reinterpret_cast<const float4 *>(gate + w * gws);
+#pragma unroll
+      for (int i = 0; i < NG; i++) {
+        const int g = lane + 32 * i;
+        gv[i] = g < K4 ? __ldg(gp + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float lo = __int_as_float(0x7f800000), hi = __int_as_float(0xff800000);
+#pragma unroll
+    for (int i = 0; i < NG; i++) {
+      const int g = lane + 32 * i;
+      if (g < K4) {
+        float4 t = v[i];
+        if (kGate) {
+          const float2 p0 = mul2_rn(make_float2(t.x, t.y), make_float2(gv[i].x, gv[i].y));
+          const float2 p1 = mul2_rn(make_float2(t.z, t.w), make_float2(gv[i].z, gv[i].w));
+          t = make_float4(p0.x, p0.y, p1.x, p1.y);
+        }
+        v[i] = t;
+        lo = fmin_nan(lo, fmin_nan(fmin_nan(t.x, t.y), fmin_nan(t.z, t.w)));
+        hi = fmax_nan(hi, fmax_nan(fmax_nan(t.x, t.y), fmax_nan(t.z, t.w)));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      lo = fmin_nan(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = fmax_nan(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    float inv, s;
+    int32_t z;
+    quant_params(lo, hi, inv, z, s);
+    if (lane == 0) { sa[r] = s; za[r] = z; }
+    uint32_t *qr = reinterpret_cast<uint32_t *>(q + (long long)r * Kq);
+    const float2 inv2 = splat2(inv);
+#pragma unroll
+    for (int i = 0; i < NG; i++) {
+      const int g = lane + 32 * i;
+      if (g < K4) {
+        const float2 p0 = mul2_rn(make_float2(v[i].x, v[i].y), inv2);
+        const float2 p1 = mul2_rn(make_float2(v[i].z, v[i].w), inv2);
+        qr[g] = quant_word(p0.x, p0.y, p1.x, p1.y, z, 4 * g < K8);
+      } else if (g < Kq4) {
+        qr[g] = ((uint32_t)z & 0xffu) * 0x01010101u;  // pads past K: the zero point
+      }
+    }
+    if (Kq4 > 32 * NG) {  // pads beyond the register groups (never for Kq = K rounded up to 32)
+      for (int g = 32 * NG + lane; g < Kq4; g += 32) qr[g] = ((uint32_t)z & 0xffu) * 0x01010101u;
+    }
+  }
+}
+
 // The general form (any K, any lda): one thread per row, the reference's loops as written.
 __global__ void k_quant_scalar(int rows, int Mw, const float *__restrict__ x, long long xws, int lda, int K, int Kq,
                                const float *__restrict__ gate, long long gws, int8_t *__restrict__ q,
@@ -188,6 +275,7 @@ __device__ __forceinline__ void epilogue_units(const uint32_t (&acc)[kEpiUnits][
                                                int32_t za, const float *psw, const float *pb, const int32_t *pcs,
                                                float *orow, const float *rrow, const uint32_t *lut) {
   const float2 sa2 = splat2(sa);
+  const uint32_t nza = 0u - (uint32_t)za;  // acc - za cs = acc + (-za) cs, one integer multiply-add (mod 2^32)
 #pragma unroll
   for (int k = 0; k < NU; k++) {
     const int c = 8 * (u0 + k * nh);
@@ -206,8 +294,8 @@ __device__ __forceinline__ void epilogue_units(const uint32_t (&acc)[kEpiUnits][
       const float2 sw = *reinterpret_cast<const float2 *>(psw + c + j), bb = *reinterpret_cast<const float2 *>(pb + c + j);
       const int2 cs = *reinterpret_cast<const int2 *>(pcs + c + j);
       // deq4 (gemm_s8n.c:105-114): int32 wrap, exact int -> fp32, sw * sa first, multiply then add (no FMA)
-      const float f0 = __int2float_rn((int32_t)(acc[kofs + k][j] - (uint32_t)cs.x * (uint32_t)za));
-      const float f1 = __int2float_rn((int32_t)(acc[kofs + k][j + 1] - (uint32_t)cs.y * (uint32_t)za));
+      const float f0 = __int2float_rn((int32_t)(acc[kofs + k][j] + (uint32_t)cs.x * nza));
+      const float f1 = __int2float_rn((int32_t)(acc[kofs + k][j + 1] + (uint32_t)cs.y * nza));
       const float2 sc = mul2_rn(sw, sa2);
       float2 v = make_float2(__fadd_rn(__fmul_rn(f0, sc.x), bb.x), __fadd_rn(__fmul_rn(f1, sc.y), bb.y));
       if (ACT == 1) {
@@ -468,6 +556,33 @@ extern "C" int bnnk_quant(int rows, int Mw, const float *x, long long xws, int l
   const bool vec = K % 4 == 0 && lda % 4 == 0 && xws % 4 == 0 && (!gate || gws % 4 == 0) && Kq % 4 == 0 &&
                    ((uintptr_t)x & 15) == 0 && (!gate || ((uintptr_t)gate & 15) == 0);
   const int nch = Kq / 16;  // 16-byte chunks of a quantized row
+  const int K4 = K / 4, ng = (K4 + 31) / 32;
+  // tuning overrides (sweeps): BNN_QUANT_W=0 keeps wide rows on the lane-group form; BNN_QUANT_RPW=n rows per warp
+  const char *ew = getenv("BNN_QUANT_W"), *er = getenv("BNN_QUANT_RPW");
+  if (vec && K >= 128 && K <= 1024 && Kq % 4 == 0 && ((uintptr_t)q & 3) == 0 && !(ew && ew[0] == '0')) {
+    // wide rows, a warp per row; rows per warp from a sweep (98k rows of 288: 4 best, 25k of 864: 2, 256 of 1024: 1;
+    // rows of 1536 were faster in the lane-group form)
+    int rpw = rows / (num_sms() * 64);
+    rpw = rpw < 1 ? 1 : rpw > 4 ? 4 : rpw;
+    if (er && atoi(er) >= 1) rpw = atoi(er);
+    const int warps = (rows + rpw - 1) / rpw;
+    const unsigned grid = (unsigned)((warps + 7) / 8);
+#define BNN_QW(NGV)                                                                                           \
+  if (gate) k_quant_w<NGV, true><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw); \
+  else k_quant_w<NGV, false><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw)
+    switch (ng) {  // K in [128, 1024]: 1 .. 8 float4 groups per lane
+    case 1: BNN_QW(1); break;
+    case 2: BNN_QW(2); break;
+    case 3: BNN_QW(3); break;
+    case 4: BNN_QW(4); break;
+    case 5: BNN_QW(5); break;
+    case 6: BNN_QW(6); break;
+    case 7: BNN_QW(7); break;
+    default: BNN_QW(8); break;
+    }
+#undef BNN_QW
+    return cudaGetLastError();
+  }
   if (!vec || Kq % 16 || nch > 32 * 3) {
     k_quant_scalar<<<(rows + 127) / 128, 128, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za);
     return cudaGetLastError();

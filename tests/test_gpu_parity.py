@@ -163,6 +163,12 @@ PW_CASES = [  # (N, K, Mw, B, act, residual, padded output (ow), gated)
     (10, 20, 7, 3, 2, True, 0, False),         # ragged: ReLU, residual, N and M not multiples of anything
     (40, 36, 100, 2, 1, True, 0, True),        # SiLU + residual + gate (the C ABI allows what v2.4 never uses)
     (5, 3, 129, 1, 1, False, 0, False),        # tiny K
+    # a gated small-K layer with SiLU and residual over a partial last tile (288 rows), K = 256 gated over 160 rows,
+    # K = 16 with ReLU, K = 40 (the last 16-element chunk ragged) with a haloed output
+    (40, 36, 96, 3, 1, True, 0, True),
+    (64, 256, 32, 5, 0, False, 0, True),
+    (16, 16, 64, 1, 2, False, 0, False),
+    (24, 40, 64, 3, 1, True, 8, False),
 ]
 
 
@@ -200,6 +206,43 @@ def test_pw_s8(lib, case):
         oracle.lib().bnno_pw_s8(oracle.ptr(x[w]), lda, Mw, n, k, kp, np_, oracle.ptr(None if gate is None else gate[w]),
                                 oracle.ptr(wq), oracle.ptr(sw), oracle.ptr(cs), oracle.ptr(bb), act, oracle.ptr(want),
                                 ldo, ow, opad, oh, oracle.ptr(None if res is None else res[w]), ldo, 0, 0,
+                                oracle.ptr(q), oracle.ptr(sa), oracle.ptr(za))
+        assert bits_equal(got[w], want), f"window {w}: " + mismatch_report(got[w], want)
+
+
+def test_pw_s8_special_rows(lib):
+    """rows with NaN, infinities, huge and tiny values, constant and all-zero rows and ties through the quantizer and
+    the GEMM epilogue, against the oracle"""
+    N, K, Mw, B = 48, 40, 64, 2
+    rng = np.random.default_rng(99)
+    (wq, sw, cs, bb), (n, k, kp, np_) = make_pw(rng, N, K)
+    x = (rng.standard_normal((B, Mw, K)) * 0.7).astype(np.float32)
+    x[0, 0, 3] = np.nan
+    x[0, 1, 5] = np.inf
+    x[0, 2, 7] = -np.inf
+    x[0, 3] = 0.0
+    x[0, 4] = 2.5
+    x[0, 5] *= 1e30
+    x[0, 6] *= 1e-30
+    x[0, 7, :] = np.arange(K) - 20.0  # exact ties at .5 after scaling
+    x[1, 9, 0] = 3.4e38
+    x[1, 9, 1] = -3.4e38
+    h = lib.bnn_pw_s8_new(n, k, kp, np_, wq.ctypes.data, sw.ctypes.data, cs.ctypes.data, bb.ctypes.data, B * Mw)
+    assert h, lib.bnn_last_error()
+    try:
+        out = torch.zeros(B * Mw * np_, dtype=torch.float32, device="cuda")
+        xd = dev(x)
+        assert lib.bnn_pw_s8_run(h, B, Mw, xd.data_ptr(), Mw * K, K, None, 0, 1, out.data_ptr(), Mw * np_, np_, 0, 0,
+                                 None, 0, 0, 0, 0, None) == 0, lib.bnn_last_error()
+        got = host(out).reshape(B, Mw * np_)
+        assert lib.bnn_pw_s8_error(h) == 0
+    finally:
+        lib.bnn_pw_s8_free(h)
+    for w in range(B):
+        want = np.zeros(Mw * np_, np.float32)
+        q, sa, za = np.zeros((Mw, kp), np.int8), np.zeros(Mw, np.float32), np.zeros(Mw, np.int32)
+        oracle.lib().bnno_pw_s8(oracle.ptr(x[w]), K, Mw, n, k, kp, np_, None, oracle.ptr(wq), oracle.ptr(sw),
+                                oracle.ptr(cs), oracle.ptr(bb), 1, oracle.ptr(want), np_, 0, 0, 0, None, np_, 0, 0,
                                 oracle.ptr(q), oracle.ptr(sa), oracle.ptr(za))
         assert bits_equal(got[w], want), f"window {w}: " + mismatch_report(got[w], want)
 
