@@ -93,6 +93,10 @@ SIGNATURES = {
     "bnn_logmel_frames": (_I, [_P]),
     "bnn_logmel_run": (_I, [_P, _I, _P, _LL, _P, _LL, _P]),
     "bnn_logmel_free": (None, [_P]),
+    "bnn_dbimg_new": (_P, [_P, _I, _P, _P, _P, _P, _I]),
+    "bnn_dbimg_image_elems": (_LL, [_P]),
+    "bnn_dbimg_run": (_I, [_P, _I, _P, _LL, _P, _LL, _P]),
+    "bnn_dbimg_free": (None, [_P]),
     "bnn_proto_s8_new": (_P, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, ctypes.c_float, _I, _I]),
     "bnn_proto_s8_run": (_I, [_P, _I, _P, _LL, _I, _P, _LL, _P, _LL, _P, _P]),
     "bnn_proto_s8h_new": (_P, [_I, _I, _I, _P, _P, _P, _P, _I, _I, ctypes.c_float, _I, _I]),

@@ -625,6 +625,7 @@ def make_package(dst, seed=0, mini=False, n_classes=None, path=PATH):
 OPC_PROTO_S8 = 35
 PERCH_SAMPLE_RATE = 32000
 BNN_MODEL_PERCH_V2 = 120
+BNN_MODEL_BIRDNET_V3 = 30
 
 
 def quant_rows_s8(w):
@@ -768,6 +769,72 @@ def write_logmel_package(dst, fe, model_id="perch_v2_frontend_synthetic"):
         n_samples=fe["nsamp"], attribution="synthetic log-mel front end")
     write_package(dst, meta, lw.tensors, [(PATH, 0, bufs, lw.records, 0, ob, None)])
     return nfr, nmel
+
+
+# ------------------------------------------------------------------ the dB-image front end (FE_DBIMG)
+
+OPC_FE_DBIMG = 16
+DB_PAD_MODES = {"none": 0, "reflect": 1, "zero": 2}
+# a BirdNET-v3.0-like geometry (the v3.0 model is not in this repository: its documented front end is reflect
+# padding, a framed DFT, power, mel, dB with a top-db floor, min/max normalisation, a bilinear resize to 224 x 468 and
+# three normalised channels, on 5 s windows at 32 kHz); the n_fft, hop, mel rows and constants here are stand-ins
+V3_SAMPLE_RATE = 32000
+V3_FE = dict(nsamp=160000, nfft=1024, hop=320, pad=512, pad_mode="reflect", nmel=128, rows=tuple(range(96)),
+             Ho=224, Wo=468, C=3, top_db=80.0, norm=1, floor=1e-10, eps=1e-6)
+
+
+def dbimg_frontend(nsamp, nfft, hop, pad, pad_mode, nmel, rows, Ho, Wo, C, top_db=80.0, norm=1, floor=1e-10,
+                   eps=1e-6, post=None, chan=None, rate=V3_SAMPLE_RATE, fmin=0.0, fmax=None):
+    """A dB-image front end: periodic Hann window of nfft samples, triangular mel filters up to fmax (default Nyquist),
+    dB = 10 log10 (ln times 10 / ln 10), the given mel rows, and C channels normalised by a seeded mean and std
+    (subtract, then divide)."""
+    fmax = fmax or rate / 2.0
+    if post is None:
+        post = [(1, float(np.float32(10.0 / np.log(10.0))))]
+    if chan is None:
+        rng = np.random.default_rng(C)
+        chan = [(4, rng.uniform(0.3, 0.6, C).astype(np.float32)), (2, rng.uniform(0.2, 0.3, C).astype(np.float32))]
+    nfr = (nsamp + 2 * pad - nfft) // hop + 1
+    return dict(nsamp=nsamp, nfft=nfft, hop=hop, pad=pad, pad_mode=pad_mode, nfr=nfr, window=_hann(nfft),
+                mel=_mel_bank(nfft, fmin, fmax, nmel, rate), rows=np.array(rows, np.int32), Ho=Ho, Wo=Wo, C=C,
+                top_db=top_db, norm=norm, floor=float(floor), eps=float(eps), post=list(post), chan=list(chan))
+
+
+def dbimg_record(fe, halo=0):
+    """(tensors {name: array}, ints, ld, halo) of FE_DBIMG as lower.py l_fe_dbimg writes them (halo 0: an image whose
+    consumers take none; a dense conv consumer takes a zero halo)"""
+    c = fe["C"]
+    ld, h = (c if c % 4 == 0 else (c + 3) & ~3), halo
+    post = list(fe["post"]) + [(0, 0.0)] * (3 - len(fe["post"]))
+    chan = list(fe["chan"]) + [(0, np.zeros(c, np.float32))] * (2 - len(fe["chan"]))
+    scalars = np.array([fe["floor"], fe["top_db"] or 0.0, fe["eps"]] + [v for _, v in post], np.float32)
+    consts = np.concatenate([scalars, np.asarray(chan[0][1], np.float32).reshape(-1),
+                             np.asarray(chan[1][1], np.float32).reshape(-1)])
+    ints = [fe["nsamp"], fe["nfft"], fe["hop"], fe["pad"], DB_PAD_MODES[fe["pad_mode"]], fe["nfr"], fe["mel"].shape[0],
+            len(fe["rows"]), int(fe["top_db"] is not None), fe["norm"], post[0][0], post[1][0], post[2][0], 1,
+            fe["Ho"], fe["Wo"], c, chan[0][0], chan[1][0], ld, h]
+    tens = {"window": fe["window"], "mel": fe["mel"], "rows": np.asarray(fe["rows"], np.int32), "consts": consts}
+    return tens, ints, ld, h
+
+
+def write_dbimg_package(dst, fe, model_id="birdnet_v3_frontend_synthetic", halo=0):
+    """A one-op neon-int8 package: FE_DBIMG on the input window, the image [Ho + 2 halo][Wo + 2 halo][ld] out (as
+    lower.py l_fe_dbimg writes the op: tensors fe/dbimg.0.{window, mel, rows, consts}; buffer Ho x Wo x C, channel
+    stride ld, the halo zero). n_classes in the metadata is the image's size. Returns the image's elements."""
+    tens, ints, ld, h = dbimg_record(fe, halo)
+    lw = _Int8Lowering([])
+    lw.bufs = [(F32, 1, 1, fe["nsamp"], fe["nsamp"], 0, fe["nsamp"])]
+    tl = [lw.tensor(f"fe/dbimg.0.{k}", tens[k]) for k in ("window", "mel", "rows", "consts")]
+    hw = (fe["Ho"] + 2 * h) * (fe["Wo"] + 2 * h) * ld
+    ob = lw.buf(F32, fe["Ho"], fe["Wo"], fe["C"], ld=ld, halo=h, elems=hw + 24 * ld + 64 if h else None)
+    lw.emit(OPC_FE_DBIMG, [0, ob], tl, ints, {})
+    bufs = plan_slots(lw.bufs, lw.records, [ob])
+    n_out = hw
+    meta = [(f"src_nodes/{PATH}", "\n".join(lw.src))] + metadata(
+        n_out, 0, labels_for(n_out), model_id=model_id, family=BNN_MODEL_BIRDNET_V3, sample_rate=V3_SAMPLE_RATE,
+        n_samples=fe["nsamp"], attribution="synthetic dB-image front end")
+    write_package(dst, meta, lw.tensors, [(PATH, 0, bufs, lw.records, 0, ob, None)])
+    return n_out
 
 
 # ------------------------------------------------------------------ a Perch-v2-architecture model (neon-fp16 + int8 head)

@@ -133,6 +133,19 @@ typedef struct {
 int bnnk_logmel(int B, const float *pcm, long long pws, const bnnk_logmel_tables *t, float *spec, long long sws,
                 bnn_stream_t st);
 
+/* ---- the dB-image front end (FE_DBIMG): pcm [B][nsamp] -> image [B][(Ho + 2 halo)(Wo + 2 halo)][ld]. Device tables:
+ * window [nfft], twiddles [nfft / 4], real-split factors [nfft / 2 + 1], the sparse mel (row offsets [nmel + 1], bins
+ * and weights of the nonzero entries), rows [R], channel values [2][C], the resize coordinates [Ho], [Wo]; the scratch
+ * holds bnnk_dbimg_scratch_floats(t, B) floats (the dB rows, the selected rows, the blocks' maxima) */
+typedef struct {
+  int nsamp, nfft, lg, hop, pad, padmode, nfr, nmel, R, has_top_db, norm, post[3], Ho, Wo, C, chan[2], ld, halo, klo, khi;
+  float floor_, top_db, eps, postv[3];
+  const float *win, *tw_re, *tw_im, *sp_re, *sp_im, *mel_w, *chv, *dy1, *dy2, *dx1, *dx2;
+  const int *mel_off, *mel_k, *rows, *ry1, *ry2, *rx1, *rx2;
+} bnnk_dbimg_tables;
+size_t bnnk_dbimg_scratch_floats(const bnnk_dbimg_tables *t, int B);
+int bnnk_dbimg(int B, const float *pcm, long long pws, const bnnk_dbimg_tables *t, float *scratch, float *img,
+               long long iws, bnn_stream_t st);
 /* ---- the int8 prototype head (PROTO_S8) */
 
 /* per-cell quantization (pc_quant_cells_f32): cells r = w * P + p of x (window stride xws, row stride ld floats;

@@ -28,6 +28,7 @@
 #include "bnn_kernels.h"
 #include "smem_attr.cuh"
 #include "emu.cuh"
+#include "ln_cr.cuh"
 #include "sync.cuh"
 #include "tc.cuh"
 
@@ -516,6 +517,7 @@ __global__ void k_test_fn(int fn, int n, const float *x, float *y) {
   case 6: r = glibc_expf(v, c_expf_tab); break;
   case 7: r = silu2(make_float2(v, -v), g_frecpe_lut).x; break;
   case 8: r = fma2_rn(make_float2(v, -v), splat2(1.7f), splat2(0.3f)).x; break;
+  case 9: r = ln_cr(v); break;
   default: r = 0.f;
   }
   y[i] = r;

@@ -53,7 +53,7 @@ static const struct { int mode; const char *name, *precision; } PATHS[] = {
  * variant 1) */
 static int path_runs_here(const bnn_pkg *p, int i) {
   static const int codes[] = {BNN_OP_FE_STFT2, BNN_OP_C0POOL, BNN_OP_PW_S8, BNN_OP_DW3, BNN_OP_SE_GATE,
-                              BNN_OP_POSTPC, BNN_OP_GEMV_S8, BNN_OP_PROTO_S8, BNN_OP_FE_LOGMEL, BNN_OP_DENSE,
+                              BNN_OP_POSTPC, BNN_OP_GEMV_S8, BNN_OP_PROTO_S8, BNN_OP_FE_LOGMEL, BNN_OP_FE_DBIMG, BNN_OP_DENSE,
                               BNN_OP_C0POOL_F16, BNN_OP_PW_F16, BNN_OP_DW3_F16, BNN_OP_SE_F16, BNN_OP_POSTPC_F16,
                               BNN_OP_DENSE_F16, BNN_OP_STEM_F16, BNN_OP_DWK_F16, BNN_OP_PAD_F16, BNN_OP_MEAN_F16,
                               BNN_OP_PROTO_F16S8};
@@ -885,6 +885,74 @@ void bnn_logmel_free(bnn_logmel *o) {
   free(o);
 }
 
+/* ---- FE_DBIMG (src/rt_ops_f32x.c:15-86, src/fe_dbimg.c:49-235) */
+
+struct bnn_dbimg {
+  bnn_devop op;
+  int batch;
+};
+
+bnn_dbimg *bnn_dbimg_new(const int32_t *p, int np, const float *window, const float *mel, const int32_t *rows,
+                         const float *consts, int batch) {
+  if (!p || np != 21 || !window || !mel || !rows || !consts || batch < 1 || batch > 65535) {
+    ERR(BNN_ERR_USAGE, "bnn_dbimg_new: expected the op record's 21 ints, its four tensors and 1 <= batch <= 65535 "
+        "(np %d, batch %d)", np, batch);
+    return NULL;
+  }
+  /* fe_db_init's checks (src/rt_ops_f32x.c:24-40) */
+  const int N = p[1], nsamp = p[0], hop = p[2], pad = p[3], pm = p[4], nfr = p[5], nmel = p[6], R = p[7];
+  const int ok = N >= 64 && N <= 8192 && !(N & (N - 1)) && hop > 0 && pad >= 0 && pm >= 0 && pm <= 2 && (pm || !pad) &&
+                 (pm != 1 || pad < nsamp) && nfr > 0 && nsamp + 2 * pad >= N && nfr == (nsamp + 2 * pad - N) / hop + 1 &&
+                 nmel > 0 && nmel <= 4096 && R > 0 && (p[8] == 0 || p[8] == 1) && p[9] >= 0 && p[9] <= 2 &&
+                 p[10] >= 0 && p[10] <= 4 && p[11] >= 0 && p[11] <= 4 && p[12] >= 0 && p[12] <= 4 && p[13] == 1 &&
+                 p[14] > 0 && p[15] > 0 && p[16] > 0 && p[16] <= 64 && p[19] >= p[16] && p[20] >= 0 && p[20] <= 3 &&
+                 p[17] >= 0 && p[17] <= 4 && p[18] >= 0 && p[18] <= 4;
+  if (!ok) {
+    ERR(BNN_ERR_USAGE, "bnn_dbimg_new: parameters [%d %d %d %d %d %d %d %d ...] fail fe_db_init's checks", p[0], p[1],
+        p[2], p[3], p[4], p[5], p[6], p[7]);
+    return NULL;
+  }
+  for (int r = 0; r < R; r++)
+    if (rows[r] < 0 || rows[r] >= nmel) {
+      ERR(BNN_ERR_USAGE, "bnn_dbimg_new: row table entry %d = %d outside 0..%d", r, rows[r], nmel - 1);
+      return NULL;
+    }
+  bnn_dbimg *o = calloc(1, sizeof *o);
+  if (!o) { ERR(BNN_ERR_OOM, "out of memory"); return NULL; }
+  o->batch = batch;
+  char err[512];
+  int kind = BNN_ERR_CPU;
+  if (bnn_dbimg_build(&o->op, p, window, mel, rows, consts, batch, err, sizeof err, &kind)) {
+    ERR(kind, "bnn_dbimg_new: %s", err);
+    bnn_dbimg_free(o);
+    return NULL;
+  }
+  return o;
+}
+
+long long bnn_dbimg_image_elems(const bnn_dbimg *o) {
+  if (!o) return -1;
+  const bnnk_dbimg_tables *t = &o->op.db;
+  return (long long)(t->Ho + 2 * t->halo) * (t->Wo + 2 * t->halo) * t->ld;
+}
+
+int bnn_dbimg_run(bnn_dbimg *o, int B, const float *d_pcm, long long pws, float *d_img, long long iws, void *stream) {
+  if (!o || B < 0 || B > o->batch || !d_pcm || !d_img ||
+      (B > 1 && (pws < o->op.db.nsamp || iws < bnn_dbimg_image_elems(o)))) {
+    ERR(BNN_ERR_USAGE, "bnn_dbimg_run: B %d window strides %lld / %lld (expected 0 <= B <= %d, strides >= nsamp and "
+        ">= the image's floats)", B, pws, iws, o ? o->batch : 0);
+    return -1;
+  }
+  return launch_rc("bnn_dbimg_run", bnnk_dbimg(B, d_pcm, pws, &o->op.db, o->op.db_scratch, d_img, iws,
+                                               (bnn_stream_t)stream));
+}
+
+void bnn_dbimg_free(bnn_dbimg *o) {
+  if (!o) return;
+  bnn_dbimg_release(&o->op);
+  free(o);
+}
+
 /* ---- PROTO_S8 (src/rt_ops_s8n.c:212-250) */
 
 struct bnn_proto_s8 {
@@ -1171,6 +1239,6 @@ int bnn_cuda_peak_hfma2(int blocks, int iters, void *d_word, void *stream) {
 }
 
 int bnn_cuda_fn(int fn, int n, const float *d_x, float *d_y, void *stream) {
-  if (fn < 0 || fn > 8 || n < 0) { ERR(BNN_ERR_USAGE, "bnn_cuda_fn: fn %d n %d", fn, n); return -1; }
+  if (fn < 0 || fn > 9 || n < 0) { ERR(BNN_ERR_USAGE, "bnn_cuda_fn: fn %d n %d", fn, n); return -1; }
   return launch_rc("bnn_cuda_fn", bnnk_test_fn(fn, n, d_x, d_y, (bnn_stream_t)stream));
 }

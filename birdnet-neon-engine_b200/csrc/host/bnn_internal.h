@@ -47,7 +47,7 @@ const char *bnn_dtype_name(uint32_t dt);
 /* ---- opcodes of the registry (src/rt.h:170-208; append-only, the same numbers) */
 enum {
   BNN_OP_FE_STFT2 = 1, BNN_OP_C0POOL = 2, BNN_OP_PW = 3, BNN_OP_DW3 = 4, BNN_OP_SE = 5, BNN_OP_POSTPC = 6,
-  BNN_OP_DENSE = 7, BNN_OP_FE_LOGMEL = 8, BNN_OP_PW_S8 = 22, BNN_OP_GEMV_S8 = 23, BNN_OP_SE_GATE = 25, BNN_OP_PROTO_S8 = 35, BNN_OP_N = 36
+  BNN_OP_DENSE = 7, BNN_OP_FE_LOGMEL = 8, BNN_OP_FE_DBIMG = 16, BNN_OP_PW_S8 = 22, BNN_OP_GEMV_S8 = 23, BNN_OP_SE_GATE = 25, BNN_OP_PROTO_S8 = 35, BNN_OP_N = 36
 };
 /* the fp16 kernels of the neon-fp16 path: base | variant 1 << 8 (src/rt_pkg.c:320-331, src/rt_ops_f16.c:286-299) */
 enum {
@@ -83,6 +83,10 @@ typedef struct {
   /* FE_LOGMEL: the device tables and their allocations */
   bnnk_logmel_tables lm;
   void *lm_mem[8];
+  /* FE_DBIMG: the device tables (one allocation) and the scratch for the batch */
+  bnnk_dbimg_tables db;
+  void *db_mem;
+  float *db_scratch;
   /* fp16 ops: hw the fp16 weights (C0POOL k-major [64][24], DW3 [9][C], DENSE [N][1024]), hwd the GEMM weights
    * k-major [Kp][Np] with each weight in both halves of a word, hb the fp16 bias */
   uint16_t *hw, *hb;
@@ -171,6 +175,11 @@ int bnn_hpack_weights(bnn_devop *d, int dup, const uint16_t *panels, const float
 int bnn_logmel_build(bnn_devop *d, int nsamp, int frame, int hop, int pad, int nfft, int nmel, const float *window,
                      const float *mel, float floor_, float scale, char *err, size_t errlen, int *kind);
 void bnn_logmel_release(bnn_devop *d);
+/* FE_DBIMG tables (fe_db_new, src/fe_dbimg.c:49-107) from the record's 21 ints and its tensors, and a scratch for
+ * batch windows */
+int bnn_dbimg_build(bnn_devop *d, const int32_t *p, const float *window, const float *mel, const int32_t *rows,
+                    const float *consts, int batch, char *err, size_t errlen, int *kind);
+void bnn_dbimg_release(bnn_devop *d);
 
 /* errors (bnn_api.c): thread-local message and kind */
 void bnn_set_error(int kind, const char *fmt, ...) __attribute__((format(printf, 2, 3)));

@@ -292,6 +292,36 @@ static int init_fe_logmel(vctx *v) { /* logmel_init (src/rt_ops_f32.c:364-380) *
   return vneed(v, 1, BNN_F32, (size_t)nfr * p[5]);
 }
 
+static int init_fe_dbimg(vctx *v) { /* fe_db_init (src/rt_ops_f32x.c:18-56), the same checks in the same order */
+  if (vneed_args(v, 2, 4, 21)) return -1;
+  const int *p = v->op->p;
+  const int N = p[1], F = N / 2 + 1, nsamp = p[0], hop = p[2], pad = p[3], padmode = p[4], nfr = p[5], nmel = p[6];
+  const int R = p[7], Ho = p[14], Wo = p[15], C = p[16], ld = p[19], h = p[20];
+  VREQ(v, N >= 64 && N <= 8192 && (N & (N - 1)) == 0);
+  VREQ(v, hop > 0 && pad >= 0 && padmode >= 0 && padmode <= 2 && (padmode || !pad));
+  VREQ(v, padmode != 1 || pad < nsamp);
+  VREQ(v, nfr > 0 && nfr == (nsamp + 2 * pad - N) / hop + 1 && nsamp + 2 * pad >= N);
+  VREQ(v, nmel > 0 && R > 0 && nmel <= 4096);
+  VREQ(v, p[8] == 0 || p[8] == 1);
+  VREQ(v, p[9] >= 0 && p[9] <= 2);
+  VREQ(v, p[10] >= 0 && p[10] <= 4 && p[11] >= 0 && p[11] <= 4 && p[12] >= 0 && p[12] <= 4 && p[13] == 1);
+  VREQ(v, Ho > 0 && Wo > 0 && C > 0 && C <= 64 && ld >= C && h >= 0 && h <= 3);
+  VREQ(v, p[17] >= 0 && p[17] <= 4 && p[18] >= 0 && p[18] <= 4);
+  if (vneed_t(v, 0, (size_t)N * 4, 0) || vneed_t(v, 1, (size_t)nmel * F * 4, 0) || vneed_t(v, 2, (size_t)R * 4, 0) ||
+      vneed_t(v, 3, (size_t)(6 + 2 * C) * 4, 0))
+    return -1;
+  const int32_t *rows = vt(v, 2, NULL);
+  for (int r = 0; r < R; r++)
+    if (rows[r] < 0 || rows[r] >= nmel) return vbad(v, "row table entry %d = %d outside 0..%d", r, rows[r], nmel - 1);
+  if (vneed(v, 0, BNN_F32, (size_t)nsamp)) return -1;
+  const bnn_buf_rec *o = vbd(v, 1);
+  if (!o) return vbad(v, "buffer argument 1 (image) is absent");
+  if (o->halo != (uint32_t)h || o->ld != (uint32_t)ld || o->H != (uint32_t)Ho || o->W != (uint32_t)Wo)
+    return vbad(v, "buffer argument 1 (buffer #%d, image): expected %d x %d, ld %d, halo %d; found %u x %u, ld %u, halo %u",
+                v->op->b[1], Ho, Wo, ld, h, o->H, o->W, o->ld, o->halo);
+  return vneed(v, 1, BNN_F32, (size_t)(Ho + 2 * h) * (Wo + 2 * h) * ld);
+}
+
 static int init_proto_s8(vctx *v) { /* proto8n_init (src/rt_ops_s8n.c:220-240) after rt_proto_geom / rt_proto_io
                                      * (src/rt_ops_f32.c:525-545) */
   if (vneed_args(v, 4, 6, 9)) return -1;
@@ -538,6 +568,7 @@ static const kdesc KERNELS[] = {
     {BNN_OP_GEMV_S8, "gemv_s8n", init_gemv_s8, 0x1e, 0, 2},
     {BNN_OP_PROTO_S8, "proto_s8n", init_proto_s8, 0xe, 0, 3},
     {BNN_OP_FE_LOGMEL, "fe_logmel", init_fe_logmel, 0x2, 0, 1},
+    {BNN_OP_FE_DBIMG, "fe_dbimg", init_fe_dbimg, 0x2, 0, 3},
     {BNN_OP_DENSE, "dense_f32", init_dense_f32, 0x2, 0, 1},
     {BNN_OP_C0POOL_F16, "c0pool_f16", init_c0pool_f16, 0x2, 0, 1},
     {BNN_OP_PW_F16, "pw_f16", init_pw_f16, 0x2, 0x4, 1},
@@ -651,7 +682,7 @@ int bnn_rt_open(bnn_ctx *c, char *err, size_t errlen, int *kind) {
       if (bnn_meta_str(c->pkg, "compiler", comp, sizeof comp) < 0) snprintf(comp, sizeof comp, "unknown");
       *kind = BNN_ERR_CPU;
       return vbad(&v, "opcode 0x%x (base %d variant %d) has no B200 kernel in this library (it runs the neon-int8 ops "
-                  "FE_STFT2, C0POOL, PW_S8, DW3, SE_GATE, POSTPC, GEMV_S8, PROTO_S8, FE_LOGMEL and DENSE, and the "
+                  "FE_STFT2, C0POOL, PW_S8, DW3, SE_GATE, POSTPC, GEMV_S8, PROTO_S8, FE_LOGMEL, FE_DBIMG and DENSE, and the "
                   "neon-fp16 ops C0POOL, PW, DW3, SE, POSTPC and DENSE of variant 1; the package was written by "
                   "compiler '%s')",
                   op->code, op->code & 0xff, var, comp);
@@ -972,6 +1003,96 @@ void bnn_logmel_release(bnn_devop *d) {
   }
 }
 
+/* fe_db_new (src/fe_dbimg.c:49-107): twiddles e^{-2 pi i k / NC} (k < NC / 2) and the real-split factors
+ * e^{-2 pi i k / N} (k <= NC) in double, rounded once; the sparse mel as each row's nonzero entries in bin order,
+ * [klo, khi) the bins any row uses; ONNX Runtime's half-pixel resize coordinates (axis_setup :37-47). All tables in one
+ * device allocation; the scratch for batch windows in another. */
+static void db_axis(int nin, int nout, int *i1, int *i2, float *d1, float *d2) {
+  const float scale = (float)nout / (float)nin;
+  for (int o = 0; o < nout; o++) {
+    float x = ((float)o + 0.5f) / scale - 0.5f;
+    if (x > (float)(nin - 1)) x = (float)(nin - 1);
+    if (x < 0.f) x = 0.f;
+    const int a = (int)x < nin - 1 ? (int)x : nin - 1;
+    const int b = a + 1 < nin - 1 ? a + 1 : nin - 1;
+    i1[o] = a; i2[o] = b;
+    d1[o] = fabsf(x - (float)a); d2[o] = fabsf(x - (float)b);
+    if (a == b) { d1[o] = 0.5f; d2[o] = 0.5f; }
+  }
+}
+int bnn_dbimg_build(bnn_devop *d, const int32_t *p, const float *window, const float *mel, const int32_t *rows,
+                    const float *consts, int batch, char *err, size_t errlen, int *kind) {
+  bnnk_dbimg_tables *t = &d->db;
+  memset(t, 0, sizeof *t);
+  t->nsamp = p[0]; t->nfft = p[1]; t->hop = p[2]; t->pad = p[3]; t->padmode = p[4]; t->nfr = p[5]; t->nmel = p[6];
+  t->R = p[7]; t->has_top_db = p[8]; t->norm = p[9]; t->post[0] = p[10]; t->post[1] = p[11]; t->post[2] = p[12];
+  t->Ho = p[14]; t->Wo = p[15]; t->C = p[16]; t->chan[0] = p[17]; t->chan[1] = p[18]; t->ld = p[19]; t->halo = p[20];
+  t->floor_ = consts[0]; t->top_db = consts[1]; t->eps = consts[2];
+  for (int u = 0; u < 3; u++) t->postv[u] = consts[3 + u];
+  const int N = t->nfft, NC = N / 2, F = NC + 1;
+  while ((1 << t->lg) < NC) t->lg++;
+  int nnz = 0, klo = F, khi = 0;
+  for (int j = 0; j < t->nmel; j++)
+    for (int k = 0; k < F; k++)
+      if (mel[(size_t)j * F + k] != 0.f) { nnz++; if (k < klo) klo = k; if (k + 1 > khi) khi = k + 1; }
+  t->klo = klo < khi ? klo : 0;
+  t->khi = khi;
+  /* sections of 4-byte elements, each starting on 64 elements */
+  const size_t cnt[18] = {(size_t)N, (size_t)NC / 2 + 1, (size_t)NC / 2 + 1, (size_t)F, (size_t)F, (size_t)nnz + 1,
+                          2 * (size_t)t->C, (size_t)t->Ho, (size_t)t->Ho, (size_t)t->Wo, (size_t)t->Wo,
+                          (size_t)t->nmel + 1, (size_t)nnz + 1, (size_t)t->R, (size_t)t->Ho, (size_t)t->Ho,
+                          (size_t)t->Wo, (size_t)t->Wo};
+  size_t off[18], total = 0;
+  for (int i = 0; i < 18; i++) { off[i] = total; total += (cnt[i] + 63) & ~(size_t)63; }
+  uint32_t *h = calloc(total, 4);
+  if (!h) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory (dB-image tables)"); return -1; }
+  float *win = (float *)(h + off[0]), *twr = (float *)(h + off[1]), *twi = (float *)(h + off[2]);
+  float *spr = (float *)(h + off[3]), *spi = (float *)(h + off[4]), *mw = (float *)(h + off[5]);
+  float *chv = (float *)(h + off[6]), *dy1 = (float *)(h + off[7]), *dy2 = (float *)(h + off[8]);
+  float *dx1 = (float *)(h + off[9]), *dx2 = (float *)(h + off[10]);
+  int *moff = (int *)(h + off[11]), *mk = (int *)(h + off[12]), *rw = (int *)(h + off[13]);
+  int *ry1 = (int *)(h + off[14]), *ry2 = (int *)(h + off[15]), *rx1 = (int *)(h + off[16]), *rx2 = (int *)(h + off[17]);
+  memcpy(win, window, sizeof(float) * (size_t)N);
+  for (int k = 0; k < NC / 2; k++) {
+    const double a = -2 * M_PI * k / NC;
+    twr[k] = (float)cos(a); twi[k] = (float)sin(a);
+  }
+  for (int k = 0; k <= NC; k++) {
+    const double a = -2 * M_PI * k / N;
+    spr[k] = (float)cos(a); spi[k] = (float)sin(a);
+  }
+  int q = 0;
+  for (int j = 0; j < t->nmel; j++) {
+    moff[j] = q;
+    for (int k = 0; k < F; k++)
+      if (mel[(size_t)j * F + k] != 0.f) { mk[q] = k; mw[q] = mel[(size_t)j * F + k]; q++; }
+  }
+  moff[t->nmel] = q;
+  memcpy(rw, rows, sizeof(int) * (size_t)t->R);
+  memcpy(chv, consts + 6, sizeof(float) * 2 * (size_t)t->C);
+  db_axis(t->R, t->Ho, ry1, ry2, dy1, dy2);
+  db_axis(t->nfr, t->Wo, rx1, rx2, dx1, dx2);
+  int rc = upload(&d->db_mem, h, total * 4, err, errlen, kind);
+  free(h);
+  if (rc) return rc;
+  uint32_t *g = d->db_mem;
+  t->win = (const float *)(g + off[0]); t->tw_re = (const float *)(g + off[1]); t->tw_im = (const float *)(g + off[2]);
+  t->sp_re = (const float *)(g + off[3]); t->sp_im = (const float *)(g + off[4]); t->mel_w = (const float *)(g + off[5]);
+  t->chv = (const float *)(g + off[6]); t->dy1 = (const float *)(g + off[7]); t->dy2 = (const float *)(g + off[8]);
+  t->dx1 = (const float *)(g + off[9]); t->dx2 = (const float *)(g + off[10]);
+  t->mel_off = (const int *)(g + off[11]); t->mel_k = (const int *)(g + off[12]); t->rows = (const int *)(g + off[13]);
+  t->ry1 = (const int *)(g + off[14]); t->ry2 = (const int *)(g + off[15]); t->rx1 = (const int *)(g + off[16]);
+  t->rx2 = (const int *)(g + off[17]);
+  CK(cudaMalloc((void **)&d->db_scratch, sizeof(float) * bnnk_dbimg_scratch_floats(t, batch)), "dB-image scratch");
+  return 0;
+}
+void bnn_dbimg_release(bnn_devop *d) {
+  cudaFree(d->db_mem);
+  cudaFree(d->db_scratch);
+  d->db_mem = NULL;
+  d->db_scratch = NULL;
+}
+
 /* hp_pack panels (src/gemm_f16.c:17-40: [Np/16][Kp][16], then a [Kp][8] tail panel when Np % 16) as the k-major
  * [Kp][Np] matrix of the B200 fp16 GEMM, each weight in both halves of a 32-bit word (dup != 0, to d->hwd) or plain
  * fp16 (to d->hw); b16 [Np] to d->hb; b32 [Np] to *b32 unless NULL */
@@ -1045,6 +1166,9 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
     return bnn_logmel_build(d, p[0], p[1], p[2], p[3], p[4], p[5], tptr(c, op, 0), tptr(c, op, 1), k[0], k[1], err,
                             errlen, kind);
   }
+  case BNN_OP_FE_DBIMG:
+    return bnn_dbimg_build(d, p, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), tptr(c, op, 3), c->batch, err, errlen,
+                           kind);
   case BNN_OP_PROTO_S8:
     return bnn_proto_weights(d, p[0], p[2], p[3], tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 3), tptr(c, op, 4),
                              p[7], ((const float *)tptr(c, op, 5))[0], err, errlen, kind);
@@ -1224,6 +1348,7 @@ void bnn_rt_device_free(bnn_ctx *c, int di) {
       for (int k = 0; k < 6; k++) cudaFree(o->f[k]);
       cudaFree(o->hw); cudaFree(o->hb); cudaFree(o->hwd);
       bnn_logmel_release(o);
+      bnn_dbimg_release(o);
     }
   for (int k = 0; k < dv->n_fe_mem; k++) cudaFree(dv->fe_mem[k]);
   if (dv->events)
@@ -1337,6 +1462,9 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
       break;
     case BNN_OP_POSTPC:
       rc = bnnk_postpc(n, IN_(0), INWS(0), o->f[2], o->f[3], o->f[0], o->f[1], dv->pcin, B_(1), WS(1), st);
+      break;
+    case BNN_OP_FE_DBIMG:
+      rc = bnnk_dbimg(n, IN_(0), INWS(0), &o->db, o->db_scratch, B_(1), WS(1), st);
       break;
     case BNN_OP_FE_LOGMEL:
       rc = bnnk_logmel(n, IN_(0), INWS(0), &o->lm, B_(1), WS(1), st);

@@ -122,6 +122,21 @@ int bnn_logmel_run(bnn_logmel *op, int B, const float *d_pcm, long long pws, flo
                    void *stream);
 void bnn_logmel_free(bnn_logmel *op);
 
+/* FE_DBIMG, the dB-image front end of the v3.0 models (src/fe_dbimg.c:49-235 driven by src/rt_ops_f32x.c:15-86),
+ * batched: p = the op record's 21 ints [nsamp N hop pad padmode nfr nmel R has_top_db norm post0 post1 post2 1 Ho Wo C
+ * chan0 chan1 ld halo] and its tensors (host pointers) window [N], mel [nmel][N / 2 + 1], rows [R],
+ * consts {floor, top_db, eps, post[3], chan0[C], chan1[C]}, checked as fe_db_init checks them; batch = the most
+ * windows one bnn_dbimg_run call takes (it sizes the device scratch). The log is the correctly rounded logf (the
+ * reference calls the C library's); see bnn_dbimg_run. */
+typedef struct bnn_dbimg bnn_dbimg;
+bnn_dbimg *bnn_dbimg_new(const int32_t *p, int np, const float *window, const float *mel, const int32_t *rows,
+                         const float *consts, int batch);
+/* floats in one window's image: (Ho + 2 halo) (Wo + 2 halo) ld, the halo zero */
+long long bnn_dbimg_image_elems(const bnn_dbimg *op);
+/* d_pcm [B][nsamp] (window stride pws floats) -> d_img [B][image] (window stride iws floats); 0 <= B <= batch */
+int bnn_dbimg_run(bnn_dbimg *op, int B, const float *d_pcm, long long pws, float *d_img, long long iws, void *stream);
+void bnn_dbimg_free(bnn_dbimg *op);
+
 /* PROTO_S8, the int8 prototype head (src/rt_ops_s8n.c:212-250: pc_quant_cells_f32 and pc_proto_colmax_s8n,
  * src/proto_s8n.c:28-164, then pc_proto_logits, src/pc_kern_f32.c:364-376), batched. The package's tensors (host
  * pointers): prototypes qw [Np/4][Kp/16][4][16] int8, sw [Np], n4 [Np/4] (checked as pc_proto_n4_check does; the GPU
@@ -208,7 +223,7 @@ int bnn_cuda_op_error(void);
 
 /* elementwise functions of the int8 path, for tests: 0 SiLU, 1 SiLU (table estimate), 2 sigmoid, 3 FRECPE,
  * 4 log2 polynomial, 5 exp2 polynomial (front end), 6 glibc expf, 7 SiLU on paired fp32 lanes (table estimate),
- * 8 fma(x, 1.7f, 0.3f) on paired fp32 lanes */
+ * 8 fma(x, 1.7f, 0.3f) on paired fp32 lanes, 9 the dB-image front end's logarithm (double log rounded to float) */
 int bnn_cuda_fn(int fn, int n, const float *d_x, float *d_y, void *stream);
 
 /* the fp16 FMA pipe's throughput, for a roofline: blocks x 256 threads each run iters x 16 fp16 FMAs (8 chains of

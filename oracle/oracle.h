@@ -64,6 +64,21 @@ void bnno_fe_run(const bnno_fe *f, const float *pcm, float *img);
 void bnno_fe_free(bnno_fe *f);
 
 /* ---- FE_LOGMEL, the framed log-mel front end (src/pc_kern_f32.c:14-149, record src/rt_ops_f32.c:362-385) */
+/* FE_DBIMG (src/fe_dbimg.c), oracle_dbimg.c: p = the record's 21 ints, consts {floor, top_db, eps, postv[3], chan0[C],
+ * chan1[C]}; log_mode 0 = this host's libm logf (as the reference build here), 1 = correctly rounded (the GPU's) */
+typedef struct bnno_dbimg bnno_dbimg;
+bnno_dbimg *bnno_dbimg_new(const int32_t *p, const float *window, const float *mel, const int32_t *rows,
+                           const float *consts);
+void bnno_dbimg_free(bnno_dbimg *f);
+int bnno_dbimg_frames_count(const bnno_dbimg *f);
+void bnno_dbimg_frames(const bnno_dbimg *f, const float *pcm, float *db, int log_mode);
+void bnno_dbimg_image(const bnno_dbimg *f, const float *db, float *img);
+void bnno_dbimg_run(const bnno_dbimg *f, const float *pcm, float *img, int log_mode);
+float bnno_logf_cr(float x);
+/* y[i] = the logarithm of x[i] for i < n: log_mode 0 this host's logf, 1 bnno_logf_cr */
+void bnno_log_n(const float *x, float *y, long n, int log_mode);
+/* FE_DBIMG's logarithm in package runs (bnno_pkg_*): 0 libm logf (default), 1 correctly rounded */
+void bnno_pkg_set_log_mode(int mode);
 typedef struct bnno_logmel bnno_logmel;
 /* NULL when the geometry is outside pc_logmel_new's limits (nfft a power of two in 16..2048, frame <= nfft, hop > 0,
  * pad >= 0, 1 <= nmel <= 512); window [frame], mel [nmel][nfft / 2 + 1] */

@@ -54,6 +54,10 @@ SIGS = {
     "bnno_mean_f16": (None, [_P, _I, _I, _I, _P]),
     "bnno_postpc_f16": (_I, [_P, _P, _P, _P, _P, _P, _P]),
     "bnno_dense_f16": (None, [_P, _P, _I, _P, _P]), "bnno_dense_f32": (None, [_P, _P, _I, _P, _P]),
+    "bnno_dbimg_new": (_P, [_P, _P, _P, _P, _P]), "bnno_dbimg_free": (None, [_P]),
+    "bnno_dbimg_frames_count": (_I, [_P]), "bnno_dbimg_frames": (None, [_P, _P, _P, _I]),
+    "bnno_dbimg_image": (None, [_P, _P, _P]), "bnno_dbimg_run": (None, [_P, _P, _P, _I]),
+    "bnno_logf_cr": (_F, [_F]), "bnno_log_n": (None, [_P, _P, _L, _I]), "bnno_pkg_set_log_mode": (None, [_I]),
 }
 DTYPES = {0: np.float32, 1: np.float16, 2: np.int8, 3: np.int32}
 _LIB = None
@@ -256,3 +260,56 @@ def run_many(path, pcm, threads=1, path_name="neon-int8"):
     if lib().bnno_pkg_run_many(path.encode(), path_name.encode(), x.shape[0], ptr(x), ptr(out), ptr(emb), threads):
         raise RuntimeError("oracle run failed")
     return out, emb
+
+
+def set_log_mode(mode):
+    """The logarithm of FE_DBIMG in packages the oracle runs: 0 this host's logf (the reference's call), 1 the
+    correctly rounded logarithm (the B200 kernel's)."""
+    lib().bnno_pkg_set_log_mode(int(mode))
+
+
+def log_f32(x, log_mode):
+    """the FE_DBIMG logarithm elementwise (bnno_log_n): log_mode 0 this host's logf, 1 the double-precision log
+    rounded once to float"""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib().bnno_log_n(ptr(x), ptr(y), x.size, int(log_mode))
+    return y
+
+
+class DbImg:
+    """FE_DBIMG (oracle_dbimg.c) from the record's 21 ints and its four tensors."""
+
+    def __init__(self, p, window, mel, rows, consts):
+        self._keep = [np.ascontiguousarray(p, np.int32), np.ascontiguousarray(window, np.float32),
+                      np.ascontiguousarray(mel, np.float32), np.ascontiguousarray(rows, np.int32),
+                      np.ascontiguousarray(consts, np.float32)]
+        self.p = self._keep[0]
+        self.h = lib().bnno_dbimg_new(*[ptr(a) for a in self._keep])
+        self.nfr = lib().bnno_dbimg_frames_count(self.h)
+
+    def image_elems(self):
+        p = self.p
+        return (int(p[14]) + 2 * int(p[20])) * (int(p[15]) + 2 * int(p[20])) * int(p[19])
+
+    def run(self, pcm, log_mode=0):
+        """windows pcm [n][nsamp] -> images [n][image elems]"""
+        x = np.ascontiguousarray(pcm, np.float32).reshape(-1, int(self.p[0]))
+        out = np.empty((x.shape[0], self.image_elems()), np.float32)
+        for w in range(x.shape[0]):
+            lib().bnno_dbimg_run(self.h, ptr(x[w]), ptr(out[w]), log_mode)
+        return out
+
+    def db(self, pcm, log_mode=0):
+        x = np.ascontiguousarray(pcm, np.float32).reshape(-1)
+        out = np.empty((int(self.p[6]), self.nfr), np.float32)
+        lib().bnno_dbimg_frames(self.h, ptr(x), ptr(out), log_mode)
+        return out
+
+    def close(self):
+        if self.h:
+            lib().bnno_dbimg_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()

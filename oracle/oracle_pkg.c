@@ -26,6 +26,7 @@ struct bnno_pkg {
   void **buf;
   bnno_fe *fe;
   bnno_logmel **logmel; /* per op: the FE_LOGMEL state (NULL for other ops) */
+  bnno_dbimg **dbimg;   /* per op: the FE_DBIMG state (NULL for other ops) */
   int n_classes, emb_dim;
 };
 
@@ -43,6 +44,10 @@ static int meta_i64(const uint8_t *m, size_t mbytes, uint32_t n, const char *key
   }
   return -1;
 }
+
+/* the natural logarithm of FE_DBIMG in package runs: 0 this host's libm logf (the reference's), 1 correctly rounded */
+static int g_log_mode;
+void bnno_pkg_set_log_mode(int mode) { g_log_mode = mode; }
 
 static const void *tdata(const bnno_pkg *p, const o_op *op, int i) {
   if (i >= op->nt || op->t[i] < 0 || (uint32_t)op->t[i] >= p->n_ten) return NULL;
@@ -105,8 +110,11 @@ bnno_pkg *bnno_pkg_open(const char *path, const char *path_name, char *err, size
   p->n_classes = meta_i64(m + off[0], off[1] - off[0], cnt[0], "n_classes", &v) ? 0 : (int)v;
   p->emb_dim = meta_i64(m + off[0], off[1] - off[0], cnt[0], "emb_dim", &v) ? 0 : (int)v;
   p->logmel = calloc(p->n_ops, sizeof(bnno_logmel *));
+  p->dbimg = calloc(p->n_ops, sizeof(bnno_dbimg *));
   for (uint32_t i = 0; i < p->n_ops; i++) {
     const o_op *op = &p->ops[i];
+    if (op->code == 16) /* FE_DBIMG: t = window, mel, rows, consts; p = 21 ints */
+      p->dbimg[i] = bnno_dbimg_new(op->p, tdata(p, op, 0), tdata(p, op, 1), tdata(p, op, 2), tdata(p, op, 3));
     if (op->code == 8) { /* FE_LOGMEL: t = window, mel, consts {floor, scale}; p = nsamp frame hop pad nfft nmel */
       const float *k = tdata(p, op, 2);
       p->logmel[i] = bnno_logmel_new(op->p[0], op->p[1], op->p[2], op->p[3], op->p[4], op->p[5], tdata(p, op, 0),
@@ -131,6 +139,9 @@ void bnno_pkg_close(bnno_pkg *p) {
   if (p->logmel)
     for (uint32_t i = 0; i < p->n_ops; i++) bnno_logmel_free(p->logmel[i]);
   free(p->logmel);
+  if (p->dbimg)
+    for (uint32_t i = 0; i < p->n_ops; i++) bnno_dbimg_free(p->dbimg[i]);
+  free(p->dbimg);
   free(p->ops);
   bnno_fe_free(p->fe);
   free(p->file);
@@ -186,6 +197,12 @@ static int run_op(bnno_pkg *p, const o_op *op) {
   case 6: /* POSTPC: b = [X, feat, pcin, pcout] */
     bnno_postpc(bptr(p, op, 0), tdata(p, op, 0), tdata(p, op, 1), tdata(p, op, 2), tdata(p, op, 3), bptr(p, op, 1));
     return 0;
+  case 16: { /* FE_DBIMG: b = [pcm, img] */
+    const bnno_dbimg *f = p->dbimg[op - p->ops];
+    if (!f) return -1;
+    bnno_dbimg_run(f, bptr(p, op, 0), bptr(p, op, 1), g_log_mode);
+    return 0;
+  }
   case 8: { /* FE_LOGMEL: b = [pcm, spec] */
     const bnno_logmel *f = p->logmel[op - p->ops];
     if (!f) return -1;

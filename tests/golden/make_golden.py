@@ -14,7 +14,8 @@ s8_packing.npz, and for the int8 prototype head (PROTO_S8): the reference loweri
 prototype heads into one-op neon-int8 packages (sha256 in proto_packages.json; bnneon_b200.synth.write_proto_package
 must write the same bytes) and its packer (quant_rows_s8, n4_panel_flags, the [Np/4][Kp/16][4][16] layout) runs on
 fixed matrices (proto_packing.npz); and the reference lowering's l_fe_logmel writes one-op log-mel front-end packages
-(logmel_packages.json); and the reference lowering writes the same v2.4 models for the neon-fp16 path (sha256 in
+(logmel_packages.json), and its l_fe_dbimg one-op dB-image front-end packages (dbimg_packages.json); and the
+reference lowering writes the same v2.4 models for the neon-fp16 path (sha256 in
 f16_packages.json, with the reference's fp16 SiLU coefficient table read from its source).
 """
 import hashlib
@@ -234,6 +235,66 @@ def f16_fixtures(ref_root):
         f.write("\n")
 
 
+# the one-op dB-image front-end packages (FE_DBIMG): keyword arguments of synth.dbimg_frontend (chan None: the seeded
+# mean / std pair)
+DBIMG_FES = {
+    "dbimg_v3": dict(synth.V3_FE, rows=list(synth.V3_FE["rows"])),
+    "dbimg_small": dict(nsamp=8000, nfft=256, hop=100, pad=128, pad_mode="reflect", nmel=40, rows=list(range(32)),
+                        Ho=48, Wo=64, C=3, top_db=80.0, norm=1),
+    "dbimg_zero": dict(nsamp=6000, nfft=512, hop=256, pad=256, pad_mode="zero", nmel=64, rows=list(range(50, 10, -1)),
+                       Ho=20, Wo=30, C=5, top_db=None, norm=2, post=[[1, 4.3429448], [3, -5.0], [2, 2.0]],
+                       chan=[[1, [0.5, 1.0, 1.5, 2.0, 2.5]], [3, [0.0, -0.25, 0.25, 1.0, -1.0]]]),
+    "dbimg_none": dict(nsamp=4096, nfft=64, hop=64, pad=0, pad_mode="none", nmel=8, rows=[7, 0, 3], Ho=3, Wo=64, C=1,
+                       top_db=10.0, norm=0, post=[], chan=[]),
+}
+
+
+def dbimg_frontend(g):
+    g = dict(g)
+    if g.get("post") is not None:
+        g["post"] = [(int(c), float(v)) for c, v in g["post"]]
+    if g.get("chan") is not None:
+        g["chan"] = [(int(c), np.asarray(v, np.float32)) for c, v in g["chan"]]
+    return synth.dbimg_frontend(**g)
+
+
+def reference_dbimg_package(ref_root, fe, dst):
+    """The reference lowering's FE_DBIMG record (lower.py l_fe_dbimg) in a one-op neon-int8 package."""
+    sys.path.insert(0, os.path.join(ref_root, "python"))
+    from bnneon.compiler import lower, pkgfmt  # pylint: disable=import-outside-toplevel
+    pkg = pkgfmt.Package()
+    lw = lower.Lowering(pkg, [], synth.PATH, fe["nsamp"])
+    o = dict(fe, out="img")
+    lw.l_fe_dbimg(0, o)
+    ob = lw.vbuf["img"]
+    bufs, _ = lower.plan_slots(lw.bufs, lw.out, [ob])
+    pkg.add_path(synth.PATH, lower.path_info(synth.PATH).hwcap, bufs, lw.out, 0, ob, None)
+    pkg.set(f"src_nodes/{synth.PATH}", "\n".join(lw.src))
+    ld = fe["C"] if fe["C"] % 4 == 0 else (fe["C"] + 3) & ~3
+    n_out = fe["Ho"] * fe["Wo"] * ld
+    for k, v in synth.metadata(n_out, 0, synth.labels_for(n_out), model_id="birdnet_v3_frontend_synthetic",
+                               family=synth.BNN_MODEL_BIRDNET_V3, sample_rate=synth.V3_SAMPLE_RATE,
+                               n_samples=fe["nsamp"], attribution="synthetic dB-image front end"):
+        pkg.set(k, v)
+    pkg.write(dst)
+
+
+def dbimg_fixtures(ref_root):
+    out = {}
+    with tempfile.TemporaryDirectory() as td:
+        for name, g in DBIMG_FES.items():
+            fe = dbimg_frontend(g)
+            ref = os.path.join(td, name + ".ref.bnpk")
+            reference_dbimg_package(ref_root, fe, ref)
+            mine = os.path.join(td, name + ".mine.bnpk")
+            synth.write_dbimg_package(mine, fe)
+            out[name] = dict(frontend=g, size=os.path.getsize(ref), sha256=sha(ref))
+            print(name, out[name]["size"], "writer matches" if sha(mine) == sha(ref) else "WRITER DIFFERS")
+    with open(os.path.join(HERE, "dbimg_packages.json"), "w", encoding="utf-8") as f:
+        json.dump(out, f, indent=1, sort_keys=True)
+        f.write("\n")
+
+
 def sha(path):
     with open(path, "rb") as f:
         return hashlib.sha256(f.read()).hexdigest()
@@ -280,6 +341,7 @@ def main():
     proto_fixtures(ref_root)
     logmel_fixtures(ref_root)
     f16_fixtures(ref_root)
+    dbimg_fixtures(ref_root)
 
 
 if __name__ == "__main__":
