@@ -9,9 +9,11 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "bnn_kernels.h"
 #include "emu.cuh"
+#include "smem_attr.cuh"
 #include "sync.cuh"
 
 namespace bnn {
@@ -121,20 +123,22 @@ __global__ void __launch_bounds__(kDwThreads) k_dw3(const float *__restrict__ xp
 }
 
 // The same DW3 with the input streamed by TMA. One CTA per (window, group of CG channels) walks the output rows:
-// the haloed input rows (W + 2 pixels x CG channels each, one 3-D tensor-map box) pass through a ring of NR slots in
-// shared memory, loaded one row step ahead (NR = S + 3: the 3 rows of this step plus the S new rows of the next), so
-// every input byte is read from HBM once and no thread waits on a global load. Thread (lane, channel quad) keeps its
+// the haloed input rows (W + 2 pixels x CG channels each, one 3-D tensor-map box) pass through a ring of nr slots in
+// shared memory (nr >= S + 3: the 3 rows of this step plus the S new rows of the next; every slot beyond those is
+// one more row of lookahead, and a ring as deep as the window's rows loads them all up front), so every input byte
+// is read from HBM once and no thread waits on a global load. Thread (lane, channel quad) keeps its
 // quad's weights in registers and computes pixel groups lane, lane + NL, ... of the row (R consecutive pixels per
 // group share their input columns), stores them and leaves them in a double-buffered row tile; after the step's
 // barrier the first CG threads continue their channel's sum over the row in pixel order.
+constexpr int kDw3MaxRing = 32;
 template <int S, int R>
 __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMap tmx, int W, int C, int CG, int Ho,
-                                              int Wo, const float *__restrict__ wt, const float *__restrict__ bias,
-                                              float *__restrict__ out, long long ows, float *__restrict__ chsum,
-                                              long long cws, int *err) {
-  constexpr int NR = S + 3, NX = (R - 1) * S + 3;
+                                              int Wo, int NR, const float *__restrict__ wt,
+                                              const float *__restrict__ bias, float *__restrict__ out, long long ows,
+                                              float *__restrict__ chsum, long long cws, int *err) {
+  constexpr int NX = (R - 1) * S + 3;
   extern __shared__ __align__(128) uint8_t dsm[];
-  __shared__ __align__(8) unsigned long long bar[NR];
+  __shared__ __align__(8) unsigned long long bar[kDw3MaxRing];
   __shared__ uint32_t lut[256];
   const int tid = threadIdx.x, nt = blockDim.x;
   for (int i = tid; i < 256; i += nt) lut[i] = g_frecpe_lut[i];
@@ -174,15 +178,17 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
       tma_load_3d(ring + sl * row_stride, &tmx, smem_u32(&bar[sl]), grp * CG, issued * Wp, win);
     }
   };
-  if (tid == 0) issue_to(S + 2);  // the rows of steps 0 and 1
+  if (tid == 0) issue_to(NR - 1);  // as many rows as the ring holds
   float cs = 0.f;
   int oy = 0;
   for (; oy < Ho; oy++) {
     bool ok = true;
+    int slot[3];
 #pragma unroll
     for (int ky = 0; ky < 3; ky++) {
       const int iy = oy * S + ky;
-      ok = ok && mbar_wait(smem_u32(&bar[iy % NR]), (uint32_t)(iy / NR) & 1u);
+      slot[ky] = iy % NR;
+      ok = ok && mbar_wait(smem_u32(&bar[slot[ky]]), (uint32_t)(iy / NR) & 1u);
     }
     float *ob = obuf + (oy & 1) * Wo * CG;
     if (comp) {
@@ -193,7 +199,7 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
         float2 acc[R][2], acb[R][2], acd[R][2];
 #pragma unroll
         for (int ky = 0; ky < 3; ky++) {
-          const float *rw = ringf + ((oy * S + ky) % NR) * (row_stride >> 2) + (x0 * S) * CG + 4 * q;
+          const float *rw = ringf + slot[ky] * (row_stride >> 2) + (x0 * S) * CG + 4 * q;
           float4 xin[NX];
 #pragma unroll
           for (int j = 0; j < NX; j++) xin[j] = *reinterpret_cast<const float4 *>(rw + j * CG);
@@ -228,7 +234,7 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
       }
     }
     if (!__syncthreads_and(ok)) break;  // every thread has left this step's rows and written its outputs
-    if (tid == 0) issue_to((oy + 2) * S + 2);
+    if (tid == 0) issue_to((oy + 1) * S + NR - 1);  // rows below (oy + 1) S are free
     if (tid < CG) {
       int x = 0;
       for (; x + 8 <= Wo; x += 8) {
@@ -604,19 +610,36 @@ static PFN_cuTensorMapEncodeTiled_v12000 conv_encode_fn(void) {
   return fn;
 }
 
-// shared memory of the TMA form for CG channels: the ring of S + 3 input rows and the two output-row tiles
-static size_t dw3t_smem(int W, int Wo, int s, int cg) {
+// shared memory of the TMA form for CG channels: the ring of nr input rows and the two output-row tiles
+static size_t dw3t_smem(int W, int Wo, int nr, int cg) {
   const size_t row_stride = ((size_t)(W + 2) * cg * 4 + 127) & ~(size_t)127;
-  return (size_t)(s + 3) * row_stride + sizeof(float) * 2 * Wo * cg;
+  return (size_t)nr * row_stride + sizeof(float) * 2 * Wo * cg;
 }
 
-// channels per CTA for the TMA form: the largest multiple of 4 dividing C, at most 256 (one box dimension) and with
-// at most 113 KB of shared memory (two CTAs per SM); 0 if none
-static int dw3t_group(int C, int W, int Wo, int s) {
+// channels per CTA for the TMA form: the largest multiple of 4 dividing C, at most 256 (one box dimension), whose
+// minimal ring of S + 3 rows leaves two CTAs per SM (budget: the dynamic shared memory each may use); 0 if none.
+// BNN_DW3_CG overrides it (a divisor of C, a multiple of 4, that fits).
+static int dw3t_group(int C, int W, int Wo, int s, size_t budget) {
   int best = 0;
   for (int cg = 4; cg <= C && cg <= 256; cg += 4)
-    if (C % cg == 0 && dw3t_smem(W, Wo, s, cg) <= 113 * 1024) best = cg;
+    if (C % cg == 0 && dw3t_smem(W, Wo, s + 3, cg) <= budget) best = cg;
+  const char *e = getenv("BNN_DW3_CG");
+  const int want = e ? atoi(e) : 0;
+  if (want >= 4 && want <= 256 && want % 4 == 0 && C % want == 0 && dw3t_smem(W, Wo, s + 3, want) <= budget)
+    best = want;
   return best;
+}
+
+// ring depth: S + 3 (one row step of lookahead, which measured as fast as deeper rings on every v2.4 layer);
+// BNN_DW3_NR asks for a deeper one (at most the rows the outputs read, kDw3MaxRing and the budget)
+static int dw3t_ring(int W, int Wo, int s, int cg, int rows_in, size_t budget) {
+  const char *e = getenv("BNN_DW3_NR");
+  int cap = e ? atoi(e) : 0;
+  if (cap > rows_in) cap = rows_in;
+  if (cap > kDw3MaxRing) cap = kDw3MaxRing;
+  int nr = s + 3;
+  while (nr < cap && dw3t_smem(W, Wo, nr + 1, cg) <= budget) nr++;
+  return nr;
 }
 
 extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int C, int s, const float *w,
@@ -624,7 +647,8 @@ extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int
                         int *err, bnn_stream_t st) {
   if (B <= 0) return 0;
   const int P = Ho * Wo, C4 = C / 4;
-  const int cg = dw3t_group(C, W, Wo, s);
+  const size_t budget = smem_budget(k_dw3t<1, 2>, 2);  // every instance has the same static shared memory
+  const int cg = dw3t_group(C, W, Wo, s, budget);
   PFN_cuTensorMapEncodeTiled_v12000 enc = conv_encode_fn();
   if (cg && enc && ((uintptr_t)xp & 15) == 0 && (xws * 4) % 16 == 0 && W + 2 <= 256 && (s == 1 || s == 2) &&
       (Ho - 1) * s + 3 <= H + 2 && ((uintptr_t)out & 15) == 0 && ows % 4 == 0) {
@@ -636,7 +660,8 @@ extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int
     if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(xp), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
-      const size_t smem = dw3t_smem(W, Wo, s, cg);
+      const int nr = dw3t_ring(W, Wo, s, cg, (Ho - 1) * s + 3, budget);
+      const size_t smem = dw3t_smem(W, Wo, nr, cg);
       const unsigned grid = (unsigned)B * (unsigned)(C / cg);
       // threads: whole channel quads up to 256, at least the CG summing threads
       const int Q = cg / 4;
@@ -647,7 +672,7 @@ extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int
 #define BNN_DW3T(SS, RR)                                                                                   \
   do {                                                                                                    \
     cudaFuncSetAttribute(k_dw3t<SS, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);         \
-    k_dw3t<SS, RR><<<grid, nt, smem, st>>>(map, W, C, cg, Ho, Wo, w, b, out, ows, chsum, cws, err);       \
+    k_dw3t<SS, RR><<<grid, nt, smem, st>>>(map, W, C, cg, Ho, Wo, nr, w, b, out, ows, chsum, cws, err);   \
   } while (0)
       if (s == 1) { if (pair) BNN_DW3T(1, 2); else BNN_DW3T(1, 1); }
       else { if (pair) BNN_DW3T(2, 2); else BNN_DW3T(2, 1); }

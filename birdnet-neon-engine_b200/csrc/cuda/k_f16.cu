@@ -22,6 +22,7 @@
 
 #include "bnn_kernels.h"
 #include "emu.cuh"
+#include "smem_attr.cuh"
 #include "sync.cuh"
 #include "tc.cuh"
 
@@ -1251,11 +1252,12 @@ extern "C" int bnnk_dw3_f16(int B, const uint16_t *xp, long long xws, int H, int
                             const uint16_t *w, const uint16_t *b, uint16_t *out, long long ows, int Ho, int Wo,
                             float *chsum, long long cws, int *err, bnn_stream_t st) {
   if (B <= 0) return 0;
-  // the TMA form: channels per CTA the largest multiple of 8 dividing C, at most 256 (one box dimension), with at
-  // most 113 KB of shared memory (two CTAs per SM)
+  // the TMA form: channels per CTA the largest multiple of 8 dividing C, at most 256 (one box dimension), with the
+  // shared memory of two CTAs per SM
+  const size_t budget = smem_budget(k_dw3t_f16<1, 2, false>, 2);
   int cg = 0;
   for (int g = 8; g <= C && g <= 256; g += 8)
-    if (C % g == 0 && dw3t_f16_smem(W, Wo, s, g) <= 113 * 1024) cg = g;
+    if (C % g == 0 && dw3t_f16_smem(W, Wo, s, g) <= budget) cg = g;
   PFN_cuTensorMapEncodeTiled_v12000 enc = f16_encode_fn();
   if (cg && enc && ((uintptr_t)xp & 15) == 0 && xws % 8 == 0 && W + 2 <= 256 && (s == 1 || s == 2) &&
       ((uintptr_t)out & 15) == 0 && ows % 8 == 0 && ((uintptr_t)w & 15) == 0 && ((uintptr_t)b & 15) == 0 &&

@@ -28,4 +28,18 @@ struct SmemAttr {
   }
 };
 
+// The dynamic shared memory each of k resident CTAs of `kernel` may use on this device: the SM's shared memory split k
+// ways, less the per-CTA reservation and the kernel's static shared memory.
+template <typename Kernel>
+size_t smem_budget(Kernel *kernel, int k) {
+  int dev = 0, per_sm = 0, reserved = 0;
+  cudaFuncAttributes fa;
+  if (cudaGetDevice(&dev) || cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) ||
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) ||
+      cudaFuncGetAttributes(&fa, kernel))
+    return 0;
+  const long long b = (long long)per_sm / k - reserved - (long long)fa.sharedSizeBytes;
+  return b > 0 ? (size_t)b : 0;
+}
+
 }  // namespace bnn
