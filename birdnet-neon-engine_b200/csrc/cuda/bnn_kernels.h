@@ -44,6 +44,8 @@ int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_cap, int kq
 /* rows of the weight buffer the plan of a layer with np (padded) output channels and rows_cap rows reads:
  * n_tiles * bn */
 int bnnk_gemm_weight_rows(int np, int rows_cap);
+/* N tiles of the plan's GEMM (1: each tile holds whole rows, so its epilogue can quantize them for the next layer) */
+int bnnk_gemm_n_tiles(const bnnk_gemm_plan *p);
 
 /* epilogue of PW_S8 (gemm_s8n.c:105-135): y = (float)(acc - za * cs) * (sw * sa) + b, act (0 none, 1 SiLU,
  * 2 ReLU), + residual, stored at the padded row of each pixel (ow / opad) of each window */
@@ -57,6 +59,13 @@ typedef struct {
   int ldr, rw, rpad;
   const float *sw, *bias;
   const int32_t *cs;
+  /* optional: the stored rows quantized for the ungated PW_S8 that reads them next (s8n_quant_rows over their first
+   * qk columns, qk % 4 == 0, qk <= 256): q [rows][qkq], sa, za [rows]. Needs one N tile (every CTA tile holds whole
+   * rows), an unpadded output (opad 0) with 16-byte aligned rows, and q distinct from this GEMM's own rows. */
+  int8_t *qo;
+  float *qsa;
+  int32_t *qza;
+  int qk, qkq;
 } bnnk_epilogue;
 int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float *sa, const int32_t *za, const bnnk_epilogue *e,
               int *err, bnn_stream_t st);

@@ -233,6 +233,8 @@ constexpr int kMaxThreads = 832;  // 2 + 24 warps: 64 + 128 * ne * nh with ne * 
 constexpr int kSPMax = 1536;      // widest layer whose epilogue parameters are staged in shared memory
 
 constexpr int kEpiUnits = 3;  // 8-column TMEM loads in flight per epilogue warp
+// the epilogue's per-row partial (min, max) for the next layer's quantizer: 2 tile parities x 6 warps of 128 rows
+constexpr size_t kQPartBytes = 2 * 6 * 128 * sizeof(float2);
 // wait for this thread's TMEM loads; the registers they fill are operands of the wait, so no use moves above it
 __device__ __forceinline__ void tmem_wait(uint32_t (&r)[kEpiUnits][8]) {
 #define BNN_R8(u) "+r"(r[u][0]), "+r"(r[u][1]), "+r"(r[u][2]), "+r"(r[u][3]), "+r"(r[u][4]), "+r"(r[u][5]), \
@@ -271,10 +273,11 @@ __device__ __forceinline__ long long padded_row(int m, int w, int pad) {
 // (RES), store; VEC: 32-byte aligned rows (8-float loads and stores). Branch-free for fixed template arguments, so
 // the units' independent chains can overlap. psw / pb / pcs point at the tile's first column of the per-column
 // parameters (shared or global memory).
-template <int ACT, bool RES, bool VEC, int NU>
+template <int ACT, bool RES, bool VEC, int NU, bool kQ = false>
 __device__ __forceinline__ void epilogue_units(const uint32_t (&acc)[kEpiUnits][8], int kofs, int u0, int nh, float sa,
                                                int32_t za, const float *psw, const float *pb, const int32_t *pcs,
-                                               float *orow, const float *rrow, const uint32_t *lut) {
+                                               float *orow, const float *rrow, const uint32_t *lut, float &lo,
+                                               float &hi, int qk) {
   const float2 sa2 = splat2(sa);
   const uint32_t nza = 0u - (uint32_t)za;  // acc - za cs = acc + (-za) cs, one integer multiply-add (mod 2^32)
 #pragma unroll
@@ -308,6 +311,11 @@ __device__ __forceinline__ void epilogue_units(const uint32_t (&acc)[kEpiUnits][
       y[j] = RES ? __fadd_rn(v.x, rv[j]) : v.x;
       y[j + 1] = RES ? __fadd_rn(v.y, rv[j + 1]) : v.y;
     }
+    if (kQ) {  // the row's NaN-propagating min / max over the next layer's K columns (s8n_quant_rows)
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+        if (c + j < qk) { lo = fmin_nan(lo, y[j]); hi = fmax_nan(hi, y[j]); }
+    }
     if (VEC) {
       st8_global(orow + c, y);
     } else {
@@ -317,13 +325,25 @@ __device__ __forceinline__ void epilogue_units(const uint32_t (&acc)[kEpiUnits][
   }
 }
 
-template <int NU>
+template <int NU, bool kQ>
 __device__ __forceinline__ void epilogue_act(const GemmArgs &a, const uint32_t (&acc)[kEpiUnits][8], int kofs, int u0,
                                              int nh, float sa, int32_t za, const float *psw, const float *pb,
-                                             const int32_t *pcs, float *orow, const float *rrow, const uint32_t *lut) {
+                                             const int32_t *pcs, float *orow, const float *rrow, const uint32_t *lut,
+                                             float &lo, float &hi) {
 #define BNN_E(ACT, RES, VEC) \
-  epilogue_units<ACT, RES, VEC, NU>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut)
+  epilogue_units<ACT, RES, VEC, NU>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut, lo, hi, 0)
   const bool vec = a.vec_out && (!rrow || a.vec_res);
+  if (kQ) {  // the rows also quantized for the next layer: linear layers (the host's rule)
+    if (rrow && vec) epilogue_units<0, true, true, NU, true>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut,
+                                                             lo, hi, a.e.qk);
+    else if (rrow) epilogue_units<0, true, false, NU, true>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut,
+                                                            lo, hi, a.e.qk);
+    else if (vec) epilogue_units<0, false, true, NU, true>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut,
+                                                           lo, hi, a.e.qk);
+    else epilogue_units<0, false, false, NU, true>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut, lo, hi,
+                                                   a.e.qk);
+    return;
+  }
   if (!vec) {  // rows off 32-byte boundaries (per-op API callers): one general form
     if (rrow) {
       if (a.e.act == 1) BNN_E(1, true, false); else if (a.e.act == 2) BNN_E(2, true, false); else BNN_E(0, true, false);
@@ -340,8 +360,57 @@ __device__ __forceinline__ void epilogue_act(const GemmArgs &a, const uint32_t (
 #undef BNN_E
 }
 
-// kSP: the per-column parameters (sw, bias, cs; np <= kSPMax columns) are staged in shared memory once per CTA
-template <int SW, bool kSP>
+// named barrier over nthreads threads with an AND of their predicates (bar.red.and): every thread of the group arrives,
+// so a group whose wait failed in some warps still leaves the barrier together
+__device__ __forceinline__ bool bar_and(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
+// The next layer's quantized row from this tile's stored row (s8n_quant_rows): the thread that stored units u0, u0 + nh,
+// ... of the row reads them back (its own stores, in order) and writes their quantized bytes; columns from qk on are
+// the zero point; the thread of the quarter's first warp also writes the pads past the last unit.
+__device__ __forceinline__ void quant_units(const GemmArgs &a, int row, const float *orow, int units, int u0, int nh,
+                                            float lo, float hi, bool first) {
+  const int qk = a.e.qk, K8 = qk & ~7;
+  float inv, s;
+  int32_t z;
+  quant_params(lo, hi, inv, z, s);
+  if (first) { a.e.qsa[row] = s; a.e.qza[row] = z; }
+  uint2 *qr = reinterpret_cast<uint2 *>(a.e.qo + (long long)row * a.e.qkq);
+  const float2 inv2 = splat2(inv);
+  const uint32_t zp = ((uint32_t)z & 0xffu) * 0x01010101u;
+  for (int u = u0; u < units; u += nh) {
+    const int c = 8 * u;
+    if (c >= a.e.qkq) break;
+    uint32_t wd[2] = {zp, zp};
+    if (c < qk) {
+      const float4 t0 = __ldcg(reinterpret_cast<const float4 *>(orow + c));
+      const float4 t1 = __ldcg(reinterpret_cast<const float4 *>(orow + c + 4));
+      const float2 p0 = mul2_rn(make_float2(t0.x, t0.y), inv2), p1 = mul2_rn(make_float2(t0.z, t0.w), inv2);
+      wd[0] = quant_word(p0.x, p0.y, p1.x, p1.y, z, c < K8);
+      if (c + 4 < qk) {
+        const float2 p2 = mul2_rn(make_float2(t1.x, t1.y), inv2), p3 = mul2_rn(make_float2(t1.z, t1.w), inv2);
+        wd[1] = quant_word(p2.x, p2.y, p3.x, p3.y, z, c + 4 < K8);
+      }
+    }
+    qr[u] = make_uint2(wd[0], wd[1]);
+  }
+  if (first)
+    for (int c = 8 * units; c < a.e.qkq; c += 8) qr[c / 8] = make_uint2(zp, zp);
+}
+
+// kSP: the per-column parameters (sw, bias, cs; np <= kSPMax columns) are staged in shared memory once per CTA;
+// kQ: the epilogue also quantizes the stored rows for the next layer (a.e.qo)
+template <int SW, bool kSP, bool kQ>
 __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constant__ CUtensorMap tma_a,
                                                            const __grid_constant__ CUtensorMap tma_b,
                                                            const GemmArgs a) {
@@ -360,6 +429,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
   uint8_t *par = dsmem + (base - smem_u32(dsmem)) + (size_t)S * stage_bytes;
   float *p_sw = reinterpret_cast<float *>(par), *p_b = p_sw + a.np;
   int32_t *p_cs = reinterpret_cast<int32_t *>(p_b + a.np);
+  // the epilogue threads' partial (min, max) of their rows, per tile parity, group and warp: [2][ne][nh][128]
+  float2 *q_part = reinterpret_cast<float2 *>(par + (kSP ? (size_t)12 * a.np : 0));
   if (kSP) {
     for (int i = threadIdx.x; i < a.np; i += blockDim.x) {
       p_sw[i] = __ldg(a.e.sw + i);
@@ -443,6 +514,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
     // epilogue: group g drains accumulator g; its 4 * nh warps split the 8-column units of a tile round robin, the
     // warp's TMEM lane quarter q (= warp % 4) fixing its 32 rows
     const int e = warp - 2, g = e / (4 * a.nh), h = (e % (4 * a.nh)) / 4, q = warp % 4;
+    constexpr bool fq = kQ;  // the tile's rows are quantized for the next layer after its epilogue
     int use = 0;
     for (int t = blockIdx.x + g * gridDim.x; t < a.tiles; t += a.ne * gridDim.x, use++) {
       const int m0 = (t / a.n_tiles) * 128, n0 = (t % a.n_tiles) * a.bn;
@@ -458,9 +530,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
         za = __ldg(a.za + row);
       }
       bool ok = mbar_wait(smem_u32(&bar_acc_full[g]), use & 1);
-      ok = __all_sync(0xffffffffu, ok) && !abort_s;
+      ok = __all_sync(0xffffffffu, ok && !abort_s);  // one outcome per warp (abort_s may change between lanes' reads)
       if (!ok) {
         if (lane == 0) { atomicExch(a.err, BNNK_ERR_EPI_WAIT); abort_s = 1; }
+        if (!fq) break;
+        bar_and(1 + g, 128 * a.nh, false);  // the group's other warps leave with this one
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -471,6 +545,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
       const float *qsw = kSP ? p_sw + n0 : a.e.sw + n0, *qb = kSP ? p_b + n0 : a.e.bias + n0;
       const int32_t *qcs = kSP ? p_cs + n0 : a.e.cs + n0;
       const uint32_t tq = tmem + (uint32_t)(g * a.acc_cols) + ((uint32_t)(q * 32) << 16);
+      float lo = __uint_as_float(0x7f800000u), hi = __uint_as_float(0xff800000u);
       for (int u0 = h; u0 < units; u0 += kEpiUnits * a.nh) {
         uint32_t acc[kEpiUnits][8];
 #pragma unroll
@@ -481,18 +556,33 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
         tmem_wait(acc);
         if (live) {
           if (u0 + (kEpiUnits - 1) * a.nh < units) {  // every unit of the batch is a real column block
-            epilogue_act<kEpiUnits>(a, acc, 0, u0, a.nh, sa, za, qsw, qb, qcs, orow, rrow, s_lut);
+            epilogue_act<kEpiUnits, kQ>(a, acc, 0, u0, a.nh, sa, za, qsw, qb, qcs, orow, rrow, s_lut, lo, hi);
           } else {
 #pragma unroll
             for (int k = 0; k < kEpiUnits; k++)
               if (u0 + k * a.nh < units)
-                epilogue_act<1>(a, acc, k, u0 + k * a.nh, a.nh, sa, za, qsw, qb, qcs, orow, rrow, s_lut);
+                epilogue_act<1, kQ>(a, acc, k, u0 + k * a.nh, a.nh, sa, za, qsw, qb, qcs, orow, rrow, s_lut, lo, hi);
           }
         }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[g]));
+      if (fq) {
+        // the row's min / max from its nh threads' partials (the barrier orders their shared stores before the reads;
+        // a warp whose wait failed arrives with false and all leave), then this thread's units quantized
+        float2 *pp = q_part + ((size_t)((use & 1) * a.ne + g) * a.nh) * 128 + q * 32 + lane;
+        pp[h * 128] = make_float2(lo, hi);
+        if (!bar_and(1 + g, 128 * a.nh, true)) break;
+        if (live) {
+          for (int hh = 0; hh < a.nh; hh++) {
+            const float2 v = pp[hh * 128];
+            lo = fmin_nan(lo, v.x);
+            hi = fmax_nan(hi, v.y);
+          }
+          quant_units(a, row, orow, units, h, a.nh, lo, hi, h == 0);
+        }
+      }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -653,6 +743,8 @@ static void n_tiling(int np, int rows_cap, int *n_tiles, int *bn) {
   *bn = (b + 15) & ~15;
 }
 
+extern "C" int bnnk_gemm_n_tiles(const bnnk_gemm_plan *p) { return p->n_tiles; }
+
 extern "C" int bnnk_gemm_weight_rows(int np, int rows_cap) {
   int t, bn;
   n_tiling(np, rows_cap, &t, &bn);
@@ -713,7 +805,7 @@ extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_
   const size_t stage = (size_t)(128 + p->bn) * p->sw;
   int s = (int)((200 * 1024 - par) / stage);
   p->stages = s < 2 ? 2 : s > kMaxStages ? kMaxStages : s;
-  p->smem = (size_t)p->stages * stage + 1024 + par;
+  p->smem = (size_t)p->stages * stage + 1024 + par + kQPartBytes;
   p->idesc = idesc_i8(p->bn);
   const int wrows = p->n_tiles * p->bn;  // the weight buffer holds n_tiles * bn rows (zero beyond n)
   int e = encode_2d(p->tma_a, q, kq, rows_cap, p->sw, 128, p->sw);
@@ -721,16 +813,20 @@ extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_
   return e;
 }
 
-template <int SW, bool kSP>
-static int launch_gemm(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
+template <int SW, bool kSP, bool kQ>
+static int launch_gemm_q(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
   // the dynamic shared memory this instantiation may use so far, per device (static + dynamic <= 227 KB)
   static SmemAttr attr;
-  const cudaError_t e = attr.ensure(k_gemm_s8<SW, kSP>, p->smem);
+  const cudaError_t e = attr.ensure(k_gemm_s8<SW, kSP, kQ>, p->smem);
   if (e) return e;
   const int grid = a.tiles < num_sms() ? a.tiles : num_sms();
-  k_gemm_s8<SW, kSP><<<grid, 64 + 128 * a.ne * a.nh, p->smem, st>>>(*(const CUtensorMap *)p->tma_a,
-                                                                    *(const CUtensorMap *)p->tma_b, a);
+  k_gemm_s8<SW, kSP, kQ><<<grid, 64 + 128 * a.ne * a.nh, p->smem, st>>>(*(const CUtensorMap *)p->tma_a,
+                                                                        *(const CUtensorMap *)p->tma_b, a);
   return cudaGetLastError();
+}
+template <int SW, bool kSP>
+static int launch_gemm(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
+  return a.e.qo ? launch_gemm_q<SW, kSP, true>(p, a, st) : launch_gemm_q<SW, kSP, false>(p, a, st);
 }
 
 static bool aligned32(const float *ptr, long long ws, int ld) {
@@ -754,6 +850,10 @@ extern "C" int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float 
   a.nh = p->nh;
   a.tmem_alloc = tmem_pow2(p->ne * p->tmem_cols);
   if (a.tmem_alloc > 512) return cudaErrorInvalidValue;
+  if (e->qo && (p->n_tiles != 1 || e->opad || e->qk <= 0 || e->qk % 4 || e->qk > 256 || e->qk > p->n ||
+                e->qkq < e->qk || e->qkq % 4 || ((uintptr_t)e->out & 15) || e->ldo % 4 || e->ows % 4 ||
+                ((uintptr_t)e->qo & 3) || !e->qsa || !e->qza))
+    return cudaErrorInvalidValue;
   a.vec_out = aligned32(e->out, e->ows, e->ldo);
   a.vec_res = e->res ? aligned32(e->res, e->rws, e->ldr) : 0;
   a.idesc = p->idesc;

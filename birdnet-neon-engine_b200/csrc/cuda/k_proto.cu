@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(kPMaxThreads, 1) k_proto_colmax(const __grid_c
     for (int t = blockIdx.x + g * gridDim.x; t < a.tiles; t += a.ne * gridDim.x, use++) {
       const int m0 = (t / a.n_ct) * 128 * MH, ct = t % a.n_ct;
       bool ok = mbar_wait(smem_u32(&bar_acc_full[g]), use & 1);
-      ok = __all_sync(0xffffffffu, ok) && !abort_s;
+      ok = __all_sync(0xffffffffu, ok && !abort_s);  // one outcome per warp
       if (!ok) {
         if (lane == 0) { atomicExch(a.err, BNNK_ERR_EPI_WAIT); abort_s = 1; }
         break;

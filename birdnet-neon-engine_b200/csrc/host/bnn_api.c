@@ -330,7 +330,7 @@ int bnn_set_batch(bnn_ctx *c, int batch) {
   return make_devices(c, n);
 }
 int bnn_get_batch(const bnn_ctx *c) { return c ? c->batch : 0; }
-int bnn_launches_per_batch(const bnn_ctx *c) { return c ? c->launches : 0; }
+int bnn_launches_per_batch(const bnn_ctx *c) { return c ? c->launches - c->launches_fused : 0; }
 
 /* ------------------------------------------------------------------ inference */
 

@@ -75,6 +75,10 @@ typedef struct {
   int32_t *cs;
   bnnk_gemm_plan plan;
   int kq;
+  /* PW_S8 pairs (pwl, then the ungated expand that reads its rows): qnext = this op's GEMM epilogue quantizes its
+   * stored rows for op i + 1; qsel = this op's quantized rows live in the second scratch (q2, sa2, za2), which the
+   * op before writes while its own GEMM still reads the first */
+  int qnext, qsel;
   /* DW3, SE_GATE, C0POOL, POSTPC; PROTO_S8: f[0] chunk maxima scratch, f[1] class weights, f[2] class biases */
   float *f[6];
   /* PROTO_S8: prototype rows w [Np][Kp], sw, the GEMM plan, eps */
@@ -103,6 +107,10 @@ typedef struct {
   void **priv;          /* per-buffer private allocations (halos, input) */
   bnn_devop *ops;
   int8_t *q;            /* int8 GEMM scratch: [batch * rows][kq] */
+  int8_t *q2;           /* the second int8 scratch (sa2, za2): rows quantized by a pwl GEMM for the expand after it */
+  float *sa2;
+  int32_t *za2;
+  int fused_q;          /* PW_S8 quantizer launches this device's set-up folded into the GEMM before */
   float *sa, *fe_minmax, *pcin;
   int32_t *za;
   uint16_t *g16;        /* SE f16: the fp16 gates [batch][C] */
@@ -142,7 +150,8 @@ struct bnn_ctx {
   int n_dev;      /* devices in use */
   int dev_ids[64];
   bnn_dev *dev[64];
-  int launches;   /* kernel launches per batch */
+  int launches;   /* kernel launches per batch, before the set-up's PW_S8 pair fusion */
+  int launches_fused; /* launches the pair fusion of the devices' set-up removed (the same on every device) */
   int prof;       /* BNN_PROF */
 };
 

@@ -1214,6 +1214,19 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
   }
 }
 
+/* ops i and i + 1 are a PW_S8 pair whose quantizer the GEMM of op i can run: op i + 1 is ungated and reads op i's
+ * output rows (same rows per window, its lda op i's ldo, no halo) over K columns, K % 4 == 0, K <= 256, K <= op i's N.
+ * (Whether op i's GEMM holds whole rows per tile depends on the batch: the set-up checks its plan.) */
+static int pw_pair(const bnn_ctx *c, int i) {
+  if (i < 0 || i + 1 >= c->n_ops) return 0;
+  const bnn_op *a = &c->ops[i], *b = &c->ops[i + 1];
+  if (a->code != BNN_OP_PW_S8 || b->code != BNN_OP_PW_S8 || (b->nb == 7 && b->b[6] >= 0)) return 0;
+  if (a->nb < 2 || a->b[1] < 0 || b->b[0] != a->b[1] || c->bufd[a->b[1]].halo) return 0;
+  const int *pa = a->p, *pb = b->p;
+  return pb[4] == pa[4] && pb[5] == pa[7] && pa[9] == 0 && pb[1] > 0 && pb[1] % 4 == 0 && pb[1] <= 256 &&
+         pb[1] <= pa[0];
+}
+
 int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
   *kind = BNN_ERR_CPU;
   bnn_dev *dv = calloc(1, sizeof *dv);
@@ -1290,10 +1303,28 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
     if (qb > qbytes) qbytes = qb;
     if (r > rows) rows = r;
   }
+  /* the second scratch: the expand layers of PW_S8 pairs, whose rows the pwl GEMM before quantizes when
+   * BNN_PW_FUSE=1. Off by default: on the v2.4 package at batch 256 the 13 fused pwl epilogues took longer than the
+   * 13 quantizer launches they replace (PW_S8 class 2.41 ms per step fused, 2.37 ms separate) */
+  size_t qbytes2 = 0, rows2 = 0;
+  if (getenv("BNN_PW_FUSE") && !strcmp(getenv("BNN_PW_FUSE"), "1"))
+    for (int i = 0; i + 1 < c->n_ops; i++)
+      if (pw_pair(c, i)) {
+        const bnn_op *op = &c->ops[i + 1];
+        const size_t r = (size_t)B * (size_t)op->p[4], qb = r * (size_t)R32(op->p[1]);
+        if (qb > qbytes2) qbytes2 = qb;
+        if (r > rows2) rows2 = r;
+      }
   CK(cudaMalloc((void **)&dv->q, qbytes), "int8 row scratch");
   CK(cudaMemset(dv->q, 0, qbytes), "int8 row scratch");
   CK(cudaMalloc((void **)&dv->sa, sizeof(float) * rows), "int8 scale scratch");
   CK(cudaMalloc((void **)&dv->za, sizeof(int32_t) * rows), "int8 zero-point scratch");
+  if (qbytes2) {
+    CK(cudaMalloc((void **)&dv->q2, qbytes2), "int8 row scratch");
+    CK(cudaMemset(dv->q2, 0, qbytes2), "int8 row scratch");
+    CK(cudaMalloc((void **)&dv->sa2, sizeof(float) * rows2), "int8 scale scratch");
+    CK(cudaMalloc((void **)&dv->za2, sizeof(int32_t) * rows2), "int8 zero-point scratch");
+  }
   CK(cudaMalloc((void **)&dv->fe_minmax, sizeof(float) * 2 * B), "front-end scratch");
   CK(cudaMalloc((void **)&dv->pcin, sizeof(float) * 6 * 1728 * B), "post-conv scratch");
   size_t gate_elems = 8;
@@ -1313,7 +1344,18 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
     if (op->code == BNN_OP_PW_S8 || op->code == BNN_OP_GEMV_S8) {
       bnn_devop *o = &dv->ops[i];
       const int r = B * (op->code == BNN_OP_PW_S8 ? op->p[4] : 1);
-      if (bnnk_gemm_plan_init(&o->plan, dv->q, r, o->kq, o->w, op->p[0], op->p[3])) {
+      /* the expand of a pair whose pwl GEMM holds whole rows (one N tile) and stores 16-byte aligned rows: its rows
+       * come quantized from that GEMM into the second scratch */
+      if (dv->q2 && pw_pair(c, i - 1) && bnnk_gemm_n_tiles(&dv->ops[i - 1].plan) == 1) {
+        const bnn_op *pl = &c->ops[i - 1];
+        const uint32_t ob = (uint32_t)pl->b[1];
+        if (((uintptr_t)dv->buf[ob] & 15) == 0 && dv->ws[ob] % 4 == 0 && pl->p[7] % 4 == 0) {
+          o->qsel = 1;
+          dv->ops[i - 1].qnext = 1;
+          dv->fused_q++;
+        }
+      }
+      if (bnnk_gemm_plan_init(&o->plan, o->qsel ? dv->q2 : dv->q, r, o->kq, o->w, op->p[0], op->p[3])) {
         *kind = BNN_ERR_CPU;
         snprintf(err, errlen, "op %d %s: TMA descriptors could not be made (driver too old?)", i, op->kname);
         return -1;
@@ -1332,6 +1374,7 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
         CK(cudaMalloc((void **)&o->f[0], sizeof(float) * (size_t)B * o->pplan.nch * np), "prototype scratch");
     }
   }
+  c->launches_fused = dv->fused_q;
   CK(cudaDeviceSynchronize(), "device set-up");
   return 0;
 }
@@ -1360,6 +1403,7 @@ void bnn_rt_device_free(bnn_ctx *c, int di) {
     for (uint32_t i = 0; i < c->path->n_buf; i++) cudaFree(dv->priv[i]);
   cudaFree(dv->arena);
   cudaFree(dv->q); cudaFree(dv->sa); cudaFree(dv->za); cudaFree(dv->fe_minmax); cudaFree(dv->pcin); cudaFree(dv->err);
+  cudaFree(dv->q2); cudaFree(dv->sa2); cudaFree(dv->za2);
   cudaFree(dv->g16);
   if (dv->err_host) cudaFreeHost(dv->err_host);
   cudaFree(dv->up[0]); cudaFree(dv->up[1]);
@@ -1435,13 +1479,25 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
     case BNN_OP_PW_S8: {
       const int M = p[4];
       const float *gate = op->nb == 7 && op->b[6] >= 0 ? B_(6) : NULL;
+      int8_t *qq = o->qsel ? dv->q2 : dv->q;
+      float *qs = o->qsel ? dv->sa2 : dv->sa;
+      int32_t *qz = o->qsel ? dv->za2 : dv->za;
       if (!pre_q)
-        rc = bnnk_quant(n * M, M, IN_(0), INWS(0), p[5], p[1], o->kq, gate, gate ? WS(6) : 0, dv->q, dv->sa, dv->za, st);
+        rc = bnnk_quant(n * M, M, IN_(0), INWS(0), p[5], p[1], o->kq, gate, gate ? WS(6) : 0, qq, qs, qz, st);
       if (!rc) {
         const bnn_buf_rec *r = op->b[2] >= 0 ? &c->bufd[op->b[2]] : NULL;
         bnnk_epilogue e = {p[6], B_(1), WS(1), p[7], p[8], p[9], B_(2), WS(2), p[10],
-                           r && r->halo ? (int)r->W : 0, r && r->halo ? (int)r->halo : 0, o->sw, o->bias, o->cs};
-        rc = bnnk_gemm(&o->plan, n * M, M, dv->sa, dv->za, &e, dv->err, st);
+                           r && r->halo ? (int)r->W : 0, r && r->halo ? (int)r->halo : 0, o->sw, o->bias, o->cs,
+                           NULL, NULL, NULL, 0, 0};
+        if (o->qnext && i + 1 < op1) {  /* this GEMM quantizes its rows for the expand after it */
+          e.qo = dv->q2;
+          e.qsa = dv->sa2;
+          e.qza = dv->za2;
+          e.qk = c->ops[i + 1].p[1];
+          e.qkq = dv->ops[i + 1].kq;
+          next_q = 1;
+        }
+        rc = bnnk_gemm(&o->plan, n * M, M, qs, qz, &e, dv->err, st);
       }
       break;
     }
