@@ -106,6 +106,8 @@ SIGNATURES = {
     "bnn_proto_s8_free": (None, [_P]),
     "bnn_cuda_dw3": (_I, [_I, _P, _LL, _I, _I, _I, _I, _P, _P, _P, _LL, _I, _I, _P, _LL, _P]),
     "bnn_cuda_fn": (_I, [_I, _I, _P, _P, _P]),
+    "bnn_debug_fail_alloc": (_I, [_I, _I]),
+    "bnn_debug_stall_next_gemm": (None, []),
     "bnn_cuda_op_error": (_I, []),
 }
 

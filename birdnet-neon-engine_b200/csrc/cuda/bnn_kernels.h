@@ -46,6 +46,8 @@ int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_cap, int kq
 int bnnk_gemm_weight_rows(int np, int rows_cap);
 /* N tiles of the plan's GEMM (1: each tile holds whole rows, so its epilogue can quantize them for the next layer) */
 int bnnk_gemm_n_tiles(const bnnk_gemm_plan *p);
+/* test hook: the next GEMM launch in this process issues no loads and its waits give up after 200 us */
+void bnnk_debug_stall_next_gemm(void);
 
 /* epilogue of PW_S8 (gemm_s8n.c:105-135): y = (float)(acc - za * cs) * (sw * sa) + b, act (0 none, 1 SiLU,
  * 2 ReLU), + residual, stored at the padded row of each pixel (ow / opad) of each window */

@@ -262,6 +262,8 @@ struct GemmArgs {
   const int32_t *za;
   bnnk_epilogue e;
   int *err;
+  unsigned long long wait_ns;  // the limit of every mbarrier wait (kWaitNs; shorter in the stall test)
+  int stall;                   // test hook: the producer issues no load, so every consumer's wait runs out
 };
 
 __device__ __forceinline__ long long padded_row(int m, int w, int pad) {
@@ -460,13 +462,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
   const uint32_t tmem = tmem_base_s;
 
   if (warp == 0) {
-    if (lane == 0) {  // TMA producer
+    if (lane == 0 && !a.stall) {  // TMA producer
       int it = 0;
       for (int t = blockIdx.x; t < a.tiles && !abort_s; t += gridDim.x) {
         const int m0 = (t / a.n_tiles) * 128, n0 = (t % a.n_tiles) * a.bn;
         for (int kb = 0; kb < a.nkb; kb++, it++) {
           const int s = it % S;
-          if (it >= S && !mbar_wait(smem_u32(&bar_empty[s]), ((it / S) - 1) & 1)) {
+          if (it >= S && !mbar_wait_ns(smem_u32(&bar_empty[s]), ((it / S) - 1) & 1, a.wait_ns)) {
             atomicExch(a.err, BNNK_ERR_TMA_WAIT);
             abort_s = 1;
             break;
@@ -483,7 +485,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
       int it = 0, lt = 0;
       for (int t = blockIdx.x; t < a.tiles && !abort_s; t += gridDim.x, lt++) {
         const int g = lt % a.ne, use = lt / a.ne;
-        if (use > 0 && !mbar_wait(smem_u32(&bar_acc_empty[g]), (use - 1) & 1)) {
+        if (use > 0 && !mbar_wait_ns(smem_u32(&bar_acc_empty[g]), (use - 1) & 1, a.wait_ns)) {
           atomicExch(a.err, BNNK_ERR_MMA_WAIT);
           abort_s = 1;
           break;
@@ -493,7 +495,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
         bool ok = true;
         for (int kb = 0; kb < a.nkb; kb++, it++) {
           const int s = it % S;
-          if (!mbar_wait(smem_u32(&bar_full[s]), (it / S) & 1)) {
+          if (!mbar_wait_ns(smem_u32(&bar_full[s]), (it / S) & 1, a.wait_ns)) {
             atomicExch(a.err, BNNK_ERR_MMA_WAIT);
             abort_s = 1;
             ok = false;
@@ -529,7 +531,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
         sa = __ldg(a.sa + row);
         za = __ldg(a.za + row);
       }
-      bool ok = mbar_wait(smem_u32(&bar_acc_full[g]), use & 1);
+      bool ok = mbar_wait_ns(smem_u32(&bar_acc_full[g]), use & 1, a.wait_ns);
       ok = __all_sync(0xffffffffu, ok && !abort_s);  // one outcome per warp (abort_s may change between lanes' reads)
       if (!ok) {
         if (lane == 0) { atomicExch(a.err, BNNK_ERR_EPI_WAIT); abort_s = 1; }
@@ -833,10 +835,16 @@ static bool aligned32(const float *ptr, long long ws, int ld) {
   return ((uintptr_t)ptr & 31) == 0 && ws % 8 == 0 && ld % 8 == 0;
 }
 
+// test hook: the next GEMM launch of this process stalls (bnnk_debug_stall_next_gemm)
+static int g_stall_next = 0;
+extern "C" void bnnk_debug_stall_next_gemm(void) { __atomic_store_n(&g_stall_next, 1, __ATOMIC_RELAXED); }
+
 extern "C" int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float *sa, const int32_t *za,
                          const bnnk_epilogue *e, int *err, bnn_stream_t st) {
   if (rows <= 0) return 0;
   GemmArgs a;
+  a.stall = __atomic_exchange_n(&g_stall_next, 0, __ATOMIC_RELAXED);
+  a.wait_ns = a.stall ? 200000ull : kWaitNs;  // a stalled launch gives up after 200 us
   a.rows = rows;
   a.Mw = Mw;
   a.nkb = p->nkb;

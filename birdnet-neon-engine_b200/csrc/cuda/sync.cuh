@@ -37,14 +37,15 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 // bounded wait for the phase with the given parity to complete; false on timeout. The timer is read only once the
 // first try has failed: a phase that is already complete costs one try_wait.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_ns(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = gtimer();
   for (;;) {
     if (mbar_try(bar, parity)) return true;
-    if (gtimer() - t0 > kWaitNs) return false;
+    if (gtimer() - t0 > limit_ns) return false;
   }
 }
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) { return mbar_wait_ns(bar, parity, kWaitNs); }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(

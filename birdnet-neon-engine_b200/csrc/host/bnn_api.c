@@ -216,11 +216,30 @@ static int make_devices(bnn_ctx *c, int n_dev) {
   return 0;
 }
 
+/* allocation-failure injection: the k-th host / device allocation from now fails (0 = none) */
+static int g_fail_host, g_fail_dev;
+static int count_down(int *k) {
+  int v = __atomic_load_n(k, __ATOMIC_RELAXED);
+  while (v > 0)
+    if (__atomic_compare_exchange_n(k, &v, v - 1, 0, __ATOMIC_RELAXED, __ATOMIC_RELAXED)) return v == 1;
+  return 0;
+}
+int bnn_fail_host_alloc(void) { return count_down(&g_fail_host); }
+int bnn_fail_dev_alloc(void) { return count_down(&g_fail_dev); }
+int bnn_debug_fail_alloc(int host_k, int dev_k) {
+  if (host_k < 0 || dev_k < 0) { ERR(BNN_ERR_USAGE, "bnn_debug_fail_alloc: %d %d", host_k, dev_k); return -1; }
+  __atomic_store_n(&g_fail_host, host_k, __ATOMIC_RELAXED);
+  __atomic_store_n(&g_fail_dev, dev_k, __ATOMIC_RELAXED);
+  return 0;
+}
+
+void bnn_debug_stall_next_gemm(void) { bnnk_debug_stall_next_gemm(); }
+
 bnn_ctx *bnn_init(const char *path, int mode) {
   bnn_info pi;
   bnn_pkg *pkg = NULL;
   if (probe_full(path, &pi, &pkg)) return NULL;
-  bnn_ctx *c = calloc(1, sizeof *c);
+  bnn_ctx *c = bnn_fail_host_alloc() ? NULL : calloc(1, sizeof *c);
   if (!c) { bnn_pkg_close(pkg); ERR(BNN_ERR_OOM, "out of memory (%zu bytes for the context)", sizeof *c); return NULL; }
   c->pkg = pkg;
   c->info = pi;

@@ -184,6 +184,10 @@ int bnn_hpack_weights(bnn_devop *d, int dup, const uint16_t *panels, const float
 int bnn_logmel_build(bnn_devop *d, int nsamp, int frame, int hop, int pad, int nfft, int nmel, const float *window,
                      const float *mel, float floor_, float scale, char *err, size_t errlen, int *kind);
 void bnn_logmel_release(bnn_devop *d);
+/* allocation-failure injection for tests (bnn_debug_fail_alloc): 1 when this host / device allocation is to fail */
+int bnn_fail_host_alloc(void);
+int bnn_fail_dev_alloc(void);
+
 /* FE_DBIMG tables (fe_db_new, src/fe_dbimg.c:49-107) from the record's 21 ints and its tensors, and a scratch for
  * batch windows */
 int bnn_dbimg_build(bnn_devop *d, const int32_t *p, const float *window, const float *mel, const int32_t *rows,

@@ -597,7 +597,7 @@ int bnn_rt_open(bnn_ctx *c, char *err, size_t errlen, int *kind) {
   *kind = BNN_ERR_PACKAGE;
   const bnn_path_rec *d = c->path;
   const uint8_t *m = c->pkg->map;
-  c->bufd = malloc(sizeof(bnn_buf_rec) * d->n_buf);
+  c->bufd = bnn_fail_host_alloc() ? NULL : malloc(sizeof(bnn_buf_rec) * d->n_buf);
   c->ops = calloc(d->n_ops, sizeof(bnn_op));
   if (!c->bufd || !c->ops) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory (op list)"); return -1; }
   memcpy(c->bufd, m + d->buf_off, sizeof(bnn_buf_rec) * d->n_buf);
@@ -724,11 +724,17 @@ static int cerr(char *err, size_t errlen, int *kind, cudaError_t e, const char *
     if (e_ != cudaSuccess) return cerr(err, errlen, kind, e_, (what));  \
   } while (0)
 
+/* every device allocation of the runtime: cudaMalloc, unless the test hook (bnn_debug_fail_alloc) fails this one */
+static cudaError_t dmalloc(void **p, size_t bytes) {
+  if (bnn_fail_dev_alloc()) return cudaErrorMemoryAllocation;
+  return cudaMalloc(p, bytes);
+}
+
 static const void *tptr(const bnn_ctx *c, const bnn_op *op, int a) {
   return c->pkg->map + c->pkg->tensors[op->t[a]].offset;
 }
 static int upload(void **dst, const void *src, size_t bytes, char *err, size_t errlen, int *kind) {
-  CK(cudaMalloc(dst, bytes ? bytes : 16), "weight upload (cudaMalloc)");
+  CK(dmalloc(dst, bytes ? bytes : 16), "weight upload (cudaMalloc)");
   if (bytes) CK(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice), "weight upload (cudaMemcpy)");
   return 0;
 }
@@ -1083,7 +1089,7 @@ int bnn_dbimg_build(bnn_devop *d, const int32_t *p, const float *window, const f
   t->mel_off = (const int *)(g + off[11]); t->mel_k = (const int *)(g + off[12]); t->rows = (const int *)(g + off[13]);
   t->ry1 = (const int *)(g + off[14]); t->ry2 = (const int *)(g + off[15]); t->rx1 = (const int *)(g + off[16]);
   t->rx2 = (const int *)(g + off[17]);
-  CK(cudaMalloc((void **)&d->db_scratch, sizeof(float) * bnnk_dbimg_scratch_floats(t, batch)), "dB-image scratch");
+  CK(dmalloc((void **)&d->db_scratch, sizeof(float) * bnnk_dbimg_scratch_floats(t, batch)), "dB-image scratch");
   return 0;
 }
 void bnn_dbimg_release(bnn_devop *d) {
@@ -1264,7 +1270,7 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
   }
   size_t total = 0;
   for (uint32_t s = 0; s < d->n_buf; s++) { slot_off[s] = total; total += slot_bytes[s] * (size_t)B; }
-  cudaError_t e = cudaMalloc(&dv->arena, total ? total : 256);
+  cudaError_t e = dmalloc(&dv->arena, total ? total : 256);
   if (!e) e = cudaMemset(dv->arena, 0, total ? total : 256);
   if (e) { free(slot_bytes); free(slot_off); return cerr(err, errlen, kind, e, "activation arena"); }
   for (uint32_t i = 0; i < d->n_buf; i++) {
@@ -1272,11 +1278,11 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
     const size_t es = dsize(b->dtype);
     if (i == d->in_buf) {
       dv->ws[i] = (long long)b->elems;
-      e = cudaMalloc(&dv->priv[i], (size_t)b->elems * es * B + 256);
+      e = dmalloc(&dv->priv[i], (size_t)b->elems * es * B + 256);
       dv->buf[i] = dv->priv[i];
     } else if (b->halo) {
       dv->ws[i] = (long long)(((size_t)b->elems * es + 255) / 256 * 256 / es);
-      e = cudaMalloc(&dv->priv[i], (size_t)dv->ws[i] * es * B);
+      e = dmalloc(&dv->priv[i], (size_t)dv->ws[i] * es * B);
       if (!e) e = cudaMemset(dv->priv[i], 0, (size_t)dv->ws[i] * es * B);
       dv->buf[i] = dv->priv[i];
     } else if (!is_scratch(c, (int)i)) {
@@ -1315,23 +1321,23 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
         if (qb > qbytes2) qbytes2 = qb;
         if (r > rows2) rows2 = r;
       }
-  CK(cudaMalloc((void **)&dv->q, qbytes), "int8 row scratch");
+  CK(dmalloc((void **)&dv->q, qbytes), "int8 row scratch");
   CK(cudaMemset(dv->q, 0, qbytes), "int8 row scratch");
-  CK(cudaMalloc((void **)&dv->sa, sizeof(float) * rows), "int8 scale scratch");
-  CK(cudaMalloc((void **)&dv->za, sizeof(int32_t) * rows), "int8 zero-point scratch");
+  CK(dmalloc((void **)&dv->sa, sizeof(float) * rows), "int8 scale scratch");
+  CK(dmalloc((void **)&dv->za, sizeof(int32_t) * rows), "int8 zero-point scratch");
   if (qbytes2) {
-    CK(cudaMalloc((void **)&dv->q2, qbytes2), "int8 row scratch");
+    CK(dmalloc((void **)&dv->q2, qbytes2), "int8 row scratch");
     CK(cudaMemset(dv->q2, 0, qbytes2), "int8 row scratch");
-    CK(cudaMalloc((void **)&dv->sa2, sizeof(float) * rows2), "int8 scale scratch");
-    CK(cudaMalloc((void **)&dv->za2, sizeof(int32_t) * rows2), "int8 zero-point scratch");
+    CK(dmalloc((void **)&dv->sa2, sizeof(float) * rows2), "int8 scale scratch");
+    CK(dmalloc((void **)&dv->za2, sizeof(int32_t) * rows2), "int8 zero-point scratch");
   }
-  CK(cudaMalloc((void **)&dv->fe_minmax, sizeof(float) * 2 * B), "front-end scratch");
-  CK(cudaMalloc((void **)&dv->pcin, sizeof(float) * 6 * 1728 * B), "post-conv scratch");
+  CK(dmalloc((void **)&dv->fe_minmax, sizeof(float) * 2 * B), "front-end scratch");
+  CK(dmalloc((void **)&dv->pcin, sizeof(float) * 6 * 1728 * B), "post-conv scratch");
   size_t gate_elems = 8;
   for (int i = 0; i < c->n_ops; i++)
     if (c->ops[i].code == BNN_OP_SE_F16 && (size_t)B * c->ops[i].p[0] > gate_elems) gate_elems = (size_t)B * c->ops[i].p[0];
-  CK(cudaMalloc((void **)&dv->g16, sizeof(uint16_t) * gate_elems), "SE gate scratch");
-  CK(cudaMalloc((void **)&dv->err, 2 * sizeof(int)), "error word");
+  CK(dmalloc((void **)&dv->g16, sizeof(uint16_t) * gate_elems), "SE gate scratch");
+  CK(dmalloc((void **)&dv->err, 2 * sizeof(int)), "error word");
   CK(cudaMemset(dv->err, 0, sizeof(int)), "error word");
   CK(cudaMemset(dv->err + 1, 0x7f, sizeof(int)), "error word");
   CK(cudaMallocHost((void **)&dv->err_host, 2 * sizeof(int)), "error word (host)");
@@ -1371,7 +1377,7 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
         return -1;
       }
       if (!o->pplan.wt)
-        CK(cudaMalloc((void **)&o->f[0], sizeof(float) * (size_t)B * o->pplan.nch * np), "prototype scratch");
+        CK(dmalloc((void **)&o->f[0], sizeof(float) * (size_t)B * o->pplan.nch * np), "prototype scratch");
     }
   }
   c->launches_fused = dv->fused_q;

@@ -221,6 +221,15 @@ int bnn_cuda_stem_f16(int B, const float *d_img, long long iws, int H, int W, in
  * -1 if it cannot be read); synchronous */
 int bnn_cuda_op_error(void);
 
+/* Failure-path hooks for tests.
+ * bnn_debug_fail_alloc: the host_k-th host allocation and the dev_k-th device allocation the library makes from now
+ * on fail as if memory had run out (0 = none); the call that makes it fails with BNN_ERR_OOM and frees what it had.
+ * bnn_debug_stall_next_gemm: the next int8 GEMM launch in this process issues no TMA load and no MMA, and every wait
+ * of its warps gives up after 200 us (nothing is in flight when they do); the call that launched it fails with
+ * BNN_ERR_WINDOW ("a GPU kernel's bounded wait ran out") and the context stays usable. */
+int bnn_debug_fail_alloc(int host_k, int dev_k);
+void bnn_debug_stall_next_gemm(void);
+
 /* elementwise functions of the int8 path, for tests: 0 SiLU, 1 SiLU (table estimate), 2 sigmoid, 3 FRECPE,
  * 4 log2 polynomial, 5 exp2 polynomial (front end), 6 glibc expf, 7 SiLU on paired fp32 lanes (table estimate),
  * 8 fma(x, 1.7f, 0.3f) on paired fp32 lanes, 9 the dB-image front end's logarithm (double log rounded to float) */

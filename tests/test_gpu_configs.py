@@ -153,3 +153,21 @@ def test_largest_int8_layers_at_batch256(cuda, full_pkg):
         for i in (3, 4, 5):
             m.run_ops(pcm, i, i + 1)
             compare(m, i)
+
+
+def test_int8_pw_pairs_fused_quantizer(cuda, full_pkg, monkeypatch):
+    """BNN_PW_FUSE=1: the pwl GEMMs quantize their stored rows for the expand layer after them (13 quantizer launches
+    fewer per batch at batch 256); logits and embeddings stay bit-exact"""
+    B = 256
+    pcm = synth.audio(B, seed=1000)
+    idx = sample_windows(B, B, 12, seed=5)
+    want, wemb = oracle.run_many(full_pkg, np.ascontiguousarray(pcm[idx]), threads=min(CORES, len(idx)),
+                                 path_name=synth.PATH)
+    with Model(full_pkg, mode=4, batch=B) as m:
+        base = m.launches_per_batch
+    monkeypatch.setenv("BNN_PW_FUSE", "1")
+    with Model(full_pkg, mode=4, batch=B) as m:
+        assert m.launches_per_batch == base - 13, (base, m.launches_per_batch)
+        for call in range(2):
+            got, gemb = m.infer_batch(pcm)
+            check(got, gemb, want, wemb, idx, f"fused quantizer, call {call}")
