@@ -837,6 +837,29 @@ def write_dbimg_package(dst, fe, model_id="birdnet_v3_frontend_synthetic", halo=
     return n_out
 
 
+def pack_f32(w, b, kp):
+    """fp32 GEMM weights as the reference packs them (fp_pack, src/gemm_f32.c:22-34): panels [Np/8][Kp][8] (+ slack)
+    and the bias [Np + 8]; returns (panels, bias, (N, K, Kp, Np))"""
+    return _Int8Lowering.pack_f32(np.asarray(w, np.float32), np.asarray(b, np.float32), kp)
+
+
+def write_ops_package(dst, bufs, tensors, records, out_buf, emb_buf=None, model_id="op_test_synthetic",
+                      family=BNN_MODEL_BIRDNET_V3, sample_rate=V3_SAMPLE_RATE, nodes=None):
+    """A neon-int8 package of the given op records, for op-level tests: bufs [(dtype, H, W, C, ld, halo, elems)] with
+    buffer 0 the input window (n_samples = its elems: an op reads the window in the layout buffer 0 declares),
+    tensors [(name, array)], records [(code, bufs, tensors, ints)]; n_classes and emb_dim in the metadata are the
+    output and embedding buffers' elements. Returns (n_classes, emb_dim)."""
+    pinned = [out_buf] + ([emb_buf] if emb_buf is not None else [])
+    bplan = plan_slots(bufs, records, pinned)
+    n_out, n_emb = bufs[out_buf][6], bufs[emb_buf][6] if emb_buf is not None else 0
+    names = nodes or [f"op{i}" for i in range(len(records))]
+    meta = [(f"src_nodes/{PATH}", "\n".join(f"'{n}'" for n in names))] + metadata(
+        n_out, n_emb, labels_for(n_out), model_id=model_id, family=family, sample_rate=sample_rate,
+        n_samples=bufs[0][6], attribution="synthetic op test")
+    write_package(dst, meta, list(tensors), [(PATH, 0, bplan, records, 0, out_buf, emb_buf)])
+    return n_out, n_emb
+
+
 # ------------------------------------------------------------------ a Perch-v2-architecture model (neon-fp16 + int8 head)
 
 OPC_PERCH = dict(STEM=0x109, DWK=0x10a, PAD=0x10b, MEAN=0x10c, PROTO_F16S8=0x20d)

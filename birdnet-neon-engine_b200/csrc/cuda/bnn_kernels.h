@@ -144,6 +144,46 @@ typedef struct {
 int bnnk_logmel(int B, const float *pcm, long long pws, const bnnk_logmel_tables *t, float *spec, long long sws,
                 bnn_stream_t st);
 
+/* ---- the fp32 ops beyond v2.4 (k_v3.cu): v3.0's CONVK, CONVW, GEM, SED, VADD (src/rt_ops_f32x.c) and Perch's fp32
+ * body ops STEM, DWK, PAD, MEAN (src/rt_ops_f32.c); per-window strides in floats */
+typedef struct {
+  int N, K, Kp, Np;
+  const float *w; /* [Np/8][Kp][8] */
+  const float *b; /* [Np] */
+} bnnk_fpack;
+typedef struct {
+  int red, H, W, C, ld, L, pk, dk, hc, Cp;
+  const float *x;
+  long long xws;
+  const float *dw, *db, *consts;
+  bnnk_fpack fc, at, cl;
+  float *out, *s, *pl, *h, *att, *cla;
+  long long ows, sws, pws, hws, aws, clws;
+} bnnk_sed_args;
+int bnnk_v3_tables_init(const unsigned long long *tab, const uint32_t *lut);
+int bnnk_vadd(int B, int n, const float *a, long long aws, const float *b, long long bws, float *o, long long ows,
+              bnn_stream_t st);
+int bnnk_gem(int B, int P, int C, int ld, const float *x, long long xws, const float *consts, float *out,
+             long long ows, bnn_stream_t st);
+int bnnk_mean_f32(int B, int P, int C, int ld, const float *x, long long xws, float *out, long long ows,
+                  bnn_stream_t st);
+int bnnk_pad_f32(int B, int H, int W, int C, int ld, int h, const float *x, long long xws, float *xp, long long pws,
+                 bnn_stream_t st);
+int bnnk_dwk_f32(int B, const float *xp, long long xws, int H, int W, int C, int k, int s, int pt, int pl,
+                 const float *w, const float *b, int act, float *out, long long ows, int Ho, int Wo, float *chsum,
+                 long long cws, bnn_stream_t st);
+int bnnk_stem_f32(int B, const float *img, long long iws, int W, int k, int s, int Ho, int Wo, const float *w,
+                  const float *bias, int Kp, int Np, int act, float *out, long long ows, int ldo, int opad, float *col,
+                  long long cws, bnn_stream_t st);
+int bnnk_convk(int B, const float *x, long long xws, int H, int W, int h, int ld, int Ho, int Wo, int kh, int kw, int s,
+               int oy0, int ox0, const float *w, const float *bias, int Kp, int Np, int act, float *out, long long ows,
+               int ldo, int opad, const float *res, long long rws, int ldr, int rh, bnn_stream_t st);
+size_t bnnk_convw_scratch_floats(int H, int W, int C, int Np); /* per window */
+int bnnk_convw(int B, const float *x, long long xws, int H, int W, int h, int C, const float *U, const float *bias,
+               int Np, int act, float *out, long long ows, int ldo, int opad, const float *res, long long rws, int rh,
+               int rld, float *scratch, bnn_stream_t st);
+int bnnk_sed(int B, const bnnk_sed_args *a, bnn_stream_t st);
+
 /* ---- the dB-image front end (FE_DBIMG): pcm [B][nsamp] -> image [B][(Ho + 2 halo)(Wo + 2 halo)][ld]. Device tables:
  * window [nfft], twiddles [nfft / 4], real-split factors [nfft / 2 + 1], the sparse mel (row offsets [nmel + 1], bins
  * and weights of the nonzero entries), rows [R], channel values [2][C], the resize coordinates [Ho], [Wo]; the scratch

@@ -641,6 +641,7 @@ extern "C" int bnnk_device_init(void) {
   e = cudaMemcpyToSymbol(g_frecpe_lut, lut, sizeof lut);
   if (e) return e;
   e = (cudaError_t)bnnk_fp32_tables_init(tab, lut);
+  if (!e) e = (cudaError_t)bnnk_v3_tables_init(tab, lut);
   return e ? e : bnnk_f16_tables_init(tab);
 }
 

@@ -56,7 +56,8 @@ static int path_runs_here(const bnn_pkg *p, int i) {
                               BNN_OP_POSTPC, BNN_OP_GEMV_S8, BNN_OP_PROTO_S8, BNN_OP_FE_LOGMEL, BNN_OP_FE_DBIMG, BNN_OP_DENSE,
                               BNN_OP_C0POOL_F16, BNN_OP_PW_F16, BNN_OP_DW3_F16, BNN_OP_SE_F16, BNN_OP_POSTPC_F16,
                               BNN_OP_DENSE_F16, BNN_OP_STEM_F16, BNN_OP_DWK_F16, BNN_OP_PAD_F16, BNN_OP_MEAN_F16,
-                              BNN_OP_PROTO_F16S8};
+                              BNN_OP_PROTO_F16S8, BNN_OP_STEM, BNN_OP_DWK, BNN_OP_PAD, BNN_OP_MEAN, BNN_OP_CONVK,
+                              BNN_OP_GEM, BNN_OP_SED, BNN_OP_VADD, BNN_OP_CONVW};
   const bnn_path_rec *d = &p->paths[i];
   const uint8_t *q = p->map + d->ops_off, *end = q + d->ops_bytes;
   for (uint32_t k = 0; k < d->n_ops; k++) {
@@ -800,7 +801,8 @@ int bnn_pw_s8_run(bnn_pw_s8 *o, int B, int Mw, const float *d_x, long long xws, 
   const int rows = B * Mw;
   int e = bnnk_quant(rows, Mw, d_x, xws, lda, o->K, o->op.kq, d_gate, gws, o->q, o->sa, o->za, st);
   if (!e) {
-    bnnk_epilogue ep = {act, d_out, ows, ldo, ow, opad, d_res, rws, ldr, rw, rpad, o->op.sw, o->op.bias, o->op.cs};
+    bnnk_epilogue ep = {act, d_out, ows, ldo, ow, opad, d_res, rws, ldr, rw, rpad, o->op.sw, o->op.bias, o->op.cs,
+                      NULL, NULL, NULL, 0, 0};
     e = bnnk_gemm(&o->op.plan, rows, Mw, o->sa, o->za, &ep, o->err, st);
   }
   return launch_rc("bnn_pw_s8_run", e);
@@ -825,7 +827,8 @@ int bnn_pw_s8_run_static(bnn_pw_s8 *o, int B, int Mw, const float *d_x, long lon
         BNN_PW_S8_STATIC_MAX_QBYTES);
     return -1;
   }
-  bnnk_epilogue ep = {act, d_out, ows, ldo, ow, opad, d_res, rws, ldr, rw, rpad, o->op.sw, o->op.bias, o->op.cs};
+  bnnk_epilogue ep = {act, d_out, ows, ldo, ow, opad, d_res, rws, ldr, rw, rpad, o->op.sw, o->op.bias, o->op.cs,
+                      NULL, NULL, NULL, 0, 0};
   return launch_rc("bnn_pw_s8_run_static", bnnk_pw_s8_static(&o->op.plan, (int)rows, Mw, d_x, xws, lda, o->K, d_gate,
                                                              gws, &ep, o->err, (bnn_stream_t)stream));
 }
@@ -840,7 +843,8 @@ int bnn_pw_s8_gemm(bnn_pw_s8 *o, int B, int Mw, const int8_t *d_q, long long ldq
         "act %d ow %d opad %d", B, Mw, ldq, o ? o->Kp : 0, ldo, act, ow, opad);
     return -1;
   }
-  bnnk_epilogue ep = {act, d_out, ows, ldo, ow, opad, d_res, rws, ldr, rw, rpad, o->op.sw, o->op.bias, o->op.cs};
+  bnnk_epilogue ep = {act, d_out, ows, ldo, ow, opad, d_res, rws, ldr, rw, rpad, o->op.sw, o->op.bias, o->op.cs,
+                      NULL, NULL, NULL, 0, 0};
   return launch_rc("bnn_pw_s8_gemm", bnnk_gemm_q(&o->op.plan, d_q, ldq, o->Kp, B * Mw, Mw, d_sa, d_za, &ep, o->err,
                                                  (bnn_stream_t)stream));
 }

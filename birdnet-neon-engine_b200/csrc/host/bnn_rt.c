@@ -527,6 +527,151 @@ static int init_mean(vctx *v) { /* rt_mean_check, src/rt_ops_f32.c:501-513 (mean
   if (x->halo) return vbad(v, "buffer argument 0 (buffer #%d, input): expected no halo, found halo %u", v->op->b[0], x->halo);
   return vneed(v, 0, (int)x->dtype, (size_t)p[0] * p[2]) || vneed(v, 1, BNN_F32, (size_t)p[1]) ? -1 : 0;
 }
+/* ---- fp32 bodies beyond v2.4: Perch's STEM / DWK (src/rt_ops_f32.c:387-472) and v3.0's CONVK, GEM, SED, VADD,
+ * CONVW (src/rt_ops_f32x.c:88-436); the same checks in the same order, with the reference's messages */
+
+static int init_stem_f32(vctx *v) { /* stem_init + rt_stem_f32_check, src/rt_ops_f32.c:390-415 */
+  if (vneed_args(v, 3, -1, -1) || vneed_args(v, -1, 2, 13) || v_fpack(v, 0, 0)) return -1;
+  const int *p = v->op->p;
+  const int K = p[1], Kp = p[2], Np = p[3], H = p[4], W = p[5], Ho = p[6], Wo = p[7], k = p[8], s = p[9];
+  const int ldo = p[11], h = p[12];
+  VREQ(v, k >= 1 && s >= 1 && Ho > 0 && Wo > 0);
+  VREQ(v, (Ho - 1) * s + k <= H && (Wo - 1) * s + k <= W); /* VALID conv */
+  VREQ(v, K == k * k);
+  VREQ(v, ldo >= Np);
+  VREQ(v, h >= 0 && h <= 3);
+  VREQ(v, p[10] >= 0 && p[10] <= 2);
+  if (vneed(v, 0, BNN_F32, (size_t)H * W) || vneed(v, 2, BNN_F32, (size_t)R8(Ho * Wo) * Kp)) return -1;
+  const bnn_buf_rec *o = vbd(v, 1);
+  if (!o) return vbad(v, "buffer argument 1 (output) is absent");
+  if (o->halo != (uint32_t)h || o->ld != (uint32_t)ldo || (h && (o->W != (uint32_t)Wo || o->H != (uint32_t)Ho)))
+    return vbad(v, "buffer argument 1 (buffer #%d, output): expected %d x %d, halo %d, ld %d; found %u x %u, halo %u, ld %u",
+                v->op->b[1], Ho, Wo, h, ldo, o->H, o->W, o->halo, o->ld);
+  if (vneed(v, 1, (int)o->dtype, (size_t)(Ho + 2 * h) * (Wo + 2 * h) * ldo) || vneed(v, 1, BNN_F32, 1)) return -1;
+  if (h) v->c->launches += 1; /* the zero halo */
+  return 0;
+}
+static int init_dwk_f32(vctx *v) { /* dwk_init = rt_dwk_check(4), src/rt_ops_f32.c:435-453 */
+  if (vneed_args(v, 3, 2, 10)) return -1;
+  const int *p = v->op->p;
+  const int H = p[0], W = p[1], C = p[2], k = p[3], s = p[4], pt = p[5], pl = p[6], Ho = p[7], Wo = p[8];
+  const int h = (k - 1) / 2;
+  VREQ(v, H > 0 && W > 0 && Ho > 0 && Wo > 0 && C > 0);
+  VREQ(v, C % 8 == 0);
+  VREQ(v, k % 2 == 1 && k >= 1 && k <= 7);
+  VREQ(v, s >= 1 && s <= 2);
+  VREQ(v, pt >= 0 && pt <= h && pl >= 0 && pl <= h);
+  VREQ(v, p[9] >= 0 && p[9] <= 1);
+  if (vneed_t(v, 0, (size_t)k * k * C * 4, 0) || vneed_t(v, 1, (size_t)C * 4, 0)) return -1;
+  VREQ(v, (Ho - 1) * s - pt + k <= H + 2 * h - h);
+  VREQ(v, (Wo - 1) * s - pl + k <= W + 2 * h - h);
+  if (vneed_haloed(v, 0, BNN_F32, H, W, C, h)) return -1;
+  return vneed(v, 1, BNN_F32, (size_t)Ho * Wo * C) || vneed(v, 2, BNN_F32, (size_t)C) ? -1 : 0;
+}
+static int init_pad_f32(vctx *v) { /* rt_pad_check; the run zeroes the halo and copies */
+  return init_pad(v);
+}
+static int init_convk(vctx *v) { /* convk_init, src/rt_ops_f32x.c:91-129 */
+  if (vneed_args(v, 3, 2, 16) || v_fpack(v, 0, 0)) return -1;
+  const int *p = v->op->p;
+  const int K = p[1], Kp = p[2], Np = p[3], H = p[4], W = p[5], Ho = p[6], Wo = p[7], kh = p[8], kw = p[9], st = p[10];
+  const int oy0 = p[11], ox0 = p[12], act = p[13], ldo = p[14], opad = p[15];
+  VREQ(v, H > 0 && W > 0 && Ho > 0 && Wo > 0 && kh >= 1 && kh <= 7 && kw >= 1 && kw <= 7 && st >= 1 && st <= 2);
+  VREQ(v, act >= 0 && act <= 2 && opad >= 0 && opad <= 3 && oy0 >= 0 && ox0 >= 0);
+  const bnn_buf_rec *x = vbd(v, 0), *o = vbd(v, 1);
+  if (!x || !o) return vbad(v, "buffer argument %d is absent", x ? 1 : 0);
+  const int h = (int)x->halo, ld = (int)x->ld, Wp = W + 2 * h;
+  if (x->dtype != BNN_F32 || x->H != (uint32_t)H || x->W != (uint32_t)W || ld % 4)
+    return vbad(v, "buffer argument 0 (buffer #%d, input): expected fp32 %d x %d with ld a multiple of 4, found %s %u x %u ld %u",
+                v->op->b[0], H, W, bnn_dtype_name(x->dtype), x->H, x->W, x->ld);
+  VREQ(v, K == kh * kw * ld && Kp == K);
+  VREQ(v, oy0 + (Ho - 1) * st + kh <= H + 2 * h && ox0 + (Wo - 1) * st + kw <= W + 2 * h);
+  const size_t last = ((size_t)(oy0 + (Ho - 1) * st + kh - 1) * Wp + ox0 + (size_t)(((Wo + 7) & ~7) - 1) * st + kw) * ld + 4;
+  if (vneed(v, 0, BNN_F32, last)) return -1;
+  if (o->dtype != BNN_F32 || o->H != (uint32_t)Ho || o->W != (uint32_t)Wo || o->ld != (uint32_t)ldo ||
+      o->halo != (uint32_t)opad || ldo < Np)
+    return vbad(v, "buffer argument 1 (buffer #%d, output): expected fp32 %d x %d ld %d (>= %d) halo %d, found %s %u x %u ld %u halo %u",
+                v->op->b[1], Ho, Wo, ldo, Np, opad, bnn_dtype_name(o->dtype), o->H, o->W, o->ld, o->halo);
+  if (vneed(v, 1, BNN_F32, (size_t)(Ho + 2 * opad) * (Wo + 2 * opad) * ldo)) return -1;
+  const bnn_buf_rec *r = vbd(v, 2);
+  if (r) {
+    if (r->dtype != BNN_F32 || r->H != (uint32_t)Ho || r->W != (uint32_t)Wo || r->ld < (uint32_t)Np)
+      return vbad(v, "buffer argument 2 (buffer #%d, residual): expected fp32 %d x %d with ld >= %d, found %s %u x %u ld %u",
+                  v->op->b[2], Ho, Wo, Np, bnn_dtype_name(r->dtype), r->H, r->W, r->ld);
+    if (vneed(v, 2, BNN_F32, (size_t)(Ho + 2 * r->halo) * (Wo + 2 * r->halo) * r->ld)) return -1;
+  }
+  if (opad) v->c->launches += 1; /* the zero halo */
+  return 0;
+}
+static int init_gem(vctx *v) { /* gem_init, src/rt_ops_f32x.c:168-176 */
+  if (vneed_args(v, 2, 1, 3)) return -1;
+  const int P = v->op->p[0], C = v->op->p[1], ld = v->op->p[2];
+  VREQ(v, P > 0 && C > 0 && C % 4 == 0 && ld >= C);
+  if (vneed_t(v, 0, 12, 0)) return -1;
+  const float *k = vt(v, 0, NULL);
+  VREQ(v, k[0] > 0.f && k[1] > 0.f);
+  return vneed_nohalo(v, 0, BNN_F32, (size_t)P * ld) || vneed(v, 1, BNN_F32, (size_t)C) ? -1 : 0;
+}
+static int init_vadd(vctx *v) { /* vadd_init, src/rt_ops_f32x.c:352-357 */
+  if (vneed_args(v, 3, 0, 1)) return -1;
+  VREQ(v, v->op->p[0] > 0);
+  const size_t n = (size_t)v->op->p[0];
+  return vneed(v, 0, BNN_F32, n) || vneed(v, 1, BNN_F32, n) || vneed(v, 2, BNN_F32, n) ? -1 : 0;
+}
+static int init_sed(vctx *v) { /* sed_init + rt_sed_geom, src/rt_ops_f32x.c:207-248 */
+  if (vneed_args(v, 7, 9, 21) || v_fpack(v, 2, 0) || v_fpack(v, 4, 4) || v_fpack(v, 6, 8)) return -1;
+  const int *p = v->op->p;
+  const int fcN = p[0], fcK = p[1], fcKp = p[2], fcNp = p[3], atN = p[4], atK = p[5], atKp = p[6], atNp = p[7];
+  const int clN = p[8], clK = p[9], clKp = p[10], clNp = p[11];
+  const int red = p[12], H = p[13], W = p[14], C = p[15], ld = p[16], L = p[17], pk = p[18], dk = p[19], hc = p[20];
+  const int L8 = (L + 7) & ~7, Cp = fcKp;
+  VREQ(v, fcKp % 8 == 0 && atKp == fcNp && clKp == fcNp);
+  VREQ(v, red == 2 || red == 3);
+  VREQ(v, H > 0 && W > 0 && C > 0 && C % 4 == 0 && ld >= C && L == (red == 3 ? H : W));
+  VREQ(v, pk >= 0 && pk <= 15 && (pk == 0 || pk % 2) && dk >= 0 && dk <= 15 && (dk == 0 || dk % 2) && (pk || dk));
+  VREQ(v, hc == 0 || hc == 1);
+  VREQ(v, L <= 64);
+  VREQ(v, fcK == C && atK == fcN && clK == fcN && atN == clN);
+  if (vneed_t(v, 0, (size_t)(dk ? dk : 1) * C * 4, 0) || vneed_t(v, 1, (size_t)C * 4, 0) || vneed_t(v, 8, 12, 0))
+    return -1;
+  const bnn_buf_rec *x = vbd(v, 0);
+  if (!x || x->halo || x->dtype != BNN_F32 || x->H != (uint32_t)H || x->W != (uint32_t)W)
+    return vbad(v, "buffer argument 0: expected an unpadded fp32 activation %d x %d", H, W);
+  return vneed(v, 0, BNN_F32, (size_t)H * W * ld) || vneed(v, 1, BNN_F32, (size_t)atN) ||
+                 vneed(v, 2, BNN_F32, (size_t)L8 * Cp) || vneed(v, 3, BNN_F32, (size_t)L8 * Cp) ||
+                 vneed(v, 4, BNN_F32, (size_t)L8 * fcNp) || vneed(v, 5, BNN_F32, (size_t)L8 * atNp) ||
+                 vneed(v, 6, BNN_F32, (size_t)L8 * clNp)
+             ? -1
+             : 0;
+}
+static int init_convw(vctx *v) { /* convw_init, src/rt_ops_f32x.c:370-412 */
+  if (vneed_args(v, 3, 2, 10)) return -1;
+  const int *p = v->op->p;
+  const int C = p[0], N = p[1], Np = p[2], H = p[3], W = p[4], act = p[5], ldo = p[6], opad = p[7], S = p[8], Nb = p[9];
+  VREQ(v, C > 0 && C % 4 == 0 && N > 0 && Np == ((N + 7) & ~7) && H > 0 && W > 0);
+  VREQ(v, act >= 0 && act <= 2 && opad >= 0 && opad <= 3 && ldo >= Np);
+  VREQ(v, S >= 1 && S <= 256 && Nb >= 8 && Nb % 8 == 0);
+  const bnn_buf_rec *x = vbd(v, 0), *o = vbd(v, 1);
+  if (!x || !o) return vbad(v, "buffer argument %d is absent", x ? 1 : 0);
+  if (x->dtype != BNN_F32 || x->H != (uint32_t)H || x->W != (uint32_t)W || x->ld != (uint32_t)C || x->halo < 1)
+    return vbad(v, "buffer argument 0 (buffer #%d, input): expected fp32 %d x %d ld %d with a halo, found %s %u x %u ld %u halo %u",
+                v->op->b[0], H, W, C, bnn_dtype_name(x->dtype), x->H, x->W, x->ld, x->halo);
+  const int h = (int)x->halo;
+  if (vneed(v, 0, BNN_F32, (size_t)(H + 2 * h) * (W + 2 * h) * C)) return -1;
+  if (o->dtype != BNN_F32 || o->H != (uint32_t)H || o->W != (uint32_t)W || o->ld != (uint32_t)ldo || o->halo != (uint32_t)opad)
+    return vbad(v, "buffer argument 1 (buffer #%d, output): expected fp32 %d x %d ld %d halo %d", v->op->b[1], H, W, ldo, opad);
+  if (vneed(v, 1, BNN_F32, (size_t)(H + 2 * opad) * (W + 2 * opad) * ldo)) return -1;
+  if (vneed_t(v, 0, (size_t)36 * Np * C * 4, 1) || vneed_t(v, 1, (size_t)Np * 4, 1)) return -1;
+  const bnn_buf_rec *r = vbd(v, 2);
+  if (r) {
+    if (r->dtype != BNN_F32 || r->H != (uint32_t)H || r->W != (uint32_t)W || r->ld < (uint32_t)Np)
+      return vbad(v, "buffer argument 2 (buffer #%d, residual): expected fp32 %d x %d with ld >= %d", v->op->b[2], H, W, Np);
+    if (vneed(v, 2, BNN_F32, (size_t)(H + 2 * r->halo) * (W + 2 * r->halo) * r->ld)) return -1;
+  }
+  if (opad) v->c->launches += 1; /* the zero halo */
+  return 0;
+}
+
 static int init_proto_f16s8(vctx *v) { /* proto8_init (src/rt_ops_f16.c:254-267) after rt_proto_geom / rt_proto_io
                                         * (src/rt_ops_f32.c:525-545) */
   if (vneed_args(v, 4, 5, 8)) return -1;
@@ -581,6 +726,15 @@ static const kdesc KERNELS[] = {
     {BNN_OP_PAD_F16, "pad_f16", init_pad, 0x2, 0, 1},
     {BNN_OP_MEAN_F16, "mean_f16", init_mean, 0x2, 0, 1},
     {BNN_OP_PROTO_F16S8, "proto_s8", init_proto_f16s8, 0xe, 0, 3},
+    {BNN_OP_STEM, "stem_f32", init_stem_f32, 0x6, 0, 2},
+    {BNN_OP_DWK, "dwk_f32", init_dwk_f32, 0x6, 0, 1},
+    {BNN_OP_PAD, "pad_f32", init_pad_f32, 0x2, 0, 2},
+    {BNN_OP_MEAN, "mean_f32", init_mean, 0x2, 0, 1},
+    {BNN_OP_CONVK, "convk_f32", init_convk, 0x2, 0x4, 1},
+    {BNN_OP_GEM, "gem_f32", init_gem, 0x2, 0, 1},
+    {BNN_OP_SED, "sed_f32", init_sed, 0x7e, 0, 5},
+    {BNN_OP_VADD, "vadd_f32", init_vadd, 0x4, 0, 1},
+    {BNN_OP_CONVW, "convw_f32", init_convw, 0x2, 0x4, 3},
 };
 static const kdesc *kernel_for(int code) {
   for (size_t i = 0; i < sizeof KERNELS / sizeof KERNELS[0]; i++)
@@ -1204,6 +1358,34 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
   case BNN_OP_STEM_F16: /* t = [w panels [Np/8][Kp][8], b [Np]] fp32, used as they are */
     return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * (size_t)p[3] * p[2], err, errlen, kind) ||
            upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * (size_t)p[3], err, errlen, kind);
+  case BNN_OP_STEM:  /* t = [w panels [Np/8][Kp][8], b [Np]] */
+  case BNN_OP_CONVK:
+    return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * (size_t)p[3] * p[2], err, errlen, kind) ||
+           upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * (size_t)p[3], err, errlen, kind);
+  case BNN_OP_DWK: {
+    const int C = p[2], k = p[3];
+    return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * (size_t)k * k * C, err, errlen, kind) ||
+           upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * C, err, errlen, kind);
+  }
+  case BNN_OP_GEM:
+    return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * 3, err, errlen, kind);
+  case BNN_OP_SED: { /* t = [dw, db, fc w b, att w b, cla w b, consts]; p = [fc, att, cla shapes, red H W C ld L pk dk hc] */
+    const int C = p[15], dk = p[19];
+    const size_t sz[9] = {(size_t)(dk ? dk : 1) * C, (size_t)C, (size_t)p[3] * p[2], (size_t)p[3], (size_t)p[7] * p[6],
+                          (size_t)p[7], (size_t)p[11] * p[10], (size_t)p[11], 3};
+    for (int i = 0; i < 9; i++)
+      if (upload((void **)&d->f[i], tptr(c, op, i), sizeof(float) * sz[i], err, errlen, kind)) return -1;
+    return 0;
+  }
+  case BNN_OP_CONVW: { /* t = [U [36][Np/8][C][8], bias [Np]]; the transform scratch of the batch */
+    const int C = p[0], Np = p[2], H = p[3], W = p[4];
+    if (upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * 36 * (size_t)Np * C, err, errlen, kind) ||
+        upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * (size_t)Np, err, errlen, kind))
+      return -1;
+    CK(dmalloc((void **)&d->f[2], sizeof(float) * bnnk_convw_scratch_floats(H, W, C, Np) * (size_t)c->batch),
+       "Winograd scratch");
+    return 0;
+  }
   case BNN_OP_DWK_F16: {
     const int C = p[2], k = p[3];
     return upload((void **)&d->hw, tptr(c, op, 0), sizeof(uint16_t) * (size_t)k * k * C, err, errlen, kind) ||
@@ -1394,7 +1576,7 @@ void bnn_rt_device_free(bnn_ctx *c, int di) {
     for (int i = 0; i < c->n_ops; i++) {
       bnn_devop *o = &dv->ops[i];
       cudaFree(o->w); cudaFree(o->sw); cudaFree(o->bias); cudaFree(o->cs);
-      for (int k = 0; k < 6; k++) cudaFree(o->f[k]);
+      for (int k = 0; k < 10; k++) cudaFree(o->f[k]);
       cudaFree(o->hw); cudaFree(o->hb); cudaFree(o->hwd);
       bnn_logmel_release(o);
       bnn_dbimg_release(o);
@@ -1510,7 +1692,7 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
     case BNN_OP_GEMV_S8: {
       rc = bnnk_quant(n, 1, IN_(0), INWS(0), p[1], p[1], o->kq, NULL, 0, dv->q, dv->sa, dv->za, st);
       if (!rc) {
-        bnnk_epilogue e = {p[4], B_(1), WS(1), p[3], 0, 0, NULL, 0, 0, 0, 0, o->sw, o->bias, o->cs};
+        bnnk_epilogue e = {p[4], B_(1), WS(1), p[3], 0, 0, NULL, 0, 0, 0, 0, o->sw, o->bias, o->cs, NULL, NULL, NULL, 0, 0};
         rc = bnnk_gemm(&o->plan, n, 1, dv->sa, dv->za, &e, dv->err, st);
       }
       break;
@@ -1565,6 +1747,49 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
     case BNN_OP_DENSE:
       rc = bnnk_dense_f32(n, p[0], B_(0), WS(0), o->f[0], o->f[1], B_(1), WS(1), st);
       break;
+    case BNN_OP_STEM:
+      rc = bnnk_stem_f32(n, IN_(0), INWS(0), p[5], p[8], p[9], p[6], p[7], o->f[0], o->f[1], p[2], p[3], p[10], B_(1),
+                         WS(1), p[11], p[12], B_(2), WS(2), st);
+      break;
+    case BNN_OP_DWK:
+      rc = bnnk_dwk_f32(n, IN_(0), INWS(0), p[0], p[1], p[2], p[3], p[4], p[5], p[6], o->f[0], o->f[1], p[9], B_(1),
+                        WS(1), p[7], p[8], B_(2), WS(2), st);
+      break;
+    case BNN_OP_PAD:
+      rc = bnnk_pad_f32(n, p[0], p[1], p[2], p[3], p[4], IN_(0), INWS(0), B_(1), WS(1), st);
+      break;
+    case BNN_OP_MEAN:
+      rc = bnnk_mean_f32(n, p[0], p[1], p[2], IN_(0), INWS(0), B_(1), WS(1), st);
+      break;
+    case BNN_OP_CONVK: {
+      const bnn_buf_rec *x = &c->bufd[op->b[0]], *r = op->b[2] >= 0 ? &c->bufd[op->b[2]] : NULL;
+      rc = bnnk_convk(n, IN_(0), INWS(0), p[4], p[5], (int)x->halo, (int)x->ld, p[6], p[7], p[8], p[9], p[10], p[11],
+                      p[12], o->f[0], o->f[1], p[2], p[3], p[13], B_(1), WS(1), p[14], p[15], r ? IN_(2) : NULL,
+                      r ? INWS(2) : 0, r ? (int)r->ld : 0, r ? (int)r->halo : 0, st);
+      break;
+    }
+    case BNN_OP_GEM:
+      rc = bnnk_gem(n, p[0], p[1], p[2], IN_(0), INWS(0), o->f[0], B_(1), WS(1), st);
+      break;
+    case BNN_OP_VADD:
+      rc = bnnk_vadd(n, p[0], IN_(0), INWS(0), IN_(1), INWS(1), B_(2), WS(2), st);
+      break;
+    case BNN_OP_SED: {
+      bnnk_sed_args a = {p[12], p[13], p[14], p[15], p[16], p[17], p[18], p[19], p[20], p[2], IN_(0), INWS(0),
+                         o->f[0], o->f[1], o->f[8],
+                         {p[0], p[1], p[2], p[3], o->f[2], o->f[3]}, {p[4], p[5], p[6], p[7], o->f[4], o->f[5]},
+                         {p[8], p[9], p[10], p[11], o->f[6], o->f[7]},
+                         B_(1), B_(2), B_(3), B_(4), B_(5), B_(6), WS(1), WS(2), WS(3), WS(4), WS(5), WS(6)};
+      rc = bnnk_sed(n, &a, st);
+      break;
+    }
+    case BNN_OP_CONVW: {
+      const bnn_buf_rec *x = &c->bufd[op->b[0]], *r = op->b[2] >= 0 ? &c->bufd[op->b[2]] : NULL;
+      rc = bnnk_convw(n, IN_(0), INWS(0), p[3], p[4], (int)x->halo, p[0], o->f[0], o->f[1], p[2], p[5], B_(1), WS(1),
+                      p[6], p[7], r ? IN_(2) : NULL, r ? INWS(2) : 0, r ? (int)r->halo : 0, r ? (int)r->ld : 0, o->f[2],
+                      st);
+      break;
+    }
     case BNN_OP_STEM_F16:
       rc = bnnk_stem_f16(n, B_(0), WS(0), p[5], p[8], p[9], p[6], p[7], o->f[0], o->f[1], p[0], p[2], p[3], p[10],
                          B_(1), WS(1), p[11], p[12], st);
