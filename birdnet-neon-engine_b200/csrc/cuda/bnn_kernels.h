@@ -183,6 +183,9 @@ int bnnk_convw(int B, const float *x, long long xws, int H, int W, int h, int C,
                int Np, int act, float *out, long long ows, int ldo, int opad, const float *res, long long rws, int rh,
                int rld, float *scratch, bnn_stream_t st);
 int bnnk_sed(int B, const bnnk_sed_args *a, bnn_stream_t st);
+/* SED's first and last stages alone (SED_S8 runs its GEMMs on the int8 path between them) */
+int bnnk_sed_pool(int B, const bnnk_sed_args *a, bnn_stream_t st);
+int bnnk_sed_out(int B, const bnnk_sed_args *a, bnn_stream_t st);
 
 /* ---- the dB-image front end (FE_DBIMG): pcm [B][nsamp] -> image [B][(Ho + 2 halo)(Wo + 2 halo)][ld]. Device tables:
  * window [nfft], twiddles [nfft / 4], real-split factors [nfft / 2 + 1], the sparse mel (row offsets [nmel + 1], bins

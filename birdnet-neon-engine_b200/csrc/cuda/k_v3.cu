@@ -576,12 +576,24 @@ extern "C" int bnnk_convw(int B, const float *x, long long xws, int H, int W, in
   return cudaGetLastError();
 }
 
-extern "C" int bnnk_sed(int B, const bnnk_sed_args *a, bnn_stream_t st) {
+extern "C" int bnnk_sed_pool(int B, const bnnk_sed_args *a, bnn_stream_t st) {
   if (B <= 0) return 0;
   k_sed_pool<<<dim3(cdiv(a->Cp, 128), (unsigned)B), 128, 0, st>>>(a->red, a->H, a->W, a->C, a->ld, a->L, a->pk, a->dk,
                                                                   a->Cp, a->x, a->xws, a->dw, a->db, a->s, a->sws,
                                                                   a->pl, a->pws);
-  int rc = cudaGetLastError();
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_sed_out(int B, const bnnk_sed_args *a, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  k_sed_out<<<cdiv((long long)B * a->at.N, 128), 128, 0, st>>>(B, a->at.N, a->L, a->hc, a->consts, a->att, a->aws,
+                                                                a->at.Np, a->cla, a->clws, a->cl.Np, a->out, a->ows);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_sed(int B, const bnnk_sed_args *a, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  int rc = bnnk_sed_pool(B, a, st);
   if (rc) return rc;
   // the three GEMMs on the L rows of every window (rows past L of the 8-row tiles are neither read nor written)
   const float *src[3] = {a->pl, a->h, a->h};
@@ -597,8 +609,5 @@ extern "C" int bnnk_sed(int B, const bnnk_sed_args *a, bnn_stream_t st) {
     g.act = i == 0 ? 2 : 0; g.out = dst[i]; g.ows = dws[i]; g.ldo = fp[i]->Np;
     rc = launch_gemm_f32<kSrcPlain>(B, g, st);
   }
-  if (rc) return rc;
-  k_sed_out<<<cdiv((long long)B * a->at.N, 128), 128, 0, st>>>(B, a->at.N, a->L, a->hc, a->consts, a->att, a->aws,
-                                                                a->at.Np, a->cla, a->clws, a->cl.Np, a->out, a->ows);
-  return cudaGetLastError();
+  return rc ? rc : bnnk_sed_out(B, a, st);
 }

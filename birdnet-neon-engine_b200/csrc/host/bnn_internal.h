@@ -48,7 +48,8 @@ const char *bnn_dtype_name(uint32_t dt);
 enum {
   BNN_OP_FE_STFT2 = 1, BNN_OP_C0POOL = 2, BNN_OP_PW = 3, BNN_OP_DW3 = 4, BNN_OP_SE = 5, BNN_OP_POSTPC = 6,
   BNN_OP_DENSE = 7, BNN_OP_FE_LOGMEL = 8, BNN_OP_STEM = 9, BNN_OP_DWK = 10, BNN_OP_PAD = 11, BNN_OP_MEAN = 12,
-  BNN_OP_FE_DBIMG = 16, BNN_OP_CONVK = 17, BNN_OP_GEM = 18, BNN_OP_SED = 19, BNN_OP_VADD = 20, BNN_OP_CONVW = 21, BNN_OP_PW_S8 = 22, BNN_OP_GEMV_S8 = 23, BNN_OP_SE_GATE = 25, BNN_OP_PROTO_S8 = 35, BNN_OP_N = 36
+  BNN_OP_FE_DBIMG = 16, BNN_OP_CONVK = 17, BNN_OP_GEM = 18, BNN_OP_SED = 19, BNN_OP_VADD = 20, BNN_OP_CONVW = 21,
+  BNN_OP_SED_S8 = 24, BNN_OP_PW_S8 = 22, BNN_OP_GEMV_S8 = 23, BNN_OP_SE_GATE = 25, BNN_OP_PROTO_S8 = 35, BNN_OP_N = 36
 };
 /* the fp16 kernels of the neon-fp16 path: base | variant 1 << 8 (src/rt_pkg.c:320-331, src/rt_ops_f16.c:286-299) */
 enum {
@@ -80,6 +81,8 @@ typedef struct {
    * stored rows for op i + 1; qsel = this op's quantized rows live in the second scratch (q2, sa2, za2), which the
    * op before writes while its own GEMM still reads the first */
   int qnext, qsel;
+  /* SED_S8: its three int8 GEMMs (fc, att, cla), each with its weights and plan as a PW_S8 op has them */
+  void *sub;
   /* DW3, SE_GATE, C0POOL, POSTPC; PROTO_S8: f[0] chunk maxima scratch, f[1] class weights, f[2] class biases */
   float *f[10];
   /* PROTO_S8: prototype rows w [Np][Kp], sw, the GEMM plan, eps */

@@ -618,21 +618,21 @@ static int init_vadd(vctx *v) { /* vadd_init, src/rt_ops_f32x.c:352-357 */
   const size_t n = (size_t)v->op->p[0];
   return vneed(v, 0, BNN_F32, n) || vneed(v, 1, BNN_F32, n) || vneed(v, 2, BNN_F32, n) ? -1 : 0;
 }
-static int init_sed(vctx *v) { /* sed_init + rt_sed_geom, src/rt_ops_f32x.c:207-248 */
-  if (vneed_args(v, 7, 9, 21) || v_fpack(v, 2, 0) || v_fpack(v, 4, 4) || v_fpack(v, 6, 8)) return -1;
+/* rt_sed_geom (src/rt_ops_f32x.c:207-236): what SED and SED_S8 check alike after their three GEMM views; kt = the consts
+ * tensor, Cp = the channel stride of s and pooled */
+static int sed_geom(vctx *v, int kt, int Cp) {
   const int *p = v->op->p;
-  const int fcN = p[0], fcK = p[1], fcKp = p[2], fcNp = p[3], atN = p[4], atK = p[5], atKp = p[6], atNp = p[7];
-  const int clN = p[8], clK = p[9], clKp = p[10], clNp = p[11];
+  const int fcN = p[0], fcK = p[1], fcNp = p[3], atN = p[4], atK = p[5], atNp = p[7], clN = p[8], clK = p[9];
+  const int clNp = p[11];
   const int red = p[12], H = p[13], W = p[14], C = p[15], ld = p[16], L = p[17], pk = p[18], dk = p[19], hc = p[20];
-  const int L8 = (L + 7) & ~7, Cp = fcKp;
-  VREQ(v, fcKp % 8 == 0 && atKp == fcNp && clKp == fcNp);
+  const int L8 = (L + 7) & ~7;
   VREQ(v, red == 2 || red == 3);
   VREQ(v, H > 0 && W > 0 && C > 0 && C % 4 == 0 && ld >= C && L == (red == 3 ? H : W));
   VREQ(v, pk >= 0 && pk <= 15 && (pk == 0 || pk % 2) && dk >= 0 && dk <= 15 && (dk == 0 || dk % 2) && (pk || dk));
   VREQ(v, hc == 0 || hc == 1);
   VREQ(v, L <= 64);
   VREQ(v, fcK == C && atK == fcN && clK == fcN && atN == clN);
-  if (vneed_t(v, 0, (size_t)(dk ? dk : 1) * C * 4, 0) || vneed_t(v, 1, (size_t)C * 4, 0) || vneed_t(v, 8, 12, 0))
+  if (vneed_t(v, 0, (size_t)(dk ? dk : 1) * C * 4, 0) || vneed_t(v, 1, (size_t)C * 4, 0) || vneed_t(v, kt, 12, 0))
     return -1;
   const bnn_buf_rec *x = vbd(v, 0);
   if (!x || x->halo || x->dtype != BNN_F32 || x->H != (uint32_t)H || x->W != (uint32_t)W)
@@ -643,6 +643,20 @@ static int init_sed(vctx *v) { /* sed_init + rt_sed_geom, src/rt_ops_f32x.c:207-
                  vneed(v, 6, BNN_F32, (size_t)L8 * clNp)
              ? -1
              : 0;
+}
+static int init_sed(vctx *v) { /* sed_init, src/rt_ops_f32x.c:237-248 */
+  if (vneed_args(v, 7, 9, 21) || v_fpack(v, 2, 0) || v_fpack(v, 4, 4) || v_fpack(v, 6, 8)) return -1;
+  const int *p = v->op->p;
+  VREQ(v, p[2] % 8 == 0 && p[6] == p[3] && p[10] == p[3]);
+  return sed_geom(v, 8, p[2]);
+}
+static int init_sed_s8(vctx *v) { /* sed8_init, src/rt_ops_s8n.c:163-174 */
+  if (vneed_args(v, 10, 15, 21) || v_s8(v, 2, 0) || v_s8(v, 6, 4) || v_s8(v, 10, 8)) return -1;
+  const int *p = v->op->p;
+  const int Cp = R8(p[15]);
+  if (sed_geom(v, 14, Cp)) return -1;
+  const size_t L8 = (size_t)R8(p[17]), Kq = (size_t)(p[2] > p[6] ? p[2] : p[6]);
+  return vneed(v, 7, BNN_I8, L8 * Kq) || vneed(v, 8, BNN_F32, L8) || vneed(v, 9, BNN_I32, L8) ? -1 : 0;
 }
 static int init_convw(vctx *v) { /* convw_init, src/rt_ops_f32x.c:370-412 */
   if (vneed_args(v, 3, 2, 10)) return -1;
@@ -733,6 +747,7 @@ static const kdesc KERNELS[] = {
     {BNN_OP_CONVK, "convk_f32", init_convk, 0x2, 0x4, 1},
     {BNN_OP_GEM, "gem_f32", init_gem, 0x2, 0, 1},
     {BNN_OP_SED, "sed_f32", init_sed, 0x7e, 0, 5},
+    {BNN_OP_SED_S8, "sed_s8n", init_sed_s8, 0x3fe, 0, 7},
     {BNN_OP_VADD, "vadd_f32", init_vadd, 0x4, 0, 1},
     {BNN_OP_CONVW, "convw_f32", init_convw, 0x2, 0x4, 3},
 };
@@ -897,7 +912,8 @@ static int upload(void **dst, const void *src, size_t bytes, char *err, size_t e
  * (the im2col rows and the fp32 GEMM output: the kernel reads the image and writes fp16 directly) */
 static void scratch_args(const bnn_op *op, int *lo, int *n) {
   const int proto = op->code == BNN_OP_PROTO_S8 || op->code == BNN_OP_PROTO_F16S8;
-  *lo = op->code == BNN_OP_PW_S8 ? 3 : op->code == BNN_OP_GEMV_S8 || proto || op->code == BNN_OP_STEM_F16 ? 2 : -1;
+  *lo = op->code == BNN_OP_PW_S8 ? 3 : op->code == BNN_OP_GEMV_S8 || proto || op->code == BNN_OP_STEM_F16 ? 2
+        : op->code == BNN_OP_SED_S8 ? 7 : -1;
   *n = proto ? 1 : op->code == BNN_OP_STEM_F16 ? 2 : 3;
 }
 static int is_scratch(const bnn_ctx *c, int buf) {
@@ -1377,6 +1393,23 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
       if (upload((void **)&d->f[i], tptr(c, op, i), sizeof(float) * sz[i], err, errlen, kind)) return -1;
     return 0;
   }
+  case BNN_OP_SED_S8: { /* t = [dw, db, fc (w sw cs b), att (4), cla (4), consts]; p as SED */
+    const int C = p[15], dk = p[19];
+    if (upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * (size_t)(dk ? dk : 1) * C, err, errlen, kind) ||
+        upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * C, err, errlen, kind) ||
+        upload((void **)&d->f[2], tptr(c, op, 14), sizeof(float) * 3, err, errlen, kind))
+      return -1;
+    bnn_devop *sub = calloc(3, sizeof(bnn_devop));
+    if (!sub) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory (SED int8 GEMMs)"); return -1; }
+    d->sub = sub;
+    for (int g = 0; g < 3; g++) {
+      const int *q = p + 4 * g, t0 = 2 + 4 * g;
+      if (bnn_s8_weights(&sub[g], q[0], q[1], q[2], q[3], tptr(c, op, t0), tptr(c, op, t0 + 1), tptr(c, op, t0 + 2),
+                         tptr(c, op, t0 + 3), c->batch * p[17], err, errlen, kind))
+        return -1;
+    }
+    return 0;
+  }
   case BNN_OP_CONVW: { /* t = [U [36][Np/8][C][8], bias [Np]]; the transform scratch of the batch */
     const int C = p[0], Np = p[2], H = p[3], W = p[4];
     if (upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * 36 * (size_t)Np * C, err, errlen, kind) ||
@@ -1485,6 +1518,12 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
       if (r > rows) rows = r;
       continue;
     }
+    if (op->code == BNN_OP_SED_S8) { /* rows = B x L; the fc rows (K = C) and the att / cla rows (K = fc N) */
+      const size_t r = (size_t)B * op->p[17], qb = r * (size_t)(R32(op->p[1]) > R32(op->p[5]) ? R32(op->p[1]) : R32(op->p[5]));
+      if (qb > qbytes) qbytes = qb;
+      if (r > rows) rows = r;
+      continue;
+    }
     if (op->code != BNN_OP_PW_S8 && op->code != BNN_OP_GEMV_S8 && op->code != BNN_OP_PROTO_S8) continue;
     const size_t r = (size_t)B * (op->code == BNN_OP_GEMV_S8 ? 1 : (size_t)op->p[4]);
     const size_t qb = r * (op->code == BNN_OP_PROTO_S8 ? (size_t)op->p[2] : (size_t)R32(op->p[1]));
@@ -1549,6 +1588,15 @@ int bnn_rt_device(bnn_ctx *c, int di, char *err, size_t errlen, int *kind) {
         return -1;
       }
     }
+    if (op->code == BNN_OP_SED_S8) {
+      bnn_devop *sub = dv->ops[i].sub;
+      for (int g = 0; g < 3; g++)
+        if (bnnk_gemm_plan_init(&sub[g].plan, dv->q, B * op->p[17], sub[g].kq, sub[g].w, op->p[4 * g], op->p[4 * g + 3])) {
+          *kind = BNN_ERR_CPU;
+          snprintf(err, errlen, "op %d %s: TMA descriptors could not be made (driver too old?)", i, op->kname);
+          return -1;
+        }
+    }
     if (op->code == BNN_OP_PROTO_S8 || op->code == BNN_OP_PROTO_F16S8) {
       bnn_devop *o = &dv->ops[i];
       const int v2 = op->code == BNN_OP_PROTO_F16S8;
@@ -1577,6 +1625,12 @@ void bnn_rt_device_free(bnn_ctx *c, int di) {
       bnn_devop *o = &dv->ops[i];
       cudaFree(o->w); cudaFree(o->sw); cudaFree(o->bias); cudaFree(o->cs);
       for (int k = 0; k < 10; k++) cudaFree(o->f[k]);
+      if (o->sub) {
+        bnn_devop *sub = o->sub;
+        for (int g = 0; g < 3; g++) { cudaFree(sub[g].w); cudaFree(sub[g].sw); cudaFree(sub[g].bias); cudaFree(sub[g].cs); }
+        free(sub);
+        o->sub = NULL;
+      }
       cudaFree(o->hw); cudaFree(o->hb); cudaFree(o->hwd);
       bnn_logmel_release(o);
       bnn_dbimg_release(o);
@@ -1781,6 +1835,30 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
                          {p[8], p[9], p[10], p[11], o->f[6], o->f[7]},
                          B_(1), B_(2), B_(3), B_(4), B_(5), B_(6), WS(1), WS(2), WS(3), WS(4), WS(5), WS(6)};
       rc = bnnk_sed(n, &a, st);
+      break;
+    }
+    case BNN_OP_SED_S8: { /* sed8_run (src/rt_ops_s8n.c:186-210): pool, quantize, fc + ReLU, quantize, att, cla, out */
+      bnn_devop *sub = o->sub;
+      const int L = p[17], C = p[15], Cp = R8(C);
+      bnnk_sed_args a = {p[12], p[13], p[14], p[15], p[16], p[17], p[18], p[19], p[20], Cp, IN_(0), INWS(0),
+                         o->f[0], o->f[1], o->f[2],
+                         {p[0], p[1], p[2], p[3], NULL, NULL}, {p[4], p[5], p[6], p[7], NULL, NULL},
+                         {p[8], p[9], p[10], p[11], NULL, NULL},
+                         B_(1), B_(2), B_(3), B_(4), B_(5), B_(6), WS(1), WS(2), WS(3), WS(4), WS(5), WS(6)};
+      rc = bnnk_sed_pool(n, &a, st);
+      if (!rc) rc = bnnk_quant(n * L, L, B_(3), WS(3), Cp, C, sub[0].kq, NULL, 0, dv->q, dv->sa, dv->za, st);
+      if (!rc) {
+        bnnk_epilogue e = {2, B_(4), WS(4), p[3], 0, 0, NULL, 0, 0, 0, 0, sub[0].sw, sub[0].bias, sub[0].cs,
+                           NULL, NULL, NULL, 0, 0};
+        rc = bnnk_gemm(&sub[0].plan, n * L, L, dv->sa, dv->za, &e, dv->err, st);
+      }
+      if (!rc) rc = bnnk_quant(n * L, L, B_(4), WS(4), p[3], p[0], sub[1].kq, NULL, 0, dv->q, dv->sa, dv->za, st);
+      for (int g = 1; g < 3 && !rc; g++) {
+        bnnk_epilogue e = {0, B_(4 + g), WS(4 + g), p[4 * g + 3], 0, 0, NULL, 0, 0, 0, 0, sub[g].sw, sub[g].bias,
+                           sub[g].cs, NULL, NULL, NULL, 0, 0};
+        rc = bnnk_gemm(&sub[g].plan, n * L, L, dv->sa, dv->za, &e, dv->err, st);
+      }
+      if (!rc) rc = bnnk_sed_out(n, &a, st);
       break;
     }
     case BNN_OP_CONVW: {

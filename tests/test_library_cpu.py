@@ -135,7 +135,7 @@ def test_validation_errors(mini_pkg, tmp_path):
     p = mutate(mini_pkg, tmp_path / "k.bnpk", off + 12 + 4 * (nb + nt) + 4, struct.pack("<i", 32))  # K 48 -> 32
     e = init_error(p)
     assert "expected Np = N rounded up to 8, Kp = K rounded up to 16" in str(e)
-    p = mutate(mini_pkg, tmp_path / "op.bnpk", off, struct.pack("<H", 17))  # CONVK: no GPU kernel here
+    p = mutate(mini_pkg, tmp_path / "op.bnpk", off, struct.pack("<H", 29))  # WINO_S8 (dotprod family): no GPU kernel
     e = init_error(p)  # the path picker skips paths with ops this library has no kernel for
     assert e.kind == "CPU" and "runs none of the package's paths" in str(e)
     p = mutate(mini_pkg, tmp_path / "buf.bnpk", off + 12, struct.pack("<i", 9999))

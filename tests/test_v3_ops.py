@@ -20,7 +20,7 @@ from bnneon_b200 import BnnError, Model, pkgread, synth
 from oracle import ref
 
 F32 = synth.F32
-VADD, GEM, SED, CONVK, CONVW = 20, 18, 19, 17, 21
+VADD, GEM, SED, CONVK, CONVW, SED_S8 = 20, 18, 19, 17, 21, 24
 STEM, DWK, PAD, MEAN = 9, 10, 11, 12
 
 
@@ -158,6 +158,35 @@ def pkg_sed(path, red=3, H=12, W=5, C=16, ld=16, hid=24, NC=10, pk=3, dk=3, hc=1
     return H * W * ld, None
 
 
+def s8_tensors(tag, w, b):
+    """the reference packer's int8 GEMM tensors (s8_tensors, lower.py:883-914) as synth writes them for PW_S8"""
+    lw = synth._Int8Lowering([])  # pylint: disable=protected-access
+    tl, shp = lw.s8(tag, np.asarray(w, np.float64), np.asarray(b, np.float32))
+    return [lw.tensors[i] for i in tl], shp
+
+
+def pkg_sed_s8(path, red=3, H=12, W=5, C=20, ld=24, hid=40, NC=12, pk=3, dk=3, hc=1, seed=5):
+    """SED_S8 (rt_ops_s8n.c:160-210): the SED head with int8 fc / att / cla GEMMs on per-row quantized rows"""
+    rng = np.random.default_rng(seed)
+    L = H if red == 3 else W
+    L8, Cp = r8(L), r8(C)
+    fc, (_, _, fkp, fnp) = s8_tensors("sed.fc", rng.standard_normal((hid, C)) * 0.3, rng.standard_normal(hid) * 0.1)
+    at, (_, _, akp, anp) = s8_tensors("sed.att", rng.standard_normal((NC, hid)) * 0.3, rng.standard_normal(NC) * 0.1)
+    cl, (_, _, ckp, cnp) = s8_tensors("sed.cla", rng.standard_normal((NC, hid)) * 0.3, rng.standard_normal(NC) * 0.1)
+    dw = (rng.standard_normal((max(dk, 1), C)) * 0.3).astype(np.float32)
+    db = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    consts = np.array([-2.0, 2.0, 0.5], np.float32)
+    kq = max(fkp, akp)
+    bufs = [(F32, H, W, C, ld, 0, H * W * ld), (F32, 1, 1, NC, NC, 0, NC),
+            (F32, L8, 1, Cp, Cp, 0, L8 * Cp), (F32, L8, 1, Cp, Cp, 0, L8 * Cp),
+            (F32, L8, 1, fnp, fnp, 0, L8 * fnp), (F32, L8, 1, anp, anp, 0, L8 * anp), (F32, L8, 1, cnp, cnp, 0, L8 * cnp),
+            (synth.I8, L8, 1, kq, kq, 0, L8 * kq), (F32, L8, 1, 1, 1, 0, L8), (synth.I32, L8, 1, 1, 1, 0, L8)]
+    tens = [("sed.dw", dw), ("sed.db", db)] + fc + at + cl + [("sed.consts", consts)]
+    ints = [hid, C, fkp, fnp, NC, hid, akp, anp, NC, hid, ckp, cnp, red, H, W, C, ld, L, pk, dk, hc]
+    synth.write_ops_package(path, bufs, tens, [(SED_S8, list(range(10)), list(range(15)), ints)], 1)
+    return H * W * ld, None
+
+
 CASES = {
     "vadd": (pkg_vadd, {}),
     "gem": (pkg_gem, {}),
@@ -177,6 +206,8 @@ CASES = {
     "sed_time": (pkg_sed, {}),
     "sed_freq_nopool": (pkg_sed, dict(red=2, H=6, W=9, pk=0, dk=5, hc=0, C=12, ld=16)),
     "sed_pool_only": (pkg_sed, dict(pk=5, dk=0)),
+    "sed_s8_time": (pkg_sed_s8, {}),
+    "sed_s8_freq": (pkg_sed_s8, dict(red=2, H=7, W=10, pk=0, dk=5, hc=0, C=16, ld=16, NC=9)),
 }
 
 
@@ -238,6 +269,7 @@ def corrupt(path, op_index, k, val, dst):
     ("dwk_k5_s2", 0, 3, 4, "k % 2 == 1"),
     ("stem", 0, 10, 5, "p[10] >= 0 && p[10] <= 2"),
     ("vadd", 0, 0, 0, "p[0] > 0"),
+    ("sed_s8_time", 0, 2, 24, "Kp = K rounded up to 16"),
 ])
 def test_record_checks(tmp_path, name, op, k, val, text):
     path, _, _ = build(tmp_path, name)
