@@ -160,6 +160,7 @@ def metadata(n_classes, emb_dim, labels, model_id="birdnet_v2.4_synthetic", fami
 
 F32, F16, I8, I32 = 0, 1, 2, 3
 OPC = dict(FE_STFT2=1, C0POOL=2, DW3=4, POSTPC=6, PW_S8=22, GEMV_S8=23, SE_GATE=25)
+OPC_PW_F32 = 3
 
 
 def _r8(x):
@@ -1088,6 +1089,148 @@ def write_perch_package(dst, ir):
         sample_rate=PERCH_SAMPLE_RATE, n_samples=fe["nsamp"],
         attribution="synthetic Perch-v2-architecture model (random weights)")
     write_package(dst, meta, lw.tensors, [(PATH_F16, 3, bufs, lw.records, 0, ob, eb)])
+    return n_classes, emb_dim, fe["nsamp"]
+
+
+class _PerchInt8Lowering(_Int8Lowering):
+    """The neon-int8 lowering of a compiled model's IR for the op kinds of Perch v2 with the reference compiler's
+    default int8 policy (lower.py INT8_DEFAULT "pw,head,sed,lin,proto"): 1x1 convs with an activation ("pw") and those
+    feeding the mean ("head") on PW_S8, the projections ("pwl": no activation, SE-gated) on the fp32 PW, the int8
+    prototype head PROTO_S8 (proto_s8n). Follows python/bnneon/compiler/lower.py: l_fe_logmel, stem (STEM variant 0:
+    im2col + fp32 GEMM into the fp32 output), pw / int8_class / out_for_dw (a zero halo of (k - 1) / 2 for a lone
+    depthwise consumer), l_dwconv / dw_input (DW3 for a 3x3 with pads 1 on a halo-1 buffer, else PAD when needed +
+    DWK), l_se (SE_GATE, the gate applied by the next 1x1 conv), l_mean, proto_s8n / emit_proto / cls_tensors."""
+
+    CLASSES = ("pw", "head", "sed", "lin", "proto")
+
+    def __init__(self, ops, nsamp):
+        super().__init__(ops)
+        self.bufs = [(F32, 1, 1, nsamp, nsamp, 0, nsamp)]
+
+    l_fe_logmel = _PerchF16Lowering.l_fe_logmel
+
+    def out_buffer(self, o, ho, wo, co):
+        cons = self.uses.get(o["out"], [])
+        if len(cons) == 1 and cons[0]["op"] == "DWCONV" and co % 8 == 0:
+            hk = (cons[0]["k"][0] - 1) // 2
+            return self.buf(F32, ho, wo, co, ld=co, halo=hk), wo, hk, co
+        ldo = _r8(co)
+        return self.buf(F32, ho, wo, co, ld=ldo), 0, 0, ldo
+
+    def int8_class(self, o):
+        if any(c["op"] in ("GEM", "SED", "MEAN") for c in self.uses.get(o["out"], [])):
+            return "head"
+        return "pwl" if o.get("act") is None else "pw"
+
+    def l_conv(self, i, o, k):
+        w, b = o["w"], o["b"]
+        co = w.shape[0]
+        ib = self.vbuf[o["ins"][0]]
+        _, h_in, w_in, _, ld, _, _ = self.bufs[ib]
+        act = {None: 0, "swish": 1, "relu": 2}[o.get("act")]
+        if o["k"] != [1, 1]:  # the stem: dense k x k VALID conv on the 1-channel fp32 image
+            kk, st = o["k"][0], o["s"][0]
+            ho, wo = self.vshape[o["out"]]
+            k_pad = (kk * kk + 3) & ~3
+            panels, bb, shp = self.pack_f32(w.reshape(co, kk * kk), b, k_pad)
+            tl = [self.tensor(f"f32/stem.{k}.w", panels), self.tensor(f"f32/stem.{k}.b", bb)]
+            ob, _, opad, ldo = self.out_buffer(o, ho, wo, co)
+            col = self.buf(F32, _r8(ho * wo), 1, k_pad)
+            self.emit(OPC_PERCH["STEM"] & 0xff, [ib, ob, col], tl, list(shp) + [h_in, w_in, ho, wo, kk, st, act, ldo, opad],
+                      o)
+            self.vbuf[o["out"]] = ob
+            return i + 1
+        w2 = w[:, :, 0, 0]
+        s8 = self.int8_class(o) in self.CLASSES
+        if s8:
+            tl, shp = self.s8(f"pw.{k}", w2, b)
+        else:
+            panels, bb, shp = self.pack_f32(w2, b, _r8(w2.shape[1]))
+            tl = [self.tensor(f"s8n/pw.{k}.w", panels), self.tensor(f"s8n/pw.{k}.b", bb)]
+        ob, ow, opad, ldo = self.out_buffer(o, h_in, w_in, co)
+        rb, ldr = -1, 0
+        if o.get("res"):
+            rb = self.vbuf[o["res"]]
+            ldr = self.bufs[rb][4]
+        gate = [self.gate[o["ins"][0]]] if o["ins"][0] in self.gate else []
+        if s8:
+            m4 = (h_in * w_in + 3) & ~3
+            qb = self.buf(I8, m4, 1, shp[2])
+            sb = self.buf(F32, m4, 1, 1)
+            zb = self.buf(I32, m4, 1, 1)
+            code, bl = OPC["PW_S8"], [ib, ob, rb, qb, sb, zb] + gate
+        else:
+            code, bl = OPC_PW_F32, [ib, ob, rb] + gate
+        self.emit(code, bl, tl, list(shp) + [h_in * w_in, ld, act, ldo, ow, opad, ldr], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+    def l_dwconv(self, i, o, k):
+        kk, st, pads = o["k"][0], o["s"][0], o["pads"]
+        ib = self.vbuf[o["ins"][0]]
+        _, h, w, c, ld, halo, _ = self.bufs[ib]
+        pt, pl, _, _ = pads
+        ho, wo = self.vshape[o["out"]]
+        self.bufs.append((F32, 1, 1, c, c, 0, c))
+        cs = len(self.bufs) - 1
+        ob = self.buf(F32, ho, wo, c)
+        w9 = o["w"][:, 0].transpose(1, 2, 0).reshape(kk * kk, c)
+        tl = [self.tensor(f"s8n/dw.{k}.w", w9.astype(np.float32)),
+              self.tensor(f"s8n/dw.{k}.b", o["b"].astype(np.float32))]
+        if kk == 3 and halo == 1 and ld == c and max(pads) <= 1 and pt == 1 and pl == 1:
+            self.emit(OPC["DW3"], [ib, ob, cs], tl, [h, w, c, st, ho, wo], o)
+        else:
+            hk = (kk - 1) // 2
+            if halo != hk or ld != c:  # dw_input: a PAD into a buffer with halo hk and ld == C
+                pb_ = self.buf(F32, h, w, c, ld=c, halo=hk)
+                self.emit(OPC_PERCH["PAD"] & 0xff, [ib, pb_], [], [h, w, c, ld, hk], o)
+                ib = pb_
+            self.emit(OPC_PERCH["DWK"] & 0xff, [ib, ob, cs], tl, [h, w, c, kk, st, pt, pl, ho, wo, 1], o)
+        self.vbuf[o["out"]] = ob
+        self.chsum = (ob, cs)
+        return i + 1
+
+    def l_mean(self, i, o, k):
+        ib = self.vbuf[o["ins"][0]]
+        _, h, w, c, ld, _, _ = self.bufs[ib]
+        ob = self.buf(F32, 1, 1, c)
+        self.emit(OPC_PERCH["MEAN"] & 0xff, [ib, ob], [], [h * w, c, ld], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+    def l_proto(self, i, o, k):
+        ib = self.vbuf[o["ins"][0]]
+        _, h, w, c, ld, _, _ = self.bufs[ib]
+        n_proto = o["P"].shape[0]
+        nc, ppc = o["cw"].shape
+        qp, sw, n4, _ = pack_proto_s8(o["P"])
+        n_pad, k_pad = qp.shape[0] * 4, qp.shape[1] * 16
+        tl = [self.tensor(f"s8n/proto.{k}.q", qp), self.tensor(f"s8n/proto.{k}.s", sw),
+              self.tensor(f"s8n/proto.{k}.n4", n4), self.tensor(f"cls.{k}.w", o["cw"]),
+              self.tensor(f"cls.{k}.b", o["cb"]), self.tensor(f"cls.{k}.eps", np.array([o["eps"]], np.float32))]
+        ob = self.buf(F32, 1, 1, nc)
+        ab = self.buf(I8, h * w, 1, k_pad)
+        cm = self.buf(F32, 1, 1, n_pad)
+        self.emit(OPC_PROTO_S8, [ib, ob, ab, cm], tl, [n_proto, c, k_pad, n_pad, h * w, c, ld, nc, ppc], o)
+        self.vbuf[o["out"]] = ob
+        return i + 1
+
+
+def write_perch_int8_package(dst, ir):
+    """Lowers perch_ir()'s result for the neon-int8 path (the reference compiler's default int8 policy) and writes the
+    package; returns (n_classes, emb_dim, n_samples)."""
+    ops, vshape, logits, emb, fe = ir
+    lw = _PerchInt8Lowering(ops, fe["nsamp"])
+    lw.vshape = vshape
+    lw.run()
+    ob, eb = lw.vbuf[logits], lw.vbuf[emb]
+    n_classes, emb_dim = lw.bufs[ob][3], lw.bufs[eb][3]
+    bufs = plan_slots(lw.bufs, lw.records, [ob, eb])
+    meta = [(f"src_nodes/{PATH}", "\n".join(lw.src))] + metadata(
+        n_classes, emb_dim, labels_for(n_classes), model_id="perch_v2_synthetic", family=BNN_MODEL_PERCH_V2,
+        sample_rate=PERCH_SAMPLE_RATE, n_samples=fe["nsamp"],
+        attribution="synthetic Perch-v2-architecture model (random weights)")
+    write_package(dst, meta, lw.tensors, [(PATH, 0, bufs, lw.records, 0, ob, eb)])
     return n_classes, emb_dim, fe["nsamp"]
 
 

@@ -172,6 +172,11 @@ int bnnk_pad_f32(int B, int H, int W, int C, int ld, int h, const float *x, long
 int bnnk_dwk_f32(int B, const float *xp, long long xws, int H, int W, int C, int k, int s, int pt, int pl,
                  const float *w, const float *b, int act, float *out, long long ows, int Ho, int Wo, float *chsum,
                  long long cws, bnn_stream_t st);
+/* PW (fp32 1x1 conv, src/rt_ops_f32.c:110-206): rows [M][lda] of each window, optional SE gate [Kp]; output rows at
+ * their padded position (ow, opad; the halo of the oH x oW output zeroed), optional residual (rw, rpad) */
+int bnnk_pw_f32(int B, const float *x, long long xws, int lda, int M, const float *gate, long long gws, const float *w,
+                const float *bias, int Kp, int Np, int act, float *out, long long ows, int ldo, int ow, int opad, int oH,
+                int oW, const float *res, long long rws, int ldr, int rw, int rpad, bnn_stream_t st);
 int bnnk_stem_f32(int B, const float *img, long long iws, int W, int k, int s, int Ho, int Wo, const float *w,
                   const float *bias, int Kp, int Np, int act, float *out, long long ows, int ldo, int opad, float *col,
                   long long cws, bnn_stream_t st);

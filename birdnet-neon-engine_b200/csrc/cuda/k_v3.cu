@@ -183,13 +183,16 @@ __global__ void k_dwk_f32(int B, int W, int C, int k, int s, int pt, int pl, con
 // Rows of A: PLAIN, row m of window w at A + w aws + m lda; PATCH (CONVK / gemm_f32_seg), output pixel m = (oy, ox)
 // reads nseg segments of segk floats, segment g at A + w aws + ((oy s + oy0 + g) Wp + ox0 + ox s) ld; IM2COL (STEM),
 // k x k taps of a 1-channel image [H][W] (zero past K up to Kp).
-enum { kSrcPlain = 0, kSrcPatch = 1, kSrcIm2col = 2 };
+enum { kSrcPlain = 0, kSrcPatch = 1, kSrcIm2col = 2, kSrcGated = 3 };
 struct F32GemmArgs {
   const float *A;
   long long aws;
   int lda, M;
   // patch / im2col geometry
   int Wo, s, oy0, ox0, Wp, ld, nseg, segk, k, Wimg;
+  // the SE gate of a gated 1x1 conv: gate + w gws [Kp], applied to A as the GEMM reads it (one rounded product)
+  const float *gate;
+  long long gws;
   // weights [Np/8][Kp][8], bias [Np]
   const float *w, *bias;
   int Kp, Np;
@@ -235,6 +238,9 @@ __global__ void __launch_bounds__(256) k_gemm_f32(const F32GemmArgs g) {
   if (SRC == kSrcPlain) {
     const float *ar = Aw + (long long)m * g.lda;
     for (int kk = 0; kk < g.Kp; kk++) step(__ldg(ar + kk), kk);
+  } else if (SRC == kSrcGated) {
+    const float *ar = Aw + (long long)m * g.lda, *gr = g.gate + w * g.gws;
+    for (int kk = 0; kk < g.Kp; kk++) step(__fmul_rn(__ldg(ar + kk), __ldg(gr + kk)), kk);
   } else if (SRC == kSrcPatch) {
     const int oy = m / g.Wo, ox = m - oy * g.Wo;
     int kk = 0;
@@ -520,6 +526,21 @@ extern "C" int bnnk_dwk_f32(int B, const float *xp, long long xws, int H, int W,
   k_dwk_f32<<<cdiv((long long)B * C, 128), 128, 0, st>>>(B, W, C, k, s, pt, pl, xp, xws, w, b, act, out, ows, Ho, Wo,
                                                          chsum, cws);
   return cudaGetLastError();
+}
+
+extern "C" int bnnk_pw_f32(int B, const float *x, long long xws, int lda, int M, const float *gate, long long gws,
+                           const float *w, const float *bias, int Kp, int Np, int act, float *out, long long ows,
+                           int ldo, int ow, int opad, int oH, int oW, const float *res, long long rws, int ldr, int rw,
+                           int rpad, bnn_stream_t st) {
+  if (B <= 0) return 0;
+  int rc = zero_halo(B, out, ows, oH, oW, ldo, opad, st);
+  if (rc) return rc;
+  F32GemmArgs g = {};
+  g.A = x; g.aws = xws; g.lda = lda; g.M = M; g.gate = gate; g.gws = gws;
+  g.w = w; g.bias = bias; g.Kp = Kp; g.Np = Np;
+  g.act = act; g.out = out; g.ows = ows; g.ldo = ldo; g.ow = ow; g.opad = opad;
+  g.res = res; g.rws = rws; g.ldr = ldr; g.rw = rw; g.rpad = rpad;
+  return gate ? launch_gemm_f32<kSrcGated>(B, g, st) : launch_gemm_f32<kSrcPlain>(B, g, st);
 }
 
 extern "C" int bnnk_stem_f32(int B, const float *img, long long iws, int W, int k, int s, int Ho, int Wo,

@@ -57,7 +57,7 @@ static int path_runs_here(const bnn_pkg *p, int i) {
                               BNN_OP_C0POOL_F16, BNN_OP_PW_F16, BNN_OP_DW3_F16, BNN_OP_SE_F16, BNN_OP_POSTPC_F16,
                               BNN_OP_DENSE_F16, BNN_OP_STEM_F16, BNN_OP_DWK_F16, BNN_OP_PAD_F16, BNN_OP_MEAN_F16,
                               BNN_OP_PROTO_F16S8, BNN_OP_STEM, BNN_OP_DWK, BNN_OP_PAD, BNN_OP_MEAN, BNN_OP_CONVK,
-                              BNN_OP_GEM, BNN_OP_SED, BNN_OP_VADD, BNN_OP_CONVW, BNN_OP_SED_S8};
+                              BNN_OP_GEM, BNN_OP_SED, BNN_OP_VADD, BNN_OP_CONVW, BNN_OP_SED_S8, BNN_OP_PW};
   const bnn_path_rec *d = &p->paths[i];
   const uint8_t *q = p->map + d->ops_off, *end = q + d->ops_bytes;
   for (uint32_t k = 0; k < d->n_ops; k++) {

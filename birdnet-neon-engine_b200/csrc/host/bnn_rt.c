@@ -530,6 +530,37 @@ static int init_mean(vctx *v) { /* rt_mean_check, src/rt_ops_f32.c:501-513 (mean
 /* ---- fp32 bodies beyond v2.4: Perch's STEM / DWK (src/rt_ops_f32.c:387-472) and v3.0's CONVK, GEM, SED, VADD,
  * CONVW (src/rt_ops_f32x.c:88-436); the same checks in the same order, with the reference's messages */
 
+static int init_pw_f32(vctx *v) { /* pw_init + rt_pw_check, src/rt_ops_f32.c:115-165 */
+  const bnn_op *op = v->op;
+  if (vneed_args(v, op->nb == 4 ? 4 : 3, 2, 11) || v_fpack(v, 0, 0)) return -1;
+  const int *p = op->p;
+  const int K = p[1], Kp = p[2], Np = p[3], M = p[4], lda = p[5], act = p[6], ldo = p[7], opad = p[9], ldr = p[10];
+  if (op->nb == 4 && op->b[3] >= 0) {
+    VREQ(v, K == Kp);
+    if (vneed(v, 3, BNN_F32, (size_t)K)) return -1;
+  }
+  VREQ(v, M > 0);
+  VREQ(v, lda >= Kp);
+  VREQ(v, ldo >= Np);
+  VREQ(v, act >= 0 && act <= 2);
+  VREQ(v, opad >= 0 && opad <= 3);
+  if (vneed(v, 0, BNN_F32, (size_t)R8(M) * lda)) return -1;
+  if (v_pw_out(v, BNN_F32)) return -1;
+  if (op->b[2] >= 0) {
+    VREQ(v, ldr >= Np);
+    const bnn_buf_rec *r = vbd(v, 2);
+    if (r->halo) {
+      if (r->ld != (uint32_t)ldr || (size_t)r->H * r->W != (size_t)M || !r->W)
+        return vbad(v, "buffer argument 2 (buffer #%d, residual): halo %u needs an fp32 buffer with ld %d and H x W = "
+                    "%d rows, found %s ld %u %ux%u", op->b[2], r->halo, ldr, M, bnn_dtype_name(r->dtype), r->ld, r->H,
+                    r->W);
+      if (vneed(v, 2, BNN_F32, (size_t)(r->H + 2 * r->halo) * (r->W + 2 * r->halo) * ldr)) return -1;
+    } else if (vneed(v, 2, BNN_F32, (size_t)M * ldr))
+      return -1;
+  }
+  if (opad) v->c->launches += 1; /* the zero halo */
+  return 0;
+}
 static int init_stem_f32(vctx *v) { /* stem_init + rt_stem_f32_check, src/rt_ops_f32.c:390-415 */
   if (vneed_args(v, 3, -1, -1) || vneed_args(v, -1, 2, 13) || v_fpack(v, 0, 0)) return -1;
   const int *p = v->op->p;
@@ -740,6 +771,7 @@ static const kdesc KERNELS[] = {
     {BNN_OP_PAD_F16, "pad_f16", init_pad, 0x2, 0, 1},
     {BNN_OP_MEAN_F16, "mean_f16", init_mean, 0x2, 0, 1},
     {BNN_OP_PROTO_F16S8, "proto_s8", init_proto_f16s8, 0xe, 0, 3},
+    {BNN_OP_PW, "pw_f32", init_pw_f32, 0x2, 0xc, 1},
     {BNN_OP_STEM, "stem_f32", init_stem_f32, 0x6, 0, 2},
     {BNN_OP_DWK, "dwk_f32", init_dwk_f32, 0x6, 0, 1},
     {BNN_OP_PAD, "pad_f32", init_pad_f32, 0x2, 0, 2},
@@ -1374,6 +1406,7 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
   case BNN_OP_STEM_F16: /* t = [w panels [Np/8][Kp][8], b [Np]] fp32, used as they are */
     return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * (size_t)p[3] * p[2], err, errlen, kind) ||
            upload((void **)&d->f[1], tptr(c, op, 1), sizeof(float) * (size_t)p[3], err, errlen, kind);
+  case BNN_OP_PW:
   case BNN_OP_STEM:  /* t = [w panels [Np/8][Kp][8], b [Np]] */
   case BNN_OP_CONVK:
     return upload((void **)&d->f[0], tptr(c, op, 0), sizeof(float) * (size_t)p[3] * p[2], err, errlen, kind) ||
@@ -1801,6 +1834,14 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
     case BNN_OP_DENSE:
       rc = bnnk_dense_f32(n, p[0], B_(0), WS(0), o->f[0], o->f[1], B_(1), WS(1), st);
       break;
+    case BNN_OP_PW: { /* pw_run (src/rt_ops_f32.c:193-206) */
+      const bnn_buf_rec *ob = &c->bufd[op->b[1]], *r = op->b[2] >= 0 ? &c->bufd[op->b[2]] : NULL;
+      const float *gate = op->nb == 4 && op->b[3] >= 0 ? IN_(3) : NULL;
+      rc = bnnk_pw_f32(n, IN_(0), INWS(0), p[5], p[4], gate, gate ? INWS(3) : 0, o->f[0], o->f[1], p[2], p[3], p[6],
+                       B_(1), WS(1), p[7], p[8], p[9], (int)ob->H, (int)ob->W, r ? IN_(2) : NULL, r ? INWS(2) : 0,
+                       p[10], r && r->halo ? (int)r->W : 0, r ? (int)r->halo : 0, st);
+      break;
+    }
     case BNN_OP_STEM:
       rc = bnnk_stem_f32(n, IN_(0), INWS(0), p[5], p[8], p[9], p[6], p[7], o->f[0], o->f[1], p[2], p[3], p[10], B_(1),
                          WS(1), p[11], p[12], B_(2), WS(2), st);

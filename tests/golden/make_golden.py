@@ -14,7 +14,8 @@ s8_packing.npz, and for the int8 prototype head (PROTO_S8): the reference loweri
 prototype heads into one-op neon-int8 packages (sha256 in proto_packages.json; bnneon_b200.synth.write_proto_package
 must write the same bytes) and its packer (quant_rows_s8, n4_panel_flags, the [Np/4][Kp/16][4][16] layout) runs on
 fixed matrices (proto_packing.npz); and the reference lowering's l_fe_logmel writes one-op log-mel front-end packages
-(logmel_packages.json), and its l_fe_dbimg one-op dB-image front-end packages (dbimg_packages.json); and the
+(logmel_packages.json), its l_fe_dbimg one-op dB-image front-end packages (dbimg_packages.json) and the Perch-v2-
+architecture model on the neon-int8 path with the default int8 policy (perch_int8_packages.json); and the
 reference lowering writes the same v2.4 models for the neon-fp16 path (sha256 in
 f16_packages.json, with the reference's fp16 SiLU coefficient table read from its source).
 """
@@ -295,6 +296,58 @@ def dbimg_fixtures(ref_root):
         f.write("\n")
 
 
+def perch_ir_for_reference(ops):
+    """perch_ir()'s ops with the log-mel front end in the reference lowering's own node form (l_fe_logmel)"""
+    out = []
+    for o in ops:
+        o = dict(o)
+        if o["op"] == "FE_LOGMEL":
+            fe = o.pop("fe")
+            o.update(mode="dft-op", pad=fe["pad"], frame=fe["frame"], hop=fe["hop"], nfft=fe["nfft"], mel=fe["mel"],
+                     window=fe["window"], floor=fe["floor"], scale=fe["scale"])
+        out.append(o)
+    return out
+
+
+def reference_perch_int8_package(ref_root, ir, dst):
+    """The reference lowering of the Perch-v2-architecture IR for the neon-int8 path with its default int8 policy
+    (bnc.py compile --paths neon-int8)."""
+    sys.path.insert(0, os.path.join(ref_root, "python"))
+    from bnneon.compiler import lower, pkgfmt  # pylint: disable=import-outside-toplevel
+    ops, vshape, lv, ev, fe = ir
+    pkg = pkgfmt.Package()
+    lw = lower.Lowering(pkg, perch_ir_for_reference(ops), synth.PATH, fe["nsamp"])
+    bufs, rops = lw.run(vshape)
+    ob, eb = lw.vbuf[lv], lw.vbuf[ev]
+    n_classes, emb_dim = bufs[ob][3], bufs[eb][3]
+    bufs, _ = lower.plan_slots(bufs, rops, [ob, eb])
+    pkg.add_path(synth.PATH, lower.path_info(synth.PATH).hwcap, bufs, rops, 0, ob, eb)
+    pkg.set(f"src_nodes/{synth.PATH}", "\n".join(lw.src))
+    for k, v in synth.metadata(n_classes, emb_dim, synth.labels_for(n_classes), model_id="perch_v2_synthetic",
+                               family=synth.BNN_MODEL_PERCH_V2, sample_rate=synth.PERCH_SAMPLE_RATE,
+                               n_samples=fe["nsamp"],
+                               attribution="synthetic Perch-v2-architecture model (random weights)"):
+        pkg.set(k, v)
+    pkg.write(dst)
+    return n_classes, emb_dim
+
+
+def perch_int8_fixtures(ref_root):
+    out = {}
+    with tempfile.TemporaryDirectory() as td:
+        for name, mini in (("perch_v2_int8_mini", True), ("perch_v2_int8", False)):
+            ref = os.path.join(td, name + ".ref.bnpk")
+            n_classes, emb_dim = reference_perch_int8_package(ref_root, synth.perch_ir(0, mini=mini), ref)
+            mine = os.path.join(td, name + ".mine.bnpk")
+            synth.write_perch_int8_package(mine, synth.perch_ir(0, mini=mini))
+            out[name] = dict(seed=0, mini=mini, n_classes=n_classes, emb_dim=emb_dim, size=os.path.getsize(ref),
+                             sha256=sha(ref))
+            print(name, out[name], "writer matches" if sha(mine) == sha(ref) else "WRITER DIFFERS")
+    with open(os.path.join(HERE, "perch_int8_packages.json"), "w", encoding="utf-8") as f:
+        json.dump(out, f, indent=1, sort_keys=True)
+        f.write("\n")
+
+
 def sha(path):
     with open(path, "rb") as f:
         return hashlib.sha256(f.read()).hexdigest()
@@ -342,6 +395,7 @@ def main():
     logmel_fixtures(ref_root)
     f16_fixtures(ref_root)
     dbimg_fixtures(ref_root)
+    perch_int8_fixtures(ref_root)
 
 
 if __name__ == "__main__":
