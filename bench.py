@@ -527,6 +527,90 @@ def perch_c4(torch, stream, batch=512, steps=5, cpu=True):
         "the embedding (tests/test_perch_cpu.py)")
 
 
+def perch_int8(torch, stream, batch=512, steps=5, cpu=True):
+    """The Perch-v2-architecture model on the neon-int8 path (the reference compiler's default int8 policy; the
+    reference ships perch_v2-neon-int8.bnpk): device-resident and end-to-end windows/s on `batch` windows, per-op-class
+    device time, the timed outputs of sampled windows against the reference runtime (oracle/_ref) bit for bit."""
+    from bnneon_b200 import Model, pkgread, synth  # pylint: disable=import-outside-toplevel
+    pkg = os.path.join(tempfile.mkdtemp(), "perch_v2_int8.bnpk")
+    _, _, ns = synth.write_perch_int8_package(pkg, synth.perch_ir(0))
+    pcm = synth.audio(batch, seed=4300, n_samples=ns, rate=synth.PERCH_SAMPLE_RATE)
+    m = Model(pkg, mode=4, batch=batch)
+    try:
+        nc, ne = m.info.n_classes, m.info.emb_dim
+        d_pcm = torch.from_numpy(pcm).cuda()
+        d_out = torch.empty((batch, nc), dtype=torch.float32, device="cuda")
+        d_emb = torch.empty((batch, ne), dtype=torch.float32, device="cuda")
+        sp = stream.cuda_stream
+
+        def run():
+            m.infer_device(batch, d_pcm.data_ptr(), d_out.data_ptr(), d_emb.data_ptr(), sp)
+        for _ in range(3):
+            run()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            run()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        h_pcm = torch.from_numpy(pcm).pin_memory()
+        h_out = torch.empty((batch, nc), dtype=torch.float32).pin_memory()
+        h_emb = torch.empty((batch, ne), dtype=torch.float32).pin_memory()
+        m.infer_batch(h_pcm.numpy(), h_out.numpy(), h_emb.numpy())
+        t0 = time.perf_counter()
+        for _ in range(3):
+            m.infer_batch(h_pcm.numpy(), h_out.numpy(), h_emb.numpy())
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / 3
+        stream.synchronize()
+        got, gemb = h_out.numpy().copy(), h_emb.numpy().copy()
+        ops, _ = pkgread.read_ops(pkg)
+        m.h.bnn_profile_begin(m.ctx)
+        for _ in range(2):
+            run()
+            m.h.bnn_profile_collect(m.ctx)
+        m.h.bnn_profile_end(m.ctx)
+        cls = {}
+        for i, (code, _, _, _) in enumerate(ops):
+            c = cls.setdefault(pkgread.NAMES.get(code, str(code)).lower(), {"ms": 0.0, "ops": 0})
+            c["ms"] += m.h.bnn_profile_op_ms(m.ctx, i) / 2
+            c["ops"] += 1
+        launches = m.launches_per_batch
+    finally:
+        m.close()
+    base = checked = None
+    if cpu:
+        cores = os.cpu_count() or 1
+        n = min(batch, cores)
+        kind, crun, what = cpu_runner(pkg, mode=4)
+        t0 = time.perf_counter()
+        crun(pcm[:n], cores)
+        dt = time.perf_counter() - t0
+        base = {"value": round(n / dt, 3), "unit": "windows/s", "cores": cores, "kind": kind,
+                "sample": f"{n} windows, one per thread, {dt:.1f} s: {what}"}
+        from oracle import ref  # pylint: disable=import-outside-toplevel
+        idx = chunk_boundary_sample(batch, batch, 4)
+        want, wemb, rc = ref.run_many(pkg, 4, np.ascontiguousarray(pcm[idx]), threads=min(len(idx), cores))
+        bad = int(sum(not (np.array_equal(got[w].view(np.int32), want[j].view(np.int32)) and
+                           np.array_equal(gemb[w].view(np.int32), wemb[j].view(np.int32))) for j, w in enumerate(idx)))
+        checked = {"windows": len(idx), "calls": ["bnn_infer_batch"], "mismatched": bad, "bit_exact": bad == 0,
+                   "reference_rc": int(np.abs(rc).sum()),
+                   "against": "oracle/_ref (the reference's own C runtime built for this host), logits and embeddings"}
+    total = sum(v["ms"] for v in cls.values())
+    return {"workload": "Perch-v2-architecture neon-int8 package (the reference compiler's default int8 policy): "
+                        "160000-sample windows, log-mel front end, fp32 stem, 26 MBConv blocks with int8 expansions "
+                        "and fp32 SE-gated projections, int8 1536-channel top conv, 14795 x 4 int8 prototypes",
+            "batch": batch, "ms_per_step": round(ms, 3), "windows_per_s": round(batch / (ms * 1e-3), 1),
+            "e2e": {"value": round(batch / (e2e_ms * 1e-3), 1), "unit": "windows/s",
+                    "h2d_bytes_per_step": batch * ns * 4, "d2h_bytes_per_step": batch * (nc + ne) * 4,
+                    "path": "bnn_infer_batch (C ABI), pinned host buffers, wall clock"},
+            "gpu_launches_per_step": launches,
+            "ops": {k: {"ms": round(v["ms"], 4), "share": round(v["ms"] / total, 4), "ops": v["ops"]}
+                    for k, v in sorted(cls.items(), key=lambda kv: -kv[1]["ms"])},
+            "parity_checked": checked, "cpu_baseline": base}
+
+
 def load_peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json"), encoding="utf-8") as f:
@@ -993,6 +1077,8 @@ def main():
             if rank == 0 and not args.no_proto else None)
     perch = (perch_c4(torch, stream, cpu=not args.no_cpu_baseline and world == 1)
              if rank == 0 and not args.no_proto else None)
+    perch8 = (perch_int8(torch, stream, cpu=not args.no_cpu_baseline and world == 1)
+              if rank == 0 and not args.no_proto else None)
 
     # ---- the library's own split (N > 1): after the ranks' processes are done, rank 0 opens one context over all
     # N GPUs (bnn_set_threads(ctx, N)), scores every rank's windows in one call and compares them with its 1-GPU logits
@@ -1046,6 +1132,7 @@ def main():
                 "parity_checked": parity,
                 "ops": ops_summary, "clocks": clocks, "s8_gemm_c1": c1, "proto_s8_c4": proto,
                 "fe_logmel_perch": logmel, "v24_fp16_c3": fp16, "perch_v2_fp16_s8_c4": perch,
+                "perch_v2_int8": perch8,
                 "copy_ceiling": copy_ceiling, "bnn_infer_latency": lat}
         if single is not None:
             line["single_context"] = single

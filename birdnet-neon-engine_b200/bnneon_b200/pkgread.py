@@ -5,11 +5,11 @@ import struct
 # scratch (q, sa, za), which the B200 runtime keeps in its own layout
 # (fp16 ops: base | 1 << 8, the fp16 path's int8 prototype head base | 2 << 8; SE f16 scales its buffer 0 in place;
 # POSTPC's im2col and GEMM rows stay in the runtime's own scratch, STEM f16 needs neither its im2col nor its fp32 rows)
-OUTMASK = {1: 0x2, 2: 0x2, 4: 0x6, 9: 0x6, 10: 0x6, 11: 0x2, 12: 0x2, 16: 0x2, 17: 0x2, 18: 0x2, 19: 0x7E, 20: 0x4, 21: 0x2, 24: 0x3FE, 6: 0xE, 7: 0x2, 8: 0x2, 25: 0x2, 22: 0x3A, 23: 0x1E, 35: 0xE,
+OUTMASK = {1: 0x2, 2: 0x2, 3: 0x2, 4: 0x6, 9: 0x6, 10: 0x6, 11: 0x2, 12: 0x2, 16: 0x2, 17: 0x2, 18: 0x2, 19: 0x7E, 20: 0x4, 21: 0x2, 24: 0x3FE, 6: 0xE, 7: 0x2, 8: 0x2, 25: 0x2, 22: 0x3A, 23: 0x1E, 35: 0xE,
            0x102: 0x2, 0x103: 0x2, 0x104: 0x6, 0x105: 0x1, 0x106: 0xE, 0x107: 0x2,
            0x109: 0xE, 0x10A: 0x6, 0x10B: 0x2, 0x10C: 0x2, 0x20D: 0xE}
 SCRATCH = {22: (3, 4, 5), 24: (7, 8, 9), 23: (2, 3, 4), 6: (2, 3), 35: (2,), 0x106: (2, 3), 0x109: (2, 3), 0x20D: (2,)}
-NAMES = {1: "FE_STFT2", 2: "C0POOL", 4: "DW3", 6: "POSTPC", 7: "DENSE", 8: "FE_LOGMEL", 9: "STEM", 10: "DWK", 11: "PAD", 12: "MEAN", 16: "FE_DBIMG", 17: "CONVK", 18: "GEM", 19: "SED",
+NAMES = {1: "FE_STFT2", 2: "C0POOL", 3: "PW", 4: "DW3", 6: "POSTPC", 7: "DENSE", 8: "FE_LOGMEL", 9: "STEM", 10: "DWK", 11: "PAD", 12: "MEAN", 16: "FE_DBIMG", 17: "CONVK", 18: "GEM", 19: "SED",
          20: "VADD", 21: "CONVW", 24: "SED_S8", 22: "PW_S8", 23: "GEMV_S8",
          25: "SE_GATE", 35: "PROTO_S8", 0x102: "C0POOL_F16", 0x103: "PW_F16", 0x104: "DW3_F16", 0x105: "SE_F16",
          0x106: "POSTPC_F16", 0x107: "DENSE_F16", 0x109: "STEM_F16", 0x10A: "DWK_F16", 0x10B: "PAD_F16",
