@@ -463,6 +463,7 @@ def fp16_package_leg(torch, stream, pkg, pcm, batch, steps, cpu, workload, parit
             if code == 0x103:
                 c["flop"] += 2.0 * batch * p[4] * p[2] * p[3]
         launches = m.launches_per_batch
+        tensor = fp16_tensor_mode(m, torch, stream, run, steps, batch, ops, h_pcm, h_out, h_emb, timed_out)
     finally:
         m.close()
     peak = hfma2_peak(m.h, torch, stream)
@@ -495,7 +496,57 @@ def fp16_package_leg(torch, stream, pkg, pcm, batch, steps, cpu, workload, parit
                          "note": "achieved = 2 M K N of the 1x1 convs (Kp, Np as packed) / their CUDA-event time"},
             "ops": {k: {"ms": round(v["ms"], 4), "share": round(v["ms"] / total, 4), "ops": v["ops"]}
                     for k, v in sorted(cls.items(), key=lambda kv: -kv[1]["ms"])},
-            "parity": parity, "parity_checked": checked, "cpu_baseline": base}
+            "parity": parity, "parity_checked": checked, "cpu_baseline": base, "tensor_mode": tensor}
+
+
+def sqnr_db(got, want):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    return float(10 * np.log10(np.sum(want ** 2) / max(np.sum((got - want) ** 2), 1e-300)))
+
+
+def fp16_tensor_mode(m, torch, stream, run, steps, batch, ops, h_pcm, h_out, h_emb, exact):
+    """The same package in the tensor mode (bnn_set_fp16_tensor: the 1x1 convs as tcgen05 kind::f16 GEMMs with fp32
+    accumulators; within a tolerance of the reference, tests/test_gpu_f16_tensor.py): device and end-to-end
+    windows/s, the 1x1 convs' device time, and the SQNR of its timed outputs against the bit-exact mode's on sampled
+    windows. Leaves the context in the bit-exact mode."""
+    from bnneon_b200 import pkgread  # pylint: disable=import-outside-toplevel
+    m.set_fp16_tensor(True)
+    try:
+        for _ in range(3):
+            run()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            run()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        m.infer_batch(h_pcm.numpy(), h_out.numpy(), h_emb.numpy())
+        t0 = time.perf_counter()
+        for _ in range(3):
+            m.infer_batch(h_pcm.numpy(), h_out.numpy(), h_emb.numpy())
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / 3
+        got, gemb = h_out.numpy().copy(), h_emb.numpy().copy()
+        m.h.bnn_profile_begin(m.ctx)
+        for _ in range(2):
+            run()
+            m.h.bnn_profile_collect(m.ctx)
+        m.h.bnn_profile_end(m.ctx)
+        pw_ms = sum(m.h.bnn_profile_op_ms(m.ctx, i) / 2 for i, (code, _, _, _) in enumerate(ops)
+                    if pkgread.NAMES.get(code) == "PW_F16")
+    finally:
+        m.set_fp16_tensor(False)
+    want, wemb = exact["bnn_infer_batch"]
+    idx = chunk_boundary_sample(batch, batch, 16)
+    return {"ms_per_step": round(ms, 3), "windows_per_s": round(batch / (ms * 1e-3), 1),
+            "e2e": {"value": round(batch / (e2e_ms * 1e-3), 1), "unit": "windows/s"},
+            "pw_f16_ms": round(pw_ms, 4),
+            "min_sqnr_db_vs_bit_exact": {"logits": round(min(sqnr_db(got[w], want[w]) for w in idx), 1),
+                                         "embedding": round(min(sqnr_db(gemb[w], wemb[w]) for w in idx), 1),
+                                         "windows": len(idx)},
+            "note": "bnn_set_fp16_tensor(ctx, 1): the 1x1 convs on tcgen05 kind::f16 with fp32 accumulation instead "
+                    "of the reference's fp16 FMA chains; parity by tolerance (tests/test_gpu_f16_tensor.py)"}
 
 
 def v24_fp16_c3(torch, stream, batch=1024, steps=10, cpu=True):

@@ -108,6 +108,8 @@ SIGNATURES = {
     "bnn_cuda_fn": (_I, [_I, _I, _P, _P, _P]),
     "bnn_debug_fail_alloc": (_I, [_I, _I]),
     "bnn_debug_stall_next_gemm": (None, []),
+    "bnn_set_fp16_tensor": (_I, [_P, _I]),
+    "bnn_get_fp16_tensor": (_I, [_P]),
     "bnn_cuda_op_error": (_I, []),
 }
 
@@ -166,7 +168,7 @@ def probe_meta(path, key, lib=None):
 class Model:
     """One context (one per thread). Results are bit-identical for any batch split and GPU count."""
 
-    def __init__(self, path, mode=MODE_DEFAULT, lib=None, batch=None, devices=None):
+    def __init__(self, path, mode=MODE_DEFAULT, lib=None, batch=None, devices=None, fp16_tensor=None):
         self.h = load_library(lib)
         self.ctx = self.h.bnn_init(path.encode(), mode)
         if not self.ctx:
@@ -178,6 +180,8 @@ class Model:
             self.set_batch(batch)
         if devices is not None:
             self.set_threads(devices)
+        if fp16_tensor is not None:
+            self.set_fp16_tensor(fp16_tensor)
 
     def _check(self, rc):
         if rc:
@@ -205,6 +209,14 @@ class Model:
 
     def set_batch(self, n):
         self._check(self.h.bnn_set_batch(self.ctx, n))
+
+    def set_fp16_tensor(self, on):
+        """the neon-fp16 path's 1x1 convs on the tensor cores (within a tolerance of the reference, not bit-exact)"""
+        self._check(self.h.bnn_set_fp16_tensor(self.ctx, 1 if on else 0))
+
+    @property
+    def fp16_tensor(self):
+        return bool(self.h.bnn_get_fp16_tensor(self.ctx))
 
     @property
     def batch(self):

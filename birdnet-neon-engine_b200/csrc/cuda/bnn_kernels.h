@@ -253,6 +253,13 @@ int bnnk_f16_tables_init(const unsigned long long *tab);
 int bnnk_gemm_f16(int rows, int Mw, const uint16_t *A, long long aws, int lda, const uint32_t *Wd, int Kp, int Np,
                   const uint16_t *b16, const float *b32, int act, uint16_t *out, long long ows, int ldo, int ow,
                   int opad, const uint16_t *res, long long rws, int ldr, bnn_stream_t st);
+/* PW f16 in the tensor mode: a tcgen05 kind::f16 GEMM with fp32 accumulators (not the reference's fp16 chains: within
+ * a tolerance of them), then + b32, one rounding to fp16, act, the fp16 residual add, the padded row. B windows of Mw
+ * rows (window stride aws, row stride lda); Wk [Np][Kp] fp16 K-major. Kp, Np, lda, aws multiples of 8; A and Wk
+ * 16-byte aligned, out / res 8; err: the device error word of the bounded waits */
+int bnnk_gemm_tc16(int B, int Mw, const uint16_t *A, long long aws, int lda, const uint16_t *Wk, int Kp, int Np,
+                   const float *b32, int act, uint16_t *out, long long ows, int ldo, int ow, int opad,
+                   const uint16_t *res, long long rws, int ldr, int *err, bnn_stream_t st);
 /* C0POOL f16: img [B][96][511][2] fp32 -> pin [B][48 * 128][48] fp16; W [64][24] k-major, b16 [24] */
 int bnnk_c0pool_f16(int B, const float *img, long long iws, const uint16_t *W, const uint16_t *b16, uint16_t *pin,
                     long long pws, bnn_stream_t st);

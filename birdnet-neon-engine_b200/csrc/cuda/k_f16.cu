@@ -353,6 +353,210 @@ __global__ void __launch_bounds__(256, TN == 8 ? 2 : kA > 4 ? 2 : 4) k_gemm_f16(
   }
 }
 
+// ------------------------------------------------------------------ PW f16 on the tensor cores (tensor mode)
+
+// The fp16 1x1 conv as a tcgen05 kind::f16 GEMM: fp16 activations and weights, fp32 accumulators in TMEM. This is the
+// path's optional tensor mode, not the reference's arithmetic: the products are exact and summed in fp32 (the
+// reference sums them in fp16 chains of <= 128 k-steps, flushed to fp32), so outputs agree with the CUDA-core form
+// within a tolerance, not bit for bit. The steps after the sum are the flush form's: + the fp32 bias, one rounding to
+// fp16, SiLU (the table) or FMAX(x, 0), the fp16 residual add, the pixel's padded row.
+//
+// One persistent CTA per SM walks the (128-row tile, BN-column tile) space, column tiles fastest. Warp 0 lane 0
+// streams 64-half (128-byte) K blocks of A and B into a ring of shared-memory stages with TMA (A by a 3-D map over
+// [windows][rows][K], so a tile never crosses a window and rows past a window's last read zero; B [Nrows][Kp] K-major;
+// 128-byte swizzle; no multicast); warp 1 lane 0 issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N BN, K 16 per
+// instruction) into one of two TMEM accumulators; each accumulator has an epilogue group of 4 NH warps that read
+// 8-column units with tcgen05.ld. Every mbarrier wait is bounded; a timeout sets the error word and the CTA winds down,
+// still freeing its TMEM.
+constexpr int kT16MaxStages = 8;
+constexpr int kT16Threads = 64 + 128 * 2 * 3;  // 2 accumulators x 3 warps per TMEM lane quarter
+
+struct Tc16Args {
+  int rows_w, mt_w;  // rows of one TMA window and its 128-row tiles
+  int Mw, rows;      // rows per package window (epilogue mapping) and in all
+  int nkb, stages, bn, np, n_tiles, tiles, acc_cols, nh, tmem_alloc;
+  uint32_t idesc;
+  const float *b32;
+  int act;
+  uint16_t *out;
+  long long ows;
+  int ldo, ow, opad;
+  const uint16_t *res;
+  long long rws;
+  int ldr;
+  int vec;  // out and res rows (and window strides) 16-byte aligned: one 16-byte access per 8-column unit
+  int *err;
+};
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+// instruction descriptor of kind::f16: fp16 A and B, fp32 D, both K-major, M 128, N n (a multiple of 16, <= 256)
+__host__ __device__ constexpr uint32_t idesc_f16(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__global__ void __launch_bounds__(kT16Threads, 1) k_gemm_tc16(const __grid_constant__ CUtensorMap tma_a,
+                                                              const __grid_constant__ CUtensorMap tma_b,
+                                                              const Tc16Args a) {
+  extern __shared__ uint8_t dsmem[];
+  __shared__ __align__(8) unsigned long long bar_full[kT16MaxStages], bar_empty[kT16MaxStages];
+  __shared__ __align__(8) unsigned long long bar_acc_full[2], bar_acc_empty[2];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int abort_s;
+  __shared__ uint32_t tab01[16], tab2[16];
+  __shared__ float s_b32[1024];
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t base = (smem_u32(dsmem) + 1023u) & ~1023u;
+  const uint32_t a_bytes = 128u * 128u, stage_bytes = (128u + a.bn) * 128u;
+  const int S = a.stages;
+  load_silu_tab(tab01, tab2);
+  const bool sb = a.np <= 1024;  // the fp32 bias staged in shared memory
+  if (sb)
+    for (int i = threadIdx.x; i < a.np; i += blockDim.x) s_b32[i] = __ldg(a.b32 + i);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; s++) { mbar_init(smem_u32(&bar_full[s]), 1); mbar_init(smem_u32(&bar_empty[s]), 1); }
+    for (int g = 0; g < 2; g++) {
+      mbar_init(smem_u32(&bar_acc_full[g]), 1);
+      mbar_init(smem_u32(&bar_acc_empty[g]), 4 * a.nh);
+    }
+    abort_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(a.tmem_alloc));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      int it = 0;
+      for (int t = blockIdx.x; t < a.tiles && !abort_s; t += gridDim.x) {
+        const int mt = t / a.n_tiles, n0 = (t % a.n_tiles) * a.bn;
+        const int z = mt / a.mt_w, y0 = (mt - z * a.mt_w) * 128;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % S;
+          if (it >= S && !mbar_wait(smem_u32(&bar_empty[s]), ((it / S) - 1) & 1)) {
+            atomicExch(a.err, BNNK_ERR_TMA_WAIT);
+            abort_s = 1;
+            break;
+          }
+          const uint32_t st = base + s * stage_bytes, bar = smem_u32(&bar_full[s]);
+          mbar_expect_tx(bar, stage_bytes);  // the full boxes: elements out of bounds arrive as zero fill
+          tma_load_3d(st, &tma_a, bar, kb * 64, y0, z);
+          tma_load_2d(st + a_bytes, &tma_b, bar, kb * 64, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      int it = 0, lt = 0;
+      for (int t = blockIdx.x; t < a.tiles && !abort_s; t += gridDim.x, lt++) {
+        const int g = lt % 2, use = lt / 2;
+        if (use > 0 && !mbar_wait(smem_u32(&bar_acc_empty[g]), (use - 1) & 1)) {
+          atomicExch(a.err, BNNK_ERR_MMA_WAIT);
+          abort_s = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t tacc = tmem + (uint32_t)(g * a.acc_cols);
+        bool ok = true;
+        for (int kb = 0; kb < a.nkb; kb++, it++) {
+          const int s = it % S;
+          if (!mbar_wait(smem_u32(&bar_full[s]), (it / S) & 1)) {
+            atomicExch(a.err, BNNK_ERR_MMA_WAIT);
+            abort_s = 1;
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t st = base + s * stage_bytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            mma_f16(tacc, smem_desc<128>(st + kk * 32), smem_desc<128>(st + a_bytes + kk * 32), a.idesc, (kb | kk) != 0);
+          mma_commit(smem_u32(&bar_empty[s]));
+        }
+        if (!ok) break;
+        mma_commit(smem_u32(&bar_acc_full[g]));
+      }
+    }
+  } else if (warp - 2 < 8 * a.nh) {
+    // epilogue: group g drains accumulator g; its 4 nh warps split the 8-column units of a tile round robin, the
+    // warp's TMEM lane quarter q (= warp % 4) fixing its 32 rows
+    const int e = warp - 2, g = e / (4 * a.nh), h = (e % (4 * a.nh)) / 4, q = warp % 4;
+    int use = 0;
+    for (int t = blockIdx.x + g * gridDim.x; t < a.tiles; t += 2 * gridDim.x, use++) {
+      const int mt = t / a.n_tiles, n0 = (t % a.n_tiles) * a.bn;
+      const int z = mt / a.mt_w, y = (mt - z * a.mt_w) * 128 + q * 32 + lane;
+      const bool live = y < a.rows_w;
+      const long long r = (long long)z * a.rows_w + y;  // the row over all windows
+      const int w = live ? (int)(r / a.Mw) : 0, m = live ? (int)(r - (long long)w * a.Mw) : 0;
+      bool ok = mbar_wait(smem_u32(&bar_acc_full[g]), use & 1);
+      ok = __all_sync(0xffffffffu, ok && !abort_s);
+      if (!ok) {
+        if (lane == 0) { atomicExch(a.err, BNNK_ERR_EPI_WAIT); abort_s = 1; }
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int units = (min(a.bn, a.np - n0) + 7) / 8;
+      const long long orow = a.opad ? (long long)((m / a.ow) + a.opad) * (a.ow + 2 * a.opad) + (m % a.ow) + a.opad
+                                    : (long long)m;
+      uint16_t *op = a.out + (long long)w * a.ows + orow * a.ldo + n0;
+      const uint16_t *rp = a.res ? a.res + (long long)w * a.rws + (long long)m * a.ldr + n0 : nullptr;
+      const uint32_t tq = tmem + (uint32_t)(g * a.acc_cols) + ((uint32_t)(q * 32) << 16);
+      for (int u = h; u < units; u += a.nh) {
+        uint32_t acc[8];
+        tmem_ld8(tq + (uint32_t)(8 * u), acc);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(acc[0]), "+r"(acc[1]), "+r"(acc[2]), "+r"(acc[3]),
+                     "+r"(acc[4]), "+r"(acc[5]), "+r"(acc[6]), "+r"(acc[7])::"memory");
+        if (!live) continue;
+        const int c = 8 * u;
+        uint32_t v[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float b0 = sb ? s_b32[n0 + c + 2 * j] : __ldg(a.b32 + n0 + c + 2 * j);
+          const float b1 = sb ? s_b32[n0 + c + 2 * j + 1] : __ldg(a.b32 + n0 + c + 2 * j + 1);
+          v[j] = pack2(f2h(__fadd_rn(__uint_as_float(acc[2 * j]), b0)), f2h(__fadd_rn(__uint_as_float(acc[2 * j + 1]), b1)));
+          if (a.act == 1) v[j] = silu2(v[j], tab01, tab2);
+          else if (a.act == 2) v[j] = relu2(v[j]);
+        }
+        if (rp) {
+          if (a.vec) {
+            const uint4 rv = __ldg(reinterpret_cast<const uint4 *>(rp + c));
+            v[0] = hadd2(v[0], rv.x); v[1] = hadd2(v[1], rv.y); v[2] = hadd2(v[2], rv.z); v[3] = hadd2(v[3], rv.w);
+          } else {
+            const uint2 r0 = __ldg(reinterpret_cast<const uint2 *>(rp + c)), r1 = __ldg(reinterpret_cast<const uint2 *>(rp + c + 4));
+            v[0] = hadd2(v[0], r0.x); v[1] = hadd2(v[1], r0.y); v[2] = hadd2(v[2], r1.x); v[3] = hadd2(v[3], r1.y);
+          }
+        }
+        if (a.vec) {
+          *reinterpret_cast<uint4 *>(op + c) = make_uint4(v[0], v[1], v[2], v[3]);
+        } else {
+          *reinterpret_cast<uint2 *>(op + c) = make_uint2(v[0], v[1]);
+          *reinterpret_cast<uint2 *>(op + c + 4) = make_uint2(v[2], v[3]);
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[g]));
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_alloc));
+}
+
 // ------------------------------------------------------------------ C0POOL f16 (src/v24_fast.c:150-164)
 //
 // One CTA per (output row oy, window), thread qx = the pooled pixel: conv pixels 2qx and 2qx + 1 as the two lanes of
@@ -1240,6 +1444,81 @@ static PFN_cuTensorMapEncodeTiled_v12000 f16_encode_fn(void) {
       fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
   });
   return fn;
+}
+
+// The tensor-mode PW f16: Wk [Np][Kp] fp16 K-major (row n holds output channel n's weights), b32 [Np]. Kp, Np, lda
+// and aws multiples of 8 (the TMA row strides are multiples of 16 bytes); A and Wk 16-byte aligned, out / res 8.
+extern "C" int bnnk_gemm_tc16(int B, int Mw, const uint16_t *A, long long aws, int lda, const uint16_t *Wk, int Kp,
+                              int Np, const float *b32, int act, uint16_t *out, long long ows, int ldo, int ow, int opad,
+                              const uint16_t *res, long long rws, int ldr, int *err, bnn_stream_t st) {
+  if (B <= 0 || Mw <= 0) return 0;
+  if (Kp % 8 || Np % 8 || Np <= 0 || lda % 8 || lda < Kp || aws % 8 || ((uintptr_t)A & 15) || ((uintptr_t)Wk & 15) ||
+      ((uintptr_t)out & 7) || ldo % 4 || ows % 4 || (res && (((uintptr_t)res & 7) || ldr % 4 || rws % 4)) ||
+      (opad && ow <= 0) || !err)
+    return cudaErrorInvalidValue;
+  PFN_cuTensorMapEncodeTiled_v12000 enc = f16_encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  Tc16Args a;
+  // windows stored back to back are one tall matrix (tiles cross window boundaries; the epilogue maps each row)
+  const bool flat = aws == (long long)Mw * lda && (long long)B * Mw < (1ll << 31);
+  const int nwin = flat ? 1 : B;
+  a.rows_w = flat ? B * Mw : Mw;
+  a.mt_w = (a.rows_w + 127) / 128;
+  a.Mw = Mw;
+  a.rows = B * Mw;
+  a.nkb = (Kp + 63) / 64;
+  // N tiles: as few of at most 256 columns as possible (equal widths rounded up to 16), then narrower (down to 32)
+  // while the row tiles alone leave SMs idle
+  const int n16 = (Np + 15) & ~15;
+  const long long mtiles = (long long)nwin * a.mt_w;
+  int nt = (n16 + 255) / 256;
+  while (mtiles * nt < num_sms() && ((n16 + nt) / (nt + 1) + 15) / 16 * 16 >= 32) nt++;
+  a.bn = ((n16 + nt - 1) / nt + 15) & ~15;
+  a.n_tiles = (Np + a.bn - 1) / a.bn;
+  a.np = Np;
+  if (mtiles * a.n_tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
+  a.tiles = (int)(mtiles * a.n_tiles);
+  a.acc_cols = a.bn <= 32 ? 32 : a.bn <= 64 ? 64 : a.bn <= 128 ? 128 : 256;
+  a.tmem_alloc = 2 * a.acc_cols < 32 ? 32 : 2 * a.acc_cols;
+  a.nh = 3;
+  a.idesc = idesc_f16(a.bn);
+  a.b32 = b32;
+  a.act = act;
+  a.out = out; a.ows = ows; a.ldo = ldo; a.ow = ow; a.opad = opad;
+  a.res = res; a.rws = rws; a.ldr = ldr;
+  a.vec = ((uintptr_t)out & 15) == 0 && ldo % 8 == 0 && ows % 8 == 0 &&
+          (!res || (((uintptr_t)res & 15) == 0 && ldr % 8 == 0 && rws % 8 == 0));
+  a.err = err;
+  const size_t stage = (size_t)(128 + a.bn) * 128;
+  int s = (int)((200 * 1024) / stage);
+  a.stages = s < 2 ? 2 : s > kT16MaxStages ? kT16MaxStages : s;
+  const size_t smem = (size_t)a.stages * stage + 1024;
+
+  CUtensorMap ma, mb;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)a.rows_w, (cuuint64_t)nwin};
+    cuuint64_t strides[2] = {(cuuint64_t)lda * 2, (cuuint64_t)(flat ? (long long)a.rows_w * lda : aws) * 2};
+    cuuint32_t box[3] = {64, 128, 1}, es[3] = {1, 1, 1};
+    if (enc(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t *>(A), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)Np};
+    cuuint64_t strides[1] = {(cuuint64_t)Kp * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)a.bn}, es[2] = {1, 1};
+    if (enc(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t *>(Wk), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  static SmemAttr attr;
+  const cudaError_t e = attr.ensure(k_gemm_tc16, smem);
+  if (e) return e;
+  const int grid = a.tiles < num_sms() ? a.tiles : num_sms();
+  k_gemm_tc16<<<grid, kT16Threads, smem, st>>>(ma, mb, a);
+  return cudaGetLastError();
 }
 
 // shared memory of the TMA form for CG channels: the ring of S + 3 input rows and the two output-row tiles

@@ -178,6 +178,96 @@ __global__ void k_dwk_f32(int B, int W, int C, int k, int s, int pt, int pl, con
   chsum[win * cws + c] = cs;
 }
 
+// The same op with the pixels spread over a CTA: CTA (channel group of 32, window), lane = channel. A row of output
+// pixels is cut into the reference's units (Wo / 4 blocks of four pixels, then the Wo % 4 tail pixels one by one);
+// the eight warps take the units of a chunk of kDwkChunk units round robin, write their pixels and leave each unit's
+// addend of the channel sum ((v0 + v1) + (v2 + v3) for a block, v for a tail pixel) in shared memory; warp 0 then adds
+// the chunk's addends to its running sums in unit order, which is the reference's raster order. KS x KS taps, the
+// weights in registers; a block reads each tap row's (4 - 1) s + KS inputs once and forms its four pixels' two tap
+// chains from them (even taps from the bias, odd taps from zero) in tap order.
+constexpr int kDwkChunk = 64;
+
+template <int KS>
+__global__ void __launch_bounds__(256) k_dwk_f32b(int W, int C, int s, int pt, int pl, const float *__restrict__ xp,
+                                                  long long xws, const float *__restrict__ wt,
+                                                  const float *__restrict__ bias, int act, float *__restrict__ out,
+                                                  long long ows, int Ho, int Wo, float *__restrict__ chsum,
+                                                  long long cws) {
+  __shared__ uint32_t lut[256];
+  __shared__ float addend[kDwkChunk][32];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = g_frecpe_lut[i];
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int c = blockIdx.x * 32 + lane, win = blockIdx.y;
+  const bool on = c < C;
+  const int cc = on ? c : C - 1;  // idle lanes compute a copy of the last channel and store nothing
+  constexpr int h = (KS - 1) / 2, KK = KS * KS;
+  const int Wp = W + 2 * h;
+  float wv[KK];
+#pragma unroll
+  for (int t = 0; t < KK; t++) wv[t] = __ldg(wt + (long long)t * C + cc);
+  const float b = __ldg(bias + cc);
+  const float *xw = xp + win * xws + cc;
+  float *ow = out + win * ows + cc;
+  const int nb = Wo / 4, nu = nb + Wo % 4, total = Ho * nu;
+  float cs = 0.f;
+  __syncthreads();
+  for (int u0 = 0; u0 < total; u0 += kDwkChunk) {
+    const int u1 = min(total, u0 + kDwkChunk);
+    for (int u = u0 + warp; u < u1; u += 8) {
+      const int oy = u / nu, j = u - oy * nu;
+      const int iy0 = oy * s - pt + h;
+      float add;
+      if (j < nb) {  // four pixels ox .. ox + 3
+        const int ox = 4 * j, ix0 = ox * s - pl + h;
+        float a[4] = {b, b, b, b}, e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ky = 0; ky < KS; ky++) {
+          const float *r = xw + ((long long)(iy0 + ky) * Wp + ix0) * C;
+          float xv[3 * 2 + KS];  // inputs ix0 .. ix0 + 3 s + KS - 1 (s <= 2)
+#pragma unroll
+          for (int i = 0; i < 3 * 2 + KS; i++)
+            if (i < 3 * s + KS) xv[i] = __ldg(r + (long long)i * C);
+#pragma unroll
+          for (int kx = 0; kx < KS; kx++) {
+            const int t = ky * KS + kx;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              const float x = s == 1 ? xv[q + kx] : xv[2 * q + kx];
+              if (t & 1) e[q] = __fmaf_rn(x, wv[t], e[q]);
+              else a[q] = __fmaf_rn(x, wv[t], a[q]);
+            }
+          }
+        }
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          v[q] = __fadd_rn(a[q], e[q]);
+          if (act == 1) v[q] = silu<true>(v[q], lut);
+          if (on) ow[(long long)(oy * Wo + ox + q) * C] = v[q];
+        }
+        add = __fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3]));
+      } else {  // a tail pixel
+        const int ox = 4 * nb + (j - nb);
+        float a = b;
+#pragma unroll
+        for (int ky = 0; ky < KS; ky++)
+#pragma unroll
+          for (int kx = 0; kx < KS; kx++)
+            a = __fmaf_rn(__ldg(xw + ((long long)(iy0 + ky) * Wp + (ox * s - pl + h + kx)) * C), wv[ky * KS + kx], a);
+        if (act == 1) a = silu<true>(a, lut);
+        if (on) ow[(long long)(oy * Wo + ox) * C] = a;
+        add = a;
+      }
+      addend[u - u0][lane] = add;
+    }
+    __syncthreads();
+    if (warp == 0)
+      for (int i = 0; i < u1 - u0; i++) cs = __fadd_rn(cs, addend[i][lane]);
+    __syncthreads();
+  }
+  if (warp == 0 && on) chsum[win * cws + c] = cs;
+}
+
 // ------------------------------------------------------------------ the fp32 GEMM with a patch source
 
 // Rows of A: PLAIN, row m of window w at A + w aws + m lda; PATCH (CONVK / gemm_f32_seg), output pixel m = (oy, ox)
@@ -275,6 +365,171 @@ static int launch_gemm_f32(int B, const F32GemmArgs &g, bnn_stream_t st) {
   const dim3 grid((unsigned)((g.M + 31) / 32), (unsigned)((g.Np / 8 + 7) / 8), (unsigned)B);
   k_gemm_f32<SRC><<<grid, 256, 0, st>>>(g);
   return cudaGetLastError();
+}
+
+// Register-tiled form of the same product for row-major sources (PLAIN, GATED): the B windows' rows are one
+// [B M] x Np product; a CTA of 256 threads computes BM = 16 TM rows x BN = 16 TN columns of it. Thread (ty, tx) =
+// (tid / 16, tid % 16) holds rows ty 4 + 64 i + r (i < TM / 4, r < 4) and columns tx 4 + 64 j + c (j < TN / 4,
+// c < 4; TN = 2: columns 2 tx, 2 tx + 1), so that a warp's shared-memory reads of A are broadcasts and its reads of
+// B cover contiguous 16-byte chunks. K advances in steps of 16 through two shared-memory stages: the next step's
+// global loads are in flight while the current one is multiplied; A is stored k-major (the SE gate applied as it is
+// staged: one rounded product per element, as the reference forms it). Every accumulator still starts at +0 and
+// takes its Kp fused multiply-adds in k order, so the results equal the per-thread form's bit for bit.
+constexpr int kTK = 16;
+
+template <int TM, int TN, bool GATED>
+__global__ void __launch_bounds__(256, 2) k_gemm_f32t(const F32GemmArgs g, int rows, int n_tiles) {
+  constexpr int BM = 16 * TM, BN = 16 * TN, AP = BM + 4;
+  constexpr int AV = BM / 64;                   // float4 loads of A (and of the gate) per thread per step
+  constexpr int BV = BN / 64 > 0 ? BN / 64 : 1;  // float4 loads of B per thread per step (BN = 32: threads < 128)
+  __shared__ __align__(16) float As[2][kTK][AP];
+  __shared__ __align__(16) float Bs[2][kTK][BN];
+  __shared__ uint32_t lut[256];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = g_frecpe_lut[i];
+  const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+  const int nt = blockIdx.x % n_tiles, mt = blockIdx.x / n_tiles;
+  const int n0 = nt * BN;
+  const long long r0 = (long long)mt * BM;
+  const int Kp = g.Kp;
+
+  // this thread's A rows for staging: row r0 + tid / 4 + 64 v, k quad tid % 4
+  const float *arow[AV];  // nullptr past the last row
+  int awin[GATED ? AV : 1];
+#pragma unroll
+  for (int v = 0; v < AV; v++) {
+    const long long r = r0 + tid / 4 + 64 * v;
+    arow[v] = nullptr;
+    if (r < rows) {
+      const int w = (int)(r / g.M), m = (int)(r - (long long)w * g.M);
+      arow[v] = g.A + w * g.aws + (long long)m * g.lda + 4 * (tid % 4);
+      if (GATED) awin[v] = w;
+    }
+  }
+  // this thread's B quads: k = q / (BN / 4), column n0 + 4 (q % (BN / 4)) for q = tid + 256 v
+  const float *bsrc = g.w + (long long)((n0 + 4 * (tid % (BN / 4))) / 8) * Kp * 8 + (long long)(tid / (BN / 4)) * 8 +
+                      (4 * (tid % (BN / 4))) % 8;
+  const bool bon = tid < kTK * BN / 4 / BV && n0 + 4 * (tid % (BN / 4)) < g.Np;
+  float4 ra[AV], rg[GATED ? AV : 1], rb[BV];
+  auto load = [&](int k0) {
+    const int ka = k0 + 4 * (tid % 4);
+#pragma unroll
+    for (int v = 0; v < AV; v++) {
+      const bool on = arow[v] && ka < Kp;
+      ra[v] = on ? __ldg(reinterpret_cast<const float4 *>(arow[v] + k0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (GATED)
+        rg[v] = on ? __ldg(reinterpret_cast<const float4 *>(g.gate + awin[v] * g.gws + ka))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int v = 0; v < BV; v++) {  // quad q = tid + 256 v: k row q / (BN / 4) = tid / (BN / 4) + 256 v / (BN / 4)
+      const int kk = tid / (BN / 4) + 256 * v / (BN / 4);
+      rb[v] = bon && k0 + kk < Kp ? __ldg(reinterpret_cast<const float4 *>(bsrc + (long long)(k0 + 256 * v / (BN / 4)) * 8))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto stage = [&](int s) {
+#pragma unroll
+    for (int v = 0; v < AV; v++) {
+      float4 t = ra[v];
+      if (GATED) {
+        t.x = __fmul_rn(t.x, rg[v].x); t.y = __fmul_rn(t.y, rg[v].y);
+        t.z = __fmul_rn(t.z, rg[v].z); t.w = __fmul_rn(t.w, rg[v].w);
+      }
+      const int m = tid / 4 + 64 * v, k = 4 * (tid % 4);
+      As[s][k][m] = t.x; As[s][k + 1][m] = t.y; As[s][k + 2][m] = t.z; As[s][k + 3][m] = t.w;
+    }
+#pragma unroll
+    for (int v = 0; v < BV; v++) {
+      const int q = tid + 256 * v;
+      if (q < kTK * BN / 4) *reinterpret_cast<float4 *>(&Bs[s][q / (BN / 4)][4 * (q % (BN / 4))]) = rb[v];
+    }
+  };
+
+  float acc[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; i++)
+#pragma unroll
+    for (int j = 0; j < TN; j++) acc[i][j] = 0.f;
+
+  const int nk = (Kp + kTK - 1) / kTK;
+  load(0);
+  stage(0);
+  __syncthreads();
+  for (int kt = 0; kt < nk; kt++) {
+    const int s = kt & 1;
+    if (kt + 1 < nk) load((kt + 1) * kTK);
+    const int kn = Kp - kt * kTK < kTK ? Kp - kt * kTK : kTK;  // block-uniform: only the last step can be short
+    auto body = [&](int kk) {
+      float a[TM], b[TN];
+#pragma unroll
+      for (int i = 0; i < TM / 4; i++) {
+        const float4 t = *reinterpret_cast<const float4 *>(&As[s][kk][4 * ty + 64 * i]);
+        a[4 * i] = t.x; a[4 * i + 1] = t.y; a[4 * i + 2] = t.z; a[4 * i + 3] = t.w;
+      }
+      if (TN == 2) {
+        const float2 t = *reinterpret_cast<const float2 *>(&Bs[s][kk][2 * tx]);
+        b[0] = t.x; b[TN - 1] = t.y;
+      } else {
+#pragma unroll
+        for (int j = 0; j < TN / 4; j++) {
+          const float4 t = *reinterpret_cast<const float4 *>(&Bs[s][kk][4 * tx + 64 * j]);
+          b[4 * j] = t.x; b[4 * j + 1] = t.y; b[4 * j + 2] = t.z; b[4 * j + 3] = t.w;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++) acc[i][j] = __fmaf_rn(b[j], a[i], acc[i][j]);
+    };
+    if (kn == kTK) {
+#pragma unroll
+      for (int kk = 0; kk < kTK; kk++) body(kk);
+    } else {
+      for (int kk = 0; kk < kn; kk++) body(kk);
+    }
+    if (kt + 1 < nk) stage(s ^ 1);
+    __syncthreads();
+  }
+
+  // epilogue (epi32): + bias, activation, residual, the padded output row
+#pragma unroll
+  for (int i = 0; i < TM; i++) {
+    const long long r = r0 + 4 * ty + 64 * (i / 4) + (i % 4);
+    if (r >= rows) continue;
+    const int w = (int)(r / g.M), m = (int)(r - (long long)w * g.M);
+    float *orow = g.out + w * g.ows + pad_row(m, g.ow, g.opad) * g.ldo;
+    const float *rrow = g.res ? g.res + w * g.rws + pad_row(m, g.rw, g.rpad) * g.ldr : nullptr;
+#pragma unroll
+    for (int j = 0; j < TN; j++) {
+      const int n = TN == 2 ? n0 + 2 * tx + j : n0 + 4 * tx + 64 * (j / 4) + (j % 4);
+      if (n >= g.Np) continue;
+      float y = act32(__fadd_rn(acc[i][j], __ldg(g.bias + n)), g.act, lut);
+      if (rrow) y = __fadd_rn(y, __ldg(rrow + n));
+      orow[n] = y;
+    }
+  }
+}
+
+// the tile shape whose padded width covers Np with the fewest columns (ties: the wider tile)
+template <bool GATED>
+static int launch_gemm_f32t(int B, const F32GemmArgs &g, bnn_stream_t st) {
+  const long long rows = (long long)B * g.M;
+  const int w128 = (g.Np + 127) / 128 * 128, w64 = (g.Np + 63) / 64 * 64, w32 = (g.Np + 31) / 32 * 32;
+  const int bn = w128 <= w64 && w128 <= w32 ? 128 : w64 <= w32 ? 64 : 32;
+  const int bm = bn == 32 ? 256 : 128;
+  const int nt = (g.Np + bn - 1) / bn;
+  const long long blocks = (rows + bm - 1) / bm * nt;
+  if (rows > 0x7fffffffLL || blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+  if (bn == 128) k_gemm_f32t<8, 8, GATED><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
+  else if (bn == 64) k_gemm_f32t<8, 4, GATED><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
+  else k_gemm_f32t<16, 2, GATED><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
+  return cudaGetLastError();
+}
+
+// row-major sources take the tiled form when its 16-byte loads are aligned
+static bool f32t_ok(const F32GemmArgs &g) {
+  return ((uintptr_t)g.A & 15) == 0 && g.aws % 4 == 0 && g.lda % 4 == 0 && ((uintptr_t)g.w & 15) == 0 &&
+         g.Np % 8 == 0 && g.Kp % 4 == 0 && (!g.gate || (((uintptr_t)g.gate & 15) == 0 && g.gws % 4 == 0));
 }
 
 // STEM's im2col rows (pc_im2col1), written to the op's column buffer as the reference writes them
@@ -523,6 +778,15 @@ extern "C" int bnnk_dwk_f32(int B, const float *xp, long long xws, int H, int W,
                             float *chsum, long long cws, bnn_stream_t st) {
   (void)H;
   if (B <= 0) return 0;
+  if ((k == 3 || k == 5 || k == 7) && (s == 1 || s == 2)) {
+    const dim3 grid((unsigned)cdiv(C, 32), (unsigned)B);
+#define BNN_DWKB(KS) k_dwk_f32b<KS><<<grid, 256, 0, st>>>(W, C, s, pt, pl, xp, xws, w, b, act, out, ows, Ho, Wo, chsum, cws)
+    if (k == 3) BNN_DWKB(3);
+    else if (k == 5) BNN_DWKB(5);
+    else BNN_DWKB(7);
+#undef BNN_DWKB
+    return cudaGetLastError();
+  }
   k_dwk_f32<<<cdiv((long long)B * C, 128), 128, 0, st>>>(B, W, C, k, s, pt, pl, xp, xws, w, b, act, out, ows, Ho, Wo,
                                                          chsum, cws);
   return cudaGetLastError();
@@ -540,6 +804,7 @@ extern "C" int bnnk_pw_f32(int B, const float *x, long long xws, int lda, int M,
   g.w = w; g.bias = bias; g.Kp = Kp; g.Np = Np;
   g.act = act; g.out = out; g.ows = ows; g.ldo = ldo; g.ow = ow; g.opad = opad;
   g.res = res; g.rws = rws; g.ldr = ldr; g.rw = rw; g.rpad = rpad;
+  if (f32t_ok(g)) return gate ? launch_gemm_f32t<true>(B, g, st) : launch_gemm_f32t<false>(B, g, st);
   return gate ? launch_gemm_f32<kSrcGated>(B, g, st) : launch_gemm_f32<kSrcPlain>(B, g, st);
 }
 

@@ -261,6 +261,8 @@ bnn_ctx *bnn_init(const char *path, int mode) {
   c->batch = eb && atoi(eb) > 0 ? atoi(eb) : 64;
   const char *ep = getenv("BNN_PROF");
   c->prof = ep ? atoi(ep) : 0;
+  const char *et = getenv("BNN_F16_TENSOR");
+  c->f16_tensor = et && atoi(et) > 0;
   char rerr[512];
   int kind = BNN_ERR_PACKAGE;
   if (bnn_rt_open(c, rerr, sizeof rerr, &kind)) {
@@ -350,6 +352,18 @@ int bnn_set_batch(bnn_ctx *c, int batch) {
   return make_devices(c, n);
 }
 int bnn_get_batch(const bnn_ctx *c) { return c ? c->batch : 0; }
+
+int bnn_set_fp16_tensor(bnn_ctx *c, int on) {
+  if (!c) { ERR(BNN_ERR_USAGE, "bnn_set_fp16_tensor: NULL context"); return -1; }
+  on = on != 0;
+  if (on == c->f16_tensor) return 0;
+  const int n = c->n_dev;
+  for (int i = 0; i < 64; i++)
+    if (c->dev[i]) bnn_rt_device_free(c, i);
+  c->f16_tensor = on;
+  return make_devices(c, n);
+}
+int bnn_get_fp16_tensor(const bnn_ctx *c) { return c ? c->f16_tensor : 0; }
 int bnn_launches_per_batch(const bnn_ctx *c) { return c ? c->launches - c->launches_fused : 0; }
 
 /* ------------------------------------------------------------------ inference */

@@ -99,6 +99,8 @@ typedef struct {
    * k-major [Kp][Np] with each weight in both halves of a word, hb the fp16 bias */
   uint16_t *hw, *hb;
   uint32_t *hwd;
+  /* PW f16 in the tensor mode: the weights K-major, [Np][Kp] fp16 (row n = output channel n) */
+  uint16_t *hwk;
 } bnn_devop;
 
 typedef struct {
@@ -157,6 +159,7 @@ struct bnn_ctx {
   int launches;   /* kernel launches per batch, before the set-up's PW_S8 pair fusion */
   int launches_fused; /* launches the pair fusion of the devices' set-up removed (the same on every device) */
   int prof;       /* BNN_PROF */
+  int f16_tensor; /* the neon-fp16 path's 1x1 convs on the tensor cores (bnn_set_fp16_tensor, BNN_F16_TENSOR) */
 };
 
 /* the runtime (bnn_rt.c) */
@@ -170,6 +173,7 @@ int bnn_rt_launch(bnn_ctx *c, int i, int n, const float *d_pcm, int op0, int op1
 /* the whole op list on n windows, replayed from a CUDA graph when the same (n, d_pcm, w_base) ran before */
 int bnn_rt_run(bnn_ctx *c, int i, int n, const float *d_pcm, void *stream);
 int c0_quantizes_next(const bnn_ctx *c, int i);
+int bnn_hpack_kmajor(bnn_devop *d, const uint16_t *panels, int Kp, int Np, char *err, size_t errlen, int *kind);
 /* the op that reports failed windows (-2) through the failed-window word (PROTO_S8, POSTPC f16), or -1 */
 int bnn_window_fail_op(const bnn_ctx *c);
 void bnn_rt_close(bnn_ctx *c);

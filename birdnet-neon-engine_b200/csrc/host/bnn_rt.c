@@ -1324,6 +1324,20 @@ int bnn_hpack_weights(bnn_devop *d, int dup, const uint16_t *panels, const float
   return rc;
 }
 
+/* hp_pack panels as the tensor mode's K-major [Np][Kp] fp16 rows (to d->hwk) */
+int bnn_hpack_kmajor(bnn_devop *d, const uint16_t *panels, int Kp, int Np, char *err, size_t errlen, int *kind) {
+  uint16_t *wt = malloc(sizeof(uint16_t) * (size_t)Kp * Np);
+  if (!wt) { *kind = BNN_ERR_OOM; snprintf(err, errlen, "out of memory (fp16 weights, %d x %d)", Np, Kp); return -1; }
+  const int n16 = Np / 16;
+  for (int n = 0; n < Np; n++)
+    for (int k = 0; k < Kp; k++)
+      wt[(size_t)n * Kp + k] = n / 16 < n16 ? panels[((size_t)(n / 16) * Kp + k) * 16 + n % 16]
+                                            : panels[(size_t)n16 * Kp * 16 + (size_t)k * 8 + n % 16];
+  const int rc = upload((void **)&d->hwk, wt, sizeof(uint16_t) * (size_t)Kp * Np, err, errlen, kind);
+  free(wt);
+  return rc;
+}
+
 /* the weights of op i in the kernels' layouts */
 static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, int *kind) {
   const bnn_op *op = &c->ops[i];
@@ -1382,8 +1396,12 @@ static int op_weights(bnn_ctx *c, bnn_dev *dv, int i, char *err, size_t errlen, 
                              p[7], ((const float *)tptr(c, op, 5))[0], err, errlen, kind);
   case BNN_OP_C0POOL_F16: /* t = [w b32 b16]; p = [24 64 64 24] */
     return bnn_hpack_weights(d, 0, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), 64, 24, NULL, err, errlen, kind);
-  case BNN_OP_PW_F16:
-    return bnn_hpack_weights(d, 1, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), p[2], p[3], &d->f[0], err, errlen, kind);
+  case BNN_OP_PW_F16: {
+    int rc = bnn_hpack_weights(d, 1, tptr(c, op, 0), tptr(c, op, 1), tptr(c, op, 2), p[2], p[3], &d->f[0], err, errlen,
+                               kind);
+    if (!rc && c->f16_tensor) rc = bnn_hpack_kmajor(d, tptr(c, op, 0), p[2], p[3], err, errlen, kind);
+    return rc;
+  }
   case BNN_OP_DW3_F16: {
     const int C = p[2];
     return upload((void **)&d->hw, tptr(c, op, 0), sizeof(uint16_t) * 9 * C, err, errlen, kind) ||
@@ -1664,7 +1682,7 @@ void bnn_rt_device_free(bnn_ctx *c, int di) {
         free(sub);
         o->sub = NULL;
       }
-      cudaFree(o->hw); cudaFree(o->hb); cudaFree(o->hwd);
+      cudaFree(o->hw); cudaFree(o->hb); cudaFree(o->hwd); cudaFree(o->hwk);
       bnn_logmel_release(o);
       bnn_dbimg_release(o);
     }
@@ -1812,6 +1830,11 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
       break;
     case BNN_OP_PW_F16: {
       const int M = p[4];
+      if (o->hwk) { /* the tensor mode */
+        rc = bnnk_gemm_tc16(n, M, B_(0), WS(0), p[5], o->hwk, p[2], p[3], o->f[0], p[6], B_(1), WS(1), p[7], p[8], p[9],
+                            B_(2), WS(2), p[10], dv->err, st);
+        break;
+      }
       rc = bnnk_gemm_f16(n * M, M, B_(0), WS(0), p[5], o->hwd, p[2], p[3], o->hb, o->f[0], p[6], B_(1), WS(1), p[7],
                          p[8], p[9], B_(2), WS(2), p[10], st);
       break;

@@ -41,6 +41,13 @@ int bnn_infer_device(bnn_ctx *ctx, int n, const float *d_pcm, float *d_out, floa
  * arena; 0 on success */
 int bnn_set_batch(bnn_ctx *ctx, int batch);
 int bnn_get_batch(const bnn_ctx *ctx);
+/* No counterpart in the reference: the neon-fp16 path's 1x1 convs (PW f16) on the tensor cores (tcgen05 kind::f16,
+ * fp32 accumulation) instead of the reference's fp16 FMA chains (src/gemm_f16.c:109-169), which the default mode
+ * reproduces bit for bit on the CUDA cores. Outputs then agree with the reference within a tolerance, not exactly.
+ * on = 1 selects it (default 0, or the BNN_F16_TENSOR environment variable at bnn_init); re-creates the context's
+ * device state (weights in both layouts), so call it before inference. 0 on success. */
+int bnn_set_fp16_tensor(bnn_ctx *ctx, int on);
+int bnn_get_fp16_tensor(const bnn_ctx *ctx);
 /* kernels launched by one bnn_infer_device call of n windows (the op list's launches) */
 int bnn_launches_per_batch(const bnn_ctx *ctx);
 

@@ -112,6 +112,36 @@ def pkg_convk(path, H=9, W=13, C=8, N=20, kh=3, kw=3, s=1, act=1, opad=1, res=Tr
     return n_in, halo_mask(H, W, C, h, n_in - base)
 
 
+def pkg_pw(path, M=300, K=40, Kp=None, lda=None, N=24, act=0, gated=True, res=True, ow=0, opad=0, seed=5):
+    """PW (the fp32 1x1 conv of the neon-int8 Perch body, pw_run, src/rt_ops_f32.c:193-206): the window is the
+    [M8][lda] input; a MEAN of it over the M rows makes the [K] input-channel gate, a VADD of it the residual"""
+    rng = np.random.default_rng(seed)
+    Kp = Kp or (K + 3) & ~3
+    lda = lda or Kp
+    panels, bias, (_, _, _, Np) = synth.pack_f32(rng.standard_normal((N, K)) * 0.2, rng.standard_normal(N) * 0.1, Kp)
+    n_in = max(r8(M) * lda, M * Np)
+    if opad:
+        out = (F32, M // ow, ow, N, Np, opad, (M // ow + 2 * opad) * (ow + 2 * opad) * Np)
+    else:
+        out = (F32, 1, M, N, Np, 0, M * Np)
+    bufs = [(F32, 1, r8(M), K, lda, 0, n_in), out]
+    recs = []
+    rb = gb = -1
+    if res:
+        bufs.append((F32, 1, M, Np, Np, 0, M * Np))
+        rb = len(bufs) - 1
+        recs.append((VADD, [0, 0, rb], [], [M * Np]))
+    if gated:
+        bufs.append((F32, 1, 1, K, K, 0, K))
+        gb = len(bufs) - 1
+        recs.append((MEAN, [0, gb], [], [M, K, lda]))
+    recs.append((3, [0, 1, rb] + ([gb] if gated else []), [0, 1], [N, K, Kp, Np, M, lda, act, Np, ow, opad, Np]))
+    synth.write_ops_package(path, bufs, [("pw.w", panels), ("pw.b", bias)], recs, 1)
+    mask = np.zeros(n_in, np.float32)
+    mask.reshape(-1)[:r8(M) * lda].reshape(r8(M), lda)[:, :K] = 1
+    return n_in, mask
+
+
 def pkg_convw(path, H=10, W=14, C=8, N=12, act=1, opad=1, res=True, seed=3):
     rng = np.random.default_rng(seed)
     h, Np = 1, r8(N)
@@ -196,11 +226,21 @@ CASES = {
     "dwk_k5_s2": (pkg_dwk, {}),
     "dwk_k3_s1": (pkg_dwk, dict(k=3, s=1, H=9, W=10, C=24)),
     "dwk_k7_s1_linear": (pkg_dwk, dict(k=7, s=1, H=12, W=9, C=8, act=0)),
+    # channel groups of 32 with a ragged last group, several chunks of 64 units per window
+    "dwk_k5_s1_c72": (pkg_dwk, dict(k=5, s=1, H=13, W=11, C=72)),
+    "dwk_k3_s2_c40": (pkg_dwk, dict(k=3, s=2, H=17, W=19, C=40)),
     "stem": (pkg_stem, {}),
     "stem_relu_nohalo": (pkg_stem, dict(act=2, opad=0, N=16, k=5, s=1, H=12, W=11)),
     "convk_s1_res": (pkg_convk, {}),
     "convk_s2": (pkg_convk, dict(s=2, res=False, act=2, N=16)),
     "convk_1x3": (pkg_convk, dict(kh=1, kw=3, act=0, opad=0)),
+    # fp32 PW at every tile width of the tiled GEMM (32, 64, 128 columns), ragged rows and K steps, padded output
+    "pw_gated_n24_res": (pkg_pw, {}),
+    "pw_silu_n136_pad": (pkg_pw, dict(M=300, K=50, Kp=52, lda=56, N=136, act=1, gated=False, res=False, ow=20,
+                                      opad=1)),
+    "pw_gated_n384_res": (pkg_pw, dict(M=129, K=144, N=384, act=0)),
+    "pw_relu_n60": (pkg_pw, dict(M=77, K=20, Kp=24, lda=28, N=60, act=2, gated=False, res=False)),
+    "pw_gated_n232_silu": (pkg_pw, dict(M=70, K=96, N=232, act=1, res=False)),
     "convw_res": (pkg_convw, {}),
     "convw_edge": (pkg_convw, dict(H=7, W=5, C=12, N=20, act=2, opad=0, res=False)),
     "sed_time": (pkg_sed, {}),
