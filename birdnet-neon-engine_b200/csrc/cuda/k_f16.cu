@@ -388,6 +388,14 @@ struct Tc16Args {
   int *err;
 };
 
+constexpr int kT16Units = 3;  // 8-column TMEM loads in flight per epilogue thread
+// wait for this thread's TMEM loads; the registers they fill are operands of the wait, so no use moves above it
+__device__ __forceinline__ void tmem_wait3(uint32_t (&r)[kT16Units][8]) {
+#define BNN_R8(u) "+r"(r[u][0]), "+r"(r[u][1]), "+r"(r[u][2]), "+r"(r[u][3]), "+r"(r[u][4]), "+r"(r[u][5]), \
+                  "+r"(r[u][6]), "+r"(r[u][7])
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : BNN_R8(0), BNN_R8(1), BNN_R8(2)::"memory");
+#undef BNN_R8
+}
 __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -514,12 +522,17 @@ __global__ void __launch_bounds__(kT16Threads, 1) k_gemm_tc16(const __grid_const
       uint16_t *op = a.out + (long long)w * a.ows + orow * a.ldo + n0;
       const uint16_t *rp = a.res ? a.res + (long long)w * a.rws + (long long)m * a.ldr + n0 : nullptr;
       const uint32_t tq = tmem + (uint32_t)(g * a.acc_cols) + ((uint32_t)(q * 32) << 16);
-      for (int u = h; u < units; u += a.nh) {
-        uint32_t acc[8];
-        tmem_ld8(tq + (uint32_t)(8 * u), acc);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(acc[0]), "+r"(acc[1]), "+r"(acc[2]), "+r"(acc[3]),
-                     "+r"(acc[4]), "+r"(acc[5]), "+r"(acc[6]), "+r"(acc[7])::"memory");
-        if (!live) continue;
+      for (int u0 = h; u0 < units; u0 += kT16Units * a.nh) {
+        uint32_t accs[kT16Units][8];  // up to three units' loads in flight behind one wait
+#pragma unroll
+        for (int k = 0; k < kT16Units; k++)
+          if (u0 + k * a.nh < units) tmem_ld8(tq + (uint32_t)(8 * (u0 + k * a.nh)), accs[k]);
+        tmem_wait3(accs);
+#pragma unroll
+        for (int k = 0; k < kT16Units; k++) {
+        const int u = u0 + k * a.nh;
+        if (!live || u >= units) continue;
+        const uint32_t *acc = accs[k];
         const int c = 8 * u;
         uint32_t v[4];
 #pragma unroll
@@ -544,6 +557,7 @@ __global__ void __launch_bounds__(kT16Threads, 1) k_gemm_tc16(const __grid_const
         } else {
           *reinterpret_cast<uint2 *>(op + c) = make_uint2(v[0], v[1]);
           *reinterpret_cast<uint2 *>(op + c + 4) = make_uint2(v[2], v[3]);
+        }
         }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

@@ -23,6 +23,7 @@
 
 #include "bnn_kernels.h"
 #include "emu.cuh"
+#include "smem_attr.cuh"
 
 namespace bnn {
 
@@ -139,8 +140,8 @@ __global__ void k_pad_f32(int H, int W, int C, int ld, int h, const float *__res
 
 // ------------------------------------------------------------------ DWK f32 (pc_kern_f32.c:163-335)
 
-// one thread per (window, channel): the pixels in raster order, so that the channel sum is added in the reference's
-// order; consecutive threads take consecutive channels (coalesced rows)
+// The general form (any k and stride, unaligned buffers): one thread per (window, channel), the pixels in raster
+// order, so that the channel sum is added in the reference's order; consecutive threads take consecutive channels
 __global__ void k_dwk_f32(int B, int W, int C, int k, int s, int pt, int pl, const float *__restrict__ xp,
                           long long xws, const float *__restrict__ wt, const float *__restrict__ bias, int act,
                           float *__restrict__ out, long long ows, int Ho, int Wo, float *__restrict__ chsum,
@@ -196,95 +197,103 @@ __global__ void k_dwk_f32(int B, int W, int C, int k, int s, int pt, int pl, con
   chsum[win * cws + c] = cs;
 }
 
-// The same op with the pixels spread over a CTA: CTA (channel group of 32, window), lane = channel. A row of output
-// pixels is cut into the reference's units (Wo / 4 blocks of four pixels, then the Wo % 4 tail pixels one by one);
-// the CTA's warps (one to eight: about one per eight units of the map, so that small maps do not pay for idle warps)
-// take the units of a chunk of kDwkChunk units round robin, write their pixels and leave each unit's addend of the
-// channel sum ((v0 + v1) + (v2 + v3) for a block, v for a tail pixel) in shared memory; warp 0 then adds the chunk's
-// addends to its running sums in unit order, which is the reference's raster order. KS x KS taps, the weights in
-// registers; a block reads each tap row's (4 - 1) s + KS inputs once and forms its four pixels' two tap chains from
-// them (even taps from the bias, odd taps from zero) in tap order.
-constexpr int kDwkChunk = 64;
-
-template <int KS>
-__global__ void __launch_bounds__(256) k_dwk_f32b(int W, int C, int s, int pt, int pl, const float *__restrict__ xp,
-                                                  long long xws, const float *__restrict__ wt,
-                                                  const float *__restrict__ bias, int act, float *__restrict__ out,
-                                                  long long ows, int Ho, int Wo, float *__restrict__ chsum,
-                                                  long long cws) {
-  __shared__ uint32_t lut[256];
-  __shared__ float addend[kDwkChunk][32];
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = g_frecpe_lut[i];
-  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
-  const int c = blockIdx.x * 32 + lane, win = blockIdx.y;
-  const bool on = c < C;
-  const int cc = on ? c : C - 1;  // idle lanes compute a copy of the last channel and store nothing
-  constexpr int h = (KS - 1) / 2, KK = KS * KS;
-  const int Wp = W + 2 * h;
-  float wv[KK];
+// The same op with a channel pair per thread and the map's rows over the CTA's thread rows: CTA (Lc channel pairs,
+// window) of Lc x (Ry + 1) threads. Thread (lane, y < Ry) computes output rows y, y + Ry, ... (one per chunk of Ry
+// rows) of its pair, unit by unit in the reference's order (blocks of four pixels, then the tail pixels), stores them
+// and leaves each unit's addend in a double-buffered shared tile; thread row Ry adds the previous chunk's addends in
+// row, then unit order (the raster order of the reference's channel sums) while the others compute the next chunk.
+// The tap weights sit in shared memory; a block reads each tap row's 3 s + K inputs once. The tap chains are paired
+// fused multiply-adds (each lane an IEEE FMA); the addends, sums of SiLU products, are scalar adds.
+template <int K, int S, int G>
+__device__ __forceinline__ float2 dwk2_unit(const float2 *xr, long long rs, long long cs, const float2 *ws, int wl,
+                                           float2 b, int act, const uint32_t *lut, float2 *o, long long os) {
+  constexpr int NX = (G - 1) * S + K;
+  float2 a[G], e[G];
 #pragma unroll
-  for (int t = 0; t < KK; t++) wv[t] = __ldg(wt + (long long)t * C + cc);
-  const float b = __ldg(bias + cc);
-  const float *xw = xp + win * xws + cc;
-  float *ow = out + win * ows + cc;
-  const int nb = Wo / 4, nu = nb + Wo % 4, total = Ho * nu;
-  float cs = 0.f;
-  __syncthreads();
-  for (int u0 = 0; u0 < total; u0 += kDwkChunk) {
-    const int u1 = min(total, u0 + kDwkChunk);
-    for (int u = u0 + warp; u < u1; u += nw) {
-      const int oy = u / nu, j = u - oy * nu;
-      const int iy0 = oy * s - pt + h;
-      float add;
-      if (j < nb) {  // four pixels ox .. ox + 3
-        const int ox = 4 * j, ix0 = ox * s - pl + h;
-        float a[4] = {b, b, b, b}, e[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int q = 0; q < G; q++) { a[q] = b; e[q] = make_float2(0.f, 0.f); }
 #pragma unroll
-        for (int ky = 0; ky < KS; ky++) {
-          const float *r = xw + ((long long)(iy0 + ky) * Wp + ix0) * C;
-          float xv[3 * 2 + KS];  // inputs ix0 .. ix0 + 3 s + KS - 1 (s <= 2)
+  for (int ky = 0; ky < K; ky++) {
+    float2 xv[NX];
 #pragma unroll
-          for (int i = 0; i < 3 * 2 + KS; i++)
-            if (i < 3 * s + KS) xv[i] = __ldg(r + (long long)i * C);
+    for (int j = 0; j < NX; j++) xv[j] = __ldg(xr + ky * rs + j * cs);
 #pragma unroll
-          for (int kx = 0; kx < KS; kx++) {
-            const int t = ky * KS + kx;
+    for (int kx = 0; kx < K; kx++) {
+      const int t = ky * K + kx;
+      const float2 w = ws[t * wl];
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-              const float x = s == 1 ? xv[q + kx] : xv[2 * q + kx];
-              if (t & 1) e[q] = __fmaf_rn(x, wv[t], e[q]);
-              else a[q] = __fmaf_rn(x, wv[t], a[q]);
-            }
-          }
-        }
-        float v[4];
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          v[q] = __fadd_rn(a[q], e[q]);
-          if (act == 1) v[q] = silu<true>(v[q], lut);
-          if (on) ow[(long long)(oy * Wo + ox + q) * C] = v[q];
-        }
-        add = __fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3]));
-      } else {  // a tail pixel
-        const int ox = 4 * nb + (j - nb);
-        float a = b;
-#pragma unroll
-        for (int ky = 0; ky < KS; ky++)
-#pragma unroll
-          for (int kx = 0; kx < KS; kx++)
-            a = __fmaf_rn(__ldg(xw + ((long long)(iy0 + ky) * Wp + (ox * s - pl + h + kx)) * C), wv[ky * KS + kx], a);
-        if (act == 1) a = silu<true>(a, lut);
-        if (on) ow[(long long)(oy * Wo + ox) * C] = a;
-        add = a;
+      for (int q = 0; q < G; q++) {
+        if (G == 4 && (t & 1)) e[q] = fma2_rn(xv[q * S + kx], w, e[q]);
+        else a[q] = fma2_rn(xv[q * S + kx], w, a[q]);
       }
-      addend[u - u0][lane] = add;
+    }
+  }
+  float2 v[G];
+#pragma unroll
+  for (int q = 0; q < G; q++) {
+    v[q] = G == 4 ? make_float2(__fadd_rn(a[q].x, e[q].x), __fadd_rn(a[q].y, e[q].y)) : a[q];
+    if (act == 1) v[q] = silu2(v[q], lut);
+    o[q * os] = v[q];
+  }
+  if (G == 4)
+    return make_float2(__fadd_rn(__fadd_rn(v[0].x, v[1].x), __fadd_rn(v[2].x, v[3].x)),
+                       __fadd_rn(__fadd_rn(v[0].y, v[1].y), __fadd_rn(v[2].y, v[3].y)));
+  return v[0];
+}
+
+template <int K, int S>
+__global__ void __launch_bounds__(256, 3) k_dwk2_f32(const float *__restrict__ xp, long long xws, int W, int C, int pt,
+                                                  int pl, const float *__restrict__ wt, const float *__restrict__ bias,
+                                                  int act, float *__restrict__ out, long long ows, int Ho, int Wo,
+                                                  int nu, float *__restrict__ chsum, long long cws) {
+  extern __shared__ float2 sd2[];  // [K K][Lc] tap weights, then [2][Ry nu][Lc] unit addends of two chunks
+  __shared__ uint32_t lut[256];
+  constexpr int KK = K * K, h = (K - 1) / 2;
+  const int Lc = blockDim.x, Ry = blockDim.y - 1, lane = threadIdx.x, win = blockIdx.y;
+  const int tid = threadIdx.y * Lc + lane, nthr = Lc * blockDim.y;
+  const int c2 = blockIdx.x * Lc + lane, C2 = C / 2;
+  const bool on = c2 < C2, summer = threadIdx.y == Ry;
+  float2 *ws = sd2, *sg = sd2 + KK * Lc;
+  const int tile = Ry * nu * Lc;
+  for (int i = tid; i < 256; i += nthr) lut[i] = g_frecpe_lut[i];
+  for (int t = threadIdx.y; t < KK; t += blockDim.y)
+    ws[t * Lc + lane] = on ? __ldg(reinterpret_cast<const float2 *>(wt) + (long long)t * C2 + c2) : make_float2(0.f, 0.f);
+  const float2 b = on ? __ldg(reinterpret_cast<const float2 *>(bias) + c2) : make_float2(0.f, 0.f);
+  __syncthreads();
+  const float2 *x = reinterpret_cast<const float2 *>(xp + win * xws) + c2;
+  float2 *o = reinterpret_cast<float2 *>(out + win * ows) + c2;
+  const long long cs = C2, rs = (long long)(W + 2 * h) * C2;
+  float sm0 = 0.f, sm1 = 0.f;
+  const int nch = (Ho + Ry - 1) / Ry;
+  for (int ci = 0; ci <= nch; ci++) {
+    if (!summer) {
+      const int oy = ci * Ry + threadIdx.y;
+      if (ci < nch && on && oy < Ho) {
+        const float2 *xr = x + (long long)(oy * S - pt + h) * rs;
+        float2 *orow = o + (long long)oy * Wo * cs;
+        float2 *g = sg + (ci & 1) * tile + threadIdx.y * nu * Lc + lane;
+        int ox = 0, gi = 0;
+        for (; ox + 4 <= Wo; ox += 4, gi++)
+          g[gi * Lc] = dwk2_unit<K, S, 4>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, ws + lane, Lc, b, act, lut,
+                                          orow + ox * cs, cs);
+        for (; ox < Wo; ox++, gi++)
+          g[gi * Lc] = dwk2_unit<K, S, 1>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, ws + lane, Lc, b, act, lut,
+                                          orow + ox * cs, cs);
+      }
+    } else if (ci > 0 && on) {  // the previous chunk's addends, row order then unit order
+      const float2 *gs = sg + ((ci - 1) & 1) * tile + lane;
+      const int n = min(Ry, Ho - (ci - 1) * Ry) * nu;
+      for (int i = 0; i < n; i++) {
+        const float2 r = gs[i * Lc];
+        sm0 = __fadd_rn(sm0, r.x);
+        sm1 = __fadd_rn(sm1, r.y);
+      }
     }
     __syncthreads();
-    if (warp == 0)
-      for (int i = 0; i < u1 - u0; i++) cs = __fadd_rn(cs, addend[i][lane]);
-    __syncthreads();
   }
-  if (warp == 0 && on) chsum[win * cws + c] = cs;
+  if (summer && on) {
+    chsum[win * cws + 2 * c2] = sm0;
+    chsum[win * cws + 2 * c2 + 1] = sm1;
+  }
 }
 
 // ------------------------------------------------------------------ the fp32 GEMM with a patch source
@@ -816,16 +825,31 @@ extern "C" int bnnk_dwk_f32(int B, const float *xp, long long xws, int H, int W,
                             float *chsum, long long cws, bnn_stream_t st) {
   (void)H;
   if (B <= 0) return 0;
-  if ((k == 3 || k == 5 || k == 7) && (s == 1 || s == 2)) {
-    const dim3 grid((unsigned)cdiv(C, 32), (unsigned)B);
-    const int units = Ho * (Wo / 4 + Wo % 4), warps = units >= 64 ? 8 : (units + 7) / 8;
-#define BNN_DWKB(KS) \
-  k_dwk_f32b<KS><<<grid, 32 * warps, 0, st>>>(W, C, s, pt, pl, xp, xws, w, b, act, out, ows, Ho, Wo, chsum, cws)
-    if (k == 3) BNN_DWKB(3);
-    else if (k == 5) BNN_DWKB(5);
-    else BNN_DWKB(7);
-#undef BNN_DWKB
-    return cudaGetLastError();
+  if ((k == 3 || k == 5 || k == 7) && (s == 1 || s == 2) && C % 2 == 0 && xws % 2 == 0 && ows % 2 == 0 &&
+      ((uintptr_t)xp & 7) == 0 && ((uintptr_t)out & 7) == 0 && ((uintptr_t)w & 7) == 0 && ((uintptr_t)b & 7) == 0) {
+    // the channel-pair form: up to 32 pairs per CTA, as many thread rows as fit 256 threads (one of them the summer)
+    const int C2 = C / 2, Lc = C2 < 32 ? C2 : 32, nu = Wo / 4 + Wo % 4;
+    int Ry = 256 / Lc - 1;
+    if (Ry > Ho) Ry = Ho;
+    if (Ry < 1) Ry = 1;
+    auto smem_of = [&](int ry) { return (size_t)(k * k + 2 * ry * nu) * Lc * 8; };
+    while (Ry > 1 && smem_of(Ry) > 48 * 1024) Ry--;
+    const size_t smem = smem_of(Ry);
+    if (smem <= 96 * 1024) {
+      const dim3 grid((unsigned)((C2 + Lc - 1) / Lc), (unsigned)B), blk((unsigned)Lc, (unsigned)(Ry + 1));
+#define BNN_DWK2(KK, SS)                                                                                        \
+  do {                                                                                                          \
+    static SmemAttr attr_;                                                                                      \
+    const cudaError_t e_ = attr_.ensure(k_dwk2_f32<KK, SS>, smem);                                             \
+    if (e_) return e_;                                                                                          \
+    k_dwk2_f32<KK, SS><<<grid, blk, smem, st>>>(xp, xws, W, C, pt, pl, w, b, act, out, ows, Ho, Wo, nu, chsum, cws); \
+  } while (0)
+      if (k == 3) { if (s == 1) BNN_DWK2(3, 1); else BNN_DWK2(3, 2); }
+      else if (k == 5) { if (s == 1) BNN_DWK2(5, 1); else BNN_DWK2(5, 2); }
+      else { if (s == 1) BNN_DWK2(7, 1); else BNN_DWK2(7, 2); }
+#undef BNN_DWK2
+      return cudaGetLastError();
+    }
   }
   k_dwk_f32<<<cdiv((long long)B * C, 128), 128, 0, st>>>(B, W, C, k, s, pt, pl, xp, xws, w, b, act, out, ows, Ho, Wo,
                                                          chsum, cws);

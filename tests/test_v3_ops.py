@@ -226,7 +226,7 @@ CASES = {
     "dwk_k5_s2": (pkg_dwk, {}),
     "dwk_k3_s1": (pkg_dwk, dict(k=3, s=1, H=9, W=10, C=24)),
     "dwk_k7_s1_linear": (pkg_dwk, dict(k=7, s=1, H=12, W=9, C=8, act=0)),
-    # channel groups of 32 with a ragged last group, several chunks of 64 units per window
+    # 32 channel pairs per CTA with a ragged last CTA, several chunks of rows per window
     "dwk_k5_s1_c72": (pkg_dwk, dict(k=5, s=1, H=13, W=11, C=72)),
     "dwk_k3_s2_c40": (pkg_dwk, dict(k=3, s=2, H=17, W=19, C=40)),
     "stem": (pkg_stem, {}),
