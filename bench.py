@@ -78,9 +78,8 @@ OP_KERNELS = {1: ("k_fe_minmax", "k_fe_spec"), 2: ("k_c0pool",), 22: ("k_quant",
 
 
 def ncu_summary(csv_path, batch):
-    """Reads an ncu launch list (gpu__time_duration.sum + dram bytes, one step of the full package) and writes
-    PROFILE: per kernel and per op class the device time, share and DRAM traffic, plus a JSON block with the DRAM
-    bytes per op that bench runs report as roofline.traffic."""
+    """Reads an ncu launch list (gpu__time_duration.sum, one step of the full package; DRAM byte counters too if the
+    capture had them) and writes PROFILE: per kernel and per op class the device time and share (and DRAM traffic)."""
     import csv  # pylint: disable=import-outside-toplevel
     from collections import OrderedDict  # pylint: disable=import-outside-toplevel
     from bnneon_b200 import pkgread, synth  # pylint: disable=import-outside-toplevel
@@ -127,40 +126,47 @@ def ncu_summary(csv_path, batch):
         k[0] += 1
         k[1] += e["us"]
         k[2] += e.get("bytes", 0.0)
+    dram = any("bytes" in e for e in lst)
     out = [f"# Launch list: full v2.4 int8 package, batch {batch}, one step ({len(lst)} launches)", "",
            "Command (GPU box, after the same command line without `ncu` exited 0):", "",
            "    python bench.py --ncu --warmup 3 && \\",
            "    " + NCU_CMD.format(skip=3 * len(lst), count=len(lst)), "",
            "then `python bench.py --ncu-summary <out>/launches.csv` wrote this file. Per-launch times are",
            "serialised and cold-cache (ncu flushes caches between launches); the shares are what compare with the",
-           "bench's per-op CUDA-event times. DRAM bytes are `dram__bytes_read.sum + dram__bytes_write.sum`.", "",
-           "| kernel | launches | total µs | share | DRAM MB | GB/s |", "|---|---:|---:|---:|---:|---:|"]
+           "bench's per-op CUDA-event times.", "",
+           "| kernel | launches | total µs | share |" + (" DRAM MB | GB/s |" if dram else ""),
+           "|---|---:|---:|---:|" + ("---:|---:|" if dram else "")]
     for k, (n, us, by) in sorted(kern.items(), key=lambda kv: -kv[1][1]):
-        out.append(f"| {k} | {n} | {us:.1f} | {100 * us / tot:.1f}% | {by / 1e6:.1f} | {by / us / 1e3:.0f} |")
-    out += [f"| **total** | {len(lst)} | {tot:.1f} | | | |", "", "Per op class (the package's ops):", "",
-            "| op class | ops | launches | total µs | share | DRAM MB per op |", "|---|---:|---:|---:|---:|---:|"]
+        out.append(f"| {k} | {n} | {us:.1f} | {100 * us / tot:.1f}% |" +
+                   (f" {by / 1e6:.1f} | {by / us / 1e3:.0f} |" if dram else ""))
+    out += [f"| **total** | {len(lst)} | {tot:.1f} | |" + (" | |" if dram else ""), "",
+            "Per op class (the package's ops):", "",
+            "| op class | ops | launches | total µs | share |", "|---|---:|---:|---:|---:|"]
     for k, c in sorted(cls.items(), key=lambda kv: -kv[1]["us"]):
-        out.append(f"| {k} | {c['ops']} | {c['launches']} | {c['us']:.1f} | {100 * c['us'] / tot:.1f}% | "
-                   f"{c['bytes'] / c['ops'] / 1e6:.2f} |")
-    traffic = {k: {"dram_bytes_per_op": round(c["bytes"] / c["ops"]), "ops": c["ops"]} for k, c in cls.items()}
-    out += ["", "Traffic per op, read by bench.py for roofline.traffic:", "", "```json",
-            json.dumps({"batch": batch, "traffic": traffic}), "```", ""]
+        out.append(f"| {k} | {c['ops']} | {c['launches']} | {c['us']:.1f} | {100 * c['us'] / tot:.1f}% |")
+    out.append("")
     with open(PROFILE, "w", encoding="utf-8") as f:
         f.write("\n".join(out))
     print(f"wrote {PROFILE}")
 
 
-def profile_traffic(cls_name, batch):
-    """DRAM bytes per op of an op class from the committed launch-list summary (None if absent or another batch)."""
+TRAFFIC = os.path.join(REPO, "profiles", "traffic_pw_s8n_v24_int8_b64.md")
+
+
+def profile_traffic(cls_name, alg_bytes_per_op):
+    """DRAM bytes per op of an op class, from the committed one-op capture (profiles/traffic_*: the DRAM bytes of one
+    representative op's launches at a small batch against that op's algorithmic bytes) scaled to the class's
+    algorithmic bytes per op: (bytes, ratio, what), or (None, None, None) if there is no capture for the class."""
     try:
-        with open(PROFILE, encoding="utf-8") as f:
+        with open(TRAFFIC, encoding="utf-8") as f:
             txt = f.read()
         blk = json.loads(txt.split("```json", 1)[1].split("```", 1)[0])
-        if blk["batch"] != batch:
-            return None
-        return blk["traffic"][cls_name]["dram_bytes_per_op"]
+        if blk["class"] != cls_name:
+            return None, None, None
+        ratio = blk["dram_bytes"] / blk["algorithmic_bytes"]
+        return round(ratio * alg_bytes_per_op), round(ratio, 3), blk["what"]
     except (OSError, IndexError, KeyError, ValueError):
-        return None
+        return None, None, None
 
 
 def c1_gemm(m, torch, stream, peak_bf16):
@@ -1102,14 +1108,16 @@ def main():
     ach = cls[top]["bytes"] / (cls[top]["ms"] / 1e3) / 1e9
     s8_ms = cls.get("pw_s8n", {"ms": 0})["ms"] + cls.get("gemv_s8n", {"ms": 0})["ms"]
     s8_macs = cls.get("pw_s8n", {"macs": 0})["macs"] + cls.get("gemv_s8n", {"macs": 0})["macs"]
+    alg_op = cls[top]["bytes"] / cls[top]["ops"]
+    traffic, t_ratio, t_what = profile_traffic(top, alg_op)
     roofline = {"bound": "hbm", "kernel": f"{top} ({cls[top]['ops']} ops per step)", "achieved": round(ach, 1),
                 "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
-                "traffic": profile_traffic(top, B),
-                "algorithmic_bytes_per_op": round(cls[top]["bytes"] / cls[top]["ops"]),
+                "traffic": traffic, "traffic_over_algorithmic": t_ratio,
+                "algorithmic_bytes_per_op": round(alg_op),
                 "peak_source": peak_src,
                 "note": "achieved = algorithmic bytes of the op class per step / its CUDA-event time (the per-op "
-                        "average); traffic = ncu DRAM bytes per op of the same class at the same batch "
-                        "(profiles/launch_list_v24_int8_b256.md)"}
+                        "average); traffic = the class's algorithmic bytes per op x the DRAM / algorithmic ratio of "
+                        f"one op captured alone ({t_what}; profiles/traffic_pw_s8n_v24_int8_b64.md)"}
     ops_summary = {k: {"ms": round(v["ms"], 4), "share": round(v["ms"] / sum(x["ms"] for x in cls.values()), 4),
                        "GB/s": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1) if v["ms"] else None, "ops": v["ops"]}
                    for k, v in sorted(cls.items(), key=lambda kv: -kv[1]["ms"])}

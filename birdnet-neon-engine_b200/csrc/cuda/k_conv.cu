@@ -15,6 +15,7 @@
 #include "emu.cuh"
 #include "smem_attr.cuh"
 #include "sync.cuh"
+#include "tc.cuh"
 
 namespace bnn {
 
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(kDwThreads) k_dw3(const float *__restrict__ xp
       for (; i < n; i++) cs = __fadd_rn(cs, buf[i * CG + tid]);
     }
   }
-  if (tid < CG) chsum[win * cws + grp * CG + tid] = cs;
+  if (chsum && tid < CG) chsum[win * cws + grp * CG + tid] = cs;
 }
 
 // The same DW3 with the input streamed by TMA. One CTA per (window, group of CG channels) walks the output rows:
@@ -130,12 +131,14 @@ __global__ void __launch_bounds__(kDwThreads) k_dw3(const float *__restrict__ xp
 // quad's weights in registers and computes pixel groups lane, lane + NL, ... of the row (R consecutive pixels per
 // group share their input columns), stores them and leaves them in a double-buffered row tile; after the step's
 // barrier the first CG threads continue their channel's sum over the row in pixel order.
+// Without the channel sums (kSum false: no op reads them in a whole-package run) the rows of a window are cut into
+// nband bands of consecutive output rows, one CTA each, so that small batches still fill the GPU.
 constexpr int kDw3MaxRing = 32;
-template <int S, int R>
+template <int S, int R, bool kSum>
 __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMap tmx, int W, int C, int CG, int Ho,
                                               int Wo, int NR, const float *__restrict__ wt,
                                               const float *__restrict__ bias, float *__restrict__ out, long long ows,
-                                              float *__restrict__ chsum, long long cws, int *err) {
+                                              float *__restrict__ chsum, long long cws, int *err, int nband) {
   constexpr int NX = (R - 1) * S + 3;
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ __align__(8) unsigned long long bar[kDw3MaxRing];
@@ -143,7 +146,10 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
   const int tid = threadIdx.x, nt = blockDim.x;
   for (int i = tid; i < 256; i += nt) lut[i] = g_frecpe_lut[i];
   const int ngroups = C / CG;
-  const int win = blockIdx.x / ngroups, grp = blockIdx.x - win * ngroups;
+  const int band = blockIdx.x % nband, wg = blockIdx.x / nband;
+  const int win = wg / ngroups, grp = wg - win * ngroups;
+  const int hb = (Ho + nband - 1) / nband, oy0 = band * hb, oy1 = min(Ho, oy0 + hb);
+  if (oy0 >= oy1) return;  // an empty last band (the whole CTA leaves before any barrier)
   const int Wp = W + 2, Q = CG >> 2, NL = nt / Q, ngrp = Wo / R;
   const uint32_t row_bytes = (uint32_t)Wp * CG * 4, row_stride = (row_bytes + 127u) & ~127u;
   const uint32_t ring = smem_u32(dsm);
@@ -169,24 +175,25 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  const int rows_in = (Ho - 1) * S + 3;  // input rows the outputs read
-  int issued = 0;                        // rows whose load thread 0 has issued
-  auto issue_to = [&](int last) {        // thread 0: load rows issued .. last
+  // ring rows are counted from the band's first input row iy0: local row l is input row iy0 + l
+  const int iy0 = oy0 * S, rows_in = (oy1 - 1 - oy0) * S + 3;  // input rows the band's outputs read
+  int issued = 0;                        // local rows whose load thread 0 has issued
+  auto issue_to = [&](int last) {        // thread 0: load local rows issued .. last
     for (; issued <= last && issued < rows_in; issued++) {
       const int sl = issued % NR;
       mbar_expect_tx(smem_u32(&bar[sl]), row_bytes);
-      tma_load_3d(ring + sl * row_stride, &tmx, smem_u32(&bar[sl]), grp * CG, issued * Wp, win);
+      tma_load_3d(ring + sl * row_stride, &tmx, smem_u32(&bar[sl]), grp * CG, (iy0 + issued) * Wp, win);
     }
   };
   if (tid == 0) issue_to(NR - 1);  // as many rows as the ring holds
   float cs = 0.f;
-  int oy = 0;
-  for (; oy < Ho; oy++) {
+  int oy = oy0;
+  for (; oy < oy1; oy++) {
     bool ok = true;
     int slot[3];
 #pragma unroll
     for (int ky = 0; ky < 3; ky++) {
-      const int iy = oy * S + ky;
+      const int iy = (oy - oy0) * S + ky;
       slot[ky] = iy % NR;
       ok = ok && mbar_wait(smem_u32(&bar[slot[ky]]), (uint32_t)(iy / NR) & 1u);
     }
@@ -229,13 +236,13 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
           const float2 y1 = silu2(add2_rn(acc[r][1], add2_rn(acb[r][1], acd[r][1])), lut);
           const float4 v = make_float4(y0.x, y0.y, y1.x, y1.y);
           *reinterpret_cast<float4 *>(out + win * ows + (long long)(oy * Wo + x0 + r) * C + c) = v;
-          *reinterpret_cast<float4 *>(ob + (x0 + r) * CG + 4 * q) = v;
+          if (kSum) *reinterpret_cast<float4 *>(ob + (x0 + r) * CG + 4 * q) = v;
         }
       }
     }
     if (!__syncthreads_and(ok)) break;  // every thread has left this step's rows and written its outputs
-    if (tid == 0) issue_to((oy + 1) * S + NR - 1);  // rows below (oy + 1) S are free
-    if (tid < CG) {
+    if (tid == 0) issue_to((oy - oy0 + 1) * S + NR - 1);  // local rows below (oy - oy0 + 1) S are free
+    if (kSum && tid < CG) {
       int x = 0;
       for (; x + 8 <= Wo; x += 8) {
         float u[8];
@@ -247,38 +254,44 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
       for (; x < Wo; x++) cs = __fadd_rn(cs, ob[x * CG + tid]);
     }
   }
-  if (oy < Ho) {  // a load never arrived: report it, then let the loads still in flight land before leaving
+  if (oy < oy1) {  // a load never arrived: report it, then let the loads still in flight land before leaving
     if (tid == 0) {
       if (err) atomicExch(err, BNNK_ERR_DW3_WAIT);
-      for (int iy = oy * S; iy < issued; iy++) mbar_wait(smem_u32(&bar[iy % NR]), (uint32_t)(iy / NR) & 1u);
+      for (int iy = (oy - oy0) * S; iy < issued; iy++) mbar_wait(smem_u32(&bar[iy % NR]), (uint32_t)(iy / NR) & 1u);
     }
     __syncthreads();
     return;
   }
-  if (tid < CG) chsum[win * cws + grp * CG + tid] = cs;
+  if (kSum && tid < CG) chsum[win * cws + grp * CG + tid] = cs;
 }
 
 // ------------------------------------------------------------------ SE_GATE (src/v24_f32.c:164-179, rt_ops_f32.c:272-283)
 
-// One CTA per window. fc1 row r: 8 threads hold the 8 NEON accumulator lanes (a0 lanes 0-3, a1 lanes 0-3) over
-// c = 8i + lane, then (a0 + a1) lane-wise and the FADDP reduction (v0 + v1) + (v2 + v3); SiLU with libm expf and an
-// IEEE division. fc2 per channel from the bias, one FMA per r in order, then the sigmoid. The chains are sequential;
-// their loads are independent, so they are issued in batches ahead of the FMAs.
+// One CTA per WB windows (the weights are read once for all of them). fc1 row r: 8 threads hold the 8 NEON
+// accumulator lanes (a0 lanes 0-3, a1 lanes 0-3) over c = 8i + lane, then (a0 + a1) lane-wise and the FADDP reduction
+// (v0 + v1) + (v2 + v3); SiLU with libm expf and an IEEE division. fc2 per channel from the bias, one FMA per r in
+// order, then the sigmoid. Each window keeps its own chains, in the same order as alone; their weight loads are
+// shared and issued in batches ahead of the FMAs.
 constexpr int kSeThreads = 512;
-__global__ void __launch_bounds__(kSeThreads) k_se_gate(int C, int rd, const float *__restrict__ w1,
+template <int WB>
+__global__ void __launch_bounds__(kSeThreads) k_se_gate(int B, int C, int rd, const float *__restrict__ w1,
                                                         const float *__restrict__ b1, const float *__restrict__ w2t,
                                                         const float *__restrict__ b2, const float *__restrict__ chsum,
                                                         long long cws, int P, float *__restrict__ gate, long long gws) {
   extern __shared__ float sm[];
-  float *mean = sm, *s1 = sm + C;
-  const int win = blockIdx.x, tid = threadIdx.x;
+  float *mean = sm, *s1 = sm + WB * C;  // [WB][C], [WB][rd]
+  const int w0 = blockIdx.x * WB, tid = threadIdx.x;
   const float inv = __fdiv_rn(1.f, __int2float_rn(P));
-  for (int c = tid; c < C; c += kSeThreads) mean[c] = __fmul_rn(chsum[win * cws + c], inv);
+  for (int j = 0; j < WB; j++)
+    for (int c = tid; c < C; c += kSeThreads)
+      mean[j * C + c] = w0 + j < B ? __fmul_rn(chsum[(w0 + j) * cws + c], inv) : 0.f;
   __syncthreads();
   const int lane8 = tid & 7, C8 = C >> 3;
   for (int r0 = 0; r0 < rd; r0 += kSeThreads / 8) {
     const int r = r0 + tid / 8;
-    float a = 0.f;
+    float a[WB];
+#pragma unroll
+    for (int j = 0; j < WB; j++) a[j] = 0.f;
     if (r < rd) {
       const float *wr = w1 + (long long)r * C + lane8;
       const float *mr = mean + lane8;
@@ -288,33 +301,52 @@ __global__ void __launch_bounds__(kSeThreads) k_se_gate(int C, int rd, const flo
 #pragma unroll
         for (int u = 0; u < 8; u++) wv[u] = __ldg(wr + 8 * (i + u));
 #pragma unroll
-        for (int u = 0; u < 8; u++) a = __fmaf_rn(wv[u], mr[8 * (i + u)], a);
+        for (int u = 0; u < 8; u++)
+#pragma unroll
+          for (int j = 0; j < WB; j++) a[j] = __fmaf_rn(wv[u], mr[j * C + 8 * (i + u)], a[j]);
       }
-      for (; i < C8; i++) a = __fmaf_rn(__ldg(wr + 8 * i), mr[8 * i], a);
+      for (; i < C8; i++) {
+        const float wv = __ldg(wr + 8 * i);
+#pragma unroll
+        for (int j = 0; j < WB; j++) a[j] = __fmaf_rn(wv, mr[j * C + 8 * i], a[j]);
+      }
     }
-    // lanes l and l + 4 hold a0[l] and a1[l]
-    const float other = __shfl_down_sync(0xffffffffu, a, 4, 8);
-    const float v = __fadd_rn(a, other);  // v[l] for l < 4
-    const float v1 = __shfl_down_sync(0xffffffffu, v, 1, 8), v2 = __shfl_down_sync(0xffffffffu, v, 2, 8),
-                v3 = __shfl_down_sync(0xffffffffu, v, 3, 8);
-    if (r < rd && lane8 == 0) {
-      const float xr = __fadd_rn(__fadd_rn(__fadd_rn(v, v1), __fadd_rn(v2, v3)), b1[r]);
-      s1[r] = __fdiv_rn(xr, __fadd_rn(1.f, glibc_expf(-xr, c_expf_tab)));
+#pragma unroll
+    for (int j = 0; j < WB; j++) {
+      // lanes l and l + 4 hold a0[l] and a1[l]
+      const float other = __shfl_down_sync(0xffffffffu, a[j], 4, 8);
+      const float v = __fadd_rn(a[j], other);  // v[l] for l < 4
+      const float v1 = __shfl_down_sync(0xffffffffu, v, 1, 8), v2 = __shfl_down_sync(0xffffffffu, v, 2, 8),
+                  v3 = __shfl_down_sync(0xffffffffu, v, 3, 8);
+      if (r < rd && lane8 == 0) {
+        const float xr = __fadd_rn(__fadd_rn(__fadd_rn(v, v1), __fadd_rn(v2, v3)), b1[r]);
+        s1[j * rd + r] = __fdiv_rn(xr, __fadd_rn(1.f, glibc_expf(-xr, c_expf_tab)));
+      }
     }
   }
   __syncthreads();
   for (int c = tid; c < C; c += kSeThreads) {
-    float g = b2[c];
+    float g[WB];
+#pragma unroll
+    for (int j = 0; j < WB; j++) g[j] = b2[c];
     int r = 0;
     for (; r + 16 <= rd; r += 16) {
       float wv[16];
 #pragma unroll
       for (int u = 0; u < 16; u++) wv[u] = __ldg(w2t + (long long)(r + u) * C + c);
 #pragma unroll
-      for (int u = 0; u < 16; u++) g = __fmaf_rn(wv[u], s1[r + u], g);
+      for (int u = 0; u < 16; u++)
+#pragma unroll
+        for (int j = 0; j < WB; j++) g[j] = __fmaf_rn(wv[u], s1[j * rd + r + u], g[j]);
     }
-    for (; r < rd; r++) g = __fmaf_rn(__ldg(w2t + (long long)r * C + c), s1[r], g);
-    gate[win * gws + c] = sigmoid(g);
+    for (; r < rd; r++) {
+      const float wv = __ldg(w2t + (long long)r * C + c);
+#pragma unroll
+      for (int j = 0; j < WB; j++) g[j] = __fmaf_rn(wv, s1[j * rd + r], g[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < WB; j++)
+      if (w0 + j < B) gate[(w0 + j) * gws + c] = sigmoid(g[j]);
   }
 }
 
@@ -647,7 +679,7 @@ extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int
                         int *err, bnn_stream_t st) {
   if (B <= 0) return 0;
   const int P = Ho * Wo, C4 = C / 4;
-  const size_t budget = smem_budget(k_dw3t<1, 2>, 2);  // every instance has the same static shared memory
+  const size_t budget = smem_budget(k_dw3t<1, 2, true>, 2);  // every instance has the same static shared memory
   const int cg = dw3t_group(C, W, Wo, s, budget);
   PFN_cuTensorMapEncodeTiled_v12000 enc = conv_encode_fn();
   if (cg && enc && ((uintptr_t)xp & 15) == 0 && (xws * 4) % 16 == 0 && W + 2 <= 256 && (s == 1 || s == 2) &&
@@ -660,23 +692,38 @@ extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int
     if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(xp), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
-      const int nr = dw3t_ring(W, Wo, s, cg, (Ho - 1) * s + 3, budget);
+      // without channel sums (chsum NULL): bands of at least 4 output rows, enough for about 4 CTAs per SM
+      const bool sum = chsum != nullptr;
+      int nband = 1;
+      if (!sum) {
+        const long long ctas = (long long)B * (C / cg);
+        nband = (int)((4LL * num_sms() + ctas - 1) / ctas);
+        if (nband > Ho / 4) nband = Ho / 4;
+        if (nband < 1) nband = 1;
+      }
+      const int hb = (Ho + nband - 1) / nband;
+      const int nr = dw3t_ring(W, Wo, s, cg, (hb - 1) * s + 3, budget);
       const size_t smem = dw3t_smem(W, Wo, nr, cg);
-      const unsigned grid = (unsigned)B * (unsigned)(C / cg);
+      const unsigned grid = (unsigned)B * (unsigned)(C / cg) * (unsigned)nband;
       // threads: whole channel quads up to 256, at least the CG summing threads
       const int Q = cg / 4;
       int nt = (256 / Q) * Q;
       if (nt < cg) nt = cg;
       nt = (nt + 31) / 32 * 32;
       const bool pair = Wo % 2 == 0;
-#define BNN_DW3T(SS, RR)                                                                                   \
-  do {                                                                                                    \
-    cudaFuncSetAttribute(k_dw3t<SS, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);         \
-    k_dw3t<SS, RR><<<grid, nt, smem, st>>>(map, W, C, cg, Ho, Wo, nr, w, b, out, ows, chsum, cws, err);   \
+#define BNN_DW3T_(SS, RR, KS)                                                                                     \
+  do {                                                                                                             \
+    cudaFuncSetAttribute(k_dw3t<SS, RR, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);              \
+    k_dw3t<SS, RR, KS><<<grid, nt, smem, st>>>(map, W, C, cg, Ho, Wo, nr, w, b, out, ows, chsum, cws, err, nband); \
+  } while (0)
+#define BNN_DW3T(SS, RR) \
+  do {                    \
+    if (sum) BNN_DW3T_(SS, RR, true); else BNN_DW3T_(SS, RR, false); \
   } while (0)
       if (s == 1) { if (pair) BNN_DW3T(1, 2); else BNN_DW3T(1, 1); }
       else { if (pair) BNN_DW3T(2, 2); else BNN_DW3T(2, 1); }
 #undef BNN_DW3T
+#undef BNN_DW3T_
       return cudaGetLastError();
     }
   }
@@ -697,8 +744,17 @@ extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int
 extern "C" int bnnk_se_gate(int B, int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,
                             const float *chsum, long long cws, int P, float *gate, long long gws, bnn_stream_t st) {
   if (B <= 0) return 0;
-  const size_t smem = sizeof(float) * (size_t)(C + rd);
-  k_se_gate<<<B, kSeThreads, smem, st>>>(C, rd, w1, b1, w2t, b2, chsum, cws, P, gate, gws);
+  // windows per CTA: two from 256 windows on (the weights are read once per CTA; 128+ CTAs still spread over the SMs)
+  const int wb = B >= 256 ? 2 : 1;
+  const size_t smem = sizeof(float) * (size_t)wb * (C + rd);
+  if (smem > 48 * 1024) {  // wide layers: one window per CTA
+    k_se_gate<1><<<B, kSeThreads, sizeof(float) * (size_t)(C + rd), st>>>(B, C, rd, w1, b1, w2t, b2, chsum, cws, P,
+                                                                          gate, gws);
+    return cudaGetLastError();
+  }
+  const unsigned grid = (unsigned)((B + wb - 1) / wb);
+  if (wb == 2) k_se_gate<2><<<grid, kSeThreads, smem, st>>>(B, C, rd, w1, b1, w2t, b2, chsum, cws, P, gate, gws);
+  else k_se_gate<1><<<grid, kSeThreads, smem, st>>>(B, C, rd, w1, b1, w2t, b2, chsum, cws, P, gate, gws);
   return cudaGetLastError();
 }
 

@@ -1802,10 +1802,12 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
       }
       break;
     }
-    case BNN_OP_DW3:
-      rc = bnnk_dw3(n, IN_(0), INWS(0), p[0], p[1], p[2], p[3], o->f[0], o->f[1], B_(1), WS(1), p[4], p[5], B_(2), WS(2),
-                    dv->err, st);
+    case BNN_OP_DW3: { /* channel sums that no op reads are not formed in a whole-package run (debug ranges keep them) */
+      const int sums = !(op0 == 0 && op1 >= c->n_ops) || used_elsewhere(c, op->b[2], i, i);
+      rc = bnnk_dw3(n, IN_(0), INWS(0), p[0], p[1], p[2], p[3], o->f[0], o->f[1], B_(1), WS(1), p[4], p[5],
+                    sums ? B_(2) : NULL, WS(2), dv->err, st);
       break;
+    }
     case BNN_OP_SE_GATE:
       rc = bnnk_se_gate(n, p[0], p[1], o->f[0], o->f[1], o->f[2], o->f[3], IN_(0), INWS(0), p[2], B_(1), WS(1), st);
       break;

@@ -192,7 +192,8 @@ int bnn_pw_f16_run(bnn_pw_f16 *op, int B, int Mw, const void *d_x, long long xws
 void bnn_pw_f16_free(bnn_pw_f16 *op);
 
 /* DW3 (src/gemm_f32.c:398-411, dw3x3_f32), batched: d_xp [B][(H+2)(W+2)][C] (zero halo 1), d_w [9][C], d_b [C] ->
- * d_out [B][Ho Wo][C], d_chsum [B][C]. A bounded device wait that ran out is reported by bnn_cuda_op_error. */
+ * d_out [B][Ho Wo][C], d_chsum [B][C] (NULL: the channel sums are not formed, and the rows of a window are spread
+ * over several CTAs). A bounded device wait that ran out is reported by bnn_cuda_op_error. */
 int bnn_cuda_dw3(int B, const float *d_xp, long long xws, int H, int W, int C, int s, const float *d_w,
                  const float *d_b, float *d_out, long long ows, int Ho, int Wo, float *d_chsum, long long cws,
                  void *stream);

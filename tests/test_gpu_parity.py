@@ -275,6 +275,30 @@ def test_dw3(lib, H, W, C, s):
         assert bits_equal(gcs[w], c), mismatch_report(gcs[w], c)
 
 
+@pytest.mark.parametrize("H,W,C,s,B", [(24, 64, 72, 1, 3), (48, 128, 72, 2, 2), (24, 64, 72, 1, 256), (13, 9, 16, 1, 5)])
+def test_dw3_without_channel_sums(lib, H, W, C, s, B):
+    """d_chsum NULL (the whole-package form for a DW3 whose sums no op reads): the output rows are cut into bands over
+    several CTAs per window; the outputs stay the reference's bit for bit (B = 256: the benchmarked batch of the
+    v2.4 block-1 layers)"""
+    rng = np.random.default_rng(H * W + C + B)
+    Ho, Wo = (H - 1) // s + 1, (W - 1) // s + 1
+    xp = np.zeros((B, H + 2, W + 2, C), np.float32)
+    xp[:, 1:-1, 1:-1, :] = rng.standard_normal((B, H, W, C)).astype(np.float32)
+    wt = (rng.standard_normal((9, C)) * 0.4).astype(np.float32)
+    bias = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    out = torch.zeros(B * Ho * Wo * C, dtype=torch.float32, device="cuda")
+    xd, wd, bd = dev(xp), dev(wt), dev(bias)
+    rc = lib.bnn_cuda_dw3(B, xd.data_ptr(), (H + 2) * (W + 2) * C, H, W, C, s, wd.data_ptr(), bd.data_ptr(),
+                          out.data_ptr(), Ho * Wo * C, Ho, Wo, None, C, None)
+    assert rc == 0, lib.bnn_last_error()
+    got = host(out).reshape(B, -1)
+    for w in sorted({0, 1, B // 2, B - 1}):
+        o, c = np.zeros(Ho * Wo * C, np.float32), np.zeros(C, np.float32)
+        oracle.lib().bnno_dw3(oracle.ptr(xp[w]), H, W, C, s, oracle.ptr(wt), oracle.ptr(bias), oracle.ptr(o), Ho, Wo,
+                              oracle.ptr(c))
+        assert bits_equal(got[w], o), f"window {w}: " + mismatch_report(got[w], o)
+
+
 # ------------------------------------------------------------------ every op of the packages, one at a time
 
 def oracle_states(pkg, pcm):
