@@ -883,6 +883,10 @@ def main():
     ap.add_argument("--perch-ncu", type=int, metavar="B", default=0,
                     help="for profiler captures: the Perch-architecture neon-fp16 package on B windows, 3 warm-ups + 1 "
                          "step")
+    ap.add_argument("--perch8-ncu", type=int, metavar="B", default=0,
+                    help="for profiler captures: the Perch-architecture neon-int8 package on B windows, 4 steps")
+    ap.add_argument("--f16-tensor", action="store_true",
+                    help="with --f16-ncu / --perch-ncu: the fp16 package in the tensor mode (bnn_set_fp16_tensor)")
     ap.add_argument("--ncu", action="store_true",
                     help="for profiler captures: warm-up steps + one step through bnn_infer_device, no timing, no JSON")
     args = ap.parse_args()
@@ -896,7 +900,7 @@ def main():
     if args.impl == "reference":
         reference_arm(args, rank)
         return
-    if args.ncu or args.proto_ncu or args.logmel_ncu or args.f16_ncu or args.perch_ncu:
+    if args.ncu or args.proto_ncu or args.logmel_ncu or args.f16_ncu or args.perch_ncu or args.perch8_ncu:
         # profiler captures use eager launches: a run that replays the op list from CUDA graphs stopped with a driver
         # LaunchFailed under ncu (the same command exits 0 without ncu)
         os.environ["BNN_GRAPHS"] = "0"
@@ -927,10 +931,16 @@ def main():
         h.bnn_logmel_free(op)
         print(f"logmel ncu mode: 4 runs of {B} windows", flush=True)
         return
-    if args.f16_ncu or args.perch_ncu:  # an fp16 package alone, for a profiler; nothing is timed or printed
-        B = args.f16_ncu or args.perch_ncu
+    if args.f16_ncu or args.perch_ncu or args.perch8_ncu:  # a package alone, for a profiler; nothing is timed
+        B = args.f16_ncu or args.perch_ncu or args.perch8_ncu
         td = tempfile.mkdtemp()
-        if args.perch_ncu:
+        mode = 3
+        if args.perch8_ncu:
+            pkg = os.path.join(td, "perch_v2_int8.bnpk")
+            _, _, ns = synth.write_perch_int8_package(pkg, synth.perch_ir(0))
+            pcm = synth.audio(B, seed=4300, n_samples=ns, rate=synth.PERCH_SAMPLE_RATE)
+            mode = 4
+        elif args.perch_ncu:
             pkg = os.path.join(td, "perch_v2_f16s8.bnpk")
             _, _, ns = synth.make_perch_package(pkg, seed=0)
             pcm = synth.audio(B, seed=4100, n_samples=ns, rate=synth.PERCH_SAMPLE_RATE)
@@ -938,7 +948,7 @@ def main():
             pkg = os.path.join(td, "v24_full_f16.bnpk")
             synth.make_package(pkg, seed=0, path=synth.PATH_F16)
             pcm = synth.audio(B, seed=4000)
-        m = Model(pkg, mode=3, batch=B)
+        m = Model(pkg, mode=mode, batch=B, fp16_tensor=True if args.f16_tensor and mode == 3 else None)
         d_pcm = torch.from_numpy(pcm).cuda()
         d_out = torch.empty((B, m.info.n_classes), dtype=torch.float32, device="cuda")
         d_emb = torch.empty((B, m.info.emb_dim), dtype=torch.float32, device="cuda")

@@ -692,12 +692,13 @@ extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int
     if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(xp), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
-      // without channel sums (chsum NULL): bands of at least 4 output rows, enough for about 4 CTAs per SM
+      // without channel sums (chsum NULL): bands of at least 4 output rows, as many as fill the two CTAs per SM
+      // that the shared memory allows in one wave (more waves of shorter bands measured no faster)
       const bool sum = chsum != nullptr;
       int nband = 1;
       if (!sum) {
         const long long ctas = (long long)B * (C / cg);
-        nband = (int)((4LL * num_sms() + ctas - 1) / ctas);
+        nband = (int)((2LL * num_sms()) / ctas);
         if (nband > Ho / 4) nband = Ho / 4;
         if (nband < 1) nband = 1;
       }
@@ -744,8 +745,9 @@ extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int
 extern "C" int bnnk_se_gate(int B, int C, int rd, const float *w1, const float *b1, const float *w2t, const float *b2,
                             const float *chsum, long long cws, int P, float *gate, long long gws, bnn_stream_t st) {
   if (B <= 0) return 0;
-  // windows per CTA: two from 256 windows on (the weights are read once per CTA; 128+ CTAs still spread over the SMs)
-  const int wb = B >= 256 ? 2 : 1;
+  // windows per CTA: two from 512 windows on (the weights are read once per CTA; measured: Perch's 26 SE at batch
+  // 512 0.85 -> 0.65 ms, while v2.4's 13 at batch 256 went 0.26 -> 0.32 ms with 128 CTAs, so they keep one)
+  const int wb = B >= 512 ? 2 : 1;
   const size_t smem = sizeof(float) * (size_t)wb * (C + rd);
   if (smem > 48 * 1024) {  // wide layers: one window per CTA
     k_se_gate<1><<<B, kSeThreads, sizeof(float) * (size_t)(C + rd), st>>>(B, C, rd, w1, b1, w2t, b2, chsum, cws, P,
