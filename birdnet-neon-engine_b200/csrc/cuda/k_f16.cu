@@ -408,7 +408,8 @@ __host__ __device__ constexpr uint32_t idesc_f16(int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-__global__ void __launch_bounds__(kT16Threads, 1) k_gemm_tc16(const __grid_constant__ CUtensorMap tma_a,
+template <int kThreads>  // 64 + 256 nh: the registers a thread may use follow the block size
+__global__ void __launch_bounds__(kThreads, 1) k_gemm_tc16(const __grid_constant__ CUtensorMap tma_a,
                                                               const __grid_constant__ CUtensorMap tma_b,
                                                               const Tc16Args a) {
   extern __shared__ uint8_t dsmem[];
@@ -1494,7 +1495,8 @@ extern "C" int bnnk_gemm_tc16(int B, int Mw, const uint16_t *A, long long aws, i
   a.tiles = (int)(mtiles * a.n_tiles);
   a.acc_cols = a.bn <= 32 ? 32 : a.bn <= 64 ? 64 : a.bn <= 128 ? 128 : 256;
   a.tmem_alloc = 2 * a.acc_cols < 32 ? 32 : 2 * a.acc_cols;
-  a.nh = 3;
+  const char *enh = getenv("BNN_TC16_NH");  // epilogue warps per TMEM lane quarter and accumulator (tuning: 2 or 3)
+  a.nh = enh && atoi(enh) == 2 ? 2 : 3;
   a.idesc = idesc_f16(a.bn);
   a.b32 = b32;
   a.act = act;
@@ -1527,11 +1529,17 @@ extern "C" int bnnk_gemm_tc16(int B, int Mw, const uint16_t *A, long long aws, i
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  static SmemAttr attr;
-  const cudaError_t e = attr.ensure(k_gemm_tc16, smem);
-  if (e) return e;
+  static SmemAttr attr3, attr2;
   const int grid = a.tiles < num_sms() ? a.tiles : num_sms();
-  k_gemm_tc16<<<grid, kT16Threads, smem, st>>>(ma, mb, a);
+  if (a.nh == 2) {
+    const cudaError_t e = attr2.ensure(k_gemm_tc16<64 + 128 * 2 * 2>, smem);
+    if (e) return e;
+    k_gemm_tc16<64 + 128 * 2 * 2><<<grid, 64 + 128 * 2 * 2, smem, st>>>(ma, mb, a);
+  } else {
+    const cudaError_t e = attr3.ensure(k_gemm_tc16<kT16Threads>, smem);
+    if (e) return e;
+    k_gemm_tc16<kT16Threads><<<grid, kT16Threads, smem, st>>>(ma, mb, a);
+  }
   return cudaGetLastError();
 }
 

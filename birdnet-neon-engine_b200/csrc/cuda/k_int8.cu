@@ -110,10 +110,6 @@ __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__
   }
 }
 
-// Wide rows (K >= 128): one warp per row, lane l holding the float4 groups l, l + 32, ... (NG of them) of the row in
-// registers: fully coalesced 512-byte loads, the min / max reduced across the warp by shuffles, each group's 4
-// quantized bytes stored as one word (128-byte warp stores). A warp walks RPW consecutive rows and keeps the SE gate
-// of the current window in registers, reloading it only when the window changes.
 template <int NG, bool kGate>
 __global__ void __launch_bounds__(256) k_quant_w(int rows, int Mw, const float *__restrict__ x, long long xws, int lda,
                                                  int K, int Kq, const float *__restrict__ gate, long long gws,
@@ -162,6 +158,86 @@ __global__ void __launch_bounds__(256) k_quant_w(int rows, int Mw, const float *
         if (kGate) {
           const float2 p0 = mul2_rn(make_float2(t.x, t.y), make_float2(gv[i].x, gv[i].y));
           const float2 p1 = mul2_rn(make_float2(t.z, t.w), make_float2(gv[i].z, gv[i].w));
+          t = make_float4(p0.x, p0.y, p1.x, p1.y);
+        }
+        v[i] = t;
+        lo = fmin_nan(lo, fmin_nan(fmin_nan(t.x, t.y), fmin_nan(t.z, t.w)));
+        hi = fmax_nan(hi, fmax_nan(fmax_nan(t.x, t.y), fmax_nan(t.z, t.w)));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      lo = fmin_nan(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = fmax_nan(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    float inv, s;
+    int32_t z;
+    quant_params(lo, hi, inv, z, s);
+    if (lane == 0) { sa[r] = s; za[r] = z; }
+    uint32_t *qr = reinterpret_cast<uint32_t *>(q + (long long)r * Kq);
+    const float2 inv2 = splat2(inv);
+#pragma unroll
+    for (int i = 0; i < NG; i++) {
+      const int g = lane + 32 * i;
+      if (g < K4) {
+        const float2 p0 = mul2_rn(make_float2(v[i].x, v[i].y), inv2);
+        const float2 p1 = mul2_rn(make_float2(v[i].z, v[i].w), inv2);
+        qr[g] = quant_word(p0.x, p0.y, p1.x, p1.y, z, 4 * g < K8);
+      } else if (g < Kq4) {
+        qr[g] = ((uint32_t)z & 0xffu) * 0x01010101u;  // pads past K: the zero point
+      }
+    }
+    if (Kq4 > 32 * NG) {  // pads beyond the register groups (never for Kq = K rounded up to 32)
+      for (int g = 32 * NG + lane; g < Kq4; g += 32) qr[g] = ((uint32_t)z & 0xffu) * 0x01010101u;
+    }
+  }
+}
+
+// The same with the loads of the next two rows in flight and the SE gate read with the row it scales (the same gate
+// serves every row of a window, so these loads hit L1): for gated rows of 288 (measured 52.7 -> 49.5 µs per 98k rows;
+// on wider rows the extra registers cost more occupancy than the deeper prefetch gained).
+template <int NG, bool kGate>
+__global__ void __launch_bounds__(256) k_quant_w2(int rows, int Mw, const float *__restrict__ x, long long xws, int lda,
+                                                 int K, int Kq, const float *__restrict__ gate, long long gws,
+                                                 int8_t *__restrict__ q, float *__restrict__ sa,
+                                                 int32_t *__restrict__ za, int rpw) {
+  const int lane = threadIdx.x % 32;
+  const int wrp = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) / 32);
+  const int r0 = wrp * rpw, r1 = min(rows, r0 + rpw);
+  const int K4 = K >> 2, Kq4 = Kq >> 2, K8 = K & ~7;
+  // rows r + 1 and r + 2 are loaded before row r is reduced and quantized
+  float4 vn[2][NG];
+  auto load_row = [&](int r, float4 (&dst)[NG]) {
+    const int w = r / Mw, m = r - w * Mw;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + w * xws + (long long)m * lda);
+#pragma unroll
+    for (int i = 0; i < NG; i++) {
+      const int g = lane + 32 * i;
+      if (g < K4) dst[i] = __ldg(xr + g);
+    }
+  };
+  if (r0 < r1) load_row(r0, vn[0]);
+  if (r0 + 1 < r1) load_row(r0 + 1, vn[1]);
+  for (int r = r0; r < r1; r++) {
+    const int w = r / Mw;
+    float4 v[NG];
+#pragma unroll
+    for (int i = 0; i < NG; i++) {
+      v[i] = vn[0][i];
+      vn[0][i] = vn[1][i];
+    }
+    if (r + 2 < r1) load_row(r + 2, vn[1]);
+    const float4 *gp = kGate ? reinterpret_cast<const float4 *>(gate + w * gws) : nullptr;
+    float lo = __int_as_float(0x7f800000), hi = __int_as_float(0xff800000);
+#pragma unroll
+    for (int i = 0; i < NG; i++) {
+      const int g = lane + 32 * i;
+      if (g < K4) {
+        float4 t = v[i];
+        if (kGate) {
+          const float4 gg = __ldg(gp + g);
+          const float2 p0 = mul2_rn(make_float2(t.x, t.y), make_float2(gg.x, gg.y));
+          const float2 p1 = mul2_rn(make_float2(t.z, t.w), make_float2(gg.z, gg.w));
           t = make_float4(p0.x, p0.y, p1.x, p1.y);
         }
         v[i] = t;
@@ -411,9 +487,10 @@ __device__ __forceinline__ void quant_units(const GemmArgs &a, int row, const fl
 }
 
 // kSP: the per-column parameters (sw, bias, cs; np <= kSPMax columns) are staged in shared memory once per CTA;
-// kQ: the epilogue also quantizes the stored rows for the next layer (a.e.qo)
-template <int SW, bool kSP, bool kQ>
-__global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constant__ CUtensorMap tma_a,
+// kQ: the epilogue also quantizes the stored rows for the next layer (a.e.qo); kThreads: the block size the registers
+// are budgeted for (832: 72 registers a thread; 576, two epilogue warps per TMEM lane quarter and accumulator: 112)
+template <int SW, bool kSP, bool kQ, int kThreads = kMaxThreads>
+__global__ void __launch_bounds__(kThreads, 1) k_gemm_s8(const __grid_constant__ CUtensorMap tma_a,
                                                            const __grid_constant__ CUtensorMap tma_b,
                                                            const GemmArgs a) {
   extern __shared__ uint8_t dsmem[];
@@ -548,6 +625,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
       const int32_t *qcs = kSP ? p_cs + n0 : a.e.cs + n0;
       const uint32_t tq = tmem + (uint32_t)(g * a.acc_cols) + ((uint32_t)(q * 32) << 16);
       float lo = __uint_as_float(0x7f800000u), hi = __uint_as_float(0xff800000u);
+      // a tile whose units take one pass frees its accumulator as soon as the loads are in registers, so the next
+      // tile's MMAs overlap the arithmetic
+      const bool single = units <= kEpiUnits * a.nh;
       for (int u0 = h; u0 < units; u0 += kEpiUnits * a.nh) {
         uint32_t acc[kEpiUnits][8];
 #pragma unroll
@@ -556,6 +636,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
           if (u < units) tmem_ld8(tq + (uint32_t)(8 * u), acc[k]);
         }
         tmem_wait(acc);
+        if (single) {
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[g]));
+        }
         if (live) {
           if (u0 + (kEpiUnits - 1) * a.nh < units) {  // every unit of the batch is a real column block
             epilogue_act<kEpiUnits, kQ>(a, acc, 0, u0, a.nh, sa, za, qsw, qb, qcs, orow, rrow, s_lut, lo, hi);
@@ -567,9 +652,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemm_s8(const __grid_constan
           }
         }
       }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[g]));
+      if (!single || h >= units) {  // after the last pass, or a warp with no unit in this tile
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[g]));
+      }
       if (fq) {
         // the row's min / max from its nh threads' partials (the barrier orders their shared stores before the reads;
         // a warp whose wait failed arrives with false and all leave), then this thread's units quantized
@@ -663,7 +750,8 @@ extern "C" int bnnk_quant(int rows, int Mw, const float *x, long long xws, int l
     const int warps = (rows + rpw - 1) / rpw;
     const unsigned grid = (unsigned)((warps + 7) / 8);
 #define BNN_QW(NGV)                                                                                           \
-  if (gate) k_quant_w<NGV, true><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw); \
+  if (gate && NGV == 3) k_quant_w2<3, true><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw); \
+  else if (gate) k_quant_w<NGV, true><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw); \
   else k_quant_w<NGV, false><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw)
     switch (ng) {  // K in [128, 1024]: 1 .. 8 float4 groups per lane
     case 1: BNN_QW(1); break;
@@ -772,11 +860,13 @@ static int tmem_pow2(int cols) {
   return c;
 }
 
-// epilogue shape: the widest epilogue that the thread limit allows with at least two accumulators, so that the MMA
-// of the next tile overlaps the epilogue of the last
+// epilogue shape: two accumulators (the MMAs of the next tile overlap the epilogue of the last) with two warps per
+// TMEM lane quarter each: 576 threads, whose 112 registers a thread keep the epilogue's values and parameters in
+// registers (at three warps, 832 threads and 72 registers, it spilled and reloaded kernel parameters: the v2.4 step's
+// PW_S8 ops measured 2390 -> 2357 µs with two)
 static void epi_shape(int tmem_cols, int *ne, int *nh) {
   const int e = 2;  // tmem_cols <= 256: two accumulators always fit the 512 columns
-  const int h = (kMaxThreads - 64) / (128 * e);
+  const int h = 2;
   const char *env = getenv("BNN_GEMM_EPI");  // "ne,nh" override for tuning sweeps
   int ee = 0, hh = 0;
   if (env && sscanf(env, "%d,%d", &ee, &hh) == 2 && ee >= 1 && ee <= kMaxEpi && tmem_pow2(ee * tmem_cols) <= 512 &&
@@ -816,16 +906,21 @@ extern "C" int bnnk_gemm_plan_init(bnnk_gemm_plan *p, const int8_t *q, int rows_
   return e;
 }
 
-template <int SW, bool kSP, bool kQ>
-static int launch_gemm_q(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
+template <int SW, bool kSP, bool kQ, int kThreads>
+static int launch_gemm_t(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
   // the dynamic shared memory this instantiation may use so far, per device (static + dynamic <= 227 KB)
   static SmemAttr attr;
-  const cudaError_t e = attr.ensure(k_gemm_s8<SW, kSP, kQ>, p->smem);
+  const cudaError_t e = attr.ensure(k_gemm_s8<SW, kSP, kQ, kThreads>, p->smem);
   if (e) return e;
   const int grid = a.tiles < num_sms() ? a.tiles : num_sms();
-  k_gemm_s8<SW, kSP, kQ><<<grid, 64 + 128 * a.ne * a.nh, p->smem, st>>>(*(const CUtensorMap *)p->tma_a,
-                                                                        *(const CUtensorMap *)p->tma_b, a);
+  k_gemm_s8<SW, kSP, kQ, kThreads><<<grid, 64 + 128 * a.ne * a.nh, p->smem, st>>>(
+      *(const CUtensorMap *)p->tma_a, *(const CUtensorMap *)p->tma_b, a);
   return cudaGetLastError();
+}
+template <int SW, bool kSP, bool kQ>
+static int launch_gemm_q(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {
+  if (!kQ && 64 + 128 * a.ne * a.nh <= 576) return launch_gemm_t<SW, kSP, false, 576>(p, a, st);
+  return launch_gemm_t<SW, kSP, kQ, kMaxThreads>(p, a, st);
 }
 template <int SW, bool kSP>
 static int launch_gemm(const bnnk_gemm_plan *p, const GemmArgs &a, bnn_stream_t st) {

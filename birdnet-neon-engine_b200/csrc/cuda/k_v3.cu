@@ -554,12 +554,14 @@ __global__ void __launch_bounds__(256, 2) k_gemm_f32t(const F32GemmArgs g, int r
   }
 }
 
-// the tile shape whose padded width covers Np with the fewest columns (ties: the wider tile)
+// the tile width with the least padded work, counting the narrower tiles' extra shared-memory reads per FMA: a
+// 128-wide tile (8 x 8 per thread) at full rate, 64 (8 x 4) at 0.8, 32 (16 x 2) at 0.6 (a 96-channel layer on
+// 32-wide tiles ran at half the FMA rate of the 128-wide ones)
 template <int SRC>
 static int launch_gemm_f32t(int B, const F32GemmArgs &g, bnn_stream_t st) {
   const long long rows = (long long)B * g.M;
-  const int w128 = (g.Np + 127) / 128 * 128, w64 = (g.Np + 63) / 64 * 64, w32 = (g.Np + 31) / 32 * 32;
-  const int bn = w128 <= w64 && w128 <= w32 ? 128 : w64 <= w32 ? 64 : 32;
+  const double c128 = (g.Np + 127) / 128 * 128, c64 = (g.Np + 63) / 64 * 64 / 0.8, c32 = (g.Np + 31) / 32 * 32 / 0.6;
+  const int bn = c128 <= c64 && c128 <= c32 ? 128 : c64 <= c32 ? 64 : 32;
   const int bm = bn == 32 ? 256 : 128;
   const int nt = (g.Np + bn - 1) / bn;
   const long long blocks = (rows + bm - 1) / bm * nt;
