@@ -308,16 +308,20 @@ constexpr int kMaxStages = 8, kMaxEpi = 4;
 constexpr int kMaxThreads = 832;  // 2 + 24 warps: 64 + 128 * ne * nh with ne * nh <= 6
 constexpr int kSPMax = 1536;      // widest layer whose epilogue parameters are staged in shared memory
 
-constexpr int kEpiUnits = 3;  // 8-column TMEM loads in flight per epilogue warp
+constexpr int kEpiUnits = 3;  // 8-column TMEM loads in flight per epilogue warp (832-thread blocks; 576: kEpiUnits2)
+constexpr int kEpiUnits2 = 3;  // (5 measured slower: 2357 -> 2470 µs per v2.4 step)
 // the epilogue's per-row partial (min, max) for the next layer's quantizer: 2 tile parities x 6 warps of 128 rows
 constexpr size_t kQPartBytes = 2 * 6 * 128 * sizeof(float2);
 // wait for this thread's TMEM loads; the registers they fill are operands of the wait, so no use moves above it
-__device__ __forceinline__ void tmem_wait(uint32_t (&r)[kEpiUnits][8]) {
 #define BNN_R8(u) "+r"(r[u][0]), "+r"(r[u][1]), "+r"(r[u][2]), "+r"(r[u][3]), "+r"(r[u][4]), "+r"(r[u][5]), \
                   "+r"(r[u][6]), "+r"(r[u][7])
+__device__ __forceinline__ void tmem_wait(uint32_t (&r)[3][8]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" : BNN_R8(0), BNN_R8(1), BNN_R8(2)::"memory");
-#undef BNN_R8
 }
+__device__ __forceinline__ void tmem_wait(uint32_t (&r)[5][8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : BNN_R8(0), BNN_R8(1), BNN_R8(2), BNN_R8(3), BNN_R8(4)::"memory");
+}
+#undef BNN_R8
 __device__ __forceinline__ void ld8_global(const float *p, float (&v)[8]) {
   asm volatile("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
@@ -351,8 +355,8 @@ __device__ __forceinline__ long long padded_row(int m, int w, int pad) {
 // (RES), store; VEC: 32-byte aligned rows (8-float loads and stores). Branch-free for fixed template arguments, so
 // the units' independent chains can overlap. psw / pb / pcs point at the tile's first column of the per-column
 // parameters (shared or global memory).
-template <int ACT, bool RES, bool VEC, int NU, bool kQ = false>
-__device__ __forceinline__ void epilogue_units(const uint32_t (&acc)[kEpiUnits][8], int kofs, int u0, int nh, float sa,
+template <int ACT, bool RES, bool VEC, int NU, bool kQ, int EU>
+__device__ __forceinline__ void epilogue_units(const uint32_t (&acc)[EU][8], int kofs, int u0, int nh, float sa,
                                                int32_t za, const float *psw, const float *pb, const int32_t *pcs,
                                                float *orow, const float *rrow, const uint32_t *lut, float &lo,
                                                float &hi, int qk) {
@@ -403,22 +407,22 @@ __device__ __forceinline__ void epilogue_units(const uint32_t (&acc)[kEpiUnits][
   }
 }
 
-template <int NU, bool kQ>
-__device__ __forceinline__ void epilogue_act(const GemmArgs &a, const uint32_t (&acc)[kEpiUnits][8], int kofs, int u0,
+template <int NU, bool kQ, int EU>
+__device__ __forceinline__ void epilogue_act(const GemmArgs &a, const uint32_t (&acc)[EU][8], int kofs, int u0,
                                              int nh, float sa, int32_t za, const float *psw, const float *pb,
                                              const int32_t *pcs, float *orow, const float *rrow, const uint32_t *lut,
                                              float &lo, float &hi) {
 #define BNN_E(ACT, RES, VEC) \
-  epilogue_units<ACT, RES, VEC, NU>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut, lo, hi, 0)
+  epilogue_units<ACT, RES, VEC, NU, false, EU>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut, lo, hi, 0)
   const bool vec = a.vec_out && (!rrow || a.vec_res);
   if (kQ) {  // the rows also quantized for the next layer: linear layers (the host's rule)
-    if (rrow && vec) epilogue_units<0, true, true, NU, true>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut,
+    if (rrow && vec) epilogue_units<0, true, true, NU, true, EU>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut,
                                                              lo, hi, a.e.qk);
-    else if (rrow) epilogue_units<0, true, false, NU, true>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut,
+    else if (rrow) epilogue_units<0, true, false, NU, true, EU>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut,
                                                             lo, hi, a.e.qk);
-    else if (vec) epilogue_units<0, false, true, NU, true>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut,
+    else if (vec) epilogue_units<0, false, true, NU, true, EU>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut,
                                                            lo, hi, a.e.qk);
-    else epilogue_units<0, false, false, NU, true>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut, lo, hi,
+    else epilogue_units<0, false, false, NU, true, EU>(acc, kofs, u0, nh, sa, za, psw, pb, pcs, orow, rrow, lut, lo, hi,
                                                    a.e.qk);
     return;
   }
@@ -627,11 +631,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_s8(const __grid_constant__
       float lo = __uint_as_float(0x7f800000u), hi = __uint_as_float(0xff800000u);
       // a tile whose units take one pass frees its accumulator as soon as the loads are in registers, so the next
       // tile's MMAs overlap the arithmetic
-      const bool single = units <= kEpiUnits * a.nh;
-      for (int u0 = h; u0 < units; u0 += kEpiUnits * a.nh) {
-        uint32_t acc[kEpiUnits][8];
+      constexpr int EU = kThreads == kMaxThreads ? kEpiUnits : kEpiUnits2;  // units in flight
+      const bool single = units <= EU * a.nh;
+      for (int u0 = h; u0 < units; u0 += EU * a.nh) {
+        uint32_t acc[EU][8];
 #pragma unroll
-        for (int k = 0; k < kEpiUnits; k++) {
+        for (int k = 0; k < EU; k++) {
           const int u = u0 + k * a.nh;
           if (u < units) tmem_ld8(tq + (uint32_t)(8 * u), acc[k]);
         }
@@ -642,13 +647,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_s8(const __grid_constant__
           if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[g]));
         }
         if (live) {
-          if (u0 + (kEpiUnits - 1) * a.nh < units) {  // every unit of the batch is a real column block
-            epilogue_act<kEpiUnits, kQ>(a, acc, 0, u0, a.nh, sa, za, qsw, qb, qcs, orow, rrow, s_lut, lo, hi);
+          if (u0 + (EU - 1) * a.nh < units) {  // every unit of the batch is a real column block
+            epilogue_act<EU, kQ, EU>(a, acc, 0, u0, a.nh, sa, za, qsw, qb, qcs, orow, rrow, s_lut, lo, hi);
           } else {
 #pragma unroll
-            for (int k = 0; k < kEpiUnits; k++)
+            for (int k = 0; k < EU; k++)
               if (u0 + k * a.nh < units)
-                epilogue_act<1, kQ>(a, acc, k, u0 + k * a.nh, a.nh, sa, za, qsw, qb, qcs, orow, rrow, s_lut, lo, hi);
+                epilogue_act<1, kQ, EU>(a, acc, k, u0 + k * a.nh, a.nh, sa, za, qsw, qb, qcs, orow, rrow, s_lut, lo, hi);
           }
         }
       }

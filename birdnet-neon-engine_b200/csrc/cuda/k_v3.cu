@@ -198,24 +198,25 @@ __global__ void k_dwk_f32(int B, int W, int C, int k, int s, int pt, int pl, con
 }
 
 // The same op with a channel pair per thread and the map's rows over the CTA's thread rows: CTA (Lc channel pairs,
-// window) of Lc x (Ry + 1) threads. Thread (lane, y < Ry) computes output rows y, y + Ry, ... (one per chunk of Ry
-// rows) of its pair, unit by unit in the reference's order (blocks of four pixels, then the tail pixels), stores them
+// window) of Lc x (Ry + 1) threads. Thread (lane, y < Ry) computes RT consecutive output rows of each chunk of Ry RT
+// rows (RT > 1 on short rows) of its pair, unit by unit in the reference's order (blocks of four pixels, then the tail
+// pixels), stores them
 // and leaves each unit's addend in a double-buffered shared tile; thread row Ry adds the previous chunk's addends in
 // row, then unit order (the raster order of the reference's channel sums) while the others compute the next chunk.
 // The tap weights sit in shared memory; a block reads each tap row's 3 s + K inputs once. The tap chains are paired
 // fused multiply-adds (each lane an IEEE FMA); the addends, sums of SiLU products, are scalar adds.
 template <int K, int S, int G>
-__device__ __forceinline__ float2 dwk2_unit(const float2 *xr, long long rs, long long cs, const float2 *ws, int wl,
-                                           float2 b, int act, const uint32_t *lut, float2 *o, long long os) {
+__device__ __forceinline__ float2 dwk2_unit(const float2 *xr, int rs, int cs, const float2 *ws, int wl, float2 b,
+                                           int act, const uint32_t *lut, float2 *o, int os) {
   constexpr int NX = (G - 1) * S + K;
   float2 a[G], e[G];
 #pragma unroll
   for (int q = 0; q < G; q++) { a[q] = b; e[q] = make_float2(0.f, 0.f); }
 #pragma unroll
-  for (int ky = 0; ky < K; ky++) {
+  for (int ky = 0; ky < K; ky++, xr += rs) {  // 32-bit offsets inside a window's rows
     float2 xv[NX];
 #pragma unroll
-    for (int j = 0; j < NX; j++) xv[j] = __ldg(xr + ky * rs + j * cs);
+    for (int j = 0; j < NX; j++) xv[j] = __ldg(xr + j * cs);
 #pragma unroll
     for (int kx = 0; kx < K; kx++) {
       const int t = ky * K + kx;
@@ -244,8 +245,9 @@ template <int K, int S>
 __global__ void __launch_bounds__(256, 3) k_dwk2_f32(const float *__restrict__ xp, long long xws, int W, int C, int pt,
                                                   int pl, const float *__restrict__ wt, const float *__restrict__ bias,
                                                   int act, float *__restrict__ out, long long ows, int Ho, int Wo,
-                                                  int nu, float *__restrict__ chsum, long long cws) {
-  extern __shared__ float2 sd2[];  // [K K][Lc] tap weights, then [2][Ry nu][Lc] unit addends of two chunks
+                                                  int nu, int RT, float *__restrict__ chsum, long long cws) {
+  // RT: consecutive rows per thread and chunk (short rows: more work between the chunk barriers)
+  extern __shared__ float2 sd2[];  // [K K][Lc] tap weights, then [2][Ry RT nu][Lc] unit addends of two chunks
   __shared__ uint32_t lut[256];
   constexpr int KK = K * K, h = (K - 1) / 2;
   const int Lc = blockDim.x, Ry = blockDim.y - 1, lane = threadIdx.x, win = blockIdx.y;
@@ -253,7 +255,7 @@ __global__ void __launch_bounds__(256, 3) k_dwk2_f32(const float *__restrict__ x
   const int c2 = blockIdx.x * Lc + lane, C2 = C / 2;
   const bool on = c2 < C2, summer = threadIdx.y == Ry;
   float2 *ws = sd2, *sg = sd2 + KK * Lc;
-  const int tile = Ry * nu * Lc;
+  const int CR = Ry * RT, tile = CR * nu * Lc;  // rows per chunk
   for (int i = tid; i < 256; i += nthr) lut[i] = g_frecpe_lut[i];
   for (int t = threadIdx.y; t < KK; t += blockDim.y)
     ws[t * Lc + lane] = on ? __ldg(reinterpret_cast<const float2 *>(wt) + (long long)t * C2 + c2) : make_float2(0.f, 0.f);
@@ -261,27 +263,29 @@ __global__ void __launch_bounds__(256, 3) k_dwk2_f32(const float *__restrict__ x
   __syncthreads();
   const float2 *x = reinterpret_cast<const float2 *>(xp + win * xws) + c2;
   float2 *o = reinterpret_cast<float2 *>(out + win * ows) + c2;
-  const long long cs = C2, rs = (long long)(W + 2 * h) * C2;
+  const int cs = C2, rs = (W + 2 * h) * C2;  // pair strides of a pixel and an input row
   float sm0 = 0.f, sm1 = 0.f;
-  const int nch = (Ho + Ry - 1) / Ry;
+  const int nch = (Ho + CR - 1) / CR;
   for (int ci = 0; ci <= nch; ci++) {
     if (!summer) {
-      const int oy = ci * Ry + threadIdx.y;
-      if (ci < nch && on && oy < Ho) {
-        const float2 *xr = x + (long long)(oy * S - pt + h) * rs;
-        float2 *orow = o + (long long)oy * Wo * cs;
-        float2 *g = sg + (ci & 1) * tile + threadIdx.y * nu * Lc + lane;
-        int ox = 0, gi = 0;
-        for (; ox + 4 <= Wo; ox += 4, gi++)
-          g[gi * Lc] = dwk2_unit<K, S, 4>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, ws + lane, Lc, b, act, lut,
-                                          orow + ox * cs, cs);
-        for (; ox < Wo; ox++, gi++)
-          g[gi * Lc] = dwk2_unit<K, S, 1>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, ws + lane, Lc, b, act, lut,
-                                          orow + ox * cs, cs);
+      for (int r = 0; r < RT; r++) {
+        const int yl = threadIdx.y * RT + r, oy = ci * CR + yl;  // row yl of the chunk
+        if (ci < nch && on && oy < Ho) {
+          const float2 *xr = x + (long long)(oy * S - pt + h) * rs;
+          float2 *orow = o + (long long)oy * Wo * cs;
+          float2 *g = sg + (ci & 1) * tile + yl * nu * Lc + lane;
+          int ox = 0, gi = 0;
+          for (; ox + 4 <= Wo; ox += 4, gi++)
+            g[gi * Lc] = dwk2_unit<K, S, 4>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, ws + lane, Lc, b, act, lut,
+                                            orow + ox * cs, cs);
+          for (; ox < Wo; ox++, gi++)
+            g[gi * Lc] = dwk2_unit<K, S, 1>(xr + (long long)(ox * S - pl + h) * cs, rs, cs, ws + lane, Lc, b, act, lut,
+                                            orow + ox * cs, cs);
+        }
       }
     } else if (ci > 0 && on) {  // the previous chunk's addends, row order then unit order
       const float2 *gs = sg + ((ci - 1) & 1) * tile + lane;
-      const int n = min(Ry, Ho - (ci - 1) * Ry) * nu;
+      const int n = min(CR, Ho - (ci - 1) * CR) * nu;
       for (int i = 0; i < n; i++) {
         const float2 r = gs[i * Lc];
         sm0 = __fadd_rn(sm0, r.x);
@@ -834,9 +838,13 @@ extern "C" int bnnk_dwk_f32(int B, const float *xp, long long xws, int H, int W,
     int Ry = 256 / Lc - 1;
     if (Ry > Ho) Ry = Ho;
     if (Ry < 1) Ry = 1;
-    auto smem_of = [&](int ry) { return (size_t)(k * k + 2 * ry * nu) * Lc * 8; };
-    while (Ry > 1 && smem_of(Ry) > 48 * 1024) Ry--;
-    const size_t smem = smem_of(Ry);
+    // rows per thread and chunk: about 8 units of work between the chunk barriers, no more rows than the map has
+    int RT = (8 + nu - 1) / nu;
+    while (RT > 1 && Ry * RT > Ho + Ry - 1) RT--;
+    auto smem_of = [&](int ry, int rt) { return (size_t)(k * k + 2 * ry * rt * nu) * Lc * 8; };
+    while (RT > 1 && smem_of(Ry, RT) > 48 * 1024) RT--;
+    while (Ry > 1 && smem_of(Ry, RT) > 48 * 1024) Ry--;
+    const size_t smem = smem_of(Ry, RT);
     if (smem <= 96 * 1024) {
       const dim3 grid((unsigned)((C2 + Lc - 1) / Lc), (unsigned)B), blk((unsigned)Lc, (unsigned)(Ry + 1));
 #define BNN_DWK2(KK, SS)                                                                                        \
@@ -844,7 +852,8 @@ extern "C" int bnnk_dwk_f32(int B, const float *xp, long long xws, int H, int W,
     static SmemAttr attr_;                                                                                      \
     const cudaError_t e_ = attr_.ensure(k_dwk2_f32<KK, SS>, smem);                                             \
     if (e_) return e_;                                                                                          \
-    k_dwk2_f32<KK, SS><<<grid, blk, smem, st>>>(xp, xws, W, C, pt, pl, w, b, act, out, ows, Ho, Wo, nu, chsum, cws); \
+    k_dwk2_f32<KK, SS><<<grid, blk, smem, st>>>(xp, xws, W, C, pt, pl, w, b, act, out, ows, Ho, Wo, nu, RT, chsum,  \
+                                               cws);                                                            \
   } while (0)
       if (k == 3) { if (s == 1) BNN_DWK2(3, 1); else BNN_DWK2(3, 2); }
       else if (k == 5) { if (s == 1) BNN_DWK2(5, 1); else BNN_DWK2(5, 2); }

@@ -229,6 +229,8 @@ CASES = {
     # 32 channel pairs per CTA with a ragged last CTA, several chunks of rows per window
     "dwk_k5_s1_c72": (pkg_dwk, dict(k=5, s=1, H=13, W=11, C=72)),
     "dwk_k3_s2_c40": (pkg_dwk, dict(k=3, s=2, H=17, W=19, C=40)),
+    # short rows, several rows per thread and chunk, two chunks of 28 rows
+    "dwk_k5_s1_tall": (pkg_dwk, dict(k=5, s=1, H=40, W=8, C=64)),
     "stem": (pkg_stem, {}),
     "stem_relu_nohalo": (pkg_stem, dict(act=2, opad=0, N=16, k=5, s=1, H=12, W=11)),
     "convk_s1_res": (pkg_convk, {}),
