@@ -410,7 +410,7 @@ static int launch_gemm_f32(int B, const F32GemmArgs &g, bnn_stream_t st) {
 constexpr int kTK = 16;
 
 template <int TM, int TN, int SRC>
-__global__ void __launch_bounds__(256, 2) k_gemm_f32t(const F32GemmArgs g, int rows, int n_tiles) {
+__global__ void __launch_bounds__(256, TM == 4 ? 4 : 2) k_gemm_f32t(const F32GemmArgs g, int rows, int n_tiles) {
   constexpr bool GATED = SRC == kSrcGated, IM2COL = SRC == kSrcIm2col;
   constexpr int BM = 16 * TM, BN = 16 * TN, AP = BM + 4;
   constexpr int AV = BM / 64;                   // float4 loads of A (and of the gate) per thread per step
@@ -566,11 +566,15 @@ static int launch_gemm_f32t(int B, const F32GemmArgs &g, bnn_stream_t st) {
   const long long rows = (long long)B * g.M;
   const double c128 = (g.Np + 127) / 128 * 128, c64 = (g.Np + 63) / 64 * 64 / 0.8, c32 = (g.Np + 31) / 32 * 32 / 0.6;
   const int bn = c128 <= c64 && c128 <= c32 ? 128 : c64 <= c32 ? 64 : 32;
-  const int bm = bn == 32 ? 256 : 128;
+  // narrow layers with short rows (K <= 64: a few multiply-adds per loaded byte) are bound by memory latency, not
+  // by the FMA pipe: 64-row tiles, few registers, many CTAs per SM
+  const bool small = bn == 32 && g.Kp <= 64;
+  const int bm = small ? 64 : bn == 32 ? 256 : 128;
   const int nt = (g.Np + bn - 1) / bn;
   const long long blocks = (rows + bm - 1) / bm * nt;
   if (rows > 0x7fffffffLL || blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
-  if (bn == 128) k_gemm_f32t<8, 8, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
+  if (small) k_gemm_f32t<4, 2, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
+  else if (bn == 128) k_gemm_f32t<8, 8, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
   else if (bn == 64) k_gemm_f32t<8, 4, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
   else k_gemm_f32t<16, 2, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
   return cudaGetLastError();
