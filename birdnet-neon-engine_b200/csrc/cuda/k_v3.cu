@@ -326,6 +326,7 @@ struct F32GemmArgs {
   const float *res;
   long long rws;
   int ldr, rw, rpad;
+  int vec;  // the tiled form's output (and residual) rows take VW-float vector accesses
 };
 
 __device__ __forceinline__ long long pad_row(int m, int w, int pad) {
@@ -540,6 +541,9 @@ __global__ void __launch_bounds__(256, TM == 4 ? 4 : 2) k_gemm_f32t(const F32Gem
   }
 
   // epilogue (epi32): + bias, activation, residual, the padded output row
+  // a thread's columns come in runs of VW (2 for TN = 2, else 4) that are stored (and read from the residual) as one
+  // vector when g.vec allows it (rows, window strides and base pointers aligned to VW floats)
+  constexpr int VW = TN == 2 ? 2 : TN == 8 ? 1 : 4;
 #pragma unroll
   for (int i = 0; i < TM; i++) {
     const long long r = r0 + 4 * ty + 64 * (i / 4) + (i % 4);
@@ -548,12 +552,34 @@ __global__ void __launch_bounds__(256, TM == 4 ? 4 : 2) k_gemm_f32t(const F32Gem
     float *orow = g.out + w * g.ows + pad_row(m, g.ow, g.opad) * g.ldo;
     const float *rrow = g.res ? g.res + w * g.rws + pad_row(m, g.rw, g.rpad) * g.ldr : nullptr;
 #pragma unroll
-    for (int j = 0; j < TN; j++) {
-      const int n = TN == 2 ? n0 + 2 * tx + j : n0 + 4 * tx + 64 * (j / 4) + (j % 4);
-      if (n >= g.Np) continue;
-      float y = act32(__fadd_rn(acc[i][j], __ldg(g.bias + n)), g.act, lut);
-      if (rrow) y = __fadd_rn(y, __ldg(rrow + n));
-      orow[n] = y;
+    for (int jg = 0; jg < TN / VW; jg++) {
+      const int n = TN == 2 ? n0 + 2 * tx : VW == 1 ? n0 + 4 * tx + 64 * (jg / 4) + (jg % 4) : n0 + 4 * tx + 64 * jg;
+      if (n >= g.Np) continue;  // Np % 8 == 0: a run is wholly inside or outside
+      float y[VW], rv[VW];
+#pragma unroll
+      for (int v = 0; v < VW; v++) y[v] = act32(__fadd_rn(acc[i][VW * jg + v], __ldg(g.bias + n + v)), g.act, lut);
+      if (rrow) {
+        if (g.vec && VW == 2) {
+          const float2 t = __ldg(reinterpret_cast<const float2 *>(rrow + n));
+          rv[0] = t.x; rv[VW - 1] = t.y;
+        } else if (g.vec) {
+          const float4 t = __ldg(reinterpret_cast<const float4 *>(rrow + n));
+          rv[0] = t.x; rv[1 % VW] = t.y; rv[2 % VW] = t.z; rv[3 % VW] = t.w;
+        } else {
+#pragma unroll
+          for (int v = 0; v < VW; v++) rv[v] = __ldg(rrow + n + v);
+        }
+#pragma unroll
+        for (int v = 0; v < VW; v++) y[v] = __fadd_rn(y[v], rv[v]);
+      }
+      if (g.vec && VW == 2) {
+        *reinterpret_cast<float2 *>(orow + n) = make_float2(y[0], y[VW - 1]);
+      } else if (g.vec) {
+        *reinterpret_cast<float4 *>(orow + n) = make_float4(y[0], y[1 % VW], y[2 % VW], y[3 % VW]);
+      } else {
+#pragma unroll
+        for (int v = 0; v < VW; v++) orow[n + v] = y[v];
+      }
     }
   }
 }
@@ -573,10 +599,15 @@ static int launch_gemm_f32t(int B, const F32GemmArgs &g, bnn_stream_t st) {
   const int nt = (g.Np + bn - 1) / bn;
   const long long blocks = (rows + bm - 1) / bm * nt;
   if (rows > 0x7fffffffLL || blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
-  if (small) k_gemm_f32t<4, 2, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
-  else if (bn == 128) k_gemm_f32t<8, 8, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
-  else if (bn == 64) k_gemm_f32t<8, 4, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
-  else k_gemm_f32t<16, 2, SRC><<<(unsigned)blocks, 256, 0, st>>>(g, (int)rows, nt);
+  const int vw = bn == 32 ? 2 : 4;  // the epilogue's run of columns per thread
+  auto al = [vw](const void *p, long long ws, int ld) { return ((uintptr_t)p & (4 * vw - 1)) == 0 && ws % vw == 0 && ld % vw == 0; };
+  F32GemmArgs gv = g;
+  // (the 128-wide tile keeps scalar accesses: its 64 accumulators leave no registers for vectors)
+  gv.vec = bn < 128 && al(g.out, g.ows, g.ldo) && (!g.res || al(g.res, g.rws, g.ldr));
+  if (small) k_gemm_f32t<4, 2, SRC><<<(unsigned)blocks, 256, 0, st>>>(gv, (int)rows, nt);
+  else if (bn == 128) k_gemm_f32t<8, 8, SRC><<<(unsigned)blocks, 256, 0, st>>>(gv, (int)rows, nt);
+  else if (bn == 64) k_gemm_f32t<8, 4, SRC><<<(unsigned)blocks, 256, 0, st>>>(gv, (int)rows, nt);
+  else k_gemm_f32t<16, 2, SRC><<<(unsigned)blocks, 256, 0, st>>>(gv, (int)rows, nt);
   return cudaGetLastError();
 }
 
