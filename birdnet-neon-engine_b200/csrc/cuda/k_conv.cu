@@ -296,10 +296,20 @@ __global__ void __launch_bounds__(kSeThreads) k_se_gate(int B, int C, int rd, co
       const float *wr = w1 + (long long)r * C + lane8;
       const float *mr = mean + lane8;
       int i = 0;
+      // the next batch of 8 weights is loaded while the current one is multiplied (the chain waits on L2 otherwise)
+      float wn[8];
+      if (C8 >= 8) {
+#pragma unroll
+        for (int u = 0; u < 8; u++) wn[u] = __ldg(wr + 8 * u);
+      }
       for (; i + 8 <= C8; i += 8) {
         float wv[8];
 #pragma unroll
-        for (int u = 0; u < 8; u++) wv[u] = __ldg(wr + 8 * (i + u));
+        for (int u = 0; u < 8; u++) wv[u] = wn[u];
+        if (i + 16 <= C8) {
+#pragma unroll
+          for (int u = 0; u < 8; u++) wn[u] = __ldg(wr + 8 * (i + 8 + u));
+        }
 #pragma unroll
         for (int u = 0; u < 8; u++)
 #pragma unroll
@@ -330,10 +340,19 @@ __global__ void __launch_bounds__(kSeThreads) k_se_gate(int B, int C, int rd, co
 #pragma unroll
     for (int j = 0; j < WB; j++) g[j] = b2[c];
     int r = 0;
+    float wn[16];  // the next batch of 16 weights in flight while the current one is multiplied
+    if (rd >= 16) {
+#pragma unroll
+      for (int u = 0; u < 16; u++) wn[u] = __ldg(w2t + (long long)u * C + c);
+    }
     for (; r + 16 <= rd; r += 16) {
       float wv[16];
 #pragma unroll
-      for (int u = 0; u < 16; u++) wv[u] = __ldg(w2t + (long long)(r + u) * C + c);
+      for (int u = 0; u < 16; u++) wv[u] = wn[u];
+      if (r + 32 <= rd) {
+#pragma unroll
+        for (int u = 0; u < 16; u++) wn[u] = __ldg(w2t + (long long)(r + 16 + u) * C + c);
+      }
 #pragma unroll
       for (int u = 0; u < 16; u++)
 #pragma unroll

@@ -908,7 +908,25 @@ __global__ void __launch_bounds__(kSe16Threads) k_se_gate_f16(int C, int rd, con
     if (r < rd) {
       const float *wr = w1 + (long long)r * C + lane8;
       const float *mr = mean + lane8;
-      for (int i = 0; i < C8; i++) a = __fmaf_rn(__ldg(wr + 8 * i), mr[8 * i], a);
+      // batches of 8 weights, the next batch in flight while the current one is multiplied (same FMA order)
+      int i = 0;
+      float wn[8];
+      if (C8 >= 8) {
+#pragma unroll
+        for (int u = 0; u < 8; u++) wn[u] = __ldg(wr + 8 * u);
+      }
+      for (; i + 8 <= C8; i += 8) {
+        float wv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) wv[u] = wn[u];
+        if (i + 16 <= C8) {
+#pragma unroll
+          for (int u = 0; u < 8; u++) wn[u] = __ldg(wr + 8 * (i + 8 + u));
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) a = __fmaf_rn(wv[u], mr[8 * (i + u)], a);
+      }
+      for (; i < C8; i++) a = __fmaf_rn(__ldg(wr + 8 * i), mr[8 * i], a);
     }
     const float other = __shfl_down_sync(0xffffffffu, a, 4, 8);
     const float v = __fadd_rn(a, other);
@@ -922,7 +940,15 @@ __global__ void __launch_bounds__(kSe16Threads) k_se_gate_f16(int C, int rd, con
   __syncthreads();
   for (int c = tid; c < C; c += kSe16Threads) {
     float gv = b2[c];
-    for (int r = 0; r < rd; r++) gv = __fmaf_rn(__ldg(w2t + (long long)r * C + c), s1[r], gv);
+    int r = 0;
+    for (; r + 8 <= rd; r += 8) {  // the batch's 8 loads issued ahead of its FMAs (same order)
+      float wv[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) wv[u] = __ldg(w2t + (long long)(r + u) * C + c);
+#pragma unroll
+      for (int u = 0; u < 8; u++) gv = __fmaf_rn(wv[u], s1[r + u], gv);
+    }
+    for (; r < rd; r++) gv = __fmaf_rn(__ldg(w2t + (long long)r * C + c), s1[r], gv);
     g16[(long long)win * C + c] = (uint16_t)f2h(sigm_f16path(gv));
   }
 }
