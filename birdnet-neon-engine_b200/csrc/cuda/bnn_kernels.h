@@ -71,6 +71,11 @@ typedef struct {
 } bnnk_epilogue;
 int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float *sa, const int32_t *za, const bnnk_epilogue *e,
               int *err, bnn_stream_t st);
+/* the ungated PW_S8 in one launch, the quantizer inside the GEMM: x [B Mw][lda] fp32 rows (xws == Mw lda), K values
+ * a row; BNNK_NOT_FUSED (nothing launched) when the layer is outside the form's limits */
+#define BNNK_NOT_FUSED (-4242)
+int bnnk_pw_s8_fq(const bnnk_gemm_plan *p, int rows, int Mw, const float *x, long long xws, int lda, int K,
+                  const bnnk_epilogue *e, int *err, bnn_stream_t st);
 
 /* the GEMM of a planned layer on quantized rows the caller holds: q [rows][ldq] (ldq % 16 == 0, the first kp bytes
  * of each row are the row, kp <= the plan's kq), sa, za [rows] */

@@ -344,7 +344,11 @@ struct GemmArgs {
   int *err;
   unsigned long long wait_ns;  // the limit of every mbarrier wait (kWaitNs; shorter in the stall test)
   int stall;                   // test hook: the producer issues no load, so every consumer's wait runs out
+  // kFQ (the quantizer in the GEMM): fp32 rows of K (a multiple of 4, at most kFQMaxK) arrive by TMA in fs slots of
+  // fp32_bytes; the A operand's K block is Kq bytes wide (one block, nkb = 1)
+  int K, fs, fp32_bytes, kqz;
 };
+constexpr int kFQMaxK = 72, kFQSlots = 2, kFQRing = kMaxStages + kMaxEpi;  // K, fp32 slots, sa / za ring
 
 __device__ __forceinline__ long long padded_row(int m, int w, int pad) {
   return pad ? (long long)((m / w) + pad) * (w + 2 * pad) + (m % w) + pad : (long long)m;
@@ -493,13 +497,20 @@ __device__ __forceinline__ void quant_units(const GemmArgs &a, int row, const fl
 // kSP: the per-column parameters (sw, bias, cs; np <= kSPMax columns) are staged in shared memory once per CTA;
 // kQ: the epilogue also quantizes the stored rows for the next layer (a.e.qo); kThreads: the block size the registers
 // are budgeted for (832: 72 registers a thread; 576, two epilogue warps per TMEM lane quarter and accumulator: 112)
-template <int SW, bool kSP, bool kQ, int kThreads = kMaxThreads>
+// kFQ: four quantizer warps (warps 2-5, one thread per tile row) turn the fp32 rows, staged by TMA (tma_a is then
+// the fp32 map), into the tile's int8 A operand in its shared-memory stage (in the layout that TMA's SW-byte swizzle
+// gives a loaded tile), with the rows' scales and zero points in a shared ring for the epilogue
+template <int SW, bool kSP, bool kQ, int kThreads = kMaxThreads, bool kFQ = false>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm_s8(const __grid_constant__ CUtensorMap tma_a,
                                                            const __grid_constant__ CUtensorMap tma_b,
                                                            const GemmArgs a) {
   extern __shared__ uint8_t dsmem[];
   __shared__ __align__(8) unsigned long long bar_full[kMaxStages], bar_empty[kMaxStages];
   __shared__ __align__(8) unsigned long long bar_acc_full[kMaxEpi], bar_acc_empty[kMaxEpi];
+  __shared__ __align__(8) unsigned long long bar_ffull[kFQ ? kFQSlots : 1], bar_fempty[kFQ ? kFQSlots : 1];
+  __shared__ __align__(8) unsigned long long bar_qdone[kFQ ? kFQRing : 1];
+  __shared__ float s_qsa[kFQ ? kFQRing : 1][kFQ ? 128 : 1];
+  __shared__ int32_t s_qza[kFQ ? kFQRing : 1][kFQ ? 128 : 1];
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int abort_s;
   __shared__ uint32_t s_lut[256];
@@ -514,6 +525,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_s8(const __grid_constant__
   int32_t *p_cs = reinterpret_cast<int32_t *>(p_b + a.np);
   // the epilogue threads' partial (min, max) of their rows, per tile parity, group and warp: [2][ne][nh][128]
   float2 *q_part = reinterpret_cast<float2 *>(par + (kSP ? (size_t)12 * a.np : 0));
+  // kFQ: the fp32 row slots (128-byte aligned) after the partials
+  const uint32_t fbase = (smem_u32(par) + (kSP ? 12u * a.np : 0u) + (uint32_t)kQPartBytes + 127u) & ~127u;
   if (kSP) {
     for (int i = threadIdx.x; i < a.np; i += blockDim.x) {
       p_sw[i] = __ldg(a.e.sw + i);
@@ -524,10 +537,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_s8(const __grid_constant__
 
   for (int i = threadIdx.x; i < 256; i += blockDim.x) s_lut[i] = g_frecpe_lut[i];
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; s++) { mbar_init(smem_u32(&bar_full[s]), 1); mbar_init(smem_u32(&bar_empty[s]), 1); }
+    for (int s = 0; s < S; s++) {
+      mbar_init(smem_u32(&bar_full[s]), kFQ ? 1 + 4 : 1);  // kFQ: the B load and the four quantizer warps
+      mbar_init(smem_u32(&bar_empty[s]), 1);
+    }
     for (int g = 0; g < a.ne; g++) {
       mbar_init(smem_u32(&bar_acc_full[g]), 1);
       mbar_init(smem_u32(&bar_acc_empty[g]), 4 * a.nh);
+    }
+    if (kFQ) {
+      for (int f = 0; f < kFQSlots; f++) { mbar_init(smem_u32(&bar_ffull[f]), 1); mbar_init(smem_u32(&bar_fempty[f]), 4); }
+      for (int r = 0; r < kFQRing; r++) mbar_init(smem_u32(&bar_qdone[r]), 4);
     }
     abort_s = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -555,6 +575,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_s8(const __grid_constant__
             break;
           }
           const uint32_t st = base + s * stage_bytes, bar = smem_u32(&bar_full[s]);
+          if (kFQ) {  // the tile's fp32 rows into their slot, B into the stage (nkb = 1: it counts tiles); both waits
+                      // come first, so a wait that runs out leaves no copy in flight
+            const int f = it % kFQSlots;
+            if (it >= kFQSlots && !mbar_wait_ns(smem_u32(&bar_fempty[f]), ((it / kFQSlots) - 1) & 1, a.wait_ns)) {
+              atomicExch(a.err, BNNK_ERR_TMA_WAIT);
+              abort_s = 1;
+              break;
+            }
+            mbar_expect_tx(smem_u32(&bar_ffull[f]), (uint32_t)a.fp32_bytes);  // rows past the last read zero
+            tma_load_2d(fbase + f * (uint32_t)a.fp32_bytes, &tma_a, smem_u32(&bar_ffull[f]), 0, m0);
+            mbar_expect_tx(bar, stage_bytes - a_bytes);
+            tma_load_2d(st + a_bytes, &tma_b, bar, 0, n0);
+            continue;
+          }
           mbar_expect_tx(bar, stage_bytes);  // the full boxes: bytes past Kq arrive as zero fill
           tma_load_2d(st, &tma_a, bar, kb * SW, m0);
           tma_load_2d(st + a_bytes, &tma_b, bar, kb * SW, n0);
@@ -593,10 +627,66 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_s8(const __grid_constant__
         mma_commit(smem_u32(&bar_acc_full[g]));  // arrives when this tile's MMAs have completed
       }
     }
-  } else if (warp - 2 < 4 * a.ne * a.nh) {
+  } else if (kFQ && warp < 6) {
+    // quantizer: thread r = row r of each tile, s8n_quant_rows on the row's K fp32 values as k_quant does (the
+    // NaN-propagating min / max, the row parameters, FCVTNS on the 8-wide part and lrintf past it, pads = the zero
+    // point), the Kq bytes written to the stage in 16-byte chunks at their swizzled places
+    const int r = threadIdx.x - 64;
+    const int K = a.K, K4 = K >> 2, K8 = K & ~7, nch = SW / 16;
+    int lt = 0;
+    for (int t = blockIdx.x; t < a.tiles && !abort_s; t += gridDim.x, lt++) {
+      const int s = lt % S, f = lt % kFQSlots, rs = lt % kFQRing;
+      bool ok = mbar_wait_ns(smem_u32(&bar_ffull[f]), (lt / kFQSlots) & 1, a.wait_ns);
+      if (ok && lt >= S) ok = mbar_wait_ns(smem_u32(&bar_empty[s]), ((lt / S) - 1) & 1, a.wait_ns);
+      ok = __all_sync(0xffffffffu, ok && !abort_s);
+      if (!ok) {
+        if (lane == 0) { atomicExch(a.err, BNNK_ERR_TMA_WAIT); abort_s = 1; }
+        break;
+      }
+      const float4 *xr = reinterpret_cast<const float4 *>(dsmem + (fbase + f * (uint32_t)a.fp32_bytes - smem_u32(dsmem))) +
+                         (size_t)r * K4;
+      float lo = __int_as_float(0x7f800000), hi = __int_as_float(0xff800000);
+      for (int g4 = 0; g4 < K4; g4++) {
+        const float4 v = xr[g4];
+        lo = fmin_nan(lo, fmin_nan(fmin_nan(v.x, v.y), fmin_nan(v.z, v.w)));
+        hi = fmax_nan(hi, fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w)));
+      }
+      float inv, sc;
+      int32_t z;
+      quant_params(lo, hi, inv, z, sc);
+      s_qsa[rs][r] = sc;
+      s_qza[rs][r] = z;
+      const uint32_t zp = ((uint32_t)z & 0xffu) * 0x01010101u;
+      uint8_t *arow = dsmem + (base + s * stage_bytes - smem_u32(dsmem)) + (size_t)r * SW;
+      for (int c = 0; c < nch; c++) {  // 16-byte chunk c of the row: 16 values, 4 words
+        uint32_t wd[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int g4 = 4 * c + j;
+          if (g4 < K4) {
+            const float4 v = xr[g4];
+            wd[j] = quant_word(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv), __fmul_rn(v.w, inv), z,
+                               4 * g4 < K8);
+          } else {
+            wd[j] = zp;  // pads past K (to the block's SW bytes): the zero point
+          }
+        }
+        // the swizzle of a TMA-written K-major tile: chunk c of row r sits at chunk c ^ (row bits) of its row
+        const int pc = SW == 128 ? (c ^ (r & 7)) : SW == 64 ? (c ^ ((r >> 1) & 3)) : (c ^ ((r >> 2) & 1));
+        *reinterpret_cast<uint4 *>(arow + 16 * pc) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the stores, seen by the tensor core
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&bar_full[s]));
+        mbar_arrive(smem_u32(&bar_fempty[f]));
+        mbar_arrive(smem_u32(&bar_qdone[rs]));
+      }
+    }
+  } else if (warp - 2 - (kFQ ? 4 : 0) < 4 * a.ne * a.nh) {
     // epilogue: group g drains accumulator g; its 4 * nh warps split the 8-column units of a tile round robin, the
     // warp's TMEM lane quarter q (= warp % 4) fixing its 32 rows
-    const int e = warp - 2, g = e / (4 * a.nh), h = (e % (4 * a.nh)) / 4, q = warp % 4;
+    const int e = warp - 2 - (kFQ ? 4 : 0), g = e / (4 * a.nh), h = (e % (4 * a.nh)) / 4, q = warp % 4;
     constexpr bool fq = kQ;  // the tile's rows are quantized for the next layer after its epilogue
     int use = 0;
     for (int t = blockIdx.x + g * gridDim.x; t < a.tiles; t += a.ne * gridDim.x, use++) {
@@ -609,10 +699,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_s8(const __grid_constant__
       if (live) {
         w = row / a.Mw;
         mm = row - w * a.Mw;
-        sa = __ldg(a.sa + row);
-        za = __ldg(a.za + row);
+        if (!kFQ) {
+          sa = __ldg(a.sa + row);
+          za = __ldg(a.za + row);
+        }
       }
       bool ok = mbar_wait_ns(smem_u32(&bar_acc_full[g]), use & 1, a.wait_ns);
+      if (kFQ) {  // the tile's row parameters, from the quantizer warps
+        const int lt = g + use * a.ne;
+        ok = ok && mbar_wait_ns(smem_u32(&bar_qdone[lt % kFQRing]), (lt / kFQRing) & 1, a.wait_ns);
+        sa = s_qsa[lt % kFQRing][q * 32 + lane];
+        za = s_qza[lt % kFQRing][q * 32 + lane];
+      }
       ok = __all_sync(0xffffffffu, ok && !abort_s);  // one outcome per warp (abort_s may change between lanes' reads)
       if (!ok) {
         if (lane == 0) { atomicExch(a.err, BNNK_ERR_EPI_WAIT); abort_s = 1; }
@@ -981,6 +1079,91 @@ extern "C" int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float 
   case 128: return launch_gemm<128, false>(p, a, st);
   case 64: return launch_gemm<64, false>(p, a, st);
   default: return launch_gemm<32, false>(p, a, st);
+  }
+}
+
+// The ungated PW_S8 with its quantizer inside the GEMM (kFQ): one launch, the fp32 rows read once by TMA, no int8
+// round trip through global memory. For one K block (Kq <= 128), K % 4 == 0 and K <= kFQMaxK, rows of lda floats
+// (lda % 4 == 0) stored back to back over the windows (xws == Mw lda), 16-byte aligned. BNNK_NOT_FUSED when a layer
+// is outside that (the caller then quantizes and multiplies in two launches); BNN_FQ=0 turns the form off.
+template <int SW, bool kSP>
+static int launch_fq(const bnnk_gemm_plan *p, const GemmArgs &a, const CUtensorMap &map, size_t smem,
+                     bnn_stream_t st) {
+  constexpr int kT = 64 + 128 + 128 * 2 * 2;  // producer + MMA warps, 4 quantizer warps, two groups of 8
+  static SmemAttr attr;
+  const cudaError_t e = attr.ensure(k_gemm_s8<SW, kSP, false, kT, true>, smem);
+  if (e) return e;
+  const int grid = a.tiles < num_sms() ? a.tiles : num_sms();
+  k_gemm_s8<SW, kSP, false, kT, true><<<grid, kT, smem, st>>>(map, *(const CUtensorMap *)p->tma_b, a);
+  return cudaGetLastError();
+}
+
+extern "C" int bnnk_pw_s8_fq(const bnnk_gemm_plan *p, int rows, int Mw, const float *x, long long xws, int lda, int K,
+                             const bnnk_epilogue *e, int *err, bnn_stream_t st) {
+  static int env = -1;
+  if (env < 0) {
+    const char *s = getenv("BNN_FQ");
+    env = !(s && s[0] == '0');
+  }
+  if (!env || rows <= 0 || p->nkb != 1 || K % 4 || K < 4 || K > kFQMaxK || lda % 4 || lda < K ||
+      xws != (long long)Mw * lda || ((uintptr_t)x & 15) || e->qo)
+    return BNNK_NOT_FUSED;
+  GemmArgs a;
+  a.stall = __atomic_exchange_n(&g_stall_next, 0, __ATOMIC_RELAXED);  // the test hook, as for bnnk_gemm
+  a.wait_ns = a.stall ? 200000ull : kWaitNs;
+  a.rows = rows;
+  a.Mw = Mw;
+  a.nkb = 1;
+  a.bn = p->bn;
+  a.np = p->np;
+  a.n_tiles = p->n_tiles;
+  a.tiles = ((rows + 127) / 128) * p->n_tiles;
+  a.acc_cols = p->tmem_cols;
+  a.ne = 2;
+  a.nh = 2;
+  a.tmem_alloc = tmem_pow2(a.ne * p->tmem_cols);
+  if (a.tmem_alloc > 512) return BNNK_NOT_FUSED;
+  a.vec_out = aligned32(e->out, e->ows, e->ldo);
+  a.vec_res = e->res ? aligned32(e->res, e->rws, e->ldr) : 0;
+  a.idesc = p->idesc;
+  a.sa = nullptr;
+  a.za = nullptr;
+  a.e = *e;
+  a.err = err;
+  a.K = K;
+  a.fs = kFQSlots;
+  a.fp32_bytes = 128 * K * 4;
+  a.kqz = p->kq;
+  // shared memory: the stage ring, the parameters, the partials, the fp32 slots (the static arrays need ~13 KB)
+  const size_t stage = (size_t)(128 + p->bn) * p->sw, par = p->sp ? (size_t)12 * p->np : 0;
+  const size_t fixed = 1024 + par + kQPartBytes + 128 + (size_t)kFQSlots * a.fp32_bytes;
+  const size_t dyn_max = 227 * 1024 - 16 * 1024;
+  if (fixed + 2 * stage > dyn_max) return BNNK_NOT_FUSED;
+  int s = (int)((dyn_max - fixed) / stage);
+  a.stages = s > kMaxStages ? kMaxStages : s;
+  const size_t smem = fixed + (size_t)a.stages * stage;
+  // the fp32 rows: [rows][K] floats at row stride lda, boxes of 128 rows (rows past the last read zero)
+  PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode();
+  if (!enc) return BNNK_NOT_FUSED;
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)lda * 4};
+  cuuint32_t box[2] = {(cuuint32_t)K, 128}, es[2] = {1, 1};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(x), dims, strides, box, es,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return BNNK_NOT_FUSED;
+  if (p->sp) {
+    switch (p->sw) {
+    case 128: return launch_fq<128, true>(p, a, map, smem, st);
+    case 64: return launch_fq<64, true>(p, a, map, smem, st);
+    default: return launch_fq<32, true>(p, a, map, smem, st);
+    }
+  }
+  switch (p->sw) {
+  case 128: return launch_fq<128, false>(p, a, map, smem, st);
+  case 64: return launch_fq<64, false>(p, a, map, smem, st);
+  default: return launch_fq<32, false>(p, a, map, smem, st);
   }
 }
 

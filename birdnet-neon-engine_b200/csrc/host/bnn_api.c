@@ -364,7 +364,9 @@ int bnn_set_fp16_tensor(bnn_ctx *c, int on) {
   return make_devices(c, n);
 }
 int bnn_get_fp16_tensor(const bnn_ctx *c) { return c ? c->f16_tensor : 0; }
-int bnn_launches_per_batch(const bnn_ctx *c) { return c ? c->launches - c->launches_fused : 0; }
+int bnn_launches_per_batch(const bnn_ctx *c) {
+  return c ? c->launches - c->launches_fused - (c->dev[0] ? c->dev[0]->launches_fq : 0) : 0;
+}
 
 /* ------------------------------------------------------------------ inference */
 
@@ -813,10 +815,14 @@ int bnn_pw_s8_run(bnn_pw_s8 *o, int B, int Mw, const float *d_x, long long xws, 
   }
   bnn_stream_t st = (bnn_stream_t)stream;
   const int rows = B * Mw;
+  bnnk_epilogue ep = {act, d_out, ows, ldo, ow, opad, d_res, rws, ldr, rw, rpad, o->op.sw, o->op.bias, o->op.cs,
+                      NULL, NULL, NULL, 0, 0};
+  if (!d_gate && rows > 0) {  /* one launch where the layer allows it: the quantizer inside the GEMM */
+    const int f = bnnk_pw_s8_fq(&o->op.plan, rows, Mw, d_x, xws, lda, o->K, &ep, o->err, st);
+    if (f != BNNK_NOT_FUSED) return launch_rc("bnn_pw_s8_run", f);
+  }
   int e = bnnk_quant(rows, Mw, d_x, xws, lda, o->K, o->op.kq, d_gate, gws, o->q, o->sa, o->za, st);
   if (!e) {
-    bnnk_epilogue ep = {act, d_out, ows, ldo, ow, opad, d_res, rws, ldr, rw, rpad, o->op.sw, o->op.bias, o->op.cs,
-                      NULL, NULL, NULL, 0, 0};
     e = bnnk_gemm(&o->op.plan, rows, Mw, o->sa, o->za, &ep, o->err, st);
   }
   return launch_rc("bnn_pw_s8_run", e);

@@ -117,6 +117,7 @@ typedef struct {
   float *sa2;
   int32_t *za2;
   int fused_q;          /* PW_S8 quantizer launches this device's set-up folded into the GEMM before */
+  int launches_fq;      /* PW_S8 ops of the last whole-package launch sequence that ran as one launch (kFQ) */
   float *sa, *fe_minmax, *pcin;
   int32_t *za;
   uint16_t *g16;        /* SE f16: the fp16 gates [batch][C] */

@@ -1747,6 +1747,7 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
     dv->prof_op1 = op1 < c->n_ops ? op1 : c->n_ops;
   }
   int pre_q = 0;  /* this op's input rows were quantized by the launch of the op before */
+  int n_fq = 0;   /* PW_S8 ops run as one launch */
   for (int i = op0; i < op1 && i < c->n_ops; i++) {
     const bnn_op *op = &c->ops[i];
     const bnn_devop *o = &dv->ops[i];
@@ -1775,13 +1776,21 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
       int8_t *qq = o->qsel ? dv->q2 : dv->q;
       float *qs = o->qsel ? dv->sa2 : dv->sa;
       int32_t *qz = o->qsel ? dv->za2 : dv->za;
+      const bnn_buf_rec *r = op->b[2] >= 0 ? &c->bufd[op->b[2]] : NULL;
+      bnnk_epilogue e = {p[6], B_(1), WS(1), p[7], p[8], p[9], B_(2), WS(2), p[10],
+                         r && r->halo ? (int)r->W : 0, r && r->halo ? (int)r->halo : 0, o->sw, o->bias, o->cs,
+                         NULL, NULL, NULL, 0, 0};
+      if (!pre_q && !gate && !(o->qnext && i + 1 < op1)) {  /* one launch: the quantizer inside the GEMM */
+        rc = bnnk_pw_s8_fq(&o->plan, n * M, M, IN_(0), INWS(0), p[5], p[1], &e, dv->err, st);
+        if (rc != BNNK_NOT_FUSED) {
+          n_fq++;
+          break;
+        }
+        rc = 0;
+      }
       if (!pre_q)
         rc = bnnk_quant(n * M, M, IN_(0), INWS(0), p[5], p[1], o->kq, gate, gate ? WS(6) : 0, qq, qs, qz, st);
       if (!rc) {
-        const bnn_buf_rec *r = op->b[2] >= 0 ? &c->bufd[op->b[2]] : NULL;
-        bnnk_epilogue e = {p[6], B_(1), WS(1), p[7], p[8], p[9], B_(2), WS(2), p[10],
-                           r && r->halo ? (int)r->W : 0, r && r->halo ? (int)r->halo : 0, o->sw, o->bias, o->cs,
-                           NULL, NULL, NULL, 0, 0};
         if (o->qnext && i + 1 < op1) {  /* this GEMM quantizes its rows for the expand after it */
           e.qo = dv->q2;
           e.qsa = dv->sa2;
@@ -1968,6 +1977,7 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
     }
     pre_q = next_q;
   }
+  if (op0 == 0 && op1 >= c->n_ops) dv->launches_fq = n_fq;
   return 0;
 }
 
