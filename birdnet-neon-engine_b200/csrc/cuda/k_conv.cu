@@ -138,17 +138,13 @@ template <int S, int R, bool kSum>
 __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMap tmx, int W, int C, int CG, int Ho,
                                               int Wo, int NR, const float *__restrict__ wt,
                                               const float *__restrict__ bias, float *__restrict__ out, long long ows,
-                                              float *__restrict__ chsum, long long cws, int *err, int nband, int SB) {
-  // SB < blockDim.x: threads SB.. are summing threads, one per channel quad, that add the previous row's outputs to
-  // the channel sums while the others compute the next row (the row sum leaves the critical path)
+                                              float *__restrict__ chsum, long long cws, int *err, int nband) {
   constexpr int NX = (R - 1) * S + 3;
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ __align__(8) unsigned long long bar[kDw3MaxRing];
   __shared__ uint32_t lut[256];
-  const int tid = threadIdx.x, nt = SB;
-  const bool summers = SB < (int)blockDim.x, summer = tid >= SB;
-  const int sp = tid - SB;  // a summer's channel quad
-  for (int i = tid; i < 256; i += blockDim.x) lut[i] = g_frecpe_lut[i];
+  const int tid = threadIdx.x, nt = blockDim.x;
+  for (int i = tid; i < 256; i += nt) lut[i] = g_frecpe_lut[i];
   const int ngroups = C / CG;
   const int band = blockIdx.x % nband, wg = blockIdx.x / nband;
   const int win = wg / ngroups, grp = wg - win * ngroups;
@@ -160,7 +156,7 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
   const float *ringf = reinterpret_cast<const float *>(dsm);
   float *obuf = reinterpret_cast<float *>(dsm + NR * row_stride);  // [2][Wo][CG]
   const int q = tid % Q, lane = tid / Q;  // lanes >= NL (the last nt % Q threads) only sum
-  const bool comp = !summer && lane < NL;
+  const bool comp = lane < NL;
   const int c = grp * CG + 4 * q;
   float2 w[9][2], b[2];
 #pragma unroll
@@ -190,18 +186,7 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
     }
   };
   if (tid == 0) issue_to(NR - 1);  // as many rows as the ring holds
-  float cs = 0.f, cs4[4] = {0.f, 0.f, 0.f, 0.f};
-  // a summer adds one row's outputs of its channel quad to the sums, pixel by pixel (four independent chains)
-  auto sum_row = [&](int row) {
-    const float *pb = obuf + (row & 1) * Wo * CG + 4 * sp;
-    for (int x = 0; x < Wo; x++) {
-      const float4 v = *reinterpret_cast<const float4 *>(pb + x * CG);
-      cs4[0] = __fadd_rn(cs4[0], v.x);
-      cs4[1] = __fadd_rn(cs4[1], v.y);
-      cs4[2] = __fadd_rn(cs4[2], v.z);
-      cs4[3] = __fadd_rn(cs4[3], v.w);
-    }
-  };
+  float cs = 0.f;
   int oy = oy0;
   for (; oy < oy1; oy++) {
     bool ok = true;
@@ -210,12 +195,10 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
     for (int ky = 0; ky < 3; ky++) {
       const int iy = (oy - oy0) * S + ky;
       slot[ky] = iy % NR;
-      if (!summer) ok = ok && mbar_wait(smem_u32(&bar[slot[ky]]), (uint32_t)(iy / NR) & 1u);
+      ok = ok && mbar_wait(smem_u32(&bar[slot[ky]]), (uint32_t)(iy / NR) & 1u);
     }
     float *ob = obuf + (oy & 1) * Wo * CG;
-    if (kSum && summer) {
-      if (oy > oy0 && sp < Q) sum_row(oy - 1);
-    } else if (comp) {
+    if (comp) {
       // groups in reverse lane order: when they do not divide evenly, the extra ones go to the high lanes, not to
       // the low threads that also add the row sums after the barrier
       for (int g = NL - 1 - lane; g < ngrp; g += NL) {
@@ -259,7 +242,7 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
     }
     if (!__syncthreads_and(ok)) break;  // every thread has left this step's rows and written its outputs
     if (tid == 0) issue_to((oy - oy0 + 1) * S + NR - 1);  // local rows below (oy - oy0 + 1) S are free
-    if (kSum && !summers && tid < CG) {
+    if (kSum && tid < CG) {
       int x = 0;
       for (; x + 8 <= Wo; x += 8) {
         float u[8];
@@ -279,15 +262,7 @@ __global__ void __launch_bounds__(256) k_dw3t(const __grid_constant__ CUtensorMa
     __syncthreads();
     return;
   }
-  if (kSum && summers) {  // the summers add the last row (the computing threads are done with the band)
-    if (summer && sp < Q) {
-      sum_row(oy1 - 1);
-#pragma unroll
-      for (int j = 0; j < 4; j++) chsum[win * cws + grp * CG + 4 * sp + j] = cs4[j];
-    }
-  } else if (kSum && tid < CG) {
-    chsum[win * cws + grp * CG + tid] = cs;
-  }
+  if (kSum && tid < CG) chsum[win * cws + grp * CG + tid] = cs;
 }
 
 // ------------------------------------------------------------------ SE_GATE (src/v24_f32.c:164-179, rt_ops_f32.c:272-283)
@@ -756,24 +731,10 @@ extern "C" int bnnk_dw3(int B, const float *xp, long long xws, int H, int W, int
       if (nt < cg) nt = cg;
       nt = (nt + 31) / 32 * 32;
       const bool pair = Wo % 2 == 0;
-      // summing warps (one thread per channel quad) where the sums are formed, rows have 16+ pixels, the summers take
-      // at most two warps, and the computing threads left still cover a row in as many passes
-      int sb = nt;
-      {
-        const int ns = 32 * ((Q + 31) / 32), ngrp = Wo / (pair ? 2 : 1);
-        const int sbc = ((256 - ns) / Q) * Q, nl_old = nt / Q, nl_new = sbc / Q;
-        const char *ev = getenv("BNN_DW3_SUMMERS");  // 0: never (tuning)
-        if (sum && Wo >= 16 && ns <= 64 && nl_new >= 1 && !(ev && ev[0] == '0') &&
-            (ngrp + nl_new - 1) / nl_new == (ngrp + nl_old - 1) / nl_old) {
-          sb = (sbc + 31) / 32 * 32;
-          nt = sb + ns;
-        }
-      }
 #define BNN_DW3T_(SS, RR, KS)                                                                                     \
   do {                                                                                                             \
     cudaFuncSetAttribute(k_dw3t<SS, RR, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);              \
-    k_dw3t<SS, RR, KS><<<grid, nt, smem, st>>>(map, W, C, cg, Ho, Wo, nr, w, b, out, ows, chsum, cws, err, nband, \
-                                               sb);                                                              \
+    k_dw3t<SS, RR, KS><<<grid, nt, smem, st>>>(map, W, C, cg, Ho, Wo, nr, w, b, out, ows, chsum, cws, err, nband); \
   } while (0)
 #define BNN_DW3T(SS, RR) \
   do {                    \
