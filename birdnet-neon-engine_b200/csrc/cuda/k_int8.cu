@@ -1084,8 +1084,11 @@ extern "C" int bnnk_gemm(const bnnk_gemm_plan *p, int rows, int Mw, const float 
 
 // The ungated PW_S8 with its quantizer inside the GEMM (kFQ): one launch, the fp32 rows read once by TMA, no int8
 // round trip through global memory. For one K block (Kq <= 128), K % 4 == 0 and K <= kFQMaxK, rows of lda floats
-// (lda % 4 == 0) stored back to back over the windows (xws == Mw lda), 16-byte aligned. BNNK_NOT_FUSED when a layer
-// is outside that (the caller then quantizes and multiplies in two launches); BNN_FQ=0 turns the form off.
+// (lda % 4 == 0) stored back to back over the windows (xws == Mw lda), 16-byte aligned, and a linear epilogue: on the
+// SiLU layers the quantizer warps take issue slots from an epilogue that is already issue-bound (measured: b1.1's
+// expansion 220 -> 254 µs fused, the 1x1 layers with a residual 91 -> 80 µs). BNNK_NOT_FUSED when a layer is outside
+// that (the caller then quantizes and multiplies in two launches); BNN_FQ=0 turns the form off, BNN_FQ=2 admits SiLU
+// layers too (tuning).
 template <int SW, bool kSP>
 static int launch_fq(const bnnk_gemm_plan *p, const GemmArgs &a, const CUtensorMap &map, size_t smem,
                      bnn_stream_t st) {
@@ -1103,10 +1106,10 @@ extern "C" int bnnk_pw_s8_fq(const bnnk_gemm_plan *p, int rows, int Mw, const fl
   static int env = -1;
   if (env < 0) {
     const char *s = getenv("BNN_FQ");
-    env = !(s && s[0] == '0');
+    env = s ? atoi(s) : 1;
   }
-  if (!env || rows <= 0 || p->nkb != 1 || K % 4 || K < 4 || K > kFQMaxK || lda % 4 || lda < K ||
-      xws != (long long)Mw * lda || ((uintptr_t)x & 15) || e->qo)
+  if (!env || (env == 1 && e->act != 0) || rows <= 0 || p->nkb != 1 || K % 4 || K < 4 || K > kFQMaxK || lda % 4 ||
+      lda < K || xws != (long long)Mw * lda || ((uintptr_t)x & 15) || e->qo)
     return BNNK_NOT_FUSED;
   GemmArgs a;
   a.stall = __atomic_exchange_n(&g_stall_next, 0, __ATOMIC_RELAXED);  // the test hook, as for bnnk_gemm

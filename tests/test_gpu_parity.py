@@ -169,6 +169,12 @@ PW_CASES = [  # (N, K, Mw, B, act, residual, padded output (ow), gated)
     (64, 256, 32, 5, 0, False, 0, True),
     (16, 16, 64, 1, 2, False, 0, False),
     (24, 40, 64, 3, 1, True, 8, False),
+    # linear layers of K <= 72 take the one-launch form (the quantizer inside the GEMM): 32-, 64- and 128-byte K
+    # blocks, several N tiles, ragged last tiles, residual and padded outputs
+    (600, 64, 200, 3, 0, True, 0, False),
+    (40, 8, 333, 2, 0, False, 9, False),
+    (96, 72, 130, 1, 0, True, 0, False),
+    (8, 4, 50, 4, 0, False, 0, False),
 ]
 
 
