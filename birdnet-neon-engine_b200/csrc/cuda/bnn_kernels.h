@@ -15,7 +15,8 @@ extern "C" {
 typedef struct CUstream_st *bnn_stream_t;
 
 /* device-side error word written by kernels whose bounded waits time out (0 = none) */
-enum { BNNK_ERR_NONE = 0, BNNK_ERR_TMA_WAIT = 1, BNNK_ERR_MMA_WAIT = 2, BNNK_ERR_EPI_WAIT = 3, BNNK_ERR_DW3_WAIT = 4 };
+enum { BNNK_ERR_NONE = 0, BNNK_ERR_TMA_WAIT = 1, BNNK_ERR_MMA_WAIT = 2, BNNK_ERR_EPI_WAIT = 3, BNNK_ERR_DW3_WAIT = 4,
+       BNNK_ERR_QUANT_WAIT = 5 };
 /* the failed-window word beside it: the smallest failed window index, or BNNK_NO_FAIL (every byte 0x7f, so that a
  * byte memset restores it) */
 #define BNNK_NO_FAIL 0x7f7f7f7f
@@ -26,9 +27,10 @@ int bnnk_device_init(void);
 /* ---- int8 1x1 conv / dense layer (PW_S8, GEMV_S8) */
 
 /* per-row dynamic quantization (s8n_quant_rows, optionally gated): rows r = w * Mw + m of x (window stride xws,
- * row stride lda; gate [B][K] at window stride gws or NULL) -> q [rows][Kq] (Kq >= K, pads = zero point), sa, za */
+ * row stride lda; gate [B][K] at window stride gws or NULL) -> q [rows][Kq] (Kq >= K, pads = zero point), sa, za.
+ * err: the device error word for the forms with bounded waits (NULL: those forms are not used) */
 int bnnk_quant(int rows, int Mw, const float *x, long long xws, int lda, int K, int Kq, const float *gate,
-               long long gws, int8_t *q, float *sa, int32_t *za, bnn_stream_t st);
+               long long gws, int8_t *q, float *sa, int32_t *za, int *err, bnn_stream_t st);
 
 /* The GEMM of one layer: weights [Nrows][Kq] int8 (row n = output channel, zero beyond N and K), q [rows_cap][Kq].
  * The plan holds the TMA descriptors (opaque, 64-byte aligned) and the tiling. */

@@ -80,6 +80,23 @@ __device__ __forceinline__ uint32_t quant_word(float t0, float t1, float t2, flo
   return __byte_perm(__byte_perm(qi[0], qi[1], 0x0040), __byte_perm(qi[2], qi[3], 0x0040), 0x5410);
 }
 
+// The same for a row whose scaled values all lie below 2^22 in magnitude (quant_fast): t + 1.5 * 2^23 falls in
+// (2^23, 2^24), where the fp32 grid is the integers, so the one rounded add rounds t to nearest-even, as FCVTNS and
+// lrintf do there, and its bits are 0x4B400000 + round(t). The products x * inv feed that add, so they stay scalar
+// (__fmul_rn: never contracted). Rows with larger values, NaN or infinities keep the conversions above.
+constexpr float kRoundMagic = 12582912.f;  // 1.5 * 2^23
+constexpr uint32_t kRoundBits = 0x4B400000u;
+__device__ __forceinline__ bool quant_fast(float lo, float hi, float inv) {
+  return __fmul_rn(fmaxf(fabsf(lo), fabsf(hi)), inv) < 4194304.f;  // false for NaN / infinite lo, hi
+}
+__device__ __forceinline__ uint32_t quant_word_fast(float4 v, float inv, uint32_t zz) {  // zz = z - kRoundBits
+  const int32_t q0 = min(max((int32_t)(__float_as_uint(__fadd_rn(__fmul_rn(v.x, inv), kRoundMagic)) + zz), -127), 127);
+  const int32_t q1 = min(max((int32_t)(__float_as_uint(__fadd_rn(__fmul_rn(v.y, inv), kRoundMagic)) + zz), -127), 127);
+  const int32_t q2 = min(max((int32_t)(__float_as_uint(__fadd_rn(__fmul_rn(v.z, inv), kRoundMagic)) + zz), -127), 127);
+  const int32_t q3 = min(max((int32_t)(__float_as_uint(__fadd_rn(__fmul_rn(v.w, inv), kRoundMagic)) + zz), -127), 127);
+  return __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);
+}
+
 // RecipEstimate of the Arm ARM for a in [256, 512): ((2^19 / (2a + 1)) + 1) / 2
 __device__ __forceinline__ uint32_t recip_estimate(uint32_t a) {
   uint32_t b = (1u << 19) / (2u * a + 1u);

@@ -90,27 +90,106 @@ __global__ void __launch_bounds__(256) k_quant(int rows, int Mw, const float *__
   uint4 *qr = reinterpret_cast<uint4 *>(q + (long long)r * Kq);
   const float2 inv2 = splat2(inv);
   const uint32_t zp = ((uint32_t)z & 0xffu) * 0x01010101u;  // a pad word: the zero point
+  const uint32_t zz = (uint32_t)z - kRoundBits;
+  const bool fast = quant_fast(lo, hi, inv);
 #pragma unroll
   for (int i = 0; i < NC; i++) {
     const int ch = lane + i * L;
     if (ch >= nch) break;
     uint32_t wd[4];
+    if (fast) {
 #pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const int g = 4 * ch + e;
-      if (g < K4) {
-        const float2 p0 = mul2_rn(make_float2(v[i][e].x, v[i][e].y), inv2);
-        const float2 p1 = mul2_rn(make_float2(v[i][e].z, v[i][e].w), inv2);
-        wd[e] = quant_word(p0.x, p0.y, p1.x, p1.y, z, 4 * g < K8);
-      } else {
-        wd[e] = zp;
+      for (int e = 0; e < 4; e++) wd[e] = 4 * ch + e < K4 ? quant_word_fast(v[i][e], inv, zz) : zp;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int g = 4 * ch + e;
+        if (g < K4) {
+          const float2 p0 = mul2_rn(make_float2(v[i][e].x, v[i][e].y), inv2);
+          const float2 p1 = mul2_rn(make_float2(v[i][e].z, v[i][e].w), inv2);
+          wd[e] = quant_word(p0.x, p0.y, p1.x, p1.y, z, 4 * g < K8);
+        } else {
+          wd[e] = zp;
+        }
       }
     }
     qr[ch] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
   }
 }
 
+// The second half of a warp-per-row quantizer: the row's gated values v (lane l holds the float4 groups l + 32 i;
+// NG = ceil(K / 128), so only the last group can fall past K) and the lane's partial min / max in, the row's
+// parameters and its quantized bytes (4-byte words, pads past K = the zero point) out.
+template <int NG>
+__device__ __forceinline__ void quant_row_out(const float4 (&v)[NG], float lo, float hi, int lane, int K4, int Kq4,
+                                              int K8, int r, int8_t *__restrict__ q, int Kq, float *__restrict__ sa,
+                                              int32_t *__restrict__ za) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = fmin_nan(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = fmax_nan(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  float inv, s;
+  int32_t z;
+  quant_params(lo, hi, inv, z, s);
+  if (lane == 0) { sa[r] = s; za[r] = z; }
+  uint32_t *qr = reinterpret_cast<uint32_t *>(q + (long long)r * Kq);
+  const uint32_t zp = ((uint32_t)z & 0xffu) * 0x01010101u;  // a pad word: the zero point
+  if (quant_fast(lo, hi, inv)) {
+    const uint32_t zz = (uint32_t)z - kRoundBits;
+#pragma unroll
+    for (int i = 0; i < NG; i++) {
+      const int g = lane + 32 * i;
+      if (i < NG - 1 || g < K4) qr[g] = quant_word_fast(v[i], inv, zz);
+      else if (g < Kq4) qr[g] = zp;
+    }
+  } else {
+    const float2 inv2 = splat2(inv);
+#pragma unroll
+    for (int i = 0; i < NG; i++) {
+      const int g = lane + 32 * i;
+      if (i < NG - 1 || g < K4) {
+        const float2 p0 = mul2_rn(make_float2(v[i].x, v[i].y), inv2);
+        const float2 p1 = mul2_rn(make_float2(v[i].z, v[i].w), inv2);
+        qr[g] = quant_word(p0.x, p0.y, p1.x, p1.y, z, 4 * g < K8);
+      } else if (g < Kq4) {
+        qr[g] = zp;
+      }
+    }
+  }
+  if (Kq4 > 32 * NG)  // pads beyond the register groups (never for Kq = K rounded up to 32)
+    for (int g = 32 * NG + lane; g < Kq4; g += 32) qr[g] = zp;
+}
+
+// The row's values times the gate (paired multiplies: their products feed no add) and the lane's NaN-propagating
+// min / max over them (the 4-wide part of s8n_quant_rows; K % 4 == 0 here, so there is no scalar tail).
 template <int NG, bool kGate>
+__device__ __forceinline__ void quant_row_in(float4 (&v)[NG], const float4 (&gv)[kGate ? NG : 1], int lane, int K4,
+                                             float &lo, float &hi) {
+  lo = __int_as_float(0x7f800000);
+  hi = __int_as_float(0xff800000);
+#pragma unroll
+  for (int i = 0; i < NG; i++) {
+    const int g = lane + 32 * i;
+    if (i < NG - 1 || g < K4) {
+      float4 t = v[i];
+      if (kGate) {
+        const float2 p0 = mul2_rn(make_float2(t.x, t.y), make_float2(gv[i].x, gv[i].y));
+        const float2 p1 = mul2_rn(make_float2(t.z, t.w), make_float2(gv[i].z, gv[i].w));
+        t = make_float4(p0.x, p0.y, p1.x, p1.y);
+      }
+      v[i] = t;
+      lo = fmin_nan(lo, fmin_nan(fmin_nan(t.x, t.y), fmin_nan(t.z, t.w)));
+      hi = fmax_nan(hi, fmax_nan(fmax_nan(t.x, t.y), fmax_nan(t.z, t.w)));
+    }
+  }
+}
+
+// Rows of 128-1536 (K % 4 == 0, 16-byte aligned rows), a warp per row: 512-byte coalesced loads, a contiguous run of
+// rpw rows per warp with D rows in flight behind the one being quantized (D + 1 register buffers rotated by a fully
+// unrolled loop, so no values move between registers). The window of a row is tracked by counting (no division per
+// row); the SE gate, one row of K per window, sits in registers and is reloaded when the window changes.
+template <int NG, bool kGate, int D>
 __global__ void __launch_bounds__(256) k_quant_w(int rows, int Mw, const float *__restrict__ x, long long xws, int lda,
                                                  int K, int Kq, const float *__restrict__ gate, long long gws,
                                                  int8_t *__restrict__ q, float *__restrict__ sa,
@@ -118,158 +197,131 @@ __global__ void __launch_bounds__(256) k_quant_w(int rows, int Mw, const float *
   const int lane = threadIdx.x % 32;
   const int wrp = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) / 32);
   const int r0 = wrp * rpw, r1 = min(rows, r0 + rpw);
+  if (r0 >= r1) return;
   const int K4 = K >> 2, Kq4 = Kq >> 2, K8 = K & ~7;
+  int wl = r0 / Mw, ml = r0 - wl * Mw;  // the next row to load
+  int wc = wl, mc = ml;                 // the next row to quantize
   float4 gv[kGate ? NG : 1];
   int gw = -1;
-  // the next row's loads are issued before the current row is reduced and quantized (one row in flight per warp
-  // behind the one being processed)
-  float4 vn[NG];
-  auto load_row = [&](int r) {
-    const int w = r / Mw, m = r - w * Mw;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + w * xws + (long long)m * lda);
+  auto load = [&](float4 (&dst)[NG]) {
+    const float4 *xr = reinterpret_cast<const float4 *>(x + wl * xws + (long long)ml * lda);
 #pragma unroll
     for (int i = 0; i < NG; i++) {
       const int g = lane + 32 * i;
-      if (g < K4) vn[i] = __ldg(xr + g);
+      if (i < NG - 1 || g < K4) dst[i] = __ldg(xr + g);
     }
+    if (++ml == Mw) { ml = 0; wl++; }
   };
-  if (r0 < r1) load_row(r0);
-  for (int r = r0; r < r1; r++) {
-    const int w = r / Mw;
-    float4 v[NG];
-#pragma unroll
-    for (int i = 0; i < NG; i++) v[i] = vn[i];
-    if (r + 1 < r1) load_row(r + 1);
-    if (kGate && w != gw) {
-      gw = w;
-      const float4 *gp = reinterpret_cast<const float4 *>(gate + w * gws);
+  auto process = [&](float4 (&v)[NG], int r) {
+    if (kGate && wc != gw) {
+      gw = wc;
+      const float4 *gp = reinterpret_cast<const float4 *>(gate + wc * gws);
 #pragma unroll
       for (int i = 0; i < NG; i++) {
         const int g = lane + 32 * i;
-        gv[i] = g < K4 ? __ldg(gp + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+        gv[i] = (i < NG - 1 || g < K4) ? __ldg(gp + g) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
-    float lo = __int_as_float(0x7f800000), hi = __int_as_float(0xff800000);
+    float lo, hi;
+    quant_row_in<NG, kGate>(v, gv, lane, K4, lo, hi);
+    quant_row_out<NG>(v, lo, hi, lane, K4, Kq4, K8, r, q, Kq, sa, za);
+    if (++mc == Mw) { mc = 0; wc++; }
+  };
+  float4 buf[D + 1][NG];
 #pragma unroll
-    for (int i = 0; i < NG; i++) {
-      const int g = lane + 32 * i;
-      if (g < K4) {
-        float4 t = v[i];
-        if (kGate) {
-          const float2 p0 = mul2_rn(make_float2(t.x, t.y), make_float2(gv[i].x, gv[i].y));
-          const float2 p1 = mul2_rn(make_float2(t.z, t.w), make_float2(gv[i].z, gv[i].w));
-          t = make_float4(p0.x, p0.y, p1.x, p1.y);
-        }
-        v[i] = t;
-        lo = fmin_nan(lo, fmin_nan(fmin_nan(t.x, t.y), fmin_nan(t.z, t.w)));
-        hi = fmax_nan(hi, fmax_nan(fmax_nan(t.x, t.y), fmax_nan(t.z, t.w)));
+  for (int d = 0; d < D; d++)
+    if (r0 + d < r1) load(buf[d]);
+  for (int r = r0; r < r1; r += D + 1) {
+#pragma unroll
+    for (int u = 0; u <= D; u++) {
+      const int rr = r + u;
+      if (rr < r1) {
+        if (rr + D < r1) load(buf[(u + D) % (D + 1)]);
+        process(buf[u], rr);
       }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      lo = fmin_nan(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-      hi = fmax_nan(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-    }
-    float inv, s;
-    int32_t z;
-    quant_params(lo, hi, inv, z, s);
-    if (lane == 0) { sa[r] = s; za[r] = z; }
-    uint32_t *qr = reinterpret_cast<uint32_t *>(q + (long long)r * Kq);
-    const float2 inv2 = splat2(inv);
-#pragma unroll
-    for (int i = 0; i < NG; i++) {
-      const int g = lane + 32 * i;
-      if (g < K4) {
-        const float2 p0 = mul2_rn(make_float2(v[i].x, v[i].y), inv2);
-        const float2 p1 = mul2_rn(make_float2(v[i].z, v[i].w), inv2);
-        qr[g] = quant_word(p0.x, p0.y, p1.x, p1.y, z, 4 * g < K8);
-      } else if (g < Kq4) {
-        qr[g] = ((uint32_t)z & 0xffu) * 0x01010101u;  // pads past K: the zero point
-      }
-    }
-    if (Kq4 > 32 * NG) {  // pads beyond the register groups (never for Kq = K rounded up to 32)
-      for (int g = 32 * NG + lane; g < Kq4; g += 32) qr[g] = ((uint32_t)z & 0xffu) * 0x01010101u;
     }
   }
 }
 
-// The same with the loads of the next two rows in flight and the SE gate read with the row it scales (the same gate
-// serves every row of a window, so these loads hit L1): for gated rows of 288 (measured 52.7 -> 49.5 µs per 98k rows;
-// on wider rows the extra registers cost more occupancy than the deeper prefetch gained).
+// Wide rows (K = 128 .. 1536, 16-byte aligned) with the row data staged in shared memory: each warp owns a ring of
+// kQBD row slots that lane 0 fills by bulk copies (cp.async.bulk, one per row, completion counted on the slot's
+// mbarrier), so kQBD rows per warp are in flight without holding registers. A warp takes a contiguous run of rows
+// (the SE gate, one row of K per window, is re-read only when the window changes) and quantizes each as k_quant_w
+// does: the row's NaN-propagating min / max, reduced over the lanes, then 4-byte words of quantized bytes. A wait that
+// runs out records BNNK_ERR_QUANT_WAIT, waits (bounded) for the warp's other copies and leaves.
+constexpr int kQBD = 4, kQBWarps = 8;
 template <int NG, bool kGate>
-__global__ void __launch_bounds__(256) k_quant_w2(int rows, int Mw, const float *__restrict__ x, long long xws, int lda,
-                                                 int K, int Kq, const float *__restrict__ gate, long long gws,
-                                                 int8_t *__restrict__ q, float *__restrict__ sa,
-                                                 int32_t *__restrict__ za, int rpw) {
-  const int lane = threadIdx.x % 32;
-  const int wrp = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) / 32);
-  const int r0 = wrp * rpw, r1 = min(rows, r0 + rpw);
-  const int K4 = K >> 2, Kq4 = Kq >> 2, K8 = K & ~7;
-  // rows r + 1 and r + 2 are loaded before row r is reduced and quantized
-  float4 vn[2][NG];
-  auto load_row = [&](int r, float4 (&dst)[NG]) {
-    const int w = r / Mw, m = r - w * Mw;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + w * xws + (long long)m * lda);
-#pragma unroll
-    for (int i = 0; i < NG; i++) {
-      const int g = lane + 32 * i;
-      if (g < K4) dst[i] = __ldg(xr + g);
-    }
+__global__ void __launch_bounds__(32 * kQBWarps) k_quant_b(int rows, int Mw, const float *__restrict__ x, long long xws,
+                                                           int lda, int K, int Kq, const float *__restrict__ gate,
+                                                           long long gws, int8_t *__restrict__ q,
+                                                           float *__restrict__ sa, int32_t *__restrict__ za, int rpw,
+                                                           int *err) {
+  extern __shared__ __align__(128) unsigned char qb_sm[];
+  __shared__ __align__(8) uint64_t bar[kQBWarps][kQBD];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const uint32_t rb = (uint32_t)K * 4u;  // row bytes, a multiple of 16
+  const float4 *slot0 = reinterpret_cast<const float4 *>(qb_sm + (size_t)wid * kQBD * rb);
+  const int r0 = (int)(((long long)blockIdx.x * kQBWarps + wid) * rpw), r1 = min(rows, r0 + rpw);
+  if (lane == 0) {
+    for (int d = 0; d < kQBD; d++) mbar_init(smem_u32(&bar[wid][d]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  int wl = r0 / Mw, ml = r0 - wl * Mw;  // the next row to copy (lane 0's count)
+  int wc = wl, mc = ml;                 // the next row to quantize
+  auto issue = [&](int d) {             // lane 0: the next row into slot d
+    const float *src = x + wl * xws + (long long)ml * lda;
+    if (++ml == Mw) { ml = 0; wl++; }
+    const uint32_t b = smem_u32(&bar[wid][d]);
+    mbar_expect_tx(b, rb);
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(qb_sm + ((size_t)wid * kQBD + d) * rb)),
+                 "l"(src), "r"(rb), "r"(b)
+                 : "memory");
   };
-  if (r0 < r1) load_row(r0, vn[0]);
-  if (r0 + 1 < r1) load_row(r0 + 1, vn[1]);
+  if (lane == 0)
+    for (int d = 0; d < kQBD && r0 + d < r1; d++) issue(d);
+  const int K4 = K >> 2, Kq4 = Kq >> 2, K8 = K & ~7;
+  float4 gv[kGate ? NG : 1];
+  int gw = -1;
   for (int r = r0; r < r1; r++) {
-    const int w = r / Mw;
+    const int j = r - r0, d = j % kQBD;
+    const bool ok = __all_sync(0xffffffffu, mbar_wait_ns(smem_u32(&bar[wid][d]), (j / kQBD) & 1, kWaitNs));
+    if (!ok) {  // record, let the copies still in flight into this warp's slots land, leave
+      if (lane == 0) {
+        atomicExch(err, BNNK_ERR_QUANT_WAIT);
+        for (int t = 0; t < kQBD && r + t < r1; t++)
+          mbar_wait_ns(smem_u32(&bar[wid][(j + t) % kQBD]), ((j + t) / kQBD) & 1, kWaitNs);
+      }
+      __syncwarp();
+      return;
+    }
+    if (kGate && wc != gw) {
+      gw = wc;
+      const float4 *gp = reinterpret_cast<const float4 *>(gate + wc * gws);
+#pragma unroll
+      for (int i = 0; i < NG; i++) {
+        const int g = lane + 32 * i;
+        gv[i] = (i < NG - 1 || g < K4) ? __ldg(gp + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    if (++mc == Mw) { mc = 0; wc++; }
+    const float4 *sl = slot0 + (size_t)d * (rb >> 4);
     float4 v[NG];
 #pragma unroll
     for (int i = 0; i < NG; i++) {
-      v[i] = vn[0][i];
-      vn[0][i] = vn[1][i];
-    }
-    if (r + 2 < r1) load_row(r + 2, vn[1]);
-    const float4 *gp = kGate ? reinterpret_cast<const float4 *>(gate + w * gws) : nullptr;
-    float lo = __int_as_float(0x7f800000), hi = __int_as_float(0xff800000);
-#pragma unroll
-    for (int i = 0; i < NG; i++) {
       const int g = lane + 32 * i;
-      if (g < K4) {
-        float4 t = v[i];
-        if (kGate) {
-          const float4 gg = __ldg(gp + g);
-          const float2 p0 = mul2_rn(make_float2(t.x, t.y), make_float2(gg.x, gg.y));
-          const float2 p1 = mul2_rn(make_float2(t.z, t.w), make_float2(gg.z, gg.w));
-          t = make_float4(p0.x, p0.y, p1.x, p1.y);
-        }
-        v[i] = t;
-        lo = fmin_nan(lo, fmin_nan(fmin_nan(t.x, t.y), fmin_nan(t.z, t.w)));
-        hi = fmax_nan(hi, fmax_nan(fmax_nan(t.x, t.y), fmax_nan(t.z, t.w)));
-      }
+      if (i < NG - 1 || g < K4) v[i] = sl[g];
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      lo = fmin_nan(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-      hi = fmax_nan(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    float lo, hi;
+    quant_row_in<NG, kGate>(v, gv, lane, K4, lo, hi);
+    // every lane's reads of the slot are done (their values are in use above): refill it with row r + kQBD
+    __syncwarp();
+    if (lane == 0 && r + kQBD < r1) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(d);
     }
-    float inv, s;
-    int32_t z;
-    quant_params(lo, hi, inv, z, s);
-    if (lane == 0) { sa[r] = s; za[r] = z; }
-    uint32_t *qr = reinterpret_cast<uint32_t *>(q + (long long)r * Kq);
-    const float2 inv2 = splat2(inv);
-#pragma unroll
-    for (int i = 0; i < NG; i++) {
-      const int g = lane + 32 * i;
-      if (g < K4) {
-        const float2 p0 = mul2_rn(make_float2(v[i].x, v[i].y), inv2);
-        const float2 p1 = mul2_rn(make_float2(v[i].z, v[i].w), inv2);
-        qr[g] = quant_word(p0.x, p0.y, p1.x, p1.y, z, 4 * g < K8);
-      } else if (g < Kq4) {
-        qr[g] = ((uint32_t)z & 0xffu) * 0x01010101u;  // pads past K: the zero point
-      }
-    }
-    if (Kq4 > 32 * NG) {  // pads beyond the register groups (never for Kq = K rounded up to 32)
-      for (int g = 32 * NG + lane; g < Kq4; g += 32) qr[g] = ((uint32_t)z & 0xffu) * 0x01010101u;
-    }
+    quant_row_out<NG>(v, lo, hi, lane, K4, Kq4, K8, r, q, Kq, sa, za);
   }
 }
 
@@ -835,15 +887,52 @@ extern "C" int bnnk_device_init(void) {
   return e ? e : bnnk_f16_tables_init(tab);
 }
 
+// k_quant_b's launch: 8 warps a block, the blocks that the slots' shared memory lets one SM hold on every SM, and a
+// contiguous run of rows per warp
+template <int NG>
+static int launch_quant_b_t(int rows, int Mw, const float *x, long long xws, int lda, int K, int Kq, const float *gate,
+                            long long gws, int8_t *q, float *sa, int32_t *za, int *err, bnn_stream_t st) {
+  const size_t smem = (size_t)kQBWarps * kQBD * K * 4;
+  static SmemAttr attr_g, attr_u;
+  const cudaError_t e = gate ? attr_g.ensure(k_quant_b<NG, true>, smem) : attr_u.ensure(k_quant_b<NG, false>, smem);
+  if (e) return e;
+  int per_sm = (int)((227 * 1024) / (smem + kQBWarps * kQBD * 8 + 1024));
+  per_sm = per_sm < 1 ? 1 : per_sm > 8 ? 8 : per_sm;
+  const long long warps_max = (long long)num_sms() * per_sm * kQBWarps;
+  const int rpw = (int)((rows + warps_max - 1) / warps_max);
+  const long long warps = (rows + rpw - 1) / rpw;
+  const unsigned grid = (unsigned)((warps + kQBWarps - 1) / kQBWarps);
+  if (gate) k_quant_b<NG, true><<<grid, 32 * kQBWarps, smem, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw, err);
+  else k_quant_b<NG, false><<<grid, 32 * kQBWarps, smem, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw, err);
+  return cudaGetLastError();
+}
+static int launch_quant_b(int rows, int Mw, const float *x, long long xws, int lda, int K, int Kq, const float *gate,
+                          long long gws, int8_t *q, float *sa, int32_t *za, int *err, bnn_stream_t st) {
+  switch ((K / 4 + 31) / 32) {  // float4 groups per lane
+#define BNN_QB(N) \
+  case N: return launch_quant_b_t<N>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, err, st)
+    BNN_QB(1); BNN_QB(2); BNN_QB(3); BNN_QB(4); BNN_QB(5); BNN_QB(6);
+    BNN_QB(7); BNN_QB(8); BNN_QB(9); BNN_QB(10); BNN_QB(11); BNN_QB(12);
+#undef BNN_QB
+  default: return BNNK_NOT_FUSED;
+  }
+}
+
 extern "C" int bnnk_quant(int rows, int Mw, const float *x, long long xws, int lda, int K, int Kq, const float *gate,
-                          long long gws, int8_t *q, float *sa, int32_t *za, bnn_stream_t st) {
+                          long long gws, int8_t *q, float *sa, int32_t *za, int *err, bnn_stream_t st) {
   if (rows <= 0) return 0;
   const bool vec = K % 4 == 0 && lda % 4 == 0 && xws % 4 == 0 && (!gate || gws % 4 == 0) && Kq % 4 == 0 &&
                    ((uintptr_t)x & 15) == 0 && (!gate || ((uintptr_t)gate & 15) == 0);
   const int nch = Kq / 16;  // 16-byte chunks of a quantized row
   const int K4 = K / 4, ng = (K4 + 31) / 32;
   // tuning overrides (sweeps): BNN_QUANT_W=0 keeps wide rows on the lane-group form; BNN_QUANT_RPW=n rows per warp
-  const char *ew = getenv("BNN_QUANT_W"), *er = getenv("BNN_QUANT_RPW");
+  const char *ew = getenv("BNN_QUANT_W"), *er = getenv("BNN_QUANT_RPW"), *ev = getenv("BNN_QUANT_V");
+  // rows of 128-1536 with an error word for the bounded waits: staged by bulk copies (k_quant_b; measured on the v2.4
+  // step's gated layers: K 288 74 -> 66 µs per op, K 864 48 -> 44, K 1536 37.4 -> 33.3; BNN_QUANT_V=0 turns it off)
+  if (err && vec && K >= 128 && K <= 1536 && Kq % 4 == 0 && ((uintptr_t)q & 3) == 0 && !(ev && ev[0] == '0')) {
+    const int rc = launch_quant_b(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, err, st);
+    if (rc != BNNK_NOT_FUSED) return rc;
+  }
   if (vec && K >= 128 && K <= 1024 && Kq % 4 == 0 && ((uintptr_t)q & 3) == 0 && !(ew && ew[0] == '0')) {
     // wide rows, a warp per row; rows per warp from a sweep (98k rows of 288: 4 best, 25k of 864: 2, 256 of 1024: 1;
     // rows of 1536 were faster in the lane-group form)
@@ -853,9 +942,9 @@ extern "C" int bnnk_quant(int rows, int Mw, const float *x, long long xws, int l
     const int warps = (rows + rpw - 1) / rpw;
     const unsigned grid = (unsigned)((warps + 7) / 8);
 #define BNN_QW(NGV)                                                                                           \
-  if (gate && NGV == 3) k_quant_w2<3, true><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw); \
-  else if (gate) k_quant_w<NGV, true><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw); \
-  else k_quant_w<NGV, false><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw)
+  if (gate && NGV == 3) k_quant_w<3, true, 2><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw); \
+  else if (gate) k_quant_w<NGV, true, 1><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw); \
+  else k_quant_w<NGV, false, 1><<<grid, 256, 0, st>>>(rows, Mw, x, xws, lda, K, Kq, gate, gws, q, sa, za, rpw)
     switch (ng) {  // K in [128, 1024]: 1 .. 8 float4 groups per lane
     case 1: BNN_QW(1); break;
     case 2: BNN_QW(2); break;
@@ -1215,7 +1304,7 @@ extern "C" int bnnk_pw_s8_static(const bnnk_gemm_plan *p, int rows, int Mw, cons
   // the op's plan with its A operand moved onto the q region (a host-side encode: no device memory)
   bnnk_gemm_plan pl = *p;
   rc = encode_2d(pl.tma_a, q, p->kq, (int)(BNNK_STATIC_QBYTES / p->kq), p->sw, 128, p->sw);
-  if (!rc) rc = bnnk_quant(rows, Mw, x, xws, lda, K, p->kq, gate, gws, q, sa, za, st);
+  if (!rc) rc = bnnk_quant(rows, Mw, x, xws, lda, K, p->kq, gate, gws, q, sa, za, err, st);
   if (!rc) rc = bnnk_gemm(&pl, rows, Mw, sa, za, e, err, st);
   return rc;
 }

@@ -400,7 +400,9 @@ static int check_err_word(bnn_ctx *c, int di) {
     cudaMemsetAsync(dv->err, 0, sizeof(int), (cudaStream_t)dv->stream);
     ERR(BNN_ERR_WINDOW, "window not scored: a GPU kernel's bounded wait ran out (code %d: %s) on GPU %d; hint: the GPU "
         "is stalled or shared with a long job: retry, and check nvidia-smi", code,
-        code == BNNK_ERR_TMA_WAIT ? "TMA load" : code == BNNK_ERR_MMA_WAIT ? "tensor-core operands" : "GEMM result",
+        code == BNNK_ERR_TMA_WAIT ? "TMA load" : code == BNNK_ERR_MMA_WAIT ? "tensor-core operands"
+        : code == BNNK_ERR_EPI_WAIT ? "GEMM result" : code == BNNK_ERR_DW3_WAIT ? "depthwise row ring"
+        : code == BNNK_ERR_QUANT_WAIT ? "quantizer row copy" : "other",
         dv->dev);
     return -1;
   }
@@ -759,7 +761,7 @@ int bnn_cuda_quant_rows(int rows, int Mw, const float *d_x, long long xws, int l
     return -1;
   }
   return launch_rc("bnn_cuda_quant_rows",
-                   bnnk_quant(rows, Mw, d_x, xws, lda, K, Kq, d_gate, gws, d_q, d_sa, d_za, (bnn_stream_t)stream));
+                   bnnk_quant(rows, Mw, d_x, xws, lda, K, Kq, d_gate, gws, d_q, d_sa, d_za, NULL, (bnn_stream_t)stream));
 }
 
 struct bnn_pw_s8 {
@@ -821,7 +823,7 @@ int bnn_pw_s8_run(bnn_pw_s8 *o, int B, int Mw, const float *d_x, long long xws, 
     const int f = bnnk_pw_s8_fq(&o->op.plan, rows, Mw, d_x, xws, lda, o->K, &ep, o->err, st);
     if (f != BNNK_NOT_FUSED) return launch_rc("bnn_pw_s8_run", f);
   }
-  int e = bnnk_quant(rows, Mw, d_x, xws, lda, o->K, o->op.kq, d_gate, gws, o->q, o->sa, o->za, st);
+  int e = bnnk_quant(rows, Mw, d_x, xws, lda, o->K, o->op.kq, d_gate, gws, o->q, o->sa, o->za, o->err, st);
   if (!e) {
     e = bnnk_gemm(&o->op.plan, rows, Mw, o->sa, o->za, &ep, o->err, st);
   }

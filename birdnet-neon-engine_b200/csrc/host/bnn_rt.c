@@ -1789,7 +1789,7 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
         rc = 0;
       }
       if (!pre_q)
-        rc = bnnk_quant(n * M, M, IN_(0), INWS(0), p[5], p[1], o->kq, gate, gate ? WS(6) : 0, qq, qs, qz, st);
+        rc = bnnk_quant(n * M, M, IN_(0), INWS(0), p[5], p[1], o->kq, gate, gate ? WS(6) : 0, qq, qs, qz, dv->err, st);
       if (!rc) {
         if (o->qnext && i + 1 < op1) {  /* this GEMM quantizes its rows for the expand after it */
           e.qo = dv->q2;
@@ -1804,7 +1804,7 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
       break;
     }
     case BNN_OP_GEMV_S8: {
-      rc = bnnk_quant(n, 1, IN_(0), INWS(0), p[1], p[1], o->kq, NULL, 0, dv->q, dv->sa, dv->za, st);
+      rc = bnnk_quant(n, 1, IN_(0), INWS(0), p[1], p[1], o->kq, NULL, 0, dv->q, dv->sa, dv->za, dv->err, st);
       if (!rc) {
         bnnk_epilogue e = {p[4], B_(1), WS(1), p[3], 0, 0, NULL, 0, 0, 0, 0, o->sw, o->bias, o->cs, NULL, NULL, NULL, 0, 0};
         rc = bnnk_gemm(&o->plan, n, 1, dv->sa, dv->za, &e, dv->err, st);
@@ -1921,13 +1921,13 @@ int bnn_rt_launch(bnn_ctx *c, int di, int n, const float *d_pcm, int op0, int op
                          {p[8], p[9], p[10], p[11], NULL, NULL},
                          B_(1), B_(2), B_(3), B_(4), B_(5), B_(6), WS(1), WS(2), WS(3), WS(4), WS(5), WS(6)};
       rc = bnnk_sed_pool(n, &a, st);
-      if (!rc) rc = bnnk_quant(n * L, L, B_(3), WS(3), Cp, C, sub[0].kq, NULL, 0, dv->q, dv->sa, dv->za, st);
+      if (!rc) rc = bnnk_quant(n * L, L, B_(3), WS(3), Cp, C, sub[0].kq, NULL, 0, dv->q, dv->sa, dv->za, dv->err, st);
       if (!rc) {
         bnnk_epilogue e = {2, B_(4), WS(4), p[3], 0, 0, NULL, 0, 0, 0, 0, sub[0].sw, sub[0].bias, sub[0].cs,
                            NULL, NULL, NULL, 0, 0};
         rc = bnnk_gemm(&sub[0].plan, n * L, L, dv->sa, dv->za, &e, dv->err, st);
       }
-      if (!rc) rc = bnnk_quant(n * L, L, B_(4), WS(4), p[3], p[0], sub[1].kq, NULL, 0, dv->q, dv->sa, dv->za, st);
+      if (!rc) rc = bnnk_quant(n * L, L, B_(4), WS(4), p[3], p[0], sub[1].kq, NULL, 0, dv->q, dv->sa, dv->za, dv->err, st);
       for (int g = 1; g < 3 && !rc; g++) {
         bnnk_epilogue e = {0, B_(4 + g), WS(4 + g), p[4 * g + 3], 0, 0, NULL, 0, 0, 0, 0, sub[g].sw, sub[g].bias,
                            sub[g].cs, NULL, NULL, NULL, 0, 0};
