@@ -29,6 +29,9 @@ __device__ __forceinline__ int sx(int p) { return p + (p >> 4); }
 // fall in distinct banks
 __device__ __forceinline__ int sg(int i) { return i + (i >> 5); }
 
+// the 4-bit reverse of e (levels 1-4 gather their 16 points in bit-reversed order)
+__host__ __device__ constexpr int rev4(int e) { return ((e & 1) << 3) | ((e & 2) << 1) | ((e & 4) >> 1) | ((e & 8) >> 3); }
+
 struct cpx {
   float r, i;
 };
@@ -112,11 +115,17 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
       // levels 1-4 on the 16 consecutive bit-reversed positions 16 lt .. 16 lt + 15
       cpx z[16];
       const int st = f * HOP;
+      // the bit reverse of 16 lt + e in LG bits is rev(16 lt) + rev4(e) 2^(LG-4): one base per thread, compile-time
+      // offsets per point. st + 2 n is even, so sample 2 n + 1 sits one word after sample 2 n in the padded segment,
+      // and the offsets 2 rev4(e) 2^(LG-4) are multiples of 32, so they pass through sg() unchanged plus 1/32.
+      const float *sb = seg + sg(st + 2 * (int)(__brev((unsigned)(16 * lt)) >> (32 - LG)));
+      const float2 *wb = reinterpret_cast<const float2 *>(win) + lt;
 #pragma unroll
       for (int e = 0; e < 16; e++) {
-        const int n = (int)(__brev((unsigned)(16 * lt + e)) >> (32 - LG));
-        const float2 w = reinterpret_cast<const float2 *>(win)[e * TPF + lt];  // (w[2n], w[2n+1]), lanes adjacent
-        z[e] = {__fmul_rn(seg[sg(st + 2 * n)], w.x), __fmul_rn(seg[sg(st + 2 * n + 1)], w.y)};
+        constexpr int kSh = LG - 3;
+        const int ce = rev4(e) << kSh;
+        const float2 w = wb[e * TPF];  // (w[2n], w[2n+1]), lanes adjacent
+        z[e] = {__fmul_rn(sb[ce + (ce >> 5)], w.x), __fmul_rn(sb[ce + (ce >> 5) + 1], w.y)};
       }
 #pragma unroll
       for (int g = 0; g < 4; g++) r4first(z[4 * g], z[4 * g + 1], z[4 * g + 2], z[4 * g + 3]);
@@ -126,19 +135,22 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
         const float4 w = __ldg(tws + j);  // stage 0 (len 8): w1 = tw[j M / 8], w2 = tw[j M / 16]
         r22(z[j], z[j + 4], z[j + 8], z[j + 12], w.x, w.y, w.z, w.w);
       }
+      float2 *fo = fp + 17 * lt;  // sx(16 lt + e) = 17 lt + e
 #pragma unroll
-      for (int e = 0; e < 16; e++) fp[sx(16 * lt + e)] = make_float2(z[e].r, z[e].i);
+      for (int e = 0; e < 16; e++) fo[e] = make_float2(z[e].r, z[e].i);
     }
     __syncthreads();
     if (live) {
       // levels 5-8 on the points base + 16 a + 64 b of a 256-block
       const int j = lt & 15, base = (lt >> 4) * 256 + j;
+      // base has j < 16 in its low four bits, so sx(base + 16 a + 64 b) = sx(base) + 17 a + 68 b
+      float2 *fb = fp + sx(base);
       cpx z[16];
 #pragma unroll
       for (int a = 0; a < 4; a++)
 #pragma unroll
         for (int b = 0; b < 4; b++) {
-          const float2 v = fp[sx(base + 16 * a + 64 * b)];
+          const float2 v = fb[17 * a + 68 * b];
           z[a + 4 * b] = {v.x, v.y};
         }
       {  // len 32: h 16, groups (a = 0..3) for each b, twiddle index j
@@ -156,31 +168,33 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
 #pragma unroll
       for (int a = 0; a < 4; a++)
 #pragma unroll
-        for (int b = 0; b < 4; b++) fp[sx(base + 16 * a + 64 * b)] = make_float2(z[a + 4 * b].r, z[a + 4 * b].i);
+        for (int b = 0; b < 4; b++) fb[17 * a + 68 * b] = make_float2(z[a + 4 * b].r, z[a + 4 * b].i);
     }
     __syncthreads();
     if (live) {
       if (LG == 10) {  // levels 9-10: len 512, h 256, st1 2, st2 1
+        float2 *fq = fp + sx(lt);  // lt < 64: sx(lt + 64 c + 256 d) = sx(lt) + 68 c + 272 d
 #pragma unroll
         for (int c = 0; c < 4; c++) {
           const int jj = lt + 64 * c;
-          const float2 va = fp[sx(jj)], vb = fp[sx(jj + 256)], vc = fp[sx(jj + 512)], vd = fp[sx(jj + 768)];
+          const float2 va = fq[68 * c], vb = fq[68 * c + 272], vc = fq[68 * c + 544], vd = fq[68 * c + 816];
           cpx a = {va.x, va.y}, b = {vb.x, vb.y}, cc = {vc.x, vc.y}, d = {vd.x, vd.y};
           const float4 w = __ldg(tws + 84 + jj);  // stage 3 (len 512): w1 = tw[2 jj], w2 = tw[jj]
           r22(a, b, cc, d, w.x, w.y, w.z, w.w);
-          fp[sx(jj)] = make_float2(a.r, a.i);
-          fp[sx(jj + 256)] = make_float2(b.r, b.i);
-          fp[sx(jj + 512)] = make_float2(cc.r, cc.i);
-          fp[sx(jj + 768)] = make_float2(d.r, d.i);
+          fq[68 * c] = make_float2(a.r, a.i);
+          fq[68 * c + 272] = make_float2(b.r, b.i);
+          fq[68 * c + 544] = make_float2(cc.r, cc.i);
+          fq[68 * c + 816] = make_float2(d.r, d.i);
         }
       } else {  // level 9 alone (radix 2): len 512, half 256, step 1 (fft_tab.h:64-76)
+        float2 *fq = fp + sx(lt);  // lt < 32: sx(lt + 32 c + 256 d) = sx(lt) + 34 c + 272 d
+        const float *tr = twr + lt, *ti = twi + lt;
 #pragma unroll
         for (int c = 0; c < 8; c++) {
-          const int jj = lt + 32 * c;
-          const float2 hv = fp[sx(jj + 256)], uv = fp[sx(jj)];
-          const cpx v = cmul({hv.x, hv.y}, twr[jj], twi[jj]);
-          fp[sx(jj)] = make_float2(__fadd_rn(uv.x, v.r), __fadd_rn(uv.y, v.i));
-          fp[sx(jj + 256)] = make_float2(__fsub_rn(uv.x, v.r), __fsub_rn(uv.y, v.i));
+          const float2 hv = fq[34 * c + 272], uv = fq[34 * c];
+          const cpx v = cmul({hv.x, hv.y}, tr[32 * c], ti[32 * c]);
+          fq[34 * c] = make_float2(__fadd_rn(uv.x, v.r), __fadd_rn(uv.y, v.i));
+          fq[34 * c + 272] = make_float2(__fsub_rn(uv.x, v.r), __fsub_rn(uv.y, v.i));
         }
       }
     }
