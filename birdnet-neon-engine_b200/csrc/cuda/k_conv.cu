@@ -388,14 +388,18 @@ __global__ void __launch_bounds__(128) k_c0pool(const float *__restrict__ img, l
   __shared__ float bs[24];
   const int oy = blockIdx.x, win = blockIdx.y, tid = threadIdx.x;
   const float *im = img + win * iws;
-  for (int i = tid; i < 4 * 8 * NI; i += 128) {
-    const int r = i / (8 * NI), rem = i - r * 8 * NI, ph = rem / NI, ii = rem - ph * NI;
-    const int cidx = 8 * ii + ph;  // float index within the padded row
-    const int y = 2 * oy + r - 1, xcol = cidx / 2 - 3, ch = cidx & 1;
-    rows[r][ph][ii] = (cidx < RF && y >= 0 && y < 96 && xcol >= 0 && xcol < 511) ? im[((long long)y * 511 + xcol) * 2 + ch]
-                                                                                  : 0.f;
+  // per row, padded float index cidx = 8 ii + ph (shifts only); the row's sample cidx / 2 - 3, channel cidx & 1
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const int y = 2 * oy + r - 1;
+    const bool yin = y >= 0 && y < 96;
+    const float *imr = im + (long long)(yin ? y : 0) * 511 * 2 - 6;  // cidx 6 is the row's first sample
+    for (int cidx = tid; cidx < 8 * NI; cidx += 128) {
+      const int xcol = (cidx >> 1) - 3;
+      rows[r][cidx & 7][cidx >> 3] = (yin && cidx < RF && xcol >= 0 && xcol < 511) ? imr[cidx] : 0.f;
+    }
   }
-  for (int i = tid; i < 64 * 24; i += 128) ws[i / 24][i % 24] = wt[i];
+  for (int i = tid; i < 64 * 24; i += 128) (&ws[0][0])[i] = wt[i];
   if (tid < 24) bs[tid] = bias[tid];
   __syncthreads();
   const int qx = tid;
