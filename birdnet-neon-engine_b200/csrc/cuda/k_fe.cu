@@ -200,16 +200,20 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
     }
     __syncthreads();
     // real part of X_k for the bins the filters use: 1/2 [(Zr_k + Zr_{M-k}) + c (Zi_k + Zi_{M-k}) - s (Zr_k - Zr_{M-k})]
-    for (int ff = 0; ff < FF && f0 + ff < nfr; ff++) {
-      const float2 *g = pts + ff * MP;
-      for (int kk = tid; kk < nk; kk += 256) {
-        const int k = klo + kk;
-        const int k1 = k == M ? 0 : k, k2 = k == 0 ? 0 : M - k;  // Z_M = Z_0 (the reference reads past its buffer)
-        const float2 zv = g[sx(k1)], yv = g[sx(k2)];
+    // bin-major: a bin's coefficients are loaded once for all the group's frames
+    const int nff = min(FF, nfr - f0);
+    for (int kk = tid; kk < nk; kk += 256) {
+      const int k = klo + kk;
+      const int k1 = k == M ? 0 : k, k2 = k == 0 ? 0 : M - k;  // Z_M = Z_0 (the reference reads past its buffer)
+      const int o1 = sx(k1), o2 = sx(k2);
+      const float pc = t.pc[BR][k], ps = t.ps[BR][k];
+      for (int ff = 0; ff < nff; ff++) {
+        const float2 *g = pts + ff * MP;
+        const float2 zv = g[o1], yv = g[o2];
         const float zr = zv.x, zi = zv.y, yr = yv.x, yi = yv.y;
         float v = __fadd_rn(zr, yr);
-        v = __fmaf_rn(__fadd_rn(zi, yi), t.pc[BR][k], v);
-        v = __fmaf_rn(-__fsub_rn(zr, yr), t.ps[BR][k], v);
+        v = __fmaf_rn(__fadd_rn(zi, yi), pc, v);
+        v = __fmaf_rn(-__fsub_rn(zr, yr), ps, v);
         R[ff * nk + kk] = __fmul_rn(v, 0.5f);
       }
     }
@@ -218,34 +222,54 @@ __device__ __forceinline__ void spec(const float *__restrict__ x, float mn, floa
     const int *__restrict__ mk = t.mel_k[BR];
     const float *__restrict__ mw = t.mel_w[BR];
     const float pw2 = t.pw2[BR], bs = t.bn_s[BR], bb = t.bn_b[BR];
-    for (int i = tid; i < FF * kNmel; i += 256) {
-      const int ff = i / kNmel, j = i - ff * kNmel, fi2 = f0 + ff;
-      if (fi2 >= nfr) continue;
+    // a thread takes one filter for FB of the group's frames: each weight is loaded once and feeds FB frames' chains
+    // (two alternating accumulators per frame, taps in order, as the reference forms them)
+    constexpr int FB = FF / 2;
+    for (int i = tid; i < 2 * kNmel; i += 256) {
+      const int fb = i / kNmel, j = i - fb * kNmel, ffb = fb * FB;
+      if (f0 + ffb >= nfr) continue;
       // a filter's taps are the consecutive bins lo .. lo + n - 1 (its nonzero range), so only the weights are
       // loaded per tap
       const int e0 = moff[j], n = moff[j + 1] - e0;
-      const float *Rf = R + ff * nk - klo + (n > 0 ? mk[e0] : klo);
+      const float *Rf = R + ffb * nk - klo + (n > 0 ? mk[e0] : klo);
       const float *wf = mw + e0;
-      float a0 = 0.f, a1 = 0.f;
+      float a0[FB], a1[FB];
+#pragma unroll
+      for (int q = 0; q < FB; q++) a0[q] = a1[q] = 0.f;
       int e = 0;
       for (; e + 8 <= n; e += 8) {
         float wv[8];
 #pragma unroll
         for (int u = 0; u < 8; u++) wv[u] = __ldg(wf + e + u);
 #pragma unroll
-        for (int u = 0; u < 8; u += 2) {
-          a0 = __fmaf_rn(Rf[e + u], wv[u], a0);
-          a1 = __fmaf_rn(Rf[e + u + 1], wv[u + 1], a1);
-        }
+        for (int q = 0; q < FB; q++)
+#pragma unroll
+          for (int u = 0; u < 8; u += 2) {
+            a0[q] = __fmaf_rn(Rf[q * nk + e + u], wv[u], a0[q]);
+            a1[q] = __fmaf_rn(Rf[q * nk + e + u + 1], wv[u + 1], a1[q]);
+          }
       }
       for (; e + 2 <= n; e += 2) {
-        a0 = __fmaf_rn(Rf[e], __ldg(wf + e), a0);
-        a1 = __fmaf_rn(Rf[e + 1], __ldg(wf + e + 1), a1);
+        const float w0 = __ldg(wf + e), w1 = __ldg(wf + e + 1);
+#pragma unroll
+        for (int q = 0; q < FB; q++) {
+          a0[q] = __fmaf_rn(Rf[q * nk + e], w0, a0[q]);
+          a1[q] = __fmaf_rn(Rf[q * nk + e + 1], w1, a1[q]);
+        }
       }
-      if (e < n) a0 = __fmaf_rn(Rf[e], __ldg(wf + e), a0);
-      const float m = fmax_nan(fabsf(__fadd_rn(a0, a1)), 1e-30f);
-      const float p = exp2_acc(__fmul_rn(pw2, log2_acc(m)));
-      img[((long long)(kNmel - 1 - j) * kNfr + t0 + fi2) * 2 + BR] = __fmaf_rn(p, bs, bb);
+      if (e < n) {
+        const float w0 = __ldg(wf + e);
+#pragma unroll
+        for (int q = 0; q < FB; q++) a0[q] = __fmaf_rn(Rf[q * nk + e], w0, a0[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < FB; q++) {
+        const int fi2 = f0 + ffb + q;
+        if (fi2 >= nfr) break;
+        const float m = fmax_nan(fabsf(__fadd_rn(a0[q], a1[q])), 1e-30f);
+        const float p = exp2_acc(__fmul_rn(pw2, log2_acc(m)));
+        img[((long long)(kNmel - 1 - j) * kNfr + t0 + fi2) * 2 + BR] = __fmaf_rn(p, bs, bb);
+      }
     }
     __syncthreads();
   }
